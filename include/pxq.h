@@ -1,0 +1,160 @@
+/*
+ * pxq.h -- C ABI of the B200 quantized-matmul backend (libpxq.so).
+ *
+ * This is the drop-in boundary for Pixelina's quantized-matmul path.  Every
+ * entry point uses plain pointers and sizes; "device" pointers are CUDA
+ * device addresses on the current device, "host" pointers are ordinary (or
+ * pinned) host memory.  Streams are passed as `void*` holding a cudaStream_t
+ * (NULL = the legacy default stream).  All functions return PXQ_OK (0) or a
+ * PXQ_ERR_* code; pxq_last_error() gives a one-line description for the
+ * calling thread.
+ *
+ * Layout conventions follow the reference (paths are within the Pixelina
+ * source tree):
+ *   - "rows" = weight rows = output features (N), "columns" = activation rows
+ *     (M), "inner" = K, exactly as in cpu_quant_matmul
+ *     (src/kernels_quant.cpp:369).
+ *   - weights are GGUF rows: rows x weight_bytes({inner}, type) bytes
+ *     (src/model.cpp:87-121);
+ *   - activations are row-major fp32 [columns][inner];
+ *   - the output is row-major [columns][ldy]: output[c*ldy + r]
+ *     (src/kernels_quant.cpp:396 has ldy == rows).
+ */
+#ifndef PXQ_H
+#define PXQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PXQ_OK 0
+#define PXQ_ERR_INVALID 1       /* bad argument (null pointer, zero size, ...) */
+#define PXQ_ERR_UNSUPPORTED 2   /* type/shape this backend does not handle */
+#define PXQ_ERR_CUDA 3          /* a CUDA runtime call failed */
+#define PXQ_ERR_NO_MEMORY 4     /* device allocation failed */
+#define PXQ_ERR_NO_DEVICE 5     /* no usable sm_100 device */
+#define PXQ_ERR_DEVICE_STATUS 6 /* a kernel reported a bounded-wait timeout */
+
+/* GGML type ids, src/model_types.h:13-21 */
+#define PXQ_TYPE_F32 0
+#define PXQ_TYPE_F16 1
+#define PXQ_TYPE_Q8_0 8
+#define PXQ_TYPE_Q5_K 13
+#define PXQ_TYPE_Q6_K 14
+#define PXQ_TYPE_BF16 30
+
+#if defined(__GNUC__)
+#define PXQ_API __attribute__((visibility("default")))
+#else
+#define PXQ_API
+#endif
+
+typedef struct pxq_weight pxq_weight; /* opaque device-resident weight */
+
+/* Library version, (major << 16) | minor. */
+PXQ_API int pxq_version(void);
+
+/* Description of the last error on the calling thread ("" if none). */
+PXQ_API const char* pxq_last_error(void);
+
+/* Select and initialise a CUDA device for the calling thread.  Replaces the
+ * session start of the GPU backend (VulkanSession::initialize,
+ * src/backend_vulkan.h:124-137).  Fails with PXQ_ERR_NO_DEVICE unless the
+ * device is compute capability 10.x. */
+PXQ_API int pxq_init(int device);
+
+/* Bytes of a [inner, rows] tensor of `type`, 0 if invalid.  Same contract as
+ * weight_bytes (src/model.cpp:87-121). */
+PXQ_API uint64_t pxq_weight_bytes(uint64_t inner, uint64_t rows, uint32_t type);
+
+/* fp32 device rows -> GGUF Q8_0 blocks on the device, bit-exact with
+ * quantize_row_q8_0_ref (src/kernels_quant.cpp:120-144).
+ * x: [rows][inner] fp32; blocks: rows * inner/32 * 34 bytes; inner % 32 == 0. */
+PXQ_API int pxq_quantize_q8_0(const float* x, void* blocks, size_t rows, size_t inner, void* stream);
+
+/* fp32 device rows -> Q8_K blocks (292 bytes per 256 values), bit-exact with
+ * quantize_row_q8_K_ref (src/kernels_quant.cpp:80-118); inner % 256 == 0. */
+PXQ_API int pxq_quantize_q8_K(const float* x, void* blocks, size_t rows, size_t inner, void* stream);
+
+/* Dequantize `count` values of a Q8_0 / Q5_K / Q6_K device buffer to fp32,
+ * bit-exact with cpu_decode (src/backend_cpu.cpp:24-101). */
+PXQ_API int pxq_decode(const void* data, uint32_t type, size_t count, float* out, void* stream);
+
+/* Make a weight device-resident.  `bytes` holds rows GGUF rows of `type`
+ * (host memory if bytes_on_device == 0, else a device pointer that is
+ * copied).  `key` (may be NULL) names the tensor; uploading the same key
+ * again returns the cached weight, as the Vulkan weight cache does with
+ * "file:name:offset:bytes" (src/backend_vulkan.cpp:742-758).
+ * Supported types: Q8_0, Q5_K. */
+PXQ_API int pxq_weight_upload(const void* bytes, int bytes_on_device, uint32_t type, size_t inner, size_t rows, const char* key,
+                      pxq_weight** out);
+
+/* Drop a weight (its device copies are freed once no call uses them). */
+PXQ_API int pxq_weight_release(pxq_weight* w);
+
+/* Drop every cached weight. */
+PXQ_API int pxq_weight_cache_clear(void);
+
+/* Device matmul through a weight: the operator behind cpu_matmul
+ * (src/backend_cpu.cpp:103-133) and vulkan_matmul
+ * (src/backend_vulkan.cpp:1083-1094).
+ *   output[c*ldy + r] = sum_k input[c][k] * W[row_first + r][k]   (+ bias[r])
+ * for c < columns, r < row_count.  row_first/row_count select a row range of
+ * the weight like tensor_linear_rows (src/tensor.cpp:529-544); bias (device,
+ * row_count floats, may be NULL) is added as tensor_linear does
+ * (src/tensor.cpp:162-170).  input, output, bias are device pointers.
+ * columns <= 8 runs the streaming matvec, larger runs the tensor-core GEMM. */
+PXQ_API int pxq_matmul(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* output,
+               size_t ldy, const float* bias, void* stream);
+
+/* pxq_matmul forced onto the small-M matvec kernel (columns <= 8), the
+ * GPU counterpart of shaders/matvec.comp's role (src/backend_vulkan.cpp:887). */
+PXQ_API int pxq_matvec(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* output,
+               size_t ldy, const float* bias, void* stream);
+
+/* pxq_matmul forced onto the tensor-core GEMM (any columns >= 1), the
+ * counterpart of shaders/quantize.comp + shaders/matmul_mmq.comp
+ * (src/backend_vulkan.cpp:963-981). */
+PXQ_API int pxq_gemm(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* output,
+             size_t ldy, const float* bias, void* stream);
+
+/* Host-buffer drop-in for cpu_quant_matmul (src/kernels_quant.cpp:369-412,
+ * declared src/tensor.h:74): same arguments, same output layout
+ * output[c*rows + r].  Weights are cached on the device by (pointer, size,
+ * type); the input is copied to the device and the output back before the
+ * call returns.  Returns PXQ_OK when handled, PXQ_ERR_UNSUPPORTED exactly
+ * where the reference returns false (unsupported type, zero sizes,
+ * inner % block != 0, inner > INT32_MAX). */
+PXQ_API int pxq_quant_matmul(const unsigned char* weights, uint32_t type, const float* input, float* output, size_t rows,
+                     size_t columns, size_t inner);
+
+/* Wait for `stream` and report any bounded-wait timeout a kernel recorded
+ * since the last call (PXQ_ERR_DEVICE_STATUS), then clear it. */
+PXQ_API int pxq_synchronize(void* stream);
+
+/* Reorder all-gathered output shards into one row-major output: src holds
+ * `shards` consecutive [columns][shard_rows] blocks (what an all-gather of
+ * per-rank outputs produces), dst is [columns][ldy] with shard s at column
+ * offset s*shard_rows.  Device pointers.  The layout step of the N-sharded
+ * multi-GPU matmul (no counterpart in the single-process reference). */
+PXQ_API int pxq_gather_shards(const float* src, size_t shards, size_t columns, size_t shard_rows, float* dst, size_t ldy,
+                      void* stream);
+
+/* Debug/parity: run the tensor-core GEMM but store, instead of the scaled
+ * sum, every exact block dot it computed.  dump (device) receives
+ * items x columns x row_count floats, item-major; items = inner/32 for Q8_0
+ * and 5*inner/256 for Q5_K (per super-block: four 64-value sums of
+ * sc*q5*q8, then the min sum of m*bsum).  These are the int32 block dots of
+ * pix_dot_q8_0 / pix_dot_q5_K (src/kernels_quant.cpp:339-365, :163-254),
+ * exact as floats. */
+PXQ_API int pxq_gemm_block_dots(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* dump,
+                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PXQ_H */

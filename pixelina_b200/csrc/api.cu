@@ -1,0 +1,589 @@
+// api.cu -- host side of the C ABI declared in include/pxq.h.
+//
+// Responsibilities:
+//   * device context per CUDA device (SM count, kernel status word, the
+//     cuTensorMapEncodeTiled entry point fetched through the runtime);
+//   * the device weight cache: raw GGUF rows uploaded once, plus a lazily
+//     built GEMM operand copy (repack.cu), keyed like the Vulkan backend's
+//     cache (src/backend_vulkan.cpp:742-758);
+//   * dispatch of a matmul to the streaming matvec (columns <= 8) or the
+//     tensor-core GEMM, with per-call scratch from the stream-ordered
+//     allocator;
+//   * the host-buffer cpu_quant_matmul drop-in.
+// There is no CPU compute path here: an unsupported case is reported as an
+// error status (the reference's `false`), never computed on the host.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <list>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "pxq.h"
+#include "pxq_internal.h"
+
+using namespace pxq;
+
+namespace {
+
+thread_local std::string t_error;
+
+int fail(int code, const char* fmt, ...)
+{
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_error = buf;
+    return code;
+}
+
+#define PXQ_CUDA(call)                                                                                 \
+    do {                                                                                               \
+        cudaError_t e_ = (call);                                                                       \
+        if (e_ != cudaSuccess) return fail(PXQ_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                                   const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct DeviceCtx {
+    bool ready = false;
+    int sms = 0;
+    uint32_t* status = nullptr;  // device word written by kernels on a bounded-wait timeout
+    EncodeTiledFn encode = nullptr;
+};
+
+constexpr int kMaxDevices = 16;
+std::mutex g_mutex;
+DeviceCtx g_dev[kMaxDevices];
+thread_local int t_device = -1;
+
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+int init_device(int device)
+{
+    if (device < 0 || device >= kMaxDevices) return fail(PXQ_ERR_NO_DEVICE, "device %d out of range", device);
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || device >= count)
+        return fail(PXQ_ERR_NO_DEVICE, "no CUDA device %d (found %d)", device, count);
+    PXQ_CUDA(cudaSetDevice(device));
+    std::lock_guard<std::mutex> lock(g_mutex);
+    DeviceCtx& d = g_dev[device];
+    if (!d.ready) {
+        cudaDeviceProp prop;
+        PXQ_CUDA(cudaGetDeviceProperties(&prop, device));
+        if (prop.major != 10)
+            return fail(PXQ_ERR_NO_DEVICE, "device %d is sm_%d%d; this build targets sm_100a", device, prop.major, prop.minor);
+        d.sms = prop.multiProcessorCount;
+        PXQ_CUDA(cudaMalloc(&d.status, 256));
+        PXQ_CUDA(cudaMemset(d.status, 0, 256));
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        PXQ_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !fn) return fail(PXQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+        d.encode = reinterpret_cast<EncodeTiledFn>(fn);
+        // keep stream-ordered scratch cached between calls
+        cudaMemPool_t pool;
+        PXQ_CUDA(cudaDeviceGetDefaultMemPool(&pool, device));
+        uint64_t threshold = UINT64_MAX;
+        PXQ_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold));
+        d.ready = true;
+    }
+    t_device = device;
+    return PXQ_OK;
+}
+
+int ensure_device(DeviceCtx** out)
+{
+    if (t_device < 0) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+        int rc = init_device(dev);
+        if (rc) return rc;
+    } else {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (cur != t_device) PXQ_CUDA(cudaSetDevice(t_device));
+    }
+    *out = &g_dev[t_device];
+    return PXQ_OK;
+}
+
+int make_map(const DeviceCtx* d, CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1,
+             uint64_t stride1_bytes, uint32_t b0, uint32_t b1, CUtensorMapSwizzle sw)
+{
+    const cuuint64_t dims[2] = {d0, d1};
+    const cuuint64_t strides[1] = {stride1_bytes};
+    const cuuint32_t box[2] = {b0, b1};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = d->encode(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(PXQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu stride %llu box %u x %u", (int)r,
+                    (unsigned long long)d0, (unsigned long long)d1, (unsigned long long)stride1_bytes, b0, b1);
+    return PXQ_OK;
+}
+
+// GEMM operand copy of (a row range of) a weight.
+struct Packed {
+    int64_t rows = 0;   // packed rows
+    int64_t ldn = 0;    // row stride of the scale planes
+    void* mem = nullptr;
+    __half* wv = nullptr;
+    float* s1 = nullptr;      // dwT (Q8_0) or dT (Q5_K)
+    float* s2 = nullptr;      // dminT (Q5_K)
+    __half* bmin = nullptr;   // Q5_K min operand
+    CUtensorMap tmB, tmSB, tmSB2, tmBmin;
+    ~Packed()
+    {
+        if (mem) cudaFree(mem);
+    }
+};
+
+}  // namespace
+
+struct pxq_weight {
+    uint32_t type = 0;
+    int64_t inner = 0, rows = 0, stride = 0;
+    int device = 0;
+    uint8_t* raw = nullptr;
+    std::string key;
+    std::unique_ptr<Packed> packed;                       // whole tensor
+    std::map<std::pair<int64_t, int64_t>, std::unique_ptr<Packed>> views;  // unaligned row views
+    ~pxq_weight()
+    {
+        if (raw) cudaFree(raw);
+    }
+};
+
+namespace {
+
+std::unordered_map<std::string, pxq_weight*> g_cache;  // guarded by g_mutex
+
+int build_packed(const DeviceCtx* d, pxq_weight* w, int64_t first, int64_t count, std::unique_ptr<Packed>& out,
+                 cudaStream_t s)
+{
+    auto pk = std::make_unique<Packed>();
+    const int64_t K = w->inner;
+    const int64_t nb = w->type == kTypeQ8_0 ? K / kQK8_0 : K / kQKK;
+    pk->rows = count;
+    pk->ldn = round_up(count, 4);
+    const size_t wv_bytes = (size_t)count * K * 2;
+    const size_t s_bytes = (size_t)nb * pk->ldn * 4;
+    const size_t bmin_bytes = w->type == kTypeQ5_K ? (size_t)count * nb * 16 * 2 : 0;
+    const size_t off_s1 = round_up((int64_t)wv_bytes, 1024);
+    const size_t off_s2 = off_s1 + round_up((int64_t)s_bytes, 1024);
+    const size_t off_bmin = off_s2 + (w->type == kTypeQ5_K ? round_up((int64_t)s_bytes, 1024) : 0);
+    const size_t total = off_bmin + round_up((int64_t)bmin_bytes, 1024) + 1024;
+    if (cudaMalloc(&pk->mem, total) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(PXQ_ERR_NO_MEMORY, "cannot allocate %zu bytes for the GEMM operand copy", total);
+    }
+    uint8_t* base = static_cast<uint8_t*>(pk->mem);
+    pk->wv = reinterpret_cast<__half*>(base);
+    pk->s1 = reinterpret_cast<float*>(base + off_s1);
+    pk->s2 = reinterpret_cast<float*>(base + off_s2);
+    pk->bmin = reinterpret_cast<__half*>(base + off_bmin);
+    PXQ_CUDA(cudaMemsetAsync(pk->mem, 0, total, s));
+    const uint8_t* src = w->raw + first * w->stride;
+    if (w->type == kTypeQ8_0) {
+        PXQ_CUDA(launch_repack_q8_0(src, count, K, w->stride, pk->wv, pk->s1, pk->ldn, s));
+    } else {
+        PXQ_CUDA(launch_repack_q5_K(src, count, K, w->stride, pk->wv, pk->s1, pk->s2, pk->bmin, pk->ldn, s));
+    }
+    const uint32_t sbox = w->type == kTypeQ8_0 ? 2 : 1;
+    int rc = make_map(d, &pk->tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pk->wv, K, count, K * 2, 64, 256,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!rc) rc = make_map(d, &pk->tmSB, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pk->s1, count, nb, pk->ldn * 4, 256, sbox,
+                           CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (!rc && w->type == kTypeQ5_K) {
+        rc = make_map(d, &pk->tmSB2, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pk->s2, count, nb, pk->ldn * 4, 256, 1,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (!rc) rc = make_map(d, &pk->tmBmin, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pk->bmin, nb * 16, count, nb * 32, 16, 256,
+                               CU_TENSOR_MAP_SWIZZLE_32B);
+    } else {
+        pk->tmSB2 = pk->tmSB;
+        pk->tmBmin = pk->tmB;
+    }
+    if (rc) return rc;
+    out = std::move(pk);
+    return PXQ_OK;
+}
+
+// Operand copy covering [first, first+count): the whole-tensor copy when the
+// view starts on a 4-row boundary (TMA coordinates of fp32 scale planes must
+// be 16-byte aligned), otherwise a dedicated copy of just the view.
+int get_packed(const DeviceCtx* d, pxq_weight* w, int64_t first, int64_t count, const Packed** pk, int64_t* n_first,
+               cudaStream_t s)
+{
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (first % 4 == 0) {
+        if (!w->packed) {
+            int rc = build_packed(d, w, 0, w->rows, w->packed, s);
+            if (rc) return rc;
+        }
+        *pk = w->packed.get();
+        *n_first = first;
+        return PXQ_OK;
+    }
+    auto key = std::make_pair(first, count);
+    auto it = w->views.find(key);
+    if (it == w->views.end()) {
+        std::unique_ptr<Packed> p;
+        int rc = build_packed(d, w, first, count, p, s);
+        if (rc) return rc;
+        it = w->views.emplace(key, std::move(p)).first;
+    }
+    *pk = it->second.get();
+    *n_first = 0;
+    return PXQ_OK;
+}
+
+int check_matmul_args(pxq_weight* w, size_t row_first, size_t row_count, const void* input, size_t columns, const void* output,
+                      size_t ldy)
+{
+    if (!w || !input || !output) return fail(PXQ_ERR_INVALID, "null weight, input or output");
+    if (!columns || !row_count) return fail(PXQ_ERR_INVALID, "zero columns or rows");
+    if (row_first > (size_t)w->rows || row_count > (size_t)w->rows - row_first)
+        return fail(PXQ_ERR_INVALID, "row range [%zu, %zu) outside weight with %lld rows", row_first, row_first + row_count,
+                    (long long)w->rows);
+    if (ldy < row_count && columns > 1) return fail(PXQ_ERR_INVALID, "ldy %zu < row_count %zu", ldy, row_count);
+    if (w->type != kTypeQ8_0 && w->type != kTypeQ5_K)
+        return fail(PXQ_ERR_UNSUPPORTED, "weight type %u not supported", w->type);
+    return PXQ_OK;
+}
+
+int run_matvec(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* output,
+               size_t ldy, const float* bias, cudaStream_t s)
+{
+    if (columns > 8) return fail(PXQ_ERR_UNSUPPORTED, "matvec handles at most 8 columns (got %zu)", columns);
+    const int64_t K = w->inner;
+    const size_t xbytes = w->type == kTypeQ8_0 ? columns * (K / kQK8_0) * kQ8_0Bytes : columns * (K / kQKK) * kQ8KBytes;
+    void* xq = nullptr;
+    if (cudaMallocAsync(&xq, xbytes + 16, s) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(PXQ_ERR_NO_MEMORY, "scratch allocation of %zu bytes failed", xbytes);
+    }
+    cudaError_t e = w->type == kTypeQ8_0 ? launch_quantize_q8_0_blocks(input, xq, columns, K, K, s)
+                                         : launch_quantize_q8_K_blocks(input, xq, columns, K, K, s);
+    if (e == cudaSuccess)
+        e = launch_matvec(w->type, w->raw + row_first * w->stride, w->stride, row_count, K, xq, columns, output, ldy, bias, s);
+    cudaFreeAsync(xq, s);
+    if (e != cudaSuccess) return fail(PXQ_ERR_CUDA, "matvec launch failed: %s", cudaGetErrorString(e));
+    return PXQ_OK;
+}
+
+int run_gemm(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns,
+             float* output, size_t ldy, const float* bias, float* dump, cudaStream_t s)
+{
+    const int64_t K = w->inner, M = (int64_t)columns;
+    if (K % 8 != 0) return fail(PXQ_ERR_UNSUPPORTED, "inner %lld not a multiple of 8", (long long)K);
+    const Packed* pk = nullptr;
+    int64_t n_first = 0;
+    int rc = get_packed(d, w, (int64_t)row_first, (int64_t)row_count, &pk, &n_first, s);
+    if (rc) return rc;
+    const bool q5 = w->type == kTypeQ5_K;
+    const int64_t nb = q5 ? K / kQKK : K / kQK8_0;
+    const int64_t ldd = round_up(M, 4);
+    const size_t xq_bytes = (size_t)M * K * 2;
+    const size_t dx_bytes = (size_t)nb * ldd * 4;
+    const size_t amin_bytes = q5 ? (size_t)M * nb * 32 : 0;
+    const size_t off_dx = round_up((int64_t)xq_bytes, 1024);
+    const size_t off_amin = off_dx + round_up((int64_t)dx_bytes, 1024);
+    const size_t total = off_amin + round_up((int64_t)amin_bytes, 1024) + 1024;
+    void* scratch = nullptr;
+    if (cudaMallocAsync(&scratch, total, s) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(PXQ_ERR_NO_MEMORY, "scratch allocation of %zu bytes failed", total);
+    }
+    uint8_t* base = static_cast<uint8_t*>(scratch);
+    __half* xq = reinterpret_cast<__half*>(base);
+    float* dxT = reinterpret_cast<float*>(base + off_dx);
+    __half* amin = reinterpret_cast<__half*>(base + off_amin);
+    cudaError_t e = q5 ? launch_quantize_q8_K_operand(input, xq, dxT, amin, M, K, K, ldd, s)
+                       : launch_quantize_q8_0_operand(input, xq, dxT, M, K, K, ldd, s);
+    GemmOperands op;
+    std::memset(&op, 0, sizeof(op));
+    op.type = w->type;
+    op.M = M;
+    op.N = (int64_t)row_count;
+    op.K = K;
+    op.n_first = n_first;
+    op.y = output;
+    op.ldy = (int64_t)ldy;
+    op.bias = bias;
+    op.dump = dump;
+    op.status = d->status;
+    if (e == cudaSuccess) {
+        rc = make_map(d, &op.tm[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xq, K, M, K * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!rc) rc = make_map(d, &op.tm[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dxT, M, nb, ldd * 4, 128, q5 ? 1 : 2,
+                               CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (!rc && q5) rc = make_map(d, &op.tm[5], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, amin, nb * 16, M, nb * 32, 16, 128,
+                                     CU_TENSOR_MAP_SWIZZLE_32B);
+        if (!q5) op.tm[5] = op.tm[0];
+        op.tm[1] = pk->tmB;
+        op.tm[3] = pk->tmSB;
+        op.tm[4] = pk->tmSB2;
+        op.tm[6] = pk->tmBmin;
+        if (!rc) e = launch_gemm(op, d->sms, s);
+    }
+    cudaFreeAsync(scratch, s);
+    if (rc) return rc;
+    if (e != cudaSuccess) return fail(PXQ_ERR_CUDA, "gemm launch failed: %s", cudaGetErrorString(e));
+    return PXQ_OK;
+}
+
+// per-thread stream for the host-buffer entry point (the reference's session
+// is thread-local too, src/backend_vulkan.cpp:86)
+thread_local cudaStream_t t_stream = nullptr;
+thread_local int t_stream_device = -1;
+
+}  // namespace
+
+extern "C" {
+
+int pxq_version(void) { return (0 << 16) | 1; }
+
+const char* pxq_last_error(void) { return t_error.c_str(); }
+
+int pxq_init(int device)
+{
+    t_error.clear();
+    return init_device(device);
+}
+
+uint64_t pxq_weight_bytes(uint64_t inner, uint64_t rows, uint32_t type)
+{
+    uint64_t block = 1, bytes;
+    switch (type) {
+    case PXQ_TYPE_F32: bytes = 4; break;
+    case PXQ_TYPE_F16:
+    case PXQ_TYPE_BF16: bytes = 2; break;
+    case PXQ_TYPE_Q8_0: block = 32; bytes = 34; break;
+    case PXQ_TYPE_Q5_K: block = 256; bytes = 176; break;
+    case PXQ_TYPE_Q6_K: block = 256; bytes = 210; break;
+    default: return 0;
+    }
+    if (!inner || inner % block || !rows) return 0;
+    uint64_t count = inner / block;
+    if (count > UINT64_MAX / rows) return 0;
+    count *= rows;
+    if (count > UINT64_MAX / bytes) return 0;
+    return count * bytes;
+}
+
+int pxq_quantize_q8_0(const float* x, void* blocks, size_t rows, size_t inner, void* stream)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (!x || !blocks || !rows || !inner) return fail(PXQ_ERR_INVALID, "null pointer or zero size");
+    if (inner % 32) return fail(PXQ_ERR_UNSUPPORTED, "inner %zu not a multiple of 32", inner);
+    PXQ_CUDA(launch_quantize_q8_0_blocks(x, blocks, rows, inner, inner, static_cast<cudaStream_t>(stream)));
+    return PXQ_OK;
+}
+
+int pxq_quantize_q8_K(const float* x, void* blocks, size_t rows, size_t inner, void* stream)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (!x || !blocks || !rows || !inner) return fail(PXQ_ERR_INVALID, "null pointer or zero size");
+    if (inner % 256) return fail(PXQ_ERR_UNSUPPORTED, "inner %zu not a multiple of 256", inner);
+    PXQ_CUDA(launch_quantize_q8_K_blocks(x, blocks, rows, inner, inner, static_cast<cudaStream_t>(stream)));
+    return PXQ_OK;
+}
+
+int pxq_decode(const void* data, uint32_t type, size_t count, float* out, void* stream)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (!data || !out || !count) return fail(PXQ_ERR_INVALID, "null pointer or zero size");
+    if (type != PXQ_TYPE_Q8_0 && type != PXQ_TYPE_Q5_K && type != PXQ_TYPE_Q6_K)
+        return fail(PXQ_ERR_UNSUPPORTED, "decode of type %u not supported", type);
+    if (count % (type == PXQ_TYPE_Q8_0 ? 32 : 256)) return fail(PXQ_ERR_INVALID, "count %zu not a whole number of blocks", count);
+    PXQ_CUDA(launch_decode(static_cast<const uint8_t*>(data), type, (int64_t)count, out, static_cast<cudaStream_t>(stream)));
+    return PXQ_OK;
+}
+
+int pxq_weight_upload(const void* bytes, int bytes_on_device, uint32_t type, size_t inner, size_t rows, const char* key,
+                      pxq_weight** out)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (!bytes || !out) return fail(PXQ_ERR_INVALID, "null bytes or out");
+    *out = nullptr;
+    if (type != PXQ_TYPE_Q8_0 && type != PXQ_TYPE_Q5_K) return fail(PXQ_ERR_UNSUPPORTED, "weight type %u not supported", type);
+    const uint64_t total = pxq_weight_bytes(inner, rows, type);
+    if (!total) return fail(PXQ_ERR_INVALID, "invalid weight shape [%zu, %zu] for type %u", inner, rows, type);
+    if (inner > 0x7fffffffu) return fail(PXQ_ERR_UNSUPPORTED, "inner %zu exceeds INT32_MAX", inner);
+    std::string k = key ? std::string(key) : std::string();
+    if (!k.empty()) {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        auto it = g_cache.find(k);
+        if (it != g_cache.end() && it->second->device == t_device) {
+            *out = it->second;
+            return PXQ_OK;
+        }
+    }
+    auto w = std::make_unique<pxq_weight>();
+    w->type = type;
+    w->inner = (int64_t)inner;
+    w->rows = (int64_t)rows;
+    w->stride = (int64_t)pxq_weight_bytes(inner, 1, type);
+    w->device = t_device;
+    w->key = k;
+    if (cudaMalloc(&w->raw, total + 64) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(PXQ_ERR_NO_MEMORY, "cannot allocate %llu bytes for weight", (unsigned long long)total);
+    }
+    PXQ_CUDA(cudaMemset(w->raw + total, 0, 64));
+    PXQ_CUDA(cudaMemcpy(w->raw, bytes, total, bytes_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
+    pxq_weight* raw = w.release();
+    if (!k.empty()) {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        g_cache[k] = raw;
+    }
+    *out = raw;
+    return PXQ_OK;
+}
+
+int pxq_weight_release(pxq_weight* w)
+{
+    if (!w) return fail(PXQ_ERR_INVALID, "null weight");
+    {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        if (!w->key.empty()) {
+            auto it = g_cache.find(w->key);
+            if (it != g_cache.end() && it->second == w) g_cache.erase(it);
+        }
+    }
+    cudaDeviceSynchronize();
+    delete w;
+    return PXQ_OK;
+}
+
+int pxq_weight_cache_clear(void)
+{
+    std::unordered_map<std::string, pxq_weight*> victims;
+    {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        victims.swap(g_cache);
+    }
+    cudaDeviceSynchronize();
+    for (auto& kv : victims) delete kv.second;
+    return PXQ_OK;
+}
+
+int pxq_matvec(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* output,
+               size_t ldy, const float* bias, void* stream)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (int rc = check_matmul_args(w, row_first, row_count, input, columns, output, ldy)) return rc;
+    return run_matvec(w, row_first, row_count, input, columns, output, ldy, bias, static_cast<cudaStream_t>(stream));
+}
+
+int pxq_gemm(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* output,
+             size_t ldy, const float* bias, void* stream)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (int rc = check_matmul_args(w, row_first, row_count, input, columns, output, ldy)) return rc;
+    return run_gemm(d, w, row_first, row_count, input, columns, output, ldy, bias, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int pxq_matmul(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* output,
+               size_t ldy, const float* bias, void* stream)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (int rc = check_matmul_args(w, row_first, row_count, input, columns, output, ldy)) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (columns <= 8) return run_matvec(w, row_first, row_count, input, columns, output, ldy, bias, s);
+    return run_gemm(d, w, row_first, row_count, input, columns, output, ldy, bias, nullptr, s);
+}
+
+int pxq_gemm_block_dots(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* dump,
+                        void* stream)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (int rc = check_matmul_args(w, row_first, row_count, input, columns, dump, row_count)) return rc;
+    return run_gemm(d, w, row_first, row_count, input, columns, dump, row_count, nullptr, dump,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int pxq_synchronize(void* stream)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    PXQ_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+    uint32_t st = 0;
+    PXQ_CUDA(cudaMemcpy(&st, d->status, 4, cudaMemcpyDeviceToHost));
+    if (st) {
+        cudaMemset(d->status, 0, 4);
+        return fail(PXQ_ERR_DEVICE_STATUS, "a kernel gave up waiting (status %u)", st);
+    }
+    return PXQ_OK;
+}
+
+int pxq_gather_shards(const float* src, size_t shards, size_t columns, size_t shard_rows, float* dst, size_t ldy, void* stream)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (!src || !dst || !shards || !columns || !shard_rows) return fail(PXQ_ERR_INVALID, "null pointer or zero size");
+    if (ldy < shards * shard_rows) return fail(PXQ_ERR_INVALID, "ldy %zu < shards*shard_rows", ldy);
+    PXQ_CUDA(launch_gather_shards(src, shards, columns, shard_rows, dst, ldy, static_cast<cudaStream_t>(stream)));
+    return PXQ_OK;
+}
+
+int pxq_quant_matmul(const unsigned char* weights, uint32_t type, const float* input, float* output, size_t rows,
+                     size_t columns, size_t inner)
+{
+    // the reference's "not handled" cases (src/kernels_quant.cpp:373-377)
+    if (type != PXQ_TYPE_Q8_0 && type != PXQ_TYPE_Q5_K && type != PXQ_TYPE_Q6_K)
+        return fail(PXQ_ERR_UNSUPPORTED, "type %u not handled", type);
+    const size_t block = type == PXQ_TYPE_Q8_0 ? 32 : 256;
+    if (!rows || !columns || !inner || inner % block || inner > 0x7fffffffu)
+        return fail(PXQ_ERR_UNSUPPORTED, "shape rows=%zu columns=%zu inner=%zu not handled", rows, columns, inner);
+    if (type == PXQ_TYPE_Q6_K) return fail(PXQ_ERR_UNSUPPORTED, "Q6_K weights are not handled by this backend yet");
+    if (!weights || !input || !output) return fail(PXQ_ERR_INVALID, "null pointer");
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    char key[96];
+    snprintf(key, sizeof(key), "host:%p:%zu:%zu:%u", (const void*)weights, rows, inner, type);
+    pxq_weight* w = nullptr;
+    if (int rc = pxq_weight_upload(weights, 0, type, inner, rows, key, &w)) return rc;
+    if (!t_stream || t_stream_device != t_device) {
+        PXQ_CUDA(cudaStreamCreateWithFlags(&t_stream, cudaStreamNonBlocking));
+        t_stream_device = t_device;
+    }
+    cudaStream_t s = t_stream;
+    float* xin = nullptr;
+    float* yout = nullptr;
+    const size_t xbytes = columns * inner * sizeof(float), ybytes = columns * rows * sizeof(float);
+    if (cudaMallocAsync(&xin, xbytes, s) != cudaSuccess || cudaMallocAsync(&yout, ybytes, s) != cudaSuccess) {
+        cudaGetLastError();
+        if (xin) cudaFreeAsync(xin, s);
+        return fail(PXQ_ERR_NO_MEMORY, "cannot allocate device buffers");
+    }
+    int rc = PXQ_OK;
+    cudaError_t e = cudaMemcpyAsync(xin, input, xbytes, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) {
+        rc = columns <= 8 ? run_matvec(w, 0, rows, xin, columns, yout, rows, nullptr, s)
+                          : run_gemm(d, w, 0, rows, xin, columns, yout, rows, nullptr, nullptr, s);
+        if (!rc) e = cudaMemcpyAsync(output, yout, ybytes, cudaMemcpyDeviceToHost, s);
+    }
+    cudaFreeAsync(xin, s);
+    cudaFreeAsync(yout, s);
+    if (e != cudaSuccess) return fail(PXQ_ERR_CUDA, "copy failed: %s", cudaGetErrorString(e));
+    if (rc) return rc;
+    return pxq_synchronize(s);
+}
+
+}  // extern "C"

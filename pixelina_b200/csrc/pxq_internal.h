@@ -1,0 +1,71 @@
+// pxq_internal.h -- declarations shared by the pxq translation units.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+namespace pxq {
+
+constexpr int kQK8_0 = 32;        // Q8_0 block length
+constexpr int kQKK = 256;         // K-quant super-block length
+constexpr int kQ8_0Bytes = 34;    // {fp16 d; int8 qs[32]}
+constexpr int kQ8KBytes = 292;    // {f32 d; int8 qs[256]; int16 bsums[16]}
+constexpr int kQ5KBytes = 176;    // {fp16 d, dmin; u8 scales[12]; u8 qh[32]; u8 qs[128]}
+constexpr int kQ6KBytes = 210;    // {u8 ql[128]; u8 qh[64]; i8 scales[16]; fp16 d}
+constexpr uint32_t kTypeQ8_0 = 8;
+constexpr uint32_t kTypeQ5_K = 13;
+constexpr uint32_t kTypeQ6_K = 14;
+
+// ---- quantize.cu -----------------------------------------------------------
+// GGUF-format activation blocks (bit-exact with the reference quantizers).
+cudaError_t launch_quantize_q8_0_blocks(const float* x, void* y, int64_t rows, int64_t inner, int64_t ldx, cudaStream_t s);
+cudaError_t launch_quantize_q8_K_blocks(const float* x, void* y, int64_t rows, int64_t inner, int64_t ldx, cudaStream_t s);
+// Tensor-core operand formats for the GEMM (same rounding, different layout):
+//   xq  fp16 [rows][inner]: the int8 quants as exact fp16 values
+//   dxT fp32 [inner/block][ldd]: per-block scale, block-major (TMA-friendly)
+//   amin fp16 [rows][inner/256*16] (Q8_K only): split 32-element sums for the
+//        Q5_K min term, (hi_j, lo_j) with bsum2_j = 64*hi_j + lo_j
+cudaError_t launch_quantize_q8_0_operand(const float* x, __half* xq, float* dxT, int64_t rows, int64_t inner, int64_t ldx,
+                                         int64_t ldd, cudaStream_t s);
+cudaError_t launch_quantize_q8_K_operand(const float* x, __half* xq, float* dxT, __half* amin, int64_t rows, int64_t inner,
+                                         int64_t ldx, int64_t ldd, cudaStream_t s);
+
+// ---- repack.cu -------------------------------------------------------------
+// One-time weight repack into the GEMM operand layout (bit-exact unpack).
+cudaError_t launch_repack_q8_0(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wq, float* dwT,
+                               int64_t ldn, cudaStream_t s);
+cudaError_t launch_repack_q5_K(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wv, float* dT,
+                               float* dminT, __half* bmin, int64_t ldn, cudaStream_t s);
+
+cudaError_t launch_decode(const uint8_t* data, uint32_t type, int64_t count, float* out, cudaStream_t s);
+
+// ---- matvec.cu -------------------------------------------------------------
+// y[c*ldy + r] = dot(W row r, X row c) for c < columns <= 8, raw GGUF weights.
+cudaError_t launch_matvec(uint32_t type, const uint8_t* w, int64_t stride, int64_t rows, int64_t inner, const void* xq,
+                          int64_t columns, float* y, int64_t ldy, const float* bias, cudaStream_t s);
+
+// ---- shards.cu -------------------------------------------------------------
+cudaError_t launch_gather_shards(const float* src, int64_t shards, int64_t columns, int64_t shard_rows, float* dst,
+                                 int64_t ldy, cudaStream_t s);
+
+// ---- gemm.cu ---------------------------------------------------------------
+struct GemmOperands {
+    uint32_t type;        // kTypeQ8_0 or kTypeQ5_K
+    int64_t M, N, K;      // activation rows, view rows (output columns), inner
+    int64_t n_first;      // first weight row of the view (multiple of 4)
+    // tensor maps: 0 A operand, 1 B operand, 2 activation scales, 3 weight
+    // scales, 4 Q5_K weight dmin, 5 Q5_K activation min operand, 6 Q5_K
+    // weight min operand (unused entries may hold any valid map)
+    CUtensorMap tm[7];
+    float* y;
+    int64_t ldy;
+    const float* bias;    // may be null (indexed by view-local column)
+    float* dump;          // debug: raw per-item block dots, or null
+    uint32_t* status;     // device status word
+};
+int gemm_smem_bytes();
+cudaError_t launch_gemm(const GemmOperands& op, int num_sms, cudaStream_t s);
+
+}  // namespace pxq

@@ -1,0 +1,273 @@
+// quantize.cu -- activation quantizers, bit-exact with Pixelina's CPU path.
+//
+//   Q8_0 (32-blocks)  restates quantize_row_q8_0_ref, src/kernels_quant.cpp:120-144
+//   Q8_K (256-blocks) restates quantize_row_q8_K_ref, src/kernels_quant.cpp:80-118
+//
+// Each comes in two output layouts: the GGUF block layout (what the reference
+// produces, used by the matvec and by the parity tests) and the tensor-core
+// operand layout used by the GEMM (exact fp16 copies of the int8 quants plus
+// block-major scale planes).  Both layouts come from the same arithmetic.
+//
+// Bit-exactness rules (all arithmetic uses explicit _rn intrinsics so that
+// nvcc's default FMA contraction cannot change a rounding):
+//   * d = amax/127 and 1/d are IEEE divisions;
+//   * Q8_0 rounds x*id half away from zero (roundf) after a rounded product;
+//   * Q8_K rounds iscale*x half to even through the 1.5*2^23 bias, and the
+//     reference build evaluates `iscale*x + bias` as ONE fused multiply-add
+//     (g++ -O3 -std=c++17 contracts it; pinned by the golden vectors), so the
+//     kernel uses __fmaf_rn for that step;
+//   * the stored fp16 scale is round-to-nearest-even (F16C with
+//     _MM_FROUND_TO_NEAREST_INT).
+#include "pxq_internal.h"
+
+namespace pxq {
+namespace {
+
+__device__ __forceinline__ float round_half_away(float v)
+{
+    const float t = truncf(v);
+    const float r = __fsub_rn(v, t);  // exact: fractional part of v
+    return fabsf(r) >= 0.5f ? __fadd_rn(t, copysignf(1.0f, v)) : t;
+}
+
+__device__ __forceinline__ int8_t q8_0_quant(float x, float id)
+{
+    return static_cast<int8_t>(static_cast<int>(round_half_away(__fmul_rn(x, id))));
+}
+
+// One Q8_0 block per 8 consecutive threads, 4 elements per thread.
+// Returns (d as stored fp16, 4 quants packed little-endian).
+struct Q80Part {
+    __half d16;
+    uint32_t packed;
+    int8_t q[4];
+};
+
+__device__ __forceinline__ Q80Part q8_0_part(const float4 v)
+{
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    Q80Part p;
+    p.d16 = __float2half_rn(d);
+    p.q[0] = q8_0_quant(v.x, id);
+    p.q[1] = q8_0_quant(v.y, id);
+    p.q[2] = q8_0_quant(v.z, id);
+    p.q[3] = q8_0_quant(v.w, id);
+    p.packed = (uint32_t)(uint8_t)p.q[0] | ((uint32_t)(uint8_t)p.q[1] << 8) | ((uint32_t)(uint8_t)p.q[2] << 16) |
+               ((uint32_t)(uint8_t)p.q[3] << 24);
+    return p;
+}
+
+// grid-stride over groups of 4 elements; all 32 lanes of a warp stay active
+// (padding lanes compute on zeros and store nothing) so the shuffles are full.
+__global__ void k_quantize_q8_0_blocks(const float* __restrict__ x, uint8_t* __restrict__ y, int64_t rows, int64_t inner,
+                                       int64_t ldx)
+{
+    const int64_t quads_per_row = inner / 4;
+    const int64_t total = rows * quads_per_row;
+    const int64_t nb = inner / kQK8_0;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < total; base += stride) {
+        const int64_t i = base + threadIdx.x;
+        const bool live = i < total;
+        const int64_t row = live ? i / quads_per_row : 0;
+        const int64_t quad = live ? i % quads_per_row : 0;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (live) v = *reinterpret_cast<const float4*>(x + row * ldx + quad * 4);
+        const Q80Part p = q8_0_part(v);
+        if (!live) continue;
+        const int64_t blk = quad / 8;
+        const int t = (int)(quad % 8);
+        uint8_t* out = y + (row * nb + blk) * kQ8_0Bytes;
+        // qs start at byte 2 of the 34-byte block: 2-byte aligned stores only
+        uint16_t* q16 = reinterpret_cast<uint16_t*>(out + 2 + 4 * t);
+        q16[0] = (uint16_t)(p.packed & 0xffffu);
+        q16[1] = (uint16_t)(p.packed >> 16);
+        if (t == 0) *reinterpret_cast<__half*>(out) = p.d16;
+    }
+}
+
+__global__ void k_quantize_q8_0_operand(const float* __restrict__ x, __half* __restrict__ xq, float* __restrict__ dxT,
+                                        int64_t rows, int64_t inner, int64_t ldx, int64_t ldd)
+{
+    const int64_t quads_per_row = inner / 4;
+    const int64_t total = rows * quads_per_row;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < total; base += stride) {
+        const int64_t i = base + threadIdx.x;
+        const bool live = i < total;
+        const int64_t row = live ? i / quads_per_row : 0;
+        const int64_t quad = live ? i % quads_per_row : 0;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (live) v = *reinterpret_cast<const float4*>(x + row * ldx + quad * 4);
+        const Q80Part p = q8_0_part(v);
+        if (!live) continue;
+        __half2 h01 = __halves2half2(__int2half_rn(p.q[0]), __int2half_rn(p.q[1]));
+        __half2 h23 = __halves2half2(__int2half_rn(p.q[2]), __int2half_rn(p.q[3]));
+        uint2 packed;
+        packed.x = *reinterpret_cast<uint32_t*>(&h01);
+        packed.y = *reinterpret_cast<uint32_t*>(&h23);
+        *reinterpret_cast<uint2*>(xq + row * inner + quad * 4) = packed;
+        if ((quad & 7) == 0) dxT[(quad / 8) * ldd + row] = __half2float(p.d16);
+    }
+}
+
+// ---- Q8_K: one warp per 256-block, 8 consecutive elements per lane ----------
+
+struct Q8KWarp {
+    float d;        // stored fp32 scale (1/iscale, or 0 for an all-zero block)
+    int8_t q[8];    // this lane's 8 quants
+};
+
+__device__ __forceinline__ Q8KWarp q8_K_warp(const float* __restrict__ src, uint32_t lane)
+{
+    const float4 a = *reinterpret_cast<const float4*>(src + lane * 8);
+    const float4 b = *reinterpret_cast<const float4*>(src + lane * 8 + 4);
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    // first element (in index order) with the largest |x|: strict '>' scan
+    float amax = 0.0f, vmax = 0.0f;
+    int idx = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float ax = fabsf(v[j]);
+        if (ax > amax) {
+            amax = ax;
+            vmax = v[j];
+            idx = (int)lane * 8 + j;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, amax, o);
+        const float ov = __shfl_xor_sync(0xffffffffu, vmax, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (oa > amax || (oa == amax && oi < idx)) {
+            amax = oa;
+            vmax = ov;
+            idx = oi;
+        }
+    }
+    Q8KWarp r;
+    if (amax == 0.0f) {
+        r.d = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) r.q[j] = 0;
+        return r;
+    }
+    const float iscale = __fdiv_rn(-127.0f, vmax);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float biased = __fmaf_rn(iscale, v[j], 12582912.0f);
+        const int bits = __float_as_int(biased);
+        const int q = (bits & 0x007fffff) - 0x00400000;
+        r.q[j] = (int8_t)(q < 127 ? q : 127);
+    }
+    r.d = __fdiv_rn(1.0f, iscale);
+    return r;
+}
+
+__global__ void k_quantize_q8_K_blocks(const float* __restrict__ x, uint8_t* __restrict__ y, int64_t rows, int64_t inner,
+                                       int64_t ldx)
+{
+    const uint32_t lane = threadIdx.x & 31u;
+    const int64_t nsb = inner / kQKK;
+    const int64_t total = rows * nsb;
+    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t w = (((int64_t)blockIdx.x * blockDim.x) >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
+        const int64_t row = w / nsb, sb = w % nsb;
+        const Q8KWarp r = q8_K_warp(x + row * ldx + sb * kQKK, lane);
+        uint8_t* out = y + w * kQ8KBytes;
+        uint32_t lo = 0, hi = 0;
+        int sum8 = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) lo |= (uint32_t)(uint8_t)r.q[j] << (8 * j);
+#pragma unroll
+        for (int j = 0; j < 4; j++) hi |= (uint32_t)(uint8_t)r.q[4 + j] << (8 * j);
+#pragma unroll
+        for (int j = 0; j < 8; j++) sum8 += r.q[j];
+        *reinterpret_cast<uint32_t*>(out + 4 + lane * 8) = lo;
+        *reinterpret_cast<uint32_t*>(out + 4 + lane * 8 + 4) = hi;
+        const int sum16 = sum8 + __shfl_xor_sync(0xffffffffu, sum8, 1);  // 16-element group = lane pair
+        if ((lane & 1u) == 0) *reinterpret_cast<int16_t*>(out + 4 + kQKK + lane) = (int16_t)sum16;
+        if (lane == 0) *reinterpret_cast<float*>(out) = r.d;
+    }
+}
+
+__global__ void k_quantize_q8_K_operand(const float* __restrict__ x, __half* __restrict__ xq, float* __restrict__ dxT,
+                                        __half* __restrict__ amin, int64_t rows, int64_t inner, int64_t ldx, int64_t ldd)
+{
+    const uint32_t lane = threadIdx.x & 31u;
+    const int64_t nsb = inner / kQKK;
+    const int64_t total = rows * nsb;
+    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t w = (((int64_t)blockIdx.x * blockDim.x) >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
+        const int64_t row = w / nsb, sb = w % nsb;
+        const Q8KWarp r = q8_K_warp(x + row * ldx + sb * kQKK, lane);
+        __half h[8];
+        int sum8 = 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            h[j] = __int2half_rn(r.q[j]);
+            sum8 += r.q[j];
+        }
+        *reinterpret_cast<uint4*>(xq + row * inner + sb * kQKK + lane * 8) = *reinterpret_cast<uint4*>(h);
+        // 32-element sub-block sums (lanes 4j..4j+3), split exactly for fp16
+        int s32 = sum8 + __shfl_xor_sync(0xffffffffu, sum8, 1);
+        s32 += __shfl_xor_sync(0xffffffffu, s32, 2);
+        if ((lane & 3u) == 0) {
+            const int j = (int)(lane >> 2);
+            const int hi = s32 >> 6;            // floor(s32 / 64)
+            const int lo = s32 - (hi << 6);     // 0..63
+            __half2 pair = __halves2half2(__int2half_rn(hi), __int2half_rn(lo));
+            *reinterpret_cast<__half2*>(amin + row * (nsb * 16) + sb * 16 + 2 * j) = pair;
+        }
+        if (lane == 0) dxT[sb * ldd + row] = r.d;
+    }
+}
+
+int grid_for(int64_t work_items, int threads)
+{
+    int64_t blocks = (work_items + threads - 1) / threads;
+    if (blocks < 1) blocks = 1;
+    if (blocks > 148 * 64) blocks = 148 * 64;
+    return (int)blocks;
+}
+
+}  // namespace
+
+cudaError_t launch_quantize_q8_0_blocks(const float* x, void* y, int64_t rows, int64_t inner, int64_t ldx, cudaStream_t s)
+{
+    const int threads = 256;
+    k_quantize_q8_0_blocks<<<grid_for(rows * inner / 4, threads), threads, 0, s>>>(x, static_cast<uint8_t*>(y), rows, inner, ldx);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_q8_K_blocks(const float* x, void* y, int64_t rows, int64_t inner, int64_t ldx, cudaStream_t s)
+{
+    const int threads = 256;
+    k_quantize_q8_K_blocks<<<grid_for(rows * (inner / kQKK) * 32, threads), threads, 0, s>>>(x, static_cast<uint8_t*>(y), rows,
+                                                                                            inner, ldx);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_q8_0_operand(const float* x, __half* xq, float* dxT, int64_t rows, int64_t inner, int64_t ldx,
+                                         int64_t ldd, cudaStream_t s)
+{
+    const int threads = 256;
+    k_quantize_q8_0_operand<<<grid_for(rows * inner / 4, threads), threads, 0, s>>>(x, xq, dxT, rows, inner, ldx, ldd);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_q8_K_operand(const float* x, __half* xq, float* dxT, __half* amin, int64_t rows, int64_t inner,
+                                         int64_t ldx, int64_t ldd, cudaStream_t s)
+{
+    const int threads = 256;
+    k_quantize_q8_K_operand<<<grid_for(rows * (inner / kQKK) * 32, threads), threads, 0, s>>>(x, xq, dxT, amin, rows, inner,
+                                                                                             ldx, ldd);
+    return cudaGetLastError();
+}
+
+}  // namespace pxq

@@ -1,0 +1,247 @@
+"""Python host mirror of the pxq C ABI (include/pxq.h).
+
+The operator surface follows Pixelina's matmul boundary (paths within the
+Pixelina source tree):
+
+* ``quant_matmul``   -- cpu_quant_matmul (src/kernels_quant.cpp:369-412):
+  host buffers in, host buffer out, ``(handled, output)`` like its bool.
+* ``Weight``         -- a device-resident GGUF tensor, the Vulkan backend's
+  weight cache entry (src/backend_vulkan.cpp:742-758).
+* ``matmul``         -- cpu_matmul / vulkan_matmul (src/backend_cpu.cpp:103,
+  src/backend_vulkan.cpp:1083) on device tensors, with the row-range view of
+  tensor_linear_rows (src/tensor.cpp:529-544) and the bias of tensor_linear
+  (src/tensor.cpp:156-172).
+* ``quantize_q8_0`` / ``quantize_q8_K`` / ``decode`` -- the reference's
+  quantizers and cpu_decode on device buffers.
+
+torch is used only for device memory and streams.  Everything computes in
+libpxq.so; importing this module on a machine without the built library or
+without a B200 raises instead of falling back to any CPU path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from typing import Optional
+
+import numpy as np
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libpxq.so")
+
+OK = 0
+ERR_INVALID = 1
+ERR_UNSUPPORTED = 2
+ERR_CUDA = 3
+ERR_NO_MEMORY = 4
+ERR_NO_DEVICE = 5
+ERR_DEVICE_STATUS = 6
+
+TYPE_Q8_0 = 8
+TYPE_Q5_K = 13
+TYPE_Q6_K = 14
+BLOCK_ELEMS = {TYPE_Q8_0: 32, TYPE_Q5_K: 256, TYPE_Q6_K: 256}
+BLOCK_BYTES = {TYPE_Q8_0: 34, TYPE_Q5_K: 176, TYPE_Q6_K: 210}
+Q8_0_BYTES = 34
+Q8_K_BYTES = 292
+
+# name -> (restype, argtypes); must list exactly the functions of include/pxq.h
+_vp, _sz, _u32, _u64, _i = C.c_void_p, C.c_size_t, C.c_uint32, C.c_uint64, C.c_int
+SIGNATURES = {
+    "pxq_version": (_i, []),
+    "pxq_last_error": (C.c_char_p, []),
+    "pxq_init": (_i, [_i]),
+    "pxq_weight_bytes": (_u64, [_u64, _u64, _u32]),
+    "pxq_quantize_q8_0": (_i, [_vp, _vp, _sz, _sz, _vp]),
+    "pxq_quantize_q8_K": (_i, [_vp, _vp, _sz, _sz, _vp]),
+    "pxq_decode": (_i, [_vp, _u32, _sz, _vp, _vp]),
+    "pxq_weight_upload": (_i, [_vp, _i, _u32, _sz, _sz, C.c_char_p, C.POINTER(_vp)]),
+    "pxq_weight_release": (_i, [_vp]),
+    "pxq_weight_cache_clear": (_i, []),
+    "pxq_matmul": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _sz, _vp, _vp]),
+    "pxq_matvec": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _sz, _vp, _vp]),
+    "pxq_gemm": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _sz, _vp, _vp]),
+    "pxq_quant_matmul": (_i, [_vp, _u32, _vp, _vp, _sz, _sz, _sz]),
+    "pxq_synchronize": (_i, [_vp]),
+    "pxq_gather_shards": (_i, [_vp, _sz, _sz, _sz, _vp, _sz, _vp]),
+    "pxq_gemm_block_dots": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _vp]),
+}
+
+
+class PxqError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"pxq error {code}: {msg}")
+        self.code = code
+
+
+_lib = None
+
+
+def load(path: str = LIB_PATH):
+    """Load libpxq.so (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise ImportError(f"{path} is missing: build it with `python -c 'import __graft_entry__ as g; g.build()'`")
+    lib = C.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        f = getattr(lib, name)
+        f.restype = res
+        f.argtypes = args
+    _lib = lib
+    return lib
+
+
+def _check(rc: int) -> None:
+    if rc != OK:
+        raise PxqError(rc, load().pxq_last_error().decode(errors="replace"))
+
+
+def last_error() -> str:
+    return load().pxq_last_error().decode(errors="replace")
+
+
+def weight_bytes(inner: int, rows: int, wtype: int) -> int:
+    return int(load().pxq_weight_bytes(inner, rows, wtype))
+
+
+# ------------------------------------------------------------ device side ---
+
+def _torch():
+    import torch  # noqa: WPS433 (device memory and streams only)
+
+    return torch
+
+
+def _stream_ptr(stream=None):
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def _ptr(t) -> C.c_void_p:
+    return C.c_void_p(t.data_ptr()) if t is not None else C.c_void_p(0)
+
+
+def init(device: int = 0) -> None:
+    torch = _torch()
+    torch.cuda.set_device(device)
+    _check(load().pxq_init(device))
+
+
+def quantize_q8_0(x, stream=None):
+    """fp32 [rows, inner] cuda tensor -> uint8 [rows, inner/32*34] GGUF Q8_0 blocks."""
+    torch = _torch()
+    x = x.contiguous()
+    rows, inner = x.shape
+    out = torch.empty((rows, inner // 32 * Q8_0_BYTES), dtype=torch.uint8, device=x.device)
+    _check(load().pxq_quantize_q8_0(_ptr(x), _ptr(out), rows, inner, _stream_ptr(stream)))
+    return out
+
+
+def quantize_q8_K(x, stream=None):
+    """fp32 [rows, inner] cuda tensor -> uint8 [rows, inner/256*292] Q8_K blocks."""
+    torch = _torch()
+    x = x.contiguous()
+    rows, inner = x.shape
+    out = torch.empty((rows, inner // 256 * Q8_K_BYTES), dtype=torch.uint8, device=x.device)
+    _check(load().pxq_quantize_q8_K(_ptr(x), _ptr(out), rows, inner, _stream_ptr(stream)))
+    return out
+
+
+def decode(data, wtype: int, count: int, stream=None):
+    torch = _torch()
+    out = torch.empty(count, dtype=torch.float32, device=data.device)
+    _check(load().pxq_decode(_ptr(data), wtype, count, _ptr(out), _stream_ptr(stream)))
+    return out
+
+
+class Weight:
+    """A GGUF weight tensor resident on the current device."""
+
+    def __init__(self, data, wtype: int, inner: int, rows: int, key: Optional[str] = None):
+        lib = load()
+        self.wtype, self.inner, self.rows = wtype, inner, rows
+        handle = C.c_void_p()
+        if hasattr(data, "data_ptr"):  # torch tensor (host or device)
+            on_dev = 1 if data.is_cuda else 0
+            ptr = C.c_void_p(data.data_ptr())
+            self._keep = data
+        else:
+            arr = np.ascontiguousarray(data, dtype=np.uint8)
+            on_dev, ptr = 0, arr.ctypes.data_as(C.c_void_p)
+            self._keep = arr
+        kb = key.encode() if key else None
+        _check(lib.pxq_weight_upload(ptr, on_dev, wtype, inner, rows, kb, C.byref(handle)))
+        self.handle = handle
+        self._keep = None
+
+    def release(self) -> None:
+        if self.handle:
+            _check(load().pxq_weight_release(self.handle))
+            self.handle = C.c_void_p()
+
+
+def matmul(w: Weight, x, row_first: int = 0, row_count: Optional[int] = None, bias=None, out=None, ldy: Optional[int] = None,
+           path: str = "auto", stream=None):
+    """Y[c, r] = sum_k x[c, k] * W[row_first + r, k] (+ bias[r]) on the device."""
+    torch = _torch()
+    x = x.contiguous()
+    columns, inner = x.shape
+    if inner != w.inner:
+        raise ValueError(f"input has {inner} features, weight expects {w.inner}")
+    rc = w.rows - row_first if row_count is None else row_count
+    if out is None:
+        out = torch.empty((columns, rc), dtype=torch.float32, device=x.device)
+        ldy = rc
+    elif ldy is None:
+        ldy = out.stride(0)
+    fn = {"auto": load().pxq_matmul, "matvec": load().pxq_matvec, "gemm": load().pxq_gemm}[path]
+    _check(fn(w.handle, row_first, rc, _ptr(x), columns, _ptr(out), ldy, _ptr(bias), _stream_ptr(stream)))
+    return out
+
+
+def gemm_block_dots(w: Weight, x, row_first: int = 0, row_count: Optional[int] = None, stream=None):
+    """Exact per-block dots from the tensor-core GEMM: [items, columns, rows]."""
+    torch = _torch()
+    x = x.contiguous()
+    columns, inner = x.shape
+    rc = w.rows - row_first if row_count is None else row_count
+    items = inner // 32 if w.wtype == TYPE_Q8_0 else 5 * (inner // 256)
+    dump = torch.zeros((items, columns, rc), dtype=torch.float32, device=x.device)
+    _check(load().pxq_gemm_block_dots(w.handle, row_first, rc, _ptr(x), columns, _ptr(dump), _stream_ptr(stream)))
+    return dump
+
+
+def gather_shards(src, shards: int, columns: int, shard_rows: int, out=None, stream=None):
+    torch = _torch()
+    if out is None:
+        out = torch.empty((columns, shards * shard_rows), dtype=torch.float32, device=src.device)
+    _check(load().pxq_gather_shards(_ptr(src), shards, columns, shard_rows, _ptr(out), out.stride(0), _stream_ptr(stream)))
+    return out
+
+
+def synchronize(stream=None) -> None:
+    _check(load().pxq_synchronize(_stream_ptr(stream)))
+
+
+# --------------------------------------------------------------- host side ---
+
+def quant_matmul(weights: np.ndarray, wtype: int, x: np.ndarray, rows: int):
+    """cpu_quant_matmul with host buffers: returns (handled, Y[columns, rows])."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    columns, inner = x.shape
+    w = np.ascontiguousarray(weights, dtype=np.uint8)
+    y = np.empty((columns, rows), dtype=np.float32)
+    rc = load().pxq_quant_matmul(w.ctypes.data_as(C.c_void_p), wtype, x.ctypes.data_as(C.c_void_p),
+                                 y.ctypes.data_as(C.c_void_p), rows, columns, inner)
+    if rc == ERR_UNSUPPORTED:
+        return False, y
+    _check(rc)
+    return True, y
+
+
+def quant_matmul_ptr(weights_ptr: int, wtype: int, x_ptr: int, y_ptr: int, rows: int, columns: int, inner: int) -> int:
+    """Raw-pointer form of pxq_quant_matmul (host addresses); returns the status."""
+    return int(load().pxq_quant_matmul(C.c_void_p(weights_ptr), wtype, C.c_void_p(x_ptr), C.c_void_p(y_ptr), rows, columns,
+                                       inner))
