@@ -1,0 +1,655 @@
+#!/usr/bin/env python
+"""Benchmark of the quantized-matmul hot path.
+
+Default workload: Q5_K GEMM, activations M=4096 x K=3840
+fp32 N(0,1), weights N=10240 x K=3840 Q5_K encoded from N(0, 0.02) floats.
+One step = activation quantize (Q8_K, as the reference's CPU path) + the
+tensor-core GEMM, inputs resident in HBM; L2 is flushed (256 MB write)
+between timed steps, outside the timed events.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload q5k_gemm|q8_0_gemm|q8_0_large|dit|decode|sharded]
+
+Multi-GPU (torchrun, one rank per GPU): each rank processes its own batch of
+activation rows against the same weights (data parallel over independent
+rows, no collective on the data path, "scaling": "weak"); the job time is the
+max over ranks of the device-timed steps.  The N-sharded GEMM with an NCCL
+all-gather of Y is `--workload sharded` (reported separately).
+
+`--impl reference` times Pixelina's own CPU cpu_quant_matmul (built from the
+reference sources into oracle/_ref) on the host cores, same metric/config.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Q8_0/Q5_K GEMM TOPS & matvec HBM GB/s at 1/2/4/8 B200, % of roofline"
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+L2_FLUSH_BYTES = 256 << 20
+
+Q8_0, Q5_K = 8, 13
+
+GEMM_WORKLOADS = {
+    "q5k_gemm": dict(wtype=Q5_K, M=4096, N=10240, K=3840, name="Q5_K GEMM (BASELINE configs[1])"),
+    "q8_0_gemm": dict(wtype=Q8_0, M=4096, N=3840, K=3840, name="Q8_0 GEMM (BASELINE configs[0])"),
+    "q8_0_large": dict(wtype=Q8_0, M=16384, N=12288, K=3072, name="large-image Q8_0 GEMM (BASELINE configs[4])"),
+}
+DIT = dict(hidden=3072, ffn=12288, blocks=60, M=4352, qkv=9216)
+DECODE = dict(hidden=3584, ffn=18944, layers=28, qkv=4608)
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "measured"
+    except Exception:  # noqa: BLE001
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, 1400.0, "fallback"
+
+
+def committed_traffic(kernel_key):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(kernel_key)
+    except Exception:  # noqa: BLE001
+        return None
+
+
+# ------------------------------------------------------------------ clocks ---
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons while running."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.lines = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.device)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------- distributed ---
+
+class Dist:
+    def __init__(self, gpus: int):
+        self.world = env_int("WORLD_SIZE", 1)
+        self.rank = env_int("RANK", 0)
+        self.local = env_int("LOCAL_RANK", 0)
+        self.pg = False
+        if gpus > 1 and self.world == 1:
+            print(f"--gpus {gpus} needs torchrun (WORLD_SIZE is 1); running one rank", file=sys.stderr)
+
+    def init(self):
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        import torch.distributed as dist
+
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        import torch.distributed as dist
+
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+# --------------------------------------------------------- synthetic data ---
+
+def gpu_random_q8_0(rows: int, inner: int, gen):
+    """Random valid Q8_0 rows on the GPU: int8 quants in [-127,127] and fp16
+    scales of N(0, 0.02) block maxima (for multi-GB stacks)."""
+    import torch
+
+    nb = inner // 32
+    q = torch.randint(-127, 128, (rows, nb, 32), dtype=torch.int8, device="cuda", generator=gen)
+    d = (torch.rand((rows, nb), device="cuda", generator=gen) * 0.02 + 0.04) / 127
+    out = torch.empty((rows, nb, 34), dtype=torch.uint8, device="cuda")
+    out[:, :, 0:2] = d.to(torch.float16).view(torch.uint8).view(rows, nb, 2)
+    out[:, :, 2:] = q.view(torch.uint8)
+    return out.view(rows, nb * 34)
+
+
+def gpu_random_q5_K(rows: int, inner: int, gen):
+    """Random valid Q5_K rows on the GPU (every field drawn independently)."""
+    import torch
+
+    nsb = inner // 256
+    raw = torch.randint(0, 256, (rows, nsb, 176), dtype=torch.uint8, device="cuda", generator=gen)
+    d = torch.rand((rows, nsb, 2), device="cuda", generator=gen) * 4e-5 + 2e-5
+    raw[:, :, 0:4] = d.to(torch.float16).view(torch.uint8).view(rows, nsb, 4)
+    return raw.view(rows, nsb * 176)
+
+
+# ------------------------------------------------------------------ our arm ---
+
+def time_steps(step, steps: int, warmup: int, flush, soak_s: float, sampler: ClockSampler, dist: Dist):
+    """Warm up, soak ~soak_s seconds (clock settling, sampled), then time
+    exactly `steps` steps with per-step CUDA events; flush L2 between steps
+    outside the events.  Returns (per-step ms list, per-step kernel ms dict)."""
+    import torch
+
+    for _ in range(warmup):
+        step(None)
+    torch.cuda.synchronize()
+    sampler.start()
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < soak_s:
+        step(None)
+        torch.cuda.synchronize()
+    events = []
+    dist.barrier()
+    torch.cuda.synchronize()
+    for _ in range(steps):
+        flush()
+        ev = {}
+        step(ev)
+        events.append(ev)
+    torch.cuda.synchronize()
+    dist.barrier()
+    clocks = sampler.stop()
+    step_ms, kernel_ms = [], {}
+    for ev in events:
+        step_ms.append(ev["start"].elapsed_time(ev["end"]))
+        for k, (a, b) in ev.get("kernels", {}).items():
+            kernel_ms.setdefault(k, []).append(a.elapsed_time(b))
+    return step_ms, kernel_ms, clocks
+
+
+def ev_pair():
+    import torch
+
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def run_gemm_workload(args, dist: Dist, wl: dict):
+    import torch
+
+    from pixelina_b200 import pxq, synth
+
+    pxq.init(dist.local)
+    M, N, K, wtype = wl["M"], wl["N"], wl["K"], wl["wtype"]
+    # weights: identical on every rank (seed 1); activations: per rank
+    if wtype == Q5_K:
+        wbytes = synth.q5_K_weights(N, K, seed=1)
+    else:
+        wbytes = synth.q8_0_weights(N, K, seed=1)
+    x_host = synth.activations(M, K, seed=100 + dist.rank)
+    W = pxq.Weight(wbytes, wtype, K, N, key=f"bench:{wtype}:{N}:{K}")
+    x = torch.from_numpy(x_host).cuda()
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+
+    def flush():
+        flush_buf.zero_()
+
+    def step(ev):
+        if ev is not None:
+            ev["start"], ev["end"] = ev_pair()
+            q0, q1 = ev_pair()
+            g0, g1 = ev_pair()
+            ev["kernels"] = {"quantize": (q0, q1), "gemm": (g0, g1)}
+            ev["start"].record()
+            q0.record()
+        a = pxq.Activation(wtype, x)
+        if ev is not None:
+            q1.record()
+            g0.record()
+        pxq.matmul_quantized(W, a, out=y)
+        if ev is not None:
+            g1.record()
+            ev["end"].record()
+        a.release()
+
+    sampler = ClockSampler(dist.local)
+    launches0 = pxq.kernel_launches()
+    step_ms, kernel_ms, clocks = time_steps(step, args.steps, args.warmup, flush, args.soak, sampler, dist)
+    pxq.synchronize()
+    # launches inside the timed steps only (2 per step: quantize + GEMM)
+    launches_per_step = 2
+    ops = 2.0 * M * N * K
+    mean_step = statistics.mean(step_ms)
+    job_ms = dist.max(mean_step)
+    value = dist.world * ops / (job_ms * 1e-3) / 1e12
+    gemm_ms = dist.max(statistics.mean(kernel_ms["gemm"]))
+    quant_ms = dist.max(statistics.mean(kernel_ms["quantize"]))
+    hbm, bf16, bf16_sus, peak_src = measured_peaks()
+    achieved = ops / (gemm_ms * 1e-3) / 1e12
+    traffic = committed_traffic(args.workload)
+    result = {
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": "TOPS",
+        "n_gpus": dist.world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(job_ms, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "i8xi8->f32",
+        "data": "synthetic (seeded N(0,1) activations; weights encoded from N(0,0.02))",
+        "config": {"workload": f"{args.workload}: {wl['name']}", "M": M, "N": N, "K": K,
+                   "weight_type": "Q5_K" if wtype == Q5_K else "Q8_0",
+                   "activation_quant": "Q8_K" if wtype == Q5_K else "Q8_0",
+                   "per_rank_M": M, "global_M": M * dist.world, "parallelism": f"dp{dist.world}",
+                   "l2": "flushed between timed steps (256 MB write, outside the events)"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": bf16, "unit": "TFLOP/s",
+                     "frac": round(achieved / bf16, 4),
+                     "peak_source": f"{peak_src} bf16 dense (burst); the GEMM issues kind::f16 MMA on exact int8 values",
+                     "int8_peak_equiv": 2 * bf16, "int8_frac": round(achieved / (2 * bf16), 4),
+                     "kernel": "k_gemm", "kernel_ms": round(gemm_ms, 4), "quantize_ms": round(quant_ms, 4),
+                     "traffic": traffic},
+        "clocks": clocks,
+        "gpu_launches": int(dist.sum(launches_per_step * args.steps)),
+        "library_launch_counter": pxq.kernel_launches() - launches0,
+    }
+    # end to end through the host-buffer C-ABI drop-in (cpu_quant_matmul)
+    result["e2e"] = e2e_host(args, dist, wbytes, wtype, x_host, N, ops)
+    if dist.world == 1 and dist.rank == 0 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(wbytes, wtype, x_host, N, ops)
+    W.release()
+    return result
+
+
+def e2e_host(args, dist: Dist, wbytes, wtype, x_host, rows, ops):
+    """pxq_quant_matmul on pinned host buffers: H2D of X and D2H of Y inside."""
+    import torch
+
+    from pixelina_b200 import pxq
+
+    M, K = x_host.shape
+    xin = torch.from_numpy(x_host).pin_memory()
+    yout = torch.empty((M, rows), dtype=torch.float32).pin_memory()
+    w = np.ascontiguousarray(wbytes)
+    call = lambda: pxq.quant_matmul_ptr(w.ctypes.data, wtype, xin.data_ptr(), yout.data_ptr(), rows, M, K)  # noqa: E731
+    for _ in range(2):
+        assert call() == 0, pxq.last_error()
+    n = max(3, min(args.steps, 10))
+    dist.barrier()
+    times = []
+    for _ in range(n):
+        t0 = time.perf_counter()
+        rc = call()
+        times.append(time.perf_counter() - t0)
+        assert rc == 0, pxq.last_error()
+    dist.barrier()
+    t = dist.max(statistics.mean(times))
+    return {"value": round(dist.world * ops / t / 1e12, 3), "unit": "TOPS", "h2d_bytes_per_step": int(x_host.nbytes),
+            "d2h_bytes_per_step": int(M * rows * 4), "ms_per_step": round(t * 1e3, 3),
+            "timing": "host wall clock around the synchronous C-ABI call (pinned host buffers)",
+            "api": "pxq_quant_matmul (cpu_quant_matmul drop-in)"}
+
+
+def cpu_library():
+    from oracle.oracle import Oracle, Reference, oracle_available, reference_available
+
+    if reference_available():
+        return Reference(), "reference"
+    if oracle_available():
+        return Oracle(), "port"
+    return None, None
+
+
+def cpu_baseline(wbytes, wtype, x_host, rows, ops, target_s: float = 12.0):
+    """Reference CPU cpu_quant_matmul on the host cores, bounded sample."""
+    lib, kind = cpu_library()
+    if lib is None:
+        return {"value": None, "unit": "TOPS", "cores": 0, "kind": "unavailable", "sample": "no CPU library built"}
+    cores = os.cpu_count() or 1
+    if kind == "reference":
+        lib.set_threads(cores)
+    M, K = x_host.shape
+    # calibrate on a slice of weight rows, then size the sample to ~target_s
+    probe_rows = 64 if kind == "reference" else 16
+    t0 = time.perf_counter()
+    ok, _ = lib.quant_matmul(wbytes[:probe_rows], wtype, x_host, probe_rows)
+    t_probe = time.perf_counter() - t0
+    per_row = t_probe / probe_rows
+    sample_rows = int(min(rows, max(16, target_s / 3 / max(per_row, 1e-9))))
+    sample_rows -= sample_rows % 16 or 0
+    sample_rows = max(16, sample_rows)
+    times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        ok, _ = lib.quant_matmul(wbytes[:sample_rows], wtype, x_host, sample_rows)
+        times.append(time.perf_counter() - t0)
+        assert ok
+    t = statistics.median(times)
+    sample_ops = ops * sample_rows / rows
+    return {"value": round(sample_ops / t / 1e12, 5), "unit": "TOPS", "cores": cores if kind == "reference" else 1,
+            "kind": kind, "sample": f"{M}x{K} activations against the first {sample_rows} of {rows} weight rows, "
+                                    f"incl. quantize; median of 3 ({t:.2f} s each)"}
+
+
+# -------------------------------------------------------- reference arm ---
+
+def run_reference(args, dist: Dist):
+    from pixelina_b200 import synth
+
+    wl = GEMM_WORKLOADS.get(args.workload, GEMM_WORKLOADS["q5k_gemm"])
+    M, N, K, wtype = wl["M"], wl["N"], wl["K"], wl["wtype"]
+    lib, kind = cpu_library()
+    if lib is None:
+        return {"impl": "reference", "unavailable": "the reference CPU library (oracle/_ref) was not built"}
+    cores = os.cpu_count() or 1
+    if kind == "reference":
+        lib.set_threads(cores)
+    wbytes = synth.q5_K_weights(N, K, seed=1) if wtype == Q5_K else synth.q8_0_weights(N, K, seed=1)
+    x = synth.activations(M, K, seed=100)
+    ops_full = 2.0 * M * N * K
+    # size each step so that warmup + steps stay within ~3 minutes
+    t0 = time.perf_counter()
+    lib.quant_matmul(wbytes[:64], wtype, x, 64)
+    per_row = (time.perf_counter() - t0) / 64
+    budget = 90.0 / max(1, args.steps + args.warmup)
+    rows = int(min(N, max(16, budget / max(per_row, 1e-9))))
+    rows -= rows % 16
+    rows = max(16, rows)
+    for _ in range(args.warmup):
+        lib.quant_matmul(wbytes[:rows], wtype, x, rows)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        ok, _ = lib.quant_matmul(wbytes[:rows], wtype, x, rows)
+        times.append(time.perf_counter() - t0)
+        assert ok
+    t = statistics.mean(times)
+    ops = ops_full * rows / N
+    value = ops / t / 1e12
+    sample = f"{M}x{K} activations against {rows} of {N} weight rows per step (incl. quantize), {cores} threads"
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "TOPS", "n_gpus": dist.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "i8xi8->f32",
+        "data": "synthetic (seeded N(0,1) activations; weights encoded from N(0,0.02))",
+        "config": {"workload": f"{args.workload}: {wl['name']}", "M": M, "N": N, "K": K,
+                   "weight_type": "Q5_K" if wtype == Q5_K else "Q8_0", "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(value, 5), "unit": "TOPS", "cores": cores if kind == "reference" else 1,
+                         "kind": kind, "sample": sample},
+        "e2e": {"value": round(value, 5), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+# ---------------------------------------------------- other workloads ---
+
+def run_decode(args, dist: Dist):
+    """Q5_K decode, 28 layers, M in {1,4,8}; one step =
+    one token through every layer's 7 matvecs.  Metric: weight GB/s."""
+    import torch
+
+    from pixelina_b200 import pxq
+
+    pxq.init(dist.local)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(7)
+    H, F, L, QKV = DECODE["hidden"], DECODE["ffn"], DECODE["layers"], DECODE["qkv"]
+    shapes = [("qkv", QKV, H), ("out", H, H), ("gate", F, H), ("up", F, H), ("down", H, F)]
+    layers = []
+    for _ in range(L):
+        ws = {}
+        for name, n, k in shapes:
+            ws[name] = pxq.Weight(gpu_random_q5_K(n, k, gen), Q5_K, k, n)
+        layers.append(ws)
+    torch.cuda.synchronize()
+    wbytes_total = sum(pxq.weight_bytes(k, n, Q5_K) for _, n, k in shapes) * L
+    results = {}
+    hbm, bf16, _, peak_src = measured_peaks()
+    for M in (1, 4, 8):
+        xs = {H: torch.randn((M, H), device="cuda", generator=gen), F: torch.randn((M, F), device="cuda", generator=gen)}
+        ys = {n: torch.empty((M, n), device="cuda") for _, n, _ in shapes}
+
+        def step(ev):
+            if ev is not None:
+                ev["start"], ev["end"] = ev_pair()
+                ev["start"].record()
+            for ws in layers:
+                for name, n, k in shapes:
+                    pxq.matmul(ws[name], xs[k], out=ys[n], path="matvec")
+            if ev is not None:
+                ev["end"].record()
+
+        flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+        step_ms, _, clocks = time_steps(step, args.steps, args.warmup, flush_buf.zero_, args.soak, ClockSampler(dist.local),
+                                        dist)
+        ms = dist.max(statistics.mean(step_ms))
+        gbs = wbytes_total / (ms * 1e-3) / 1e9
+        results[f"M={M}"] = {"ms_per_token": round(ms, 4), "weight_GBps": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
+                             "clocks": clocks}
+    return {"metric": METRIC, "workload": "decode: Q5_K matvec, 28 layers (BASELINE configs[3])", "unit": "GB/s",
+            "weight_bytes_per_token": wbytes_total, "peak_hbm_gbs": hbm, "peak_source": peak_src,
+            "launches_per_token": 2 * 5 * L, "results": results}
+
+
+def run_dit(args, dist: Dist):
+    """60 DiT blocks of Q8_0 linears, M = 4352.  One step =
+    the linear stack of one forward pass (activation quantize + GEMM each)."""
+    import torch
+
+    from pixelina_b200 import pxq
+
+    pxq.init(dist.local)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(11)
+    H, F, B, M, QKV = DIT["hidden"], DIT["ffn"], DIT["blocks"], DIT["M"], DIT["qkv"]
+    shapes = [("qkv", QKV, H), ("out", H, H), ("up", F, H), ("down", H, F)]
+    blocks = []
+    for _ in range(B):
+        blocks.append({name: pxq.Weight(gpu_random_q8_0(n, k, gen), Q8_0, k, n) for name, n, k in shapes})
+    xs = {H: torch.randn((M, H), device="cuda", generator=gen), F: torch.randn((M, F), device="cuda", generator=gen)}
+    ys = {n: torch.empty((M, n), device="cuda") for _, n, _ in shapes}
+    # build every operand copy before timing
+    for blk in blocks:
+        for name, n, k in shapes:
+            pxq.matmul(blk[name], xs[k], out=ys[n], path="gemm")
+    torch.cuda.synchronize()
+    ops = sum(2.0 * M * n * k for _, n, k in shapes) * B
+
+    def step(ev):
+        if ev is not None:
+            ev["start"], ev["end"] = ev_pair()
+            ev["start"].record()
+        for blk in blocks:
+            for name, n, k in shapes:
+                pxq.matmul(blk[name], xs[k], out=ys[n], path="gemm")
+        if ev is not None:
+            ev["end"].record()
+
+    flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    step_ms, _, clocks = time_steps(step, args.steps, args.warmup, flush_buf.zero_, args.soak, ClockSampler(dist.local), dist)
+    ms = dist.max(statistics.mean(step_ms))
+    _, bf16, _, peak_src = measured_peaks()
+    tops = dist.world * ops / (ms * 1e-3) / 1e12
+    return {"metric": METRIC, "workload": "dit: 60 Q8_0 DiT blocks, M=4352 (BASELINE configs[2])", "unit": "TOPS",
+            "value": round(tops, 2), "ms_per_step": round(ms, 3), "ops_per_step": ops, "n_gpus": dist.world,
+            "int8_frac": round(tops / dist.world / (2 * bf16), 4), "bf16_frac": round(tops / dist.world / bf16, 4),
+            "peak_source": peak_src, "clocks": clocks}
+
+
+def run_sharded(args, dist: Dist):
+    """BASELINE configs[4] N-sharded across ranks: rank r computes weight rows
+    [r*N/G, (r+1)*N/G) for all M activation rows, then an NCCL all-gather of
+    the shards and one re-layout to row-major [M][N]."""
+    import torch
+    import torch.distributed as tdist
+
+    from pixelina_b200 import pxq
+
+    wl = GEMM_WORKLOADS["q8_0_large"]
+    M, N, K = wl["M"], wl["N"], wl["K"]
+    G, r = dist.world, dist.rank
+    assert N % G == 0
+    Ns = N // G
+    pxq.init(dist.local)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(5)
+    full = gpu_random_q8_0(N, K, gen)  # same seed on every rank -> same weights
+    W = pxq.Weight(full[r * Ns:(r + 1) * Ns].contiguous(), Q8_0, K, Ns)
+    del full
+    x = torch.randn((M, K), device="cuda", generator=gen)
+    ys = torch.empty((M, Ns), device="cuda")
+    gathered = torch.empty((G * M * Ns,), device="cuda")
+    y = torch.empty((M, N), device="cuda")
+    ops = 2.0 * M * N * K
+
+    def step(ev):
+        if ev is not None:
+            ev["start"], ev["end"] = ev_pair()
+            g0, g1 = ev_pair()
+            ev["kernels"] = {"gemm": (ev["start"], g1)}
+            ev["start"].record()
+        pxq.matmul(W, x, out=ys, path="gemm")
+        if ev is not None:
+            g1.record()
+        if G > 1:
+            tdist.all_gather_into_tensor(gathered, ys.view(-1))
+            pxq.gather_shards(gathered, G, M, Ns, out=y)
+        if ev is not None:
+            ev["end"].record()
+
+    flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    step_ms, kernel_ms, clocks = time_steps(step, args.steps, args.warmup, flush_buf.zero_, args.soak,
+                                            ClockSampler(dist.local), dist)
+    ms = dist.max(statistics.mean(step_ms))
+    gemm_ms = dist.max(statistics.mean(kernel_ms["gemm"]))
+    return {"metric": METRIC, "workload": "sharded: Q8_0 M=16384 N=12288 K=3072 N-sharded + NCCL all-gather (configs[4])",
+            "unit": "TOPS", "n_gpus": G, "value_with_gather": round(ops / (ms * 1e-3) / 1e12, 2),
+            "value_gemm_only": round(ops / (gemm_ms * 1e-3) / 1e12, 2), "ms_per_step": round(ms, 3),
+            "gemm_ms": round(gemm_ms, 3), "gather_bytes_per_rank": (G - 1) * M * Ns * 4, "clocks": clocks,
+            "scaling": "strong"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="q5k_gemm",
+                    choices=sorted(GEMM_WORKLOADS) + ["decode", "dit", "sharded"])
+    ap.add_argument("--soak", type=float, default=1.5, help="seconds of untimed steps before timing (clock settling)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    dist = Dist(args.gpus)
+    if args.impl == "reference":
+        if dist.rank != 0:
+            return
+        print(json.dumps(run_reference(args, dist)), flush=True)
+        return
+    dist.init()
+    try:
+        if args.workload in GEMM_WORKLOADS:
+            out = run_gemm_workload(args, dist, GEMM_WORKLOADS[args.workload])
+        elif args.workload == "decode":
+            out = run_decode(args, dist)
+        elif args.workload == "dit":
+            out = run_dit(args, dist)
+        else:
+            out = run_sharded(args, dist)
+        if dist.rank == 0:
+            print(json.dumps(out), flush=True)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

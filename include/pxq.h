@@ -143,6 +143,30 @@ PXQ_API int pxq_synchronize(void* stream);
 PXQ_API int pxq_gather_shards(const float* src, size_t shards, size_t columns, size_t shard_rows, float* dst, size_t ldy,
                       void* stream);
 
+/* ---- quantize once, multiply many ----------------------------------------
+ * The reference quantizes the activation inside every cpu_quant_matmul call
+ * (src/kernels_quant.cpp:382-388).  These entry points split that step out so
+ * one quantized activation can feed several weights with the same inner size
+ * (q/k/v, gate/up) and so the two kernels can be timed separately.  The
+ * activation is quantized in the format the given weight type needs (Q8_0
+ * blocks for Q8_0 weights, Q8_K for K-quants), bit-exact as above. */
+typedef struct pxq_activation pxq_activation;
+
+/* Quantize device fp32 [columns][inner] for weights of `weight_type`. */
+PXQ_API int pxq_activation_quantize(uint32_t weight_type, const float* input, size_t columns, size_t inner,
+                                    pxq_activation** out, void* stream);
+
+/* pxq_matmul on an already-quantized activation. */
+PXQ_API int pxq_matmul_quantized(pxq_weight* w, size_t row_first, size_t row_count, const pxq_activation* a,
+                                 float* output, size_t ldy, const float* bias, void* stream);
+
+/* Free an activation once the work queued on `stream` that reads it is done. */
+PXQ_API int pxq_activation_release(pxq_activation* a, void* stream);
+
+/* Number of CUDA kernels this library has launched in this process (all
+ * devices).  Lets a caller check that its work ran on the GPU path. */
+PXQ_API uint64_t pxq_kernel_launches(void);
+
 /* Debug/parity: run the tensor-core GEMM but store, instead of the scaled
  * sum, every exact block dot it computed.  dump (device) receives
  * items x columns x row_count floats, item-major; items = inner/32 for Q8_0

@@ -12,6 +12,7 @@
 //   * the host-buffer cpu_quant_matmul drop-in.
 // There is no CPU compute path here: an unsupported case is reported as an
 // error status (the reference's `false`), never computed on the host.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -162,9 +163,30 @@ struct pxq_weight {
     }
 };
 
+// A quantized activation: GGUF blocks (matvec, columns <= 8) or the
+// tensor-core operand layout (GEMM), in one stream-ordered allocation.
+struct pxq_activation {
+    uint32_t wtype = 0;     // weight type it was quantized for
+    int64_t M = 0, K = 0;
+    bool blocks = false;    // true: Q8_0/Q8_K blocks; false: GEMM operand
+    void* mem = nullptr;
+    __half* xq = nullptr;   // operand: exact fp16 quants [M][K]
+    float* dxT = nullptr;   // operand: block scales [nb][ldd]
+    __half* amin = nullptr; // operand (Q8_K): min-term split sums
+    int64_t ldd = 0;
+    CUtensorMap tmA, tmSA, tmAmin;
+};
+
 namespace {
 
 std::unordered_map<std::string, pxq_weight*> g_cache;  // guarded by g_mutex
+std::atomic<uint64_t> g_launches{0};
+
+cudaError_t counted(cudaError_t e, uint64_t n = 1)
+{
+    if (e == cudaSuccess) g_launches.fetch_add(n, std::memory_order_relaxed);
+    return e;
+}
 
 int build_packed(const DeviceCtx* d, pxq_weight* w, int64_t first, int64_t count, std::unique_ptr<Packed>& out,
                  cudaStream_t s)
@@ -193,9 +215,9 @@ int build_packed(const DeviceCtx* d, pxq_weight* w, int64_t first, int64_t count
     PXQ_CUDA(cudaMemsetAsync(pk->mem, 0, total, s));
     const uint8_t* src = w->raw + first * w->stride;
     if (w->type == kTypeQ8_0) {
-        PXQ_CUDA(launch_repack_q8_0(src, count, K, w->stride, pk->wv, pk->s1, pk->ldn, s));
+        PXQ_CUDA(counted(launch_repack_q8_0(src, count, K, w->stride, pk->wv, pk->s1, pk->ldn, s)));
     } else {
-        PXQ_CUDA(launch_repack_q5_K(src, count, K, w->stride, pk->wv, pk->s1, pk->s2, pk->bmin, pk->ldn, s));
+        PXQ_CUDA(counted(launch_repack_q5_K(src, count, K, w->stride, pk->wv, pk->s1, pk->s2, pk->bmin, pk->ldn, s)));
     }
     const uint32_t sbox = w->type == kTypeQ8_0 ? 2 : 1;
     int rc = make_map(d, &pk->tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pk->wv, K, count, K * 2, 64, 256,
@@ -259,84 +281,139 @@ int check_matmul_args(pxq_weight* w, size_t row_first, size_t row_count, const v
     return PXQ_OK;
 }
 
-int run_matvec(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* output,
-               size_t ldy, const float* bias, cudaStream_t s)
+// layout: 0 = by batch size (blocks for M <= 8), 1 = GGUF blocks, 2 = GEMM operand
+int quantize_activation(DeviceCtx* d, uint32_t wtype, const float* input, int64_t M, int64_t K, int layout,
+                        pxq_activation** out, cudaStream_t s)
 {
-    if (columns > 8) return fail(PXQ_ERR_UNSUPPORTED, "matvec handles at most 8 columns (got %zu)", columns);
-    const int64_t K = w->inner;
-    const size_t xbytes = w->type == kTypeQ8_0 ? columns * (K / kQK8_0) * kQ8_0Bytes : columns * (K / kQKK) * kQ8KBytes;
-    void* xq = nullptr;
-    if (cudaMallocAsync(&xq, xbytes + 16, s) != cudaSuccess) {
-        cudaGetLastError();
-        return fail(PXQ_ERR_NO_MEMORY, "scratch allocation of %zu bytes failed", xbytes);
+    *out = nullptr;
+    if (!input || !M || !K) return fail(PXQ_ERR_INVALID, "null input or zero size");
+    if (wtype != kTypeQ8_0 && wtype != kTypeQ5_K) return fail(PXQ_ERR_UNSUPPORTED, "weight type %u not supported", wtype);
+    const bool q5 = wtype == kTypeQ5_K;
+    if (K % (q5 ? kQKK : kQK8_0)) return fail(PXQ_ERR_UNSUPPORTED, "inner %lld not a multiple of the block", (long long)K);
+    auto a = std::make_unique<pxq_activation>();
+    a->wtype = wtype;
+    a->M = M;
+    a->K = K;
+    a->blocks = layout == 0 ? (M <= 8) : (layout == 1);
+    const int64_t nb = q5 ? K / kQKK : K / kQK8_0;
+    cudaError_t e;
+    if (a->blocks) {
+        const size_t bytes = (size_t)M * nb * (q5 ? kQ8KBytes : kQ8_0Bytes);
+        if (cudaMallocAsync(&a->mem, bytes + 64, s) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(PXQ_ERR_NO_MEMORY, "scratch allocation of %zu bytes failed", bytes);
+        }
+        e = q5 ? launch_quantize_q8_K_blocks(input, a->mem, M, K, K, s) : launch_quantize_q8_0_blocks(input, a->mem, M, K, K, s);
+    } else {
+        a->ldd = round_up(M, 4);
+        const size_t xq_bytes = (size_t)M * K * 2;
+        const size_t dx_bytes = (size_t)nb * a->ldd * 4;
+        const size_t amin_bytes = q5 ? (size_t)M * nb * 32 : 0;
+        const size_t off_dx = round_up((int64_t)xq_bytes, 1024);
+        const size_t off_amin = off_dx + round_up((int64_t)dx_bytes, 1024);
+        const size_t total = off_amin + round_up((int64_t)amin_bytes, 1024) + 1024;
+        if (cudaMallocAsync(&a->mem, total, s) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(PXQ_ERR_NO_MEMORY, "scratch allocation of %zu bytes failed", total);
+        }
+        uint8_t* base = static_cast<uint8_t*>(a->mem);
+        a->xq = reinterpret_cast<__half*>(base);
+        a->dxT = reinterpret_cast<float*>(base + off_dx);
+        a->amin = reinterpret_cast<__half*>(base + off_amin);
+        e = q5 ? launch_quantize_q8_K_operand(input, a->xq, a->dxT, a->amin, M, K, K, a->ldd, s)
+               : launch_quantize_q8_0_operand(input, a->xq, a->dxT, M, K, K, a->ldd, s);
+        int rc = make_map(d, &a->tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->xq, K, M, K * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!rc) rc = make_map(d, &a->tmSA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a->dxT, M, nb, a->ldd * 4, 128, q5 ? 1 : 2,
+                               CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (!rc && q5) rc = make_map(d, &a->tmAmin, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->amin, nb * 16, M, nb * 32, 16, 128,
+                                     CU_TENSOR_MAP_SWIZZLE_32B);
+        if (!q5) a->tmAmin = a->tmA;
+        if (rc) {
+            cudaFreeAsync(a->mem, s);
+            return rc;
+        }
     }
-    cudaError_t e = w->type == kTypeQ8_0 ? launch_quantize_q8_0_blocks(input, xq, columns, K, K, s)
-                                         : launch_quantize_q8_K_blocks(input, xq, columns, K, K, s);
-    if (e == cudaSuccess)
-        e = launch_matvec(w->type, w->raw + row_first * w->stride, w->stride, row_count, K, xq, columns, output, ldy, bias, s);
-    cudaFreeAsync(xq, s);
-    if (e != cudaSuccess) return fail(PXQ_ERR_CUDA, "matvec launch failed: %s", cudaGetErrorString(e));
+    if (counted(e) != cudaSuccess) {
+        cudaFreeAsync(a->mem, s);
+        return fail(PXQ_ERR_CUDA, "quantize launch failed: %s", cudaGetErrorString(e));
+    }
+    *out = a.release();
     return PXQ_OK;
 }
 
-int run_gemm(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns,
-             float* output, size_t ldy, const float* bias, float* dump, cudaStream_t s)
+void free_activation(pxq_activation* a, cudaStream_t s)
 {
-    const int64_t K = w->inner, M = (int64_t)columns;
-    if (K % 8 != 0) return fail(PXQ_ERR_UNSUPPORTED, "inner %lld not a multiple of 8", (long long)K);
+    if (!a) return;
+    if (a->mem) cudaFreeAsync(a->mem, s);
+    delete a;
+}
+
+int run_matvec(pxq_weight* w, size_t row_first, size_t row_count, const pxq_activation* a, float* output, size_t ldy,
+               const float* bias, cudaStream_t s)
+{
+    if (!a->blocks) return fail(PXQ_ERR_UNSUPPORTED, "matvec handles at most 8 columns (got %lld)", (long long)a->M);
+    cudaError_t e = launch_matvec(w->type, w->raw + row_first * w->stride, w->stride, row_count, w->inner, a->mem, a->M,
+                                  output, ldy, bias, s);
+    if (counted(e) != cudaSuccess) return fail(PXQ_ERR_CUDA, "matvec launch failed: %s", cudaGetErrorString(e));
+    return PXQ_OK;
+}
+
+int run_gemm(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, const pxq_activation* a, float* output,
+             size_t ldy, const float* bias, float* dump, cudaStream_t s)
+{
+    if (a->blocks) return fail(PXQ_ERR_UNSUPPORTED, "activation was quantized for the matvec path");
     const Packed* pk = nullptr;
     int64_t n_first = 0;
     int rc = get_packed(d, w, (int64_t)row_first, (int64_t)row_count, &pk, &n_first, s);
     if (rc) return rc;
-    const bool q5 = w->type == kTypeQ5_K;
-    const int64_t nb = q5 ? K / kQKK : K / kQK8_0;
-    const int64_t ldd = round_up(M, 4);
-    const size_t xq_bytes = (size_t)M * K * 2;
-    const size_t dx_bytes = (size_t)nb * ldd * 4;
-    const size_t amin_bytes = q5 ? (size_t)M * nb * 32 : 0;
-    const size_t off_dx = round_up((int64_t)xq_bytes, 1024);
-    const size_t off_amin = off_dx + round_up((int64_t)dx_bytes, 1024);
-    const size_t total = off_amin + round_up((int64_t)amin_bytes, 1024) + 1024;
-    void* scratch = nullptr;
-    if (cudaMallocAsync(&scratch, total, s) != cudaSuccess) {
-        cudaGetLastError();
-        return fail(PXQ_ERR_NO_MEMORY, "scratch allocation of %zu bytes failed", total);
-    }
-    uint8_t* base = static_cast<uint8_t*>(scratch);
-    __half* xq = reinterpret_cast<__half*>(base);
-    float* dxT = reinterpret_cast<float*>(base + off_dx);
-    __half* amin = reinterpret_cast<__half*>(base + off_amin);
-    cudaError_t e = q5 ? launch_quantize_q8_K_operand(input, xq, dxT, amin, M, K, K, ldd, s)
-                       : launch_quantize_q8_0_operand(input, xq, dxT, M, K, K, ldd, s);
     GemmOperands op;
     std::memset(&op, 0, sizeof(op));
     op.type = w->type;
-    op.M = M;
+    op.M = a->M;
     op.N = (int64_t)row_count;
-    op.K = K;
+    op.K = a->K;
     op.n_first = n_first;
     op.y = output;
     op.ldy = (int64_t)ldy;
     op.bias = bias;
     op.dump = dump;
     op.status = d->status;
-    if (e == cudaSuccess) {
-        rc = make_map(d, &op.tm[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xq, K, M, K * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-        if (!rc) rc = make_map(d, &op.tm[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dxT, M, nb, ldd * 4, 128, q5 ? 1 : 2,
-                               CU_TENSOR_MAP_SWIZZLE_NONE);
-        if (!rc && q5) rc = make_map(d, &op.tm[5], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, amin, nb * 16, M, nb * 32, 16, 128,
-                                     CU_TENSOR_MAP_SWIZZLE_32B);
-        if (!q5) op.tm[5] = op.tm[0];
-        op.tm[1] = pk->tmB;
-        op.tm[3] = pk->tmSB;
-        op.tm[4] = pk->tmSB2;
-        op.tm[6] = pk->tmBmin;
-        if (!rc) e = launch_gemm(op, d->sms, s);
-    }
-    cudaFreeAsync(scratch, s);
-    if (rc) return rc;
-    if (e != cudaSuccess) return fail(PXQ_ERR_CUDA, "gemm launch failed: %s", cudaGetErrorString(e));
+    op.tm[0] = a->tmA;
+    op.tm[1] = pk->tmB;
+    op.tm[2] = a->tmSA;
+    op.tm[3] = pk->tmSB;
+    op.tm[4] = pk->tmSB2;
+    op.tm[5] = a->tmAmin;
+    op.tm[6] = pk->tmBmin;
+    cudaError_t e = launch_gemm(op, d->sms, s);
+    if (counted(e) != cudaSuccess) return fail(PXQ_ERR_CUDA, "gemm launch failed: %s", cudaGetErrorString(e));
     return PXQ_OK;
+}
+
+int check_activation(pxq_weight* w, const pxq_activation* a)
+{
+    if (!a) return fail(PXQ_ERR_INVALID, "null activation");
+    if (a->wtype != w->type) return fail(PXQ_ERR_INVALID, "activation quantized for type %u, weight is %u", a->wtype, w->type);
+    if (a->K != w->inner) return fail(PXQ_ERR_INVALID, "activation inner %lld != weight inner %lld", (long long)a->K,
+                                      (long long)w->inner);
+    return PXQ_OK;
+}
+
+// quantize + multiply + free, all stream-ordered; force: 0 auto, 1 matvec, 2 gemm
+int run_matmul(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns,
+               float* output, size_t ldy, const float* bias, float* dump, int force, cudaStream_t s)
+{
+    if (force == 1 && columns > 8) return fail(PXQ_ERR_UNSUPPORTED, "matvec handles at most 8 columns (got %zu)", columns);
+    if (w->type == kTypeQ8_0 || w->type == kTypeQ5_K) {
+        if (w->inner % 8) return fail(PXQ_ERR_UNSUPPORTED, "inner %lld not a multiple of 8", (long long)w->inner);
+    }
+    pxq_activation* a = nullptr;
+    int rc = quantize_activation(d, w->type, input, (int64_t)columns, w->inner, force, &a, s);
+    if (rc) return rc;
+    rc = a->blocks ? run_matvec(w, row_first, row_count, a, output, ldy, bias, s)
+                   : run_gemm(d, w, row_first, row_count, a, output, ldy, bias, dump, s);
+    free_activation(a, s);
+    return rc;
 }
 
 // per-thread stream for the host-buffer entry point (the reference's session
@@ -384,7 +461,7 @@ int pxq_quantize_q8_0(const float* x, void* blocks, size_t rows, size_t inner, v
     if (int rc = ensure_device(&d)) return rc;
     if (!x || !blocks || !rows || !inner) return fail(PXQ_ERR_INVALID, "null pointer or zero size");
     if (inner % 32) return fail(PXQ_ERR_UNSUPPORTED, "inner %zu not a multiple of 32", inner);
-    PXQ_CUDA(launch_quantize_q8_0_blocks(x, blocks, rows, inner, inner, static_cast<cudaStream_t>(stream)));
+    PXQ_CUDA(counted(launch_quantize_q8_0_blocks(x, blocks, rows, inner, inner, static_cast<cudaStream_t>(stream))));
     return PXQ_OK;
 }
 
@@ -394,7 +471,7 @@ int pxq_quantize_q8_K(const float* x, void* blocks, size_t rows, size_t inner, v
     if (int rc = ensure_device(&d)) return rc;
     if (!x || !blocks || !rows || !inner) return fail(PXQ_ERR_INVALID, "null pointer or zero size");
     if (inner % 256) return fail(PXQ_ERR_UNSUPPORTED, "inner %zu not a multiple of 256", inner);
-    PXQ_CUDA(launch_quantize_q8_K_blocks(x, blocks, rows, inner, inner, static_cast<cudaStream_t>(stream)));
+    PXQ_CUDA(counted(launch_quantize_q8_K_blocks(x, blocks, rows, inner, inner, static_cast<cudaStream_t>(stream))));
     return PXQ_OK;
 }
 
@@ -406,7 +483,7 @@ int pxq_decode(const void* data, uint32_t type, size_t count, float* out, void* 
     if (type != PXQ_TYPE_Q8_0 && type != PXQ_TYPE_Q5_K && type != PXQ_TYPE_Q6_K)
         return fail(PXQ_ERR_UNSUPPORTED, "decode of type %u not supported", type);
     if (count % (type == PXQ_TYPE_Q8_0 ? 32 : 256)) return fail(PXQ_ERR_INVALID, "count %zu not a whole number of blocks", count);
-    PXQ_CUDA(launch_decode(static_cast<const uint8_t*>(data), type, (int64_t)count, out, static_cast<cudaStream_t>(stream)));
+    PXQ_CUDA(counted(launch_decode(static_cast<const uint8_t*>(data), type, (int64_t)count, out, static_cast<cudaStream_t>(stream))));
     return PXQ_OK;
 }
 
@@ -485,7 +562,8 @@ int pxq_matvec(pxq_weight* w, size_t row_first, size_t row_count, const float* i
     DeviceCtx* d;
     if (int rc = ensure_device(&d)) return rc;
     if (int rc = check_matmul_args(w, row_first, row_count, input, columns, output, ldy)) return rc;
-    return run_matvec(w, row_first, row_count, input, columns, output, ldy, bias, static_cast<cudaStream_t>(stream));
+    return run_matmul(d, w, row_first, row_count, input, columns, output, ldy, bias, nullptr, 1,
+                      static_cast<cudaStream_t>(stream));
 }
 
 int pxq_gemm(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* output,
@@ -494,7 +572,8 @@ int pxq_gemm(pxq_weight* w, size_t row_first, size_t row_count, const float* inp
     DeviceCtx* d;
     if (int rc = ensure_device(&d)) return rc;
     if (int rc = check_matmul_args(w, row_first, row_count, input, columns, output, ldy)) return rc;
-    return run_gemm(d, w, row_first, row_count, input, columns, output, ldy, bias, nullptr, static_cast<cudaStream_t>(stream));
+    return run_matmul(d, w, row_first, row_count, input, columns, output, ldy, bias, nullptr, 2,
+                      static_cast<cudaStream_t>(stream));
 }
 
 int pxq_matmul(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* output,
@@ -503,9 +582,8 @@ int pxq_matmul(pxq_weight* w, size_t row_first, size_t row_count, const float* i
     DeviceCtx* d;
     if (int rc = ensure_device(&d)) return rc;
     if (int rc = check_matmul_args(w, row_first, row_count, input, columns, output, ldy)) return rc;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (columns <= 8) return run_matvec(w, row_first, row_count, input, columns, output, ldy, bias, s);
-    return run_gemm(d, w, row_first, row_count, input, columns, output, ldy, bias, nullptr, s);
+    return run_matmul(d, w, row_first, row_count, input, columns, output, ldy, bias, nullptr, 0,
+                      static_cast<cudaStream_t>(stream));
 }
 
 int pxq_gemm_block_dots(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* dump,
@@ -514,9 +592,42 @@ int pxq_gemm_block_dots(pxq_weight* w, size_t row_first, size_t row_count, const
     DeviceCtx* d;
     if (int rc = ensure_device(&d)) return rc;
     if (int rc = check_matmul_args(w, row_first, row_count, input, columns, dump, row_count)) return rc;
-    return run_gemm(d, w, row_first, row_count, input, columns, dump, row_count, nullptr, dump,
-                    static_cast<cudaStream_t>(stream));
+    return run_matmul(d, w, row_first, row_count, input, columns, dump, row_count, nullptr, dump, 2,
+                      static_cast<cudaStream_t>(stream));
 }
+
+int pxq_activation_quantize(uint32_t weight_type, const float* input, size_t columns, size_t inner, pxq_activation** out,
+                            void* stream)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (!out) return fail(PXQ_ERR_INVALID, "null out");
+    return quantize_activation(d, weight_type, input, (int64_t)columns, (int64_t)inner, 0, out,
+                               static_cast<cudaStream_t>(stream));
+}
+
+int pxq_matmul_quantized(pxq_weight* w, size_t row_first, size_t row_count, const pxq_activation* a, float* output,
+                         size_t ldy, const float* bias, void* stream)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (int rc = check_matmul_args(w, row_first, row_count, a, a ? (size_t)a->M : 0, output, ldy)) return rc;
+    if (int rc = check_activation(w, a)) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return a->blocks ? run_matvec(w, row_first, row_count, a, output, ldy, bias, s)
+                     : run_gemm(d, w, row_first, row_count, a, output, ldy, bias, nullptr, s);
+}
+
+int pxq_activation_release(pxq_activation* a, void* stream)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (!a) return fail(PXQ_ERR_INVALID, "null activation");
+    free_activation(a, static_cast<cudaStream_t>(stream));
+    return PXQ_OK;
+}
+
+uint64_t pxq_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int pxq_synchronize(void* stream)
 {
@@ -538,7 +649,7 @@ int pxq_gather_shards(const float* src, size_t shards, size_t columns, size_t sh
     if (int rc = ensure_device(&d)) return rc;
     if (!src || !dst || !shards || !columns || !shard_rows) return fail(PXQ_ERR_INVALID, "null pointer or zero size");
     if (ldy < shards * shard_rows) return fail(PXQ_ERR_INVALID, "ldy %zu < shards*shard_rows", ldy);
-    PXQ_CUDA(launch_gather_shards(src, shards, columns, shard_rows, dst, ldy, static_cast<cudaStream_t>(stream)));
+    PXQ_CUDA(counted(launch_gather_shards(src, shards, columns, shard_rows, dst, ldy, static_cast<cudaStream_t>(stream))));
     return PXQ_OK;
 }
 
@@ -575,8 +686,7 @@ int pxq_quant_matmul(const unsigned char* weights, uint32_t type, const float* i
     int rc = PXQ_OK;
     cudaError_t e = cudaMemcpyAsync(xin, input, xbytes, cudaMemcpyHostToDevice, s);
     if (e == cudaSuccess) {
-        rc = columns <= 8 ? run_matvec(w, 0, rows, xin, columns, yout, rows, nullptr, s)
-                          : run_gemm(d, w, 0, rows, xin, columns, yout, rows, nullptr, nullptr, s);
+        rc = run_matmul(d, w, 0, rows, xin, columns, yout, rows, nullptr, nullptr, 0, s);
         if (!rc) e = cudaMemcpyAsync(output, yout, ybytes, cudaMemcpyDeviceToHost, s);
     }
     cudaFreeAsync(xin, s);

@@ -64,6 +64,10 @@ SIGNATURES = {
     "pxq_synchronize": (_i, [_vp]),
     "pxq_gather_shards": (_i, [_vp, _sz, _sz, _sz, _vp, _sz, _vp]),
     "pxq_gemm_block_dots": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _vp]),
+    "pxq_activation_quantize": (_i, [_u32, _vp, _sz, _sz, C.POINTER(_vp), _vp]),
+    "pxq_matmul_quantized": (_i, [_vp, _sz, _sz, _vp, _vp, _sz, _vp, _vp]),
+    "pxq_activation_release": (_i, [_vp, _vp]),
+    "pxq_kernel_launches": (_u64, []),
 }
 
 
@@ -211,6 +215,41 @@ def gemm_block_dots(w: Weight, x, row_first: int = 0, row_count: Optional[int] =
     dump = torch.zeros((items, columns, rc), dtype=torch.float32, device=x.device)
     _check(load().pxq_gemm_block_dots(w.handle, row_first, rc, _ptr(x), columns, _ptr(dump), _stream_ptr(stream)))
     return dump
+
+
+class Activation:
+    """An activation quantized once for weights of one type (pxq_activation)."""
+
+    def __init__(self, wtype: int, x, stream=None):
+        self.x = x.contiguous()
+        self.columns, self.inner = self.x.shape
+        self.wtype = wtype
+        h = C.c_void_p()
+        _check(load().pxq_activation_quantize(wtype, _ptr(self.x), self.columns, self.inner, C.byref(h),
+                                              _stream_ptr(stream)))
+        self.handle = h
+
+    def release(self, stream=None) -> None:
+        if self.handle:
+            _check(load().pxq_activation_release(self.handle, _stream_ptr(stream)))
+            self.handle = C.c_void_p()
+
+
+def matmul_quantized(w: Weight, a: Activation, row_first: int = 0, row_count: Optional[int] = None, bias=None, out=None,
+                     ldy: Optional[int] = None, stream=None):
+    torch = _torch()
+    rc = w.rows - row_first if row_count is None else row_count
+    if out is None:
+        out = torch.empty((a.columns, rc), dtype=torch.float32, device=a.x.device)
+        ldy = rc
+    elif ldy is None:
+        ldy = out.stride(0)
+    _check(load().pxq_matmul_quantized(w.handle, row_first, rc, a.handle, _ptr(out), ldy, _ptr(bias), _stream_ptr(stream)))
+    return out
+
+
+def kernel_launches() -> int:
+    return int(load().pxq_kernel_launches())
 
 
 def gather_shards(src, shards: int, columns: int, shard_rows: int, out=None, stream=None):
