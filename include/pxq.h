@@ -131,6 +131,13 @@ PXQ_API int pxq_gemm(pxq_weight* w, size_t row_first, size_t row_count, const fl
 PXQ_API int pxq_quant_matmul(const unsigned char* weights, uint32_t type, const float* input, float* output, size_t rows,
                      size_t columns, size_t inner);
 
+/* pxq_matmul with HOST input and output buffers through a device-resident
+ * weight: the input is copied to the device, the product computed there and
+ * the output copied back before the call returns (what cpu_matmul's callers
+ * expect, src/backend_cpu.cpp:103-133).  Uses a per-thread stream. */
+PXQ_API int pxq_matmul_host(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns,
+                            float* output, size_t ldy);
+
 /* Wait for `stream` and report any bounded-wait timeout a kernel recorded
  * since the last call (PXQ_ERR_DEVICE_STATUS), then clear it. */
 PXQ_API int pxq_synchronize(void* stream);

@@ -653,6 +653,44 @@ int pxq_gather_shards(const float* src, size_t shards, size_t columns, size_t sh
     return PXQ_OK;
 }
 
+int pxq_matmul_host(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* output,
+                    size_t ldy)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (int rc = check_matmul_args(w, row_first, row_count, input, columns, output, ldy)) return rc;
+    if (!t_stream || t_stream_device != t_device) {
+        PXQ_CUDA(cudaStreamCreateWithFlags(&t_stream, cudaStreamNonBlocking));
+        t_stream_device = t_device;
+    }
+    cudaStream_t s = t_stream;
+    const size_t inner = (size_t)w->inner;
+    const size_t out_elems = (columns - 1) * ldy + row_count;
+    float* xin = nullptr;
+    float* yout = nullptr;
+    const size_t xbytes = columns * inner * sizeof(float), ybytes = out_elems * sizeof(float);
+    if (cudaMallocAsync(&xin, xbytes, s) != cudaSuccess || cudaMallocAsync(&yout, ybytes, s) != cudaSuccess) {
+        cudaGetLastError();
+        if (xin) cudaFreeAsync(xin, s);
+        return fail(PXQ_ERR_NO_MEMORY, "cannot allocate device buffers");
+    }
+    int rc = PXQ_OK;
+    cudaError_t e = cudaMemcpyAsync(xin, input, xbytes, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) {
+        // keep caller-owned output elements between rows (ldy > row_count) intact
+        if (ldy != row_count && columns > 1) e = cudaMemcpyAsync(yout, output, ybytes, cudaMemcpyHostToDevice, s);
+    }
+    if (e == cudaSuccess) {
+        rc = run_matmul(d, w, row_first, row_count, xin, columns, yout, ldy, nullptr, nullptr, 0, s);
+        if (!rc) e = cudaMemcpyAsync(output, yout, ybytes, cudaMemcpyDeviceToHost, s);
+    }
+    cudaFreeAsync(xin, s);
+    cudaFreeAsync(yout, s);
+    if (e != cudaSuccess) return fail(PXQ_ERR_CUDA, "copy failed: %s", cudaGetErrorString(e));
+    if (rc) return rc;
+    return pxq_synchronize(s);
+}
+
 int pxq_quant_matmul(const unsigned char* weights, uint32_t type, const float* input, float* output, size_t rows,
                      size_t columns, size_t inner)
 {
@@ -670,30 +708,7 @@ int pxq_quant_matmul(const unsigned char* weights, uint32_t type, const float* i
     snprintf(key, sizeof(key), "host:%p:%zu:%zu:%u", (const void*)weights, rows, inner, type);
     pxq_weight* w = nullptr;
     if (int rc = pxq_weight_upload(weights, 0, type, inner, rows, key, &w)) return rc;
-    if (!t_stream || t_stream_device != t_device) {
-        PXQ_CUDA(cudaStreamCreateWithFlags(&t_stream, cudaStreamNonBlocking));
-        t_stream_device = t_device;
-    }
-    cudaStream_t s = t_stream;
-    float* xin = nullptr;
-    float* yout = nullptr;
-    const size_t xbytes = columns * inner * sizeof(float), ybytes = columns * rows * sizeof(float);
-    if (cudaMallocAsync(&xin, xbytes, s) != cudaSuccess || cudaMallocAsync(&yout, ybytes, s) != cudaSuccess) {
-        cudaGetLastError();
-        if (xin) cudaFreeAsync(xin, s);
-        return fail(PXQ_ERR_NO_MEMORY, "cannot allocate device buffers");
-    }
-    int rc = PXQ_OK;
-    cudaError_t e = cudaMemcpyAsync(xin, input, xbytes, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) {
-        rc = run_matmul(d, w, 0, rows, xin, columns, yout, rows, nullptr, nullptr, 0, s);
-        if (!rc) e = cudaMemcpyAsync(output, yout, ybytes, cudaMemcpyDeviceToHost, s);
-    }
-    cudaFreeAsync(xin, s);
-    cudaFreeAsync(yout, s);
-    if (e != cudaSuccess) return fail(PXQ_ERR_CUDA, "copy failed: %s", cudaGetErrorString(e));
-    if (rc) return rc;
-    return pxq_synchronize(s);
+    return pxq_matmul_host(w, 0, rows, input, columns, output, rows);
 }
 
 }  // extern "C"

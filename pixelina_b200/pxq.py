@@ -61,6 +61,7 @@ SIGNATURES = {
     "pxq_matvec": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _sz, _vp, _vp]),
     "pxq_gemm": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _sz, _vp, _vp]),
     "pxq_quant_matmul": (_i, [_vp, _u32, _vp, _vp, _sz, _sz, _sz]),
+    "pxq_matmul_host": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _sz]),
     "pxq_synchronize": (_i, [_vp]),
     "pxq_gather_shards": (_i, [_vp, _sz, _sz, _sz, _vp, _sz, _vp]),
     "pxq_gemm_block_dots": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _vp]),
