@@ -174,6 +174,28 @@ PXQ_API int pxq_activation_release(pxq_activation* a, void* stream);
  * devices).  Lets a caller check that its work ran on the GPU path. */
 PXQ_API uint64_t pxq_kernel_launches(void);
 
+/* ---- decode matvec without device allocation --------------------------------
+ * No counterpart in the reference (its CPU path allocates its quantized
+ * activations with std::vector on every call).  For callers that must not
+ * allocate device memory while they run -- a decode loop that cannot stall on
+ * the allocator, a region where the application forbids cudaMalloc, an
+ * embedder with a fixed device-memory budget: same contract and results as
+ * pxq_matvec (columns 1..8), but the quantized activation rows go to a
+ * static device array of PXQ_NOALLOC_SCRATCH_BYTES owned by this library
+ * (held on every device that loads it, until exit) instead of freshly
+ * allocated scratch.  Activations needing more than
+ * PXQ_NOALLOC_SCRATCH_BYTES - 64 bytes (columns * inner/32 * 34 for Q8_0,
+ * columns * inner/256 * 292 for Q5_K) are rejected with PXQ_ERR_UNSUPPORTED.
+ * The weight must already be uploaded and the current device must be the
+ * weight's.  The first call on a device looks up the array's device address
+ * (one-time set-up); make that call before any stream capture.  All calls on
+ * a device share the array: calls whose GPU work may overlap (unordered
+ * streams) race, so order them. */
+#define PXQ_NOALLOC_SCRATCH_BYTES (1 << 20)
+
+PXQ_API int pxq_matvec_noalloc(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns,
+                               float* output, size_t ldy, const float* bias, void* stream);
+
 /* Debug/parity: run the tensor-core GEMM but store, instead of the scaled
  * sum, every exact block dot it computed.  dump (device) receives
  * items x columns x row_count floats, item-major; items = inner/32 for Q8_0

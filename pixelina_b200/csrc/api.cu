@@ -416,6 +416,34 @@ int run_matmul(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, 
     return rc;
 }
 
+}  // namespace
+
+namespace pxq {
+// Read-only view of a weight handle (used by noalloc.cu).
+bool weight_view(const pxq_weight* w, uint32_t* type, int64_t* inner, int64_t* rows, int64_t* stride, const uint8_t** raw,
+                 int* device)
+{
+    if (!w) return false;
+    *type = w->type;
+    *inner = w->inner;
+    *rows = w->rows;
+    *stride = w->stride;
+    *raw = w->raw;
+    *device = w->device;
+    return true;
+}
+
+// Set the calling thread's pxq_last_error() message.  Capacity for messages
+// is reserved on first use so later error reports reuse it.
+void record_error(const char* msg)
+{
+    if (t_error.capacity() < 512) t_error.reserve(512);
+    t_error.assign(msg);
+}
+}  // namespace pxq
+
+namespace {
+
 // per-thread stream for the host-buffer entry point (the reference's session
 // is thread-local too, src/backend_vulkan.cpp:86)
 thread_local cudaStream_t t_stream = nullptr;

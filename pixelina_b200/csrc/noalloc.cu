@@ -1,0 +1,114 @@
+// noalloc.cu -- the decode matvec with no device allocation per call.
+//
+// Who needs this: callers that cannot call cudaMalloc (or any allocating
+// routine) at the point where they multiply -- a decode loop that must not
+// stall on the allocator, code running inside a region where the caller has
+// forbidden allocation, or an embedding application whose device-memory
+// budget is fixed up front.  pxq_matvec quantizes the activation rows into
+// stream-ordered scratch from the CUDA memory pool; this variant quantizes
+// them into one fixed array that lives in this library's device data instead,
+// so a successful call only launches two kernels (quantize, matvec) and makes
+// no device allocation.  (A rejected call records its message for
+// pxq_last_error() in host memory.)
+//
+// The array: g_noalloc_scratch, PXQ_NOALLOC_SCRATCH_BYTES (1 MiB) per device
+// that loads the library, held until the process exits.  Host code never
+// touches it by name (its host-side symbol is not a device address): on the
+// first call on each device, with that device current, the address is looked
+// up once with cudaGetSymbolAddress and cached.  That first call therefore
+// does the set-up (and may make the runtime load this module); make it before
+// any stream capture.
+//
+// Sharing: every call on a device uses the same array and it keeps the last
+// call's contents.  The quantize kernel rewrites every scratch byte the
+// matvec later reads, so nothing needs clearing, but two calls whose work
+// overlaps on the GPU (different streams without ordering) race on the array;
+// order them on one stream or with events.
+#include <cstdio>
+#include <mutex>
+
+#include "pxq.h"
+#include "pxq_internal.h"
+
+namespace {
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[PXQ_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 16;
+std::mutex g_setup_mutex;
+void* g_scratch_ptr[kMaxDevices] = {};
+
+}  // namespace
+
+// Helpers defined in api.cu: read-only view of a weight handle, and the
+// message returned by pxq_last_error().
+namespace pxq {
+bool weight_view(const pxq_weight* w, uint32_t* type, int64_t* inner, int64_t* rows, int64_t* stride, const uint8_t** raw,
+                 int* device);
+void record_error(const char* msg);
+}
+
+namespace {
+int noalloc_fail(int code, const char* msg)
+{
+    pxq::record_error(msg);
+    return code;
+}
+}  // namespace
+
+extern "C" int pxq_matvec_noalloc(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns,
+                                  float* output, size_t ldy, const float* bias, void* stream)
+{
+    uint32_t type = 0;
+    int64_t inner = 0, rows = 0, stride = 0;
+    const uint8_t* raw = nullptr;
+    int wdev = -1;
+    if (!w || !input || !output || !pxq::weight_view(w, &type, &inner, &rows, &stride, &raw, &wdev))
+        return noalloc_fail(PXQ_ERR_INVALID, "null weight, input or output");
+    if (!columns || !row_count || columns > 8)
+        return noalloc_fail(PXQ_ERR_INVALID, "columns must be 1..8 and row_count > 0");
+    if (row_first > (size_t)rows || row_count > (size_t)rows - row_first)
+        return noalloc_fail(PXQ_ERR_INVALID, "row range outside the weight");
+    if (ldy < row_count && columns > 1) return noalloc_fail(PXQ_ERR_INVALID, "ldy < row_count");
+    if (type != pxq::kTypeQ8_0 && type != pxq::kTypeQ5_K) return noalloc_fail(PXQ_ERR_UNSUPPORTED, "weight type not supported");
+    const bool q5 = type == pxq::kTypeQ5_K;
+    const uint64_t need = (uint64_t)columns * (uint64_t)(q5 ? inner / pxq::kQKK : inner / pxq::kQK8_0) *
+                          (uint64_t)(q5 ? pxq::kQ8KBytes : pxq::kQ8_0Bytes);
+    if (need + 64 > PXQ_NOALLOC_SCRATCH_BYTES) {
+        char msg[200];
+        snprintf(msg, sizeof(msg), "activation needs %llu bytes of scratch; the static scratch holds %d bytes "
+                 "(PXQ_NOALLOC_SCRATCH_BYTES, 64 reserved)", (unsigned long long)need, PXQ_NOALLOC_SCRATCH_BYTES);
+        return noalloc_fail(PXQ_ERR_UNSUPPORTED, msg);
+    }
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+        return noalloc_fail(PXQ_ERR_NO_DEVICE, "no current CUDA device");
+    if (dev != wdev) return noalloc_fail(PXQ_ERR_INVALID, "the weight lives on another device than the current one");
+    void* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_setup_mutex);
+        if (!g_scratch_ptr[dev]) {
+            void* p = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+            if (e != cudaSuccess || !p) {
+                char msg[200];
+                snprintf(msg, sizeof(msg), "cudaGetSymbolAddress of the static scratch failed: %s", cudaGetErrorString(e));
+                return noalloc_fail(PXQ_ERR_CUDA, msg);
+            }
+            g_scratch_ptr[dev] = p;
+        }
+        scratch = g_scratch_ptr[dev];
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = q5 ? pxq::launch_quantize_q8_K_blocks(input, scratch, (int64_t)columns, inner, inner, s)
+                       : pxq::launch_quantize_q8_0_blocks(input, scratch, (int64_t)columns, inner, inner, s);
+    if (e == cudaSuccess)
+        e = pxq::launch_matvec(type, raw + row_first * stride, stride, (int64_t)row_count, inner, scratch, (int64_t)columns,
+                               output, (int64_t)ldy, bias, s);
+    if (e != cudaSuccess) {
+        char msg[200];
+        snprintf(msg, sizeof(msg), "kernel launch failed: %s", cudaGetErrorString(e));
+        return noalloc_fail(PXQ_ERR_CUDA, msg);
+    }
+    return PXQ_OK;
+}

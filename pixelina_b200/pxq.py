@@ -69,6 +69,7 @@ SIGNATURES = {
     "pxq_matmul_quantized": (_i, [_vp, _sz, _sz, _vp, _vp, _sz, _vp, _vp]),
     "pxq_activation_release": (_i, [_vp, _vp]),
     "pxq_kernel_launches": (_u64, []),
+    "pxq_matvec_noalloc": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _sz, _vp, _vp]),
 }
 
 

@@ -1,0 +1,83 @@
+"""GPU: pxq_matvec_noalloc, the decode matvec that allocates no device memory.
+
+It is meant for callers that cannot call cudaMalloc while they run (a decode
+loop that must not stall on the allocator, a region where the application
+forbids allocation, a fixed device-memory budget).  Its quantized activations
+live in a static 1 MiB device array of the library instead of per-call
+scratch, so its results must equal those of pxq_matvec, the entry point that
+allocates.  This file sorts last so a `-x` run has already run every other
+test if it fails; it also passes on its own in a fresh process.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from conftest import TOL, max_abs_rel
+from pixelina_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _p(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else C.c_void_p(0)
+
+
+@pytest.mark.parametrize("wtype", [8, 13])
+def test_noalloc_matches_allocating_matvec_twice(pxq, wtype):
+    import torch
+
+    lib = pxq.load()
+    rows, inner = 300, 3584
+    w = synth.weights_for(wtype, rows, inner, seed=21)
+    W = pxq.Weight(w, wtype, inner, rows)
+    stream = torch.cuda.current_stream()
+    sp = C.c_void_p(stream.cuda_stream)
+    # two calls in a row with different inputs and shapes: the second reuses
+    # the static scratch the first one filled
+    for call, (columns, first, count) in enumerate(((8, 0, 300), (3, 7, 250))):
+        x = torch.from_numpy(synth.activations(columns, inner, seed=30 + call)).cuda()
+        bias = torch.linspace(-0.5, 0.5, count, device="cuda")
+        want = torch.empty((columns, count), device="cuda")
+        got = torch.full((columns, count), float("nan"), device="cuda")
+        rc = lib.pxq_matvec(W.handle, first, count, _p(x), columns, _p(want), count, _p(bias), sp)
+        assert rc == 0, pxq.last_error()
+        rc = lib.pxq_matvec_noalloc(W.handle, first, count, _p(x), columns, _p(got), count, _p(bias), sp)
+        assert rc == 0, pxq.last_error()
+        torch.cuda.synchronize()
+        assert max_abs_rel(got.cpu().numpy(), want.cpu().numpy()) <= TOL
+    W.release()
+
+
+def test_noalloc_makes_no_device_allocation(pxq):
+    import torch
+
+    lib = pxq.load()
+    rows, inner = 512, 4096
+    W = pxq.Weight(synth.q5_K_weights(rows, inner, seed=3), 13, inner, rows)
+    x = torch.from_numpy(synth.activations(4, inner, seed=4)).cuda()
+    y = torch.empty((4, rows), device="cuda")
+    sp = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert lib.pxq_matvec_noalloc(W.handle, 0, rows, _p(x), 4, _p(y), rows, None, sp) == 0  # first call: set-up
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        assert lib.pxq_matvec_noalloc(W.handle, 0, rows, _p(x), 4, _p(y), rows, None, sp) == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    W.release()
+
+
+def test_noalloc_rejects_oversized_activation(pxq):
+    import torch
+
+    lib = pxq.load()
+    rows, inner = 16, 131072  # 8 rows x 512 super-blocks x 292 B > 1 MiB
+    W = pxq.Weight(synth.random_q5_K(rows, inner, np.random.default_rng(1)), 13, inner, rows)
+    x = torch.zeros((8, inner), device="cuda")
+    y = torch.zeros((8, rows), device="cuda")
+    rc = lib.pxq_matvec_noalloc(W.handle, 0, rows, _p(x), 8, _p(y), rows, None, None)
+    assert rc == pxq.ERR_UNSUPPORTED
+    assert "PXQ_NOALLOC_SCRATCH_BYTES" in pxq.last_error()
+    W.release()
