@@ -134,13 +134,13 @@ int make_map(const DeviceCtx* d, CUtensorMap* m, CUtensorMapDataType dt, const v
 // GEMM operand copy of (a row range of) a weight.
 struct Packed {
     int64_t rows = 0;   // packed rows
-    int64_t ldn = 0;    // row stride of the scale planes
+    int64_t ldn = 0;    // row stride of the Q5_K scale planes
     void* mem = nullptr;
-    __half* wv = nullptr;
-    float* s1 = nullptr;      // dwT (Q8_0) or dT (Q5_K)
-    float* s2 = nullptr;      // dminT (Q5_K)
-    __half* bmin = nullptr;   // Q5_K min operand
-    CUtensorMap tmB, tmSB, tmSB2, tmBmin;
+    __half* wv = nullptr;     // fp16 operand [rows][K]
+    __half* ws = nullptr;     // Q8_0 one-hot scales [rows][nb*16] / Q5_K min operand [rows][nsb*16]
+    float* d = nullptr;       // Q5_K d    [nsb][ldn]
+    float* dmin = nullptr;    // Q5_K dmin [nsb][ldn]
+    CUtensorMap tmW, tmWs, tmD, tmDm;
     ~Packed()
     {
         if (mem) cudaFree(mem);
@@ -171,10 +171,10 @@ struct pxq_activation {
     bool blocks = false;    // true: Q8_0/Q8_K blocks; false: GEMM operand
     void* mem = nullptr;
     __half* xq = nullptr;   // operand: exact fp16 quants [M][K]
-    float* dxT = nullptr;   // operand: block scales [nb][ldd]
-    __half* amin = nullptr; // operand (Q8_K): min-term split sums
+    void* scale = nullptr;  // operand: Q8_0 fp16 scales [M][ldd] / Q8_K fp32 d [nsb][ldd]
+    __half* amin = nullptr; // operand (Q8_K): min-term split sums [M][nsb*16]
     int64_t ldd = 0;
-    CUtensorMap tmA, tmSA, tmAmin;
+    CUtensorMap tmX, tmXs, tmDx;
 };
 
 namespace {
@@ -193,45 +193,45 @@ int build_packed(const DeviceCtx* d, pxq_weight* w, int64_t first, int64_t count
 {
     auto pk = std::make_unique<Packed>();
     const int64_t K = w->inner;
-    const int64_t nb = w->type == kTypeQ8_0 ? K / kQK8_0 : K / kQKK;
+    const bool q5 = w->type == kTypeQ5_K;
+    const int64_t nb = q5 ? K / kQKK : K / kQK8_0;
     pk->rows = count;
     pk->ldn = round_up(count, 4);
     const size_t wv_bytes = (size_t)count * K * 2;
-    const size_t s_bytes = (size_t)nb * pk->ldn * 4;
-    const size_t bmin_bytes = w->type == kTypeQ5_K ? (size_t)count * nb * 16 * 2 : 0;
-    const size_t off_s1 = round_up((int64_t)wv_bytes, 1024);
-    const size_t off_s2 = off_s1 + round_up((int64_t)s_bytes, 1024);
-    const size_t off_bmin = off_s2 + (w->type == kTypeQ5_K ? round_up((int64_t)s_bytes, 1024) : 0);
-    const size_t total = off_bmin + round_up((int64_t)bmin_bytes, 1024) + 1024;
+    const size_t ws_bytes = (size_t)count * nb * 32;
+    const size_t s_bytes = q5 ? (size_t)nb * pk->ldn * 4 : 0;
+    const size_t off_ws = round_up((int64_t)wv_bytes, 1024);
+    const size_t off_d = off_ws + round_up((int64_t)ws_bytes, 1024);
+    const size_t off_dm = off_d + round_up((int64_t)s_bytes, 1024);
+    const size_t total = off_dm + round_up((int64_t)s_bytes, 1024) + 1024;
     if (cudaMalloc(&pk->mem, total) != cudaSuccess) {
         cudaGetLastError();
         return fail(PXQ_ERR_NO_MEMORY, "cannot allocate %zu bytes for the GEMM operand copy", total);
     }
     uint8_t* base = static_cast<uint8_t*>(pk->mem);
     pk->wv = reinterpret_cast<__half*>(base);
-    pk->s1 = reinterpret_cast<float*>(base + off_s1);
-    pk->s2 = reinterpret_cast<float*>(base + off_s2);
-    pk->bmin = reinterpret_cast<__half*>(base + off_bmin);
+    pk->ws = reinterpret_cast<__half*>(base + off_ws);
+    pk->d = reinterpret_cast<float*>(base + off_d);
+    pk->dmin = reinterpret_cast<float*>(base + off_dm);
     PXQ_CUDA(cudaMemsetAsync(pk->mem, 0, total, s));
     const uint8_t* src = w->raw + first * w->stride;
-    if (w->type == kTypeQ8_0) {
-        PXQ_CUDA(counted(launch_repack_q8_0(src, count, K, w->stride, pk->wv, pk->s1, pk->ldn, s)));
+    if (!q5) {
+        PXQ_CUDA(counted(launch_repack_q8_0(src, count, K, w->stride, pk->wv, pk->ws, s)));
     } else {
-        PXQ_CUDA(counted(launch_repack_q5_K(src, count, K, w->stride, pk->wv, pk->s1, pk->s2, pk->bmin, pk->ldn, s)));
+        PXQ_CUDA(counted(launch_repack_q5_K(src, count, K, w->stride, pk->wv, pk->d, pk->dmin, pk->ws, pk->ldn, s)));
     }
-    const uint32_t sbox = w->type == kTypeQ8_0 ? 2 : 1;
-    int rc = make_map(d, &pk->tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pk->wv, K, count, K * 2, 64, 256,
+    int rc = make_map(d, &pk->tmW, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pk->wv, K, count, K * 2, 64, 128,
                       CU_TENSOR_MAP_SWIZZLE_128B);
-    if (!rc) rc = make_map(d, &pk->tmSB, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pk->s1, count, nb, pk->ldn * 4, 256, sbox,
-                           CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (!rc && w->type == kTypeQ5_K) {
-        rc = make_map(d, &pk->tmSB2, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pk->s2, count, nb, pk->ldn * 4, 256, 1,
+    if (!rc) rc = make_map(d, &pk->tmWs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pk->ws, nb * 16, count, nb * 32, 16, 128,
+                           CU_TENSOR_MAP_SWIZZLE_32B);
+    if (!rc && q5) {
+        rc = make_map(d, &pk->tmD, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pk->d, count, nb, pk->ldn * 4, 128, 1,
                       CU_TENSOR_MAP_SWIZZLE_NONE);
-        if (!rc) rc = make_map(d, &pk->tmBmin, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pk->bmin, nb * 16, count, nb * 32, 16, 256,
-                               CU_TENSOR_MAP_SWIZZLE_32B);
+        if (!rc) rc = make_map(d, &pk->tmDm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pk->dmin, count, nb, pk->ldn * 4, 128, 1,
+                               CU_TENSOR_MAP_SWIZZLE_NONE);
     } else {
-        pk->tmSB2 = pk->tmSB;
-        pk->tmBmin = pk->tmB;
+        pk->tmD = pk->tmW;
+        pk->tmDm = pk->tmW;
     }
     if (rc) return rc;
     out = std::move(pk);
@@ -305,12 +305,12 @@ int quantize_activation(DeviceCtx* d, uint32_t wtype, const float* input, int64_
         }
         e = q5 ? launch_quantize_q8_K_blocks(input, a->mem, M, K, K, s) : launch_quantize_q8_0_blocks(input, a->mem, M, K, K, s);
     } else {
-        a->ldd = round_up(M, 4);
+        a->ldd = q5 ? round_up(M, 4) : round_up(nb, 8);
         const size_t xq_bytes = (size_t)M * K * 2;
-        const size_t dx_bytes = (size_t)nb * a->ldd * 4;
+        const size_t sc_bytes = q5 ? (size_t)nb * a->ldd * 4 : (size_t)M * a->ldd * 2;
         const size_t amin_bytes = q5 ? (size_t)M * nb * 32 : 0;
-        const size_t off_dx = round_up((int64_t)xq_bytes, 1024);
-        const size_t off_amin = off_dx + round_up((int64_t)dx_bytes, 1024);
+        const size_t off_sc = round_up((int64_t)xq_bytes, 1024);
+        const size_t off_amin = off_sc + round_up((int64_t)sc_bytes, 1024);
         const size_t total = off_amin + round_up((int64_t)amin_bytes, 1024) + 1024;
         if (cudaMallocAsync(&a->mem, total, s) != cudaSuccess) {
             cudaGetLastError();
@@ -318,16 +318,21 @@ int quantize_activation(DeviceCtx* d, uint32_t wtype, const float* input, int64_
         }
         uint8_t* base = static_cast<uint8_t*>(a->mem);
         a->xq = reinterpret_cast<__half*>(base);
-        a->dxT = reinterpret_cast<float*>(base + off_dx);
+        a->scale = base + off_sc;
         a->amin = reinterpret_cast<__half*>(base + off_amin);
-        e = q5 ? launch_quantize_q8_K_operand(input, a->xq, a->dxT, a->amin, M, K, K, a->ldd, s)
-               : launch_quantize_q8_0_operand(input, a->xq, a->dxT, M, K, K, a->ldd, s);
-        int rc = make_map(d, &a->tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->xq, K, M, K * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-        if (!rc) rc = make_map(d, &a->tmSA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a->dxT, M, nb, a->ldd * 4, 128, q5 ? 1 : 2,
-                               CU_TENSOR_MAP_SWIZZLE_NONE);
-        if (!rc && q5) rc = make_map(d, &a->tmAmin, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->amin, nb * 16, M, nb * 32, 16, 128,
-                                     CU_TENSOR_MAP_SWIZZLE_32B);
-        if (!q5) a->tmAmin = a->tmA;
+        e = q5 ? launch_quantize_q8_K_operand(input, a->xq, static_cast<float*>(a->scale), a->amin, M, K, K, a->ldd, s)
+               : launch_quantize_q8_0_operand(input, a->xq, static_cast<__half*>(a->scale), M, K, K, a->ldd, s);
+        int rc = make_map(d, &a->tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->xq, K, M, K * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!rc && q5) {
+            rc = make_map(d, &a->tmXs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->amin, nb * 16, M, nb * 32, 16, 128,
+                          CU_TENSOR_MAP_SWIZZLE_32B);
+            if (!rc) rc = make_map(d, &a->tmDx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a->scale, M, nb, a->ldd * 4, 128, 1,
+                                   CU_TENSOR_MAP_SWIZZLE_NONE);
+        } else if (!rc) {
+            rc = make_map(d, &a->tmXs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->scale, nb, M, a->ldd * 2, 16, 128,
+                          CU_TENSOR_MAP_SWIZZLE_32B);
+            a->tmDx = a->tmX;
+        }
         if (rc) {
             cudaFreeAsync(a->mem, s);
             return rc;
@@ -378,13 +383,25 @@ int run_gemm(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, co
     op.bias = bias;
     op.dump = dump;
     op.status = d->status;
-    op.tm[0] = a->tmA;
-    op.tm[1] = pk->tmB;
-    op.tm[2] = a->tmSA;
-    op.tm[3] = pk->tmSB;
-    op.tm[4] = pk->tmSB2;
-    op.tm[5] = a->tmAmin;
-    op.tm[6] = pk->tmBmin;
+    op.tm[0] = pk->tmW;
+    op.tm[1] = a->tmX;
+    op.tm[2] = pk->tmWs;
+    op.tm[3] = a->tmXs;
+    op.tm[4] = pk->tmD;
+    op.tm[5] = pk->tmDm;
+    op.tm[6] = a->tmDx;
+    // TMA-store epilogue when output rows start 16-byte aligned and the row
+    // length is a whole number of 16-byte units (a bulk tensor store clips the
+    // innermost dimension only at 16-byte granularity)
+    op.tma_store = 0;
+    op.tm_y = op.tm[0];
+    if (!dump && (reinterpret_cast<uintptr_t>(output) & 15u) == 0 && (ldy % 4) == 0 && (row_count % 4) == 0) {
+        if (make_map(d, &op.tm_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, output, row_count, (uint64_t)a->M, ldy * 4, 32, 64,
+                     CU_TENSOR_MAP_SWIZZLE_NONE) == PXQ_OK)
+            op.tma_store = 1;
+        else
+            op.tm_y = op.tm[0];
+    }
     cudaError_t e = launch_gemm(op, d->sms, s);
     if (counted(e) != cudaSuccess) return fail(PXQ_ERR_CUDA, "gemm launch failed: %s", cudaGetErrorString(e));
     return PXQ_OK;

@@ -24,18 +24,19 @@ cudaError_t launch_quantize_q8_0_blocks(const float* x, void* y, int64_t rows, i
 cudaError_t launch_quantize_q8_K_blocks(const float* x, void* y, int64_t rows, int64_t inner, int64_t ldx, cudaStream_t s);
 // Tensor-core operand formats for the GEMM (same rounding, different layout):
 //   xq  fp16 [rows][inner]: the int8 quants as exact fp16 values
-//   dxT fp32 [inner/block][ldd]: per-block scale, block-major (TMA-friendly)
-//   amin fp16 [rows][inner/256*16] (Q8_K only): split 32-element sums for the
-//        Q5_K min term, (hi_j, lo_j) with bsum2_j = 64*hi_j + lo_j
-cudaError_t launch_quantize_q8_0_operand(const float* x, __half* xq, float* dxT, int64_t rows, int64_t inner, int64_t ldx,
+//   Q8_0: dx16 fp16 [rows][ldd]: the stored fp16 block scales, row-major
+//   Q8_K: dxT fp32 [inner/256][ldd]: per-block scale, block-major
+//         amin fp16 [rows][inner/256*16]: split 32-element sums for the Q5_K
+//         min term, (hi_j, lo_j) with bsum2_j = 64*hi_j + lo_j
+cudaError_t launch_quantize_q8_0_operand(const float* x, __half* xq, __half* dx16, int64_t rows, int64_t inner, int64_t ldx,
                                          int64_t ldd, cudaStream_t s);
 cudaError_t launch_quantize_q8_K_operand(const float* x, __half* xq, float* dxT, __half* amin, int64_t rows, int64_t inner,
                                          int64_t ldx, int64_t ldd, cudaStream_t s);
 
 // ---- repack.cu -------------------------------------------------------------
 // One-time weight repack into the GEMM operand layout (bit-exact unpack).
-cudaError_t launch_repack_q8_0(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wq, float* dwT,
-                               int64_t ldn, cudaStream_t s);
+cudaError_t launch_repack_q8_0(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wq, __half* ws1h,
+                               cudaStream_t s);
 cudaError_t launch_repack_q5_K(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wv, float* dT,
                                float* dminT, __half* bmin, int64_t ldn, cudaStream_t s);
 
@@ -55,10 +56,13 @@ struct GemmOperands {
     uint32_t type;        // kTypeQ8_0 or kTypeQ5_K
     int64_t M, N, K;      // activation rows, view rows (output columns), inner
     int64_t n_first;      // first weight row of the view (multiple of 4)
-    // tensor maps: 0 A operand, 1 B operand, 2 activation scales, 3 weight
-    // scales, 4 Q5_K weight dmin, 5 Q5_K activation min operand, 6 Q5_K
-    // weight min operand (unused entries may hold any valid map)
+    // tensor maps: 0 weight operand, 1 activation operand, 2 weight scale
+    // tile (Q8_0 one-hot scales / Q5_K min operand), 3 activation scale tile
+    // (Q8_0 fp16 scales / Q8_K min operand), 4 Q5_K weight d, 5 Q5_K weight
+    // dmin, 6 Q8_K activation d (unused entries may hold any valid map)
     CUtensorMap tm[7];
+    CUtensorMap tm_y;     // output map (fp32 [M][ldy], box {32, 64}) when tma_store
+    int tma_store;        // 1: write the output tile with TMA stores
     float* y;
     int64_t ldy;
     const float* bias;    // may be null (indexed by view-local column)

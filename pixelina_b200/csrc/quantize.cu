@@ -90,7 +90,7 @@ __global__ void k_quantize_q8_0_blocks(const float* __restrict__ x, uint8_t* __r
     }
 }
 
-__global__ void k_quantize_q8_0_operand(const float* __restrict__ x, __half* __restrict__ xq, float* __restrict__ dxT,
+__global__ void k_quantize_q8_0_operand(const float* __restrict__ x, __half* __restrict__ xq, __half* __restrict__ dx16,
                                         int64_t rows, int64_t inner, int64_t ldx, int64_t ldd)
 {
     const int64_t quads_per_row = inner / 4;
@@ -111,7 +111,7 @@ __global__ void k_quantize_q8_0_operand(const float* __restrict__ x, __half* __r
         packed.x = *reinterpret_cast<uint32_t*>(&h01);
         packed.y = *reinterpret_cast<uint32_t*>(&h23);
         *reinterpret_cast<uint2*>(xq + row * inner + quad * 4) = packed;
-        if ((quad & 7) == 0) dxT[(quad / 8) * ldd + row] = __half2float(p.d16);
+        if ((quad & 7) == 0) dx16[row * ldd + quad / 8] = p.d16;
     }
 }
 
@@ -253,11 +253,11 @@ cudaError_t launch_quantize_q8_K_blocks(const float* x, void* y, int64_t rows, i
     return cudaGetLastError();
 }
 
-cudaError_t launch_quantize_q8_0_operand(const float* x, __half* xq, float* dxT, int64_t rows, int64_t inner, int64_t ldx,
+cudaError_t launch_quantize_q8_0_operand(const float* x, __half* xq, __half* dx16, int64_t rows, int64_t inner, int64_t ldx,
                                          int64_t ldd, cudaStream_t s)
 {
     const int threads = 256;
-    k_quantize_q8_0_operand<<<grid_for(rows * inner / 4, threads), threads, 0, s>>>(x, xq, dxT, rows, inner, ldx, ldd);
+    k_quantize_q8_0_operand<<<grid_for(rows * inner / 4, threads), threads, 0, s>>>(x, xq, dx16, rows, inner, ldx, ldd);
     return cudaGetLastError();
 }
 

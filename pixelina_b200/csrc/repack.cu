@@ -5,7 +5,9 @@
 //     (the device-side counterpart of the Vulkan backend's upload cache,
 //     src/backend_vulkan.cpp:742-758):
 //       Q8_0: wq   fp16 [rows][inner]   = the int8 quants, exactly
-//             dwT  fp32 [inner/32][ldn] = fp16 block scale as fp32
+//             ws1h fp16 [rows][inner/32*16]: for block b a 16-wide group holding
+//                  the block's fp16 scale at position b%16 and zeros elsewhere
+//                  (the weight side of the tensor-core scale product)
 //       Q5_K: wv   fp16 [rows][inner]   = sc_g * q5 (<= 63*31 = 1953, exact)
 //             dT, dminT fp32 [inner/256][ldn]
 //             bmin fp16 [rows][inner/256*16] = (64*m_g, m_g) pairs, the weight
@@ -37,7 +39,7 @@ __device__ __forceinline__ float load_half(const uint8_t* p)
 }
 
 __global__ void k_repack_q8_0(const uint8_t* __restrict__ raw, int64_t rows, int64_t inner, int64_t stride,
-                              __half* __restrict__ wq, float* __restrict__ dwT, int64_t ldn)
+                              __half* __restrict__ wq, __half* __restrict__ ws1h)
 {
     const int64_t nb = inner / kQK8_0;
     const int64_t total = rows * nb;
@@ -50,7 +52,13 @@ __global__ void k_repack_q8_0(const uint8_t* __restrict__ raw, int64_t rows, int
         uint4* dst = reinterpret_cast<uint4*>(wq + r * inner + b * kQK8_0);
 #pragma unroll
         for (int j = 0; j < 4; j++) dst[j] = reinterpret_cast<uint4*>(h)[j];
-        dwT[b * ldn + r] = load_half(blk);
+        __half g[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) g[j] = __ushort_as_half((unsigned short)0);
+        g[b % 16] = __ushort_as_half((unsigned short)((uint16_t)blk[0] | ((uint16_t)blk[1] << 8)));
+        uint4* gd = reinterpret_cast<uint4*>(ws1h + (r * nb + b) * 16);
+        gd[0] = reinterpret_cast<uint4*>(g)[0];
+        gd[1] = reinterpret_cast<uint4*>(g)[1];
     }
 }
 
@@ -131,10 +139,10 @@ int grid_for(int64_t work, int threads)
 
 }  // namespace
 
-cudaError_t launch_repack_q8_0(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wq, float* dwT,
-                               int64_t ldn, cudaStream_t s)
+cudaError_t launch_repack_q8_0(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wq, __half* ws1h,
+                               cudaStream_t s)
 {
-    k_repack_q8_0<<<grid_for(rows * (inner / kQK8_0), 256), 256, 0, s>>>(raw, rows, inner, stride, wq, dwT, ldn);
+    k_repack_q8_0<<<grid_for(rows * (inner / kQK8_0), 256), 256, 0, s>>>(raw, rows, inner, stride, wq, ws1h);
     return cudaGetLastError();
 }
 

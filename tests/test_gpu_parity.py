@@ -147,10 +147,12 @@ def test_row_views_ldy_bias(pxq, oracle, path, wtype):
     x = synth.activations(columns, inner, seed=10)
     W = pxq.Weight(w, wtype, inner, rows)
     ok, ref = oracle.quant_matmul(w, wtype, x, rows)
-    for first, count in ((0, 300), (4, 256), (3, 97), (128, 172)):
+    # counts and strides exercise both epilogues (TMA store: count % 4 == 0 and
+    # ldy % 4 == 0; direct stores otherwise)
+    for first, count, pad in ((0, 300, 7), (4, 256, 4), (3, 97, 7), (3, 97, 3), (128, 172, 4), (8, 96, 0)):
         bias = torch.linspace(-1, 1, count, device="cuda", dtype=torch.float32)
-        out = torch.full((columns, count + 7), float("nan"), device="cuda")
-        pxq.matmul(W, cuda(x), row_first=first, row_count=count, bias=bias, out=out, ldy=count + 7, path=path)
+        out = torch.full((columns, count + pad), float("nan"), device="cuda")
+        pxq.matmul(W, cuda(x), row_first=first, row_count=count, bias=bias, out=out, ldy=count + pad, path=path)
         pxq.synchronize()
         got = out.cpu().numpy()
         want = ref[:, first:first + count] + bias.cpu().numpy()[None, :]
