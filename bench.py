@@ -497,13 +497,31 @@ def run_decode(args, dist: Dist):
         xs = {H: torch.randn((M, H), device="cuda", generator=gen), F: torch.randn((M, F), device="cuda", generator=gen)}
         ys = {n: torch.empty((M, n), device="cuda") for _, n, _ in shapes}
 
+        def token():
+            for ws in layers:
+                for name, n, k in shapes:
+                    pxq.matmul(ws[name], xs[k], out=ys[n], path="matvec")
+
+        # one token = 140 matvecs (each: activation quantize + matvec); replay it as a
+        # CUDA graph so that host launch overhead does not hide the device time
+        token()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            token()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph):
+            token()
+        torch.cuda.synchronize()
+
         def step(ev):
             if ev is not None:
                 ev["start"], ev["end"] = ev_pair()
                 ev["start"].record()
-            for ws in layers:
-                for name, n, k in shapes:
-                    pxq.matmul(ws[name], xs[k], out=ys[n], path="matvec")
+            graph.replay()
             if ev is not None:
                 ev["end"].record()
 
@@ -514,6 +532,7 @@ def run_decode(args, dist: Dist):
         gbs = wbytes_total / (ms * 1e-3) / 1e9
         results[f"M={M}"] = {"ms_per_token": round(ms, 4), "weight_GBps": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
                              "clocks": clocks}
+        del graph
     return {"metric": METRIC, "workload": "decode: Q5_K matvec, 28 layers (BASELINE configs[3])", "unit": "GB/s",
             "weight_bytes_per_token": wbytes_total, "peak_hbm_gbs": hbm, "peak_source": peak_src,
             "launches_per_token": 2 * 5 * L, "results": results}

@@ -183,9 +183,12 @@ PXQ_API uint64_t pxq_kernel_launches(void);
  * pxq_matvec (columns 1..8), but the quantized activation rows go to a
  * static device array of PXQ_NOALLOC_SCRATCH_BYTES owned by this library
  * (held on every device that loads it, until exit) instead of freshly
- * allocated scratch.  Activations needing more than
- * PXQ_NOALLOC_SCRATCH_BYTES - 64 bytes (columns * inner/32 * 34 for Q8_0,
- * columns * inner/256 * 292 for Q5_K) are rejected with PXQ_ERR_UNSUPPORTED.
+ * allocated scratch.  The array holds the quantized activation rows
+ * (columns * inner/32 * 34 bytes for Q8_0, columns * inner/256 * 292 for
+ * Q5_K) and, for shapes the matvec splits along K, its fp32 partial sums
+ * (up to a few hundred KB for 8 columns); a call whose total exceeds
+ * PXQ_NOALLOC_SCRATCH_BYTES is rejected with PXQ_ERR_UNSUPPORTED before any
+ * work is queued.
  * The weight must already be uploaded and the current device must be the
  * weight's.  The first call on a device looks up the array's device address
  * (one-time set-up); make that call before any stream capture.  All calls on

@@ -353,12 +353,27 @@ void free_activation(pxq_activation* a, cudaStream_t s)
     delete a;
 }
 
-int run_matvec(pxq_weight* w, size_t row_first, size_t row_count, const pxq_activation* a, float* output, size_t ldy,
-               const float* bias, cudaStream_t s)
+int run_matvec(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, const pxq_activation* a, float* output,
+               size_t ldy, const float* bias, cudaStream_t s)
 {
     if (!a->blocks) return fail(PXQ_ERR_UNSUPPORTED, "matvec handles at most 8 columns (got %lld)", (long long)a->M);
+    const MatvecPlan plan = plan_matvec(w->type, (int64_t)row_count, w->inner, a->M, d->sms);
+    void* ws = nullptr;
+    float* partial = nullptr;
+    uint32_t* counters = nullptr;
+    if (plan.ks > 1) {
+        const size_t off_c = (plan.partial_bytes + 255) / 256 * 256;
+        if (cudaMallocAsync(&ws, off_c + plan.counter_bytes, s) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(PXQ_ERR_NO_MEMORY, "split-K workspace allocation failed");
+        }
+        partial = static_cast<float*>(ws);
+        counters = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + off_c);
+        PXQ_CUDA(cudaMemsetAsync(counters, 0, plan.counter_bytes, s));
+    }
     cudaError_t e = launch_matvec(w->type, w->raw + row_first * w->stride, w->stride, row_count, w->inner, a->mem, a->M,
-                                  output, ldy, bias, s);
+                                  output, ldy, bias, plan, partial, counters, s);
+    if (ws) cudaFreeAsync(ws, s);
     if (counted(e) != cudaSuccess) return fail(PXQ_ERR_CUDA, "matvec launch failed: %s", cudaGetErrorString(e));
     return PXQ_OK;
 }
@@ -427,7 +442,7 @@ int run_matmul(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, 
     pxq_activation* a = nullptr;
     int rc = quantize_activation(d, w->type, input, (int64_t)columns, w->inner, force, &a, s);
     if (rc) return rc;
-    rc = a->blocks ? run_matvec(w, row_first, row_count, a, output, ldy, bias, s)
+    rc = a->blocks ? run_matvec(d, w, row_first, row_count, a, output, ldy, bias, s)
                    : run_gemm(d, w, row_first, row_count, a, output, ldy, bias, dump, s);
     free_activation(a, s);
     return rc;
@@ -437,6 +452,8 @@ int run_matmul(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, 
 
 namespace pxq {
 // Read-only view of a weight handle (used by noalloc.cu).
+int device_sm_count(int device) { return (device >= 0 && device < kMaxDevices && g_dev[device].ready) ? g_dev[device].sms : 148; }
+
 bool weight_view(const pxq_weight* w, uint32_t* type, int64_t* inner, int64_t* rows, int64_t* stride, const uint8_t** raw,
                  int* device)
 {
@@ -659,7 +676,7 @@ int pxq_matmul_quantized(pxq_weight* w, size_t row_first, size_t row_count, cons
     if (int rc = check_matmul_args(w, row_first, row_count, a, a ? (size_t)a->M : 0, output, ldy)) return rc;
     if (int rc = check_activation(w, a)) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    return a->blocks ? run_matvec(w, row_first, row_count, a, output, ldy, bias, s)
+    return a->blocks ? run_matvec(d, w, row_first, row_count, a, output, ldy, bias, s)
                      : run_gemm(d, w, row_first, row_count, a, output, ldy, bias, nullptr, s);
 }
 

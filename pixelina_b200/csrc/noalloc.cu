@@ -19,11 +19,16 @@
 // does the set-up (and may make the runtime load this module); make it before
 // any stream capture.
 //
+// Layout of the array per call: the quantized activation rows, then (when the
+// matvec splits K over several CTAs) the fp32 partial sums and one counter per
+// 16-row group.  The counters must start at zero, so each call clears them
+// with cudaMemsetAsync on its stream before launching; every other byte the
+// kernels read is written earlier in the same call.
+//
 // Sharing: every call on a device uses the same array and it keeps the last
-// call's contents.  The quantize kernel rewrites every scratch byte the
-// matvec later reads, so nothing needs clearing, but two calls whose work
-// overlaps on the GPU (different streams without ordering) race on the array;
-// order them on one stream or with events.
+// call's contents.  Two calls whose work overlaps on the GPU (different
+// streams without ordering) race on the array; order them on one stream or
+// with events.
 #include <cstdio>
 #include <mutex>
 
@@ -46,6 +51,7 @@ namespace pxq {
 bool weight_view(const pxq_weight* w, uint32_t* type, int64_t* inner, int64_t* rows, int64_t* stride, const uint8_t** raw,
                  int* device);
 void record_error(const char* msg);
+int device_sm_count(int device);
 }
 
 namespace {
@@ -72,12 +78,20 @@ extern "C" int pxq_matvec_noalloc(pxq_weight* w, size_t row_first, size_t row_co
     if (ldy < row_count && columns > 1) return noalloc_fail(PXQ_ERR_INVALID, "ldy < row_count");
     if (type != pxq::kTypeQ8_0 && type != pxq::kTypeQ5_K) return noalloc_fail(PXQ_ERR_UNSUPPORTED, "weight type not supported");
     const bool q5 = type == pxq::kTypeQ5_K;
-    const uint64_t need = (uint64_t)columns * (uint64_t)(q5 ? inner / pxq::kQKK : inner / pxq::kQK8_0) *
-                          (uint64_t)(q5 ? pxq::kQ8KBytes : pxq::kQ8_0Bytes);
-    if (need + 64 > PXQ_NOALLOC_SCRATCH_BYTES) {
+    // the static array holds the quantized activation rows and, when the
+    // matvec splits K over several CTAs, its partial sums and counters
+    const uint64_t act = (uint64_t)columns * (uint64_t)(q5 ? inner / pxq::kQKK : inner / pxq::kQK8_0) *
+                         (uint64_t)(q5 ? pxq::kQ8KBytes : pxq::kQ8_0Bytes);
+    int cur_dev = -1;
+    cudaGetDevice(&cur_dev);
+    const pxq::MatvecPlan plan = pxq::plan_matvec(type, (int64_t)row_count, inner, (int64_t)columns, pxq::device_sm_count(cur_dev));
+    const uint64_t off_partial = (act + 64 + 255) / 256 * 256;
+    const uint64_t off_counters = (off_partial + plan.partial_bytes + 255) / 256 * 256;
+    const uint64_t need = off_counters + plan.counter_bytes;
+    if (need > PXQ_NOALLOC_SCRATCH_BYTES) {
         char msg[200];
-        snprintf(msg, sizeof(msg), "activation needs %llu bytes of scratch; the static scratch holds %d bytes "
-                 "(PXQ_NOALLOC_SCRATCH_BYTES, 64 reserved)", (unsigned long long)need, PXQ_NOALLOC_SCRATCH_BYTES);
+        snprintf(msg, sizeof(msg), "this call needs %llu bytes of scratch; the static scratch holds %d bytes "
+                 "(PXQ_NOALLOC_SCRATCH_BYTES)", (unsigned long long)need, PXQ_NOALLOC_SCRATCH_BYTES);
         return noalloc_fail(PXQ_ERR_UNSUPPORTED, msg);
     }
     int dev = -1;
@@ -100,11 +114,17 @@ extern "C" int pxq_matvec_noalloc(pxq_weight* w, size_t row_first, size_t row_co
         scratch = g_scratch_ptr[dev];
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    cudaError_t e = q5 ? pxq::launch_quantize_q8_K_blocks(input, scratch, (int64_t)columns, inner, inner, s)
-                       : pxq::launch_quantize_q8_0_blocks(input, scratch, (int64_t)columns, inner, inner, s);
+    uint8_t* base = static_cast<uint8_t*>(scratch);
+    float* partial = plan.ks > 1 ? reinterpret_cast<float*>(base + off_partial) : nullptr;
+    uint32_t* counters = plan.ks > 1 ? reinterpret_cast<uint32_t*>(base + off_counters) : nullptr;
+    cudaError_t e = cudaSuccess;
+    if (counters) e = cudaMemsetAsync(counters, 0, plan.counter_bytes, s);  // counters start at zero
+    if (e == cudaSuccess)
+        e = q5 ? pxq::launch_quantize_q8_K_blocks(input, scratch, (int64_t)columns, inner, inner, s)
+               : pxq::launch_quantize_q8_0_blocks(input, scratch, (int64_t)columns, inner, inner, s);
     if (e == cudaSuccess)
         e = pxq::launch_matvec(type, raw + row_first * stride, stride, (int64_t)row_count, inner, scratch, (int64_t)columns,
-                               output, (int64_t)ldy, bias, s);
+                               output, (int64_t)ldy, bias, plan, partial, counters, s);
     if (e != cudaSuccess) {
         char msg[200];
         snprintf(msg, sizeof(msg), "kernel launch failed: %s", cudaGetErrorString(e));

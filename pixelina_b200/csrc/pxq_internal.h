@@ -44,8 +44,21 @@ cudaError_t launch_decode(const uint8_t* data, uint32_t type, int64_t count, flo
 
 // ---- matvec.cu -------------------------------------------------------------
 // y[c*ldy + r] = dot(W row r, X row c) for c < columns <= 8, raw GGUF weights.
+// The plan splits K over `ks` CTAs per 16-row group when rows are few; then
+// the launch needs `partial_bytes` of fp32 workspace and `counter_bytes` of
+// counters that are zero at launch (the kernel leaves them zero again).
+struct MatvecPlan {
+    int ks = 1;               // K slices per row group
+    int chunk = 0;            // K blocks per slice
+    int64_t rowgroups = 0;    // 16-row groups
+    size_t smem_bytes = 0;    // dynamic shared memory per CTA
+    size_t partial_bytes = 0; // split-K workspace (0 when ks == 1)
+    size_t counter_bytes = 0;
+};
+MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t columns, int num_sms);
 cudaError_t launch_matvec(uint32_t type, const uint8_t* w, int64_t stride, int64_t rows, int64_t inner, const void* xq,
-                          int64_t columns, float* y, int64_t ldy, const float* bias, cudaStream_t s);
+                          int64_t columns, float* y, int64_t ldy, const float* bias, const MatvecPlan& plan, float* partial,
+                          uint32_t* counters, cudaStream_t s);
 
 // ---- shards.cu -------------------------------------------------------------
 cudaError_t launch_gather_shards(const float* src, int64_t shards, int64_t columns, int64_t shard_rows, float* dst,
