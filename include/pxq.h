@@ -184,17 +184,17 @@ PXQ_API uint64_t pxq_kernel_launches(void);
  * static device array of PXQ_NOALLOC_SCRATCH_BYTES owned by this library
  * (held on every device that loads it, until exit) instead of freshly
  * allocated scratch.  The array holds the quantized activation rows
- * (columns * inner/32 * 34 bytes for Q8_0, columns * inner/256 * 292 for
- * Q5_K) and, for shapes the matvec splits along K, its fp32 partial sums
- * (up to a few hundred KB for 8 columns); a call whose total exceeds
- * PXQ_NOALLOC_SCRATCH_BYTES is rejected with PXQ_ERR_UNSUPPORTED before any
- * work is queued.
+ * (columns * inner/32 * 34 bytes for Q8_0, columns * inner/256 * 288 for
+ * Q5_K) and the matvec's fp32 partial sums (up to 2 * columns * 256 bytes
+ * per CTA, about 1.2 MB for 8 columns on a 148-SM GPU); a call whose total
+ * exceeds PXQ_NOALLOC_SCRATCH_BYTES is rejected with PXQ_ERR_UNSUPPORTED
+ * before any work is queued.
  * The weight must already be uploaded and the current device must be the
  * weight's.  The first call on a device looks up the array's device address
  * (one-time set-up); make that call before any stream capture.  All calls on
  * a device share the array: calls whose GPU work may overlap (unordered
  * streams) race, so order them. */
-#define PXQ_NOALLOC_SCRATCH_BYTES (1 << 20)
+#define PXQ_NOALLOC_SCRATCH_BYTES (4 << 20)
 
 PXQ_API int pxq_matvec_noalloc(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns,
                                float* output, size_t ldy, const float* bias, void* stream);

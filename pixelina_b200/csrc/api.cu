@@ -7,8 +7,9 @@
 //     built GEMM operand copy (repack.cu), keyed like the Vulkan backend's
 //     cache (src/backend_vulkan.cpp:742-758);
 //   * dispatch of a matmul to the streaming matvec (columns <= 8) or the
-//     tensor-core GEMM, with per-call scratch from the stream-ordered
-//     allocator;
+//     tensor-core GEMM; the matvec's scratch is a buffer kept per (device,
+//     stream) so a steady decode loop allocates nothing, the GEMM's comes
+//     from the stream-ordered allocator;
 //   * the host-buffer cpu_quant_matmul drop-in.
 // There is no CPU compute path here: an unsupported case is reported as an
 // error status (the reference's `false`), never computed on the host.
@@ -22,6 +23,7 @@
 #include <mutex>
 #include <string>
 #include <unordered_map>
+#include <vector>
 
 #include "pxq.h"
 #include "pxq_internal.h"
@@ -131,6 +133,22 @@ int make_map(const DeviceCtx* d, CUtensorMap* m, CUtensorMapDataType dt, const v
     return PXQ_OK;
 }
 
+// 3-D tiled map: dims {d0, d1, d2}, byte strides {s1, s2}, box {b0, b1, b2}.
+int make_map3(const DeviceCtx* d, CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1,
+              uint64_t d2, uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2)
+{
+    const cuuint64_t dims[3] = {d0, d1, d2};
+    const cuuint64_t strides[2] = {s1, s2};
+    const cuuint32_t box[3] = {b0, b1, b2};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = d->encode(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(PXQ_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d): dims %llu x %llu x %llu box %u x %u x %u", (int)r,
+                    (unsigned long long)d0, (unsigned long long)d1, (unsigned long long)d2, b0, b1, b2);
+    return PXQ_OK;
+}
+
 // GEMM operand copy of (a row range of) a weight.
 struct Packed {
     int64_t rows = 0;   // packed rows
@@ -154,6 +172,7 @@ struct pxq_weight {
     int64_t inner = 0, rows = 0, stride = 0;
     int device = 0;
     uint8_t* raw = nullptr;
+    CUtensorMap mv_map[kMvTileShapes];  // Q5_K: raw bytes as u64 [rows][stride/8], the matvec's TMA views
     std::string key;
     std::unique_ptr<Packed> packed;                       // whole tensor
     std::map<std::pair<int64_t, int64_t>, std::unique_ptr<Packed>> views;  // unaligned row views
@@ -163,12 +182,13 @@ struct pxq_weight {
     }
 };
 
-// A quantized activation: GGUF blocks (matvec, columns <= 8) or the
-// tensor-core operand layout (GEMM), in one stream-ordered allocation.
+// A quantized activation: the matvec operand (columns <= 8: Q8_0 blocks, or
+// the Q8_K matvec records) or the tensor-core operand layout (GEMM), in one
+// stream-ordered allocation.
 struct pxq_activation {
     uint32_t wtype = 0;     // weight type it was quantized for
     int64_t M = 0, K = 0;
-    bool blocks = false;    // true: Q8_0/Q8_K blocks; false: GEMM operand
+    bool blocks = false;    // true: matvec operand; false: GEMM operand
     void* mem = nullptr;
     __half* xq = nullptr;   // operand: exact fp16 quants [M][K]
     void* scale = nullptr;  // operand: Q8_0 fp16 scales [M][ldd] / Q8_K fp32 d [nsb][ldd]
@@ -176,6 +196,12 @@ struct pxq_activation {
     int64_t ldd = 0;
     CUtensorMap tmX, tmXs, tmDx;
 };
+
+namespace pxq {
+cudaError_t matvec_fused(const pxq_weight* w, size_t row_first, size_t row_count, const float* input, float* output,
+                         size_t ldy, const float* bias, const MatvecPlan& plan, uint8_t* scratch, uint32_t* status,
+                         cudaStream_t s);
+}
 
 namespace {
 
@@ -298,12 +324,12 @@ int quantize_activation(DeviceCtx* d, uint32_t wtype, const float* input, int64_
     const int64_t nb = q5 ? K / kQKK : K / kQK8_0;
     cudaError_t e;
     if (a->blocks) {
-        const size_t bytes = (size_t)M * nb * (q5 ? kQ8KBytes : kQ8_0Bytes);
-        if (cudaMallocAsync(&a->mem, bytes + 64, s) != cudaSuccess) {
+        const MatvecPlan plan = plan_matvec(wtype, 1, K, M, d->sms);
+        if (cudaMallocAsync(&a->mem, plan.act_bytes, s) != cudaSuccess) {
             cudaGetLastError();
-            return fail(PXQ_ERR_NO_MEMORY, "scratch allocation of %zu bytes failed", bytes);
+            return fail(PXQ_ERR_NO_MEMORY, "scratch allocation of %zu bytes failed", plan.act_bytes);
         }
-        e = q5 ? launch_quantize_q8_K_blocks(input, a->mem, M, K, K, s) : launch_quantize_q8_0_blocks(input, a->mem, M, K, K, s);
+        e = launch_matvec_quantize(plan, input, K, a->mem, nullptr, s);
     } else {
         a->ldd = q5 ? round_up(M, 4) : round_up(nb, 8);
         const size_t xq_bytes = (size_t)M * K * 2;
@@ -353,29 +379,71 @@ void free_activation(pxq_activation* a, cudaStream_t s)
     delete a;
 }
 
+// Matvec of a pre-quantized activation: partial sums and counters from the
+// stream-ordered allocator, counters cleared by a memset.
 int run_matvec(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, const pxq_activation* a, float* output,
                size_t ldy, const float* bias, cudaStream_t s)
 {
     if (!a->blocks) return fail(PXQ_ERR_UNSUPPORTED, "matvec handles at most 8 columns (got %lld)", (long long)a->M);
     const MatvecPlan plan = plan_matvec(w->type, (int64_t)row_count, w->inner, a->M, d->sms);
+    const size_t ws_bytes = plan.total_bytes - plan.off_partial;
     void* ws = nullptr;
     float* partial = nullptr;
     uint32_t* counters = nullptr;
-    if (plan.ks > 1) {
-        const size_t off_c = (plan.partial_bytes + 255) / 256 * 256;
-        if (cudaMallocAsync(&ws, off_c + plan.counter_bytes, s) != cudaSuccess) {
+    if (ws_bytes) {
+        if (cudaMallocAsync(&ws, ws_bytes, s) != cudaSuccess) {
             cudaGetLastError();
-            return fail(PXQ_ERR_NO_MEMORY, "split-K workspace allocation failed");
+            return fail(PXQ_ERR_NO_MEMORY, "matvec workspace allocation failed");
         }
         partial = static_cast<float*>(ws);
-        counters = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + off_c);
-        PXQ_CUDA(cudaMemsetAsync(counters, 0, plan.counter_bytes, s));
+        counters = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + (plan.off_counters - plan.off_partial));
+        if (plan.counter_bytes) PXQ_CUDA(cudaMemsetAsync(counters, 0, plan.counter_bytes, s));
     }
-    cudaError_t e = launch_matvec(w->type, w->raw + row_first * w->stride, w->stride, row_count, w->inner, a->mem, a->M,
-                                  output, ldy, bias, plan, partial, counters, s);
+    cudaError_t e = launch_matvec(plan, w->mv_map, (int64_t)row_first, w->raw + row_first * w->stride, w->stride, a->mem,
+                                  output, (int64_t)ldy, bias, partial, counters, d->status, s);
     if (ws) cudaFreeAsync(ws, s);
     if (counted(e) != cudaSuccess) return fail(PXQ_ERR_CUDA, "matvec launch failed: %s", cudaGetErrorString(e));
     return PXQ_OK;
+}
+
+// Scratch kept per (device, stream) for the fused quantize + matvec, so that
+// a steady decode loop makes no allocation (and no allocator node separates
+// its kernels in a captured graph).  Work on one stream is ordered, so one
+// buffer per stream is race-free.  A buffer is only replaced when a call
+// needs more; the old one is kept for the life of the process because a
+// captured graph may still name it.
+struct StreamScratch {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+std::map<std::pair<int, cudaStream_t>, StreamScratch> g_stream_scratch;  // guarded by g_mutex
+std::vector<void*> g_retired_scratch;                                     // guarded by g_mutex
+
+// The stream's scratch (at least `need` bytes), or null when no device memory
+// is left.  Growing it during a stream capture is allowed: like PyTorch's
+// allocator, the cudaMalloc runs with this thread's capture mode relaxed, so
+// the buffer outlives the graph and no allocator node enters it.
+void* stream_scratch(int device, cudaStream_t s, size_t need)
+{
+    std::lock_guard<std::mutex> lock(g_mutex);
+    StreamScratch& e = g_stream_scratch[{device, s}];
+    if (e.bytes >= need) return e.ptr;
+    size_t bytes = need > 2 * e.bytes ? need : 2 * e.bytes;
+    if (bytes < ((size_t)4 << 20)) bytes = (size_t)4 << 20;
+    bytes = (bytes + ((size_t)1 << 20) - 1) & ~(((size_t)1 << 20) - 1);
+    void* p = nullptr;
+    cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+    cudaThreadExchangeStreamCaptureMode(&mode);
+    const cudaError_t err = cudaMalloc(&p, bytes);
+    cudaThreadExchangeStreamCaptureMode(&mode);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    if (e.ptr) g_retired_scratch.push_back(e.ptr);
+    e.ptr = p;
+    e.bytes = bytes;
+    return p;
 }
 
 int run_gemm(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, const pxq_activation* a, float* output,
@@ -439,11 +507,25 @@ int run_matmul(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, 
     if (w->type == kTypeQ8_0 || w->type == kTypeQ5_K) {
         if (w->inner % 8) return fail(PXQ_ERR_UNSUPPORTED, "inner %lld not a multiple of 8", (long long)w->inner);
     }
+    if (force == 1 || (force == 0 && columns <= 8)) {
+        if (!input) return fail(PXQ_ERR_INVALID, "null input");
+        const MatvecPlan plan = plan_matvec(w->type, (int64_t)row_count, w->inner, (int64_t)columns, d->sms);
+        void* scratch = stream_scratch(t_device, s, plan.total_bytes);
+        const bool own = scratch == nullptr;
+        if (own && cudaMallocAsync(&scratch, plan.total_bytes, s) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(PXQ_ERR_NO_MEMORY, "matvec scratch allocation of %zu bytes failed", plan.total_bytes);
+        }
+        cudaError_t e = matvec_fused(w, row_first, row_count, input, output, ldy, bias, plan, static_cast<uint8_t*>(scratch),
+                                     d->status, s);
+        if (own) cudaFreeAsync(scratch, s);
+        if (e != cudaSuccess) return fail(PXQ_ERR_CUDA, "matvec launch failed: %s", cudaGetErrorString(e));
+        return PXQ_OK;
+    }
     pxq_activation* a = nullptr;
     int rc = quantize_activation(d, w->type, input, (int64_t)columns, w->inner, force, &a, s);
     if (rc) return rc;
-    rc = a->blocks ? run_matvec(d, w, row_first, row_count, a, output, ldy, bias, s)
-                   : run_gemm(d, w, row_first, row_count, a, output, ldy, bias, dump, s);
+    rc = run_gemm(d, w, row_first, row_count, a, output, ldy, bias, dump, s);
     free_activation(a, s);
     return rc;
 }
@@ -451,8 +533,25 @@ int run_matmul(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, 
 }  // namespace
 
 namespace pxq {
+// Quantize + matvec with all scratch in `scratch` (plan.total_bytes, 256-byte
+// aligned): the quantize kernel clears the counters, both kernels are
+// launched with programmatic stream serialization.
+cudaError_t matvec_fused(const pxq_weight* w, size_t row_first, size_t row_count, const float* input, float* output,
+                         size_t ldy, const float* bias, const MatvecPlan& plan, uint8_t* scratch, uint32_t* status,
+                         cudaStream_t s)
+{
+    float* partial = plan.partial_bytes ? reinterpret_cast<float*>(scratch + plan.off_partial) : nullptr;
+    uint32_t* counters = plan.counter_bytes ? reinterpret_cast<uint32_t*>(scratch + plan.off_counters) : nullptr;
+    cudaError_t e = counted(launch_matvec_quantize(plan, input, w->inner, scratch, counters, s));
+    if (e == cudaSuccess)
+        e = counted(launch_matvec(plan, w->mv_map, (int64_t)row_first, w->raw + row_first * w->stride, w->stride, scratch,
+                                  output, (int64_t)ldy, bias, partial, counters, status, s));
+    return e;
+}
+
 // Read-only view of a weight handle (used by noalloc.cu).
 int device_sm_count(int device) { return (device >= 0 && device < kMaxDevices && g_dev[device].ready) ? g_dev[device].sms : 148; }
+uint32_t* device_status(int device) { return (device >= 0 && device < kMaxDevices && g_dev[device].ready) ? g_dev[device].status : nullptr; }
 
 bool weight_view(const pxq_weight* w, uint32_t* type, int64_t* inner, int64_t* rows, int64_t* stride, const uint8_t** raw,
                  int* device)
@@ -559,7 +658,8 @@ int pxq_weight_upload(const void* bytes, int bytes_on_device, uint32_t type, siz
     if (type != PXQ_TYPE_Q8_0 && type != PXQ_TYPE_Q5_K) return fail(PXQ_ERR_UNSUPPORTED, "weight type %u not supported", type);
     const uint64_t total = pxq_weight_bytes(inner, rows, type);
     if (!total) return fail(PXQ_ERR_INVALID, "invalid weight shape [%zu, %zu] for type %u", inner, rows, type);
-    if (inner > 0x7fffffffu) return fail(PXQ_ERR_UNSUPPORTED, "inner %zu exceeds INT32_MAX", inner);
+    if (inner > 0x7fffffffu || rows > 0x7fffffffu)
+        return fail(PXQ_ERR_UNSUPPORTED, "weight shape [%zu, %zu] exceeds INT32_MAX", inner, rows);
     std::string k = key ? std::string(key) : std::string();
     if (!k.empty()) {
         std::lock_guard<std::mutex> lock(g_mutex);
@@ -582,6 +682,24 @@ int pxq_weight_upload(const void* bytes, int bytes_on_device, uint32_t type, siz
     }
     PXQ_CUDA(cudaMemset(w->raw + total, 0, 64));
     PXQ_CUDA(cudaMemcpy(w->raw, bytes, total, bytes_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
+    std::memset(w->mv_map, 0, sizeof(w->mv_map));
+    if (type == PXQ_TYPE_Q5_K) {
+        // the matvec's TMA views, one box = one stage of a tr-row tile
+        // (kMvStageSuperBlocks*16/tr super-blocks): 64 rows as a 2-D view
+        // (rows of stride/8 64-bit words), 32 and 16 rows as a 3-D view
+        // (super-block, row, 22 words) that lands super-block-major
+        const uint64_t nsb = inner / 256;
+        if (int rc = make_map(d, &w->mv_map[matvec_map_index(64)], CU_TENSOR_MAP_DATA_TYPE_UINT64, w->raw,
+                              (uint64_t)w->stride / 8, rows, (uint64_t)w->stride,
+                              (uint32_t)(kMvStageSuperBlocks / 4 * kQ5KBytes / 8), 64, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return rc;
+        for (int tr : {32, 16}) {
+            if (int rc = make_map3(d, &w->mv_map[matvec_map_index(tr)], CU_TENSOR_MAP_DATA_TYPE_UINT64, w->raw,
+                                   kQ5KBytes / 8, rows, nsb, (uint64_t)w->stride, kQ5KBytes, kQ5KBytes / 8, (uint32_t)tr,
+                                   (uint32_t)(kMvStageSuperBlocks * 16 / tr)))
+                return rc;
+        }
+    }
     pxq_weight* raw = w.release();
     if (!k.empty()) {
         std::lock_guard<std::mutex> lock(g_mutex);

@@ -2,27 +2,39 @@
 //
 // Restates, for columns <= 8, the inner loop of cpu_quant_matmul
 // (src/kernels_quant.cpp:389-400) with the dots pix_dot_q8_0 (:339-365) and
-// pix_dot_q5_K (:163-254) on GPU: activations are the reference's Q8_0 /
-// Q8_K blocks (produced by quantize.cu), weights stream straight from the raw
-// GGUF rows in HBM.
+// pix_dot_q5_K (:163-254) on GPU: activations are quantized exactly as the
+// reference quantizes them (quantize.cu), weights stream straight from the
+// raw GGUF rows in HBM.  Every 32-value block dot is one int8 tensor-core
+// mma.sync m16n8k32: A = 16 weight rows unpacked in registers, B = the up-to-8
+// activation rows (n = activation row, zero-padded), so one weight fragment
+// serves all rows.  The exact int32 block dot comes out of the MMA; the
+// per-block fp32 scaling and the Q5_K sub-block scales / min term are applied
+// exactly as the reference does (int32 super-block sums, then one fp32 FMA
+// per super-block).  The K order inside a 32-block is permuted identically for
+// A and B (a dot product does not depend on the order of its terms) so that
+// each thread's 8 weight bytes per block are contiguous in memory.  All sums
+// across warps, stages and CTAs are taken in a fixed order: results are
+// deterministic.
 //
-// Mapping.  A CTA of 4 warps owns 16 weight rows and a range of K blocks
-// (the whole row, or a 1/ks slice when there are too few row groups to fill
-// the GPU -- split-K).  Its warps walk the K blocks round-robin, each with the
-// next block's weight bytes already in flight (register double buffering);
-// the small activation blocks are read through L1, shared by all CTAs.
-// Each 32-value block is one int8 tensor-core mma.sync m16n8k32: A = the 16
-// weight rows unpacked in registers, B = the up-to-8 activation rows
-// (n = activation row, zero-padded), so one weight fragment serves all rows.
-// The exact int32 block dot comes out of the MMA; the per-block fp32 scaling
-// and the Q5_K sub-block scales / min term are applied in registers exactly
-// as the reference does (int32 super-block sums, then one fp32 FMA per
-// super-block).  The K order inside a 32-block is permuted identically for A
-// and B (a dot product does not depend on the order of its terms) so that
-// each thread's 8 weight bytes per block are contiguous in memory.
-// Partials of the 4 warps are summed in shared memory in fixed order; with
-// split-K the slices are summed, again in fixed order, by the last CTA of the
-// row group to finish.  Results are therefore deterministic.
+// Q5_K (the decode format): a persistent, warp-specialised stream-K kernel.
+// One producer warp streams 64-row x 2-super-block weight tiles (22.5 KB),
+// and the matching activation records, into a 4-stage shared-memory ring with
+// TMA / bulk copies; eight consumer warps (4 row groups x 2 super-block
+// halves) unpack them into MMA fragments.  The stage sequence of all tiles is
+// split evenly over one CTA per SM, so every SM streams the same number of
+// bytes whatever the matrix shape; a tile shared by several CTAs is summed,
+// in CTA order, by the last to finish.  Launched with programmatic stream
+// serialization, and sized (110 KB of shared memory, 288 threads) so that a
+// CTA of the next such kernel fits on the same SM: the producer requests its
+// first stages' weights as soon as the CTA is resident, while the kernels
+// before it still run, and waits for them (griddep_wait) before it fetches
+// activations; the consumers wait before touching any output.
+//
+// Q8_0: a CTA of 4 warps owns 16 weight rows and a range of K blocks (the
+// whole row, or a 1/ks slice when there are too few row groups to fill the
+// GPU); warps walk the blocks round-robin with the next block's weight bytes
+// in flight (register double buffering).
+#include "pxq_device.cuh"
 #include "pxq_internal.h"
 
 namespace pxq {
@@ -54,6 +66,23 @@ __device__ __forceinline__ uint2 ld8_unaligned(const uint8_t* p)
 __device__ __forceinline__ float ld_half(const uint8_t* p)
 {
     return __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short*>(p))));
+}
+
+// The same two loads for activation bytes, which the kernel before this one
+// writes (coherent loads, see ld_dep_u32).
+__device__ __forceinline__ uint2 ld8_unaligned_dep(const uint8_t* p)
+{
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~(uintptr_t)3);
+    const uint32_t sh = (uint32_t)(a & 3u) * 8u;
+    const uint32_t w0 = ld_dep_u32(w), w1 = ld_dep_u32(w + 1);
+    const uint32_t w2 = sh ? ld_dep_u32(w + 2) : 0u;
+    return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
+}
+
+__device__ __forceinline__ float ld_half_dep(const uint8_t* p)
+{
+    return __half2float(__ushort_as_half(ld_dep_u16(p)));
 }
 
 // Cross-warp sum (fixed order), then either the final store or the split-K
@@ -105,7 +134,7 @@ __device__ __forceinline__ void finish(float (&part)[kWarps][kRowsPerCta][8], in
 // ---------------------------------------------------------------- Q8_0 ------
 
 __global__ void __launch_bounds__(kThreads) k_matvec_q8_0(const uint8_t* __restrict__ w, int64_t stride, int64_t rows,
-                                                          int64_t inner, const uint8_t* __restrict__ xq, int64_t columns,
+                                                          int64_t inner, const uint8_t* xq, int64_t columns,
                                                           float* __restrict__ y, int64_t ldy, const float* __restrict__ bias,
                                                           int ks, int chunk, float* __restrict__ partial,
                                                           uint32_t* __restrict__ counters)
@@ -133,10 +162,14 @@ __global__ void __launch_bounds__(kThreads) k_matvec_q8_0(const uint8_t* __restr
     int64_t b = b0 + warp;
     uint2 qa = make_uint2(0, 0), qb = make_uint2(0, 0);
     float dwa = 0.f, dwb = 0.f;
+    griddep_launch_dependents();
     if (b < b1) {
         if (va) { qa = ld8_unaligned(wa + b * kQ8_0Bytes + 2 + 8 * t); dwa = ld_half(wa + b * kQ8_0Bytes); }
         if (vb) { qb = ld8_unaligned(wb + b * kQ8_0Bytes + 2 + 8 * t); dwb = ld_half(wb + b * kQ8_0Bytes); }
     }
+    // weights above are read-only; the activation, outputs and split-K
+    // scratch belong to the kernels before this one
+    griddep_wait();
     for (; b < b1; b += kWarps) {
         // next block's weights in flight while this one computes
         uint2 na = make_uint2(0, 0), nbv = make_uint2(0, 0);
@@ -147,11 +180,11 @@ __global__ void __launch_bounds__(kThreads) k_matvec_q8_0(const uint8_t* __restr
             if (vb) { nbv = ld8_unaligned(wb + bn * kQ8_0Bytes + 2 + 8 * t); ndwb = ld_half(wb + bn * kQ8_0Bytes); }
         }
         const int64_t off = (b - b0) * kQ8_0Bytes;
-        const uint2 qx = vx ? ld8_unaligned(xr + off + 2 + 8 * t) : make_uint2(0, 0);
+        const uint2 qx = vx ? ld8_unaligned_dep(xr + off + 2 + 8 * t) : make_uint2(0, 0);
         const uint32_t a[4] = {qa.x, qb.x, qa.y, qb.y};
         int d[4];
         mma_s8(d, a, qx.x, qx.y);
-        const float dx0 = ld_half(xc0 + off), dx1 = ld_half(xc1 + off);
+        const float dx0 = ld_half_dep(xc0 + off), dx1 = ld_half_dep(xc1 + off);
         // pix_dot_q8_0: acc = fma(fp16(dw) * fp16(dx), float(block dot), acc)
         acc[0] = __fmaf_rn(__fmul_rn(dwa, dx0), (float)d[0], acc[0]);
         acc[1] = __fmaf_rn(__fmul_rn(dwa, dx1), (float)d[1], acc[1]);
@@ -171,187 +204,487 @@ __global__ void __launch_bounds__(kThreads) k_matvec_q8_0(const uint8_t* __restr
 
 // ---------------------------------------------------------------- Q5_K ------
 
-__device__ __forceinline__ void unpack_scales(const uint4 hdr, int (&sc)[8], int (&mn)[8])
-{
-    // bytes 4..15 of the super-block: the 12 packed 6-bit scales/mins
-    const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
-    const uint8_t s[12] = {(uint8_t)s0, (uint8_t)(s0 >> 8), (uint8_t)(s0 >> 16), (uint8_t)(s0 >> 24),
-                           (uint8_t)s1, (uint8_t)(s1 >> 8), (uint8_t)(s1 >> 16), (uint8_t)(s1 >> 24),
-                           (uint8_t)s2, (uint8_t)(s2 >> 8), (uint8_t)(s2 >> 16), (uint8_t)(s2 >> 24)};
-#pragma unroll
-    for (int g = 0; g < 4; g++) {
-        sc[g] = s[g] & 63;
-        mn[g] = s[g + 4] & 63;
-        sc[g + 4] = (s[g + 8] & 15) | ((s[g] >> 6) << 4);
-        mn[g + 4] = (s[g + 8] >> 4) | ((s[g + 4] >> 6) << 4);
-    }
-}
-
-// One thread's share of a super-block of its two weight rows (g and g+8).
-struct Q5Frag {
-    uint4 ha, hb;      // d, dmin, scales
-    uint2 qha, qhb;    // high bits, bytes 8t..8t+7
-    uint2 qsa[4], qsb[4];
+// Tile shapes: TR weight rows x 128/TR super-blocks per stage.  Every stage is
+// 22.5 KB of weights; consumer warp w takes rows 16*(w % (TR/16)) .. +15 of
+// the tile and super-block w / (TR/16) of the stage, so all eight warps work
+// on every stage whatever the shape.  The 64-row stage lands in shared memory
+// row-major ([64][352 B], a 2-D box); the 32- and 16-row stages super-block-
+// major ([sb][TR][176 B], a 3-D box), because a row pitch of 704 or 1408
+// bytes would put all rows of a fragment load in the same banks.
+template <int TR>
+struct MvShape {
+    static constexpr int kRowGroups = TR / 16;                      // 16-row MMA groups per tile
+    static constexpr int kSbs = kMvStageSuperBlocks / kRowGroups;    // super-blocks per stage
+    static constexpr int kRowBytes = kSbs * kQ5KBytes;              // one row's bytes per stage
+    static constexpr int kRowPitch = TR == 64 ? kRowBytes : kQ5KBytes;    // shared-memory row pitch
+    static constexpr int kSbPitch = TR == 64 ? kQ5KBytes : TR * kQ5KBytes; // shared-memory super-block pitch
+    static constexpr int kWeightBytes = TR * kRowBytes;             // 22528
+    static constexpr int kActPitch = kSbs * kQ8KMvBytes;            // one activation row's records per stage
+    static constexpr int kActBytes = 8 * kActPitch;                 // up to 8 activation rows
+    static constexpr int kStages = TR == 16 ? 2 : 3;                // two CTAs per SM within 228 KB
+    static_assert(kRowBytes % 16 == 0 && kActPitch % 16 == 0, "bulk copies move 16-byte multiples");
+    static_assert(kWeightBytes == kMvStageWeightBytes, "every shape streams the same stage size");
 };
 
-__device__ __forceinline__ void load_q5(Q5Frag& f, const uint8_t* ba, const uint8_t* bb, bool va, bool vb, uint32_t t)
+constexpr int kMvConsumers = 8;
+constexpr int kMvThreads = (kMvConsumers + 1) * 32;  // + 1 producer warp
+
+template <int TR>
+struct MvSmem {
+    using Sh = MvShape<TR>;
+    uint8_t weight[Sh::kStages][Sh::kWeightBytes];  // [TR][kSbs x 176] (TR = 64) or [kSbs][TR][176]
+    uint8_t act[Sh::kStages][Sh::kActBytes];        // [8 activation rows][kSbs super-blocks x 288]
+    // sums of warps with super-block lane >= 1, handed to lane 0, by segment parity
+    float red[2][Sh::kSbs - 1][Sh::kRowGroups][16][8];
+    uint64_t full[Sh::kStages], empty[Sh::kStages];
+    uint32_t abort;
+    int last;
+};
+
+struct MvParams {
+    CUtensorMap map;                   // raw weight bytes: 2-D u64 [rows][stride/8], box {kSbs*22, TR} (TR = 64),
+                                       // else 3-D u64 [nsb][rows][22], box {22, TR, kSbs}
+    const uint8_t* act;                // activation records [columns][nsb][kQ8KMvBytes]
+    float* y;
+    const float* bias;
+    float* partial;                    // [grid][2][columns][TR]
+    uint32_t* counters;                // [tiles]
+    uint32_t* status;
+    int64_t ldy, rows, row_first, stages;
+    int32_t nsb, spt, columns;
+};
+
+// First CTA whose stage range [c*S/G, (c+1)*S/G) holds stage s.
+__device__ __forceinline__ int64_t cta_of_stage(int64_t s, int64_t S, int64_t G) { return ((s + 1) * G - 1) / S; }
+
+// Slot (0 or 1) of CTA c's partial sums for tile T: 0 for the first tile of
+// its range, 1 for the last (only the first and last tiles can be partial).
+__device__ __forceinline__ int64_t partial_slot(int64_t c, int64_t T, int64_t S, int64_t G, int64_t spt)
 {
-    f.ha = va ? __ldg(reinterpret_cast<const uint4*>(ba)) : make_uint4(0, 0, 0, 0);
-    f.hb = vb ? __ldg(reinterpret_cast<const uint4*>(bb)) : make_uint4(0, 0, 0, 0);
-    f.qha = va ? __ldg(reinterpret_cast<const uint2*>(ba + 16 + 8 * t)) : make_uint2(0, 0);
-    f.qhb = vb ? __ldg(reinterpret_cast<const uint2*>(bb + 16 + 8 * t)) : make_uint2(0, 0);
-#pragma unroll
-    for (int p = 0; p < 4; p++) {
-        f.qsa[p] = va ? __ldg(reinterpret_cast<const uint2*>(ba + 48 + 32 * p + 8 * t)) : make_uint2(0, 0);
-        f.qsb[p] = vb ? __ldg(reinterpret_cast<const uint2*>(bb + 48 + 32 * p + 8 * t)) : make_uint2(0, 0);
+    return T == (c * S / G) / spt ? 0 : 1;
+}
+
+// Packed 6-bit scales and mins of one super-block header (bytes 4..15 as
+// words h.y, h.z, h.w), four sub-blocks per word: sc[0..3], sc[4..7], m[0..3], m[4..7].
+__device__ __forceinline__ void q5_scales(const uint4 h, uint32_t& sc_lo, uint32_t& sc_hi, uint32_t& mn_lo, uint32_t& mn_hi)
+{
+    sc_lo = h.y & 0x3f3f3f3fu;
+    mn_lo = h.z & 0x3f3f3f3fu;
+    sc_hi = (h.w & 0x0f0f0f0fu) | ((h.y >> 2) & 0x30303030u);
+    mn_hi = ((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u);
+}
+
+// Four 5-bit quants of sub-block J as int8 bytes: the low (E = 0) or high
+// (E = 1) nibbles of q plus bit J of each byte of the high-bit word h.
+template <int J, int E>
+__device__ __forceinline__ uint32_t q5_frag(uint32_t q, uint32_t h)
+{
+    const uint32_t lo = (E ? (q >> 4) : q) & 0x0f0f0f0fu;
+    const uint32_t hs = J <= 4 ? (h << (4 - J)) : (h >> (J - 4));
+    return lo | (hs & 0x10101010u);
+}
+
+// sum_j m_j * bs_j over the 8 sub-blocks: bs = eight int16 32-element sums
+// (two per word), m = eight 6-bit mins (four bytes per word).
+__device__ __forceinline__ int min_dot(const uint4 bs, uint32_t m_lo, uint32_t m_hi)
+{
+    int r = __dp2a_lo((int)bs.x, (int)m_lo, 0);
+    r = __dp2a_hi((int)bs.y, (int)m_lo, r);
+    r = __dp2a_lo((int)bs.z, (int)m_hi, r);
+    return __dp2a_hi((int)bs.w, (int)m_hi, r);
+}
+
+// Sub-blocks 2PR and 2PR+1 of one super-block for weight rows a, b (A) and
+// activation row g (B, zero when vx is false); sca/scb hold the four packed
+// scales of sub-blocks 4*(PR/2) .. 4*(PR/2)+3.  Every lane must call it: the
+// MMA is warp-wide.
+template <int PR>
+__device__ __forceinline__ void q5_pair(const uint8_t* wa, const uint8_t* wb, const uint8_t* xr, bool vx, uint32_t t,
+                                        uint2 qha, uint2 qhb, uint32_t sca, uint32_t scb, int (&sumi)[4])
+{
+    // sub-blocks 2PR (low nibbles) and 2PR+1 (high nibbles) share these qs bytes
+    const uint2 qa = *reinterpret_cast<const uint2*>(wa + 48 + 32 * PR + 8 * t);
+    const uint2 qb = *reinterpret_cast<const uint2*>(wb + 48 + 32 * PR + 8 * t);
+    const uint4 bx = vx ? *reinterpret_cast<const uint4*>(xr + 64 * PR) : make_uint4(0, 0, 0, 0);
+    constexpr int kSh = 16 * (PR & 1);
+    {
+        constexpr int J = 2 * PR;
+        const uint32_t a[4] = {q5_frag<J, 0>(qa.x, qha.x), q5_frag<J, 0>(qb.x, qhb.x), q5_frag<J, 0>(qa.y, qha.y),
+                               q5_frag<J, 0>(qb.y, qhb.y)};
+        int d[4];
+        mma_s8(d, a, bx.x, bx.y);
+        const int s0 = (int)((sca >> kSh) & 0xffu), s1 = (int)((scb >> kSh) & 0xffu);
+        sumi[0] += s0 * d[0];
+        sumi[1] += s0 * d[1];
+        sumi[2] += s1 * d[2];
+        sumi[3] += s1 * d[3];
+    }
+    {
+        constexpr int J = 2 * PR + 1;
+        const uint32_t a[4] = {q5_frag<J, 1>(qa.x, qha.x), q5_frag<J, 1>(qb.x, qhb.x), q5_frag<J, 1>(qa.y, qha.y),
+                               q5_frag<J, 1>(qb.y, qhb.y)};
+        int d[4];
+        mma_s8(d, a, bx.z, bx.w);
+        const int s0 = (int)((sca >> (kSh + 8)) & 0xffu), s1 = (int)((scb >> (kSh + 8)) & 0xffu);
+        sumi[0] += s0 * d[0];
+        sumi[1] += s0 * d[1];
+        sumi[2] += s1 * d[2];
+        sumi[3] += s1 * d[3];
     }
 }
 
-__global__ void __launch_bounds__(kThreads) k_matvec_q5_K(const uint8_t* __restrict__ w, int64_t stride, int64_t rows,
-                                                          int64_t inner, const uint8_t* __restrict__ xq, int64_t columns,
-                                                          float* __restrict__ y, int64_t ldy, const float* __restrict__ bias,
-                                                          int ks, int chunk, float* __restrict__ partial,
-                                                          uint32_t* __restrict__ counters)
+__device__ __forceinline__ void store_out(const MvParams& p, int64_t r, int64_t col, float v)
 {
-    __shared__ float part[kWarps][kRowsPerCta][8];
-    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-    const uint32_t g = lane >> 2, t = lane & 3u;
-    const int64_t rg = blockIdx.x / ks;
-    const int kc = (int)(blockIdx.x % ks);
-    const int64_t r0 = rg * kRowsPerCta;
-    const int64_t nsb = inner / kQKK;
-    const int64_t s0 = (int64_t)kc * chunk, s1 = min(nsb, s0 + chunk);
-    const int64_t ra = r0 + g, rb = r0 + g + 8;
-    const bool va = ra < rows, vb = rb < rows;
-    const bool vx = (int64_t)g < columns;
-    const uint8_t* wa = w + (va ? ra : 0) * stride;
-    const uint8_t* wb = w + (vb ? rb : 0) * stride;
-    // activation blocks are small and shared by every CTA: read through L1
-    const int64_t cstride = nsb * kQ8KBytes;
-    const uint8_t* xr = xq + (vx ? g : 0) * cstride + s0 * kQ8KBytes;
-    const bool vc0 = (int64_t)(2 * t) < columns, vc1 = (int64_t)(2 * t + 1) < columns;
-    const uint8_t* xc0 = xq + (vc0 ? 2 * t : 0) * cstride + s0 * kQ8KBytes;
-    const uint8_t* xc1 = xq + (vc1 ? 2 * t + 1 : 0) * cstride + s0 * kQ8KBytes;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    float summ[4] = {0.f, 0.f, 0.f, 0.f};
-    int64_t sb = s0 + warp;
-    Q5Frag cur;
-    if (sb < s1) load_q5(cur, wa + sb * kQ5KBytes, wb + sb * kQ5KBytes, va, vb, t);
-    for (; sb < s1; sb += kWarps) {
-        // next super-block's weights in flight while this one computes
-        Q5Frag nxt;
-        const int64_t sn = sb + kWarps;
-        if (sn < s1) load_q5(nxt, wa + sn * kQ5KBytes, wb + sn * kQ5KBytes, va, vb, t);
-        const uint8_t* bx = xr + (sb - s0) * kQ8KBytes;
-        int sca[8], mna[8], scb[8], mnb[8];
-        unpack_scales(cur.ha, sca, mna);
-        unpack_scales(cur.hb, scb, mnb);
-        int sumi[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const int p = j / 2;
-            const uint32_t sh = (j & 1) ? 4u : 0u;
-            const uint32_t la0 = (cur.qsa[p].x >> sh) & 0x0f0f0f0fu, la1 = (cur.qsa[p].y >> sh) & 0x0f0f0f0fu;
-            const uint32_t lb0 = (cur.qsb[p].x >> sh) & 0x0f0f0f0fu, lb1 = (cur.qsb[p].y >> sh) & 0x0f0f0f0fu;
-            const uint32_t a[4] = {la0 | (((cur.qha.x >> j) & 0x01010101u) << 4),
-                                   lb0 | (((cur.qhb.x >> j) & 0x01010101u) << 4),
-                                   la1 | (((cur.qha.y >> j) & 0x01010101u) << 4),
-                                   lb1 | (((cur.qhb.y >> j) & 0x01010101u) << 4)};
-            uint32_t bq0 = 0, bq1 = 0;
-            if (vx) {
-                const uint32_t* q8 = reinterpret_cast<const uint32_t*>(bx + 4 + 32 * j + 8 * t);
-                bq0 = __ldg(q8);
-                bq1 = __ldg(q8 + 1);
-            }
-            int d[4];
-            mma_s8(d, a, bq0, bq1);
-            sumi[0] += sca[j] * d[0];
-            sumi[1] += sca[j] * d[1];
-            sumi[2] += scb[j] * d[2];
-            sumi[3] += scb[j] * d[3];
+    p.y[col * p.ldy + r] = p.bias ? __fadd_rn(v, p.bias[r]) : v;
+}
+
+template <int TR>
+__global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_constant__ MvParams p)
+{
+    using Sh = MvShape<TR>;
+    constexpr int kStages = Sh::kStages, kSbs = Sh::kSbs, kRg = Sh::kRowGroups;
+    extern __shared__ __align__(128) uint8_t mv_smem[];
+    MvSmem<TR>& sm = *reinterpret_cast<MvSmem<TR>*>(mv_smem);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    griddep_launch_dependents();
+    const int64_t G = gridDim.x, c = blockIdx.x, S = p.stages, spt = p.spt;
+    const int64_t s_begin = c * S / G, s_end = (c + 1) * S / G;
+    const int64_t T0 = s_begin / spt, q0 = s_begin % spt;  // the only divisions on the stage index
+    const int64_t nsb = p.nsb, columns = p.columns;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kStages; i++) {
+            mbar_init(&sm.full[i], 1);
+            mbar_init(&sm.empty[i], kMvConsumers);
         }
-        // min term: sum_j m_j * (bsum_2j + bsum_2j+1) per (weight row, activation row)
-        int msum[4] = {0, 0, 0, 0};
-        const uint8_t* bx0 = xc0 + (sb - s0) * kQ8KBytes;
-        const uint8_t* bx1 = xc1 + (sb - s0) * kQ8KBytes;
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const uint32_t p0 = vc0 ? __ldg(reinterpret_cast<const uint32_t*>(bx0 + 4 + kQKK + 4 * j)) : 0u;
-            const uint32_t p1 = vc1 ? __ldg(reinterpret_cast<const uint32_t*>(bx1 + 4 + kQKK + 4 * j)) : 0u;
-            const int q0 = (int)(int16_t)(p0 & 0xffffu) + (int)(int16_t)(p0 >> 16);
-            const int q1 = (int)(int16_t)(p1 & 0xffffu) + (int)(int16_t)(p1 >> 16);
-            msum[0] += mna[j] * q0;
-            msum[1] += mna[j] * q1;
-            msum[2] += mnb[j] * q0;
-            msum[3] += mnb[j] * q1;
-        }
-        const float dx0 = vc0 ? __ldg(reinterpret_cast<const float*>(bx0)) : 0.f;
-        const float dx1 = vc1 ? __ldg(reinterpret_cast<const float*>(bx1)) : 0.f;
-        const float da = __half2float(__ushort_as_half((unsigned short)(cur.ha.x & 0xffffu)));
-        const float dma = __half2float(__ushort_as_half((unsigned short)(cur.ha.x >> 16)));
-        const float db = __half2float(__ushort_as_half((unsigned short)(cur.hb.x & 0xffffu)));
-        const float dmb = __half2float(__ushort_as_half((unsigned short)(cur.hb.x >> 16)));
-        // pix_dot_q5_K: d = y.d * fp16(x.d); dmin = -y.d * fp16(x.dmin)
-        acc[0] = __fmaf_rn(__fmul_rn(dx0, da), (float)sumi[0], acc[0]);
-        acc[1] = __fmaf_rn(__fmul_rn(dx1, da), (float)sumi[1], acc[1]);
-        acc[2] = __fmaf_rn(__fmul_rn(dx0, db), (float)sumi[2], acc[2]);
-        acc[3] = __fmaf_rn(__fmul_rn(dx1, db), (float)sumi[3], acc[3]);
-        summ[0] = __fmaf_rn(__fmul_rn(-dx0, dma), (float)msum[0], summ[0]);
-        summ[1] = __fmaf_rn(__fmul_rn(-dx1, dma), (float)msum[1], summ[1]);
-        summ[2] = __fmaf_rn(__fmul_rn(-dx0, dmb), (float)msum[2], summ[2]);
-        summ[3] = __fmaf_rn(__fmul_rn(-dx1, dmb), (float)msum[3], summ[3]);
-        if (sn < s1) cur = nxt;
+        sm.abort = 0;
+        fence_mbar_init();
     }
-    part[warp][g][2 * t] = acc[0] + summ[0];
-    part[warp][g][2 * t + 1] = acc[1] + summ[1];
-    part[warp][g + 8][2 * t] = acc[2] + summ[2];
-    part[warp][g + 8][2 * t + 1] = acc[3] + summ[3];
-    finish(part, r0, rows, columns, y, ldy, bias, ks, kc, rg, partial, counters);
+    __syncthreads();
+
+    if (warp == kMvConsumers) {
+        if (lane == 0) {
+            // producer.  The weights do not depend on earlier kernels: the
+            // first stages' weights are requested before griddep_wait, their
+            // activation records after it.
+            tma_prefetch_desc(&p.map);
+            const int64_t R = s_end - s_begin;
+            const int64_t pre = R < kStages ? R : kStages;
+            int64_t T = T0, q = q0, issued = 0;
+            for (int64_t i = 0; i < R; i++) {
+                const int slot = (int)(i % kStages);
+                const uint32_t round = (uint32_t)(i / kStages);
+                if (i >= kStages && !mbar_wait(&sm.empty[slot], (round - 1) & 1u, &sm.abort, p.status, kDevTimeoutEmpty))
+                    break;
+                const int64_t nsb_here = nsb - kSbs * q < kSbs ? nsb - kSbs * q : kSbs;
+                mbar_expect_tx(&sm.full[slot], Sh::kWeightBytes + (uint32_t)(columns * nsb_here * kQ8KMvBytes));
+                if (TR == 64)
+                    tma_load_2d(sm.weight[slot], &p.map, &sm.full[slot], (int32_t)(q * (Sh::kRowBytes / 8)),
+                                (int32_t)(p.row_first + T * TR));
+                else
+                    tma_load_3d(sm.weight[slot], &p.map, &sm.full[slot], 0, (int32_t)(p.row_first + T * TR),
+                                (int32_t)(q * kSbs));
+                if (i == pre - 1) {
+                    griddep_wait();
+                    // activation records of the stages requested so far
+                    int64_t qj = q0;
+                    for (int64_t k = 0; k <= i; k++) {
+                        const int64_t nk = nsb - kSbs * qj < kSbs ? nsb - kSbs * qj : kSbs;
+                        for (int64_t col = 0; col < columns; col++)
+                            bulk_load(sm.act[k] + col * Sh::kActPitch, p.act + (col * nsb + kSbs * qj) * kQ8KMvBytes,
+                                      (uint32_t)(nk * kQ8KMvBytes), &sm.full[k]);
+                        if (++qj == spt) qj = 0;
+                    }
+                } else if (i >= pre) {
+                    for (int64_t col = 0; col < columns; col++)
+                        bulk_load(sm.act[slot] + col * Sh::kActPitch, p.act + (col * nsb + kSbs * q) * kQ8KMvBytes,
+                                  (uint32_t)(nsb_here * kQ8KMvBytes), &sm.full[slot]);
+                }
+                issued = i + 1;
+                if (++q == spt) { q = 0; T++; }
+            }
+            // every copy of this CTA lands before it may exit, also after an
+            // abort (bounded: a stage that never lands is reported)
+            uint32_t never = 0;
+            for (int64_t i = issued - kStages > 0 ? issued - kStages : 0; i < issued; i++)
+                mbar_wait(&sm.full[i % kStages], (uint32_t)(i / kStages) & 1u, &never, p.status, kDevTimeoutFull);
+        }
+        return;
+    }
+
+    // consumers: outputs, partials and counters belong to the kernels before this one
+    griddep_wait();
+    const uint32_t rg = warp % kRg, sbl = warp / kRg;  // row group, super-block lane
+    const uint32_t g = lane >> 2, t = lane & 3u;
+    const bool vx = (int64_t)g < columns;
+    const bool vc0 = (int64_t)(2 * t) < columns, vc1 = (int64_t)(2 * t + 1) < columns;
+    const uint32_t row_off = (16 * rg + g) * Sh::kRowPitch + sbl * Sh::kSbPitch;
+    const uint32_t xg_off = g * Sh::kActPitch + sbl * kQ8KMvBytes + 16 * t;        // B fragments, activation row g
+    const uint32_t x0_off = (2 * t) * Sh::kActPitch + sbl * kQ8KMvBytes + kQKK;    // sums + d, activation row 2t
+    const uint32_t x1_off = x0_off + Sh::kActPitch;                                // activation row 2t+1
+    float acc[4] = {0.f, 0.f, 0.f, 0.f}, summ[4] = {0.f, 0.f, 0.f, 0.f};
+    bool ok = true;
+    uint32_t seg = 0;
+    bool seg_whole_start = q0 == 0;  // this segment starts at its tile's first stage
+    int64_t T = T0, q = q0;
+    for (int64_t i = 0; i < s_end - s_begin; i++) {
+        const int slot = (int)(i % kStages);
+        const uint32_t round = (uint32_t)(i / kStages);
+        const int64_t sb = kSbs * q + sbl;
+        if (ok) ok = mbar_wait(&sm.full[slot], round & 1u, &sm.abort, p.status, kDevTimeoutFull);
+        if (ok && sb < nsb) {
+            const uint8_t* wa = sm.weight[slot] + row_off;
+            const uint8_t* wb = wa + 8 * Sh::kRowPitch;
+            const uint8_t* xs = sm.act[slot];
+            const uint4 ha = *reinterpret_cast<const uint4*>(wa), hb = *reinterpret_cast<const uint4*>(wb);
+            const uint2 qha = *reinterpret_cast<const uint2*>(wa + 16 + 8 * t);
+            const uint2 qhb = *reinterpret_cast<const uint2*>(wb + 16 + 8 * t);
+            uint32_t sca_lo, sca_hi, mna_lo, mna_hi, scb_lo, scb_hi, mnb_lo, mnb_hi;
+            q5_scales(ha, sca_lo, sca_hi, mna_lo, mna_hi);
+            q5_scales(hb, scb_lo, scb_hi, mnb_lo, mnb_hi);
+            // activation rows >= columns hold stale bytes: their fragments are zero
+            const uint8_t* xr = xs + xg_off;
+            int sumi[4] = {0, 0, 0, 0};
+            q5_pair<0>(wa, wb, xr, vx, t, qha, qhb, sca_lo, scb_lo, sumi);
+            q5_pair<1>(wa, wb, xr, vx, t, qha, qhb, sca_lo, scb_lo, sumi);
+            q5_pair<2>(wa, wb, xr, vx, t, qha, qhb, sca_hi, scb_hi, sumi);
+            q5_pair<3>(wa, wb, xr, vx, t, qha, qhb, sca_hi, scb_hi, sumi);
+            const uint4 s0 = vc0 ? *reinterpret_cast<const uint4*>(xs + x0_off) : make_uint4(0, 0, 0, 0);
+            const uint4 s1 = vc1 ? *reinterpret_cast<const uint4*>(xs + x1_off) : make_uint4(0, 0, 0, 0);
+            const int msum[4] = {min_dot(s0, mna_lo, mna_hi), min_dot(s1, mna_lo, mna_hi), min_dot(s0, mnb_lo, mnb_hi),
+                                 min_dot(s1, mnb_lo, mnb_hi)};
+            const float dx0 = vc0 ? *reinterpret_cast<const float*>(xs + x0_off + 16) : 0.f;
+            const float dx1 = vc1 ? *reinterpret_cast<const float*>(xs + x1_off + 16) : 0.f;
+            const float da = __half2float(__ushort_as_half((unsigned short)(ha.x & 0xffffu)));
+            const float dma = __half2float(__ushort_as_half((unsigned short)(ha.x >> 16)));
+            const float db = __half2float(__ushort_as_half((unsigned short)(hb.x & 0xffffu)));
+            const float dmb = __half2float(__ushort_as_half((unsigned short)(hb.x >> 16)));
+            // pix_dot_q5_K: d = y.d * fp16(x.d); dmin = -y.d * fp16(x.dmin)
+            acc[0] = __fmaf_rn(__fmul_rn(dx0, da), (float)sumi[0], acc[0]);
+            acc[1] = __fmaf_rn(__fmul_rn(dx1, da), (float)sumi[1], acc[1]);
+            acc[2] = __fmaf_rn(__fmul_rn(dx0, db), (float)sumi[2], acc[2]);
+            acc[3] = __fmaf_rn(__fmul_rn(dx1, db), (float)sumi[3], acc[3]);
+            summ[0] = __fmaf_rn(__fmul_rn(-dx0, dma), (float)msum[0], summ[0]);
+            summ[1] = __fmaf_rn(__fmul_rn(-dx1, dma), (float)msum[1], summ[1]);
+            summ[2] = __fmaf_rn(__fmul_rn(-dx0, dmb), (float)msum[2], summ[2]);
+            summ[3] = __fmaf_rn(__fmul_rn(-dx1, dmb), (float)msum[3], summ[3]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.empty[slot]);
+        const bool tile_last = q == spt - 1;
+        const int64_t Tcur = T;
+        if (++q == spt) { q = 0; T++; }
+        if (!tile_last && i != s_end - s_begin - 1) continue;
+
+        // ---- end of this CTA's segment of tile Tcur ----
+        float v[4] = {acc[0] + summ[0], acc[1] + summ[1], acc[2] + summ[2], acc[3] + summ[3]};
+        // lanes >= 1 hand their sums to lane 0 through a buffer alternating
+        // by segment: before one can write it again, lane 0 has passed the
+        // next segment's barrier, i.e. finished reading it
+        float (*red)[kRg][16][8] = sm.red[seg & 1u];
+        if (sbl > 0) {
+            red[sbl - 1][rg][g][2 * t] = v[0];
+            red[sbl - 1][rg][g][2 * t + 1] = v[1];
+            red[sbl - 1][rg][g + 8][2 * t] = v[2];
+            red[sbl - 1][rg][g + 8][2 * t + 1] = v[3];
+        }
+        named_bar_sync(1 + rg, 32 * kSbs);
+        const bool whole = seg_whole_start && tile_last;
+        if (sbl == 0) {
+#pragma unroll
+            for (int k = 0; k < kSbs - 1; k++) {  // fixed order: lane 0, 1, 2, ...
+                v[0] += red[k][rg][g][2 * t];
+                v[1] += red[k][rg][g][2 * t + 1];
+                v[2] += red[k][rg][g + 8][2 * t];
+                v[3] += red[k][rg][g + 8][2 * t + 1];
+            }
+            const int64_t ra = Tcur * TR + 16 * rg + g, rb = ra + 8;
+            if (whole) {
+                if (vc0 && ra < p.rows) store_out(p, ra, 2 * t, v[0]);
+                if (vc1 && ra < p.rows) store_out(p, ra, 2 * t + 1, v[1]);
+                if (vc0 && rb < p.rows) store_out(p, rb, 2 * t, v[2]);
+                if (vc1 && rb < p.rows) store_out(p, rb, 2 * t + 1, v[3]);
+            } else {
+                // partial: store, count, and the last contributor sums all of them in CTA order
+                float* mine = p.partial + (c * 2 + partial_slot(c, Tcur, S, G, spt)) * columns * TR;
+                const uint32_t la = 16 * rg + g, lb = la + 8;
+                if (vc0) {
+                    mine[(2 * t) * TR + la] = v[0];
+                    mine[(2 * t) * TR + lb] = v[2];
+                }
+                if (vc1) {
+                    mine[(2 * t + 1) * TR + la] = v[1];
+                    mine[(2 * t + 1) * TR + lb] = v[3];
+                }
+                // the lane-0 warps' stores are ordered before the count by one
+                // thread's gpu-scope fence after the barrier (cumulativity),
+                // and the last contributor's reads after it by the same
+                const int64_t c_first = cta_of_stage(Tcur * spt, S, G), c_last = cta_of_stage((Tcur + 1) * spt - 1, S, G);
+                named_bar_sync(5, 32 * kRg);
+                if (threadIdx.x == 0) {
+                    __threadfence();
+                    const bool last = atomicAdd(&p.counters[Tcur], 1u) == (uint32_t)(c_last - c_first);
+                    if (last) __threadfence();
+                    sm.last = last;
+                }
+                named_bar_sync(5, 32 * kRg);
+                if (sm.last) {
+                    float w[4] = {0.f, 0.f, 0.f, 0.f};
+                    for (int64_t k0 = c_first; k0 <= c_last; k0 += 4) {
+                        // four contributors' loads in flight, then summed in CTA order
+                        float pv[4][4];
+#pragma unroll
+                        for (int u = 0; u < 4; u++) {
+                            const int64_t k = k0 + u;
+                            const float* src = p.partial + (k * 2 + partial_slot(k, Tcur, S, G, spt)) * columns * TR;
+                            const bool in = k <= c_last;
+                            pv[u][0] = in && vc0 ? __ldcg(&src[(2 * t) * TR + la]) : 0.f;
+                            pv[u][1] = in && vc1 ? __ldcg(&src[(2 * t + 1) * TR + la]) : 0.f;
+                            pv[u][2] = in && vc0 ? __ldcg(&src[(2 * t) * TR + lb]) : 0.f;
+                            pv[u][3] = in && vc1 ? __ldcg(&src[(2 * t + 1) * TR + lb]) : 0.f;
+                        }
+#pragma unroll
+                        for (int u = 0; u < 4; u++)
+                            if (k0 + u <= c_last) {
+                                w[0] += pv[u][0];
+                                w[1] += pv[u][1];
+                                w[2] += pv[u][2];
+                                w[3] += pv[u][3];
+                            }
+                    }
+                    if (vc0 && ra < p.rows) store_out(p, ra, 2 * t, w[0]);
+                    if (vc1 && ra < p.rows) store_out(p, ra, 2 * t + 1, w[1]);
+                    if (vc0 && rb < p.rows) store_out(p, rb, 2 * t, w[2]);
+                    if (vc1 && rb < p.rows) store_out(p, rb, 2 * t + 1, w[3]);
+                    if (threadIdx.x == 0) p.counters[Tcur] = 0u;  // ready for the next call
+                }
+            }
+        }
+        acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+        summ[0] = summ[1] = summ[2] = summ[3] = 0.f;
+        seg++;
+        seg_whole_start = true;  // later segments start at a tile's first stage
+    }
+}
+
+template <int TR>
+cudaError_t launch_q5(const MatvecPlan& plan, const CUtensorMap* map, int64_t row_first, const void* act, float* y,
+                      int64_t ldy, const float* bias, float* partial, uint32_t* counters, uint32_t* status, cudaStream_t s)
+{
+    static bool attr_set[16] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 16 && !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(k_matvec_q5_K<TR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)sizeof(MvSmem<TR>));
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_matvec_q5_K<TR>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     (int)cudaSharedmemCarveoutMaxShared);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    MvParams prm;
+    prm.map = *map;
+    prm.act = static_cast<const uint8_t*>(act);
+    prm.y = y;
+    prm.bias = bias;
+    prm.partial = partial;
+    prm.counters = counters;
+    prm.status = status;
+    prm.ldy = ldy;
+    prm.rows = plan.rows;
+    prm.row_first = row_first;
+    prm.stages = plan.stages;
+    prm.nsb = (int32_t)(plan.inner / kQKK);
+    prm.spt = (int32_t)plan.spt;
+    prm.columns = (int32_t)plan.columns;
+    return launch_pdl(k_matvec_q5_K<TR>, dim3(plan.grid), dim3(kMvThreads), sizeof(MvSmem<TR>), s, prm);
 }
 
 }  // namespace
 
+int matvec_map_index(int tile_rows) { return tile_rows == 64 ? 0 : tile_rows == 32 ? 1 : 2; }
+
 MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t columns, int num_sms)
 {
     MatvecPlan p;
-    const int64_t nblocks = type == kTypeQ8_0 ? inner / kQK8_0 : inner / kQKK;
-    const int64_t min_chunk = type == kTypeQ8_0 ? 32 : 4;  // keep every warp busy on a slice
-    p.rowgroups = (rows + kRowsPerCta - 1) / kRowsPerCta;
-    // enough CTAs to cover every SM a few times, and an activation slice that fits the staging budget
-    const int64_t target = (int64_t)num_sms * 4;
-    int64_t ks = (target + p.rowgroups - 1) / p.rowgroups;
-    const int64_t max_ks_work = nblocks / min_chunk > 1 ? nblocks / min_chunk : 1;
-    if (ks > max_ks_work) ks = max_ks_work;
-    if (ks < 1) ks = 1;
-    const int64_t chunk = (nblocks + ks - 1) / ks;
-    ks = (nblocks + chunk - 1) / chunk;
-    p.ks = (int)ks;
-    p.chunk = (int)chunk;
-    p.smem_bytes = 0;
-    p.partial_bytes = ks > 1 ? (size_t)ks * columns * rows * sizeof(float) : 0;
-    p.counter_bytes = ks > 1 ? (size_t)p.rowgroups * sizeof(uint32_t) : 0;
+    p.type = type;
+    p.rows = rows;
+    p.inner = inner;
+    p.columns = columns;
+    if (type == kTypeQ5_K) {
+        const int64_t nsb = inner / kQKK;
+        const int64_t slots = (int64_t)num_sms * 2;  // two CTAs per SM
+        // Whole tiles per CTA (no cross-CTA sums) when some tile height gives
+        // a tile count that fills the grid well, or when the matrix is small
+        // enough that the extra wave costs less than the cross-CTA sums;
+        // otherwise 64-row tiles in a stream-K split over the whole grid.
+        p.tile_rows = 64;
+        bool whole = false;
+        for (int tr : {64, 32, 16}) {
+            const int64_t tiles = (rows + tr - 1) / tr;
+            const int64_t tile_bytes = (int64_t)tr * nsb * kQ5KBytes;
+            if (tiles <= slots && (tiles * 20 >= slots * 19 || (tiles * 4 >= slots * 3 && tile_bytes <= 64 * 1024))) {
+                p.tile_rows = tr;
+                whole = true;
+                break;
+            }
+        }
+        const int sbs = kMvStageSuperBlocks / (p.tile_rows / 16);
+        p.tiles = (rows + p.tile_rows - 1) / p.tile_rows;
+        p.spt = (nsb + sbs - 1) / sbs;
+        p.stages = p.tiles * p.spt;
+        p.grid = (int)(whole ? p.tiles : (p.stages < slots ? p.stages : slots));
+        p.act_bytes = (size_t)(columns * nsb * kQ8KMvBytes);
+        p.partial_bytes = whole ? 0 : (size_t)p.grid * 2 * columns * p.tile_rows * sizeof(float);
+        p.counter_bytes = (size_t)p.tiles * sizeof(uint32_t);
+    } else {
+        const int64_t nblocks = inner / kQK8_0;
+        const int64_t min_chunk = 32;  // keep every warp busy on a slice
+        p.rowgroups = (rows + kRowsPerCta - 1) / kRowsPerCta;
+        // enough CTAs to cover every SM a few times
+        const int64_t target = (int64_t)num_sms * 4;
+        int64_t ks = (target + p.rowgroups - 1) / p.rowgroups;
+        const int64_t max_ks_work = nblocks / min_chunk > 1 ? nblocks / min_chunk : 1;
+        if (ks > max_ks_work) ks = max_ks_work;
+        if (ks < 1) ks = 1;
+        const int64_t chunk = (nblocks + ks - 1) / ks;
+        ks = (nblocks + chunk - 1) / chunk;
+        p.ks = (int)ks;
+        p.chunk = (int)chunk;
+        p.grid = (int)(p.rowgroups * ks);
+        // + 64: the 2-byte-aligned activation reads may touch a few bytes past the last block
+        p.act_bytes = (size_t)(columns * nblocks * kQ8_0Bytes) + 64;
+        p.partial_bytes = ks > 1 ? (size_t)ks * columns * rows * sizeof(float) : 0;
+        p.counter_bytes = ks > 1 ? (size_t)p.rowgroups * sizeof(uint32_t) : 0;
+    }
+    p.off_partial = (p.act_bytes + 255) / 256 * 256;
+    p.off_counters = (p.off_partial + p.partial_bytes + 255) / 256 * 256;
+    p.total_bytes = p.off_counters + p.counter_bytes;
     return p;
 }
 
-cudaError_t launch_matvec(uint32_t type, const uint8_t* w, int64_t stride, int64_t rows, int64_t inner, const void* xq,
-                          int64_t columns, float* y, int64_t ldy, const float* bias, const MatvecPlan& plan, float* partial,
-                          uint32_t* counters, cudaStream_t s)
+cudaError_t launch_matvec(const MatvecPlan& plan, const CUtensorMap* maps, int64_t row_first, const uint8_t* w,
+                          int64_t stride, const void* act, float* y, int64_t ldy, const float* bias, float* partial,
+                          uint32_t* counters, uint32_t* status, cudaStream_t s)
 {
-    if (columns < 1 || columns > 8) return cudaErrorInvalidValue;
-    const int64_t ctas = plan.rowgroups * plan.ks;
-    if (ctas > 0x7fffffff || ctas < 1) return cudaErrorInvalidValue;
-    if (plan.ks > 1 && (!partial || !counters)) return cudaErrorInvalidValue;
-    const uint8_t* x = static_cast<const uint8_t*>(xq);
-    if (type == kTypeQ8_0) {
-        k_matvec_q8_0<<<(unsigned)ctas, kThreads, plan.smem_bytes, s>>>(w, stride, rows, inner, x, columns, y, ldy, bias,
-                                                                        plan.ks, plan.chunk, partial, counters);
-    } else if (type == kTypeQ5_K) {
-        k_matvec_q5_K<<<(unsigned)ctas, kThreads, plan.smem_bytes, s>>>(w, stride, rows, inner, x, columns, y, ldy, bias,
-                                                                        plan.ks, plan.chunk, partial, counters);
-    } else {
-        return cudaErrorInvalidValue;
+    if (plan.columns < 1 || plan.columns > 8 || plan.grid < 1) return cudaErrorInvalidValue;
+    if (plan.type == kTypeQ5_K) {
+        if (!maps || !counters || (plan.partial_bytes && !partial)) return cudaErrorInvalidValue;
+        const CUtensorMap* map = maps + matvec_map_index(plan.tile_rows);
+        switch (plan.tile_rows) {
+        case 64: return launch_q5<64>(plan, map, row_first, act, y, ldy, bias, partial, counters, status, s);
+        case 32: return launch_q5<32>(plan, map, row_first, act, y, ldy, bias, partial, counters, status, s);
+        case 16: return launch_q5<16>(plan, map, row_first, act, y, ldy, bias, partial, counters, status, s);
+        default: return cudaErrorInvalidValue;
+        }
     }
-    return cudaGetLastError();
+    if (plan.type == kTypeQ8_0) {
+        if (plan.ks > 1 && (!partial || !counters)) return cudaErrorInvalidValue;
+        return launch_pdl(k_matvec_q8_0, dim3(plan.grid), dim3(kThreads), 0, s, w, stride, plan.rows, plan.inner,
+                          static_cast<const uint8_t*>(act), plan.columns, y, ldy, bias, plan.ks, plan.chunk, partial,
+                          counters);
+    }
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace pxq

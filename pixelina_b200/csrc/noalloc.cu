@@ -19,11 +19,10 @@
 // does the set-up (and may make the runtime load this module); make it before
 // any stream capture.
 //
-// Layout of the array per call: the quantized activation rows, then (when the
-// matvec splits K over several CTAs) the fp32 partial sums and one counter per
-// 16-row group.  The counters must start at zero, so each call clears them
-// with cudaMemsetAsync on its stream before launching; every other byte the
-// kernels read is written earlier in the same call.
+// Layout of the array per call: the quantized activation rows, then the
+// matvec's fp32 partial sums and counters.  The counters must start at zero:
+// the quantize kernel of each call clears them before the matvec uses them;
+// every other byte the kernels read is written earlier in the same call.
 //
 // Sharing: every call on a device uses the same array and it keeps the last
 // call's contents.  Two calls whose work overlaps on the GPU (different
@@ -52,6 +51,10 @@ bool weight_view(const pxq_weight* w, uint32_t* type, int64_t* inner, int64_t* r
                  int* device);
 void record_error(const char* msg);
 int device_sm_count(int device);
+uint32_t* device_status(int device);
+cudaError_t matvec_fused(const pxq_weight* w, size_t row_first, size_t row_count, const float* input, float* output,
+                         size_t ldy, const float* bias, const MatvecPlan& plan, uint8_t* scratch, uint32_t* status,
+                         cudaStream_t s);
 }
 
 namespace {
@@ -77,17 +80,12 @@ extern "C" int pxq_matvec_noalloc(pxq_weight* w, size_t row_first, size_t row_co
         return noalloc_fail(PXQ_ERR_INVALID, "row range outside the weight");
     if (ldy < row_count && columns > 1) return noalloc_fail(PXQ_ERR_INVALID, "ldy < row_count");
     if (type != pxq::kTypeQ8_0 && type != pxq::kTypeQ5_K) return noalloc_fail(PXQ_ERR_UNSUPPORTED, "weight type not supported");
-    const bool q5 = type == pxq::kTypeQ5_K;
-    // the static array holds the quantized activation rows and, when the
-    // matvec splits K over several CTAs, its partial sums and counters
-    const uint64_t act = (uint64_t)columns * (uint64_t)(q5 ? inner / pxq::kQKK : inner / pxq::kQK8_0) *
-                         (uint64_t)(q5 ? pxq::kQ8KBytes : pxq::kQ8_0Bytes);
+    // the static array holds the quantized activation rows and the matvec's
+    // partial sums and counters
     int cur_dev = -1;
     cudaGetDevice(&cur_dev);
     const pxq::MatvecPlan plan = pxq::plan_matvec(type, (int64_t)row_count, inner, (int64_t)columns, pxq::device_sm_count(cur_dev));
-    const uint64_t off_partial = (act + 64 + 255) / 256 * 256;
-    const uint64_t off_counters = (off_partial + plan.partial_bytes + 255) / 256 * 256;
-    const uint64_t need = off_counters + plan.counter_bytes;
+    const uint64_t need = plan.total_bytes;
     if (need > PXQ_NOALLOC_SCRATCH_BYTES) {
         char msg[200];
         snprintf(msg, sizeof(msg), "this call needs %llu bytes of scratch; the static scratch holds %d bytes "
@@ -114,17 +112,8 @@ extern "C" int pxq_matvec_noalloc(pxq_weight* w, size_t row_first, size_t row_co
         scratch = g_scratch_ptr[dev];
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    uint8_t* base = static_cast<uint8_t*>(scratch);
-    float* partial = plan.ks > 1 ? reinterpret_cast<float*>(base + off_partial) : nullptr;
-    uint32_t* counters = plan.ks > 1 ? reinterpret_cast<uint32_t*>(base + off_counters) : nullptr;
-    cudaError_t e = cudaSuccess;
-    if (counters) e = cudaMemsetAsync(counters, 0, plan.counter_bytes, s);  // counters start at zero
-    if (e == cudaSuccess)
-        e = q5 ? pxq::launch_quantize_q8_K_blocks(input, scratch, (int64_t)columns, inner, inner, s)
-               : pxq::launch_quantize_q8_0_blocks(input, scratch, (int64_t)columns, inner, inner, s);
-    if (e == cudaSuccess)
-        e = pxq::launch_matvec(type, raw + row_first * stride, stride, (int64_t)row_count, inner, scratch, (int64_t)columns,
-                               output, (int64_t)ldy, bias, plan, partial, counters, s);
+    const cudaError_t e = pxq::matvec_fused(w, row_first, row_count, input, output, ldy, bias, plan,
+                                            static_cast<uint8_t*>(scratch), pxq::device_status(dev), s);
     if (e != cudaSuccess) {
         char msg[200];
         snprintf(msg, sizeof(msg), "kernel launch failed: %s", cudaGetErrorString(e));

@@ -132,6 +132,24 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_
         : "memory");
 }
 
+// 3-D tiled load of one box (c0 innermost).
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_t* bar, int32_t c0, int32_t c1, int32_t c2)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(tmap), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+// Plain bulk copy global -> this CTA's shared memory (no tensor map, no
+// cluster broadcast); both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 // 2-D tiled store of one box from shared memory (bulk-group completion).
 // Elements of the box outside the tensor are not written.
 __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, int32_t c0, int32_t c1)
@@ -151,6 +169,44 @@ __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.p
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count)
 {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// ------------------------------------------- programmatic dependent launch ---
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel of its stream still runs.  griddep_wait() blocks until
+// that kernel has completed and its memory is visible (a no-op for a normal
+// launch); griddep_launch_dependents() lets the next such kernel launch early.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Plain (coherent) global loads for data that an earlier kernel of the stream
+// writes: under programmatic serialization that kernel may still be writing
+// while this one starts, so such data is not read-only for this kernel's
+// lifetime and must not go through the non-coherent (ld.global.nc) path.
+// volatile keeps them after griddep_wait().
+__device__ __forceinline__ uint4 ld_dep_u128(const void* p)
+{
+    uint4 v;
+    asm volatile("ld.global.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ld_dep_u32(const void* p)
+{
+    uint32_t v;
+    asm volatile("ld.global.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint16_t ld_dep_u16(const void* p)
+{
+    uint16_t v;
+    asm volatile("ld.global.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float4 ld_dep_f4(const float* p)
+{
+    float4 v;
+    asm volatile("ld.global.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
 }
 
 // ---------------------------------------------------------------- tcgen05 ---

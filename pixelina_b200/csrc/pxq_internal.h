@@ -44,21 +44,72 @@ cudaError_t launch_decode(const uint8_t* data, uint32_t type, int64_t count, flo
 
 // ---- matvec.cu -------------------------------------------------------------
 // y[c*ldy + r] = dot(W row r, X row c) for c < columns <= 8, raw GGUF weights.
-// The plan splits K over `ks` CTAs per 16-row group when rows are few; then
-// the launch needs `partial_bytes` of fp32 workspace and `counter_bytes` of
-// counters that are zero at launch (the kernel leaves them zero again).
+//
+// Q5_K: a persistent kernel over tiles of TR = 64, 32 or 16 weight rows, each
+// tile's K range cut into stages of 128/TR super-blocks (22.5 KB), loaded by
+// TMA through a tensor map over the raw weight bytes (64-bit elements, box
+// {128/TR*176/8, TR}; the weight keeps one map per tile shape, index
+// matvec_map_index(TR)).  Either every CTA owns whole tiles, or the flattened
+// stage sequence is split evenly over the CTAs (stream-K) and a tile whose
+// stages span several CTAs is finished, in fixed CTA order, by the last of
+// them to arrive.  The activation is the matvec operand below (records of
+// kQ8KMvBytes).
+// Q8_0: 16-row groups, K split over `ks` CTAs per group when groups are few;
+// the activation is GGUF Q8_0 blocks.
+//
+// One call's scratch (256-byte aligned, total_bytes): the activation operand
+// at 0, fp32 partial sums at off_partial, uint32 counters at off_counters.
+// The counters must be zero when the matvec starts: the quantize kernel
+// clears them, and the matvec leaves them zero again.
+constexpr int kMvStageSuperBlocks = 8;                    // tile rows / 16 x super-blocks per stage
+constexpr int kMvStageWeightBytes = 16 * kMvStageSuperBlocks * kQ5KBytes;  // 22528, any tile shape
+constexpr int kMvTileShapes = 3;                         // 64 x 2, 32 x 4 and 16 x 8 super-blocks
+constexpr int kQ8KMvBytes = 288;  // {i8 quants [4 pairs][4 lanes][2][8]; i16 32-element sums[8]; f32 d; pad}
+
 struct MatvecPlan {
-    int ks = 1;               // K slices per row group
-    int chunk = 0;            // K blocks per slice
-    int64_t rowgroups = 0;    // 16-row groups
-    size_t smem_bytes = 0;    // dynamic shared memory per CTA
-    size_t partial_bytes = 0; // split-K workspace (0 when ks == 1)
-    size_t counter_bytes = 0;
+    uint32_t type = 0;
+    int64_t rows = 0, inner = 0, columns = 0;
+    int tile_rows = 64;                      // Q5_K: tile height
+    int64_t tiles = 0, spt = 0, stages = 0;  // Q5_K: tiles, stages per tile, total stages
+    int grid = 0;                            // CTAs
+    int ks = 1, chunk = 0;                   // Q8_0: K slices per row group, blocks per slice
+    int64_t rowgroups = 0;                   // Q8_0: 16-row groups
+    size_t act_bytes = 0, partial_bytes = 0, counter_bytes = 0;
+    size_t off_partial = 0, off_counters = 0, total_bytes = 0;
 };
 MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t columns, int num_sms);
-cudaError_t launch_matvec(uint32_t type, const uint8_t* w, int64_t stride, int64_t rows, int64_t inner, const void* xq,
-                          int64_t columns, float* y, int64_t ldy, const float* bias, const MatvecPlan& plan, float* partial,
-                          uint32_t* counters, cudaStream_t s);
+int matvec_map_index(int tile_rows);
+// Quantize the plan's `columns` activation rows (row stride ldx floats) into
+// the operand at `act`; clears `counters` (plan.counter_bytes) when non-null.
+// Launched with programmatic stream serialization.
+cudaError_t launch_matvec_quantize(const MatvecPlan& plan, const float* x, int64_t ldx, void* act, uint32_t* counters,
+                                   cudaStream_t s);
+// The matvec.  Q5_K reads the weight through maps[matvec_map_index(tile
+// rows)] (tensor maps over the whole weight) starting at row `row_first`; Q8_0 reads `w` (the view's first
+// row).  Launched with programmatic stream serialization: the Q5_K kernel
+// streams weights before the previous kernel of the stream has finished and
+// touches every other buffer only after it.
+cudaError_t launch_matvec(const MatvecPlan& plan, const CUtensorMap* maps, int64_t row_first, const uint8_t* w,
+                          int64_t stride, const void* act, float* y, int64_t ldy, const float* bias, float* partial,
+                          uint32_t* counters, uint32_t* status, cudaStream_t s);
+
+// Launch with programmatic stream serialization (see griddep_wait in
+// pxq_device.cuh).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 
 // ---- shards.cu -------------------------------------------------------------
 cudaError_t launch_gather_shards(const float* src, int64_t shards, int64_t columns, int64_t shard_rows, float* dst,

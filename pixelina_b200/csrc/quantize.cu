@@ -3,10 +3,12 @@
 //   Q8_0 (32-blocks)  restates quantize_row_q8_0_ref, src/kernels_quant.cpp:120-144
 //   Q8_K (256-blocks) restates quantize_row_q8_K_ref, src/kernels_quant.cpp:80-118
 //
-// Each comes in two output layouts: the GGUF block layout (what the reference
-// produces, used by the matvec and by the parity tests) and the tensor-core
-// operand layout used by the GEMM (exact fp16 copies of the int8 quants plus
-// block-major scale planes).  Both layouts come from the same arithmetic.
+// Each comes in several output layouts: the GGUF block layout (what the
+// reference produces, checked by the parity tests; the Q8_0 matvec reads it
+// too), the Q8_K matvec operand (the same bytes permuted for the matvec's
+// fragments, plus 32-element sums), and the tensor-core operand layout used
+// by the GEMM (exact fp16 copies of the int8 quants plus block-major scale
+// planes).  All layouts come from the same arithmetic.
 //
 // Bit-exactness rules (all arithmetic uses explicit _rn intrinsics so that
 // nvcc's default FMA contraction cannot change a rounding):
@@ -18,6 +20,7 @@
 //     kernel uses __fmaf_rn for that step;
 //   * the stored fp16 scale is round-to-nearest-even (F16C with
 //     _MM_FROUND_TO_NEAREST_INT).
+#include "pxq_device.cuh"
 #include "pxq_internal.h"
 
 namespace pxq {
@@ -63,9 +66,22 @@ __device__ __forceinline__ Q80Part q8_0_part(const float4 v)
 
 // grid-stride over groups of 4 elements; all 32 lanes of a warp stay active
 // (padding lanes compute on zeros and store nothing) so the shuffles are full.
-__global__ void k_quantize_q8_0_blocks(const float* __restrict__ x, uint8_t* __restrict__ y, int64_t rows, int64_t inner,
-                                       int64_t ldx)
+// Start of every kernel that may run under programmatic stream serialization:
+// let the next kernel launch, wait for the previous one, then clear the
+// caller's counters (the matvec's split-K counters) if any.
+__device__ __forceinline__ void pdl_prologue(uint32_t* __restrict__ zero, int64_t nzero)
 {
+    griddep_launch_dependents();
+    griddep_wait();
+    if (zero)
+        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nzero; i += (int64_t)gridDim.x * blockDim.x)
+            zero[i] = 0u;
+}
+
+__global__ void k_quantize_q8_0_blocks(const float* x, uint8_t* __restrict__ y, int64_t rows, int64_t inner,
+                                       int64_t ldx, uint32_t* __restrict__ zero, int64_t nzero)
+{
+    pdl_prologue(zero, nzero);
     const int64_t quads_per_row = inner / 4;
     const int64_t total = rows * quads_per_row;
     const int64_t nb = inner / kQK8_0;
@@ -76,7 +92,7 @@ __global__ void k_quantize_q8_0_blocks(const float* __restrict__ x, uint8_t* __r
         const int64_t row = live ? i / quads_per_row : 0;
         const int64_t quad = live ? i % quads_per_row : 0;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (live) v = *reinterpret_cast<const float4*>(x + row * ldx + quad * 4);
+        if (live) v = ld_dep_f4(x + row * ldx + quad * 4);
         const Q80Part p = q8_0_part(v);
         if (!live) continue;
         const int64_t blk = quad / 8;
@@ -102,7 +118,7 @@ __global__ void k_quantize_q8_0_operand(const float* __restrict__ x, __half* __r
         const int64_t row = live ? i / quads_per_row : 0;
         const int64_t quad = live ? i % quads_per_row : 0;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (live) v = *reinterpret_cast<const float4*>(x + row * ldx + quad * 4);
+        if (live) v = ld_dep_f4(x + row * ldx + quad * 4);
         const Q80Part p = q8_0_part(v);
         if (!live) continue;
         __half2 h01 = __halves2half2(__int2half_rn(p.q[0]), __int2half_rn(p.q[1]));
@@ -122,10 +138,10 @@ struct Q8KWarp {
     int8_t q[8];    // this lane's 8 quants
 };
 
-__device__ __forceinline__ Q8KWarp q8_K_warp(const float* __restrict__ src, uint32_t lane)
+__device__ __forceinline__ Q8KWarp q8_K_warp(const float* src, uint32_t lane)
 {
-    const float4 a = *reinterpret_cast<const float4*>(src + lane * 8);
-    const float4 b = *reinterpret_cast<const float4*>(src + lane * 8 + 4);
+    const float4 a = ld_dep_f4(src + lane * 8);
+    const float4 b = ld_dep_f4(src + lane * 8 + 4);
     const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     // first element (in index order) with the largest |x|: strict '>' scan
     float amax = 0.0f, vmax = 0.0f;
@@ -196,6 +212,43 @@ __global__ void k_quantize_q8_K_blocks(const float* __restrict__ x, uint8_t* __r
     }
 }
 
+// Matvec operand: one record of kQ8KMvBytes per (row, super-block), holding
+// the same quants and scale as the Q8_K block, permuted for the matvec's
+// tensor-core fragments: quants of sub-block j (32 values), elements
+// 8t..8t+7 (t = 0..3), at byte 64*(j/2) + 16*t + 8*(j%2), so a thread's B
+// fragments of two sub-blocks are one 16-byte word and the four threads of a
+// fragment read 64 contiguous bytes; then the eight 32-element sums
+// bsums[2j] + bsums[2j+1] as int16 at byte 256, and d (fp32) at byte 272.
+__global__ void k_quantize_q8_K_mv(const float* x, uint8_t* __restrict__ y, int64_t rows, int64_t inner,
+                                   int64_t ldx, uint32_t* __restrict__ zero, int64_t nzero)
+{
+    pdl_prologue(zero, nzero);
+    const uint32_t lane = threadIdx.x & 31u;
+    const int64_t nsb = inner / kQKK;
+    const int64_t total = rows * nsb;
+    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t w = (((int64_t)blockIdx.x * blockDim.x) >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
+        const int64_t row = w / nsb, sb = w % nsb;
+        const Q8KWarp r = q8_K_warp(x + row * ldx + sb * kQKK, lane);
+        uint8_t* out = y + w * kQ8KMvBytes;
+        uint32_t lo = 0, hi = 0;
+        int sum8 = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) lo |= (uint32_t)(uint8_t)r.q[j] << (8 * j);
+#pragma unroll
+        for (int j = 0; j < 4; j++) hi |= (uint32_t)(uint8_t)r.q[4 + j] << (8 * j);
+#pragma unroll
+        for (int j = 0; j < 8; j++) sum8 += r.q[j];
+        // lane = 4*j + t holds elements 8t..8t+7 of sub-block j
+        const uint32_t j = lane >> 2, t = lane & 3u;
+        *reinterpret_cast<uint2*>(out + 64 * (j >> 1) + 16 * t + 8 * (j & 1u)) = make_uint2(lo, hi);
+        int s32 = sum8 + __shfl_xor_sync(0xffffffffu, sum8, 1);
+        s32 += __shfl_xor_sync(0xffffffffu, s32, 2);
+        if (t == 0) *reinterpret_cast<int16_t*>(out + kQKK + 2 * j) = (int16_t)s32;
+        if (lane == 0) *reinterpret_cast<float*>(out + kQKK + 16) = r.d;
+    }
+}
+
 __global__ void k_quantize_q8_K_operand(const float* __restrict__ x, __half* __restrict__ xq, float* __restrict__ dxT,
                                         __half* __restrict__ amin, int64_t rows, int64_t inner, int64_t ldx, int64_t ldd)
 {
@@ -241,8 +294,36 @@ int grid_for(int64_t work_items, int threads)
 cudaError_t launch_quantize_q8_0_blocks(const float* x, void* y, int64_t rows, int64_t inner, int64_t ldx, cudaStream_t s)
 {
     const int threads = 256;
-    k_quantize_q8_0_blocks<<<grid_for(rows * inner / 4, threads), threads, 0, s>>>(x, static_cast<uint8_t*>(y), rows, inner, ldx);
+    k_quantize_q8_0_blocks<<<grid_for(rows * inner / 4, threads), threads, 0, s>>>(x, static_cast<uint8_t*>(y), rows, inner, ldx,
+                                                                                   nullptr, 0);
     return cudaGetLastError();
+}
+
+cudaError_t launch_matvec_quantize(const MatvecPlan& plan, const float* x, int64_t ldx, void* act, uint32_t* counters,
+                                   cudaStream_t s)
+{
+    const int threads = 256;
+    const int64_t nzero = counters ? (int64_t)(plan.counter_bytes / 4) : 0;
+    uint8_t* out = static_cast<uint8_t*>(act);
+    if (plan.type == kTypeQ8_0)
+        return launch_pdl(k_quantize_q8_0_blocks, dim3(grid_for(plan.columns * plan.inner / 4, threads)), dim3(threads), 0, s,
+                          x, out, plan.columns, plan.inner, ldx, counters, nzero);
+    if (plan.type == kTypeQ5_K) {
+        // same shared-memory carveout as the matvec, so that the SMs need no
+        // reconfiguration between the two kernels
+        static bool carveout_set[16] = {};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev >= 0 && dev < 16 && !carveout_set[dev]) {
+            cudaError_t e = cudaFuncSetAttribute(k_quantize_q8_K_mv, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                                 (int)cudaSharedmemCarveoutMaxShared);
+            if (e != cudaSuccess) return e;
+            carveout_set[dev] = true;
+        }
+        return launch_pdl(k_quantize_q8_K_mv, dim3(grid_for(plan.columns * (plan.inner / kQKK) * 32, threads)), dim3(threads), 0,
+                          s, x, out, plan.columns, plan.inner, ldx, counters, nzero);
+    }
+    return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_quantize_q8_K_blocks(const float* x, void* y, int64_t rows, int64_t inner, int64_t ldx, cudaStream_t s)

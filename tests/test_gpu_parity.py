@@ -80,6 +80,22 @@ def test_matvec_vs_oracle(pxq, oracle, wtype, columns):
     assert ok and max_abs_rel(y, ref) <= TOL
 
 
+@pytest.mark.parametrize("rows", [18944, 9472, 4608, 3584, 200])
+@pytest.mark.parametrize("inner,columns", [(256, 1), (768, 3), (3584, 8)])
+def test_matvec_q5_K_tile_shapes(pxq, oracle, rows, inner, columns):
+    """Every Q5_K matvec schedule: on a 148-SM B200 these row counts select
+    whole 64-, 32- and 16-row tiles per CTA and the stream-K split; odd
+    super-block counts leave the last stage partly empty."""
+    w = synth.random_q5_K(rows, inner, np.random.default_rng(rows + inner))
+    x = synth.activations(columns, inner, seed=columns)
+    W = pxq.Weight(w, Q5_K, inner, rows)
+    y = pxq.matmul(W, cuda(x), path="matvec").cpu().numpy()
+    pxq.synchronize()
+    W.release()
+    ok, ref = oracle.quant_matmul(w, Q5_K, x, rows)
+    assert ok and max_abs_rel(y, ref) <= TOL
+
+
 @pytest.mark.parametrize("wtype", [Q8_0, Q5_K])
 @pytest.mark.parametrize("columns,rows,inner", [(9, 48, 512), (130, 260, 512), (259, 520, 768), (128, 256, 2048),
                                                 (200, 300, 256)])

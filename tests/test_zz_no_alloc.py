@@ -3,7 +3,7 @@
 It is meant for callers that cannot call cudaMalloc while they run (a decode
 loop that must not stall on the allocator, a region where the application
 forbids allocation, a fixed device-memory budget).  Its quantized activations
-live in a static 1 MiB device array of the library instead of per-call
+live in a static 4 MiB device array of the library instead of per-call
 scratch, so its results must equal those of pxq_matvec, the entry point that
 allocates.  This file sorts last so a `-x` run has already run every other
 test if it fails; it also passes on its own in a fresh process.
@@ -73,7 +73,7 @@ def test_noalloc_rejects_oversized_activation(pxq):
     import torch
 
     lib = pxq.load()
-    rows, inner = 16, 131072  # 8 rows x 512 super-blocks x 292 B > 1 MiB
+    rows, inner = 16, 524288  # activation alone: 8 rows x 2048 super-blocks x 288 B > 4 MiB
     W = pxq.Weight(synth.random_q5_K(rows, inner, np.random.default_rng(1)), 13, inner, rows)
     x = torch.zeros((8, inner), device="cuda")
     y = torch.zeros((8, rows), device="cuda")
