@@ -220,25 +220,28 @@ struct MvShape {
     static constexpr int kSbPitch = TR == 64 ? kQ5KBytes : TR * kQ5KBytes; // shared-memory super-block pitch
     static constexpr int kWeightBytes = TR * kRowBytes;             // 22528
     static constexpr int kActPitch = kSbs * kQ8KMvBytes;            // one activation row's records per stage
-    static constexpr int kActBytes = 8 * kActPitch;                 // up to 8 activation rows
+    static constexpr int kActBytes = 8 * kActPitch + 512;           // up to 8 activation rows, skewed
     static constexpr int kStages = TR == 16 ? 2 : 3;                // two CTAs per SM within 228 KB
     static_assert(kRowBytes % 16 == 0 && kActPitch % 16 == 0, "bulk copies move 16-byte multiples");
     static_assert(kWeightBytes == kMvStageWeightBytes, "every shape streams the same stage size");
 };
 
 constexpr int kMvConsumers = 8;
-constexpr int kMvThreads = (kMvConsumers + 1) * 32;  // + 1 producer warp
+constexpr int kMvProducerWarp = kMvConsumers;            // TMA / bulk-copy issue
+constexpr int kMvFixupWarp = kMvConsumers + 1;           // cross-CTA sums of shared tiles
+constexpr int kMvThreads = (kMvConsumers + 2) * 32;
 
 template <int TR>
 struct MvSmem {
     using Sh = MvShape<TR>;
     uint8_t weight[Sh::kStages][Sh::kWeightBytes];  // [TR][kSbs x 176] (TR = 64) or [kSbs][TR][176]
-    uint8_t act[Sh::kStages][Sh::kActBytes];        // [8 activation rows][kSbs super-blocks x 288]
+    uint8_t act[Sh::kStages][Sh::kActBytes];        // 8 activation rows of kSbs x 288 bytes at act_row_off
     // sums of warps with super-block lane >= 1, handed to lane 0, by segment parity
     float red[2][Sh::kSbs - 1][Sh::kRowGroups][16][8];
     uint64_t full[Sh::kStages], empty[Sh::kStages];
+    uint64_t part;                                   // the first shared tile's partial sums are stored
     uint32_t abort;
-    int last;
+    uint32_t last;                                   // this CTA completes its last shared tile
 };
 
 struct MvParams {
@@ -338,6 +341,91 @@ __device__ __forceinline__ void store_out(const MvParams& p, int64_t r, int64_t 
     p.y[col * p.ldy + r] = p.bias ? __fadd_rn(v, p.bias[r]) : v;
 }
 
+// Shared-memory offset of activation row c within a stage: row pitch
+// kActPitch plus a skew that grows with c (rows never overlap), chosen so that
+// both the B-fragment loads (rows g, g+1 of a quarter warp) and the sum loads
+// (rows 2t of four lanes) hit distinct banks: 16 bytes per row pair when the
+// pitch is an odd multiple of 64 bytes, else 144 bytes per row pair plus 64
+// for odd rows.
+template <int TR>
+__device__ __host__ constexpr uint32_t act_row_off(uint32_t c)
+{
+    return c * MvShape<TR>::kActPitch +
+           (MvShape<TR>::kActPitch % 128 == 0 ? 144 * (c >> 1) + 64 * (c & 1) : 16 * (c >> 1));
+}
+static_assert(act_row_off<16>(7) + MvShape<16>::kActPitch <= MvShape<16>::kActBytes, "activation rows fit the stage");
+static_assert(act_row_off<32>(7) + MvShape<32>::kActPitch <= MvShape<32>::kActBytes, "activation rows fit the stage");
+static_assert(act_row_off<64>(7) + MvShape<64>::kActPitch <= MvShape<64>::kActBytes, "activation rows fit the stage");
+
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v)
+{
+    uint32_t old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+// Sum of the partial sums of tile Tk over its contributing CTAs, in CTA
+// order, stored as the tile's outputs; nthr threads (index tid) share the
+// tile's outputs, and every contributor's load of an output is in flight
+// before the sum.
+template <int TR>
+__device__ __forceinline__ void mv_tile_sum(const MvParams& p, int64_t Tk, int64_t S, int64_t G, uint32_t spt, uint32_t tid,
+                                            uint32_t nthr)
+{
+    const uint32_t columns = (uint32_t)p.columns;
+    const int64_t c_first = cta_of_stage(Tk * spt, S, G), c_last = cta_of_stage((Tk + 1) * spt - 1, S, G);
+    const int64_t tile_floats = (int64_t)columns * TR;
+    // every contributor after the first starts its range in tile Tk, so its
+    // partial sums are in its slot 0; only the first one's slot varies
+    const float* first = p.partial + (c_first * 2 + partial_slot(c_first, Tk, S, G, spt)) * tile_floats;
+    const float* rest = p.partial + (c_first + 1) * 2 * tile_floats;  // slot 0 of CTA c_first + 1
+    const int64_t n_rest = c_last - c_first;
+    for (uint32_t idx = tid; idx < columns * TR; idx += nthr) {  // [column][row of the tile]
+        float w = __ldcg(first + idx);
+        int64_t k = 0;
+        for (; k + 8 <= n_rest; k += 8) {
+            float pv[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) pv[u] = __ldcg(rest + (k + u) * 2 * tile_floats + idx);
+#pragma unroll
+            for (int u = 0; u < 8; u++) w += pv[u];
+        }
+        float pv[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) pv[u] = k + u < n_rest ? __ldcg(rest + (k + u) * 2 * tile_floats + idx) : 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+            if (k + u < n_rest) w += pv[u];
+        const int64_t r = Tk * TR + idx % TR;
+        if (r < p.rows) store_out(p, r, idx / TR, w);
+    }
+}
+
+__device__ __forceinline__ int64_t contributors(int64_t Tk, int64_t S, int64_t G, uint32_t spt)
+{
+    return cta_of_stage((Tk + 1) * spt - 1, S, G) - cta_of_stage(Tk * spt, S, G) + 1;
+}
+
+// Fix-up warp: the first tile of this CTA's range, when it is shared with
+// other CTAs and is not also the last one.  Waits until the consumers stored
+// their partial sums, counts the contribution, and if it is the last one,
+// sums all contributions and stores the tile.  Runs while the consumers go on
+// with the rest of the range.
+template <int TR>
+__device__ __forceinline__ void mv_fixup_first(const MvParams& p, MvSmem<TR>& sm, int64_t S, int64_t G, uint32_t spt,
+                                               uint32_t T0, uint32_t lane)
+{
+    if (!mbar_wait(&sm.part, 0, &sm.abort, p.status, kDevTimeoutFull)) return;
+    // release: the consumers' stores, ordered before by the mbarrier;
+    // acquire: the other contributors' stores, for the loads below
+    uint32_t last = 0;
+    if (lane == 0) last = atom_add_acq_rel_gpu(&p.counters[T0], 1u) == (uint32_t)(contributors(T0, S, G, spt) - 1);
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    mv_tile_sum<TR>(p, T0, S, G, spt, lane, 32);
+    if (lane == 0) p.counters[T0] = 0u;  // ready for the next call
+}
+
 template <int TR>
 __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_constant__ MvParams p)
 {
@@ -347,66 +435,83 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
     MvSmem<TR>& sm = *reinterpret_cast<MvSmem<TR>*>(mv_smem);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     griddep_launch_dependents();
-    const int64_t G = gridDim.x, c = blockIdx.x, S = p.stages, spt = p.spt;
+    const int64_t G = gridDim.x, c = blockIdx.x, S = p.stages;
     const int64_t s_begin = c * S / G, s_end = (c + 1) * S / G;
-    const int64_t T0 = s_begin / spt, q0 = s_begin % spt;  // the only divisions on the stage index
-    const int64_t nsb = p.nsb, columns = p.columns;
+    const uint32_t spt = (uint32_t)p.spt, nst = (uint32_t)(s_end - s_begin);
+    const uint32_t T0 = (uint32_t)(s_begin / spt), q0 = (uint32_t)(s_begin % spt);  // the only divisions
+    const uint32_t nsb = (uint32_t)p.nsb, columns = (uint32_t)p.columns;
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; i++) {
             mbar_init(&sm.full[i], 1);
             mbar_init(&sm.empty[i], kMvConsumers);
         }
+        mbar_init(&sm.part, kRg);
         sm.abort = 0;
         fence_mbar_init();
     }
     __syncthreads();
 
-    if (warp == kMvConsumers) {
+    // Tiles this CTA shares with other CTAs: its first when the range starts
+    // inside it or ends before its end, its last when that differs and the
+    // range ends before its end.  The fix-up warp finishes a shared first tile
+    // that is not also the last; the consumers finish the last one at the end.
+    const uint32_t T1 = (uint32_t)((s_end - 1) / spt), q1 = (uint32_t)((s_end - 1) % spt);
+    const bool first_shared = q0 != 0 || (T1 == T0 && q1 != spt - 1);
+    const bool first_async = first_shared && T1 != T0;
+    const bool last_shared = T1 == T0 ? first_shared : q1 != spt - 1;
+
+    if (warp == kMvFixupWarp) {
+        if (first_async) {
+            griddep_wait();  // counters and partial sums belong to the kernels before this one
+            mv_fixup_first<TR>(p, sm, S, G, spt, T0, lane);
+        }
+        return;
+    }
+
+    if (warp == kMvProducerWarp) {
         if (lane == 0) {
             // producer.  The weights do not depend on earlier kernels: the
             // first stages' weights are requested before griddep_wait, their
             // activation records after it.
             tma_prefetch_desc(&p.map);
-            const int64_t R = s_end - s_begin;
-            const int64_t pre = R < kStages ? R : kStages;
-            int64_t T = T0, q = q0, issued = 0;
-            for (int64_t i = 0; i < R; i++) {
-                const int slot = (int)(i % kStages);
-                const uint32_t round = (uint32_t)(i / kStages);
-                if (i >= kStages && !mbar_wait(&sm.empty[slot], (round - 1) & 1u, &sm.abort, p.status, kDevTimeoutEmpty))
+            const uint32_t pre = nst < (uint32_t)kStages ? nst : (uint32_t)kStages;
+            uint32_t T = T0, q = q0, slot = 0, phase = 0, issued = 0;
+            for (uint32_t i = 0; i < nst; i++) {
+                if (i >= (uint32_t)kStages && !mbar_wait(&sm.empty[slot], phase ^ 1u, &sm.abort, p.status, kDevTimeoutEmpty))
                     break;
-                const int64_t nsb_here = nsb - kSbs * q < kSbs ? nsb - kSbs * q : kSbs;
-                mbar_expect_tx(&sm.full[slot], Sh::kWeightBytes + (uint32_t)(columns * nsb_here * kQ8KMvBytes));
+                const uint32_t nsb_here = nsb - kSbs * q < (uint32_t)kSbs ? nsb - kSbs * q : (uint32_t)kSbs;
+                mbar_expect_tx(&sm.full[slot], Sh::kWeightBytes + columns * nsb_here * kQ8KMvBytes);
                 if (TR == 64)
                     tma_load_2d(sm.weight[slot], &p.map, &sm.full[slot], (int32_t)(q * (Sh::kRowBytes / 8)),
-                                (int32_t)(p.row_first + T * TR));
+                                (int32_t)(p.row_first + (int64_t)T * TR));
                 else
-                    tma_load_3d(sm.weight[slot], &p.map, &sm.full[slot], 0, (int32_t)(p.row_first + T * TR),
+                    tma_load_3d(sm.weight[slot], &p.map, &sm.full[slot], 0, (int32_t)(p.row_first + (int64_t)T * TR),
                                 (int32_t)(q * kSbs));
                 if (i == pre - 1) {
                     griddep_wait();
-                    // activation records of the stages requested so far
-                    int64_t qj = q0;
-                    for (int64_t k = 0; k <= i; k++) {
-                        const int64_t nk = nsb - kSbs * qj < kSbs ? nsb - kSbs * qj : kSbs;
-                        for (int64_t col = 0; col < columns; col++)
-                            bulk_load(sm.act[k] + col * Sh::kActPitch, p.act + (col * nsb + kSbs * qj) * kQ8KMvBytes,
-                                      (uint32_t)(nk * kQ8KMvBytes), &sm.full[k]);
+                    // activation records of the stages requested so far (slots 0..i)
+                    uint32_t qj = q0;
+                    for (uint32_t k = 0; k <= i; k++) {
+                        const uint32_t nk = nsb - kSbs * qj < (uint32_t)kSbs ? nsb - kSbs * qj : (uint32_t)kSbs;
+                        for (uint32_t col = 0; col < columns; col++)
+                            bulk_load(sm.act[k] + act_row_off<TR>(col), p.act + ((int64_t)col * nsb + kSbs * qj) * kQ8KMvBytes,
+                                      nk * kQ8KMvBytes, &sm.full[k]);
                         if (++qj == spt) qj = 0;
                     }
                 } else if (i >= pre) {
-                    for (int64_t col = 0; col < columns; col++)
-                        bulk_load(sm.act[slot] + col * Sh::kActPitch, p.act + (col * nsb + kSbs * q) * kQ8KMvBytes,
-                                  (uint32_t)(nsb_here * kQ8KMvBytes), &sm.full[slot]);
+                    for (uint32_t col = 0; col < columns; col++)
+                        bulk_load(sm.act[slot] + act_row_off<TR>(col), p.act + ((int64_t)col * nsb + kSbs * q) * kQ8KMvBytes,
+                                  nsb_here * kQ8KMvBytes, &sm.full[slot]);
                 }
                 issued = i + 1;
                 if (++q == spt) { q = 0; T++; }
+                if (++slot == (uint32_t)kStages) { slot = 0; phase ^= 1u; }
             }
             // every copy of this CTA lands before it may exit, also after an
             // abort (bounded: a stage that never lands is reported)
             uint32_t never = 0;
-            for (int64_t i = issued - kStages > 0 ? issued - kStages : 0; i < issued; i++)
-                mbar_wait(&sm.full[i % kStages], (uint32_t)(i / kStages) & 1u, &never, p.status, kDevTimeoutFull);
+            for (uint32_t i = issued > (uint32_t)kStages ? issued - kStages : 0; i < issued; i++)
+                mbar_wait(&sm.full[i % kStages], (i / kStages) & 1u, &never, p.status, kDevTimeoutFull);
         }
         return;
     }
@@ -415,22 +520,19 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
     griddep_wait();
     const uint32_t rg = warp % kRg, sbl = warp / kRg;  // row group, super-block lane
     const uint32_t g = lane >> 2, t = lane & 3u;
-    const bool vx = (int64_t)g < columns;
-    const bool vc0 = (int64_t)(2 * t) < columns, vc1 = (int64_t)(2 * t + 1) < columns;
+    const bool vx = g < columns;
+    const bool vc0 = 2 * t < columns, vc1 = 2 * t + 1 < columns;
     const uint32_t row_off = (16 * rg + g) * Sh::kRowPitch + sbl * Sh::kSbPitch;
-    const uint32_t xg_off = g * Sh::kActPitch + sbl * kQ8KMvBytes + 16 * t;        // B fragments, activation row g
-    const uint32_t x0_off = (2 * t) * Sh::kActPitch + sbl * kQ8KMvBytes + kQKK;    // sums + d, activation row 2t
-    const uint32_t x1_off = x0_off + Sh::kActPitch;                                // activation row 2t+1
+    const uint32_t xg_off = act_row_off<TR>(g) + sbl * kQ8KMvBytes + 16 * t;        // B fragments, activation row g
+    const uint32_t x0_off = act_row_off<TR>(2 * t) + sbl * kQ8KMvBytes + kQKK;      // sums + d, activation row 2t
+    const uint32_t x1_off = act_row_off<TR>(2 * t + 1) + sbl * kQ8KMvBytes + kQKK;  // activation row 2t+1
     float acc[4] = {0.f, 0.f, 0.f, 0.f}, summ[4] = {0.f, 0.f, 0.f, 0.f};
     bool ok = true;
-    uint32_t seg = 0;
+    uint32_t seg = 0, slot = 0, phase = 0, T = T0, q = q0;
     bool seg_whole_start = q0 == 0;  // this segment starts at its tile's first stage
-    int64_t T = T0, q = q0;
-    for (int64_t i = 0; i < s_end - s_begin; i++) {
-        const int slot = (int)(i % kStages);
-        const uint32_t round = (uint32_t)(i / kStages);
-        const int64_t sb = kSbs * q + sbl;
-        if (ok) ok = mbar_wait(&sm.full[slot], round & 1u, &sm.abort, p.status, kDevTimeoutFull);
+    for (uint32_t i = 0; i < nst; i++) {
+        const uint32_t sb = kSbs * q + sbl;
+        if (ok) ok = mbar_wait(&sm.full[slot], phase, &sm.abort, p.status, kDevTimeoutFull);
         if (ok && sb < nsb) {
             const uint8_t* wa = sm.weight[slot] + row_off;
             const uint8_t* wb = wa + 8 * Sh::kRowPitch;
@@ -470,10 +572,11 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.empty[slot]);
+        if (++slot == (uint32_t)kStages) { slot = 0; phase ^= 1u; }
         const bool tile_last = q == spt - 1;
-        const int64_t Tcur = T;
+        const uint32_t Tcur = T;
         if (++q == spt) { q = 0; T++; }
-        if (!tile_last && i != s_end - s_begin - 1) continue;
+        if (!tile_last && i != nst - 1) continue;
 
         // ---- end of this CTA's segment of tile Tcur ----
         float v[4] = {acc[0] + summ[0], acc[1] + summ[1], acc[2] + summ[2], acc[3] + summ[3]};
@@ -488,7 +591,6 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
             red[sbl - 1][rg][g + 8][2 * t + 1] = v[3];
         }
         named_bar_sync(1 + rg, 32 * kSbs);
-        const bool whole = seg_whole_start && tile_last;
         if (sbl == 0) {
 #pragma unroll
             for (int k = 0; k < kSbs - 1; k++) {  // fixed order: lane 0, 1, 2, ...
@@ -497,14 +599,14 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
                 v[2] += red[k][rg][g + 8][2 * t];
                 v[3] += red[k][rg][g + 8][2 * t + 1];
             }
-            const int64_t ra = Tcur * TR + 16 * rg + g, rb = ra + 8;
-            if (whole) {
+            const int64_t ra = (int64_t)Tcur * TR + 16 * rg + g, rb = ra + 8;
+            if (seg_whole_start && tile_last) {
                 if (vc0 && ra < p.rows) store_out(p, ra, 2 * t, v[0]);
                 if (vc1 && ra < p.rows) store_out(p, ra, 2 * t + 1, v[1]);
                 if (vc0 && rb < p.rows) store_out(p, rb, 2 * t, v[2]);
                 if (vc1 && rb < p.rows) store_out(p, rb, 2 * t + 1, v[3]);
             } else {
-                // partial: store, count, and the last contributor sums all of them in CTA order
+                // partial sums of this segment for the fix-up warp
                 float* mine = p.partial + (c * 2 + partial_slot(c, Tcur, S, G, spt)) * columns * TR;
                 const uint32_t la = 16 * rg + g, lb = la + 8;
                 if (vc0) {
@@ -515,48 +617,8 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
                     mine[(2 * t + 1) * TR + la] = v[1];
                     mine[(2 * t + 1) * TR + lb] = v[3];
                 }
-                // the lane-0 warps' stores are ordered before the count by one
-                // thread's gpu-scope fence after the barrier (cumulativity),
-                // and the last contributor's reads after it by the same
-                const int64_t c_first = cta_of_stage(Tcur * spt, S, G), c_last = cta_of_stage((Tcur + 1) * spt - 1, S, G);
-                named_bar_sync(5, 32 * kRg);
-                if (threadIdx.x == 0) {
-                    __threadfence();
-                    const bool last = atomicAdd(&p.counters[Tcur], 1u) == (uint32_t)(c_last - c_first);
-                    if (last) __threadfence();
-                    sm.last = last;
-                }
-                named_bar_sync(5, 32 * kRg);
-                if (sm.last) {
-                    float w[4] = {0.f, 0.f, 0.f, 0.f};
-                    for (int64_t k0 = c_first; k0 <= c_last; k0 += 4) {
-                        // four contributors' loads in flight, then summed in CTA order
-                        float pv[4][4];
-#pragma unroll
-                        for (int u = 0; u < 4; u++) {
-                            const int64_t k = k0 + u;
-                            const float* src = p.partial + (k * 2 + partial_slot(k, Tcur, S, G, spt)) * columns * TR;
-                            const bool in = k <= c_last;
-                            pv[u][0] = in && vc0 ? __ldcg(&src[(2 * t) * TR + la]) : 0.f;
-                            pv[u][1] = in && vc1 ? __ldcg(&src[(2 * t + 1) * TR + la]) : 0.f;
-                            pv[u][2] = in && vc0 ? __ldcg(&src[(2 * t) * TR + lb]) : 0.f;
-                            pv[u][3] = in && vc1 ? __ldcg(&src[(2 * t + 1) * TR + lb]) : 0.f;
-                        }
-#pragma unroll
-                        for (int u = 0; u < 4; u++)
-                            if (k0 + u <= c_last) {
-                                w[0] += pv[u][0];
-                                w[1] += pv[u][1];
-                                w[2] += pv[u][2];
-                                w[3] += pv[u][3];
-                            }
-                    }
-                    if (vc0 && ra < p.rows) store_out(p, ra, 2 * t, w[0]);
-                    if (vc1 && ra < p.rows) store_out(p, ra, 2 * t + 1, w[1]);
-                    if (vc0 && rb < p.rows) store_out(p, rb, 2 * t, w[2]);
-                    if (vc1 && rb < p.rows) store_out(p, rb, 2 * t + 1, w[3]);
-                    if (threadIdx.x == 0) p.counters[Tcur] = 0u;  // ready for the next call
-                }
+                __syncwarp();
+                if (seg == 0 && first_async && lane == 0) mbar_arrive(&sm.part);
             }
         }
         acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
@@ -564,6 +626,19 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
         seg++;
         seg_whole_start = true;  // later segments start at a tile's first stage
     }
+
+    // ---- the range's last tile, when shared: count, and the last contributor
+    // sums it with all consumer threads.  The row-group lane-0 warps' stores
+    // are ordered before the count by the barrier and thread 0's release, the
+    // loads after its acquire by the second barrier. ----
+    if (!last_shared) return;
+    named_bar_sync(6, 32 * kMvConsumers);
+    if (threadIdx.x == 0)
+        sm.last = atom_add_acq_rel_gpu(&p.counters[T1], 1u) == (uint32_t)(contributors(T1, S, G, spt) - 1);
+    named_bar_sync(6, 32 * kMvConsumers);
+    if (!sm.last) return;
+    mv_tile_sum<TR>(p, T1, S, G, spt, threadIdx.x, 32 * kMvConsumers);
+    if (threadIdx.x == 0) p.counters[T1] = 0u;  // ready for the next call
 }
 
 template <int TR>
