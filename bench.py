@@ -590,22 +590,20 @@ def run_sharded(args, dist: Dist):
     import torch
     import torch.distributed as tdist
 
-    from pixelina_b200 import pxq
+    from pixelina_b200 import pxq, sharded
 
     wl = GEMM_WORKLOADS["q8_0_large"]
     M, N, K = wl["M"], wl["N"], wl["K"]
     G, r = dist.world, dist.rank
-    assert N % G == 0
-    Ns = N // G
     pxq.init(dist.local)
     gen = torch.Generator(device="cuda")
     gen.manual_seed(5)
     full = gpu_random_q8_0(N, K, gen)  # same seed on every rank -> same weights
-    W = pxq.Weight(full[r * Ns:(r + 1) * Ns].contiguous(), Q8_0, K, Ns)
+    sw = sharded.ShardedWeight(full, Q8_0, K, N, G, r)
+    Ns = sw.count
     del full
     x = torch.randn((M, K), device="cuda", generator=gen)
-    ys = torch.empty((M, Ns), device="cuda")
-    gathered = torch.empty((G * M * Ns,), device="cuda")
+    scratch = (torch.empty((M, Ns), device="cuda"), torch.empty((G * M * Ns,), device="cuda"))
     y = torch.empty((M, N), device="cuda")
     ops = 2.0 * M * N * K
 
@@ -615,12 +613,12 @@ def run_sharded(args, dist: Dist):
             g0, g1 = ev_pair()
             ev["kernels"] = {"gemm": (ev["start"], g1)}
             ev["start"].record()
-        pxq.matmul(W, x, out=ys, path="gemm")
+        pxq.matmul(sw.weight, x, out=scratch[0], path="gemm")
         if ev is not None:
             g1.record()
         if G > 1:
-            tdist.all_gather_into_tensor(gathered, ys.view(-1))
-            pxq.gather_shards(gathered, G, M, Ns, out=y)
+            tdist.all_gather_into_tensor(scratch[1], scratch[0].view(-1))
+            pxq.gather_shards(scratch[1], G, M, Ns, out=y)
         if ev is not None:
             ev["end"].record()
 

@@ -298,17 +298,16 @@ __device__ __forceinline__ int min_dot(const uint4 bs, uint32_t m_lo, uint32_t m
 }
 
 // Sub-blocks 2PR and 2PR+1 of one super-block for weight rows a, b (A) and
-// activation row g (B, zero when vx is false); sca/scb hold the four packed
-// scales of sub-blocks 4*(PR/2) .. 4*(PR/2)+3.  Every lane must call it: the
-// MMA is warp-wide.
+// activation row g (B); sca/scb hold the four packed scales of sub-blocks
+// 4*(PR/2) .. 4*(PR/2)+3.  Every lane must call it: the MMA is warp-wide.
 template <int PR>
-__device__ __forceinline__ void q5_pair(const uint8_t* wa, const uint8_t* wb, const uint8_t* xr, bool vx, uint32_t t,
-                                        uint2 qha, uint2 qhb, uint32_t sca, uint32_t scb, int (&sumi)[4])
+__device__ __forceinline__ void q5_pair(const uint8_t* wa, const uint8_t* wb, const uint8_t* xr, uint32_t t, uint2 qha,
+                                        uint2 qhb, uint32_t sca, uint32_t scb, int (&sumi)[4])
 {
     // sub-blocks 2PR (low nibbles) and 2PR+1 (high nibbles) share these qs bytes
     const uint2 qa = *reinterpret_cast<const uint2*>(wa + 48 + 32 * PR + 8 * t);
     const uint2 qb = *reinterpret_cast<const uint2*>(wb + 48 + 32 * PR + 8 * t);
-    const uint4 bx = vx ? *reinterpret_cast<const uint4*>(xr + 64 * PR) : make_uint4(0, 0, 0, 0);
+    const uint4 bx = *reinterpret_cast<const uint4*>(xr + 64 * PR);
     constexpr int kSh = 16 * (PR & 1);
     {
         constexpr int J = 2 * PR;
@@ -516,12 +515,19 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
         return;
     }
 
-    // consumers: outputs, partials and counters belong to the kernels before this one
+    // consumers.  Activation rows >= columns are never copied: zero them once
+    // in every stage, so that their fragments, sums and scales are zero and
+    // the math needs no predication on the row count.
+    for (uint32_t k = 0; k < (uint32_t)kStages; k++)
+        for (uint32_t c8 = columns; c8 < 8; c8++)
+            for (uint32_t o = threadIdx.x * 16; o < (uint32_t)Sh::kActPitch; o += 32 * kMvConsumers * 16)
+                *reinterpret_cast<uint4*>(sm.act[k] + act_row_off<TR>(c8) + o) = make_uint4(0, 0, 0, 0);
+    named_bar_sync(7, 32 * kMvConsumers);
+    // outputs, partials and counters belong to the kernels before this one
     griddep_wait();
     const uint32_t rg = warp % kRg, sbl = warp / kRg;  // row group, super-block lane
     const uint32_t g = lane >> 2, t = lane & 3u;
-    const bool vx = g < columns;
-    const bool vc0 = 2 * t < columns, vc1 = 2 * t + 1 < columns;
+    const bool vc0 = 2 * t < columns, vc1 = 2 * t + 1 < columns;  // output columns of this lane
     const uint32_t row_off = (16 * rg + g) * Sh::kRowPitch + sbl * Sh::kSbPitch;
     const uint32_t xg_off = act_row_off<TR>(g) + sbl * kQ8KMvBytes + 16 * t;        // B fragments, activation row g
     const uint32_t x0_off = act_row_off<TR>(2 * t) + sbl * kQ8KMvBytes + kQKK;      // sums + d, activation row 2t
@@ -543,19 +549,18 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
             uint32_t sca_lo, sca_hi, mna_lo, mna_hi, scb_lo, scb_hi, mnb_lo, mnb_hi;
             q5_scales(ha, sca_lo, sca_hi, mna_lo, mna_hi);
             q5_scales(hb, scb_lo, scb_hi, mnb_lo, mnb_hi);
-            // activation rows >= columns hold stale bytes: their fragments are zero
             const uint8_t* xr = xs + xg_off;
             int sumi[4] = {0, 0, 0, 0};
-            q5_pair<0>(wa, wb, xr, vx, t, qha, qhb, sca_lo, scb_lo, sumi);
-            q5_pair<1>(wa, wb, xr, vx, t, qha, qhb, sca_lo, scb_lo, sumi);
-            q5_pair<2>(wa, wb, xr, vx, t, qha, qhb, sca_hi, scb_hi, sumi);
-            q5_pair<3>(wa, wb, xr, vx, t, qha, qhb, sca_hi, scb_hi, sumi);
-            const uint4 s0 = vc0 ? *reinterpret_cast<const uint4*>(xs + x0_off) : make_uint4(0, 0, 0, 0);
-            const uint4 s1 = vc1 ? *reinterpret_cast<const uint4*>(xs + x1_off) : make_uint4(0, 0, 0, 0);
+            q5_pair<0>(wa, wb, xr, t, qha, qhb, sca_lo, scb_lo, sumi);
+            q5_pair<1>(wa, wb, xr, t, qha, qhb, sca_lo, scb_lo, sumi);
+            q5_pair<2>(wa, wb, xr, t, qha, qhb, sca_hi, scb_hi, sumi);
+            q5_pair<3>(wa, wb, xr, t, qha, qhb, sca_hi, scb_hi, sumi);
+            const uint4 s0 = *reinterpret_cast<const uint4*>(xs + x0_off);
+            const uint4 s1 = *reinterpret_cast<const uint4*>(xs + x1_off);
             const int msum[4] = {min_dot(s0, mna_lo, mna_hi), min_dot(s1, mna_lo, mna_hi), min_dot(s0, mnb_lo, mnb_hi),
                                  min_dot(s1, mnb_lo, mnb_hi)};
-            const float dx0 = vc0 ? *reinterpret_cast<const float*>(xs + x0_off + 16) : 0.f;
-            const float dx1 = vc1 ? *reinterpret_cast<const float*>(xs + x1_off + 16) : 0.f;
+            const float dx0 = *reinterpret_cast<const float*>(xs + x0_off + 16);
+            const float dx1 = *reinterpret_cast<const float*>(xs + x1_off + 16);
             const float da = __half2float(__ushort_as_half((unsigned short)(ha.x & 0xffffu)));
             const float dma = __half2float(__ushort_as_half((unsigned short)(ha.x >> 16)));
             const float db = __half2float(__ushort_as_half((unsigned short)(hb.x & 0xffffu)));
