@@ -8,7 +8,7 @@ tensor-core GEMM, inputs resident in HBM; L2 is flushed (256 MB write)
 between timed steps, outside the timed events.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload q5k_gemm|q8_0_gemm|q8_0_large|dit|decode|sharded]
+                    [--workload q5k_gemm|q8_0_gemm|q8_0_large|dit|decode|decode_shapes|sharded]
 
 Multi-GPU (torchrun, one rank per GPU): each rank processes its own batch of
 activation rows against the same weights (data parallel over independent
@@ -538,6 +538,65 @@ def run_decode(args, dist: Dist):
             "launches_per_token": 2 * 5 * L, "results": results}
 
 
+def run_decode_shapes(args, dist: Dist):
+    """Per-shape view of BASELINE configs[3]: each decode matrix (QKV, out,
+    gate/up, down) at M = 1 and 8, one call = activation quantize + matvec.
+    Each shape cycles through enough distinct copies of its weight to exceed
+    the 126 MB L2, replayed as a CUDA graph, so the rate is HBM, not L2."""
+    import torch
+
+    from pixelina_b200 import pxq
+
+    pxq.init(dist.local)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(9)
+    H, F, QKV = DECODE["hidden"], DECODE["ffn"], DECODE["qkv"]
+    hbm, _, _, peak_src = measured_peaks()
+    results = {}
+    for name, n, k in (("qkv", QKV, H), ("out", H, H), ("gate_up", F, H), ("down", H, F)):
+        wbytes = pxq.weight_bytes(k, n, Q5_K)
+        copies = max(2, -(-(320 << 20) // wbytes))
+        ws = [pxq.Weight(gpu_random_q5_K(n, k, gen), Q5_K, k, n) for _ in range(copies)]
+        for M in (1, 8):
+            x = torch.randn((M, k), device="cuda", generator=gen)
+            y = torch.empty((M, n), device="cuda")
+
+            def calls():
+                for w in ws:
+                    pxq.matmul(w, x, out=y, path="matvec")
+
+            calls()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                calls()
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(graph):
+                calls()
+            for _ in range(max(3, args.warmup)):
+                graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = ev_pair()
+            e0.record()
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (args.steps * copies)
+            us = dist.max(us)
+            gbs = wbytes / (us * 1e-6) / 1e9
+            results[f"{name} M={M}"] = {"us_per_call": round(us, 2), "weight_GBps": round(gbs, 1),
+                                        "hbm_frac": round(gbs / hbm, 4)}
+            del graph
+        for w in ws:
+            w.release()
+    return {"metric": METRIC, "workload": "decode_shapes: Q5_K quantize + matvec per decode matrix (BASELINE configs[3])",
+            "unit": "GB/s", "peak_hbm_gbs": hbm, "peak_source": peak_src, "results": results}
+
+
 def run_dit(args, dist: Dist):
     """60 DiT blocks of Q8_0 linears, M = 4352.  One step =
     the linear stack of one forward pass (activation quantize + GEMM each)."""
@@ -641,7 +700,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="q5k_gemm",
-                    choices=sorted(GEMM_WORKLOADS) + ["decode", "dit", "sharded"])
+                    choices=sorted(GEMM_WORKLOADS) + ["decode", "decode_shapes", "dit", "sharded"])
     ap.add_argument("--soak", type=float, default=1.5, help="seconds of untimed steps before timing (clock settling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -658,6 +717,8 @@ def main():
             out = run_gemm_workload(args, dist, GEMM_WORKLOADS[args.workload])
         elif args.workload == "decode":
             out = run_decode(args, dist)
+        elif args.workload == "decode_shapes":
+            out = run_decode_shapes(args, dist)
         elif args.workload == "dit":
             out = run_dit(args, dist)
         else:
