@@ -79,6 +79,16 @@ PXQ_API int pxq_quantize_q8_0(const float* x, void* blocks, size_t rows, size_t 
  * quantize_row_q8_K_ref (src/kernels_quant.cpp:80-118); inner % 256 == 0. */
 PXQ_API int pxq_quantize_q8_K(const float* x, void* blocks, size_t rows, size_t inner, void* stream);
 
+/* fp32 device rows -> the matvec's Q8_K records (PXQ_Q8K_MATVEC_BYTES per 256
+ * values): the same quants and scale as pxq_quantize_q8_K, permuted for the
+ * matvec's tensor-core fragments -- quants of sub-block j (32 values), elements
+ * 8t..8t+7, at byte 64*(j/2) + 16*t + 8*(j%2) (t = 0..3) -- then the eight
+ * 32-element sums bsums[2j] + bsums[2j+1] (int16) at byte 256 and d (fp32) at
+ * byte 272.  The layout pxq_matvec feeds itself for Q5_K weights; exported so
+ * it can be checked bit for bit.  inner % 256 == 0, rows <= 8. */
+#define PXQ_Q8K_MATVEC_BYTES 288
+PXQ_API int pxq_quantize_q8_K_matvec(const float* x, void* records, size_t rows, size_t inner, void* stream);
+
 /* Dequantize `count` values of a Q8_0 / Q5_K / Q6_K device buffer to fp32,
  * bit-exact with cpu_decode (src/backend_cpu.cpp:24-101). */
 PXQ_API int pxq_decode(const void* data, uint32_t type, size_t count, float* out, void* stream);

@@ -386,21 +386,21 @@ int run_matvec(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, 
 {
     if (!a->blocks) return fail(PXQ_ERR_UNSUPPORTED, "matvec handles at most 8 columns (got %lld)", (long long)a->M);
     const MatvecPlan plan = plan_matvec(w->type, (int64_t)row_count, w->inner, a->M, d->sms);
-    const size_t ws_bytes = plan.total_bytes - plan.off_partial;
+    // counters and partial sums of this call; its activation region stays unused
     void* ws = nullptr;
     float* partial = nullptr;
     uint32_t* counters = nullptr;
-    if (ws_bytes) {
-        if (cudaMallocAsync(&ws, ws_bytes, s) != cudaSuccess) {
+    if (plan.counter_bytes || plan.partial_bytes) {
+        if (cudaMallocAsync(&ws, plan.total_bytes, s) != cudaSuccess) {
             cudaGetLastError();
             return fail(PXQ_ERR_NO_MEMORY, "matvec workspace allocation failed");
         }
-        partial = static_cast<float*>(ws);
-        counters = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + (plan.off_counters - plan.off_partial));
+        partial = plan.partial_bytes ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + plan.off_partial) : nullptr;
+        counters = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + plan.off_counters);
         if (plan.counter_bytes) PXQ_CUDA(cudaMemsetAsync(counters, 0, plan.counter_bytes, s));
     }
     cudaError_t e = launch_matvec(plan, w->mv_map, (int64_t)row_first, w->raw + row_first * w->stride, w->stride, a->mem,
-                                  output, (int64_t)ldy, bias, partial, counters, d->status, s);
+                                  nullptr, 0, output, (int64_t)ldy, bias, partial, counters, d->status, s);
     if (ws) cudaFreeAsync(ws, s);
     if (counted(e) != cudaSuccess) return fail(PXQ_ERR_CUDA, "matvec launch failed: %s", cudaGetErrorString(e));
     return PXQ_OK;
@@ -438,6 +438,12 @@ void* stream_scratch(int device, cudaStream_t s, size_t need)
     cudaThreadExchangeStreamCaptureMode(&mode);
     if (err != cudaSuccess) {
         cudaGetLastError();
+        return nullptr;
+    }
+    // counters in the scratch must start at zero (calls leave them zero)
+    if (cudaMemsetAsync(p, 0, bytes, s) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(p);
         return nullptr;
     }
     if (e.ptr) g_retired_scratch.push_back(e.ptr);
@@ -509,13 +515,15 @@ int run_matmul(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, 
     }
     if (force == 1 || (force == 0 && columns <= 8)) {
         if (!input) return fail(PXQ_ERR_INVALID, "null input");
-        const MatvecPlan plan = plan_matvec(w->type, (int64_t)row_count, w->inner, (int64_t)columns, d->sms);
+        const MatvecPlan plan = plan_matvec(w->type, (int64_t)row_count, w->inner, (int64_t)columns, d->sms, true);
         void* scratch = stream_scratch(t_device, s, plan.total_bytes);
         const bool own = scratch == nullptr;
         if (own && cudaMallocAsync(&scratch, plan.total_bytes, s) != cudaSuccess) {
             cudaGetLastError();
             return fail(PXQ_ERR_NO_MEMORY, "matvec scratch allocation of %zu bytes failed", plan.total_bytes);
         }
+        if (own && plan.fused && plan.counter_bytes)  // fresh memory: no quantize kernel clears the counters
+            PXQ_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(scratch) + plan.off_counters, 0, plan.counter_bytes, s));
         cudaError_t e = matvec_fused(w, row_first, row_count, input, output, ldy, bias, plan, static_cast<uint8_t*>(scratch),
                                      d->status, s);
         if (own) cudaFreeAsync(scratch, s);
@@ -542,10 +550,12 @@ cudaError_t matvec_fused(const pxq_weight* w, size_t row_first, size_t row_count
 {
     float* partial = plan.partial_bytes ? reinterpret_cast<float*>(scratch + plan.off_partial) : nullptr;
     uint32_t* counters = plan.counter_bytes ? reinterpret_cast<uint32_t*>(scratch + plan.off_counters) : nullptr;
-    cudaError_t e = counted(launch_matvec_quantize(plan, input, w->inner, scratch, counters, s));
+    cudaError_t e = cudaSuccess;
+    uint8_t* act = scratch + plan.off_act;
+    if (!plan.fused) e = counted(launch_matvec_quantize(plan, input, w->inner, act, counters, s));
     if (e == cudaSuccess)
-        e = counted(launch_matvec(plan, w->mv_map, (int64_t)row_first, w->raw + row_first * w->stride, w->stride, scratch,
-                                  output, (int64_t)ldy, bias, partial, counters, status, s));
+        e = counted(launch_matvec(plan, w->mv_map, (int64_t)row_first, w->raw + row_first * w->stride, w->stride, act, input,
+                                  w->inner, output, (int64_t)ldy, bias, partial, counters, status, s));
     return e;
 }
 
@@ -633,6 +643,19 @@ int pxq_quantize_q8_K(const float* x, void* blocks, size_t rows, size_t inner, v
     if (!x || !blocks || !rows || !inner) return fail(PXQ_ERR_INVALID, "null pointer or zero size");
     if (inner % 256) return fail(PXQ_ERR_UNSUPPORTED, "inner %zu not a multiple of 256", inner);
     PXQ_CUDA(counted(launch_quantize_q8_K_blocks(x, blocks, rows, inner, inner, static_cast<cudaStream_t>(stream))));
+    return PXQ_OK;
+}
+
+int pxq_quantize_q8_K_matvec(const float* x, void* records, size_t rows, size_t inner, void* stream)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (!x || !records || !rows || !inner) return fail(PXQ_ERR_INVALID, "null pointer or zero size");
+    if (inner % kQKK) return fail(PXQ_ERR_UNSUPPORTED, "inner %zu not a multiple of 256", inner);
+    if (rows > 8) return fail(PXQ_ERR_UNSUPPORTED, "the matvec operand holds at most 8 rows (got %zu)", rows);
+    static_assert(PXQ_Q8K_MATVEC_BYTES == kQ8KMvBytes, "record size");
+    const MatvecPlan plan = plan_matvec(kTypeQ5_K, 1, (int64_t)inner, (int64_t)rows, d->sms);
+    PXQ_CUDA(counted(launch_matvec_quantize(plan, x, (int64_t)inner, records, nullptr, static_cast<cudaStream_t>(stream))));
     return PXQ_OK;
 }
 

@@ -36,6 +36,7 @@
 // in flight (register double buffering).
 #include "pxq_device.cuh"
 #include "pxq_internal.h"
+#include "q8k.cuh"
 
 namespace pxq {
 namespace {
@@ -227,6 +228,7 @@ struct MvShape {
 };
 
 constexpr int kMvConsumers = 8;
+constexpr int kMvFusedRecords = 32;  // activation records a CTA may quantize itself (the plan checks)
 constexpr int kMvProducerWarp = kMvConsumers;            // TMA / bulk-copy issue
 constexpr int kMvFixupWarp = kMvConsumers + 1;           // cross-CTA sums of shared tiles
 constexpr int kMvThreads = (kMvConsumers + 2) * 32;
@@ -247,7 +249,9 @@ struct MvSmem {
 struct MvParams {
     CUtensorMap map;                   // raw weight bytes: 2-D u64 [rows][stride/8], box {kSbs*22, TR} (TR = 64),
                                        // else 3-D u64 [nsb][rows][22], box {22, TR, kSbs}
-    const uint8_t* act;                // activation records [columns][nsb][kQ8KMvBytes]
+    const uint8_t* act;                // activation records [columns][nsb][kQ8KMvBytes] (not fused)
+    const float* x;                    // fp32 activation rows (fused quantize)
+    int64_t ldx;
     float* y;
     const float* bias;
     float* partial;                    // [grid][2][columns][TR]
@@ -255,6 +259,7 @@ struct MvParams {
     uint32_t* status;
     int64_t ldy, rows, row_first, stages;
     int32_t nsb, spt, columns;
+    int32_t fused;                     // consumers quantize x themselves (small activations)
 };
 
 // First CTA whose stage range [c*S/G, (c+1)*S/G) holds stage s.
@@ -353,6 +358,10 @@ __device__ __host__ constexpr uint32_t act_row_off(uint32_t c)
            (MvShape<TR>::kActPitch % 128 == 0 ? 144 * (c >> 1) + 64 * (c & 1) : 16 * (c >> 1));
 }
 static_assert(act_row_off<16>(7) + MvShape<16>::kActPitch <= MvShape<16>::kActBytes, "activation rows fit the stage");
+static_assert((kMvFusedRecords + 1) * kQ8KMvBytes <= MvShape<64>::kStages * MvShape<64>::kActBytes &&
+                  (kMvFusedRecords + 1) * kQ8KMvBytes <= MvShape<32>::kStages * MvShape<32>::kActBytes &&
+                  (kMvFusedRecords + 1) * kQ8KMvBytes <= MvShape<16>::kStages * MvShape<16>::kActBytes,
+              "fused activation records and the zero record fit the activation buffers");
 static_assert(act_row_off<32>(7) + MvShape<32>::kActPitch <= MvShape<32>::kActBytes, "activation rows fit the stage");
 static_assert(act_row_off<64>(7) + MvShape<64>::kActPitch <= MvShape<64>::kActBytes, "activation rows fit the stage");
 
@@ -439,6 +448,7 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
     const uint32_t spt = (uint32_t)p.spt, nst = (uint32_t)(s_end - s_begin);
     const uint32_t T0 = (uint32_t)(s_begin / spt), q0 = (uint32_t)(s_begin % spt);  // the only divisions
     const uint32_t nsb = (uint32_t)p.nsb, columns = (uint32_t)p.columns;
+    const bool fused = p.fused != 0;
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; i++) {
             mbar_init(&sm.full[i], 1);
@@ -479,14 +489,17 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
                 if (i >= (uint32_t)kStages && !mbar_wait(&sm.empty[slot], phase ^ 1u, &sm.abort, p.status, kDevTimeoutEmpty))
                     break;
                 const uint32_t nsb_here = nsb - kSbs * q < (uint32_t)kSbs ? nsb - kSbs * q : (uint32_t)kSbs;
-                mbar_expect_tx(&sm.full[slot], Sh::kWeightBytes + columns * nsb_here * kQ8KMvBytes);
+                const uint32_t act_tx = fused ? 0u : columns * nsb_here * kQ8KMvBytes;
+                mbar_expect_tx(&sm.full[slot], Sh::kWeightBytes + act_tx);
                 if (TR == 64)
                     tma_load_2d(sm.weight[slot], &p.map, &sm.full[slot], (int32_t)(q * (Sh::kRowBytes / 8)),
                                 (int32_t)(p.row_first + (int64_t)T * TR));
                 else
                     tma_load_3d(sm.weight[slot], &p.map, &sm.full[slot], 0, (int32_t)(p.row_first + (int64_t)T * TR),
                                 (int32_t)(q * kSbs));
-                if (i == pre - 1) {
+                if (fused) {
+                    // the consumers quantize the activation themselves
+                } else if (i == pre - 1) {
                     griddep_wait();
                     // activation records of the stages requested so far (slots 0..i)
                     uint32_t qj = q0;
@@ -515,20 +528,41 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
         return;
     }
 
-    // consumers.  Activation rows >= columns are never copied: zero them once
-    // in every stage, so that their fragments, sums and scales are zero and
-    // the math needs no predication on the row count.
-    for (uint32_t k = 0; k < (uint32_t)kStages; k++)
-        for (uint32_t c8 = columns; c8 < 8; c8++)
-            for (uint32_t o = threadIdx.x * 16; o < (uint32_t)Sh::kActPitch; o += 32 * kMvConsumers * 16)
-                *reinterpret_cast<uint4*>(sm.act[k] + act_row_off<TR>(c8) + o) = make_uint4(0, 0, 0, 0);
-    named_bar_sync(7, 32 * kMvConsumers);
-    // outputs, partials and counters belong to the kernels before this one
-    griddep_wait();
+    // consumers.
     const uint32_t rg = warp % kRg, sbl = warp / kRg;  // row group, super-block lane
     const uint32_t g = lane >> 2, t = lane & 3u;
     const bool vc0 = 2 * t < columns, vc1 = 2 * t + 1 < columns;  // output columns of this lane
     const uint32_t row_off = (16 * rg + g) * Sh::kRowPitch + sbl * Sh::kSbPitch;
+    // Activation, two ways.  Copied per stage: row c of a stage's buffer at
+    // act_row_off(c); rows >= columns are never copied, so zero them once and
+    // their fragments, sums and scales are zero.  Fused: the records of all
+    // of this CTA's stages, [stage][super-block lane][row] x kQ8KMvBytes, in
+    // the same memory, quantized here from x, plus one zero record for rows
+    // >= columns.
+    uint8_t* const act_flat = &sm.act[0][0];
+    uint8_t* const zero_rec = act_flat + kMvFusedRecords * kQ8KMvBytes;
+    if (!fused) {
+        for (uint32_t k = 0; k < (uint32_t)kStages; k++)
+            for (uint32_t c8 = columns; c8 < 8; c8++)
+                for (uint32_t o = threadIdx.x * 16; o < (uint32_t)Sh::kActPitch; o += 32 * kMvConsumers * 16)
+                    *reinterpret_cast<uint4*>(sm.act[k] + act_row_off<TR>(c8) + o) = make_uint4(0, 0, 0, 0);
+    } else if (threadIdx.x < kQ8KMvBytes / 16) {
+        reinterpret_cast<uint4*>(zero_rec)[threadIdx.x] = make_uint4(0, 0, 0, 0);
+    }
+    // outputs, partials, counters and x belong to the kernels before this one
+    griddep_wait();
+    if (fused) {
+        const uint32_t per_stage = kSbs * columns, ntask = nst * per_stage;
+        for (uint32_t task = warp; task < ntask; task += kMvConsumers) {
+            const uint32_t i = task / per_stage, rem = task % per_stage;
+            const uint32_t lane_sb = rem / columns, c = rem % columns;
+            const uint32_t sb = kSbs * ((q0 + i) % spt) + lane_sb;
+            if (sb >= nsb) continue;  // past the end of K: never read
+            const Q8KWarp r = q8_K_warp(p.x + (int64_t)c * p.ldx + (int64_t)sb * kQKK, lane);
+            q8_K_store_mv(act_flat + task * kQ8KMvBytes, r, lane);
+        }
+    }
+    named_bar_sync(7, 32 * kMvConsumers);
     const uint32_t xg_off = act_row_off<TR>(g) + sbl * kQ8KMvBytes + 16 * t;        // B fragments, activation row g
     const uint32_t x0_off = act_row_off<TR>(2 * t) + sbl * kQ8KMvBytes + kQKK;      // sums + d, activation row 2t
     const uint32_t x1_off = act_row_off<TR>(2 * t + 1) + sbl * kQ8KMvBytes + kQKK;  // activation row 2t+1
@@ -542,25 +576,34 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
         if (ok && sb < nsb) {
             const uint8_t* wa = sm.weight[slot] + row_off;
             const uint8_t* wb = wa + 8 * Sh::kRowPitch;
-            const uint8_t* xs = sm.act[slot];
+            const uint8_t *xr, *x0, *x1;  // B fragments of row g; sums + d of rows 2t, 2t+1
+            if (!fused) {
+                xr = sm.act[slot] + xg_off;
+                x0 = sm.act[slot] + x0_off;
+                x1 = sm.act[slot] + x1_off;
+            } else {
+                const uint8_t* rec = act_flat + (i * kSbs + sbl) * columns * kQ8KMvBytes;
+                xr = (g < columns ? rec + g * kQ8KMvBytes : zero_rec) + 16 * t;
+                x0 = (vc0 ? rec + 2 * t * kQ8KMvBytes : zero_rec) + kQKK;
+                x1 = (vc1 ? rec + (2 * t + 1) * kQ8KMvBytes : zero_rec) + kQKK;
+            }
             const uint4 ha = *reinterpret_cast<const uint4*>(wa), hb = *reinterpret_cast<const uint4*>(wb);
             const uint2 qha = *reinterpret_cast<const uint2*>(wa + 16 + 8 * t);
             const uint2 qhb = *reinterpret_cast<const uint2*>(wb + 16 + 8 * t);
             uint32_t sca_lo, sca_hi, mna_lo, mna_hi, scb_lo, scb_hi, mnb_lo, mnb_hi;
             q5_scales(ha, sca_lo, sca_hi, mna_lo, mna_hi);
             q5_scales(hb, scb_lo, scb_hi, mnb_lo, mnb_hi);
-            const uint8_t* xr = xs + xg_off;
             int sumi[4] = {0, 0, 0, 0};
             q5_pair<0>(wa, wb, xr, t, qha, qhb, sca_lo, scb_lo, sumi);
             q5_pair<1>(wa, wb, xr, t, qha, qhb, sca_lo, scb_lo, sumi);
             q5_pair<2>(wa, wb, xr, t, qha, qhb, sca_hi, scb_hi, sumi);
             q5_pair<3>(wa, wb, xr, t, qha, qhb, sca_hi, scb_hi, sumi);
-            const uint4 s0 = *reinterpret_cast<const uint4*>(xs + x0_off);
-            const uint4 s1 = *reinterpret_cast<const uint4*>(xs + x1_off);
+            const uint4 s0 = *reinterpret_cast<const uint4*>(x0);
+            const uint4 s1 = *reinterpret_cast<const uint4*>(x1);
             const int msum[4] = {min_dot(s0, mna_lo, mna_hi), min_dot(s1, mna_lo, mna_hi), min_dot(s0, mnb_lo, mnb_hi),
                                  min_dot(s1, mnb_lo, mnb_hi)};
-            const float dx0 = *reinterpret_cast<const float*>(xs + x0_off + 16);
-            const float dx1 = *reinterpret_cast<const float*>(xs + x1_off + 16);
+            const float dx0 = *reinterpret_cast<const float*>(x0 + 16);
+            const float dx1 = *reinterpret_cast<const float*>(x1 + 16);
             const float da = __half2float(__ushort_as_half((unsigned short)(ha.x & 0xffffu)));
             const float dma = __half2float(__ushort_as_half((unsigned short)(ha.x >> 16)));
             const float db = __half2float(__ushort_as_half((unsigned short)(hb.x & 0xffffu)));
@@ -647,8 +690,9 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
 }
 
 template <int TR>
-cudaError_t launch_q5(const MatvecPlan& plan, const CUtensorMap* map, int64_t row_first, const void* act, float* y,
-                      int64_t ldy, const float* bias, float* partial, uint32_t* counters, uint32_t* status, cudaStream_t s)
+cudaError_t launch_q5(const MatvecPlan& plan, const CUtensorMap* map, int64_t row_first, const void* act, const float* x,
+                      int64_t ldx, float* y, int64_t ldy, const float* bias, float* partial, uint32_t* counters,
+                      uint32_t* status, cudaStream_t s)
 {
     static bool attr_set[16] = {};
     int dev = 0;
@@ -665,6 +709,9 @@ cudaError_t launch_q5(const MatvecPlan& plan, const CUtensorMap* map, int64_t ro
     MvParams prm;
     prm.map = *map;
     prm.act = static_cast<const uint8_t*>(act);
+    prm.x = x;
+    prm.ldx = ldx;
+    prm.fused = plan.fused ? 1 : 0;
     prm.y = y;
     prm.bias = bias;
     prm.partial = partial;
@@ -684,7 +731,7 @@ cudaError_t launch_q5(const MatvecPlan& plan, const CUtensorMap* map, int64_t ro
 
 int matvec_map_index(int tile_rows) { return tile_rows == 64 ? 0 : tile_rows == 32 ? 1 : 2; }
 
-MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t columns, int num_sms)
+MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t columns, int num_sms, bool fuse_quantize)
 {
     MatvecPlan p;
     p.type = type;
@@ -714,7 +761,11 @@ MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t colum
         p.spt = (nsb + sbs - 1) / sbs;
         p.stages = p.tiles * p.spt;
         p.grid = (int)(whole ? p.tiles : (p.stages < slots ? p.stages : slots));
-        p.act_bytes = (size_t)(columns * nsb * kQ8KMvBytes);
+        // small activations: every CTA quantizes the records of its own stages
+        // (at most kMvFusedRecords), no separate quantize kernel
+        const int64_t max_stages = (p.stages + p.grid - 1) / p.grid;
+        p.fused = fuse_quantize && columns * max_stages * sbs <= kMvFusedRecords;
+        p.act_bytes = p.fused ? 0 : (size_t)(columns * nsb * kQ8KMvBytes);
         p.partial_bytes = whole ? 0 : (size_t)p.grid * 2 * columns * p.tile_rows * sizeof(float);
         p.counter_bytes = (size_t)p.tiles * sizeof(uint32_t);
     } else {
@@ -737,29 +788,38 @@ MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t colum
         p.partial_bytes = ks > 1 ? (size_t)ks * columns * rows * sizeof(float) : 0;
         p.counter_bytes = ks > 1 ? (size_t)p.rowgroups * sizeof(uint32_t) : 0;
     }
-    p.off_partial = (p.act_bytes + 255) / 256 * 256;
-    p.off_counters = (p.off_partial + p.partial_bytes + 255) / 256 * 256;
-    p.total_bytes = p.off_counters + p.counter_bytes;
+    // The counters sit at the start of the scratch, in a region that only ever
+    // holds counters; calls leave them zero, so a fused call (no quantize
+    // kernel to clear them) finds zeros there whatever the previous call was.
+    if (p.fused && p.counter_bytes > kMvCounterRegion) {
+        p.fused = false;
+        p.act_bytes = (size_t)(columns * (inner / kQKK) * kQ8KMvBytes);
+    }
+    p.off_counters = 0;
+    p.off_act = (p.counter_bytes > kMvCounterRegion ? p.counter_bytes + 255 : kMvCounterRegion) / 256 * 256;
+    p.off_partial = (p.off_act + p.act_bytes + 255) / 256 * 256;
+    p.total_bytes = p.off_partial + p.partial_bytes;
     return p;
 }
 
 cudaError_t launch_matvec(const MatvecPlan& plan, const CUtensorMap* maps, int64_t row_first, const uint8_t* w,
-                          int64_t stride, const void* act, float* y, int64_t ldy, const float* bias, float* partial,
-                          uint32_t* counters, uint32_t* status, cudaStream_t s)
+                          int64_t stride, const void* act, const float* x, int64_t ldx, float* y, int64_t ldy,
+                          const float* bias, float* partial, uint32_t* counters, uint32_t* status, cudaStream_t s)
 {
     if (plan.columns < 1 || plan.columns > 8 || plan.grid < 1) return cudaErrorInvalidValue;
     if (plan.type == kTypeQ5_K) {
         if (!maps || !counters || (plan.partial_bytes && !partial)) return cudaErrorInvalidValue;
+        if (plan.fused ? !x : !act) return cudaErrorInvalidValue;
         const CUtensorMap* map = maps + matvec_map_index(plan.tile_rows);
         switch (plan.tile_rows) {
-        case 64: return launch_q5<64>(plan, map, row_first, act, y, ldy, bias, partial, counters, status, s);
-        case 32: return launch_q5<32>(plan, map, row_first, act, y, ldy, bias, partial, counters, status, s);
-        case 16: return launch_q5<16>(plan, map, row_first, act, y, ldy, bias, partial, counters, status, s);
+        case 64: return launch_q5<64>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
+        case 32: return launch_q5<32>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
+        case 16: return launch_q5<16>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
         default: return cudaErrorInvalidValue;
         }
     }
     if (plan.type == kTypeQ8_0) {
-        if (plan.ks > 1 && (!partial || !counters)) return cudaErrorInvalidValue;
+        if (plan.fused || (plan.ks > 1 && (!partial || !counters))) return cudaErrorInvalidValue;
         return launch_pdl(k_matvec_q8_0, dim3(plan.grid), dim3(kThreads), 0, s, w, stride, plan.rows, plan.inner,
                           static_cast<const uint8_t*>(act), plan.columns, y, ldy, bias, plan.ks, plan.chunk, partial,
                           counters);

@@ -19,10 +19,12 @@
 // does the set-up (and may make the runtime load this module); make it before
 // any stream capture.
 //
-// Layout of the array per call: the quantized activation rows, then the
-// matvec's fp32 partial sums and counters.  The counters must start at zero:
-// the quantize kernel of each call clears them before the matvec uses them;
-// every other byte the kernels read is written earlier in the same call.
+// Layout of the array per call: the quantized activation rows (none when the
+// matvec quantizes a small activation itself), then the matvec's fp32 partial
+// sums and counters.  The counters must start at zero: the array starts
+// zeroed, the quantize kernel of a call (when there is one) clears them, and
+// every completed matvec leaves them zero; every other byte the kernels read
+// is written earlier in the same call.
 //
 // Sharing: every call on a device uses the same array and it keeps the last
 // call's contents.  Two calls whose work overlaps on the GPU (different
@@ -84,7 +86,8 @@ extern "C" int pxq_matvec_noalloc(pxq_weight* w, size_t row_first, size_t row_co
     // partial sums and counters
     int cur_dev = -1;
     cudaGetDevice(&cur_dev);
-    const pxq::MatvecPlan plan = pxq::plan_matvec(type, (int64_t)row_count, inner, (int64_t)columns, pxq::device_sm_count(cur_dev));
+    const pxq::MatvecPlan plan = pxq::plan_matvec(type, (int64_t)row_count, inner, (int64_t)columns, pxq::device_sm_count(cur_dev),
+                                                  true);
     const uint64_t need = plan.total_bytes;
     if (need > PXQ_NOALLOC_SCRATCH_BYTES) {
         char msg[200];

@@ -57,14 +57,18 @@ cudaError_t launch_decode(const uint8_t* data, uint32_t type, int64_t count, flo
 // Q8_0: 16-row groups, K split over `ks` CTAs per group when groups are few;
 // the activation is GGUF Q8_0 blocks.
 //
-// One call's scratch (256-byte aligned, total_bytes): the activation operand
-// at 0, fp32 partial sums at off_partial, uint32 counters at off_counters.
-// The counters must be zero when the matvec starts: the quantize kernel
-// clears them, and the matvec leaves them zero again.
+// One call's scratch (256-byte aligned, total_bytes): uint32 counters at
+// off_counters = 0, in a region of at least kMvCounterRegion bytes that holds
+// nothing else; the activation operand at off_act; fp32 partial sums at
+// off_partial.  The counters must be zero when the matvec starts: the scratch
+// starts zeroed, the quantize kernel of a call clears them, and every
+// completed matvec leaves them zero again -- so a fused call (no quantize
+// kernel) finds them zero whatever the previous call on the scratch was.
 constexpr int kMvStageSuperBlocks = 8;                    // tile rows / 16 x super-blocks per stage
 constexpr int kMvStageWeightBytes = 16 * kMvStageSuperBlocks * kQ5KBytes;  // 22528, any tile shape
 constexpr int kMvTileShapes = 3;                         // 64 x 2, 32 x 4 and 16 x 8 super-blocks
-constexpr int kQ8KMvBytes = 288;  // {i8 quants [4 pairs][4 lanes][2][8]; i16 32-element sums[8]; f32 d; pad}
+constexpr int kQ8KMvBytes = 288;
+constexpr size_t kMvCounterRegion = 16 << 10;            // scratch bytes reserved for counters  // {i8 quants [4 pairs][4 lanes][2][8]; i16 32-element sums[8]; f32 d; pad}
 
 struct MatvecPlan {
     uint32_t type = 0;
@@ -74,10 +78,13 @@ struct MatvecPlan {
     int grid = 0;                            // CTAs
     int ks = 1, chunk = 0;                   // Q8_0: K slices per row group, blocks per slice
     int64_t rowgroups = 0;                   // Q8_0: 16-row groups
+    bool fused = false;                      // Q5_K: the matvec quantizes the activation itself
     size_t act_bytes = 0, partial_bytes = 0, counter_bytes = 0;
-    size_t off_partial = 0, off_counters = 0, total_bytes = 0;
+    size_t off_counters = 0, off_act = 0, off_partial = 0, total_bytes = 0;
 };
-MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t columns, int num_sms);
+// fuse_quantize: allow the plan to let the matvec quantize a small
+// activation itself (then act_bytes is 0 and launch_matvec takes x).
+MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t columns, int num_sms, bool fuse_quantize = false);
 int matvec_map_index(int tile_rows);
 // Quantize the plan's `columns` activation rows (row stride ldx floats) into
 // the operand at `act`; clears `counters` (plan.counter_bytes) when non-null.
@@ -90,8 +97,8 @@ cudaError_t launch_matvec_quantize(const MatvecPlan& plan, const float* x, int64
 // streams weights before the previous kernel of the stream has finished and
 // touches every other buffer only after it.
 cudaError_t launch_matvec(const MatvecPlan& plan, const CUtensorMap* maps, int64_t row_first, const uint8_t* w,
-                          int64_t stride, const void* act, float* y, int64_t ldy, const float* bias, float* partial,
-                          uint32_t* counters, uint32_t* status, cudaStream_t s);
+                          int64_t stride, const void* act, const float* x, int64_t ldx, float* y, int64_t ldy,
+                          const float* bias, float* partial, uint32_t* counters, uint32_t* status, cudaStream_t s);
 
 // Launch with programmatic stream serialization (see griddep_wait in
 // pxq_device.cuh).

@@ -1,0 +1,89 @@
+// q8k.cuh -- the Q8_K activation quantizer for one 256-value block, one warp
+// per block, 8 consecutive values per lane; shared by the quantize kernels
+// (quantize.cu) and the matvec's fused quantize (matvec.cu), so that both
+// produce the same bytes.  Restates quantize_row_q8_K_ref
+// (src/kernels_quant.cpp:80-118); the rounding rules are listed at the top of
+// quantize.cu.
+#pragma once
+#include "pxq_device.cuh"
+#include "pxq_internal.h"
+
+namespace pxq {
+
+struct Q8KWarp {
+    float d;        // stored fp32 scale (1/iscale, or 0 for an all-zero block)
+    int8_t q[8];    // this lane's 8 quants
+};
+
+__device__ __forceinline__ Q8KWarp q8_K_warp(const float* src, uint32_t lane)
+{
+    const float4 a = ld_dep_f4(src + lane * 8);
+    const float4 b = ld_dep_f4(src + lane * 8 + 4);
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    // first element (in index order) with the largest |x|: strict '>' scan
+    float amax = 0.0f, vmax = 0.0f;
+    int idx = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float ax = fabsf(v[j]);
+        if (ax > amax) {
+            amax = ax;
+            vmax = v[j];
+            idx = (int)lane * 8 + j;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, amax, o);
+        const float ov = __shfl_xor_sync(0xffffffffu, vmax, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (oa > amax || (oa == amax && oi < idx)) {
+            amax = oa;
+            vmax = ov;
+            idx = oi;
+        }
+    }
+    Q8KWarp r;
+    if (amax == 0.0f) {
+        r.d = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) r.q[j] = 0;
+        return r;
+    }
+    const float iscale = __fdiv_rn(-127.0f, vmax);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float biased = __fmaf_rn(iscale, v[j], 12582912.0f);
+        const int bits = __float_as_int(biased);
+        const int q = (bits & 0x007fffff) - 0x00400000;
+        r.q[j] = (int8_t)(q < 127 ? q : 127);
+    }
+    r.d = __fdiv_rn(1.0f, iscale);
+    return r;
+}
+
+// This warp's block as a matvec record (kQ8KMvBytes at `out`, global or
+// shared memory): quants of sub-block j (32 values), elements 8t..8t+7
+// (t = 0..3), at byte 64*(j/2) + 16*t + 8*(j%2) -- lane 4j+t's eight bytes --
+// so a lane's MMA B fragments of two sub-blocks are one 16-byte word and the
+// four lanes of a fragment read 64 contiguous bytes; then the eight 32-element
+// sums bsums[2j] + bsums[2j+1] as int16 at byte 256, and d (fp32) at byte 272.
+__device__ __forceinline__ void q8_K_store_mv(uint8_t* out, const Q8KWarp& r, uint32_t lane)
+{
+    uint32_t lo = 0, hi = 0;
+    int sum8 = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) lo |= (uint32_t)(uint8_t)r.q[j] << (8 * j);
+#pragma unroll
+    for (int j = 0; j < 4; j++) hi |= (uint32_t)(uint8_t)r.q[4 + j] << (8 * j);
+#pragma unroll
+    for (int j = 0; j < 8; j++) sum8 += r.q[j];
+    const uint32_t j = lane >> 2, t = lane & 3u;
+    *reinterpret_cast<uint2*>(out + 64 * (j >> 1) + 16 * t + 8 * (j & 1u)) = make_uint2(lo, hi);
+    int s32 = sum8 + __shfl_xor_sync(0xffffffffu, sum8, 1);
+    s32 += __shfl_xor_sync(0xffffffffu, s32, 2);
+    if (t == 0) *reinterpret_cast<int16_t*>(out + kQKK + 2 * j) = (int16_t)s32;
+    if (lane == 0) *reinterpret_cast<float*>(out + kQKK + 16) = r.d;
+}
+
+}  // namespace pxq

@@ -53,6 +53,7 @@ SIGNATURES = {
     "pxq_weight_bytes": (_u64, [_u64, _u64, _u32]),
     "pxq_quantize_q8_0": (_i, [_vp, _vp, _sz, _sz, _vp]),
     "pxq_quantize_q8_K": (_i, [_vp, _vp, _sz, _sz, _vp]),
+    "pxq_quantize_q8_K_matvec": (_i, [_vp, _vp, _sz, _sz, _vp]),
     "pxq_decode": (_i, [_vp, _u32, _sz, _vp, _vp]),
     "pxq_weight_upload": (_i, [_vp, _i, _u32, _sz, _sz, C.c_char_p, C.POINTER(_vp)]),
     "pxq_weight_release": (_i, [_vp]),
@@ -152,6 +153,20 @@ def quantize_q8_K(x, stream=None):
     rows, inner = x.shape
     out = torch.empty((rows, inner // 256 * Q8_K_BYTES), dtype=torch.uint8, device=x.device)
     _check(load().pxq_quantize_q8_K(_ptr(x), _ptr(out), rows, inner, _stream_ptr(stream)))
+    return out
+
+
+Q8K_MATVEC_BYTES = 288
+
+
+def quantize_q8_K_matvec(x, stream=None):
+    """fp32 [rows <= 8, inner] cuda tensor -> uint8 [rows, inner/256*288] matvec
+    records (the Q8_K quants, permuted, plus 32-element sums and d)."""
+    torch = _torch()
+    x = x.contiguous()
+    rows, inner = x.shape
+    out = torch.empty((rows, inner // 256 * Q8K_MATVEC_BYTES), dtype=torch.uint8, device=x.device)
+    _check(load().pxq_quantize_q8_K_matvec(_ptr(x), _ptr(out), rows, inner, _stream_ptr(stream)))
     return out
 
 

@@ -44,6 +44,45 @@ def test_quantize_random_bitexact(pxq, oracle, rows, inner, scale):
         assert np.array_equal(pxq.quantize_q8_K(xd).cpu().numpy(), oracle.quantize_q8_K(x))
 
 
+def _records_to_q8_K_blocks(rec: np.ndarray) -> np.ndarray:
+    """Undo the matvec record permutation: [rows, nsb*288] -> [rows, nsb*292]
+    GGUF Q8_K blocks (d, qs[256], bsums[16] rebuilt from the quants), and
+    return the records' 32-element sums for a separate check."""
+    rows = rec.shape[0]
+    r = rec.reshape(rows, -1, 288)
+    nsb = r.shape[1]
+    qs = np.empty((rows, nsb, 256), np.int8)
+    for j in range(8):
+        for t in range(4):
+            off = 64 * (j // 2) + 16 * t + 8 * (j % 2)
+            qs[:, :, 32 * j + 8 * t:32 * j + 8 * t + 8] = r[:, :, off:off + 8].view(np.int8)
+    d = r[:, :, 272:276].copy().view(np.float32)
+    sums = r[:, :, 256:272].copy().view(np.int16)
+    bsums = qs.reshape(rows, nsb, 16, 16).astype(np.int32).sum(axis=3).astype(np.int16)
+    blocks = np.concatenate([d.view(np.uint8), qs.view(np.uint8), bsums.view(np.uint8)], axis=2)
+    return blocks.reshape(rows, nsb * 292), sums
+
+
+@pytest.mark.parametrize("src", ["golden", "random"])
+def test_quantize_q8_K_matvec_records_bitexact(pxq, oracle, golden, src):
+    """The matvec's Q8_K records carry exactly the reference's quants, scale
+    and 32-element sums (permuted), for every row count 1..8."""
+    if src == "golden":
+        x = golden["q8_K_x"]
+    else:
+        rng = np.random.default_rng(5)
+        x = (rng.standard_normal((8, 3584)) * 3).astype(np.float32)
+        x[1, :256] = 0.0
+    for rows in sorted({1, min(8, x.shape[0]), x.shape[0] if x.shape[0] <= 8 else 8}):
+        xs = np.ascontiguousarray(x[:rows])
+        rec = pxq.quantize_q8_K_matvec(cuda(xs)).cpu().numpy()
+        blocks, sums = _records_to_q8_K_blocks(rec)
+        want = oracle.quantize_q8_K(xs)
+        assert np.array_equal(blocks, want)
+        wb = want.reshape(rows, -1, 292)[:, :, 260:292].copy().view(np.int16).astype(np.int32)
+        assert np.array_equal(sums.astype(np.int32), wb[:, :, 0::2] + wb[:, :, 1::2])
+
+
 @pytest.mark.parametrize("name,wtype", [("q8_0", Q8_0), ("q5_K", Q5_K), ("q6_K", Q6_K)])
 def test_decode_golden(pxq, golden, name, wtype):
     w = golden[f"w_{name}"]
@@ -94,6 +133,33 @@ def test_matvec_q5_K_tile_shapes(pxq, oracle, rows, inner, columns):
     W.release()
     ok, ref = oracle.quant_matmul(w, Q5_K, x, rows)
     assert ok and max_abs_rel(y, ref) <= TOL
+
+
+def test_matvec_scratch_reuse_across_schedules(pxq, oracle):
+    """Consecutive calls on one stream share the matvec scratch: activation
+    sizes, fused vs separate quantize and whole-tile vs stream-K alternate
+    (down-shape 3584x18944 at M=8 is stream-K with a separate quantize, at M=1
+    stream-K with the quantize fused into the matvec; QKV-shape whole tiles),
+    and every result must still match the oracle."""
+    down = synth.random_q5_K(3584, 18944, np.random.default_rng(21))
+    qkv = synth.random_q5_K(4608, 3584, np.random.default_rng(22))
+    xd = synth.activations(8, 18944, seed=23)
+    xq = synth.activations(8, 3584, seed=24)
+    Wd = pxq.Weight(down, Q5_K, 18944, 3584)
+    Wq = pxq.Weight(qkv, Q5_K, 3584, 4608)
+    refs = {}
+    for W, w, x, m in ((Wd, down, xd, 8), (Wd, down, xd, 1), (Wq, qkv, xq, 1), (Wd, down, xd, 2), (Wd, down, xd, 8),
+                       (Wq, qkv, xq, 8), (Wd, down, xd, 1)):
+        rows = W.rows
+        y = pxq.matmul(W, cuda(x[:m]), path="matvec").cpu().numpy()
+        pxq.synchronize()
+        key = (rows, m)
+        if key not in refs:
+            ok, refs[key] = oracle.quant_matmul(w, Q5_K, x[:m], rows)
+            assert ok
+        assert max_abs_rel(y, refs[key]) <= TOL, key
+    Wd.release()
+    Wq.release()
 
 
 @pytest.mark.parametrize("wtype", [Q8_0, Q5_K])
