@@ -205,6 +205,8 @@ __global__ void __launch_bounds__(kThreads) k_matvec_q8_0(const uint8_t* __restr
 
 // ---------------------------------------------------------------- Q5_K ------
 
+constexpr int kMvFusedRecords = 32;  // activation records a CTA may quantize itself (the plan checks)
+
 // Tile shapes: TR weight rows x 128/TR super-blocks per stage.  Every stage is
 // 22.5 KB of weights; consumer warp w takes rows 16*(w % (TR/16)) .. +15 of
 // the tile and super-block w / (TR/16) of the stage, so all eight warps work
@@ -212,7 +214,7 @@ __global__ void __launch_bounds__(kThreads) k_matvec_q8_0(const uint8_t* __restr
 // row-major ([64][352 B], a 2-D box); the 32- and 16-row stages super-block-
 // major ([sb][TR][176 B], a 3-D box), because a row pitch of 704 or 1408
 // bytes would put all rows of a fragment load in the same banks.
-template <int TR>
+template <int TR, bool FUSED = false>
 struct MvShape {
     static constexpr int kRowGroups = TR / 16;                      // 16-row MMA groups per tile
     static constexpr int kSbs = kMvStageSuperBlocks / kRowGroups;    // super-blocks per stage
@@ -222,35 +224,41 @@ struct MvShape {
     static constexpr int kWeightBytes = TR * kRowBytes;             // 22528
     static constexpr int kActPitch = kSbs * kQ8KMvBytes;            // one activation row's records per stage
     static constexpr int kActBytes = 8 * kActPitch + 512;           // up to 8 activation rows, skewed
-    static constexpr int kStages = TR == 16 ? 2 : 3;                // two CTAs per SM within 228 KB
+    // two CTAs per SM within 228 KB; with a fused quantize there is no
+    // per-stage activation buffer, so the weight ring gets a fourth stage
+    static constexpr int kStages = FUSED ? 4 : (TR == 16 ? 2 : 3);
     static_assert(kRowBytes % 16 == 0 && kActPitch % 16 == 0, "bulk copies move 16-byte multiples");
     static_assert(kWeightBytes == kMvStageWeightBytes, "every shape streams the same stage size");
 };
 
 constexpr int kMvConsumers = 8;
-constexpr int kMvFusedRecords = 32;  // activation records a CTA may quantize itself (the plan checks)
 constexpr int kMvProducerWarp = kMvConsumers;            // TMA / bulk-copy issue
 constexpr int kMvFixupWarp = kMvConsumers + 1;           // cross-CTA sums of shared tiles
 constexpr int kMvThreads = (kMvConsumers + 2) * 32;
 
-template <int TR>
+template <int TR, bool FUSED>
 struct MvSmem {
-    using Sh = MvShape<TR>;
+    using Sh = MvShape<TR, FUSED>;
+    // activation: per-stage buffers (8 rows of kSbs x 288 bytes at
+    // act_row_off), or with a fused quantize the records of all of the CTA's
+    // stages plus one zero record
+    static constexpr int kActAreaBytes = FUSED ? (kMvFusedRecords + 1) * kQ8KMvBytes : Sh::kStages * Sh::kActBytes;
     uint8_t weight[Sh::kStages][Sh::kWeightBytes];  // [TR][kSbs x 176] (TR = 64) or [kSbs][TR][176]
-    uint8_t act[Sh::kStages][Sh::kActBytes];        // 8 activation rows of kSbs x 288 bytes at act_row_off
+    uint8_t act_area[kActAreaBytes];
     // sums of warps with super-block lane >= 1, handed to lane 0, by segment parity
     float red[2][Sh::kSbs - 1][Sh::kRowGroups][16][8];
     uint64_t full[Sh::kStages], empty[Sh::kStages];
     uint64_t part;                                   // the first shared tile's partial sums are stored
     uint32_t abort;
     uint32_t last;                                   // this CTA completes its last shared tile
+    __device__ uint8_t* act(uint32_t k) { return act_area + k * Sh::kActBytes; }
 };
 
 struct MvParams {
     CUtensorMap map;                   // raw weight bytes: 2-D u64 [rows][stride/8], box {kSbs*22, TR} (TR = 64),
                                        // else 3-D u64 [nsb][rows][22], box {22, TR, kSbs}
     const uint8_t* act;                // activation records [columns][nsb][kQ8KMvBytes] (not fused)
-    const float* x;                    // fp32 activation rows (fused quantize)
+    const float* x;                    // fp32 activation rows (fused quantize: the kernel's FUSED variant)
     int64_t ldx;
     float* y;
     const float* bias;
@@ -259,7 +267,6 @@ struct MvParams {
     uint32_t* status;
     int64_t ldy, rows, row_first, stages;
     int32_t nsb, spt, columns;
-    int32_t fused;                     // consumers quantize x themselves (small activations)
 };
 
 // First CTA whose stage range [c*S/G, (c+1)*S/G) holds stage s.
@@ -358,10 +365,7 @@ __device__ __host__ constexpr uint32_t act_row_off(uint32_t c)
            (MvShape<TR>::kActPitch % 128 == 0 ? 144 * (c >> 1) + 64 * (c & 1) : 16 * (c >> 1));
 }
 static_assert(act_row_off<16>(7) + MvShape<16>::kActPitch <= MvShape<16>::kActBytes, "activation rows fit the stage");
-static_assert((kMvFusedRecords + 1) * kQ8KMvBytes <= MvShape<64>::kStages * MvShape<64>::kActBytes &&
-                  (kMvFusedRecords + 1) * kQ8KMvBytes <= MvShape<32>::kStages * MvShape<32>::kActBytes &&
-                  (kMvFusedRecords + 1) * kQ8KMvBytes <= MvShape<16>::kStages * MvShape<16>::kActBytes,
-              "fused activation records and the zero record fit the activation buffers");
+
 static_assert(act_row_off<32>(7) + MvShape<32>::kActPitch <= MvShape<32>::kActBytes, "activation rows fit the stage");
 static_assert(act_row_off<64>(7) + MvShape<64>::kActPitch <= MvShape<64>::kActBytes, "activation rows fit the stage");
 
@@ -419,8 +423,8 @@ __device__ __forceinline__ int64_t contributors(int64_t Tk, int64_t S, int64_t G
 // their partial sums, counts the contribution, and if it is the last one,
 // sums all contributions and stores the tile.  Runs while the consumers go on
 // with the rest of the range.
-template <int TR>
-__device__ __forceinline__ void mv_fixup_first(const MvParams& p, MvSmem<TR>& sm, int64_t S, int64_t G, uint32_t spt,
+template <int TR, bool FUSED>
+__device__ __forceinline__ void mv_fixup_first(const MvParams& p, MvSmem<TR, FUSED>& sm, int64_t S, int64_t G, uint32_t spt,
                                                uint32_t T0, uint32_t lane)
 {
     if (!mbar_wait(&sm.part, 0, &sm.abort, p.status, kDevTimeoutFull)) return;
@@ -434,13 +438,13 @@ __device__ __forceinline__ void mv_fixup_first(const MvParams& p, MvSmem<TR>& sm
     if (lane == 0) p.counters[T0] = 0u;  // ready for the next call
 }
 
-template <int TR>
+template <int TR, bool FUSED>
 __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_constant__ MvParams p)
 {
-    using Sh = MvShape<TR>;
+    using Sh = MvShape<TR, FUSED>;
     constexpr int kStages = Sh::kStages, kSbs = Sh::kSbs, kRg = Sh::kRowGroups;
     extern __shared__ __align__(128) uint8_t mv_smem[];
-    MvSmem<TR>& sm = *reinterpret_cast<MvSmem<TR>*>(mv_smem);
+    MvSmem<TR, FUSED>& sm = *reinterpret_cast<MvSmem<TR, FUSED>*>(mv_smem);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     griddep_launch_dependents();
     const int64_t G = gridDim.x, c = blockIdx.x, S = p.stages;
@@ -448,7 +452,7 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
     const uint32_t spt = (uint32_t)p.spt, nst = (uint32_t)(s_end - s_begin);
     const uint32_t T0 = (uint32_t)(s_begin / spt), q0 = (uint32_t)(s_begin % spt);  // the only divisions
     const uint32_t nsb = (uint32_t)p.nsb, columns = (uint32_t)p.columns;
-    const bool fused = p.fused != 0;
+    constexpr bool fused = FUSED;
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; i++) {
             mbar_init(&sm.full[i], 1);
@@ -472,7 +476,7 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
     if (warp == kMvFixupWarp) {
         if (first_async) {
             griddep_wait();  // counters and partial sums belong to the kernels before this one
-            mv_fixup_first<TR>(p, sm, S, G, spt, T0, lane);
+            mv_fixup_first<TR, FUSED>(p, sm, S, G, spt, T0, lane);
         }
         return;
     }
@@ -506,13 +510,13 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
                     for (uint32_t k = 0; k <= i; k++) {
                         const uint32_t nk = nsb - kSbs * qj < (uint32_t)kSbs ? nsb - kSbs * qj : (uint32_t)kSbs;
                         for (uint32_t col = 0; col < columns; col++)
-                            bulk_load(sm.act[k] + act_row_off<TR>(col), p.act + ((int64_t)col * nsb + kSbs * qj) * kQ8KMvBytes,
+                            bulk_load(sm.act(k) + act_row_off<TR>(col), p.act + ((int64_t)col * nsb + kSbs * qj) * kQ8KMvBytes,
                                       nk * kQ8KMvBytes, &sm.full[k]);
                         if (++qj == spt) qj = 0;
                     }
                 } else if (i >= pre) {
                     for (uint32_t col = 0; col < columns; col++)
-                        bulk_load(sm.act[slot] + act_row_off<TR>(col), p.act + ((int64_t)col * nsb + kSbs * q) * kQ8KMvBytes,
+                        bulk_load(sm.act(slot) + act_row_off<TR>(col), p.act + ((int64_t)col * nsb + kSbs * q) * kQ8KMvBytes,
                                   nsb_here * kQ8KMvBytes, &sm.full[slot]);
                 }
                 issued = i + 1;
@@ -539,27 +543,38 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
     // of this CTA's stages, [stage][super-block lane][row] x kQ8KMvBytes, in
     // the same memory, quantized here from x, plus one zero record for rows
     // >= columns.
-    uint8_t* const act_flat = &sm.act[0][0];
+    uint8_t* const act_flat = sm.act_area;
     uint8_t* const zero_rec = act_flat + kMvFusedRecords * kQ8KMvBytes;
     if (!fused) {
         for (uint32_t k = 0; k < (uint32_t)kStages; k++)
             for (uint32_t c8 = columns; c8 < 8; c8++)
                 for (uint32_t o = threadIdx.x * 16; o < (uint32_t)Sh::kActPitch; o += 32 * kMvConsumers * 16)
-                    *reinterpret_cast<uint4*>(sm.act[k] + act_row_off<TR>(c8) + o) = make_uint4(0, 0, 0, 0);
+                    *reinterpret_cast<uint4*>(sm.act(k) + act_row_off<TR>(c8) + o) = make_uint4(0, 0, 0, 0);
     } else if (threadIdx.x < kQ8KMvBytes / 16) {
         reinterpret_cast<uint4*>(zero_rec)[threadIdx.x] = make_uint4(0, 0, 0, 0);
     }
     // outputs, partials, counters and x belong to the kernels before this one
     griddep_wait();
     if (fused) {
+        // this warp's tasks (at most kMvFusedRecords / 8): every load in
+        // flight before the first block is quantized
+        constexpr int kPerWarp = kMvFusedRecords / kMvConsumers;
         const uint32_t per_stage = kSbs * columns, ntask = nst * per_stage;
-        for (uint32_t task = warp; task < ntask; task += kMvConsumers) {
+        float v[kPerWarp][8];
+        uint32_t sbk[kPerWarp];
+#pragma unroll
+        for (int k = 0; k < kPerWarp; k++) {
+            const uint32_t task = warp + kMvConsumers * k;
             const uint32_t i = task / per_stage, rem = task % per_stage;
             const uint32_t lane_sb = rem / columns, c = rem % columns;
-            const uint32_t sb = kSbs * ((q0 + i) % spt) + lane_sb;
-            if (sb >= nsb) continue;  // past the end of K: never read
-            const Q8KWarp r = q8_K_warp(p.x + (int64_t)c * p.ldx + (int64_t)sb * kQKK, lane);
-            q8_K_store_mv(act_flat + task * kQ8KMvBytes, r, lane);
+            sbk[k] = task < ntask ? kSbs * ((q0 + i) % spt) + lane_sb : nsb;  // >= nsb: nothing to do
+            if (sbk[k] < nsb) q8_K_load(p.x + (int64_t)c * p.ldx + (int64_t)sbk[k] * kQKK, lane, v[k]);
+        }
+#pragma unroll
+        for (int k = 0; k < kPerWarp; k++) {
+            if (sbk[k] >= nsb) continue;  // warp-uniform; past the end of K the record is never read
+            const Q8KWarp r = q8_K_warp_vals(v[k], lane);
+            q8_K_store_mv(act_flat + (warp + kMvConsumers * k) * kQ8KMvBytes, r, lane);
         }
     }
     named_bar_sync(7, 32 * kMvConsumers);
@@ -578,9 +593,9 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
             const uint8_t* wb = wa + 8 * Sh::kRowPitch;
             const uint8_t *xr, *x0, *x1;  // B fragments of row g; sums + d of rows 2t, 2t+1
             if (!fused) {
-                xr = sm.act[slot] + xg_off;
-                x0 = sm.act[slot] + x0_off;
-                x1 = sm.act[slot] + x1_off;
+                xr = sm.act(slot) + xg_off;
+                x0 = sm.act(slot) + x0_off;
+                x1 = sm.act(slot) + x1_off;
             } else {
                 const uint8_t* rec = act_flat + (i * kSbs + sbl) * columns * kQ8KMvBytes;
                 xr = (g < columns ? rec + g * kQ8KMvBytes : zero_rec) + 16 * t;
@@ -689,7 +704,7 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
     if (threadIdx.x == 0) p.counters[T1] = 0u;  // ready for the next call
 }
 
-template <int TR>
+template <int TR, bool FUSED>
 cudaError_t launch_q5(const MatvecPlan& plan, const CUtensorMap* map, int64_t row_first, const void* act, const float* x,
                       int64_t ldx, float* y, int64_t ldy, const float* bias, float* partial, uint32_t* counters,
                       uint32_t* status, cudaStream_t s)
@@ -698,10 +713,10 @@ cudaError_t launch_q5(const MatvecPlan& plan, const CUtensorMap* map, int64_t ro
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 16 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(k_matvec_q5_K<TR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)sizeof(MvSmem<TR>));
+        cudaError_t e = cudaFuncSetAttribute(k_matvec_q5_K<TR, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)sizeof(MvSmem<TR, FUSED>));
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(k_matvec_q5_K<TR>, cudaFuncAttributePreferredSharedMemoryCarveout,
+            e = cudaFuncSetAttribute(k_matvec_q5_K<TR, FUSED>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                      (int)cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
@@ -711,7 +726,6 @@ cudaError_t launch_q5(const MatvecPlan& plan, const CUtensorMap* map, int64_t ro
     prm.act = static_cast<const uint8_t*>(act);
     prm.x = x;
     prm.ldx = ldx;
-    prm.fused = plan.fused ? 1 : 0;
     prm.y = y;
     prm.bias = bias;
     prm.partial = partial;
@@ -724,7 +738,7 @@ cudaError_t launch_q5(const MatvecPlan& plan, const CUtensorMap* map, int64_t ro
     prm.nsb = (int32_t)(plan.inner / kQKK);
     prm.spt = (int32_t)plan.spt;
     prm.columns = (int32_t)plan.columns;
-    return launch_pdl(k_matvec_q5_K<TR>, dim3(plan.grid), dim3(kMvThreads), sizeof(MvSmem<TR>), s, prm);
+    return launch_pdl(k_matvec_q5_K<TR, FUSED>, dim3(plan.grid), dim3(kMvThreads), sizeof(MvSmem<TR, FUSED>), s, prm);
 }
 
 }  // namespace
@@ -812,9 +826,15 @@ cudaError_t launch_matvec(const MatvecPlan& plan, const CUtensorMap* maps, int64
         if (plan.fused ? !x : !act) return cudaErrorInvalidValue;
         const CUtensorMap* map = maps + matvec_map_index(plan.tile_rows);
         switch (plan.tile_rows) {
-        case 64: return launch_q5<64>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
-        case 32: return launch_q5<32>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
-        case 16: return launch_q5<16>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
+        case 64:
+            return plan.fused ? launch_q5<64, true>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s)
+                              : launch_q5<64, false>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
+        case 32:
+            return plan.fused ? launch_q5<32, true>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s)
+                              : launch_q5<32, false>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
+        case 16:
+            return plan.fused ? launch_q5<16, true>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s)
+                              : launch_q5<16, false>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
         default: return cudaErrorInvalidValue;
         }
     }

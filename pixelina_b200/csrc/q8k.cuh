@@ -15,11 +15,18 @@ struct Q8KWarp {
     int8_t q[8];    // this lane's 8 quants
 };
 
-__device__ __forceinline__ Q8KWarp q8_K_warp(const float* src, uint32_t lane)
+// The block's values 8*lane .. 8*lane+7 (coherent loads: an earlier kernel
+// may have written them).
+__device__ __forceinline__ void q8_K_load(const float* src, uint32_t lane, float (&v)[8])
 {
     const float4 a = ld_dep_f4(src + lane * 8);
     const float4 b = ld_dep_f4(src + lane * 8 + 4);
-    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ Q8KWarp q8_K_warp_vals(const float (&v)[8], uint32_t lane)
+{
     // first element (in index order) with the largest |x|: strict '>' scan
     float amax = 0.0f, vmax = 0.0f;
     int idx = 0x7fffffff;
@@ -60,6 +67,13 @@ __device__ __forceinline__ Q8KWarp q8_K_warp(const float* src, uint32_t lane)
     }
     r.d = __fdiv_rn(1.0f, iscale);
     return r;
+}
+
+__device__ __forceinline__ Q8KWarp q8_K_warp(const float* src, uint32_t lane)
+{
+    float v[8];
+    q8_K_load(src, lane, v);
+    return q8_K_warp_vals(v, lane);
 }
 
 // This warp's block as a matvec record (kQ8KMvBytes at `out`, global or
