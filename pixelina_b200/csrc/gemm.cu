@@ -23,10 +23,16 @@
 //     because fp16*fp16 fits fp32 -- so the drain is one FMA per element per
 //     block and reads no scale from shared memory.
 //   * Q5_K: 6-bit sub-block scales are folded into the weight operand
-//     (sc*q5 <= 1953, exact in fp16): one MMA item per 64 values.  The min term
+//     (sc*q5 <= 1953, exact in fp16), so every 64-value chunk dot is exact in
+//     the fp32 accumulator, and the four chunks of a super-block, which share
+//     its scale dW*dX, accumulate into one TMEM slot: one drain per
+//     super-block.  Their sum is exact while it stays below 2^24 in magnitude
+//     (always, for real activations; the reference rounds its int32 sum to
+//     fp32 once, the tensor core at most at each chunk boundary beyond that).
+//     The block-dot dump (pxq_gemm_block_dots) drains every chunk on its own,
+//     so the exact int32 chunk dots stay checkable.  The min term
 //     sum_j m_j*bsum_j is a K=16 MMA per super-block on exact (hi, lo) splits,
-//     drained first; the super-block scale dW*dX is then cached in registers
-//     for the four chunks.
+//     drained first.
 //   * Warp roles (12 warps, 3 warpgroups): warpgroups 0-1 drain TMEM (warp w
 //     reads lane quadrant w%4 and column half w/4) with 232 registers
 //     (setmaxnreg); warpgroup 2 runs the TMA producer (warp 8) and the
@@ -303,18 +309,28 @@ __global__ void __launch_bounds__(THREADS, 1)
                             }
                         }
                     } else {
-                        if (!mbar_wait(&tempty[slot], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
-                        tc_fence_after();
+                        // Q5_K: the four 64-value chunks of a super-block share its scale, so
+                        // they accumulate into one TMEM slot (one drain per super-block); the
+                        // block-dot dump keeps one slot per chunk
+                        const bool first = DUMP || kc % 4 == 0;
+                        const bool last = DUMP || kc % 4 == 3 || kc == nchunks - 1;
+                        if (first) {
+                            if (!mbar_wait(&tempty[slot], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
+                            tc_fence_after();
+                        }
                         const uint32_t d = tmem_base + (uint32_t)slot * TM;
 #pragma unroll
                         for (int k = 0; k < 4; k++) {
                             const uint32_t koff = (uint32_t)k * 32u;
-                            mma_f16(d, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC, (uint32_t)k);
+                            mma_f16(d, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC,
+                                    (first && k == 0) ? 0u : 1u);
                         }
-                        mma_commit(&tfull[slot]);
-                        if (++slot == SLOTS) {
-                            slot = 0;
-                            tph ^= 1u;
+                        if (last) {
+                            mma_commit(&tfull[slot]);
+                            if (++slot == SLOTS) {
+                                slot = 0;
+                                tph ^= 1u;
+                            }
                         }
                     }
                     mma_commit(&empty[stage]);
@@ -397,8 +413,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                         s[4 * j + 2] = __fmul_rn(-v.z, dmw);
                         s[4 * j + 3] = __fmul_rn(-v.w, dmw);
                     }
+                    // items: the min term, then the super-block's chunk sum (one per chunk
+                    // when dumping block dots)
 #pragma unroll 1
-                    for (int it = 0; it < 5; it++) {
+                    for (int it = 0; it < (DUMP ? 5 : 2); it++) {
                         if (it == 1) {
                             // d = y.d * fp16(x.d), cached for the four chunks
 #pragma unroll
