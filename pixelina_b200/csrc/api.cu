@@ -302,7 +302,7 @@ int check_matmul_args(pxq_weight* w, size_t row_first, size_t row_count, const v
         return fail(PXQ_ERR_INVALID, "row range [%zu, %zu) outside weight with %lld rows", row_first, row_first + row_count,
                     (long long)w->rows);
     if (ldy < row_count && columns > 1) return fail(PXQ_ERR_INVALID, "ldy %zu < row_count %zu", ldy, row_count);
-    if (w->type != kTypeQ8_0 && w->type != kTypeQ5_K)
+    if (w->type != kTypeQ8_0 && w->type != kTypeQ5_K && w->type != kTypeQ6_K)
         return fail(PXQ_ERR_UNSUPPORTED, "weight type %u not supported", w->type);
     return PXQ_OK;
 }
@@ -313,14 +313,17 @@ int quantize_activation(DeviceCtx* d, uint32_t wtype, const float* input, int64_
 {
     *out = nullptr;
     if (!input || !M || !K) return fail(PXQ_ERR_INVALID, "null input or zero size");
-    if (wtype != kTypeQ8_0 && wtype != kTypeQ5_K) return fail(PXQ_ERR_UNSUPPORTED, "weight type %u not supported", wtype);
-    const bool q5 = wtype == kTypeQ5_K;
+    if (wtype != kTypeQ8_0 && wtype != kTypeQ5_K && wtype != kTypeQ6_K)
+        return fail(PXQ_ERR_UNSUPPORTED, "weight type %u not supported", wtype);
+    const bool q5 = wtype != kTypeQ8_0;  // K-quants: Q8_K activations
     if (K % (q5 ? kQKK : kQK8_0)) return fail(PXQ_ERR_UNSUPPORTED, "inner %lld not a multiple of the block", (long long)K);
     auto a = std::make_unique<pxq_activation>();
     a->wtype = wtype;
     a->M = M;
     a->K = K;
     a->blocks = layout == 0 ? (M <= 8) : (layout == 1);
+    if (wtype == kTypeQ6_K && (!a->blocks || M > 8))
+        return fail(PXQ_ERR_UNSUPPORTED, "Q6_K weights: only the matvec (at most 8 activation rows) is supported");
     const int64_t nb = q5 ? K / kQKK : K / kQK8_0;
     cudaError_t e;
     if (a->blocks) {
@@ -510,6 +513,8 @@ int run_matmul(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, 
                float* output, size_t ldy, const float* bias, float* dump, int force, cudaStream_t s)
 {
     if (force == 1 && columns > 8) return fail(PXQ_ERR_UNSUPPORTED, "matvec handles at most 8 columns (got %zu)", columns);
+    if (w->type == kTypeQ6_K && (force == 2 || columns > 8))
+        return fail(PXQ_ERR_UNSUPPORTED, "Q6_K weights: only the matvec (at most 8 activation rows) is supported");
     if (w->type == kTypeQ8_0 || w->type == kTypeQ5_K) {
         if (w->inner % 8) return fail(PXQ_ERR_UNSUPPORTED, "inner %lld not a multiple of 8", (long long)w->inner);
     }
@@ -678,7 +683,8 @@ int pxq_weight_upload(const void* bytes, int bytes_on_device, uint32_t type, siz
     if (int rc = ensure_device(&d)) return rc;
     if (!bytes || !out) return fail(PXQ_ERR_INVALID, "null bytes or out");
     *out = nullptr;
-    if (type != PXQ_TYPE_Q8_0 && type != PXQ_TYPE_Q5_K) return fail(PXQ_ERR_UNSUPPORTED, "weight type %u not supported", type);
+    if (type != PXQ_TYPE_Q8_0 && type != PXQ_TYPE_Q5_K && type != PXQ_TYPE_Q6_K)
+        return fail(PXQ_ERR_UNSUPPORTED, "weight type %u not supported", type);
     const uint64_t total = pxq_weight_bytes(inner, rows, type);
     if (!total) return fail(PXQ_ERR_INVALID, "invalid weight shape [%zu, %zu] for type %u", inner, rows, type);
     if (inner > 0x7fffffffu || rows > 0x7fffffffu)
@@ -699,26 +705,56 @@ int pxq_weight_upload(const void* bytes, int bytes_on_device, uint32_t type, siz
     w->stride = (int64_t)pxq_weight_bytes(inner, 1, type);
     w->device = t_device;
     w->key = k;
-    if (cudaMalloc(&w->raw, total + 64) != cudaSuccess) {
+    const bool q6 = type == PXQ_TYPE_Q6_K;
+    const uint64_t nsb = inner / 256;
+    // Q6_K rows live on the device with every 210-byte super-block padded to
+    // 224 bytes (16-byte multiples, as TMA rows need)
+    if (q6) w->stride = (int64_t)(nsb * kQ6KPadBytes);
+    const uint64_t dev_bytes = q6 ? (uint64_t)w->stride * rows : total;
+    if (cudaMalloc(&w->raw, dev_bytes + 64) != cudaSuccess) {
         cudaGetLastError();
-        return fail(PXQ_ERR_NO_MEMORY, "cannot allocate %llu bytes for weight", (unsigned long long)total);
+        return fail(PXQ_ERR_NO_MEMORY, "cannot allocate %llu bytes for weight", (unsigned long long)dev_bytes);
     }
-    PXQ_CUDA(cudaMemset(w->raw + total, 0, 64));
-    PXQ_CUDA(cudaMemcpy(w->raw, bytes, total, bytes_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
+    PXQ_CUDA(cudaMemset(w->raw + dev_bytes, 0, 64));
+    if (!q6) {
+        PXQ_CUDA(cudaMemcpy(w->raw, bytes, total, bytes_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
+    } else {
+        const void* src = bytes;
+        void* tmp = nullptr;
+        if (!bytes_on_device || (reinterpret_cast<uintptr_t>(bytes) & 1u)) {
+            if (cudaMalloc(&tmp, total) != cudaSuccess) {
+                cudaGetLastError();
+                return fail(PXQ_ERR_NO_MEMORY, "cannot allocate %llu bytes of upload staging", (unsigned long long)total);
+            }
+            const cudaError_t e = cudaMemcpy(tmp, bytes, total, bytes_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) {
+                cudaFree(tmp);
+                return fail(PXQ_ERR_CUDA, "weight copy failed: %s", cudaGetErrorString(e));
+            }
+            src = tmp;
+        }
+        cudaError_t e = launch_pad_q6_K(src, w->raw, (int64_t)(nsb * rows), nullptr);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (tmp) cudaFree(tmp);
+        if (e != cudaSuccess) return fail(PXQ_ERR_CUDA, "Q6_K padding failed: %s", cudaGetErrorString(e));
+    }
     std::memset(w->mv_map, 0, sizeof(w->mv_map));
-    if (type == PXQ_TYPE_Q5_K) {
+    if (type == PXQ_TYPE_Q5_K || q6) {
         // the matvec's TMA views, one box = one stage of a tr-row tile
-        // (kMvStageSuperBlocks*16/tr super-blocks): 64 rows as a 2-D view
-        // (rows of stride/8 64-bit words), 32 and 16 rows as a 3-D view
-        // (super-block, row, 22 words) that lands super-block-major
-        const uint64_t nsb = inner / 256;
-        if (int rc = make_map(d, &w->mv_map[matvec_map_index(64)], CU_TENSOR_MAP_DATA_TYPE_UINT64, w->raw,
-                              (uint64_t)w->stride / 8, rows, (uint64_t)w->stride,
-                              (uint32_t)(kMvStageSuperBlocks / 4 * kQ5KBytes / 8), 64, CU_TENSOR_MAP_SWIZZLE_NONE))
-            return rc;
-        for (int tr : {32, 16}) {
-            if (int rc = make_map3(d, &w->mv_map[matvec_map_index(tr)], CU_TENSOR_MAP_DATA_TYPE_UINT64, w->raw,
-                                   kQ5KBytes / 8, rows, nsb, (uint64_t)w->stride, kQ5KBytes, kQ5KBytes / 8, (uint32_t)tr,
+        // (kMvStageSuperBlocks*16/tr super-blocks): Q5_K 64-row stages as a
+        // 2-D view (rows of stride/8 64-bit words), the others as a 3-D view
+        // (super-block, row, super-block words) that lands super-block-major
+        const uint32_t sbb = q6 ? kQ6KPadBytes : kQ5KBytes;
+        if (!q6) {
+            if (int rc = make_map(d, &w->mv_map[matvec_map_index(64)], CU_TENSOR_MAP_DATA_TYPE_UINT64, w->raw,
+                                  (uint64_t)w->stride / 8, rows, (uint64_t)w->stride,
+                                  (uint32_t)(kMvStageSuperBlocks / 4 * kQ5KBytes / 8), 64, CU_TENSOR_MAP_SWIZZLE_NONE))
+                return rc;
+        }
+        for (int tr : {64, 32, 16}) {
+            if (tr == 64 && !q6) continue;
+            if (int rc = make_map3(d, &w->mv_map[matvec_map_index(tr)], CU_TENSOR_MAP_DATA_TYPE_UINT64, w->raw, sbb / 8, rows,
+                                   nsb, (uint64_t)w->stride, sbb, sbb / 8, (uint32_t)tr,
                                    (uint32_t)(kMvStageSuperBlocks * 16 / tr)))
                 return rc;
         }
@@ -903,7 +939,8 @@ int pxq_quant_matmul(const unsigned char* weights, uint32_t type, const float* i
     const size_t block = type == PXQ_TYPE_Q8_0 ? 32 : 256;
     if (!rows || !columns || !inner || inner % block || inner > 0x7fffffffu)
         return fail(PXQ_ERR_UNSUPPORTED, "shape rows=%zu columns=%zu inner=%zu not handled", rows, columns, inner);
-    if (type == PXQ_TYPE_Q6_K) return fail(PXQ_ERR_UNSUPPORTED, "Q6_K weights are not handled by this backend yet");
+    if (type == PXQ_TYPE_Q6_K && columns > 8)
+        return fail(PXQ_ERR_UNSUPPORTED, "Q6_K weights: only the matvec (at most 8 activation rows) is handled");
     if (!weights || !input || !output) return fail(PXQ_ERR_INVALID, "null pointer");
     DeviceCtx* d;
     if (int rc = ensure_device(&d)) return rc;

@@ -207,28 +207,57 @@ __global__ void __launch_bounds__(kThreads) k_matvec_q8_0(const uint8_t* __restr
 
 constexpr int kMvFusedRecords = 32;  // activation records a CTA may quantize itself (the plan checks)
 
+__device__ __forceinline__ void mma_u8s8_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0)
+{
+    asm("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// Weight formats of the TMA-fed matvec: bytes of one 256-value super-block
+// as stored on the device, the activation record it reads (quantize.cu,
+// q8k.cuh), and whether 64-row stages land row-major (Q5_K: a 352-byte row
+// pitch spreads the fragment loads over the banks; Q6_K's 448 would not).
+template <uint32_t WT>
+struct MvFmt;
+template <>
+struct MvFmt<kTypeQ5_K> {
+    static constexpr int kSbBytes = kQ5KBytes;    // 176
+    static constexpr int kRecBytes = kQ8KMvBytes; // 288
+    static constexpr bool kRowMajor64 = true;
+};
+template <>
+struct MvFmt<kTypeQ6_K> {
+    static constexpr int kSbBytes = kQ6KPadBytes; // 224: 210 bytes padded at upload
+    static constexpr int kRecBytes = kQ8KQ6Bytes; // 304
+    static constexpr bool kRowMajor64 = false;
+};
+
 // Tile shapes: TR weight rows x 128/TR super-blocks per stage.  Every stage is
-// 22.5 KB of weights; consumer warp w takes rows 16*(w % (TR/16)) .. +15 of
-// the tile and super-block w / (TR/16) of the stage, so all eight warps work
-// on every stage whatever the shape.  The 64-row stage lands in shared memory
-// row-major ([64][352 B], a 2-D box); the 32- and 16-row stages super-block-
-// major ([sb][TR][176 B], a 3-D box), because a row pitch of 704 or 1408
-// bytes would put all rows of a fragment load in the same banks.
-template <int TR, bool FUSED = false>
+// 128 row-super-blocks of weights (22.5 KB of Q5_K, 28 KB of Q6_K); consumer
+// warp w takes rows 16*(w % (TR/16)) .. +15 of the tile and super-block
+// w / (TR/16) of the stage, so all eight warps work on every stage whatever
+// the shape.  A Q5_K 64-row stage lands in shared memory row-major ([64][352
+// B], a 2-D box); the others super-block-major ([sb][TR][sb bytes], a 3-D
+// box), because a row pitch that is a multiple of 128 bytes would put all
+// rows of a fragment load in the same banks.
+template <int TR, bool FUSED, uint32_t WT>
 struct MvShape {
+    using Fmt = MvFmt<WT>;
+    static constexpr bool kRowMajor = TR == 64 && Fmt::kRowMajor64;
     static constexpr int kRowGroups = TR / 16;                      // 16-row MMA groups per tile
     static constexpr int kSbs = kMvStageSuperBlocks / kRowGroups;    // super-blocks per stage
-    static constexpr int kRowBytes = kSbs * kQ5KBytes;              // one row's bytes per stage
-    static constexpr int kRowPitch = TR == 64 ? kRowBytes : kQ5KBytes;    // shared-memory row pitch
-    static constexpr int kSbPitch = TR == 64 ? kQ5KBytes : TR * kQ5KBytes; // shared-memory super-block pitch
-    static constexpr int kWeightBytes = TR * kRowBytes;             // 22528
-    static constexpr int kActPitch = kSbs * kQ8KMvBytes;            // one activation row's records per stage
+    static constexpr int kRowBytes = kSbs * Fmt::kSbBytes;          // one row's bytes per stage
+    static constexpr int kRowPitch = kRowMajor ? kRowBytes : Fmt::kSbBytes;    // shared-memory row pitch
+    static constexpr int kSbPitch = kRowMajor ? Fmt::kSbBytes : TR * Fmt::kSbBytes;  // super-block pitch
+    static constexpr int kWeightBytes = TR * kRowBytes;
+    static constexpr int kActPitch = kSbs * Fmt::kRecBytes;         // one activation row's records per stage
     static constexpr int kActBytes = 8 * kActPitch + 512;           // up to 8 activation rows, skewed
     // two CTAs per SM within 228 KB; with a fused quantize there is no
-    // per-stage activation buffer, so the weight ring gets a fourth stage
-    static constexpr int kStages = FUSED ? 4 : (TR == 16 ? 2 : 3);
+    // per-stage activation buffer, so the Q5_K weight ring gets a fourth stage
+    static constexpr int kStages = FUSED ? (WT == kTypeQ5_K ? 4 : 3) : (TR == 16 ? 2 : 3);
     static_assert(kRowBytes % 16 == 0 && kActPitch % 16 == 0, "bulk copies move 16-byte multiples");
-    static_assert(kWeightBytes == kMvStageWeightBytes, "every shape streams the same stage size");
+    static_assert(kWeightBytes == 16 * kMvStageSuperBlocks * Fmt::kSbBytes, "every shape streams the same stage size");
 };
 
 constexpr int kMvConsumers = 8;
@@ -236,14 +265,15 @@ constexpr int kMvProducerWarp = kMvConsumers;            // TMA / bulk-copy issu
 constexpr int kMvFixupWarp = kMvConsumers + 1;           // cross-CTA sums of shared tiles
 constexpr int kMvThreads = (kMvConsumers + 2) * 32;
 
-template <int TR, bool FUSED>
+template <int TR, bool FUSED, uint32_t WT>
 struct MvSmem {
-    using Sh = MvShape<TR, FUSED>;
-    // activation: per-stage buffers (8 rows of kSbs x 288 bytes at
-    // act_row_off), or with a fused quantize the records of all of the CTA's
-    // stages plus one zero record
-    static constexpr int kActAreaBytes = FUSED ? (kMvFusedRecords + 1) * kQ8KMvBytes : Sh::kStages * Sh::kActBytes;
-    uint8_t weight[Sh::kStages][Sh::kWeightBytes];  // [TR][kSbs x 176] (TR = 64) or [kSbs][TR][176]
+    using Sh = MvShape<TR, FUSED, WT>;
+    static constexpr int kRec = MvFmt<WT>::kRecBytes;
+    // activation: per-stage buffers (8 rows of kSbs records at act_row_off),
+    // or with a fused quantize the records of all of the CTA's stages plus
+    // one zero record
+    static constexpr int kActAreaBytes = FUSED ? (kMvFusedRecords + 1) * kRec : Sh::kStages * Sh::kActBytes;
+    uint8_t weight[Sh::kStages][Sh::kWeightBytes];
     uint8_t act_area[kActAreaBytes];
     // sums of warps with super-block lane >= 1, handed to lane 0, by segment parity
     float red[2][Sh::kSbs - 1][Sh::kRowGroups][16][8];
@@ -255,9 +285,9 @@ struct MvSmem {
 };
 
 struct MvParams {
-    CUtensorMap map;                   // raw weight bytes: 2-D u64 [rows][stride/8], box {kSbs*22, TR} (TR = 64),
-                                       // else 3-D u64 [nsb][rows][22], box {22, TR, kSbs}
-    const uint8_t* act;                // activation records [columns][nsb][kQ8KMvBytes] (not fused)
+    CUtensorMap map;                   // weight bytes: 2-D u64 [rows][stride/8], box {kRowBytes/8, TR} (row-major
+                                       // stages), else 3-D u64 [nsb][rows][sb bytes/8], box {sb bytes/8, TR, kSbs}
+    const uint8_t* act;                // activation records [columns][nsb][record bytes] (not fused)
     const float* x;                    // fp32 activation rows (fused quantize: the kernel's FUSED variant)
     int64_t ldx;
     float* y;
@@ -347,6 +377,126 @@ __device__ __forceinline__ void q5_pair(const uint8_t* wa, const uint8_t* wb, co
     }
 }
 
+// One Q5_K super-block of weight rows a = g, b = g+8 against activation rows
+// g (B fragments from record xg) and 2t, 2t+1 (32-element sums and scale
+// from records x0, x1): the int32 super-block sums of pix_dot_q5_K, then its
+// two fp32 FMAs.  Record layout: q8_K_store_mv (q8k.cuh).
+__device__ __forceinline__ void q5_unit(const uint8_t* wa, const uint8_t* wb, const uint8_t* xg, const uint8_t* x0,
+                                        const uint8_t* x1, uint32_t t, float (&acc)[4], float (&summ)[4])
+{
+    const uint4 ha = *reinterpret_cast<const uint4*>(wa), hb = *reinterpret_cast<const uint4*>(wb);
+    const uint2 qha = *reinterpret_cast<const uint2*>(wa + 16 + 8 * t);
+    const uint2 qhb = *reinterpret_cast<const uint2*>(wb + 16 + 8 * t);
+    uint32_t sca_lo, sca_hi, mna_lo, mna_hi, scb_lo, scb_hi, mnb_lo, mnb_hi;
+    q5_scales(ha, sca_lo, sca_hi, mna_lo, mna_hi);
+    q5_scales(hb, scb_lo, scb_hi, mnb_lo, mnb_hi);
+    const uint8_t* xr = xg + 16 * t;
+    int sumi[4] = {0, 0, 0, 0};
+    q5_pair<0>(wa, wb, xr, t, qha, qhb, sca_lo, scb_lo, sumi);
+    q5_pair<1>(wa, wb, xr, t, qha, qhb, sca_lo, scb_lo, sumi);
+    q5_pair<2>(wa, wb, xr, t, qha, qhb, sca_hi, scb_hi, sumi);
+    q5_pair<3>(wa, wb, xr, t, qha, qhb, sca_hi, scb_hi, sumi);
+    const uint4 s0 = *reinterpret_cast<const uint4*>(x0 + kQKK);
+    const uint4 s1 = *reinterpret_cast<const uint4*>(x1 + kQKK);
+    const int msum[4] = {min_dot(s0, mna_lo, mna_hi), min_dot(s1, mna_lo, mna_hi), min_dot(s0, mnb_lo, mnb_hi),
+                         min_dot(s1, mnb_lo, mnb_hi)};
+    const float dx0 = *reinterpret_cast<const float*>(x0 + kQKK + 16);
+    const float dx1 = *reinterpret_cast<const float*>(x1 + kQKK + 16);
+    const float da = __half2float(__ushort_as_half((unsigned short)(ha.x & 0xffffu)));
+    const float dma = __half2float(__ushort_as_half((unsigned short)(ha.x >> 16)));
+    const float db = __half2float(__ushort_as_half((unsigned short)(hb.x & 0xffffu)));
+    const float dmb = __half2float(__ushort_as_half((unsigned short)(hb.x >> 16)));
+    // pix_dot_q5_K: d = y.d * fp16(x.d); dmin = -y.d * fp16(x.dmin)
+    acc[0] = __fmaf_rn(__fmul_rn(dx0, da), (float)sumi[0], acc[0]);
+    acc[1] = __fmaf_rn(__fmul_rn(dx1, da), (float)sumi[1], acc[1]);
+    acc[2] = __fmaf_rn(__fmul_rn(dx0, db), (float)sumi[2], acc[2]);
+    acc[3] = __fmaf_rn(__fmul_rn(dx1, db), (float)sumi[3], acc[3]);
+    summ[0] = __fmaf_rn(__fmul_rn(-dx0, dma), (float)msum[0], summ[0]);
+    summ[1] = __fmaf_rn(__fmul_rn(-dx1, dma), (float)msum[1], summ[1]);
+    summ[2] = __fmaf_rn(__fmul_rn(-dx0, dmb), (float)msum[2], summ[2]);
+    summ[3] = __fmaf_rn(__fmul_rn(-dx1, dmb), (float)msum[3], summ[3]);
+}
+
+// Sign-extended byte k (0..15) of a 16-byte word group.
+__device__ __forceinline__ int sbyte(const uint4 w, int k)
+{
+    const uint32_t v = k < 4 ? w.x : k < 8 ? w.y : k < 12 ? w.z : w.w;
+    return (int)(int8_t)(uint8_t)(v >> (8 * (k & 3)));
+}
+
+// sum_s sc_s * bsum_s over the 16 sixteen-value groups: bs = 16 int16 sums
+// (two per word), sc = 16 int8 scales (four per word).
+__device__ __forceinline__ int q6_scaled_sums(const uint4 bs0, const uint4 bs1, const uint4 sc)
+{
+    int r = __dp2a_lo((int)bs0.x, (int)sc.x, 0);
+    r = __dp2a_hi((int)bs0.y, (int)sc.x, r);
+    r = __dp2a_lo((int)bs0.z, (int)sc.y, r);
+    r = __dp2a_hi((int)bs0.w, (int)sc.y, r);
+    r = __dp2a_lo((int)bs1.x, (int)sc.z, r);
+    r = __dp2a_hi((int)bs1.y, (int)sc.z, r);
+    r = __dp2a_lo((int)bs1.z, (int)sc.w, r);
+    return __dp2a_hi((int)bs1.w, (int)sc.w, r);
+}
+
+// One Q6_K super-block (padded 224-byte layout: ql[128] qh[64] int8 sc[16]
+// fp16 d at 208) of weight rows a = g, b = g+8 against activation rows g, 2t,
+// 2t+1 (Q8_K records: d at 0, quants at 16, int16 16-element sums at 272).
+// pix_dot_q6_K (src/kernels_quant.cpp:256-337): value index 128j + 32k + b
+// has low bits from ql[64j + 32(k%2) + b] (nibble k/2) and high bits 2k..2k+1
+// of qh[32j + b]; scale sc[8j + 2k + b/16].  Each 16-value group is one
+// u8 x s8 m16n8k16 MMA on the unsigned 6-bit quants; the -32 offset is the
+// reference's separate term 32 * sum_s sc_s * bsum_s.
+__device__ __forceinline__ void q6_unit(const uint8_t* wa, const uint8_t* wb, const uint8_t* xg, const uint8_t* x0,
+                                        const uint8_t* x1, uint32_t t, float (&acc)[4])
+{
+    const uint4 sca = *reinterpret_cast<const uint4*>(wa + 192), scb = *reinterpret_cast<const uint4*>(wb + 192);
+    int sumi[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint32_t qha = *reinterpret_cast<const uint32_t*>(wa + 128 + 32 * j + 16 * h + 4 * t);
+            const uint32_t qhb = *reinterpret_cast<const uint32_t*>(wb + 128 + 32 * j + 16 * h + 4 * t);
+#pragma unroll
+            for (int kk = 0; kk < 2; kk++) {
+                const uint32_t qla = *reinterpret_cast<const uint32_t*>(wa + 64 * j + 32 * kk + 16 * h + 4 * t);
+                const uint32_t qlb = *reinterpret_cast<const uint32_t*>(wb + 64 * j + 32 * kk + 16 * h + 4 * t);
+#pragma unroll
+                for (int khi = 0; khi < 2; khi++) {
+                    const int k = kk + 2 * khi;
+                    const uint32_t ha = k == 0 ? qha << 4 : k == 1 ? qha << 2 : k == 2 ? qha : qha >> 2;
+                    const uint32_t hb = k == 0 ? qhb << 4 : k == 1 ? qhb << 2 : k == 2 ? qhb : qhb >> 2;
+                    const uint32_t aa = ((khi ? qla >> 4 : qla) & 0x0f0f0f0fu) | (ha & 0x30303030u);
+                    const uint32_t ab = ((khi ? qlb >> 4 : qlb) & 0x0f0f0f0fu) | (hb & 0x30303030u);
+                    const uint32_t bx = *reinterpret_cast<const uint32_t*>(xg + 16 + 128 * j + 32 * k + 16 * h + 4 * t);
+                    int d[4];
+                    mma_u8s8_k16(d, aa, ab, bx);
+                    const int si = 8 * j + 2 * k + h;
+                    const int s0 = sbyte(sca, si), s1 = sbyte(scb, si);
+                    sumi[0] += s0 * d[0];
+                    sumi[1] += s0 * d[1];
+                    sumi[2] += s1 * d[2];
+                    sumi[3] += s1 * d[3];
+                }
+            }
+        }
+    }
+    const uint4 b00 = *reinterpret_cast<const uint4*>(x0 + 272), b01 = *reinterpret_cast<const uint4*>(x0 + 288);
+    const uint4 b10 = *reinterpret_cast<const uint4*>(x1 + 272), b11 = *reinterpret_cast<const uint4*>(x1 + 288);
+    sumi[0] -= 32 * q6_scaled_sums(b00, b01, sca);
+    sumi[1] -= 32 * q6_scaled_sums(b10, b11, sca);
+    sumi[2] -= 32 * q6_scaled_sums(b00, b01, scb);
+    sumi[3] -= 32 * q6_scaled_sums(b10, b11, scb);
+    const float dx0 = *reinterpret_cast<const float*>(x0), dx1 = *reinterpret_cast<const float*>(x1);
+    const float da = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(wa + 208)));
+    const float db = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(wb + 208)));
+    // pix_dot_q6_K: d = y.d * fp16(x.d); acc += d * float(sumi - 32 * sum_s sc_s * bsum_s)
+    acc[0] = __fmaf_rn(__fmul_rn(dx0, da), (float)sumi[0], acc[0]);
+    acc[1] = __fmaf_rn(__fmul_rn(dx1, da), (float)sumi[1], acc[1]);
+    acc[2] = __fmaf_rn(__fmul_rn(dx0, db), (float)sumi[2], acc[2]);
+    acc[3] = __fmaf_rn(__fmul_rn(dx1, db), (float)sumi[3], acc[3]);
+}
+
 __device__ __forceinline__ void store_out(const MvParams& p, int64_t r, int64_t col, float v)
 {
     p.y[col * p.ldy + r] = p.bias ? __fadd_rn(v, p.bias[r]) : v;
@@ -358,16 +508,24 @@ __device__ __forceinline__ void store_out(const MvParams& p, int64_t r, int64_t 
 // (rows 2t of four lanes) hit distinct banks: 16 bytes per row pair when the
 // pitch is an odd multiple of 64 bytes, else 144 bytes per row pair plus 64
 // for odd rows.
-template <int TR>
+template <int TR, uint32_t WT>
 __device__ __host__ constexpr uint32_t act_row_off(uint32_t c)
 {
-    return c * MvShape<TR>::kActPitch +
-           (MvShape<TR>::kActPitch % 128 == 0 ? 144 * (c >> 1) + 64 * (c & 1) : 16 * (c >> 1));
+    constexpr uint32_t P = MvShape<TR, false, WT>::kActPitch;
+    return c * P + (P % 128 == 0 ? 144 * (c >> 1) + 64 * (c & 1) : 16 * (c >> 1));
 }
-static_assert(act_row_off<16>(7) + MvShape<16>::kActPitch <= MvShape<16>::kActBytes, "activation rows fit the stage");
-
-static_assert(act_row_off<32>(7) + MvShape<32>::kActPitch <= MvShape<32>::kActBytes, "activation rows fit the stage");
-static_assert(act_row_off<64>(7) + MvShape<64>::kActPitch <= MvShape<64>::kActBytes, "activation rows fit the stage");
+static_assert(act_row_off<16, kTypeQ5_K>(7) + MvShape<16, false, kTypeQ5_K>::kActPitch <= MvShape<16, false, kTypeQ5_K>::kActBytes,
+              "activation rows fit the stage");
+static_assert(act_row_off<32, kTypeQ5_K>(7) + MvShape<32, false, kTypeQ5_K>::kActPitch <= MvShape<32, false, kTypeQ5_K>::kActBytes,
+              "activation rows fit the stage");
+static_assert(act_row_off<64, kTypeQ5_K>(7) + MvShape<64, false, kTypeQ5_K>::kActPitch <= MvShape<64, false, kTypeQ5_K>::kActBytes,
+              "activation rows fit the stage");
+static_assert(act_row_off<16, kTypeQ6_K>(7) + MvShape<16, false, kTypeQ6_K>::kActPitch <= MvShape<16, false, kTypeQ6_K>::kActBytes,
+              "activation rows fit the stage");
+static_assert(act_row_off<32, kTypeQ6_K>(7) + MvShape<32, false, kTypeQ6_K>::kActPitch <= MvShape<32, false, kTypeQ6_K>::kActBytes,
+              "activation rows fit the stage");
+static_assert(act_row_off<64, kTypeQ6_K>(7) + MvShape<64, false, kTypeQ6_K>::kActPitch <= MvShape<64, false, kTypeQ6_K>::kActBytes,
+              "activation rows fit the stage");
 
 __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v)
 {
@@ -423,8 +581,8 @@ __device__ __forceinline__ int64_t contributors(int64_t Tk, int64_t S, int64_t G
 // their partial sums, counts the contribution, and if it is the last one,
 // sums all contributions and stores the tile.  Runs while the consumers go on
 // with the rest of the range.
-template <int TR, bool FUSED>
-__device__ __forceinline__ void mv_fixup_first(const MvParams& p, MvSmem<TR, FUSED>& sm, int64_t S, int64_t G, uint32_t spt,
+template <int TR, bool FUSED, uint32_t WT>
+__device__ __forceinline__ void mv_fixup_first(const MvParams& p, MvSmem<TR, FUSED, WT>& sm, int64_t S, int64_t G, uint32_t spt,
                                                uint32_t T0, uint32_t lane)
 {
     if (!mbar_wait(&sm.part, 0, &sm.abort, p.status, kDevTimeoutFull)) return;
@@ -438,13 +596,14 @@ __device__ __forceinline__ void mv_fixup_first(const MvParams& p, MvSmem<TR, FUS
     if (lane == 0) p.counters[T0] = 0u;  // ready for the next call
 }
 
-template <int TR, bool FUSED>
-__global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_constant__ MvParams p)
+template <int TR, bool FUSED, uint32_t WT>
+__global__ void __launch_bounds__(kMvThreads, 2) k_matvec_kq(const __grid_constant__ MvParams p)
 {
-    using Sh = MvShape<TR, FUSED>;
+    using Sh = MvShape<TR, FUSED, WT>;
     constexpr int kStages = Sh::kStages, kSbs = Sh::kSbs, kRg = Sh::kRowGroups;
+    constexpr int kRec = MvFmt<WT>::kRecBytes;
     extern __shared__ __align__(128) uint8_t mv_smem[];
-    MvSmem<TR, FUSED>& sm = *reinterpret_cast<MvSmem<TR, FUSED>*>(mv_smem);
+    MvSmem<TR, FUSED, WT>& sm = *reinterpret_cast<MvSmem<TR, FUSED, WT>*>(mv_smem);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     griddep_launch_dependents();
     const int64_t G = gridDim.x, c = blockIdx.x, S = p.stages;
@@ -476,7 +635,7 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
     if (warp == kMvFixupWarp) {
         if (first_async) {
             griddep_wait();  // counters and partial sums belong to the kernels before this one
-            mv_fixup_first<TR, FUSED>(p, sm, S, G, spt, T0, lane);
+            mv_fixup_first<TR, FUSED, WT>(p, sm, S, G, spt, T0, lane);
         }
         return;
     }
@@ -493,9 +652,9 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
                 if (i >= (uint32_t)kStages && !mbar_wait(&sm.empty[slot], phase ^ 1u, &sm.abort, p.status, kDevTimeoutEmpty))
                     break;
                 const uint32_t nsb_here = nsb - kSbs * q < (uint32_t)kSbs ? nsb - kSbs * q : (uint32_t)kSbs;
-                const uint32_t act_tx = fused ? 0u : columns * nsb_here * kQ8KMvBytes;
+                const uint32_t act_tx = fused ? 0u : columns * nsb_here * kRec;
                 mbar_expect_tx(&sm.full[slot], Sh::kWeightBytes + act_tx);
-                if (TR == 64)
+                if (Sh::kRowMajor)
                     tma_load_2d(sm.weight[slot], &p.map, &sm.full[slot], (int32_t)(q * (Sh::kRowBytes / 8)),
                                 (int32_t)(p.row_first + (int64_t)T * TR));
                 else
@@ -510,14 +669,14 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
                     for (uint32_t k = 0; k <= i; k++) {
                         const uint32_t nk = nsb - kSbs * qj < (uint32_t)kSbs ? nsb - kSbs * qj : (uint32_t)kSbs;
                         for (uint32_t col = 0; col < columns; col++)
-                            bulk_load(sm.act(k) + act_row_off<TR>(col), p.act + ((int64_t)col * nsb + kSbs * qj) * kQ8KMvBytes,
-                                      nk * kQ8KMvBytes, &sm.full[k]);
+                            bulk_load(sm.act(k) + act_row_off<TR, WT>(col), p.act + ((int64_t)col * nsb + kSbs * qj) * kRec,
+                                      nk * kRec, &sm.full[k]);
                         if (++qj == spt) qj = 0;
                     }
                 } else if (i >= pre) {
                     for (uint32_t col = 0; col < columns; col++)
-                        bulk_load(sm.act(slot) + act_row_off<TR>(col), p.act + ((int64_t)col * nsb + kSbs * q) * kQ8KMvBytes,
-                                  nsb_here * kQ8KMvBytes, &sm.full[slot]);
+                        bulk_load(sm.act(slot) + act_row_off<TR, WT>(col), p.act + ((int64_t)col * nsb + kSbs * q) * kRec,
+                                  nsb_here * kRec, &sm.full[slot]);
                 }
                 issued = i + 1;
                 if (++q == spt) { q = 0; T++; }
@@ -540,17 +699,17 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
     // Activation, two ways.  Copied per stage: row c of a stage's buffer at
     // act_row_off(c); rows >= columns are never copied, so zero them once and
     // their fragments, sums and scales are zero.  Fused: the records of all
-    // of this CTA's stages, [stage][super-block lane][row] x kQ8KMvBytes, in
+    // of this CTA's stages, [stage][super-block lane][row] x kRec bytes, in
     // the same memory, quantized here from x, plus one zero record for rows
     // >= columns.
     uint8_t* const act_flat = sm.act_area;
-    uint8_t* const zero_rec = act_flat + kMvFusedRecords * kQ8KMvBytes;
+    uint8_t* const zero_rec = act_flat + kMvFusedRecords * kRec;
     if (!fused) {
         for (uint32_t k = 0; k < (uint32_t)kStages; k++)
             for (uint32_t c8 = columns; c8 < 8; c8++)
                 for (uint32_t o = threadIdx.x * 16; o < (uint32_t)Sh::kActPitch; o += 32 * kMvConsumers * 16)
-                    *reinterpret_cast<uint4*>(sm.act(k) + act_row_off<TR>(c8) + o) = make_uint4(0, 0, 0, 0);
-    } else if (threadIdx.x < kQ8KMvBytes / 16) {
+                    *reinterpret_cast<uint4*>(sm.act(k) + act_row_off<TR, WT>(c8) + o) = make_uint4(0, 0, 0, 0);
+    } else if (threadIdx.x < kRec / 16) {
         reinterpret_cast<uint4*>(zero_rec)[threadIdx.x] = make_uint4(0, 0, 0, 0);
     }
     // outputs, partials, counters and x belong to the kernels before this one
@@ -574,13 +733,16 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
         for (int k = 0; k < kPerWarp; k++) {
             if (sbk[k] >= nsb) continue;  // warp-uniform; past the end of K the record is never read
             const Q8KWarp r = q8_K_warp_vals(v[k], lane);
-            q8_K_store_mv(act_flat + (warp + kMvConsumers * k) * kQ8KMvBytes, r, lane);
+            if constexpr (WT == kTypeQ5_K)
+                q8_K_store_mv(act_flat + (warp + kMvConsumers * k) * kRec, r, lane);
+            else
+                q8_K_store_q6(act_flat + (warp + kMvConsumers * k) * kRec, r, lane);
         }
     }
     named_bar_sync(7, 32 * kMvConsumers);
-    const uint32_t xg_off = act_row_off<TR>(g) + sbl * kQ8KMvBytes + 16 * t;        // B fragments, activation row g
-    const uint32_t x0_off = act_row_off<TR>(2 * t) + sbl * kQ8KMvBytes + kQKK;      // sums + d, activation row 2t
-    const uint32_t x1_off = act_row_off<TR>(2 * t + 1) + sbl * kQ8KMvBytes + kQKK;  // activation row 2t+1
+    const uint32_t xg_off = act_row_off<TR, WT>(g) + sbl * kRec;          // record of activation row g
+    const uint32_t x0_off = act_row_off<TR, WT>(2 * t) + sbl * kRec;      // activation row 2t
+    const uint32_t x1_off = act_row_off<TR, WT>(2 * t + 1) + sbl * kRec;  // activation row 2t+1
     float acc[4] = {0.f, 0.f, 0.f, 0.f}, summ[4] = {0.f, 0.f, 0.f, 0.f};
     bool ok = true;
     uint32_t seg = 0, slot = 0, phase = 0, T = T0, q = q0;
@@ -591,47 +753,21 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
         if (ok && sb < nsb) {
             const uint8_t* wa = sm.weight[slot] + row_off;
             const uint8_t* wb = wa + 8 * Sh::kRowPitch;
-            const uint8_t *xr, *x0, *x1;  // B fragments of row g; sums + d of rows 2t, 2t+1
+            const uint8_t *xg, *x0, *x1;  // records of activation rows g, 2t, 2t+1
             if (!fused) {
-                xr = sm.act(slot) + xg_off;
+                xg = sm.act(slot) + xg_off;
                 x0 = sm.act(slot) + x0_off;
                 x1 = sm.act(slot) + x1_off;
             } else {
-                const uint8_t* rec = act_flat + (i * kSbs + sbl) * columns * kQ8KMvBytes;
-                xr = (g < columns ? rec + g * kQ8KMvBytes : zero_rec) + 16 * t;
-                x0 = (vc0 ? rec + 2 * t * kQ8KMvBytes : zero_rec) + kQKK;
-                x1 = (vc1 ? rec + (2 * t + 1) * kQ8KMvBytes : zero_rec) + kQKK;
+                const uint8_t* rec = act_flat + (i * kSbs + sbl) * columns * kRec;
+                xg = g < columns ? rec + g * kRec : zero_rec;
+                x0 = vc0 ? rec + 2 * t * kRec : zero_rec;
+                x1 = vc1 ? rec + (2 * t + 1) * kRec : zero_rec;
             }
-            const uint4 ha = *reinterpret_cast<const uint4*>(wa), hb = *reinterpret_cast<const uint4*>(wb);
-            const uint2 qha = *reinterpret_cast<const uint2*>(wa + 16 + 8 * t);
-            const uint2 qhb = *reinterpret_cast<const uint2*>(wb + 16 + 8 * t);
-            uint32_t sca_lo, sca_hi, mna_lo, mna_hi, scb_lo, scb_hi, mnb_lo, mnb_hi;
-            q5_scales(ha, sca_lo, sca_hi, mna_lo, mna_hi);
-            q5_scales(hb, scb_lo, scb_hi, mnb_lo, mnb_hi);
-            int sumi[4] = {0, 0, 0, 0};
-            q5_pair<0>(wa, wb, xr, t, qha, qhb, sca_lo, scb_lo, sumi);
-            q5_pair<1>(wa, wb, xr, t, qha, qhb, sca_lo, scb_lo, sumi);
-            q5_pair<2>(wa, wb, xr, t, qha, qhb, sca_hi, scb_hi, sumi);
-            q5_pair<3>(wa, wb, xr, t, qha, qhb, sca_hi, scb_hi, sumi);
-            const uint4 s0 = *reinterpret_cast<const uint4*>(x0);
-            const uint4 s1 = *reinterpret_cast<const uint4*>(x1);
-            const int msum[4] = {min_dot(s0, mna_lo, mna_hi), min_dot(s1, mna_lo, mna_hi), min_dot(s0, mnb_lo, mnb_hi),
-                                 min_dot(s1, mnb_lo, mnb_hi)};
-            const float dx0 = *reinterpret_cast<const float*>(x0 + 16);
-            const float dx1 = *reinterpret_cast<const float*>(x1 + 16);
-            const float da = __half2float(__ushort_as_half((unsigned short)(ha.x & 0xffffu)));
-            const float dma = __half2float(__ushort_as_half((unsigned short)(ha.x >> 16)));
-            const float db = __half2float(__ushort_as_half((unsigned short)(hb.x & 0xffffu)));
-            const float dmb = __half2float(__ushort_as_half((unsigned short)(hb.x >> 16)));
-            // pix_dot_q5_K: d = y.d * fp16(x.d); dmin = -y.d * fp16(x.dmin)
-            acc[0] = __fmaf_rn(__fmul_rn(dx0, da), (float)sumi[0], acc[0]);
-            acc[1] = __fmaf_rn(__fmul_rn(dx1, da), (float)sumi[1], acc[1]);
-            acc[2] = __fmaf_rn(__fmul_rn(dx0, db), (float)sumi[2], acc[2]);
-            acc[3] = __fmaf_rn(__fmul_rn(dx1, db), (float)sumi[3], acc[3]);
-            summ[0] = __fmaf_rn(__fmul_rn(-dx0, dma), (float)msum[0], summ[0]);
-            summ[1] = __fmaf_rn(__fmul_rn(-dx1, dma), (float)msum[1], summ[1]);
-            summ[2] = __fmaf_rn(__fmul_rn(-dx0, dmb), (float)msum[2], summ[2]);
-            summ[3] = __fmaf_rn(__fmul_rn(-dx1, dmb), (float)msum[3], summ[3]);
+            if constexpr (WT == kTypeQ5_K)
+                q5_unit(wa, wb, xg, x0, x1, t, acc, summ);
+            else
+                q6_unit(wa, wb, xg, x0, x1, t, acc);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.empty[slot]);
@@ -704,8 +840,8 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_q5_K(const __grid_cons
     if (threadIdx.x == 0) p.counters[T1] = 0u;  // ready for the next call
 }
 
-template <int TR, bool FUSED>
-cudaError_t launch_q5(const MatvecPlan& plan, const CUtensorMap* map, int64_t row_first, const void* act, const float* x,
+template <int TR, bool FUSED, uint32_t WT>
+cudaError_t launch_kq(const MatvecPlan& plan, const CUtensorMap* map, int64_t row_first, const void* act, const float* x,
                       int64_t ldx, float* y, int64_t ldy, const float* bias, float* partial, uint32_t* counters,
                       uint32_t* status, cudaStream_t s)
 {
@@ -713,10 +849,10 @@ cudaError_t launch_q5(const MatvecPlan& plan, const CUtensorMap* map, int64_t ro
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 16 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(k_matvec_q5_K<TR, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)sizeof(MvSmem<TR, FUSED>));
+        cudaError_t e = cudaFuncSetAttribute(k_matvec_kq<TR, FUSED, WT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)sizeof(MvSmem<TR, FUSED, WT>));
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(k_matvec_q5_K<TR, FUSED>, cudaFuncAttributePreferredSharedMemoryCarveout,
+            e = cudaFuncSetAttribute(k_matvec_kq<TR, FUSED, WT>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                      (int)cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
@@ -738,7 +874,20 @@ cudaError_t launch_q5(const MatvecPlan& plan, const CUtensorMap* map, int64_t ro
     prm.nsb = (int32_t)(plan.inner / kQKK);
     prm.spt = (int32_t)plan.spt;
     prm.columns = (int32_t)plan.columns;
-    return launch_pdl(k_matvec_q5_K<TR, FUSED>, dim3(plan.grid), dim3(kMvThreads), sizeof(MvSmem<TR, FUSED>), s, prm);
+    return launch_pdl(k_matvec_kq<TR, FUSED, WT>, dim3(plan.grid), dim3(kMvThreads), sizeof(MvSmem<TR, FUSED, WT>), s, prm);
+}
+
+// The kernel instance for a plan: weight format x fused quantize.
+template <int TR>
+cudaError_t launch_kq3(const MatvecPlan& plan, const CUtensorMap* map, int64_t row_first, const void* act, const float* x,
+                       int64_t ldx, float* y, int64_t ldy, const float* bias, float* partial, uint32_t* counters,
+                       uint32_t* status, cudaStream_t s)
+{
+    if (plan.type == kTypeQ5_K)
+        return plan.fused ? launch_kq<TR, true, kTypeQ5_K>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s)
+                          : launch_kq<TR, false, kTypeQ5_K>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
+    return plan.fused ? launch_kq<TR, true, kTypeQ6_K>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s)
+                      : launch_kq<TR, false, kTypeQ6_K>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
 }
 
 }  // namespace
@@ -752,8 +901,10 @@ MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t colum
     p.rows = rows;
     p.inner = inner;
     p.columns = columns;
-    if (type == kTypeQ5_K) {
+    if (type == kTypeQ5_K || type == kTypeQ6_K) {
         const int64_t nsb = inner / kQKK;
+        const int64_t sb_bytes = type == kTypeQ5_K ? kQ5KBytes : kQ6KPadBytes;
+        const int64_t rec_bytes = type == kTypeQ5_K ? kQ8KMvBytes : kQ8KQ6Bytes;
         const int64_t slots = (int64_t)num_sms * 2;  // two CTAs per SM
         // Whole tiles per CTA (no cross-CTA sums) when some tile height gives
         // a tile count that fills the grid well, or when the matrix is small
@@ -763,7 +914,7 @@ MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t colum
         bool whole = false;
         for (int tr : {64, 32, 16}) {
             const int64_t tiles = (rows + tr - 1) / tr;
-            const int64_t tile_bytes = (int64_t)tr * nsb * kQ5KBytes;
+            const int64_t tile_bytes = (int64_t)tr * nsb * sb_bytes;
             if (tiles <= slots && (tiles * 20 >= slots * 19 || (tiles * 4 >= slots * 3 && tile_bytes <= 64 * 1024))) {
                 p.tile_rows = tr;
                 whole = true;
@@ -779,7 +930,7 @@ MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t colum
         // (at most kMvFusedRecords), no separate quantize kernel
         const int64_t max_stages = (p.stages + p.grid - 1) / p.grid;
         p.fused = fuse_quantize && columns * max_stages * sbs <= kMvFusedRecords;
-        p.act_bytes = p.fused ? 0 : (size_t)(columns * nsb * kQ8KMvBytes);
+        p.act_bytes = p.fused ? 0 : (size_t)(columns * nsb * rec_bytes);
         p.partial_bytes = whole ? 0 : (size_t)p.grid * 2 * columns * p.tile_rows * sizeof(float);
         p.counter_bytes = (size_t)p.tiles * sizeof(uint32_t);
     } else {
@@ -807,7 +958,7 @@ MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t colum
     // kernel to clear them) finds zeros there whatever the previous call was.
     if (p.fused && p.counter_bytes > kMvCounterRegion) {
         p.fused = false;
-        p.act_bytes = (size_t)(columns * (inner / kQKK) * kQ8KMvBytes);
+        p.act_bytes = (size_t)(columns * (inner / kQKK) * (type == kTypeQ5_K ? kQ8KMvBytes : kQ8KQ6Bytes));
     }
     p.off_counters = 0;
     p.off_act = (p.counter_bytes > kMvCounterRegion ? p.counter_bytes + 255 : kMvCounterRegion) / 256 * 256;
@@ -821,20 +972,14 @@ cudaError_t launch_matvec(const MatvecPlan& plan, const CUtensorMap* maps, int64
                           const float* bias, float* partial, uint32_t* counters, uint32_t* status, cudaStream_t s)
 {
     if (plan.columns < 1 || plan.columns > 8 || plan.grid < 1) return cudaErrorInvalidValue;
-    if (plan.type == kTypeQ5_K) {
+    if (plan.type == kTypeQ5_K || plan.type == kTypeQ6_K) {
         if (!maps || !counters || (plan.partial_bytes && !partial)) return cudaErrorInvalidValue;
         if (plan.fused ? !x : !act) return cudaErrorInvalidValue;
         const CUtensorMap* map = maps + matvec_map_index(plan.tile_rows);
         switch (plan.tile_rows) {
-        case 64:
-            return plan.fused ? launch_q5<64, true>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s)
-                              : launch_q5<64, false>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
-        case 32:
-            return plan.fused ? launch_q5<32, true>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s)
-                              : launch_q5<32, false>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
-        case 16:
-            return plan.fused ? launch_q5<16, true>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s)
-                              : launch_q5<16, false>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
+        case 64: return launch_kq3<64>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
+        case 32: return launch_kq3<32>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
+        case 16: return launch_kq3<16>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
         default: return cudaErrorInvalidValue;
         }
     }

@@ -81,7 +81,8 @@ extern "C" int pxq_matvec_noalloc(pxq_weight* w, size_t row_first, size_t row_co
     if (row_first > (size_t)rows || row_count > (size_t)rows - row_first)
         return noalloc_fail(PXQ_ERR_INVALID, "row range outside the weight");
     if (ldy < row_count && columns > 1) return noalloc_fail(PXQ_ERR_INVALID, "ldy < row_count");
-    if (type != pxq::kTypeQ8_0 && type != pxq::kTypeQ5_K) return noalloc_fail(PXQ_ERR_UNSUPPORTED, "weight type not supported");
+    if (type != pxq::kTypeQ8_0 && type != pxq::kTypeQ5_K && type != pxq::kTypeQ6_K)
+        return noalloc_fail(PXQ_ERR_UNSUPPORTED, "weight type not supported");
     // the static array holds the quantized activation rows and the matvec's
     // partial sums and counters
     int cur_dev = -1;

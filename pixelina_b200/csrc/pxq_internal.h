@@ -14,6 +14,7 @@ constexpr int kQ8_0Bytes = 34;    // {fp16 d; int8 qs[32]}
 constexpr int kQ8KBytes = 292;    // {f32 d; int8 qs[256]; int16 bsums[16]}
 constexpr int kQ5KBytes = 176;    // {fp16 d, dmin; u8 scales[12]; u8 qh[32]; u8 qs[128]}
 constexpr int kQ6KBytes = 210;    // {u8 ql[128]; u8 qh[64]; i8 scales[16]; fp16 d}
+constexpr int kQ6KPadBytes = 224; // the same, padded to 16-byte multiples on the device (TMA rows)
 constexpr uint32_t kTypeQ8_0 = 8;
 constexpr uint32_t kTypeQ5_K = 13;
 constexpr uint32_t kTypeQ6_K = 14;
@@ -32,6 +33,9 @@ cudaError_t launch_quantize_q8_0_operand(const float* x, __half* xq, __half* dx1
                                          int64_t ldd, cudaStream_t s);
 cudaError_t launch_quantize_q8_K_operand(const float* x, __half* xq, float* dxT, __half* amin, int64_t rows, int64_t inner,
                                          int64_t ldx, int64_t ldd, cudaStream_t s);
+
+// Q6_K weight rows padded for the device: 210-byte super-blocks -> 224.
+cudaError_t launch_pad_q6_K(const void* src, void* dst, int64_t superblocks, cudaStream_t s);
 
 // ---- repack.cu -------------------------------------------------------------
 // One-time weight repack into the GEMM operand layout (bit-exact unpack).
@@ -68,6 +72,7 @@ constexpr int kMvStageSuperBlocks = 8;                    // tile rows / 16 x su
 constexpr int kMvStageWeightBytes = 16 * kMvStageSuperBlocks * kQ5KBytes;  // 22528, any tile shape
 constexpr int kMvTileShapes = 3;                         // 64 x 2, 32 x 4 and 16 x 8 super-blocks
 constexpr int kQ8KMvBytes = 288;
+constexpr int kQ8KQ6Bytes = 304;                          // Q8_K record for Q6_K weights: {f32 d; pad; i8 qs[256] at 16; i16 bsums[16] at 272}
 constexpr size_t kMvCounterRegion = 16 << 10;            // scratch bytes reserved for counters  // {i8 quants [4 pairs][4 lanes][2][8]; i16 32-element sums[8]; f32 d; pad}
 
 struct MatvecPlan {

@@ -100,4 +100,23 @@ __device__ __forceinline__ void q8_K_store_mv(uint8_t* out, const Q8KWarp& r, ui
     if (lane == 0) *reinterpret_cast<float*>(out + kQKK + 16) = r.d;
 }
 
+// This warp's block as a Q6_K matvec record (kQ8KQ6Bytes at `out`): d (fp32)
+// at byte 0, the quants in their natural order at byte 16 (lane l's eight at
+// 16 + 8l), the sixteen 16-element sums (int16) at byte 272.
+__device__ __forceinline__ void q8_K_store_q6(uint8_t* out, const Q8KWarp& r, uint32_t lane)
+{
+    uint32_t lo = 0, hi = 0;
+    int sum8 = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) lo |= (uint32_t)(uint8_t)r.q[j] << (8 * j);
+#pragma unroll
+    for (int j = 0; j < 4; j++) hi |= (uint32_t)(uint8_t)r.q[4 + j] << (8 * j);
+#pragma unroll
+    for (int j = 0; j < 8; j++) sum8 += r.q[j];
+    *reinterpret_cast<uint2*>(out + 16 + 8 * lane) = make_uint2(lo, hi);
+    const int s16 = sum8 + __shfl_xor_sync(0xffffffffu, sum8, 1);  // 16-element group = lane pair
+    if ((lane & 1u) == 0) *reinterpret_cast<int16_t*>(out + 16 + kQKK + lane) = (int16_t)s16;
+    if (lane == 0) *reinterpret_cast<float*>(out) = r.d;
+}
+
 }  // namespace pxq

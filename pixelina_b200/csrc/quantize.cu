@@ -161,8 +161,10 @@ __global__ void k_quantize_q8_K_blocks(const float* __restrict__ x, uint8_t* __r
     }
 }
 
-// Matvec operand: one record of kQ8KMvBytes per (row, super-block)
-// (layout: q8_K_store_mv, q8k.cuh).
+// Matvec operand: one record per (row, super-block), kQ8KMvBytes for Q5_K
+// weights (layout: q8_K_store_mv, q8k.cuh), kQ8KQ6Bytes for Q6_K weights
+// (q8_K_store_q6).
+template <bool Q6>
 __global__ void k_quantize_q8_K_mv(const float* x, uint8_t* __restrict__ y, int64_t rows, int64_t inner,
                                    int64_t ldx, uint32_t* __restrict__ zero, int64_t nzero)
 {
@@ -174,7 +176,10 @@ __global__ void k_quantize_q8_K_mv(const float* x, uint8_t* __restrict__ y, int6
     for (int64_t w = (((int64_t)blockIdx.x * blockDim.x) >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
         const int64_t row = w / nsb, sb = w % nsb;
         const Q8KWarp r = q8_K_warp(x + row * ldx + sb * kQKK, lane);
-        q8_K_store_mv(y + w * kQ8KMvBytes, r, lane);
+        if (Q6)
+            q8_K_store_q6(y + w * kQ8KQ6Bytes, r, lane);
+        else
+            q8_K_store_mv(y + w * kQ8KMvBytes, r, lane);
     }
 }
 
@@ -218,7 +223,26 @@ int grid_for(int64_t work_items, int threads)
     return (int)blocks;
 }
 
+// Q6_K rows for the device: every 210-byte super-block padded to 224 bytes
+// (16-byte multiples, as TMA rows need); bytes 210..223 are zero.
+__global__ void k_pad_q6_K(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst, int64_t superblocks)
+{
+    const int64_t total = superblocks * (kQ6KPadBytes / 2);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t sb = i / (kQ6KPadBytes / 2), e = i % (kQ6KPadBytes / 2);
+        dst[i] = e < kQ6KBytes / 2 ? src[sb * (kQ6KBytes / 2) + e] : (uint16_t)0;
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_pad_q6_K(const void* src, void* dst, int64_t superblocks, cudaStream_t s)
+{
+    const int threads = 256;
+    k_pad_q6_K<<<grid_for(superblocks * (kQ6KPadBytes / 2), threads), threads, 0, s>>>(static_cast<const uint16_t*>(src),
+                                                                                     static_cast<uint16_t*>(dst), superblocks);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_quantize_q8_0_blocks(const float* x, void* y, int64_t rows, int64_t inner, int64_t ldx, cudaStream_t s)
 {
@@ -237,20 +261,22 @@ cudaError_t launch_matvec_quantize(const MatvecPlan& plan, const float* x, int64
     if (plan.type == kTypeQ8_0)
         return launch_pdl(k_quantize_q8_0_blocks, dim3(grid_for(plan.columns * plan.inner / 4, threads)), dim3(threads), 0, s,
                           x, out, plan.columns, plan.inner, ldx, counters, nzero);
-    if (plan.type == kTypeQ5_K) {
+    if (plan.type == kTypeQ5_K || plan.type == kTypeQ6_K) {
+        const bool q6 = plan.type == kTypeQ6_K;
+        auto kern = q6 ? k_quantize_q8_K_mv<true> : k_quantize_q8_K_mv<false>;
         // same shared-memory carveout as the matvec, so that the SMs need no
         // reconfiguration between the two kernels
-        static bool carveout_set[16] = {};
+        static bool carveout_set[2][16] = {};
         int dev = 0;
         cudaGetDevice(&dev);
-        if (dev >= 0 && dev < 16 && !carveout_set[dev]) {
-            cudaError_t e = cudaFuncSetAttribute(k_quantize_q8_K_mv, cudaFuncAttributePreferredSharedMemoryCarveout,
+        if (dev >= 0 && dev < 16 && !carveout_set[q6][dev]) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                                                  (int)cudaSharedmemCarveoutMaxShared);
             if (e != cudaSuccess) return e;
-            carveout_set[dev] = true;
+            carveout_set[q6][dev] = true;
         }
-        return launch_pdl(k_quantize_q8_K_mv, dim3(grid_for(plan.columns * (plan.inner / kQKK) * 32, threads)), dim3(threads), 0,
-                          s, x, out, plan.columns, plan.inner, ldx, counters, nzero);
+        return launch_pdl(kern, dim3(grid_for(plan.columns * (plan.inner / kQKK) * 32, threads)), dim3(threads), 0, s, x, out,
+                          plan.columns, plan.inner, ldx, counters, nzero);
     }
     return cudaErrorInvalidValue;
 }

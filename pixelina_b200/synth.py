@@ -113,6 +113,18 @@ def random_q5_K(rows: int, inner: int, rng: np.random.Generator, d_scale: float 
     return _pack_q5_K(d16, dmin16, sc, mn, q).reshape(rows, inner // 256 * 176)
 
 
+def random_q6_K(rows: int, inner: int, rng: np.random.Generator, d_scale: float = 0.02 / 32 / 64) -> np.ndarray:
+    """Structurally valid random Q6_K rows: {u8 ql[128]; u8 qh[64]; i8 scales[16]; fp16 d}
+    per 256 values (src/kernels_quant.cpp:25-29), fields drawn independently."""
+    assert inner % 256 == 0
+    S = rows * inner // 256
+    ql = rng.integers(0, 256, size=(S, 128), dtype=np.uint8)
+    qh = rng.integers(0, 256, size=(S, 64), dtype=np.uint8)
+    sc = rng.integers(-128, 128, size=(S, 16)).astype(np.int8).view(np.uint8)
+    d16 = (rng.uniform(0.5, 1.5, S) * d_scale).astype(np.float16).view(np.uint8).reshape(S, 2)
+    return np.concatenate([ql, qh, sc, d16], axis=1).reshape(rows, inner // 256 * 210)
+
+
 def q8_0_weights(rows: int, inner: int, seed: int, std: float = 0.02) -> np.ndarray:
     rng = np.random.default_rng(seed)
     return encode_q8_0(rng.normal(0.0, std, size=(rows, inner)).astype(np.float32))
@@ -133,4 +145,6 @@ def weights_for(wtype: int, rows: int, inner: int, seed: int) -> np.ndarray:
         return q8_0_weights(rows, inner, seed)
     if wtype == TYPE_Q5_K:
         return q5_K_weights(rows, inner, seed)
+    if wtype == TYPE_Q6_K:
+        return random_q6_K(rows, inner, np.random.default_rng(seed))
     raise ValueError(f"no synthetic encoder for type {wtype}")

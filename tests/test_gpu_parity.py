@@ -105,7 +105,7 @@ def test_matmul_golden(pxq, golden, name, wtype, path):
     assert max_abs_rel(y, golden[f"mm_{name}"]) <= TOL
 
 
-@pytest.mark.parametrize("wtype", [Q8_0, Q5_K])
+@pytest.mark.parametrize("wtype", [Q8_0, Q5_K, Q6_K])
 @pytest.mark.parametrize("columns", [1, 2, 3, 4, 5, 8])
 def test_matvec_vs_oracle(pxq, oracle, wtype, columns):
     rows, inner = 100, 1024
@@ -119,20 +119,40 @@ def test_matvec_vs_oracle(pxq, oracle, wtype, columns):
     assert ok and max_abs_rel(y, ref) <= TOL
 
 
+@pytest.mark.parametrize("wtype", [Q5_K, Q6_K])
 @pytest.mark.parametrize("rows", [18944, 9472, 4608, 3584, 200])
 @pytest.mark.parametrize("inner,columns", [(256, 1), (768, 3), (3584, 8)])
-def test_matvec_q5_K_tile_shapes(pxq, oracle, rows, inner, columns):
-    """Every Q5_K matvec schedule: on a 148-SM B200 these row counts select
+def test_matvec_kquant_tile_shapes(pxq, oracle, wtype, rows, inner, columns):
+    """Every K-quant matvec schedule: on a 148-SM B200 these row counts select
     whole 64-, 32- and 16-row tiles per CTA and the stream-K split; odd
     super-block counts leave the last stage partly empty."""
-    w = synth.random_q5_K(rows, inner, np.random.default_rng(rows + inner))
+    rng = np.random.default_rng(rows + inner)
+    w = synth.random_q5_K(rows, inner, rng) if wtype == Q5_K else synth.random_q6_K(rows, inner, rng)
     x = synth.activations(columns, inner, seed=columns)
-    W = pxq.Weight(w, Q5_K, inner, rows)
+    W = pxq.Weight(w, wtype, inner, rows)
     y = pxq.matmul(W, cuda(x), path="matvec").cpu().numpy()
     pxq.synchronize()
     W.release()
-    ok, ref = oracle.quant_matmul(w, Q5_K, x, rows)
+    ok, ref = oracle.quant_matmul(w, wtype, x, rows)
     assert ok and max_abs_rel(y, ref) <= TOL
+
+
+def test_q6_K_golden_and_limits(pxq, golden):
+    """Q6_K weights: the matvec against the reference build's outputs; larger
+    activation batches are reported as not handled (the reference's `false`)."""
+    w = golden["w_q6_K"]
+    rows, inner = w.shape[0], golden["mm_x"].shape[1]
+    W = pxq.Weight(w, Q6_K, inner, rows)
+    for path in ("matvec", "auto"):
+        y = pxq.matmul(W, cuda(golden["mm_x"]), path=path).cpu().numpy()
+        pxq.synchronize()
+        assert max_abs_rel(y, golden["mm_q6_K"]) <= TOL
+    x9 = np.concatenate([golden["mm_x"], golden["mm_x"][:2]])
+    for path in ("gemm", "auto"):
+        with pytest.raises(pxq.PxqError) as err:
+            pxq.matmul(W, cuda(x9), path=path)
+        assert err.value.code == pxq.ERR_UNSUPPORTED
+    W.release()
 
 
 def test_matvec_scratch_reuse_across_schedules(pxq, oracle):
@@ -217,8 +237,7 @@ def test_gemm_block_dots_exact(pxq, oracle, wtype):
                 assert np.array_equal(items[:, 4].astype(np.int64), m.astype(np.int64))
 
 
-@pytest.mark.parametrize("path", ["matvec", "gemm"])
-@pytest.mark.parametrize("wtype", [Q8_0, Q5_K])
+@pytest.mark.parametrize("path,wtype", [("matvec", Q8_0), ("matvec", Q5_K), ("matvec", Q6_K), ("gemm", Q8_0), ("gemm", Q5_K)])
 def test_row_views_ldy_bias(pxq, oracle, path, wtype):
     """tensor_linear_rows-style row ranges, strided output, fused bias."""
     import torch
@@ -248,8 +267,11 @@ def test_host_drop_in_matches_reference_contract(pxq, oracle, golden):
         w = golden[f"w_{name}"]
         handled, y = pxq.quant_matmul(w, wtype, golden["mm_x"], w.shape[0])
         assert handled and max_abs_rel(y, golden[f"mm_{name}"]) <= TOL
-    handled, _ = pxq.quant_matmul(golden["w_q6_K"], Q6_K, golden["mm_x"], 24)
-    assert not handled  # not handled yet: the caller's fallback path runs, as for any `false`
+    handled, y = pxq.quant_matmul(golden["w_q6_K"], Q6_K, golden["mm_x"], 24)
+    assert handled and max_abs_rel(y, golden["mm_q6_K"]) <= TOL  # Q6_K: the matvec, up to 8 activation rows
+    x9 = np.concatenate([golden["mm_x"], golden["mm_x"][:2]])
+    handled, _ = pxq.quant_matmul(golden["w_q6_K"], Q6_K, x9, 24)
+    assert not handled  # 9 rows of Q6_K: not handled, the caller's fallback runs, as for any `false`
     # large-M through the host entry point
     w = synth.q8_0_weights(256, 1024, seed=5)
     x = synth.activations(300, 1024, seed=6)
