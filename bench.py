@@ -40,7 +40,7 @@ FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 L2_FLUSH_BYTES = 256 << 20
 
-Q8_0, Q5_K = 8, 13
+Q8_0, Q5_K, Q6_K = 8, 13, 14
 
 GEMM_WORKLOADS = {
     "q5k_gemm": dict(wtype=Q5_K, M=4096, N=10240, K=3840, name="Q5_K GEMM (BASELINE configs[1])"),
@@ -217,6 +217,17 @@ def gpu_random_q5_K(rows: int, inner: int, gen):
     d = torch.rand((rows, nsb, 2), device="cuda", generator=gen) * 4e-5 + 2e-5
     raw[:, :, 0:4] = d.to(torch.float16).view(torch.uint8).view(rows, nsb, 4)
     return raw.view(rows, nsb * 176)
+
+
+def gpu_random_q6_K(rows: int, inner: int, gen):
+    """Random valid Q6_K rows on the GPU: random quants and int8 scales, small fp16 d."""
+    import torch
+
+    nsb = inner // 256
+    raw = torch.randint(0, 256, (rows, nsb, 210), dtype=torch.uint8, device="cuda", generator=gen)
+    d = torch.rand((rows, nsb, 1), device="cuda", generator=gen) * 1e-5 + 5e-6
+    raw[:, :, 208:210] = d.to(torch.float16).view(torch.uint8).view(rows, nsb, 2)
+    return raw.view(rows, nsb * 210)
 
 
 # ------------------------------------------------------------------ our arm ---
@@ -540,7 +551,8 @@ def run_decode(args, dist: Dist):
 
 def run_decode_shapes(args, dist: Dist):
     """Per-shape view of BASELINE configs[3]: each decode matrix (QKV, out,
-    gate/up, down) at M = 1 and 8, one call = activation quantize + matvec.
+    gate/up, down) at M = 1 and 8, one call = activation quantize + matvec;
+    also gate/up and down as Q6_K (GGUF mixes Q6_K tensors into Q5_K models).
     Each shape cycles through enough distinct copies of its weight to exceed
     the 126 MB L2, replayed as a CUDA graph, so the rate is HBM, not L2."""
     import torch
@@ -553,10 +565,13 @@ def run_decode_shapes(args, dist: Dist):
     H, F, QKV = DECODE["hidden"], DECODE["ffn"], DECODE["qkv"]
     hbm, _, _, peak_src = measured_peaks()
     results = {}
-    for name, n, k in (("qkv", QKV, H), ("out", H, H), ("gate_up", F, H), ("down", H, F)):
-        wbytes = pxq.weight_bytes(k, n, Q5_K)
+    shapes = [("qkv", QKV, H, Q5_K), ("out", H, H, Q5_K), ("gate_up", F, H, Q5_K), ("down", H, F, Q5_K),
+              ("gate_up q6_K", F, H, Q6_K), ("down q6_K", H, F, Q6_K)]
+    for name, n, k, wtype in shapes:
+        wbytes = pxq.weight_bytes(k, n, wtype)
         copies = max(2, -(-(320 << 20) // wbytes))
-        ws = [pxq.Weight(gpu_random_q5_K(n, k, gen), Q5_K, k, n) for _ in range(copies)]
+        make = gpu_random_q5_K if wtype == Q5_K else gpu_random_q6_K
+        ws = [pxq.Weight(make(n, k, gen), wtype, k, n) for _ in range(copies)]
         for M in (1, 8):
             x = torch.randn((M, k), device="cuda", generator=gen)
             y = torch.empty((M, n), device="cuda")
