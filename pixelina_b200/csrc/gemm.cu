@@ -383,12 +383,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 p.dump[(b * p.M + m) * p.N + n] = __uint_as_float(j < 32 ? iv[j] : iv2[j - 32]);
                         }
                     } else {
-                        // pix_dot_q8_0: acc = fma(fp16(dw)*fp16(dx), float(block dot), acc)
+                        // pix_dot_q8_0: acc = fma(fp16(dw)*fp16(dx), float(block dot), acc), two per instruction
 #pragma unroll
-                        for (int j = 0; j < 32; j++) acc[j] = __fmaf_rn(__uint_as_float(sv[j]), __uint_as_float(iv[j]), acc[j]);
+                        for (int j = 0; j < 32; j += 2)
+                            ffma2(acc[j], acc[j + 1], __uint_as_float(sv[j]), __uint_as_float(sv[j + 1]), __uint_as_float(iv[j]),
+                                  __uint_as_float(iv[j + 1]));
 #pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            acc[32 + j] = __fmaf_rn(__uint_as_float(sv2[j]), __uint_as_float(iv2[j]), acc[32 + j]);
+                        for (int j = 0; j < 32; j += 2)
+                            ffma2(acc[32 + j], acc[33 + j], __uint_as_float(sv2[j]), __uint_as_float(sv2[j + 1]),
+                                  __uint_as_float(iv2[j]), __uint_as_float(iv2[j + 1]));
                     }
                     slot += 2;
                     if (slot == SLOTS) {
@@ -408,10 +411,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
                         const float4 v = dx4[j];
-                        s[4 * j + 0] = __fmul_rn(-v.x, dmw);
-                        s[4 * j + 1] = __fmul_rn(-v.y, dmw);
-                        s[4 * j + 2] = __fmul_rn(-v.z, dmw);
-                        s[4 * j + 3] = __fmul_rn(-v.w, dmw);
+                        fmul2(s[4 * j + 0], s[4 * j + 1], -v.x, -v.y, dmw, dmw);
+                        fmul2(s[4 * j + 2], s[4 * j + 3], -v.z, -v.w, dmw, dmw);
                     }
                     // items: the min term, then the super-block's chunk sum (one per chunk
                     // when dumping block dots)
@@ -422,10 +423,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                             for (int j = 0; j < 16; j++) {
                                 const float4 v = dx4[j];
-                                s[4 * j + 0] = __fmul_rn(v.x, dw);
-                                s[4 * j + 1] = __fmul_rn(v.y, dw);
-                                s[4 * j + 2] = __fmul_rn(v.z, dw);
-                                s[4 * j + 3] = __fmul_rn(v.w, dw);
+                                fmul2(s[4 * j + 0], s[4 * j + 1], v.x, v.y, dw, dw);
+                                fmul2(s[4 * j + 2], s[4 * j + 3], v.z, v.w, dw, dw);
                             }
                             __syncwarp();
                             if (lane == 0) mbar_arrive(&sempty[se]);
@@ -451,9 +450,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                             }
                         } else {
 #pragma unroll
-                            for (int j = 0; j < 32; j++) acc[j] = __fmaf_rn(s[j], __uint_as_float(v0[j]), acc[j]);
+                            for (int j = 0; j < 32; j += 2)
+                                ffma2(acc[j], acc[j + 1], s[j], s[j + 1], __uint_as_float(v0[j]), __uint_as_float(v0[j + 1]));
 #pragma unroll
-                            for (int j = 0; j < 32; j++) acc[32 + j] = __fmaf_rn(s[32 + j], __uint_as_float(v1[j]), acc[32 + j]);
+                            for (int j = 0; j < 32; j += 2)
+                                ffma2(acc[32 + j], acc[33 + j], s[32 + j], s[33 + j], __uint_as_float(v1[j]),
+                                      __uint_as_float(v1[j + 1]));
                         }
                         if (++slot == SLOTS) {
                             slot = 0;
