@@ -8,7 +8,7 @@ tensor-core GEMM, inputs resident in HBM; L2 is flushed (256 MB write)
 between timed steps, outside the timed events.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload q5k_gemm|q8_0_gemm|q8_0_large|dit|decode|decode_shapes|sharded]
+                    [--workload q5k_gemm|q8_0_gemm|q8_0_large|q6k_gemm|dit|decode|decode_shapes|sharded]
 
 Multi-GPU (torchrun, one rank per GPU): each rank processes its own batch of
 activation rows against the same weights (data parallel over independent
@@ -46,7 +46,9 @@ GEMM_WORKLOADS = {
     "q5k_gemm": dict(wtype=Q5_K, M=4096, N=10240, K=3840, name="Q5_K GEMM (BASELINE configs[1])"),
     "q8_0_gemm": dict(wtype=Q8_0, M=4096, N=3840, K=3840, name="Q8_0 GEMM (BASELINE configs[0])"),
     "q8_0_large": dict(wtype=Q8_0, M=16384, N=12288, K=3072, name="large-image Q8_0 GEMM (BASELINE configs[4])"),
+    "q6k_gemm": dict(wtype=Q6_K, M=4096, N=10240, K=3840, name="Q6_K GEMM at the configs[1] shape"),
 }
+TYPE_NAMES = {Q8_0: "Q8_0", Q5_K: "Q5_K", Q6_K: "Q6_K"}
 DIT = dict(hidden=3072, ffn=12288, blocks=60, M=4352, qkv=9216)
 DECODE = dict(hidden=3584, ffn=18944, layers=28, qkv=4608)
 
@@ -279,10 +281,7 @@ def run_gemm_workload(args, dist: Dist, wl: dict):
     pxq.init(dist.local)
     M, N, K, wtype = wl["M"], wl["N"], wl["K"], wl["wtype"]
     # weights: identical on every rank (seed 1); activations: per rank
-    if wtype == Q5_K:
-        wbytes = synth.q5_K_weights(N, K, seed=1)
-    else:
-        wbytes = synth.q8_0_weights(N, K, seed=1)
+    wbytes = synth.weights_for(wtype, N, K, seed=1)
     x_host = synth.activations(M, K, seed=100 + dist.rank)
     W = pxq.Weight(wbytes, wtype, K, N, key=f"bench:{wtype}:{N}:{K}")
     x = torch.from_numpy(x_host).cuda()
@@ -337,10 +336,11 @@ def run_gemm_workload(args, dist: Dist, wl: dict):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "i8xi8->f32",
-        "data": "synthetic (seeded N(0,1) activations; weights encoded from N(0,0.02))",
+        "data": "synthetic (seeded N(0,1) activations; " + ("weights with uniformly random Q6_K fields)" if wtype == Q6_K
+                                                            else "weights encoded from N(0,0.02))"),
         "config": {"workload": f"{args.workload}: {wl['name']}", "M": M, "N": N, "K": K,
-                   "weight_type": "Q5_K" if wtype == Q5_K else "Q8_0",
-                   "activation_quant": "Q8_K" if wtype == Q5_K else "Q8_0",
+                   "weight_type": TYPE_NAMES[wtype],
+                   "activation_quant": "Q8_0" if wtype == Q8_0 else "Q8_K",
                    "per_rank_M": M, "global_M": M * dist.world, "parallelism": f"dp{dist.world}",
                    "l2": "flushed between timed steps (256 MB write, outside the events)"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": bf16, "unit": "TFLOP/s",
@@ -444,7 +444,7 @@ def run_reference(args, dist: Dist):
     cores = os.cpu_count() or 1
     if kind == "reference":
         lib.set_threads(cores)
-    wbytes = synth.q5_K_weights(N, K, seed=1) if wtype == Q5_K else synth.q8_0_weights(N, K, seed=1)
+    wbytes = synth.weights_for(wtype, N, K, seed=1)
     x = synth.activations(M, K, seed=100)
     ops_full = 2.0 * M * N * K
     # size each step so that warmup + steps stay within ~3 minutes
@@ -471,9 +471,10 @@ def run_reference(args, dist: Dist):
         "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "TOPS", "n_gpus": dist.world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "i8xi8->f32",
-        "data": "synthetic (seeded N(0,1) activations; weights encoded from N(0,0.02))",
+        "data": "synthetic (seeded N(0,1) activations; " + ("weights with uniformly random Q6_K fields)" if wtype == Q6_K
+                                                            else "weights encoded from N(0,0.02))"),
         "config": {"workload": f"{args.workload}: {wl['name']}", "M": M, "N": N, "K": K,
-                   "weight_type": "Q5_K" if wtype == Q5_K else "Q8_0", "parallelism": "host threads"},
+                   "weight_type": TYPE_NAMES[wtype], "parallelism": "host threads"},
         "cpu_baseline": {"value": round(value, 5), "unit": "TOPS", "cores": cores if kind == "reference" else 1,
                          "kind": kind, "sample": sample},
         "e2e": {"value": round(value, 5), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

@@ -211,11 +211,12 @@ PXQ_API int pxq_matvec_noalloc(pxq_weight* w, size_t row_first, size_t row_count
 
 /* Debug/parity: run the tensor-core GEMM but store, instead of the scaled
  * sum, every exact block dot it computed.  dump (device) receives
- * items x columns x row_count floats, item-major; items = inner/32 for Q8_0
- * and 5*inner/256 for Q5_K (per super-block: four 64-value sums of
- * sc*q5*q8, then the min sum of m*bsum).  These are the int32 block dots of
- * pix_dot_q8_0 / pix_dot_q5_K (src/kernels_quant.cpp:339-365, :163-254),
- * exact as floats. */
+ * items x columns x row_count floats, item-major; items = inner/32 for Q8_0,
+ * 5*inner/256 for Q5_K (per super-block: four 64-value sums of sc*q5*q8,
+ * then the min sum of m*bsum) and 4*inner/256 for Q6_K (per super-block:
+ * four 64-value sums of sc*(q6-32)*q8).  These are the int32 block dots of
+ * pix_dot_q8_0 / pix_dot_q5_K / pix_dot_q6_K (src/kernels_quant.cpp:339-365,
+ * :163-254, :256-337), exact as floats. */
 PXQ_API int pxq_gemm_block_dots(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* dump,
                         void* stream);
 

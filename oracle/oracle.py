@@ -124,6 +124,8 @@ class Oracle(_Lib):
         L.pxo_block_dots_q8_0.restype = None
         L.pxo_block_dots_q5_K.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
         L.pxo_block_dots_q5_K.restype = None
+        L.pxo_block_dots_q6_K.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+        L.pxo_block_dots_q6_K.restype = None
         L.pxo_float_to_half.argtypes = [C.c_float]
         L.pxo_float_to_half.restype = C.c_uint16
         L.pxo_half_to_float.argtypes = [C.c_uint16]
@@ -139,6 +141,13 @@ class Oracle(_Lib):
         m = np.zeros(inner // 256, dtype=np.int32)
         self.lib.pxo_block_dots_q5_K(inner, _ptr(np.ascontiguousarray(wrow)), _ptr(np.ascontiguousarray(arow)), _ptr(s), _ptr(m))
         return s, m
+
+    def block_dots_q6_K(self, inner: int, wrow: np.ndarray, arow: np.ndarray):
+        """(super-block dots [nsb], 64-value chunk dots [nsb, 4]), exact int32."""
+        s = np.zeros(inner // 256, dtype=np.int32)
+        ch = np.zeros(inner // 64, dtype=np.int32)
+        self.lib.pxo_block_dots_q6_K(inner, _ptr(np.ascontiguousarray(wrow)), _ptr(np.ascontiguousarray(arow)), _ptr(s), _ptr(ch))
+        return s, ch.reshape(-1, 4)
 
     def float_to_half(self, f: float) -> int:
         return int(self.lib.pxo_float_to_half(f))

@@ -14,6 +14,7 @@
  *   pxo_dot_q8_0            src/kernels_quant.cpp:339-365  pix_dot_q8_0
  *   pxo_dot_q5_K            src/kernels_quant.cpp:163-254  pix_dot_q5_K
  *   pxo_dot_q6_K            src/kernels_quant.cpp:256-337  pix_dot_q6_K
+ *   pxo_block_dots_q6_K     src/kernels_quant.cpp:256-337  its exact int32 super-block sums
  *   pxo_quant_matmul        src/kernels_quant.cpp:369-412  cpu_quant_matmul
  *   pxo_decode              src/backend_cpu.cpp:24-101     cpu_decode
  *   pxo_weight_bytes        src/model.cpp:87-121           weight_bytes
@@ -442,6 +443,39 @@ void pxo_block_dots_q5_K(int n, const uint8_t* x, const uint8_t* y, int32_t* sum
         }
         sumi[i] = s;
         msum[i] = m;
+    }
+}
+
+/* Exact int32 super-block dots of the Q6_K dot (src/kernels_quant.cpp:256-337):
+ *   sumi[i]        = sum over the 8 lanes of (sumi_l - q8sclsub_l), i.e.
+ *                    sum_j sc_j * sum_{16} q6 * q8  -  32 * sum_j sc_j * bsum_j
+ *                    (scaled by d = y.d * fp16(x.d) in the reference), and
+ *   chunk[4*i + c] = sum over values 64c..64c+63 of the super-block of
+ *                    sc * (q6 - 32) * q8, the same integer split in four.
+ * Values are indexed as in cpu_decode (src/backend_cpu.cpp:80-96): value
+ * 128*h + 32*g + t has its low nibble in ql[64*h + 32*(g%2) + t] (low half
+ * for g < 2), its high two bits at qh[32*h + t] >> 2g, scale
+ * scales[8*h + 2*g + t/16]. */
+void pxo_block_dots_q6_K(int n, const uint8_t* x, const uint8_t* y, int32_t* sumi, int32_t* chunk)
+{
+    for (int i = 0; i < n / PXO_QK_K; i++) {
+        const uint8_t* xb = x + (size_t)i * PXO_Q6_K_BYTES;
+        const uint8_t* yb = y + (size_t)i * PXO_Q8_K_BYTES;
+        const int8_t* scales = (const int8_t*)(xb + 192);
+        const int8_t* q8 = (const int8_t*)(yb + 4);
+        int32_t pos = 0, sub = 0;
+        for (int j = 0; j < 16; j++) sub += (int32_t)scales[j] * q8k_bsum(yb, j);
+        for (int c = 0; c < 4; c++) chunk[4 * i + c] = 0;
+        for (int e = 0; e < PXO_QK_K; e++) {
+            const int h = e / 128, g = (e % 128) / 32, t = e % 32;
+            unsigned q = xb[64 * h + 32 * (g % 2) + t];
+            q = g < 2 ? (q & 15u) : (q >> 4);
+            q |= ((xb[128 + 32 * h + t] >> (2 * g)) & 3u) << 4;
+            const int32_t s = scales[8 * h + 2 * g + t / 16];
+            pos += s * (int32_t)q * q8[e];
+            chunk[4 * i + e / 64] += s * ((int32_t)q - 32) * q8[e];
+        }
+        sumi[i] = pos - 32 * sub;
     }
 }
 

@@ -152,11 +152,11 @@ int make_map3(const DeviceCtx* d, CUtensorMap* m, CUtensorMapDataType dt, const 
 // GEMM operand copy of (a row range of) a weight.
 struct Packed {
     int64_t rows = 0;   // packed rows
-    int64_t ldn = 0;    // row stride of the Q5_K scale planes
+    int64_t ldn = 0;    // row stride of the K-quant scale planes
     void* mem = nullptr;
-    __half* wv = nullptr;     // fp16 operand [rows][K]
+    __half* wv = nullptr;     // fp16 operand [rows][K] (Q6_K: [rows][2K], even and parity planes)
     __half* ws = nullptr;     // Q8_0 one-hot scales [rows][nb*16] / Q5_K min operand [rows][nsb*16]
-    float* d = nullptr;       // Q5_K d    [nsb][ldn]
+    float* d = nullptr;       // Q5_K / Q6_K d [nsb][ldn]
     float* dmin = nullptr;    // Q5_K dmin [nsb][ldn]
     CUtensorMap tmW, tmWs, tmD, tmDm;
     ~Packed()
@@ -219,13 +219,14 @@ int build_packed(const DeviceCtx* d, pxq_weight* w, int64_t first, int64_t count
 {
     auto pk = std::make_unique<Packed>();
     const int64_t K = w->inner;
-    const bool q5 = w->type == kTypeQ5_K;
-    const int64_t nb = q5 ? K / kQKK : K / kQK8_0;
+    const bool q5 = w->type == kTypeQ5_K, q6 = w->type == kTypeQ6_K;
+    const int64_t nb = (q5 || q6) ? K / kQKK : K / kQK8_0;
+    const int64_t Kop = q6 ? 2 * K : K;  // Q6_K: even and parity planes per chunk
     pk->rows = count;
     pk->ldn = round_up(count, 4);
-    const size_t wv_bytes = (size_t)count * K * 2;
-    const size_t ws_bytes = (size_t)count * nb * 32;
-    const size_t s_bytes = q5 ? (size_t)nb * pk->ldn * 4 : 0;
+    const size_t wv_bytes = (size_t)count * Kop * 2;
+    const size_t ws_bytes = q6 ? 0 : (size_t)count * nb * 32;
+    const size_t s_bytes = (q5 || q6) ? (size_t)nb * pk->ldn * 4 : 0;
     const size_t off_ws = round_up((int64_t)wv_bytes, 1024);
     const size_t off_d = off_ws + round_up((int64_t)ws_bytes, 1024);
     const size_t off_dm = off_d + round_up((int64_t)s_bytes, 1024);
@@ -241,24 +242,26 @@ int build_packed(const DeviceCtx* d, pxq_weight* w, int64_t first, int64_t count
     pk->dmin = reinterpret_cast<float*>(base + off_dm);
     PXQ_CUDA(cudaMemsetAsync(pk->mem, 0, total, s));
     const uint8_t* src = w->raw + first * w->stride;
-    if (!q5) {
+    if (q6) {
+        PXQ_CUDA(counted(launch_repack_q6_K(src, count, K, w->stride, pk->wv, pk->d, pk->ldn, s)));
+    } else if (!q5) {
         PXQ_CUDA(counted(launch_repack_q8_0(src, count, K, w->stride, pk->wv, pk->ws, s)));
     } else {
         PXQ_CUDA(counted(launch_repack_q5_K(src, count, K, w->stride, pk->wv, pk->d, pk->dmin, pk->ws, pk->ldn, s)));
     }
-    int rc = make_map(d, &pk->tmW, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pk->wv, K, count, K * 2, 64, 128,
+    int rc = make_map(d, &pk->tmW, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pk->wv, Kop, count, Kop * 2, 64, 128,
                       CU_TENSOR_MAP_SWIZZLE_128B);
-    if (!rc) rc = make_map(d, &pk->tmWs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pk->ws, nb * 16, count, nb * 32, 16, 128,
-                           CU_TENSOR_MAP_SWIZZLE_32B);
-    if (!rc && q5) {
+    // unused maps of a type hold the weight map (any valid map will do)
+    pk->tmWs = pk->tmD = pk->tmDm = pk->tmW;
+    if (!rc && !q6)
+        rc = make_map(d, &pk->tmWs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pk->ws, nb * 16, count, nb * 32, 16, 128,
+                      CU_TENSOR_MAP_SWIZZLE_32B);
+    if (!rc && (q5 || q6))
         rc = make_map(d, &pk->tmD, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pk->d, count, nb, pk->ldn * 4, 128, 1,
                       CU_TENSOR_MAP_SWIZZLE_NONE);
-        if (!rc) rc = make_map(d, &pk->tmDm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pk->dmin, count, nb, pk->ldn * 4, 128, 1,
-                               CU_TENSOR_MAP_SWIZZLE_NONE);
-    } else {
-        pk->tmD = pk->tmW;
-        pk->tmDm = pk->tmW;
-    }
+    if (!rc && q5)
+        rc = make_map(d, &pk->tmDm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pk->dmin, count, nb, pk->ldn * 4, 128, 1,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
     out = std::move(pk);
     return PXQ_OK;
@@ -322,8 +325,6 @@ int quantize_activation(DeviceCtx* d, uint32_t wtype, const float* input, int64_
     a->M = M;
     a->K = K;
     a->blocks = layout == 0 ? (M <= 8) : (layout == 1);
-    if (wtype == kTypeQ6_K && (!a->blocks || M > 8))
-        return fail(PXQ_ERR_UNSUPPORTED, "Q6_K weights: only the matvec (at most 8 activation rows) is supported");
     const int64_t nb = q5 ? K / kQKK : K / kQK8_0;
     cudaError_t e;
     if (a->blocks) {
@@ -513,8 +514,6 @@ int run_matmul(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, 
                float* output, size_t ldy, const float* bias, float* dump, int force, cudaStream_t s)
 {
     if (force == 1 && columns > 8) return fail(PXQ_ERR_UNSUPPORTED, "matvec handles at most 8 columns (got %zu)", columns);
-    if (w->type == kTypeQ6_K && (force == 2 || columns > 8))
-        return fail(PXQ_ERR_UNSUPPORTED, "Q6_K weights: only the matvec (at most 8 activation rows) is supported");
     if (w->type == kTypeQ8_0 || w->type == kTypeQ5_K) {
         if (w->inner % 8) return fail(PXQ_ERR_UNSUPPORTED, "inner %lld not a multiple of 8", (long long)w->inner);
     }
@@ -939,8 +938,6 @@ int pxq_quant_matmul(const unsigned char* weights, uint32_t type, const float* i
     const size_t block = type == PXQ_TYPE_Q8_0 ? 32 : 256;
     if (!rows || !columns || !inner || inner % block || inner > 0x7fffffffu)
         return fail(PXQ_ERR_UNSUPPORTED, "shape rows=%zu columns=%zu inner=%zu not handled", rows, columns, inner);
-    if (type == PXQ_TYPE_Q6_K && columns > 8)
-        return fail(PXQ_ERR_UNSUPPORTED, "Q6_K weights: only the matvec (at most 8 activation rows) is handled");
     if (!weights || !input || !output) return fail(PXQ_ERR_INVALID, "null pointer");
     DeviceCtx* d;
     if (int rc = ensure_device(&d)) return rc;

@@ -33,6 +33,12 @@
 //     so the exact int32 chunk dots stay checkable.  The min term
 //     sum_j m_j*bsum_j is a K=16 MMA per super-block on exact (hi, lo) splits,
 //     drained first.
+//   * Q6_K (pix_dot_q6_K, :256-337): the 8-bit scale and the -32 offset fold
+//     into v = sc*(q6-32), |v| <= 4096 -- 13 bits, one more than fp16 holds
+//     for odd values.  The repack splits v into an even part (exact in fp16)
+//     and its parity bit, two operand planes that two MMAs per K step
+//     accumulate into the same TMEM slot, so the chunk dots stay exact
+//     integers.  No min term; one drain per super-block.
 //   * Warp roles (12 warps, 3 warpgroups): warpgroups 0-1 drain TMEM (warp w
 //     reads lane quadrant w%4 and column half w/4) with 232 registers
 //     (setmaxnreg); warpgroup 2 runs the TMA producer (warp 8) and the
@@ -73,6 +79,10 @@ constexpr int Q5_STAGES = 4;
 constexpr int Q5_STAGE = W_BYTES + X_BYTES;                                // 32 KB
 constexpr int Q5_SB_ENTRY = 2 * SW32_TILE + 3 * 512;                      // 9.5 KB
 constexpr int Q5_SB_DEPTH = 2;
+// Q6_K stage: W even part | W parity part | X;  super-block entries: dW | dX
+constexpr int Q6_STAGES = 3;
+constexpr int Q6_STAGE = 2 * W_BYTES + X_BYTES;                            // 48 KB
+constexpr int Q6_SB_ENTRY = 2 * 512;
 
 template <uint32_t TYPE>
 struct Cfg;
@@ -80,13 +90,25 @@ template <>
 struct Cfg<kTypeQ8_0> {
     static constexpr int STAGES = Q80_STAGES;
     static constexpr int STAGE = Q80_STAGE;
+    static constexpr int SB_ENTRY = 0;
     static constexpr int SB_REGION = 0;
+    static constexpr int OFF_DW = 0, OFF_DMW = 0, OFF_DX = 0;  // no super-block entries
 };
 template <>
 struct Cfg<kTypeQ5_K> {
     static constexpr int STAGES = Q5_STAGES;
     static constexpr int STAGE = Q5_STAGE;
+    static constexpr int SB_ENTRY = Q5_SB_ENTRY;
     static constexpr int SB_REGION = Q5_SB_ENTRY * Q5_SB_DEPTH;
+    static constexpr int OFF_DW = 2 * SW32_TILE, OFF_DMW = OFF_DW + 512, OFF_DX = OFF_DW + 1024;  // in an entry
+};
+template <>
+struct Cfg<kTypeQ6_K> {
+    static constexpr int STAGES = Q6_STAGES;
+    static constexpr int STAGE = Q6_STAGE;
+    static constexpr int SB_ENTRY = Q6_SB_ENTRY;
+    static constexpr int SB_REGION = Q6_SB_ENTRY * Q5_SB_DEPTH;
+    static constexpr int OFF_DW = 0, OFF_DMW = 0, OFF_DX = 512;
 };
 
 template <uint32_t TYPE>
@@ -105,9 +127,11 @@ __host__ __device__ constexpr int smem_bytes()
 {
     return off_bar<TYPE>() + NUM_BARS * 8 + 16 + 1024;
 }
-static_assert(Q80_STAGES <= MAX_STAGES && Q5_STAGES <= MAX_STAGES, "stage count");
+static_assert(Q80_STAGES <= MAX_STAGES && Q5_STAGES <= MAX_STAGES && Q6_STAGES <= MAX_STAGES, "stage count");
 static_assert(smem_bytes<kTypeQ8_0>() <= 232448, "Q8_0 shared memory");
 static_assert(smem_bytes<kTypeQ5_K>() <= 232448, "Q5_K shared memory");
+static_assert(smem_bytes<kTypeQ6_K>() <= 232448, "Q6_K shared memory");
+static_assert(Q6_STAGE % 1024 == 0 && Q5_STAGE % 1024 == 0, "128B-swizzled tiles need 1024-byte alignment");
 
 struct Params {
     int64_t M, N, K;
@@ -124,7 +148,7 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) { return smem_des
 __device__ __forceinline__ uint64_t desc_sw32(uint32_t saddr) { return smem_desc(saddr, 16, 256, 6); }
 
 // tensor maps:
-//   tmW   weight operand fp16 [N][K]            box {64, 128}  128B swizzle
+//   tmW   weight operand fp16 [N][K] (Q6_K: [N][2K])  box {64, 128}  128B swizzle
 //   tmX   activation operand fp16 [M][K]        box {64, 128}  128B swizzle
 //   Q8_0: tmWs  one-hot weight scales fp16 [N][nb*16]   box {16, 128} 32B swizzle
 //         tmXs  activation scales fp16 [M][nb]          box {16, 128} 32B swizzle
@@ -133,6 +157,7 @@ __device__ __forceinline__ uint64_t desc_sw32(uint32_t saddr) { return smem_desc
 //         tmD   weight d   fp32 [nsb][N4]  box {128, 1}
 //         tmDm  weight dmin fp32 [nsb][N4] box {128, 1}
 //         tmDx  activation d fp32 [nsb][M4] box {128, 1}
+//   Q6_K: tmD, tmDx as for Q5_K (the others unused)
 template <uint32_t TYPE, bool DUMP>
 __global__ void __launch_bounds__(THREADS, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
@@ -142,6 +167,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 {
     using C = Cfg<TYPE>;
     constexpr bool Q8 = TYPE == kTypeQ8_0;
+    constexpr bool Q6 = TYPE == kTypeQ6_K;
     constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -165,7 +191,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         for (int i = 0; i < Q5_SB_DEPTH; i++) {
             mbar_init(&sfull[i], 1);
-            mbar_init(&sempty[i], DRAIN_WARPS + 1);  // drain warps + the MMA thread (min operands)
+            mbar_init(&sempty[i], Q6 ? DRAIN_WARPS : DRAIN_WARPS + 1);  // drain warps (+ the MMA thread: Q5_K min operands)
         }
         for (int i = 0; i < SLOTS; i++) {
             mbar_init(&tfull[i], 1);
@@ -215,14 +241,16 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int64_t kc = 0; kc < nchunks; kc++) {
                     if (!Q8 && kc % 4 == 0) {
                         if (!mbar_wait(&sempty[se], sph ^ 1u, abort_flag, status, kDevTimeoutScaleEmpty)) goto done;
-                        uint8_t* e = sb_region + se * Q5_SB_ENTRY;
+                        uint8_t* e = sb_region + se * Cfg<TYPE>::SB_ENTRY;
                         const int32_t sb = (int32_t)(kc / 4);
-                        mbar_expect_tx(&sfull[se], Q5_SB_ENTRY);
-                        tma_load_2d(e, &tmWs, &sfull[se], sb * 16, n0);
-                        tma_load_2d(e + SW32_TILE, &tmXs, &sfull[se], sb * 16, m0);
-                        tma_load_2d(e + 2 * SW32_TILE, &tmD, &sfull[se], n0, sb);
-                        tma_load_2d(e + 2 * SW32_TILE + 512, &tmDm, &sfull[se], n0, sb);
-                        tma_load_2d(e + 2 * SW32_TILE + 1024, &tmDx, &sfull[se], m0, sb);
+                        mbar_expect_tx(&sfull[se], Cfg<TYPE>::SB_ENTRY);
+                        if (!Q6) {
+                            tma_load_2d(e, &tmWs, &sfull[se], sb * 16, n0);
+                            tma_load_2d(e + SW32_TILE, &tmXs, &sfull[se], sb * 16, m0);
+                            tma_load_2d(e + C::OFF_DMW, &tmDm, &sfull[se], n0, sb);
+                        }
+                        tma_load_2d(e + C::OFF_DW, &tmD, &sfull[se], n0, sb);
+                        tma_load_2d(e + C::OFF_DX, &tmDx, &sfull[se], m0, sb);
                         if (++se == Q5_SB_DEPTH) {
                             se = 0;
                             sph ^= 1u;
@@ -240,6 +268,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                                         (int32_t)((2 * kc + b) * 16), n0);
                         tma_load_2d(st + W_BYTES + X_BYTES + 2 * SW32_TILE, &tmXs, &full[stage],
                                     (int32_t)(((2 * kc) / 16) * 16), m0);
+                    } else if (Q6) {
+                        // chunk kc's even and parity planes sit side by side in the [N][2K] operand
+                        mbar_expect_tx(&full[stage], 2 * W_BYTES + X_BYTES);
+                        tma_load_2d(st, &tmW, &full[stage], (int32_t)(kc * 2 * BK), n0);
+                        tma_load_2d(st + W_BYTES, &tmW, &full[stage], (int32_t)(kc * 2 * BK + BK), n0);
+                        tma_load_2d(st + 2 * W_BYTES, &tmX, &full[stage], (int32_t)(kc * BK), m0);
                     } else {
                         mbar_expect_tx(&full[stage], W_BYTES + X_BYTES);
                         tma_load_2d(st, &tmW, &full[stage], (int32_t)(kc * BK), n0);
@@ -260,7 +294,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint32_t sph = 0;
             for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
                 for (int64_t kc = 0; kc < nchunks; kc++) {
-                    if (!Q8 && kc % 4 == 0) {
+                    if (!Q8 && !Q6 && kc % 4 == 0) {
                         // min-term item of this super-block, drained first
                         if (!mbar_wait(&sfull[se], sph, abort_flag, status, kDevTimeoutScaleFull)) goto done;
                         if (!mbar_wait(&tempty[slot], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
@@ -281,7 +315,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (!mbar_wait(&full[stage], ph, abort_flag, status, kDevTimeoutFull)) goto done;
                     tc_fence_after();
                     const uint32_t w_addr = smem_u32(smem + stage * C::STAGE);
-                    const uint32_t x_addr = w_addr + W_BYTES;
+                    const uint32_t x_addr = w_addr + (Q6 ? 2 * W_BYTES : W_BYTES);
                     if (Q8) {
                         const uint32_t ws_addr = x_addr + X_BYTES;
                         const uint32_t xs_addr = ws_addr + 2 * SW32_TILE;
@@ -309,9 +343,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                             }
                         }
                     } else {
-                        // Q5_K: the four 64-value chunks of a super-block share its scale, so
-                        // they accumulate into one TMEM slot (one drain per super-block); the
-                        // block-dot dump keeps one slot per chunk
+                        // K-quants: the four 64-value chunks of a super-block share its scale,
+                        // so they accumulate into one TMEM slot (one drain per super-block);
+                        // the block-dot dump keeps one slot per chunk.  Q6_K adds each K step's
+                        // parity plane into the same accumulator.
                         const bool first = DUMP || kc % 4 == 0;
                         const bool last = DUMP || kc % 4 == 3 || kc == nchunks - 1;
                         if (first) {
@@ -324,6 +359,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                             const uint32_t koff = (uint32_t)k * 32u;
                             mma_f16(d, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC,
                                     (first && k == 0) ? 0u : 1u);
+                            if (Q6) mma_f16(d, desc_sw128(w_addr + W_BYTES + koff), desc_sw128(x_addr + koff), IDESC, 1u);
                         }
                         if (last) {
                             mma_commit(&tfull[slot]);
@@ -402,23 +438,36 @@ __global__ void __launch_bounds__(THREADS, 1)
             } else {
                 for (int64_t sb = 0; sb < nb; sb++) {
                     if (!mbar_wait(&sfull[se], sph, abort_flag, status, kDevTimeoutScaleFull)) goto done;
-                    const uint8_t* e = sb_region + se * Q5_SB_ENTRY;
-                    const float dw = reinterpret_cast<const float*>(e + 2 * SW32_TILE)[wrow];
-                    const float dmw = reinterpret_cast<const float*>(e + 2 * SW32_TILE + 512)[wrow];
-                    const float4* dx4 = reinterpret_cast<const float4*>(e + 2 * SW32_TILE + 1024) + half * 16;
+                    const uint8_t* e = sb_region + se * C::SB_ENTRY;
+                    const float dw = reinterpret_cast<const float*>(e + C::OFF_DW)[wrow];
+                    const float4* dx4 = reinterpret_cast<const float4*>(e + C::OFF_DX) + half * 16;
                     float s[64];
-                    // pix_dot_q5_K: dmin = -y.d * fp16(x.dmin)
+                    if (Q6) {
+                        // pix_dot_q6_K: d = y.d * fp16(x.d)
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        const float4 v = dx4[j];
-                        fmul2(s[4 * j + 0], s[4 * j + 1], -v.x, -v.y, dmw, dmw);
-                        fmul2(s[4 * j + 2], s[4 * j + 3], -v.z, -v.w, dmw, dmw);
+                        for (int j = 0; j < 16; j++) {
+                            const float4 v = dx4[j];
+                            fmul2(s[4 * j + 0], s[4 * j + 1], v.x, v.y, dw, dw);
+                            fmul2(s[4 * j + 2], s[4 * j + 3], v.z, v.w, dw, dw);
+                        }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&sempty[se]);
+                    } else {
+                        // pix_dot_q5_K: dmin = -y.d * fp16(x.dmin)
+                        const float dmw = reinterpret_cast<const float*>(e + C::OFF_DMW)[wrow];
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            const float4 v = dx4[j];
+                            fmul2(s[4 * j + 0], s[4 * j + 1], -v.x, -v.y, dmw, dmw);
+                            fmul2(s[4 * j + 2], s[4 * j + 3], -v.z, -v.w, dmw, dmw);
+                        }
                     }
-                    // items: the min term, then the super-block's chunk sum (one per chunk
-                    // when dumping block dots)
+                    // items: Q5_K the min term, then the super-block's chunk sum; Q6_K the
+                    // chunk sum alone (one item per chunk when dumping block dots)
+                    constexpr int ITEMS = Q6 ? (DUMP ? 4 : 1) : (DUMP ? 5 : 2);
 #pragma unroll 1
-                    for (int it = 0; it < (DUMP ? 5 : 2); it++) {
-                        if (it == 1) {
+                    for (int it = 0; it < ITEMS; it++) {
+                        if (!Q6 && it == 1) {
                             // d = y.d * fp16(x.d), cached for the four chunks
 #pragma unroll
                             for (int j = 0; j < 16; j++) {
@@ -440,7 +489,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&tempty[slot]);
                         if (DUMP) {
-                            const int64_t item = sb * 5 + (it == 0 ? 4 : it - 1);
+                            const int64_t item = Q6 ? sb * 4 + it : sb * 5 + (it == 0 ? 4 : it - 1);
                             const int64_t n = n0 + wrow;
 #pragma unroll
                             for (int j = 0; j < 64; j++) {
@@ -533,6 +582,9 @@ cudaError_t launch_gemm(const GemmOperands& op, int num_sms, cudaStream_t s)
     }
     if (op.type == kTypeQ5_K) {
         return op.dump ? launch_typed<kTypeQ5_K, true>(op, num_sms, s) : launch_typed<kTypeQ5_K, false>(op, num_sms, s);
+    }
+    if (op.type == kTypeQ6_K) {
+        return op.dump ? launch_typed<kTypeQ6_K, true>(op, num_sms, s) : launch_typed<kTypeQ6_K, false>(op, num_sms, s);
     }
     return cudaErrorInvalidValue;
 }

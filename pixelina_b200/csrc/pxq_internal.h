@@ -43,6 +43,9 @@ cudaError_t launch_repack_q8_0(const uint8_t* raw, int64_t rows, int64_t inner, 
                                cudaStream_t s);
 cudaError_t launch_repack_q5_K(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wv, float* dT,
                                float* dminT, __half* bmin, int64_t ldn, cudaStream_t s);
+// Q6_K: raw rows are the device's padded super-blocks (stride bytes per row).
+cudaError_t launch_repack_q6_K(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wab, float* dT,
+                               int64_t ldn, cudaStream_t s);
 
 cudaError_t launch_decode(const uint8_t* data, uint32_t type, int64_t count, float* out, cudaStream_t s);
 
@@ -129,13 +132,13 @@ cudaError_t launch_gather_shards(const float* src, int64_t shards, int64_t colum
 
 // ---- gemm.cu ---------------------------------------------------------------
 struct GemmOperands {
-    uint32_t type;        // kTypeQ8_0 or kTypeQ5_K
+    uint32_t type;        // kTypeQ8_0, kTypeQ5_K or kTypeQ6_K
     int64_t M, N, K;      // activation rows, view rows (output columns), inner
     int64_t n_first;      // first weight row of the view (multiple of 4)
     // tensor maps: 0 weight operand, 1 activation operand, 2 weight scale
     // tile (Q8_0 one-hot scales / Q5_K min operand), 3 activation scale tile
-    // (Q8_0 fp16 scales / Q8_K min operand), 4 Q5_K weight d, 5 Q5_K weight
-    // dmin, 6 Q8_K activation d (unused entries may hold any valid map)
+    // (Q8_0 fp16 scales / Q8_K min operand), 4 K-quant weight d, 5 Q5_K
+    // weight dmin, 6 Q8_K activation d (unused entries may hold any valid map)
     CUtensorMap tm[7];
     CUtensorMap tm_y;     // output map (fp32 [M][ldy], box {32, 64}) when tma_store
     int tma_store;        // 1: write the output tile with TMA stores

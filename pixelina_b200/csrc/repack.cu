@@ -12,6 +12,12 @@
 //             dT, dminT fp32 [inner/256][ldn]
 //             bmin fp16 [rows][inner/256*16] = (64*m_g, m_g) pairs, the weight
 //                  side of the exact min-term product
+//       Q6_K: wab  fp16 [rows][2*inner]: v = sc*(q6-32) (src/kernels_quant.cpp:
+//                  256-337 folded per value) split into an even part a = v & ~1
+//                  (|a| <= 4096, exact in fp16) and a parity part b = v & 1, so
+//                  that a + b = v exactly; per 64-value chunk c, a fills
+//                  [128c, 128c+64) and b [128c+64, 128c+128)
+//             dT   fp32 [inner/256][ldn]
 //     The bit layouts read here are those of src/backend_cpu.cpp:92-120
 //     (cpu_decode) and src/kernels_quant.cpp:18-23 / 189-194.
 // (2) pxq decode: dequantize to fp32 exactly as cpu_decode does
@@ -96,6 +102,42 @@ __global__ void k_repack_q5_K(const uint8_t* __restrict__ raw, int64_t rows, int
     }
 }
 
+// Q6_K rows as stored on the device: 224-byte padded super-blocks with the
+// GGUF field offsets (ql at 0, qh at 128, scales at 192, d at 208).
+__global__ void k_repack_q6_K(const uint8_t* __restrict__ raw, int64_t rows, int64_t inner, int64_t stride,
+                              __half* __restrict__ wab, float* __restrict__ dT, int64_t ldn)
+{
+    const int64_t nsb = inner / kQKK;
+    const int64_t total = rows * nsb * 8;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int G = (int)(i % 8);  // values 32G .. 32G+31 of the super-block
+        const int64_t sbi = i / 8;
+        const int64_t r = sbi / nsb, sb = sbi % nsb;
+        const uint8_t* blk = raw + r * stride + sb * kQ6KPadBytes;
+        const int h = G / 4, g = G % 4;
+        const uint8_t* ql = blk + 64 * h + 32 * (g % 2);
+        const uint8_t* qh = blk + 128 + 32 * h;
+        __half a[32], b[32];
+#pragma unroll
+        for (int t = 0; t < 32; t++) {
+            int q = g < 2 ? (ql[t] & 15) : (ql[t] >> 4);
+            q |= ((qh[t] >> (2 * g)) & 3) << 4;
+            const int v = (int)(int8_t)blk[192 + 8 * h + 2 * g + t / 16] * (q - 32);
+            a[t] = __int2half_rn(v & ~1);
+            b[t] = __int2half_rn(v & 1);
+        }
+        const int64_t col = (sb * 4 + G / 2) * 128 + (G % 2) * 32;  // chunk G/2 of this super-block
+        uint4* da = reinterpret_cast<uint4*>(wab + r * 2 * inner + col);
+        uint4* db = reinterpret_cast<uint4*>(wab + r * 2 * inner + col + 64);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            da[j] = reinterpret_cast<uint4*>(a)[j];
+            db[j] = reinterpret_cast<uint4*>(b)[j];
+        }
+        if (G == 0) dT[sb * ldn + r] = load_half(blk + 208);
+    }
+}
+
 __global__ void k_decode(const uint8_t* __restrict__ data, uint32_t type, int64_t count, float* __restrict__ out)
 {
     const int64_t blk_elems = type == kTypeQ8_0 ? kQK8_0 : kQKK;
@@ -150,6 +192,13 @@ cudaError_t launch_repack_q5_K(const uint8_t* raw, int64_t rows, int64_t inner, 
                                float* dminT, __half* bmin, int64_t ldn, cudaStream_t s)
 {
     k_repack_q5_K<<<grid_for(rows * (inner / kQKK) * 8, 256), 256, 0, s>>>(raw, rows, inner, stride, wv, dT, dminT, bmin, ldn);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_repack_q6_K(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wab, float* dT,
+                               int64_t ldn, cudaStream_t s)
+{
+    k_repack_q6_K<<<grid_for(rows * (inner / kQKK) * 8, 256), 256, 0, s>>>(raw, rows, inner, stride, wab, dT, ldn);
     return cudaGetLastError();
 }
 

@@ -228,7 +228,7 @@ def gemm_block_dots(w: Weight, x, row_first: int = 0, row_count: Optional[int] =
     x = x.contiguous()
     columns, inner = x.shape
     rc = w.rows - row_first if row_count is None else row_count
-    items = inner // 32 if w.wtype == TYPE_Q8_0 else 5 * (inner // 256)
+    items = {TYPE_Q8_0: inner // 32, TYPE_Q5_K: 5 * (inner // 256), TYPE_Q6_K: 4 * (inner // 256)}[w.wtype]
     dump = torch.zeros((items, columns, rc), dtype=torch.float32, device=x.device)
     _check(load().pxq_gemm_block_dots(w.handle, row_first, rc, _ptr(x), columns, _ptr(dump), _stream_ptr(stream)))
     return dump

@@ -93,7 +93,7 @@ def test_decode_golden(pxq, golden, name, wtype):
 
 # ------------------------------------------------------------------ matmul --
 
-@pytest.mark.parametrize("name,wtype", [("q8_0", Q8_0), ("q5_K", Q5_K)])
+@pytest.mark.parametrize("name,wtype", [("q8_0", Q8_0), ("q5_K", Q5_K), ("q6_K", Q6_K)])
 @pytest.mark.parametrize("path", ["matvec", "gemm", "auto"])
 def test_matmul_golden(pxq, golden, name, wtype, path):
     w = golden[f"w_{name}"]
@@ -137,21 +137,20 @@ def test_matvec_kquant_tile_shapes(pxq, oracle, wtype, rows, inner, columns):
     assert ok and max_abs_rel(y, ref) <= TOL
 
 
-def test_q6_K_golden_and_limits(pxq, golden):
-    """Q6_K weights: the matvec against the reference build's outputs; larger
-    activation batches are reported as not handled (the reference's `false`)."""
+def test_q6_K_golden_past_the_matvec(pxq, golden):
+    """Q6_K weights with more activation rows than the matvec takes go to the
+    tensor-core GEMM; each output row depends on its own activation row only,
+    so the reference build's outputs for the golden rows, repeated, are the
+    expected result."""
     w = golden["w_q6_K"]
     rows, inner = w.shape[0], golden["mm_x"].shape[1]
     W = pxq.Weight(w, Q6_K, inner, rows)
-    for path in ("matvec", "auto"):
-        y = pxq.matmul(W, cuda(golden["mm_x"]), path=path).cpu().numpy()
-        pxq.synchronize()
-        assert max_abs_rel(y, golden["mm_q6_K"]) <= TOL
     x9 = np.concatenate([golden["mm_x"], golden["mm_x"][:2]])
+    want = np.concatenate([golden["mm_q6_K"], golden["mm_q6_K"][:2]])
     for path in ("gemm", "auto"):
-        with pytest.raises(pxq.PxqError) as err:
-            pxq.matmul(W, cuda(x9), path=path)
-        assert err.value.code == pxq.ERR_UNSUPPORTED
+        y = pxq.matmul(W, cuda(x9), path=path).cpu().numpy()
+        pxq.synchronize()
+        assert max_abs_rel(y, want) <= TOL
     W.release()
 
 
@@ -182,7 +181,7 @@ def test_matvec_scratch_reuse_across_schedules(pxq, oracle):
     Wq.release()
 
 
-@pytest.mark.parametrize("wtype", [Q8_0, Q5_K])
+@pytest.mark.parametrize("wtype", [Q8_0, Q5_K, Q6_K])
 @pytest.mark.parametrize("columns,rows,inner", [(9, 48, 512), (130, 260, 512), (259, 520, 768), (128, 256, 2048),
                                                 (200, 300, 256)])
 def test_gemm_vs_oracle(pxq, oracle, wtype, columns, rows, inner):
@@ -209,7 +208,7 @@ def test_gemm_q8_0_odd_block_count(pxq, oracle):
     assert ok and max_abs_rel(y, ref) <= TOL
 
 
-@pytest.mark.parametrize("wtype", [Q8_0, Q5_K])
+@pytest.mark.parametrize("wtype", [Q8_0, Q5_K, Q6_K])
 def test_gemm_block_dots_exact(pxq, oracle, wtype):
     """The tensor-core path's per-block integer dots equal the reference's."""
     rows, inner, columns = 40, 512, 20
@@ -225,6 +224,14 @@ def test_gemm_block_dots_exact(pxq, oracle, wtype):
             for r in range(rows):
                 want = oracle.block_dots_q8_0(inner, w[r], xq[c])
                 assert np.array_equal(dump[:, c, r], want.astype(np.float32))
+    elif wtype == Q6_K:
+        xq = oracle.quantize_q8_K(x)
+        for c in range(columns):
+            for r in range(rows):
+                s, chunks = oracle.block_dots_q6_K(inner, w[r], xq[c])
+                items = dump[:, c, r].reshape(-1, 4)
+                assert np.array_equal(items, chunks.astype(np.float32))  # every 64-value chunk, exactly
+                assert np.array_equal(items.astype(np.int64).sum(axis=1), s.astype(np.int64))
     else:
         xq = oracle.quantize_q8_K(x)
         nsb = inner // 256
@@ -237,7 +244,8 @@ def test_gemm_block_dots_exact(pxq, oracle, wtype):
                 assert np.array_equal(items[:, 4].astype(np.int64), m.astype(np.int64))
 
 
-@pytest.mark.parametrize("path,wtype", [("matvec", Q8_0), ("matvec", Q5_K), ("matvec", Q6_K), ("gemm", Q8_0), ("gemm", Q5_K)])
+@pytest.mark.parametrize("path,wtype", [("matvec", Q8_0), ("matvec", Q5_K), ("matvec", Q6_K), ("gemm", Q8_0), ("gemm", Q5_K),
+                                        ("gemm", Q6_K)])
 def test_row_views_ldy_bias(pxq, oracle, path, wtype):
     """tensor_linear_rows-style row ranges, strided output, fused bias."""
     import torch
@@ -268,10 +276,10 @@ def test_host_drop_in_matches_reference_contract(pxq, oracle, golden):
         handled, y = pxq.quant_matmul(w, wtype, golden["mm_x"], w.shape[0])
         assert handled and max_abs_rel(y, golden[f"mm_{name}"]) <= TOL
     handled, y = pxq.quant_matmul(golden["w_q6_K"], Q6_K, golden["mm_x"], 24)
-    assert handled and max_abs_rel(y, golden["mm_q6_K"]) <= TOL  # Q6_K: the matvec, up to 8 activation rows
+    assert handled and max_abs_rel(y, golden["mm_q6_K"]) <= TOL  # Q6_K on the matvec
     x9 = np.concatenate([golden["mm_x"], golden["mm_x"][:2]])
-    handled, _ = pxq.quant_matmul(golden["w_q6_K"], Q6_K, x9, 24)
-    assert not handled  # 9 rows of Q6_K: not handled, the caller's fallback runs, as for any `false`
+    handled, y = pxq.quant_matmul(golden["w_q6_K"], Q6_K, x9, 24)  # and on the GEMM
+    assert handled and max_abs_rel(y, np.concatenate([golden["mm_q6_K"], golden["mm_q6_K"][:2]])) <= TOL
     # large-M through the host entry point
     w = synth.q8_0_weights(256, 1024, seed=5)
     x = synth.activations(300, 1024, seed=6)

@@ -81,6 +81,15 @@ def test_block_dots_match_float_dots(oracle):
         yd = xk[0].reshape(-1, 292)[:, 0:4].copy().view(np.float32).astype(np.float64)[:, 0]
         exact = float((yd * d * s).sum() - (yd * dm * m).sum())
         assert abs(exact - oracle.dot(TYPE_Q5_K, 512, w5[r], xk[0])) <= 1e-5 * max(1.0, abs(exact))
+    w6 = synth.random_q6_K(3, 512, np.random.default_rng(8))
+    for r in range(3):
+        for c in range(3):
+            s, ch = oracle.block_dots_q6_K(512, w6[r], xk[c])
+            assert np.array_equal(ch.astype(np.int64).sum(axis=1), s.astype(np.int64))
+            d = w6[r].reshape(-1, 210)[:, 208:210].copy().view(np.float16).astype(np.float64)[:, 0]
+            yd = xk[c].reshape(-1, 292)[:, 0:4].copy().view(np.float32).astype(np.float64)[:, 0]
+            exact = float((yd * d * s).sum())
+            assert abs(exact - oracle.dot(TYPE_Q6_K, 512, w6[r], xk[c])) <= 1e-5 * max(1.0, abs(exact))
 
 
 def test_synth_q8_0_matches_reference_quantizer(oracle):
