@@ -352,14 +352,16 @@ int quantize_activation(DeviceCtx* d, uint32_t wtype, const float* input, int64_
         a->amin = reinterpret_cast<__half*>(base + off_amin);
         e = q5 ? launch_quantize_q8_K_operand(input, a->xq, static_cast<float*>(a->scale), a->amin, M, K, K, a->ldd, s)
                : launch_quantize_q8_0_operand(input, a->xq, static_cast<__half*>(a->scale), M, K, K, a->ldd, s);
-        int rc = make_map(d, &a->tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->xq, K, M, K * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+        const uint32_t xr = (uint32_t)gemm_activation_rows(wtype);  // one CTA's rows of an output tile
+        int rc = make_map(d, &a->tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->xq, K, M, K * 2, 64, xr, CU_TENSOR_MAP_SWIZZLE_128B);
         if (!rc && q5) {
-            rc = make_map(d, &a->tmXs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->amin, nb * 16, M, nb * 32, 16, 128,
+            rc = make_map(d, &a->tmXs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->amin, nb * 16, M, nb * 32, 16, xr,
                           CU_TENSOR_MAP_SWIZZLE_32B);
-            if (!rc) rc = make_map(d, &a->tmDx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a->scale, M, nb, a->ldd * 4, 128, 1,
+            if (!rc) rc = make_map(d, &a->tmDx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a->scale, M, nb, a->ldd * 4,
+                                   (uint32_t)gemm_tile_activation_rows(wtype), 1,
                                    CU_TENSOR_MAP_SWIZZLE_NONE);
         } else if (!rc) {
-            rc = make_map(d, &a->tmXs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->scale, nb, M, a->ldd * 2, 16, 128,
+            rc = make_map(d, &a->tmXs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->scale, nb, M, a->ldd * 2, 16, xr,
                           CU_TENSOR_MAP_SWIZZLE_32B);
             a->tmDx = a->tmX;
         }
@@ -489,7 +491,8 @@ int run_gemm(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, co
     op.tma_store = 0;
     op.tm_y = op.tm[0];
     if (!dump && (reinterpret_cast<uintptr_t>(output) & 15u) == 0 && (ldy % 4) == 0 && (row_count % 4) == 0) {
-        if (make_map(d, &op.tm_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, output, row_count, (uint64_t)a->M, ldy * 4, 32, 64,
+        if (make_map(d, &op.tm_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, output, row_count, (uint64_t)a->M, ldy * 4, 32,
+                     (uint32_t)gemm_store_rows(w->type),
                      CU_TENSOR_MAP_SWIZZLE_NONE) == PXQ_OK)
             op.tma_store = 1;
         else

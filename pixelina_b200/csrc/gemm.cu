@@ -1,137 +1,156 @@
-// gemm.cu -- large-M quantized GEMM on the 5th-generation tensor cores.
+// gemm.cu -- large-M quantized GEMM on the 5th-generation tensor cores,
+// one CTA pair per output tile.
 //
 // Computes Y[m, n] = sum over K-blocks b of  s(m,n,b) * I(m,n,b)
 // where I is the exact integer dot of one block of quants and s the product
 // of the block scales -- the arithmetic of pix_dot_q8_0
-// (src/kernels_quant.cpp:339-365) and pix_dot_q5_K (:163-254) as driven by
-// cpu_quant_matmul (:389-400), for every (activation row m, weight row n).
+// (src/kernels_quant.cpp:339-365), pix_dot_q5_K (:163-254) and pix_dot_q6_K
+// (:256-337) as driven by cpu_quant_matmul (:389-400), for every
+// (activation row m, weight row n).
 //
 // Design (sm_100a):
 //   * Operands are exact fp16 copies of the int8 quants (activations from
 //     quantize.cu, weights from the one-time repack in repack.cu).  A
 //     kind::f16 tcgen05.mma with fp32 accumulation computes each block dot
-//     exactly (|I| <= 32*127*127 for Q8_0, <= 64*127*1953 < 2^24 for a Q5_K
-//     64-value chunk) and hands the drain a float.  (kind::i8 runs the MMA
-//     twice as fast but needs an int->float conversion per element per block
-//     on the CUDA cores, which bound this kernel.)
-//   * Orientation: TMEM lanes are WEIGHT rows (the MMA's M side), TMEM
-//     columns are ACTIVATION rows.  Per-weight-row scales are then per-thread
-//     scalars, and the 32 lanes of a warp store 32 consecutive outputs.
-//   * Q8_0: the per-block scale product dW[n,b]*dX[m,b] is itself computed by
-//     the tensor core -- a K=16 MMA of a one-hot weight-scale tile (dW at
-//     position b%16) against the activations' 16-block fp16 scale tile, exact
-//     because fp16*fp16 fits fp32 -- so the drain is one FMA per element per
-//     block and reads no scale from shared memory.
-//   * Q5_K: 6-bit sub-block scales are folded into the weight operand
-//     (sc*q5 <= 1953, exact in fp16), so every 64-value chunk dot is exact in
-//     the fp32 accumulator, and the four chunks of a super-block, which share
-//     its scale dW*dX, accumulate into one TMEM slot: one drain per
-//     super-block.  Their sum is exact while it stays below 2^24 in magnitude
+//     exactly (|I| <= 32*127*127 for Q8_0, < 2^24 for a K-quant 64-value
+//     chunk with the sub-block scale folded in) and hands the drain a float.
+//     (kind::i8 runs the MMA twice as fast but needs an int->float
+//     conversion per element per block on the CUDA cores.)
+//   * CTA pairs (cta_group::2): the two CTAs of a cluster share every MMA.
+//     The pair's tile is 256 weight rows (the MMA's M; each CTA stages and
+//     accumulates its 128) by TMP activation rows (the MMA's N; each CTA
+//     stages TMP/2 of them and receives all TMP columns in its TMEM).  Per
+//     FLOP each CTA moves half the operand bytes of a one-CTA 128-row tile,
+//     which is what bounds that design: the operand stream into shared
+//     memory and the MMA's reads of it share one memory.
+//     The even CTA issues the MMAs; both CTAs' TMA loads report on its stage
+//     barriers; its commits arrive on the barriers of both CTAs; the odd
+//     CTA's drain warps release accumulator slots on the even CTA's
+//     barriers.
+//   * Orientation: TMEM lanes are WEIGHT rows, TMEM columns are ACTIVATION
+//     rows.  Per-weight-row scales are then per-thread scalars, and the 32
+//     lanes of a warp store 32 consecutive outputs.
+//   * Q8_0 (TMP = 128, four 128-column slots): the per-block scale product
+//     dW[n,b]*dX[m,b] is itself computed by the tensor core -- a K=16 MMA of
+//     a one-hot weight-scale tile (dW at position b%16) against the
+//     activations' 16-block fp16 scale tile, exact because fp16*fp16 fits
+//     fp32 -- so the drain is one FMA per element per block.
+//   * Q5_K (TMP = 256, two 256-column slots): 6-bit sub-block scales are
+//     folded into the weight operand (sc*q5 <= 1953, exact in fp16), so every
+//     64-value chunk dot is exact in the fp32 accumulator, and the four
+//     chunks of a super-block, which share its scale dW*dX, accumulate into
+//     one slot.  Their sum is exact while it stays below 2^24 in magnitude
 //     (always, for real activations; the reference rounds its int32 sum to
-//     fp32 once, the tensor core at most at each chunk boundary beyond that).
-//     The block-dot dump (pxq_gemm_block_dots) drains every chunk on its own,
-//     so the exact int32 chunk dots stay checkable.  The min term
-//     sum_j m_j*bsum_j is a K=16 MMA per super-block on exact (hi, lo) splits,
-//     drained first.
-//   * Q6_K (pix_dot_q6_K, :256-337): the 8-bit scale and the -32 offset fold
-//     into v = sc*(q6-32), |v| <= 4096 -- 13 bits, one more than fp16 holds
-//     for odd values.  The repack splits v into an even part (exact in fp16)
-//     and its parity bit, two operand planes that two MMAs per K step
-//     accumulate into the same TMEM slot, so the chunk dots stay exact
-//     integers.  No min term; one drain per super-block.
+//     fp32 once).  The min term sum_j m_j*bsum_j is a K=16 MMA per
+//     super-block on exact (hi, lo) splits into the other slot; the two slots
+//     swap roles every super-block, and the min MMA is issued after the
+//     third chunk stage, so the drain of the previous super-block's chunk
+//     sum overlaps three stages of MMAs.
+//   * Q6_K (TMP = 256, two slots alternating per super-block): the 8-bit
+//     scale and the -32 offset fold into v = sc*(q6-32), |v| <= 4096 -- odd
+//     values above 2048 need one bit more than fp16 has, so the repack keeps
+//     an even plane (exact in fp16) and a parity plane, two MMAs per K step
+//     into the same slot.  No min term; one drain per super-block.
+//   * The block-dot dump (pxq_gemm_block_dots) drains every block / chunk /
+//     min sum on its own, so the exact int32 dots stay checkable.
 //   * Warp roles (12 warps, 3 warpgroups): warpgroups 0-1 drain TMEM (warp w
-//     reads lane quadrant w%4 and column half w/4) with 232 registers
-//     (setmaxnreg); warpgroup 2 runs the TMA producer (warp 8) and the
-//     single-thread MMA issuer (warp 9) with 40.  Persistent CTAs walk
-//     128x128 output tiles; four 128-column TMEM slots let the MMA run up to
-//     four items ahead of the drain.
+//     reads lane quadrant w%4 and column half w/4) with 224-232 registers
+//     (setmaxnreg); warpgroup 2 runs the TMA producer (warp 8, every CTA)
+//     and the single-thread MMA issuer (warp 9 of the even CTA) with 40-56,
+//     within the 384*168 registers the block launches with.
+//     Persistent pairs walk the output tiles.
 //   * Every mbarrier wait is bounded (pxq_device.cuh).  Every CTA loads its
-//     own tiles from this GPU's HBM; no cluster broadcast of any kind.
+//     own tiles from this GPU's HBM into its own shared memory; no cluster
+//     broadcast of any load.
 #include <cuda.h>
+#include <mutex>
 #include "pxq_device.cuh"
 #include "pxq_internal.h"
 
 namespace pxq {
 namespace {
 
-constexpr int TN = 128;                // weight rows per tile (TMEM lanes, MMA M)
-constexpr int TM = 128;                // activation rows per tile (TMEM columns, MMA N)
+constexpr int TN = 128;                // weight rows per CTA (TMEM lanes); the pair's MMA M is 256
 constexpr int BK = 64;                 // fp16 K elements per stage (128-byte rows)
 constexpr int W_BYTES = TN * BK * 2;   // 16 KB
-constexpr int X_BYTES = TM * BK * 2;   // 16 KB
-constexpr int SW32_TILE = 128 * 32;    // [128][16] fp16 tile, 32-byte swizzle: 4 KB
+constexpr int SW32_W = TN * 32;        // [128][16] fp16 tile, 32-byte swizzle: 4 KB
 constexpr int DRAIN_WARPS = 8;
 constexpr int PRODUCER_WARP = 8;
 constexpr int MMA_WARP = 9;
 constexpr int THREADS = 384;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr int SLOTS = 4;               // TMEM slots of 128 columns
 constexpr int MAX_STAGES = 6;
-constexpr uint32_t IDESC = idesc_f16_f32(TN, TM);
-
-// output staging for the TMA-store epilogue: per drain warp [64 activation rows][32 weight rows] fp32
-constexpr int STAGING = 2 * 64 * TN * 4;                                  // 64 KB
-// Q8_0 stage: W | X | one-hot weight scales for the stage's 2 blocks | activation scales (16 blocks)
-constexpr int Q80_STAGES = 3;
-constexpr int Q80_STAGE = W_BYTES + X_BYTES + 2 * SW32_TILE + SW32_TILE;  // 44 KB
-// Q5_K stage: W | X;  super-block entries: Wmin | Xmin | dW | dminW | dX
-constexpr int Q5_STAGES = 4;
-constexpr int Q5_STAGE = W_BYTES + X_BYTES;                                // 32 KB
-constexpr int Q5_SB_ENTRY = 2 * SW32_TILE + 3 * 512;                      // 9.5 KB
-constexpr int Q5_SB_DEPTH = 2;
-// Q6_K stage: W even part | W parity part | X;  super-block entries: dW | dX
-constexpr int Q6_STAGES = 3;
-constexpr int Q6_STAGE = 2 * W_BYTES + X_BYTES;                            // 48 KB
-constexpr int Q6_SB_ENTRY = 2 * 512;
+constexpr int DEPTH = 2;               // super-block entry and min-operand rings
 
 template <uint32_t TYPE>
 struct Cfg;
 template <>
 struct Cfg<kTypeQ8_0> {
-    static constexpr int STAGES = Q80_STAGES;
-    static constexpr int STAGE = Q80_STAGE;
-    static constexpr int SB_ENTRY = 0;
-    static constexpr int SB_REGION = 0;
+    // one CTA per tile: a Q8_0 block is too little MMA work to cover a
+    // hand-off between two SMs per block
+    static constexpr int CG = 1, TMP = 128, SLOTS = 4, STAGES = 3;
+    static constexpr uint32_t PRODUCER_REGS = 40, DRAIN_REGS = 232;
+    static constexpr int SROWS = 64;  // activation rows per TMA store of a drain warp
+    static constexpr int XR = TMP / CG, X_BYTES = XR * BK * 2, SW32_X = XR * 32;
+    // stage: W | X | one-hot weight scales of the stage's 2 blocks | activation scales (16 blocks)
+    static constexpr int STAGE = W_BYTES + X_BYTES + 2 * SW32_W + SW32_X;  // 44 KB
+    static constexpr int MIN_ENTRY = 0, SB_ENTRY = 0;
     static constexpr int OFF_DW = 0, OFF_DMW = 0, OFF_DX = 0;  // no super-block entries
 };
 template <>
 struct Cfg<kTypeQ5_K> {
-    static constexpr int STAGES = Q5_STAGES;
-    static constexpr int STAGE = Q5_STAGE;
-    static constexpr int SB_ENTRY = Q5_SB_ENTRY;
-    static constexpr int SB_REGION = Q5_SB_ENTRY * Q5_SB_DEPTH;
-    static constexpr int OFF_DW = 2 * SW32_TILE, OFF_DMW = OFF_DW + 512, OFF_DX = OFF_DW + 1024;  // in an entry
+    static constexpr int CG = 2, TMP = 256, SLOTS = 2, STAGES = 4;
+    static constexpr uint32_t PRODUCER_REGS = 56, DRAIN_REGS = 224;
+    static constexpr int SROWS = 64;
+    static constexpr int XR = TMP / CG, X_BYTES = XR * BK * 2, SW32_X = XR * 32;
+    static constexpr int STAGE = W_BYTES + X_BYTES;                          // 32 KB
+    static constexpr int MIN_ENTRY = SW32_W + SW32_X;                        // weight | activation min operands
+    static constexpr int SB_ENTRY = 2048;                                    // dW | dminW | dX (TMP floats)
+    static constexpr int OFF_DW = 0, OFF_DMW = 512, OFF_DX = 1024;
 };
 template <>
 struct Cfg<kTypeQ6_K> {
-    static constexpr int STAGES = Q6_STAGES;
-    static constexpr int STAGE = Q6_STAGE;
-    static constexpr int SB_ENTRY = Q6_SB_ENTRY;
-    static constexpr int SB_REGION = Q6_SB_ENTRY * Q5_SB_DEPTH;
-    static constexpr int OFF_DW = 0, OFF_DMW = 0, OFF_DX = 512;
+    static constexpr int CG = 2, TMP = 256, SLOTS = 2, STAGES = 3;
+    static constexpr uint32_t PRODUCER_REGS = 56, DRAIN_REGS = 224;
+    static constexpr int SROWS = 64;
+    static constexpr int XR = TMP / CG, X_BYTES = XR * BK * 2, SW32_X = XR * 32;
+    static constexpr int STAGE = 2 * W_BYTES + X_BYTES;                      // even | parity | X: 48 KB
+    static constexpr int MIN_ENTRY = 0;
+    static constexpr int SB_ENTRY = 2048;                                    // dW | dX (TMP floats)
+    static constexpr int OFF_DW = 0, OFF_DMW = 0, OFF_DX = 1024;
 };
 
 template <uint32_t TYPE>
-__host__ __device__ constexpr int off_staging()
-{
-    return Cfg<TYPE>::STAGES * Cfg<TYPE>::STAGE + Cfg<TYPE>::SB_REGION;
-}
+__host__ __device__ constexpr int off_min() { return Cfg<TYPE>::STAGES * Cfg<TYPE>::STAGE; }
 template <uint32_t TYPE>
-__host__ __device__ constexpr int off_bar()
-{
-    return off_staging<TYPE>() + STAGING;
-}
-constexpr int NUM_BARS = 2 * MAX_STAGES + 2 * Q5_SB_DEPTH + 2 * SLOTS;  // full/empty, sfull/sempty, tfull/tempty
+__host__ __device__ constexpr int off_sb() { return off_min<TYPE>() + DEPTH * Cfg<TYPE>::MIN_ENTRY; }
 template <uint32_t TYPE>
-__host__ __device__ constexpr int smem_bytes()
-{
-    return off_bar<TYPE>() + NUM_BARS * 8 + 16 + 1024;
-}
-static_assert(Q80_STAGES <= MAX_STAGES && Q5_STAGES <= MAX_STAGES && Q6_STAGES <= MAX_STAGES, "stage count");
+__host__ __device__ constexpr int off_staging() { return off_sb<TYPE>() + DEPTH * Cfg<TYPE>::SB_ENTRY; }
+// output staging for the TMA-store epilogue: per drain warp [SROWS activation rows][32 weight rows] fp32
+template <uint32_t TYPE>
+__host__ __device__ constexpr int staging_bytes() { return DRAIN_WARPS * Cfg<TYPE>::SROWS * 32 * 4; }
+template <uint32_t TYPE>
+__host__ __device__ constexpr int off_bar() { return off_staging<TYPE>() + staging_bytes<TYPE>(); }
+// full/empty, min full/empty, entry full/empty, slot full/empty, MMA drain-out
+constexpr int NUM_BARS = 2 * MAX_STAGES + 4 * DEPTH + 2 * 4 + 1;
+template <uint32_t TYPE>
+__host__ __device__ constexpr int smem_bytes() { return off_bar<TYPE>() + NUM_BARS * 8 + 16 + 1024; }
+
+// register split: two drain warpgroups and the producer warpgroup within the
+// 384 x 168 registers the block launches with
+template <uint32_t TYPE>
+constexpr bool regs_fit() { return 256 * Cfg<TYPE>::DRAIN_REGS + 128 * Cfg<TYPE>::PRODUCER_REGS <= 384 * 168; }
+static_assert(regs_fit<kTypeQ8_0>() && regs_fit<kTypeQ5_K>() && regs_fit<kTypeQ6_K>(), "setmaxnreg split");
+static_assert(Cfg<kTypeQ8_0>::STAGES <= MAX_STAGES && Cfg<kTypeQ5_K>::STAGES <= MAX_STAGES &&
+                  Cfg<kTypeQ6_K>::STAGES <= MAX_STAGES, "stage count");
 static_assert(smem_bytes<kTypeQ8_0>() <= 232448, "Q8_0 shared memory");
 static_assert(smem_bytes<kTypeQ5_K>() <= 232448, "Q5_K shared memory");
 static_assert(smem_bytes<kTypeQ6_K>() <= 232448, "Q6_K shared memory");
-static_assert(Q6_STAGE % 1024 == 0 && Q5_STAGE % 1024 == 0, "128B-swizzled tiles need 1024-byte alignment");
+static_assert(Cfg<kTypeQ8_0>::STAGE % 1024 == 0 && Cfg<kTypeQ5_K>::STAGE % 1024 == 0 && Cfg<kTypeQ6_K>::STAGE % 1024 == 0 &&
+                  Cfg<kTypeQ5_K>::MIN_ENTRY % 1024 == 0 && Cfg<kTypeQ5_K>::SB_ENTRY % 1024 == 0,
+              "swizzled tiles need 1024-byte alignment");
+static_assert(Cfg<kTypeQ8_0>::SLOTS * Cfg<kTypeQ8_0>::TMP <= (int)TMEM_COLS && Cfg<kTypeQ5_K>::SLOTS * Cfg<kTypeQ5_K>::TMP <= (int)TMEM_COLS,
+              "TMEM columns");
 
 struct Params {
     int64_t M, N, K;
@@ -144,19 +163,113 @@ struct Params {
     int tma_store;  // 1: epilogue through shared memory + TMA store (tmY)
 };
 
+// tcgen05 and stage-load forms for one CTA per tile (CG = 1) or a CTA pair
+// (CG = 2); a kernel uses one form throughout, as tcgen05 requires.
+template <int CG>
+struct Grp;
+template <>
+struct Grp<1> {
+    static __device__ __forceinline__ void alloc(uint32_t* dst, uint32_t n) { tmem_alloc(dst, n); }
+    static __device__ __forceinline__ void relinquish() { tmem_relinquish(); }
+    static __device__ __forceinline__ void dealloc(uint32_t t, uint32_t n) { tmem_dealloc(t, n); }
+    static __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc)
+    {
+        mma_f16(d, a, b, idesc, acc);
+    }
+    static __device__ __forceinline__ void commit(uint64_t* bar) { mma_commit(bar); }
+    static __device__ __forceinline__ void commit_local(uint64_t* bar) { mma_commit(bar); }
+    // stage load reporting on this CTA's barrier
+    static __device__ __forceinline__ void load(void* dst, const void* map, uint64_t* bar, uint32_t, int32_t c0, int32_t c1)
+    {
+        tma_load_2d(dst, map, bar, c0, c1);
+    }
+    static __device__ __forceinline__ void sync() { __syncthreads(); }
+};
+template <>
+struct Grp<2> {
+    static __device__ __forceinline__ void alloc(uint32_t* dst, uint32_t n) { tmem_alloc_pair(dst, n); }
+    static __device__ __forceinline__ void relinquish() { tmem_relinquish_pair(); }
+    static __device__ __forceinline__ void dealloc(uint32_t t, uint32_t n) { tmem_dealloc_pair(t, n); }
+    static __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc)
+    {
+        mma_f16_pair(d, a, b, idesc, acc);
+    }
+    static __device__ __forceinline__ void commit(uint64_t* bar) { mma_commit_pair(bar); }
+    static __device__ __forceinline__ void commit_local(uint64_t* bar) { mma_commit_pair_local(bar); }
+    // stage load reporting on the even CTA's barrier (cluster address)
+    static __device__ __forceinline__ void load(void* dst, const void* map, uint64_t*, uint32_t bar, int32_t c0, int32_t c1)
+    {
+        tma_load_2d_pair(dst, map, bar, c0, c1);
+    }
+    static __device__ __forceinline__ void sync() { cluster_sync(); }
+};
+
 __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) { return smem_desc(saddr, 16, 1024, 2); }
 __device__ __forceinline__ uint64_t desc_sw32(uint32_t saddr) { return smem_desc(saddr, 16, 256, 6); }
 
+// K-quant accumulators use the 16x256b TMEM layout: a drain warp covers its
+// 32 lanes x 128 columns as acc[((ch*2 + lh)*8 + k)*4 + 2h + c] = lane
+// 16lh + 8h + t/4, column 64ch + 8k + 2(t%4) + c (t = lane id).  Each thread
+// then needs 32 per-column activation scales (not 128) and 4 per-lane weight
+// scales.
+__host__ __device__ constexpr int split_idx(int ch, int lh, int k, int h, int c) { return (((ch * 2 + lh) * 8 + k) * 4) + 2 * h + c; }
+
+// acc += (dx[column] * w[lane]) * v over one drained item (taddr: the warp's
+// lane quadrant and first column; dx: the warp's first column's scale;
+// w[2lh + h]: the scale of lane 16lh + 8h + t/4).
+__device__ __forceinline__ void drain_split(float (&acc)[128], uint32_t taddr, const float* dx, const float (&w)[4], uint32_t t)
+{
+#pragma unroll
+    for (int ch = 0; ch < 2; ch++) {
+        float2 d[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) d[k] = *reinterpret_cast<const float2*>(dx + 64 * ch + 8 * k + 2 * (t & 3));
+#pragma unroll
+        for (int lh = 0; lh < 2; lh++) {
+            uint32_t v[32];
+            tmem_ld16x256_x8(taddr + ((16u * lh) << 16) + 64u * ch, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    float s0, s1;
+                    fmul2(s0, s1, d[k].x, d[k].y, w[2 * lh + h], w[2 * lh + h]);
+                    const int i = split_idx(ch, lh, k, h, 0);
+                    ffma2(acc[i], acc[i + 1], s0, s1, __uint_as_float(v[4 * k + 2 * h]), __uint_as_float(v[4 * k + 2 * h + 1]));
+                }
+            }
+        }
+    }
+}
+
+// Store one drained item as raw block dots (pxq_gemm_block_dots).
+template <int HC>
+__device__ __forceinline__ void drain_dump(uint32_t taddr, const Params& p, int64_t item, int64_t m_first, int64_t n)
+{
+#pragma unroll 1
+    for (int g = 0; g < HC / 32; g++) {
+        uint32_t v[32];
+        tmem_ld32(taddr + 32u * g, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const int64_t m = m_first + 32 * g + j;
+            if (n < p.N && m < p.M) p.dump[(item * p.M + m) * p.N + n] = __uint_as_float(v[j]);
+        }
+    }
+}
+
 // tensor maps:
 //   tmW   weight operand fp16 [N][K] (Q6_K: [N][2K])  box {64, 128}  128B swizzle
-//   tmX   activation operand fp16 [M][K]        box {64, 128}  128B swizzle
+//   tmX   activation operand fp16 [M][K]               box {64, TMP/2} 128B swizzle
 //   Q8_0: tmWs  one-hot weight scales fp16 [N][nb*16]   box {16, 128} 32B swizzle
-//         tmXs  activation scales fp16 [M][nb]          box {16, 128} 32B swizzle
+//         tmXs  activation scales fp16 [M][nb]          box {16, TMP/2} 32B swizzle
 //   Q5_K: tmWs  weight min operand fp16 [N][nsb*16]     box {16, 128} 32B swizzle
-//         tmXs  activation min operand fp16 [M][nsb*16] box {16, 128} 32B swizzle
+//         tmXs  activation min operand fp16 [M][nsb*16] box {16, TMP/2} 32B swizzle
 //         tmD   weight d   fp32 [nsb][N4]  box {128, 1}
 //         tmDm  weight dmin fp32 [nsb][N4] box {128, 1}
-//         tmDx  activation d fp32 [nsb][M4] box {128, 1}
+//         tmDx  activation d fp32 [nsb][M4] box {TMP, 1}
 //   Q6_K: tmD, tmDx as for Q5_K (the others unused)
 template <uint32_t TYPE, bool DUMP>
 __global__ void __launch_bounds__(THREADS, 1)
@@ -166,118 +279,151 @@ __global__ void __launch_bounds__(THREADS, 1)
            const __grid_constant__ CUtensorMap tmDx, const __grid_constant__ CUtensorMap tmY, const Params p)
 {
     using C = Cfg<TYPE>;
+    using G = Grp<C::CG>;
+    constexpr int CG = C::CG;
     constexpr bool Q8 = TYPE == kTypeQ8_0;
+    constexpr bool Q5 = TYPE == kTypeQ5_K;
     constexpr bool Q6 = TYPE == kTypeQ6_K;
-    constexpr int STAGES = C::STAGES;
+    constexpr int TMP = C::TMP, XR = C::XR, SLOTS = C::SLOTS, STAGES = C::STAGES;
+    constexpr int HC = TMP / 2;  // TMEM columns per drain warp
+    constexpr bool SPLIT = !Q8;  // K-quant accumulators in the 16x256b layout (drain_split)
+    static_assert(!SPLIT || HC == 128, "split layout covers 128 columns per warp");
+    constexpr uint32_t IDESC = idesc_f16_f32(CG * TN, TMP);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + off_bar<TYPE>());
-    uint64_t* full = bars;
-    uint64_t* empty = bars + MAX_STAGES;
-    uint64_t* sfull = bars + 2 * MAX_STAGES;
-    uint64_t* sempty = sfull + Q5_SB_DEPTH;
-    uint64_t* tfull = sempty + Q5_SB_DEPTH;
-    uint64_t* tempty = tfull + SLOTS;
+    uint64_t* full = bars;                   // even CTA: stage loaded (both CTAs' bytes)
+    uint64_t* empty = bars + MAX_STAGES;     // stage consumed (both CTAs)
+    uint64_t* mfull = empty + MAX_STAGES;    // even CTA: min operands loaded (both CTAs' bytes)
+    uint64_t* mempty = mfull + DEPTH;        // min operands consumed (both CTAs)
+    uint64_t* sfull = mempty + DEPTH;        // this CTA's super-block scale entry loaded
+    uint64_t* sempty = sfull + DEPTH;        // ... and read by this CTA's drain warps
+    uint64_t* tfull = sempty + DEPTH;        // accumulator slot complete (both CTAs)
+    uint64_t* tempty = tfull + 4;            // even CTA: slot drained by both CTAs
+    uint64_t* mma_done = tempty + 4;         // even CTA: every issued MMA finished (exit path)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
     volatile uint32_t* abort_flag = tmem_slot + 1;
-    uint8_t* sb_region = smem + STAGES * C::STAGE;
+    uint8_t* min_region = smem + off_min<TYPE>();
+    uint8_t* sb_region = smem + off_sb<TYPE>();
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
+    const bool leader = rank == 0;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < STAGES; i++) {
+        for (int i = 0; i < MAX_STAGES; i++) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
-        for (int i = 0; i < Q5_SB_DEPTH; i++) {
+        for (int i = 0; i < DEPTH; i++) {
+            mbar_init(&mfull[i], 1);
+            mbar_init(&mempty[i], 1);
             mbar_init(&sfull[i], 1);
-            mbar_init(&sempty[i], Q6 ? DRAIN_WARPS : DRAIN_WARPS + 1);  // drain warps (+ the MMA thread: Q5_K min operands)
+            mbar_init(&sempty[i], DRAIN_WARPS);
         }
-        for (int i = 0; i < SLOTS; i++) {
+        for (int i = 0; i < 4; i++) {
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], DRAIN_WARPS);
+            mbar_init(&tempty[i], CG * DRAIN_WARPS);  // the drain warps of every CTA of the tile
         }
+        mbar_init(mma_done, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
     if (warp == 0) {
-        tmem_alloc(tmem_slot, TMEM_COLS);
-        tmem_relinquish();
+        G::alloc(tmem_slot, TMEM_COLS);
+        G::relinquish();
     }
     if (warp == PRODUCER_WARP && lane == 0) {
         tma_prefetch_desc(&tmW);
         tma_prefetch_desc(&tmX);
-        tma_prefetch_desc(&tmWs);
-        tma_prefetch_desc(&tmXs);
+        if (!Q6) {
+            tma_prefetch_desc(&tmWs);
+            tma_prefetch_desc(&tmXs);
+        }
         if (p.tma_store) tma_prefetch_desc(&tmY);
         if (!Q8) {
             tma_prefetch_desc(&tmD);
-            tma_prefetch_desc(&tmDm);
             tma_prefetch_desc(&tmDx);
         }
+        if (Q5) tma_prefetch_desc(&tmDm);
     }
+    // barriers initialised and TMEM allocated in both CTAs before any cross-CTA traffic
     tc_fence_before();
-    __syncthreads();
+    G::sync();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    const int64_t mt_count = (p.M + TM - 1) / TM;
-    const int64_t nt_count = (p.N + TN - 1) / TN;
+    const int64_t mt_count = (p.M + TMP - 1) / TMP;
+    const int64_t nt_count = (p.N + CG * TN - 1) / (CG * TN);
     const int64_t tiles = mt_count * nt_count;
-    const int64_t nb = Q8 ? p.K / kQK8_0 : p.K / kQKK;  // blocks (Q8_0) or super-blocks (Q5_K)
+    const int64_t pair = CG == 2 ? (int64_t)cluster_id_x() : (int64_t)blockIdx.x;
+    const int64_t pairs = CG == 2 ? (int64_t)cluster_count_x() : (int64_t)gridDim.x;
+    const int64_t nb = Q8 ? p.K / kQK8_0 : p.K / kQKK;  // blocks (Q8_0) or super-blocks
     const int64_t nchunks = (p.K + BK - 1) / BK;
     uint32_t* status = p.status;
 
     if (warp >= 8) {
-        regs_dec<40>();
+        regs_dec<C::PRODUCER_REGS>();
         if (warp == PRODUCER_WARP && lane == 0) {
-            int stage = 0;
-            uint32_t ph = 0;
-            int se = 0;
-            uint32_t sph = 0;
-            for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-                const int32_t m0 = (int32_t)((tile % mt_count) * TM);
-                const int32_t n0 = (int32_t)(p.n_first + (tile / mt_count) * TN);
+            // the even CTA's stage and min barriers, as cluster addresses
+            const uint32_t full0 = CG == 2 ? cluster_map(smem_u32(full), 0) : 0u;
+            const uint32_t mfull0 = CG == 2 ? cluster_map(smem_u32(mfull), 0) : 0u;
+            int stage = 0, se = 0, me = 0;
+            uint32_t ph = 0, sph = 0, mph = 0;
+            for (int64_t tile = pair; tile < tiles; tile += pairs) {
+                const int32_t m0 = (int32_t)((tile % mt_count) * TMP);
+                const int32_t mc = m0 + (int32_t)(rank * XR);
+                const int32_t nc = (int32_t)(p.n_first + (tile / mt_count) * CG * TN + rank * TN);
                 for (int64_t kc = 0; kc < nchunks; kc++) {
                     if (!Q8 && kc % 4 == 0) {
-                        if (!mbar_wait(&sempty[se], sph ^ 1u, abort_flag, status, kDevTimeoutScaleEmpty)) goto done;
-                        uint8_t* e = sb_region + se * Cfg<TYPE>::SB_ENTRY;
                         const int32_t sb = (int32_t)(kc / 4);
-                        mbar_expect_tx(&sfull[se], Cfg<TYPE>::SB_ENTRY);
-                        if (!Q6) {
-                            tma_load_2d(e, &tmWs, &sfull[se], sb * 16, n0);
-                            tma_load_2d(e + SW32_TILE, &tmXs, &sfull[se], sb * 16, m0);
-                            tma_load_2d(e + C::OFF_DMW, &tmDm, &sfull[se], n0, sb);
-                        }
-                        tma_load_2d(e + C::OFF_DW, &tmD, &sfull[se], n0, sb);
+                        // this CTA's scales for its drain
+                        if (!mbar_wait(&sempty[se], sph ^ 1u, abort_flag, status, kDevTimeoutScaleEmpty)) goto done;
+                        uint8_t* e = sb_region + se * C::SB_ENTRY;
+                        mbar_expect_tx(&sfull[se], (Q5 ? 2 * 512 : 512) + TMP * 4);
+                        tma_load_2d(e + C::OFF_DW, &tmD, &sfull[se], nc, sb);
+                        if (Q5) tma_load_2d(e + C::OFF_DMW, &tmDm, &sfull[se], nc, sb);
                         tma_load_2d(e + C::OFF_DX, &tmDx, &sfull[se], m0, sb);
-                        if (++se == Q5_SB_DEPTH) {
+                        if (++se == DEPTH) {
                             se = 0;
                             sph ^= 1u;
+                        }
+                        if (Q5) {
+                            // this CTA's halves of the min-term operands
+                            if (!mbar_wait(&mempty[me], mph ^ 1u, abort_flag, status, kDevTimeoutScaleEmpty)) goto done;
+                            uint8_t* mn = min_region + me * C::MIN_ENTRY;
+                            if (leader) mbar_expect_tx(&mfull[me], CG * C::MIN_ENTRY);
+                            G::load(mn, &tmWs, &mfull[me], mfull0 + 8u * me, sb * 16, nc);
+                            G::load(mn + SW32_W, &tmXs, &mfull[me], mfull0 + 8u * me, sb * 16, mc);
+                            if (++me == DEPTH) {
+                                me = 0;
+                                mph ^= 1u;
+                            }
                         }
                     }
                     if (!mbar_wait(&empty[stage], ph ^ 1u, abort_flag, status, kDevTimeoutEmpty)) goto done;
                     uint8_t* st = smem + stage * C::STAGE;
+                    const uint32_t fb = full0 + 8u * stage;
+                    uint64_t* fl = &full[stage];
+                    const int32_t kx = (int32_t)(kc * BK);
                     if (Q8) {
                         const int nblk = (2 * kc + 1 < nb) ? 2 : 1;
-                        mbar_expect_tx(&full[stage], W_BYTES + X_BYTES + (nblk + 1) * SW32_TILE);
-                        tma_load_2d(st, &tmW, &full[stage], (int32_t)(kc * BK), n0);
-                        tma_load_2d(st + W_BYTES, &tmX, &full[stage], (int32_t)(kc * BK), m0);
+                        if (leader) mbar_expect_tx(fl, CG * (W_BYTES + C::X_BYTES + nblk * SW32_W + C::SW32_X));
+                        G::load(st, &tmW, fl, fb, kx, nc);
+                        G::load(st + W_BYTES, &tmX, fl, fb, kx, mc);
                         for (int b = 0; b < nblk; b++)
-                            tma_load_2d(st + W_BYTES + X_BYTES + b * SW32_TILE, &tmWs, &full[stage],
-                                        (int32_t)((2 * kc + b) * 16), n0);
-                        tma_load_2d(st + W_BYTES + X_BYTES + 2 * SW32_TILE, &tmXs, &full[stage],
-                                    (int32_t)(((2 * kc) / 16) * 16), m0);
+                            G::load(st + W_BYTES + C::X_BYTES + b * SW32_W, &tmWs, fl, fb, (int32_t)((2 * kc + b) * 16), nc);
+                        G::load(st + W_BYTES + C::X_BYTES + 2 * SW32_W, &tmXs, fl, fb, (int32_t)(((2 * kc) / 16) * 16), mc);
                     } else if (Q6) {
                         // chunk kc's even and parity planes sit side by side in the [N][2K] operand
-                        mbar_expect_tx(&full[stage], 2 * W_BYTES + X_BYTES);
-                        tma_load_2d(st, &tmW, &full[stage], (int32_t)(kc * 2 * BK), n0);
-                        tma_load_2d(st + W_BYTES, &tmW, &full[stage], (int32_t)(kc * 2 * BK + BK), n0);
-                        tma_load_2d(st + 2 * W_BYTES, &tmX, &full[stage], (int32_t)(kc * BK), m0);
+                        if (leader) mbar_expect_tx(fl, CG * (2 * W_BYTES + C::X_BYTES));
+                        G::load(st, &tmW, fl, fb, 2 * kx, nc);
+                        G::load(st + W_BYTES, &tmW, fl, fb, 2 * kx + BK, nc);
+                        G::load(st + 2 * W_BYTES, &tmX, fl, fb, kx, mc);
                     } else {
-                        mbar_expect_tx(&full[stage], W_BYTES + X_BYTES);
-                        tma_load_2d(st, &tmW, &full[stage], (int32_t)(kc * BK), n0);
-                        tma_load_2d(st + W_BYTES, &tmX, &full[stage], (int32_t)(kc * BK), m0);
+                        if (leader) mbar_expect_tx(fl, CG * (W_BYTES + C::X_BYTES));
+                        G::load(st, &tmW, fl, fb, kx, nc);
+                        G::load(st + W_BYTES, &tmX, fl, fb, kx, mc);
                     }
                     if (++stage == STAGES) {
                         stage = 0;
@@ -285,31 +431,29 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                 }
             }
-        } else if (warp == MMA_WARP && lane == 0) {
-            int stage = 0;
-            uint32_t ph = 0;
-            int slot = 0;
-            uint32_t tph = 0;
-            int se = 0;
-            uint32_t sph = 0;
-            for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        } else if (warp == MMA_WARP && lane == 0 && leader) {
+            int stage = 0, me = 0, slot = 0;
+            uint32_t ph = 0, mph = 0, tph = 0;
+            uint64_t gsb = 0;   // super-blocks issued (K-quants): selects the slots' roles
+            uint64_t item = 0;  // items issued (K-quant block-dot dump: every item in the next slot)
+            for (int64_t tile = pair; tile < tiles; tile += pairs) {
                 for (int64_t kc = 0; kc < nchunks; kc++) {
-                    if (!Q8 && !Q6 && kc % 4 == 0) {
-                        // min-term item of this super-block, drained first
-                        if (!mbar_wait(&sfull[se], sph, abort_flag, status, kDevTimeoutScaleFull)) goto done;
-                        if (!mbar_wait(&tempty[slot], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
+                    const int q = (int)(kc % 4);
+                    if (Q5 && DUMP && q == 0) {
+                        // dump: the min item first, in its own slot
+                        if (!mbar_wait(&mfull[me], mph, abort_flag, status, kDevTimeoutScaleFull)) goto done;
+                        const int s = (int)(item & 1);
+                        if (!mbar_wait_cluster(&tempty[s], (uint32_t)((item >> 1) & 1) ^ 1u, abort_flag, status,
+                                               kDevTimeoutTmemEmpty)) goto done;
                         tc_fence_after();
-                        const uint32_t e = smem_u32(sb_region + se * Q5_SB_ENTRY);
-                        mma_f16(tmem_base + (uint32_t)slot * TM, desc_sw32(e), desc_sw32(e + SW32_TILE), IDESC, 0u);
-                        mma_commit(&tfull[slot]);
-                        mma_commit(&sempty[se]);
-                        if (++slot == SLOTS) {
-                            slot = 0;
-                            tph ^= 1u;
-                        }
-                        if (++se == Q5_SB_DEPTH) {
-                            se = 0;
-                            sph ^= 1u;
+                        const uint32_t mn = smem_u32(min_region + me * C::MIN_ENTRY);
+                        G::mma(tmem_base + (uint32_t)(s * TMP), desc_sw32(mn), desc_sw32(mn + SW32_W), IDESC, 0u);
+                        G::commit(&tfull[s]);
+                        G::commit(&mempty[me]);
+                        item++;
+                        if (++me == DEPTH) {
+                            me = 0;
+                            mph ^= 1u;
                         }
                     }
                     if (!mbar_wait(&full[stage], ph, abort_flag, status, kDevTimeoutFull)) goto done;
@@ -317,25 +461,26 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const uint32_t w_addr = smem_u32(smem + stage * C::STAGE);
                     const uint32_t x_addr = w_addr + (Q6 ? 2 * W_BYTES : W_BYTES);
                     if (Q8) {
-                        const uint32_t ws_addr = x_addr + X_BYTES;
-                        const uint32_t xs_addr = ws_addr + 2 * SW32_TILE;
+                        const uint32_t ws_addr = x_addr + C::X_BYTES;
+                        const uint32_t xs_addr = ws_addr + 2 * SW32_W;
 #pragma unroll
                         for (int blk = 0; blk < 2; blk++) {
                             if (2 * kc + blk >= nb) break;
                             // slots (slot, slot+1) hold (scale product, block dot); slot is even
-                            if (!mbar_wait(&tempty[slot], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
-                            if (!mbar_wait(&tempty[slot + 1], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
+                            if (!mbar_wait_cluster(&tempty[slot], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
+                            if (!mbar_wait_cluster(&tempty[slot + 1], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty))
+                                goto done;
                             tc_fence_after();
-                            const uint32_t ds = tmem_base + (uint32_t)slot * TM;
+                            const uint32_t ds = tmem_base + (uint32_t)slot * TMP;
                             // the activation scale tile covers blocks 16*g .. 16*g+15; the one-hot
                             // weight tile selects block (2kc+blk) % 16 of it
-                            mma_f16(ds, desc_sw32(ws_addr + blk * SW32_TILE), desc_sw32(xs_addr), IDESC, 0u);
+                            G::mma(ds, desc_sw32(ws_addr + blk * SW32_W), desc_sw32(xs_addr), IDESC, 0u);
 #pragma unroll
                             for (int k = 0; k < 2; k++) {
                                 const uint32_t koff = (uint32_t)(blk * 2 + k) * 32u;  // 16 fp16 = 32 bytes
-                                mma_f16(ds + TM, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC, (uint32_t)k);
+                                G::mma(ds + TMP, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC, (uint32_t)k);
                             }
-                            mma_commit(&tfull[slot]);
+                            G::commit(&tfull[slot]);
                             slot += 2;
                             if (slot == SLOTS) {
                                 slot = 0;
@@ -343,33 +488,52 @@ __global__ void __launch_bounds__(THREADS, 1)
                             }
                         }
                     } else {
-                        // K-quants: the four 64-value chunks of a super-block share its scale,
-                        // so they accumulate into one TMEM slot (one drain per super-block);
-                        // the block-dot dump keeps one slot per chunk.  Q6_K adds each K step's
-                        // parity plane into the same accumulator.
-                        const bool first = DUMP || kc % 4 == 0;
-                        const bool last = DUMP || kc % 4 == 3 || kc == nchunks - 1;
+                        // this stage's chunk: into the super-block's chunk slot (or, dumping, its own slot)
+                        const bool first = DUMP || q == 0;
+                        const bool last = DUMP || q == 3 || kc == nchunks - 1;
+                        // slot and phase: Q5_K uses both slots once per super-block (phase
+                        // gsb & 1); Q6_K and the dump use one slot per item, alternating
+                        const uint64_t use = DUMP ? item : gsb;
+                        const int cs = (int)(use & 1);
+                        const uint32_t cpar = (Q5 && !DUMP) ? (uint32_t)(gsb & 1) : (uint32_t)((use >> 1) & 1);
                         if (first) {
-                            if (!mbar_wait(&tempty[slot], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
+                            if (!mbar_wait_cluster(&tempty[cs], cpar ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
                             tc_fence_after();
                         }
-                        const uint32_t d = tmem_base + (uint32_t)slot * TM;
+                        const uint32_t d = tmem_base + (uint32_t)(cs * TMP);
 #pragma unroll
                         for (int k = 0; k < 4; k++) {
                             const uint32_t koff = (uint32_t)k * 32u;
-                            mma_f16(d, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC,
-                                    (first && k == 0) ? 0u : 1u);
-                            if (Q6) mma_f16(d, desc_sw128(w_addr + W_BYTES + koff), desc_sw128(x_addr + koff), IDESC, 1u);
+                            G::mma(d, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC,
+                                         (first && k == 0) ? 0u : 1u);
+                            if (Q6) G::mma(d, desc_sw128(w_addr + W_BYTES + koff), desc_sw128(x_addr + koff), IDESC, 1u);
                         }
-                        if (last) {
-                            mma_commit(&tfull[slot]);
-                            if (++slot == SLOTS) {
-                                slot = 0;
-                                tph ^= 1u;
+                        if (Q5 && !DUMP && q == 2) {
+                            // the min item, into the other slot: that slot held the previous
+                            // super-block's chunk sum, whose drain overlapped the first three
+                            // stages; the drain reads the min item during the last one
+                            if (!mbar_wait(&mfull[me], mph, abort_flag, status, kDevTimeoutScaleFull)) goto done;
+                            if (!mbar_wait_cluster(&tempty[cs ^ 1], cpar ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty))
+                                goto done;
+                            tc_fence_after();
+                            const uint32_t mn = smem_u32(min_region + me * C::MIN_ENTRY);
+                            G::mma(tmem_base + (uint32_t)((cs ^ 1) * TMP), desc_sw32(mn), desc_sw32(mn + SW32_W), IDESC, 0u);
+                            G::commit(&tfull[cs ^ 1]);
+                            G::commit(&mempty[me]);
+                            if (++me == DEPTH) {
+                                me = 0;
+                                mph ^= 1u;
                             }
                         }
+                        if (last) {
+                            G::commit(&tfull[cs]);
+                            if (DUMP)
+                                item++;
+                            else
+                                gsb++;
+                        }
                     }
-                    mma_commit(&empty[stage]);
+                    G::commit(&empty[stage]);
                     if (++stage == STAGES) {
                         stage = 0;
                         ph ^= 1u;
@@ -379,46 +543,47 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else {
         // ------------------------------------------------------ drain warps --
-        regs_inc<232>();
+        regs_inc<C::DRAIN_REGS>();
         const uint32_t quad = warp & 3u, half = warp >> 2;
-        const uint32_t wrow = quad * 32u + lane;              // tile-local weight row == TMEM lane
+        const uint32_t wrow = quad * 32u + lane;              // CTA-local weight row == TMEM lane
         const uint32_t lane_base = (quad * 32u) << 16;
-        int slot = 0;
-        uint32_t tph = 0;
-        int se = 0;
-        uint32_t sph = 0;
-        for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-            const int64_t m0 = (tile % mt_count) * TM;
-            const int64_t n0 = (tile / mt_count) * TN;  // view-local
-            float acc[64];
+        // slot releases go to the even CTA's barriers
+        const uint32_t tempty0 = CG == 2 ? cluster_map(smem_u32(tempty), 0) : 0u;
+        auto release = [&](int s) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if (leader)
+                    mbar_arrive(&tempty[s]);
+                else
+                    mbar_arrive_remote(tempty0 + 8u * (uint32_t)s);
+            }
+        };
+        int slot = 0, se = 0;
+        uint32_t tph = 0, sph = 0;
+        uint64_t gsb = 0, item = 0;
+        for (int64_t tile = pair; tile < tiles; tile += pairs) {
+            const int64_t m0 = (tile % mt_count) * TMP;
+            const int64_t n0 = (tile / mt_count) * CG * TN + rank * TN;  // view-local, this CTA's rows
+            const int64_t n = n0 + wrow;
+            const int64_t mfirst = m0 + half * HC;
+            float acc[HC];
 #pragma unroll
-            for (int i = 0; i < 64; i++) acc[i] = 0.f;
-            if (Q8) {
+            for (int i = 0; i < HC; i++) acc[i] = 0.f;
+            if constexpr (Q8) {
                 for (int64_t b = 0; b < nb; b++) {
                     if (!mbar_wait(&tfull[slot], tph, abort_flag, status, kDevTimeoutTmemFull)) goto done;
                     tc_fence_after();
-                    const uint32_t ts = tmem_base + lane_base + (uint32_t)slot * TM + half * 64u;
-                    uint32_t sv[32], sv2[32], iv[32], iv2[32];
-                    tmem_ld32(ts, sv);
-                    tmem_ld32(ts + 32, sv2);
-                    tmem_ld32(ts + TM, iv);
-                    tmem_ld32(ts + TM + 32, iv2);
-                    tmem_ld_wait();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) {
-                        mbar_arrive(&tempty[slot]);
-                        mbar_arrive(&tempty[slot + 1]);
-                    }
+                    const uint32_t ts = tmem_base + lane_base + (uint32_t)slot * TMP + half * HC;
                     if (DUMP) {
-                        const int64_t n = n0 + wrow;
-#pragma unroll
-                        for (int j = 0; j < 64; j++) {
-                            const int64_t m = m0 + half * 64 + j;
-                            if (n < p.N && m < p.M)
-                                p.dump[(b * p.M + m) * p.N + n] = __uint_as_float(j < 32 ? iv[j] : iv2[j - 32]);
-                        }
+                        drain_dump<HC>(ts + TMP, p, b, mfirst, n);
                     } else {
+                        uint32_t sv[32], sv2[32], iv[32], iv2[32];
+                        tmem_ld32(ts, sv);
+                        tmem_ld32(ts + 32, sv2);
+                        tmem_ld32(ts + TMP, iv);
+                        tmem_ld32(ts + TMP + 32, iv2);
+                        tmem_ld_wait();
                         // pix_dot_q8_0: acc = fma(fp16(dw)*fp16(dx), float(block dot), acc), two per instruction
 #pragma unroll
                         for (int j = 0; j < 32; j += 2)
@@ -429,6 +594,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                             ffma2(acc[32 + j], acc[33 + j], __uint_as_float(sv2[j]), __uint_as_float(sv2[j + 1]),
                                   __uint_as_float(iv2[j]), __uint_as_float(iv2[j + 1]));
                     }
+                    release(slot);
+                    release(slot + 1);
                     slot += 2;
                     if (slot == SLOTS) {
                         slot = 0;
@@ -439,109 +606,118 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int64_t sb = 0; sb < nb; sb++) {
                     if (!mbar_wait(&sfull[se], sph, abort_flag, status, kDevTimeoutScaleFull)) goto done;
                     const uint8_t* e = sb_region + se * C::SB_ENTRY;
-                    const float dw = reinterpret_cast<const float*>(e + C::OFF_DW)[wrow];
-                    const float4* dx4 = reinterpret_cast<const float4*>(e + C::OFF_DX) + half * 16;
-                    float s[64];
-                    if (Q6) {
-                        // pix_dot_q6_K: d = y.d * fp16(x.d)
-#pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            const float4 v = dx4[j];
-                            fmul2(s[4 * j + 0], s[4 * j + 1], v.x, v.y, dw, dw);
-                            fmul2(s[4 * j + 2], s[4 * j + 3], v.z, v.w, dw, dw);
+                    const float* dx = reinterpret_cast<const float*>(e + C::OFF_DX) + half * HC;
+                    if (!DUMP) {
+                        const int cs = (int)(gsb & 1);
+                        const uint32_t par = Q5 ? (uint32_t)(gsb & 1) : (uint32_t)((gsb >> 1) & 1);
+                        // this thread's lanes: 32*quad + 16lh + 8h + lane/4
+                        const float* dwv = reinterpret_cast<const float*>(e + C::OFF_DW) + quad * 32u + (lane >> 2);
+                        if (Q5) {
+                            // pix_dot_q5_K: summs += (-y.d * fp16(x.dmin)) * float(sum_j m_j * bsum_j)
+                            const float* dmv = reinterpret_cast<const float*>(e + C::OFF_DMW) + quad * 32u + (lane >> 2);
+                            const float w[4] = {-dmv[0], -dmv[8], -dmv[16], -dmv[24]};
+                            if (!mbar_wait(&tfull[cs ^ 1], par, abort_flag, status, kDevTimeoutTmemFull)) goto done;
+                            tc_fence_after();
+                            drain_split(acc, tmem_base + lane_base + (uint32_t)((cs ^ 1) * TMP) + half * HC, dx, w, lane);
+                            release(cs ^ 1);
                         }
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&sempty[se]);
-                    } else {
-                        // pix_dot_q5_K: dmin = -y.d * fp16(x.dmin)
-                        const float dmw = reinterpret_cast<const float*>(e + C::OFF_DMW)[wrow];
-#pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            const float4 v = dx4[j];
-                            fmul2(s[4 * j + 0], s[4 * j + 1], -v.x, -v.y, dmw, dmw);
-                            fmul2(s[4 * j + 2], s[4 * j + 3], -v.z, -v.w, dmw, dmw);
-                        }
-                    }
-                    // items: Q5_K the min term, then the super-block's chunk sum; Q6_K the
-                    // chunk sum alone (one item per chunk when dumping block dots)
-                    constexpr int ITEMS = Q6 ? (DUMP ? 4 : 1) : (DUMP ? 5 : 2);
-#pragma unroll 1
-                    for (int it = 0; it < ITEMS; it++) {
-                        if (!Q6 && it == 1) {
-                            // d = y.d * fp16(x.d), cached for the four chunks
-#pragma unroll
-                            for (int j = 0; j < 16; j++) {
-                                const float4 v = dx4[j];
-                                fmul2(s[4 * j + 0], s[4 * j + 1], v.x, v.y, dw, dw);
-                                fmul2(s[4 * j + 2], s[4 * j + 3], v.z, v.w, dw, dw);
-                            }
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&sempty[se]);
-                        }
-                        if (!mbar_wait(&tfull[slot], tph, abort_flag, status, kDevTimeoutTmemFull)) goto done;
+                        // acc += (y.d * fp16(x.d)) * float(sumi)
+                        const float w[4] = {dwv[0], dwv[8], dwv[16], dwv[24]};
+                        if (!mbar_wait(&tfull[cs], par, abort_flag, status, kDevTimeoutTmemFull)) goto done;
                         tc_fence_after();
-                        const uint32_t ta = tmem_base + lane_base + (uint32_t)slot * TM + half * 64u;
-                        uint32_t v0[32], v1[32];
-                        tmem_ld32(ta, v0);
-                        tmem_ld32(ta + 32, v1);
-                        tmem_ld_wait();
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&tempty[slot]);
-                        if (DUMP) {
-                            const int64_t item = Q6 ? sb * 4 + it : sb * 5 + (it == 0 ? 4 : it - 1);
-                            const int64_t n = n0 + wrow;
-#pragma unroll
-                            for (int j = 0; j < 64; j++) {
-                                const int64_t m = m0 + half * 64 + j;
-                                if (n < p.N && m < p.M)
-                                    p.dump[(item * p.M + m) * p.N + n] = __uint_as_float(j < 32 ? v0[j] : v1[j - 32]);
-                            }
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 32; j += 2)
-                                ffma2(acc[j], acc[j + 1], s[j], s[j + 1], __uint_as_float(v0[j]), __uint_as_float(v0[j + 1]));
-#pragma unroll
-                            for (int j = 0; j < 32; j += 2)
-                                ffma2(acc[32 + j], acc[33 + j], s[32 + j], s[33 + j], __uint_as_float(v1[j]),
-                                      __uint_as_float(v1[j + 1]));
-                        }
-                        if (++slot == SLOTS) {
-                            slot = 0;
-                            tph ^= 1u;
+                        drain_split(acc, tmem_base + lane_base + (uint32_t)(cs * TMP) + half * HC, dx, w, lane);
+                        release(cs);
+                        gsb++;
+                    } else {
+                        // items in issue order: Q5_K the min sum, then the four chunk sums
+                        constexpr int ITEMS = Q5 ? 5 : 4;
+#pragma unroll 1
+                        for (int it = 0; it < ITEMS; it++) {
+                            const int s = (int)(item & 1);
+                            if (!mbar_wait(&tfull[s], (uint32_t)((item >> 1) & 1), abort_flag, status, kDevTimeoutTmemFull))
+                                goto done;
+                            tc_fence_after();
+                            const int64_t idx = Q5 ? sb * 5 + (it == 0 ? 4 : it - 1) : sb * 4 + it;
+                            drain_dump<HC>(tmem_base + lane_base + (uint32_t)(s * TMP) + half * HC, p, idx, mfirst, n);
+                            release(s);
+                            item++;
                         }
                     }
-                    if (++se == Q5_SB_DEPTH) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sempty[se]);
+                    if (++se == DEPTH) {
                         se = 0;
                         sph ^= 1u;
                     }
                 }
             }
             if (!DUMP) {
-                const int64_t n = n0 + wrow;
-                const float bv = (p.bias && n < p.N) ? p.bias[n] : 0.f;
-                if (p.tma_store) {
-                    // each warp stages its [64 activation rows][32 weight rows] block and
-                    // stores it with one TMA store; lane 0 first waits until the warp's
-                    // previous store has finished reading the buffer (no cross-warp sync)
-                    float* stg = reinterpret_cast<float*>(smem + off_staging<TYPE>()) + warp * (64 * 32);
-                    if (lane == 0) bulk_wait_read_all();
-                    __syncwarp();
+                // this thread's lanes (weight rows, CTA-local): row layout (Q8_0) the
+                // thread's own lane; split layout lane_off(lh, h) = 16lh + 8h + lane/4
+                float bv[4];
 #pragma unroll
-                    for (int j = 0; j < 64; j++) stg[j * 32 + lane] = p.bias ? __fadd_rn(acc[j], bv) : acc[j];
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) {
-                        tma_store_2d(&tmY, stg, (int32_t)(n0 + quad * 32), (int32_t)(m0 + half * 64));
-                        bulk_commit();
+                for (int i = 0; i < 4; i++) {
+                    const int64_t nn = n0 + quad * 32 + (SPLIT ? 8 * i + (lane >> 2) : lane);
+                    bv[i] = (p.bias && nn < p.N) ? p.bias[nn] : 0.f;
+                }
+                if (p.tma_store) {
+                    // each warp stages [SROWS activation rows][32 weight rows] blocks and
+                    // stores each with one TMA store; lane 0 first waits until the warp's
+                    // previous store has finished reading the buffer (no cross-warp sync)
+                    constexpr int SR = C::SROWS;
+                    static_assert(!SPLIT || SR == 64, "split layout stages 64 columns per round");
+                    float* stg = reinterpret_cast<float*>(smem + off_staging<TYPE>()) + warp * (SR * 32);
+#pragma unroll
+                    for (int r = 0; r < HC / SR; r++) {
+                        if (lane == 0) bulk_wait_read_all();
+                        __syncwarp();
+                        if (SPLIT) {
+#pragma unroll
+                            for (int lh = 0; lh < 2; lh++)
+#pragma unroll
+                                for (int k = 0; k < 8; k++)
+#pragma unroll
+                                    for (int h = 0; h < 2; h++)
+#pragma unroll
+                                        for (int c = 0; c < 2; c++) {
+                                            const float v = acc[split_idx(r, lh, k, h, c)];
+                                            stg[(8 * k + 2 * (lane & 3) + c) * 32 + 16 * lh + 8 * h + (lane >> 2)] =
+                                                p.bias ? __fadd_rn(v, bv[2 * lh + h]) : v;
+                                        }
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < SR; j++) stg[j * 32 + lane] = p.bias ? __fadd_rn(acc[SR * r + j], bv[0]) : acc[SR * r + j];
+                        }
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&tmY, stg, (int32_t)(n0 + quad * 32), (int32_t)(mfirst + SR * r));
+                            bulk_commit();
+                        }
                     }
+                } else if (SPLIT) {
+#pragma unroll
+                    for (int ch = 0; ch < 2; ch++)
+#pragma unroll
+                        for (int lh = 0; lh < 2; lh++)
+#pragma unroll
+                            for (int k = 0; k < 8; k++)
+#pragma unroll
+                                for (int h = 0; h < 2; h++)
+#pragma unroll
+                                    for (int c = 0; c < 2; c++) {
+                                        const int64_t nn = n0 + quad * 32 + 16 * lh + 8 * h + (lane >> 2);
+                                        const int64_t m = mfirst + 64 * ch + 8 * k + 2 * (lane & 3) + c;
+                                        const float v = acc[split_idx(ch, lh, k, h, c)];
+                                        if (nn < p.N && m < p.M) p.y[m * p.ldy + nn] = p.bias ? __fadd_rn(v, bv[2 * lh + h]) : v;
+                                    }
                 } else if (n < p.N) {
                     // lane = weight row: for each activation row, 32 lanes store 128 contiguous bytes
                     float* yc = p.y + n;
 #pragma unroll
-                    for (int j = 0; j < 64; j++) {
-                        const int64_t m = m0 + half * 64 + j;
-                        if (m < p.M) yc[m * p.ldy] = p.bias ? __fadd_rn(acc[j], bv) : acc[j];
+                    for (int j = 0; j < HC; j++) {
+                        const int64_t m = mfirst + j;
+                        if (m < p.M) yc[m * p.ldy] = p.bias ? __fadd_rn(acc[j], bv[0]) : acc[j];
                     }
                 }
             }
@@ -550,10 +726,20 @@ __global__ void __launch_bounds__(THREADS, 1)
 done:
     // outstanding output stores must finish reading shared memory before exit
     if (p.tma_store && warp < DRAIN_WARPS && lane == 0) bulk_wait_all();
+    if (warp == MMA_WARP && lane == 0 && leader) {
+        // no MMA of this pair may still be writing TMEM when it is freed (after a
+        // normal run the drains have consumed every result; this covers aborts)
+        G::commit_local(mma_done);
+        const uint64_t t0 = global_ns();
+        while (!mbar_try_wait(mma_done, 0) && global_ns() - t0 < PXQ_WAIT_NS) {
+        }
+    }
+    __syncwarp();
+    // the peer CTA no longer touches this CTA's barriers or TMEM after this
     tc_fence_before();
-    __syncthreads();
+    G::sync();
     tc_fence_after();
-    if (warp == 0) tmem_dealloc(tmem_base, TMEM_COLS);
+    if (warp == 0) G::dealloc(tmem_base, TMEM_COLS);
 }
 
 template <uint32_t TYPE, bool DUMP>
@@ -563,17 +749,50 @@ cudaError_t launch_typed(const GemmOperands& op, int num_sms, cudaStream_t s)
     constexpr int smem = smem_bytes<TYPE>();
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    const int64_t tiles = ((op.M + TM - 1) / TM) * ((op.N + TN - 1) / TN);
-    int grid = (int)(tiles < num_sms ? tiles : num_sms);
-    if (grid < 1) grid = 1;
+    constexpr int CG = Cfg<TYPE>::CG;
+    const int64_t tiles = ((op.M + Cfg<TYPE>::TMP - 1) / Cfg<TYPE>::TMP) * ((op.N + CG * TN - 1) / (CG * TN));
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CG;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = CG == 2 ? 1 : 0;
+    int64_t groups = num_sms;  // one CTA per SM
+    if (CG == 2) {
+        // pairs that can be resident at once
+        static int max_pairs = 0;
+        static std::once_flag once;
+        std::call_once(once, [&] {
+            cfg.gridDim = dim3(2 * (num_sms / 2));
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
+                cudaGetLastError();
+                n = num_sms / 2;
+            }
+            max_pairs = n;
+        });
+        groups = max_pairs;
+    }
+    if (tiles < groups) groups = tiles;
+    if (groups < 1) groups = 1;
+    cfg.gridDim = dim3((unsigned)(CG * groups));
     Params p{op.M, op.N, op.K, op.n_first, op.y, op.ldy, op.bias, op.dump, op.status, (op.tma_store && !DUMP) ? 1 : 0};
-    kern<<<grid, THREADS, smem, s>>>(op.tm[0], op.tm[1], op.tm[2], op.tm[3], op.tm[4], op.tm[5], op.tm[6], op.tm_y, p);
-    return cudaGetLastError();
+    return cudaLaunchKernelEx(&cfg, kern, op.tm[0], op.tm[1], op.tm[2], op.tm[3], op.tm[4], op.tm[5], op.tm[6], op.tm_y, p);
 }
 
 }  // namespace
 
-int gemm_smem_bytes() { return smem_bytes<kTypeQ8_0>(); }
+int gemm_activation_rows(uint32_t type) { return type == kTypeQ8_0 ? Cfg<kTypeQ8_0>::XR : Cfg<kTypeQ5_K>::XR; }
+int gemm_tile_activation_rows(uint32_t type) { return type == kTypeQ8_0 ? Cfg<kTypeQ8_0>::TMP : Cfg<kTypeQ5_K>::TMP; }
+int gemm_store_rows(uint32_t type)
+{
+    return type == kTypeQ8_0 ? Cfg<kTypeQ8_0>::SROWS : type == kTypeQ5_K ? Cfg<kTypeQ5_K>::SROWS : Cfg<kTypeQ6_K>::SROWS;
+}
 
 cudaError_t launch_gemm(const GemmOperands& op, int num_sms, cudaStream_t s)
 {

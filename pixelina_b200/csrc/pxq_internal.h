@@ -135,12 +135,12 @@ struct GemmOperands {
     uint32_t type;        // kTypeQ8_0, kTypeQ5_K or kTypeQ6_K
     int64_t M, N, K;      // activation rows, view rows (output columns), inner
     int64_t n_first;      // first weight row of the view (multiple of 4)
-    // tensor maps: 0 weight operand, 1 activation operand, 2 weight scale
+    // tensor maps (boxes as listed in gemm.cu): 0 weight operand, 1 activation operand, 2 weight scale
     // tile (Q8_0 one-hot scales / Q5_K min operand), 3 activation scale tile
     // (Q8_0 fp16 scales / Q8_K min operand), 4 K-quant weight d, 5 Q5_K
     // weight dmin, 6 Q8_K activation d (unused entries may hold any valid map)
     CUtensorMap tm[7];
-    CUtensorMap tm_y;     // output map (fp32 [M][ldy], box {32, 64}) when tma_store
+    CUtensorMap tm_y;     // output map (fp32 [M][ldy], box {32, gemm_store_rows}) when tma_store
     int tma_store;        // 1: write the output tile with TMA stores
     float* y;
     int64_t ldy;
@@ -148,7 +148,12 @@ struct GemmOperands {
     float* dump;          // debug: raw per-item block dots, or null
     uint32_t* status;     // device status word
 };
-int gemm_smem_bytes();
+// Rows of one CTA's activation box in the GEMM's tensor maps (tmX, tmXs),
+// and of a whole output tile (the activation scale map tmDx's box).
+int gemm_activation_rows(uint32_t type);
+int gemm_tile_activation_rows(uint32_t type);
+// Activation rows of one output TMA store (the output map's box is {32, rows}).
+int gemm_store_rows(uint32_t type);
 cudaError_t launch_gemm(const GemmOperands& op, int num_sms, cudaStream_t s);
 
 }  // namespace pxq
