@@ -490,7 +490,8 @@ int run_gemm(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, co
     // innermost dimension only at 16-byte granularity)
     op.tma_store = 0;
     op.tm_y = op.tm[0];
-    if (!dump && (reinterpret_cast<uintptr_t>(output) & 15u) == 0 && (ldy % 4) == 0 && (row_count % 4) == 0) {
+    if (!dump && gemm_store_rows(w->type) > 0 && (reinterpret_cast<uintptr_t>(output) & 15u) == 0 && (ldy % 4) == 0 &&
+        (row_count % 4) == 0) {
         if (make_map(d, &op.tm_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, output, row_count, (uint64_t)a->M, ldy * 4, 32,
                      (uint32_t)gemm_store_rows(w->type),
                      CU_TENSOR_MAP_SWIZZLE_NONE) == PXQ_OK)

@@ -80,7 +80,8 @@ constexpr int MMA_WARP = 9;
 constexpr int THREADS = 384;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int MAX_STAGES = 6;
-constexpr int DEPTH = 2;               // super-block entry and min-operand rings
+constexpr int DEPTH = 2;               // min-operand ring
+constexpr int MAX_SB_DEPTH = 4;        // super-block scale entry ring (per type: Cfg::SB_DEPTH)
 
 template <uint32_t TYPE>
 struct Cfg;
@@ -90,11 +91,11 @@ struct Cfg<kTypeQ8_0> {
     // hand-off between two SMs per block
     static constexpr int CG = 1, TMP = 128, SLOTS = 4, STAGES = 3;
     static constexpr uint32_t PRODUCER_REGS = 40, DRAIN_REGS = 232;
-    static constexpr int SROWS = 64;  // activation rows per TMA store of a drain warp
+    static constexpr int SROWS = 64;  // activation rows per TMA store of a drain warp (0: direct stores)
     static constexpr int XR = TMP / CG, X_BYTES = XR * BK * 2, SW32_X = XR * 32;
     // stage: W | X | one-hot weight scales of the stage's 2 blocks | activation scales (16 blocks)
     static constexpr int STAGE = W_BYTES + X_BYTES + 2 * SW32_W + SW32_X;  // 44 KB
-    static constexpr int MIN_ENTRY = 0, SB_ENTRY = 0;
+    static constexpr int MIN_ENTRY = 0, SB_ENTRY = 0, SB_DEPTH = 1;
     static constexpr int OFF_DW = 0, OFF_DMW = 0, OFF_DX = 0;  // no super-block entries
 };
 template <>
@@ -105,7 +106,7 @@ struct Cfg<kTypeQ5_K> {
     static constexpr int XR = TMP / CG, X_BYTES = XR * BK * 2, SW32_X = XR * 32;
     static constexpr int STAGE = W_BYTES + X_BYTES;                          // 32 KB
     static constexpr int MIN_ENTRY = SW32_W + SW32_X;                        // weight | activation min operands
-    static constexpr int SB_ENTRY = 2048;                                    // dW | dminW | dX (TMP floats)
+    static constexpr int SB_ENTRY = 2048, SB_DEPTH = 2;                      // dW | dminW | dX (TMP floats)
     static constexpr int OFF_DW = 0, OFF_DMW = 512, OFF_DX = 1024;
 };
 template <>
@@ -116,7 +117,9 @@ struct Cfg<kTypeQ6_K> {
     static constexpr int XR = TMP / CG, X_BYTES = XR * BK * 2, SW32_X = XR * 32;
     static constexpr int STAGE = 2 * W_BYTES + X_BYTES;                      // even | parity | X: 48 KB
     static constexpr int MIN_ENTRY = 0;
-    static constexpr int SB_ENTRY = 2048;                                    // dW | dX (TMP floats)
+    // an entry is freed only when the drain has finished its super-block, one
+    // super-block after its MMAs: four entries keep the producer clear of the drain
+    static constexpr int SB_ENTRY = 2048, SB_DEPTH = 4;                      // dW | dX (TMP floats)
     static constexpr int OFF_DW = 0, OFF_DMW = 0, OFF_DX = 1024;
 };
 
@@ -125,14 +128,14 @@ __host__ __device__ constexpr int off_min() { return Cfg<TYPE>::STAGES * Cfg<TYP
 template <uint32_t TYPE>
 __host__ __device__ constexpr int off_sb() { return off_min<TYPE>() + DEPTH * Cfg<TYPE>::MIN_ENTRY; }
 template <uint32_t TYPE>
-__host__ __device__ constexpr int off_staging() { return off_sb<TYPE>() + DEPTH * Cfg<TYPE>::SB_ENTRY; }
+__host__ __device__ constexpr int off_staging() { return off_sb<TYPE>() + Cfg<TYPE>::SB_DEPTH * Cfg<TYPE>::SB_ENTRY; }
 // output staging for the TMA-store epilogue: per drain warp [SROWS activation rows][32 weight rows] fp32
 template <uint32_t TYPE>
 __host__ __device__ constexpr int staging_bytes() { return DRAIN_WARPS * Cfg<TYPE>::SROWS * 32 * 4; }
 template <uint32_t TYPE>
 __host__ __device__ constexpr int off_bar() { return off_staging<TYPE>() + staging_bytes<TYPE>(); }
 // full/empty, min full/empty, entry full/empty, slot full/empty, MMA drain-out
-constexpr int NUM_BARS = 2 * MAX_STAGES + 4 * DEPTH + 2 * 4 + 1;
+constexpr int NUM_BARS = 2 * MAX_STAGES + 2 * DEPTH + 2 * MAX_SB_DEPTH + 2 * 4 + 1;
 template <uint32_t TYPE>
 __host__ __device__ constexpr int smem_bytes() { return off_bar<TYPE>() + NUM_BARS * 8 + 16 + 1024; }
 
@@ -216,14 +219,11 @@ __host__ __device__ constexpr int split_idx(int ch, int lh, int k, int h, int c)
 
 // acc += (dx[column] * w[lane]) * v over one drained item (taddr: the warp's
 // lane quadrant and first column; dx: the warp's first column's scale;
-// w[2lh + h]: the scale of lane 16lh + 8h + t/4).
-__device__ __forceinline__ void drain_split(float (&acc)[128], uint32_t taddr, const float* dx, const float (&w)[4], uint32_t t)
+// w4 components x, y, z, w: the scales of lanes t/4, 8 + t/4, 16 + t/4, 24 + t/4).
+__device__ __forceinline__ void drain_split(float (&acc)[128], uint32_t taddr, const float* dx, float4 w4, uint32_t t)
 {
 #pragma unroll
     for (int ch = 0; ch < 2; ch++) {
-        float2 d[8];
-#pragma unroll
-        for (int k = 0; k < 8; k++) d[k] = *reinterpret_cast<const float2*>(dx + 64 * ch + 8 * k + 2 * (t & 3));
 #pragma unroll
         for (int lh = 0; lh < 2; lh++) {
             uint32_t v[32];
@@ -231,10 +231,13 @@ __device__ __forceinline__ void drain_split(float (&acc)[128], uint32_t taddr, c
             tmem_ld_wait();
 #pragma unroll
             for (int k = 0; k < 8; k++) {
+                // re-read per lane half: keeps the drain's live registers below its budget
+                const float2 d = *reinterpret_cast<const float2*>(dx + 64 * ch + 8 * k + 2 * (t & 3));
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
+                    const float w = (2 * lh + h) == 0 ? w4.x : (2 * lh + h) == 1 ? w4.y : (2 * lh + h) == 2 ? w4.z : w4.w;
                     float s0, s1;
-                    fmul2(s0, s1, d[k].x, d[k].y, w[2 * lh + h], w[2 * lh + h]);
+                    fmul2(s0, s1, d.x, d.y, w, w);
                     const int i = split_idx(ch, lh, k, h, 0);
                     ffma2(acc[i], acc[i + 1], s0, s1, __uint_as_float(v[4 * k + 2 * h]), __uint_as_float(v[4 * k + 2 * h + 1]));
                 }
@@ -297,8 +300,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t* mfull = empty + MAX_STAGES;    // even CTA: min operands loaded (both CTAs' bytes)
     uint64_t* mempty = mfull + DEPTH;        // min operands consumed (both CTAs)
     uint64_t* sfull = mempty + DEPTH;        // this CTA's super-block scale entry loaded
-    uint64_t* sempty = sfull + DEPTH;        // ... and read by this CTA's drain warps
-    uint64_t* tfull = sempty + DEPTH;        // accumulator slot complete (both CTAs)
+    uint64_t* sempty = sfull + MAX_SB_DEPTH; // ... and read by this CTA's drain warps
+    uint64_t* tfull = sempty + MAX_SB_DEPTH; // accumulator slot complete (both CTAs)
     uint64_t* tempty = tfull + 4;            // even CTA: slot drained by both CTAs
     uint64_t* mma_done = tempty + 4;         // even CTA: every issued MMA finished (exit path)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
@@ -318,6 +321,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int i = 0; i < DEPTH; i++) {
             mbar_init(&mfull[i], 1);
             mbar_init(&mempty[i], 1);
+        }
+        for (int i = 0; i < MAX_SB_DEPTH; i++) {
             mbar_init(&sfull[i], 1);
             mbar_init(&sempty[i], DRAIN_WARPS);
         }
@@ -340,7 +345,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             tma_prefetch_desc(&tmWs);
             tma_prefetch_desc(&tmXs);
         }
-        if (p.tma_store) tma_prefetch_desc(&tmY);
+        if (C::SROWS > 0 && p.tma_store) tma_prefetch_desc(&tmY);
         if (!Q8) {
             tma_prefetch_desc(&tmD);
             tma_prefetch_desc(&tmDx);
@@ -384,7 +389,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         tma_load_2d(e + C::OFF_DW, &tmD, &sfull[se], nc, sb);
                         if (Q5) tma_load_2d(e + C::OFF_DMW, &tmDm, &sfull[se], nc, sb);
                         tma_load_2d(e + C::OFF_DX, &tmDx, &sfull[se], m0, sb);
-                        if (++se == DEPTH) {
+                        if (++se == C::SB_DEPTH) {
                             se = 0;
                             sph ^= 1u;
                         }
@@ -615,14 +620,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                         if (Q5) {
                             // pix_dot_q5_K: summs += (-y.d * fp16(x.dmin)) * float(sum_j m_j * bsum_j)
                             const float* dmv = reinterpret_cast<const float*>(e + C::OFF_DMW) + quad * 32u + (lane >> 2);
-                            const float w[4] = {-dmv[0], -dmv[8], -dmv[16], -dmv[24]};
+                            const float4 w = make_float4(-dmv[0], -dmv[8], -dmv[16], -dmv[24]);
                             if (!mbar_wait(&tfull[cs ^ 1], par, abort_flag, status, kDevTimeoutTmemFull)) goto done;
                             tc_fence_after();
                             drain_split(acc, tmem_base + lane_base + (uint32_t)((cs ^ 1) * TMP) + half * HC, dx, w, lane);
                             release(cs ^ 1);
                         }
                         // acc += (y.d * fp16(x.d)) * float(sumi)
-                        const float w[4] = {dwv[0], dwv[8], dwv[16], dwv[24]};
+                        const float4 w = make_float4(dwv[0], dwv[8], dwv[16], dwv[24]);
                         if (!mbar_wait(&tfull[cs], par, abort_flag, status, kDevTimeoutTmemFull)) goto done;
                         tc_fence_after();
                         drain_split(acc, tmem_base + lane_base + (uint32_t)(cs * TMP) + half * HC, dx, w, lane);
@@ -645,7 +650,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&sempty[se]);
-                    if (++se == DEPTH) {
+                    if (++se == C::SB_DEPTH) {
                         se = 0;
                         sph ^= 1u;
                     }
@@ -660,11 +665,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const int64_t nn = n0 + quad * 32 + (SPLIT ? 8 * i + (lane >> 2) : lane);
                     bv[i] = (p.bias && nn < p.N) ? p.bias[nn] : 0.f;
                 }
-                if (p.tma_store) {
+                if (C::SROWS > 0 && p.tma_store) {
                     // each warp stages [SROWS activation rows][32 weight rows] blocks and
                     // stores each with one TMA store; lane 0 first waits until the warp's
                     // previous store has finished reading the buffer (no cross-warp sync)
-                    constexpr int SR = C::SROWS;
+                    constexpr int SR = C::SROWS > 0 ? C::SROWS : 64;
                     static_assert(!SPLIT || SR == 64, "split layout stages 64 columns per round");
                     float* stg = reinterpret_cast<float*>(smem + off_staging<TYPE>()) + warp * (SR * 32);
 #pragma unroll
@@ -725,7 +730,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 done:
     // outstanding output stores must finish reading shared memory before exit
-    if (p.tma_store && warp < DRAIN_WARPS && lane == 0) bulk_wait_all();
+    if (C::SROWS > 0 && p.tma_store && warp < DRAIN_WARPS && lane == 0) bulk_wait_all();
     if (warp == MMA_WARP && lane == 0 && leader) {
         // no MMA of this pair may still be writing TMEM when it is freed (after a
         // normal run the drains have consumed every result; this covers aborts)

@@ -152,7 +152,8 @@ struct GemmOperands {
 // and of a whole output tile (the activation scale map tmDx's box).
 int gemm_activation_rows(uint32_t type);
 int gemm_tile_activation_rows(uint32_t type);
-// Activation rows of one output TMA store (the output map's box is {32, rows}).
+// Activation rows of one output TMA store (the output map's box is {32, rows});
+// 0 when the type's epilogue stores directly.
 int gemm_store_rows(uint32_t type);
 cudaError_t launch_gemm(const GemmOperands& op, int num_sms, cudaStream_t s);
 
