@@ -195,9 +195,12 @@ def test_gemm_vs_oracle(pxq, oracle, wtype, columns, rows, inner):
     assert ok and max_abs_rel(y, ref) <= TOL
 
 
-def test_gemm_q8_0_odd_block_count(pxq, oracle):
-    # inner = 96: three 32-blocks, the last 64-wide stage is half empty
-    rows, inner, columns = 70, 96, 140
+@pytest.mark.parametrize("rows,columns", [(70, 140), (2560, 2048)])
+def test_gemm_q8_0_odd_block_count(pxq, oracle, rows, columns):
+    # inner = 96: three 32-blocks, the last 64-wide stage is half empty; with
+    # 320 output tiles every CTA walks several, so the per-block accumulator
+    # slots start a new tile mid-cycle
+    inner = 96
     w = synth.q8_0_weights(rows, inner, seed=1)
     x = synth.activations(columns, inner, seed=2)
     W = pxq.Weight(w, Q8_0, inner, rows)
