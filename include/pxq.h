@@ -98,9 +98,27 @@ PXQ_API int pxq_decode(const void* data, uint32_t type, size_t count, float* out
  * copied).  `key` (may be NULL) names the tensor; uploading the same key
  * again returns the cached weight, as the Vulkan weight cache does with
  * "file:name:offset:bytes" (src/backend_vulkan.cpp:742-758).
- * Supported types: Q8_0, Q5_K. */
+ * Supported types: Q8_0, Q5_K, Q6_K. */
 PXQ_API int pxq_weight_upload(const void* bytes, int bytes_on_device, uint32_t type, size_t inner, size_t rows, const char* key,
                       pxq_weight** out);
+
+/* Upload the gate and up projections of a gated feed-forward as one weight
+ * for pxq_matmul_gated: `gate` and `up` each hold `rows` GGUF rows of `type`
+ * (host or device, as for pxq_weight_upload).  The callers' pairs: separate
+ * tensors (src/inference.cpp:331-332, src/qwen_vl.cpp:396) or the two row
+ * slices of one fused tensor (src/qwen_image.cpp:271).  rows must be a
+ * multiple of 64.  The weight serves pxq_matmul_gated only. */
+PXQ_API int pxq_weight_upload_gated(const void* gate, const void* up, int bytes_on_device, uint32_t type, size_t inner,
+                                    size_t rows, const char* key, pxq_weight** out);
+
+/* Gated feed-forward projection in one call:
+ *   output[c*ldy + r] = silu(g) * u,  g = input[c] . gate[r],  u = input[c] . up[r]
+ * with silu(g) = g / (1 + exp(-g)) -- the callers' tensor_linear, tensor_linear,
+ * tensor_silu, tensor_gate sequence (src/tensor.cpp:199-208, :334-345) with
+ * no intermediate tensors.  columns <= 8 runs the matvec over both
+ * projections and a small epilogue kernel; larger runs the tensor-core GEMM
+ * with the gate applied in its epilogue. */
+PXQ_API int pxq_matmul_gated(pxq_weight* w, const float* input, size_t columns, float* output, size_t ldy, void* stream);
 
 /* Drop a weight (its device copies are freed once no call uses them). */
 PXQ_API int pxq_weight_release(pxq_weight* w);

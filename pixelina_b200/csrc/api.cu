@@ -170,6 +170,9 @@ struct Packed {
 struct pxq_weight {
     uint32_t type = 0;
     int64_t inner = 0, rows = 0, stride = 0;
+    // gated: rows = 2F, the gate projection's F rows then the up projection's
+    // F rows (pxq_weight_upload_gated); only pxq_matmul_gated takes it
+    bool gated = false;
     int device = 0;
     uint8_t* raw = nullptr;
     CUtensorMap mv_map[kMvTileShapes];  // Q5_K: raw bytes as u64 [rows][stride/8], the matvec's TMA views
@@ -242,12 +245,13 @@ int build_packed(const DeviceCtx* d, pxq_weight* w, int64_t first, int64_t count
     pk->dmin = reinterpret_cast<float*>(base + off_dm);
     PXQ_CUDA(cudaMemsetAsync(pk->mem, 0, total, s));
     const uint8_t* src = w->raw + first * w->stride;
+    const int64_t gate_rows = w->gated ? w->rows / 2 : 0;  // whole-tensor copies only (first = 0)
     if (q6) {
-        PXQ_CUDA(counted(launch_repack_q6_K(src, count, K, w->stride, pk->wv, pk->d, pk->ldn, s)));
+        PXQ_CUDA(counted(launch_repack_q6_K(src, count, K, w->stride, pk->wv, pk->d, pk->ldn, gate_rows, s)));
     } else if (!q5) {
-        PXQ_CUDA(counted(launch_repack_q8_0(src, count, K, w->stride, pk->wv, pk->ws, s)));
+        PXQ_CUDA(counted(launch_repack_q8_0(src, count, K, w->stride, pk->wv, pk->ws, gate_rows, s)));
     } else {
-        PXQ_CUDA(counted(launch_repack_q5_K(src, count, K, w->stride, pk->wv, pk->d, pk->dmin, pk->ws, pk->ldn, s)));
+        PXQ_CUDA(counted(launch_repack_q5_K(src, count, K, w->stride, pk->wv, pk->d, pk->dmin, pk->ws, pk->ldn, gate_rows, s)));
     }
     int rc = make_map(d, &pk->tmW, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pk->wv, Kop, count, Kop * 2, 64, 128,
                       CU_TENSOR_MAP_SWIZZLE_128B);
@@ -300,6 +304,7 @@ int check_matmul_args(pxq_weight* w, size_t row_first, size_t row_count, const v
                       size_t ldy)
 {
     if (!w || !input || !output) return fail(PXQ_ERR_INVALID, "null weight, input or output");
+    if (w->gated) return fail(PXQ_ERR_INVALID, "gated weight: use pxq_matmul_gated");
     if (!columns || !row_count) return fail(PXQ_ERR_INVALID, "zero columns or rows");
     if (row_first > (size_t)w->rows || row_count > (size_t)w->rows - row_first)
         return fail(PXQ_ERR_INVALID, "row range [%zu, %zu) outside weight with %lld rows", row_first, row_first + row_count,
@@ -478,6 +483,7 @@ int run_gemm(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, co
     op.bias = bias;
     op.dump = dump;
     op.status = d->status;
+    op.gated = w->gated ? 1 : 0;
     op.tm[0] = pk->tmW;
     op.tm[1] = a->tmX;
     op.tm[2] = pk->tmWs;
@@ -490,8 +496,8 @@ int run_gemm(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, co
     // innermost dimension only at 16-byte granularity)
     op.tma_store = 0;
     op.tm_y = op.tm[0];
-    if (!dump && gemm_store_rows(w->type) > 0 && (reinterpret_cast<uintptr_t>(output) & 15u) == 0 && (ldy % 4) == 0 &&
-        (row_count % 4) == 0) {
+    if (!dump && !w->gated && gemm_store_rows(w->type) > 0 && (reinterpret_cast<uintptr_t>(output) & 15u) == 0 &&
+        (ldy % 4) == 0 && (row_count % 4) == 0) {
         if (make_map(d, &op.tm_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, output, row_count, (uint64_t)a->M, ldy * 4, 32,
                      (uint32_t)gemm_store_rows(w->type),
                      CU_TENSOR_MAP_SWIZZLE_NONE) == PXQ_OK)
@@ -574,7 +580,7 @@ uint32_t* device_status(int device) { return (device >= 0 && device < kMaxDevice
 bool weight_view(const pxq_weight* w, uint32_t* type, int64_t* inner, int64_t* rows, int64_t* stride, const uint8_t** raw,
                  int* device)
 {
-    if (!w) return false;
+    if (!w || w->gated) return false;
     *type = w->type;
     *inner = w->inner;
     *rows = w->rows;
@@ -679,24 +685,60 @@ int pxq_decode(const void* data, uint32_t type, size_t count, float* out, void* 
     return PXQ_OK;
 }
 
-int pxq_weight_upload(const void* bytes, int bytes_on_device, uint32_t type, size_t inner, size_t rows, const char* key,
-                      pxq_weight** out)
+}  // extern "C"
+
+namespace {
+
+// Copy `count` raw GGUF rows (host or device bytes) into rows [first,
+// first+count) of w's device copy; Q6_K super-blocks are padded to 224 bytes.
+int copy_rows(pxq_weight* w, const void* bytes, int bytes_on_device, int64_t first, int64_t count)
 {
-    DeviceCtx* d;
-    if (int rc = ensure_device(&d)) return rc;
-    if (!bytes || !out) return fail(PXQ_ERR_INVALID, "null bytes or out");
+    const uint64_t total = pxq_weight_bytes((uint64_t)w->inner, (uint64_t)count, w->type);
+    uint8_t* dst = w->raw + first * w->stride;
+    if (w->type != PXQ_TYPE_Q6_K) {
+        PXQ_CUDA(cudaMemcpy(dst, bytes, total, bytes_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
+        return PXQ_OK;
+    }
+    const void* src = bytes;
+    void* tmp = nullptr;
+    if (!bytes_on_device || (reinterpret_cast<uintptr_t>(bytes) & 1u)) {
+        if (cudaMalloc(&tmp, total) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(PXQ_ERR_NO_MEMORY, "cannot allocate %llu bytes of upload staging", (unsigned long long)total);
+        }
+        const cudaError_t e = cudaMemcpy(tmp, bytes, total, bytes_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            cudaFree(tmp);
+            return fail(PXQ_ERR_CUDA, "weight copy failed: %s", cudaGetErrorString(e));
+        }
+        src = tmp;
+    }
+    cudaError_t e = launch_pad_q6_K(src, dst, (int64_t)(w->inner / 256 * count), nullptr);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (tmp) cudaFree(tmp);
+    if (e != cudaSuccess) return fail(PXQ_ERR_CUDA, "Q6_K padding failed: %s", cudaGetErrorString(e));
+    return PXQ_OK;
+}
+
+// Upload one weight from `parts` sources of `rows` rows each (one plain
+// weight, or the gate and up projections of a gated weight, stacked).
+int create_weight(DeviceCtx* d, const void* const* parts, int nparts, int bytes_on_device, uint32_t type, size_t inner,
+                  size_t rows, const char* key, pxq_weight** out)
+{
     *out = nullptr;
     if (type != PXQ_TYPE_Q8_0 && type != PXQ_TYPE_Q5_K && type != PXQ_TYPE_Q6_K)
         return fail(PXQ_ERR_UNSUPPORTED, "weight type %u not supported", type);
     const uint64_t total = pxq_weight_bytes(inner, rows, type);
     if (!total) return fail(PXQ_ERR_INVALID, "invalid weight shape [%zu, %zu] for type %u", inner, rows, type);
-    if (inner > 0x7fffffffu || rows > 0x7fffffffu)
+    if (inner > 0x7fffffffu || rows * nparts > 0x7fffffffu)
         return fail(PXQ_ERR_UNSUPPORTED, "weight shape [%zu, %zu] exceeds INT32_MAX", inner, rows);
     std::string k = key ? std::string(key) : std::string();
     if (!k.empty()) {
         std::lock_guard<std::mutex> lock(g_mutex);
         auto it = g_cache.find(k);
         if (it != g_cache.end() && it->second->device == t_device) {
+            if (it->second->gated != (nparts == 2))
+                return fail(PXQ_ERR_INVALID, "cached weight \"%s\" was uploaded %s gated", k.c_str(), nparts == 2 ? "not" : "as");
             *out = it->second;
             return PXQ_OK;
         }
@@ -704,7 +746,8 @@ int pxq_weight_upload(const void* bytes, int bytes_on_device, uint32_t type, siz
     auto w = std::make_unique<pxq_weight>();
     w->type = type;
     w->inner = (int64_t)inner;
-    w->rows = (int64_t)rows;
+    w->rows = (int64_t)(rows * nparts);
+    w->gated = nparts == 2;
     w->stride = (int64_t)pxq_weight_bytes(inner, 1, type);
     w->device = t_device;
     w->key = k;
@@ -713,34 +756,15 @@ int pxq_weight_upload(const void* bytes, int bytes_on_device, uint32_t type, siz
     // Q6_K rows live on the device with every 210-byte super-block padded to
     // 224 bytes (16-byte multiples, as TMA rows need)
     if (q6) w->stride = (int64_t)(nsb * kQ6KPadBytes);
-    const uint64_t dev_bytes = q6 ? (uint64_t)w->stride * rows : total;
+    const uint64_t dev_bytes = (uint64_t)w->stride * (uint64_t)w->rows;
     if (cudaMalloc(&w->raw, dev_bytes + 64) != cudaSuccess) {
         cudaGetLastError();
         return fail(PXQ_ERR_NO_MEMORY, "cannot allocate %llu bytes for weight", (unsigned long long)dev_bytes);
     }
     PXQ_CUDA(cudaMemset(w->raw + dev_bytes, 0, 64));
-    if (!q6) {
-        PXQ_CUDA(cudaMemcpy(w->raw, bytes, total, bytes_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
-    } else {
-        const void* src = bytes;
-        void* tmp = nullptr;
-        if (!bytes_on_device || (reinterpret_cast<uintptr_t>(bytes) & 1u)) {
-            if (cudaMalloc(&tmp, total) != cudaSuccess) {
-                cudaGetLastError();
-                return fail(PXQ_ERR_NO_MEMORY, "cannot allocate %llu bytes of upload staging", (unsigned long long)total);
-            }
-            const cudaError_t e = cudaMemcpy(tmp, bytes, total, bytes_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
-            if (e != cudaSuccess) {
-                cudaFree(tmp);
-                return fail(PXQ_ERR_CUDA, "weight copy failed: %s", cudaGetErrorString(e));
-            }
-            src = tmp;
-        }
-        cudaError_t e = launch_pad_q6_K(src, w->raw, (int64_t)(nsb * rows), nullptr);
-        if (e == cudaSuccess) e = cudaDeviceSynchronize();
-        if (tmp) cudaFree(tmp);
-        if (e != cudaSuccess) return fail(PXQ_ERR_CUDA, "Q6_K padding failed: %s", cudaGetErrorString(e));
-    }
+    for (int i = 0; i < nparts; i++)
+        if (int rc = copy_rows(w.get(), parts[i], bytes_on_device, (int64_t)(i * rows), (int64_t)rows)) return rc;
+    const uint64_t all_rows = (uint64_t)w->rows;
     std::memset(w->mv_map, 0, sizeof(w->mv_map));
     if (type == PXQ_TYPE_Q5_K || q6) {
         // the matvec's TMA views, one box = one stage of a tr-row tile
@@ -750,14 +774,14 @@ int pxq_weight_upload(const void* bytes, int bytes_on_device, uint32_t type, siz
         const uint32_t sbb = q6 ? kQ6KPadBytes : kQ5KBytes;
         if (!q6) {
             if (int rc = make_map(d, &w->mv_map[matvec_map_index(64)], CU_TENSOR_MAP_DATA_TYPE_UINT64, w->raw,
-                                  (uint64_t)w->stride / 8, rows, (uint64_t)w->stride,
+                                  (uint64_t)w->stride / 8, all_rows, (uint64_t)w->stride,
                                   (uint32_t)(kMvStageSuperBlocks / 4 * kQ5KBytes / 8), 64, CU_TENSOR_MAP_SWIZZLE_NONE))
                 return rc;
         }
         for (int tr : {64, 32, 16}) {
             if (tr == 64 && !q6) continue;
-            if (int rc = make_map3(d, &w->mv_map[matvec_map_index(tr)], CU_TENSOR_MAP_DATA_TYPE_UINT64, w->raw, sbb / 8, rows,
-                                   nsb, (uint64_t)w->stride, sbb, sbb / 8, (uint32_t)tr,
+            if (int rc = make_map3(d, &w->mv_map[matvec_map_index(tr)], CU_TENSOR_MAP_DATA_TYPE_UINT64, w->raw, sbb / 8,
+                                   all_rows, nsb, (uint64_t)w->stride, sbb, sbb / 8, (uint32_t)tr,
                                    (uint32_t)(kMvStageSuperBlocks * 16 / tr)))
                 return rc;
         }
@@ -769,6 +793,31 @@ int pxq_weight_upload(const void* bytes, int bytes_on_device, uint32_t type, siz
     }
     *out = raw;
     return PXQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int pxq_weight_upload(const void* bytes, int bytes_on_device, uint32_t type, size_t inner, size_t rows, const char* key,
+                      pxq_weight** out)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (!bytes || !out) return fail(PXQ_ERR_INVALID, "null bytes or out");
+    const void* parts[1] = {bytes};
+    return create_weight(d, parts, 1, bytes_on_device, type, inner, rows, key, out);
+}
+
+int pxq_weight_upload_gated(const void* gate, const void* up, int bytes_on_device, uint32_t type, size_t inner, size_t rows,
+                            const char* key, pxq_weight** out)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (!gate || !up || !out) return fail(PXQ_ERR_INVALID, "null gate, up or out");
+    if (rows % 64) return fail(PXQ_ERR_UNSUPPORTED, "gated weights need a multiple of 64 rows (got %zu)", rows);
+    const void* parts[2] = {gate, up};
+    return create_weight(d, parts, 2, bytes_on_device, type, inner, rows, key, out);
 }
 
 int pxq_weight_release(pxq_weight* w)
@@ -826,6 +875,46 @@ int pxq_matmul(pxq_weight* w, size_t row_first, size_t row_count, const float* i
     if (int rc = check_matmul_args(w, row_first, row_count, input, columns, output, ldy)) return rc;
     return run_matmul(d, w, row_first, row_count, input, columns, output, ldy, bias, nullptr, 0,
                       static_cast<cudaStream_t>(stream));
+}
+
+int pxq_matmul_gated(pxq_weight* w, const float* input, size_t columns, float* output, size_t ldy, void* stream)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (!w || !input || !output) return fail(PXQ_ERR_INVALID, "null weight, input or output");
+    if (!w->gated) return fail(PXQ_ERR_INVALID, "weight was not uploaded with pxq_weight_upload_gated");
+    if (!columns) return fail(PXQ_ERR_INVALID, "zero columns");
+    const int64_t F = w->rows / 2;
+    if (ldy < (size_t)F && columns > 1) return fail(PXQ_ERR_INVALID, "ldy %zu < %lld output rows", ldy, (long long)F);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (columns > 8) {
+        // tensor-core GEMM over the interleaved 2F rows, silu(gate) * up in its epilogue
+        pxq_activation* a = nullptr;
+        int rc = quantize_activation(d, w->type, input, (int64_t)columns, w->inner, 2, &a, s);
+        if (rc) return rc;
+        rc = run_gemm(d, w, 0, (size_t)w->rows, a, output, ldy, nullptr, nullptr, s);
+        free_activation(a, s);
+        return rc;
+    }
+    // matvec over the 2F rows into scratch after the matvec's own, then the epilogue
+    const MatvecPlan plan = plan_matvec(w->type, w->rows, w->inner, (int64_t)columns, d->sms, true);
+    const size_t off_s = (plan.total_bytes + 255) & ~(size_t)255;
+    const size_t need = off_s + (size_t)columns * (size_t)w->rows * 4;
+    void* scratch = stream_scratch(t_device, s, need);
+    const bool own = scratch == nullptr;
+    if (own && cudaMallocAsync(&scratch, need, s) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(PXQ_ERR_NO_MEMORY, "gated matvec scratch allocation of %zu bytes failed", need);
+    }
+    if (own && plan.fused && plan.counter_bytes)  // fresh memory: no quantize kernel clears the counters
+        PXQ_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(scratch) + plan.off_counters, 0, plan.counter_bytes, s));
+    float* sums = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + off_s);
+    cudaError_t e = matvec_fused(w, 0, (size_t)w->rows, input, sums, (size_t)w->rows, nullptr, plan,
+                                 static_cast<uint8_t*>(scratch), d->status, s);
+    if (e == cudaSuccess) e = counted(launch_gate_rows(sums, (int64_t)columns, F, output, (int64_t)ldy, s));
+    if (own) cudaFreeAsync(scratch, s);
+    if (e != cudaSuccess) return fail(PXQ_ERR_CUDA, "gated matvec launch failed: %s", cudaGetErrorString(e));
+    return PXQ_OK;
 }
 
 int pxq_gemm_block_dots(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* dump,

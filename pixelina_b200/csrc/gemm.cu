@@ -134,8 +134,8 @@ template <uint32_t TYPE>
 __host__ __device__ constexpr int staging_bytes() { return DRAIN_WARPS * Cfg<TYPE>::SROWS * 32 * 4; }
 template <uint32_t TYPE>
 __host__ __device__ constexpr int off_bar() { return off_staging<TYPE>() + staging_bytes<TYPE>(); }
-// full/empty, min full/empty, entry full/empty, slot full/empty, MMA drain-out
-constexpr int NUM_BARS = 2 * MAX_STAGES + 2 * DEPTH + 2 * MAX_SB_DEPTH + 2 * 4 + 1;
+// full/empty, min full/empty, entry full/empty, slot full/empty, MMA drain-out, gated hand-over
+constexpr int NUM_BARS = 2 * MAX_STAGES + 2 * DEPTH + 2 * MAX_SB_DEPTH + 2 * 4 + 1 + 2;
 template <uint32_t TYPE>
 __host__ __device__ constexpr int smem_bytes() { return off_bar<TYPE>() + NUM_BARS * 8 + 16 + 1024; }
 
@@ -164,6 +164,7 @@ struct Params {
     float* dump;
     uint32_t* status;
     int tma_store;  // 1: epilogue through shared memory + TMA store (tmY)
+    int gated;      // 1: gated weight, y = silu(gate) * up over N/2 outputs (direct stores)
 };
 
 // tcgen05 and stage-load forms for one CTA per tile (CG = 1) or a CTA pair
@@ -304,6 +305,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t* tfull = sempty + MAX_SB_DEPTH; // accumulator slot complete (both CTAs)
     uint64_t* tempty = tfull + 4;            // even CTA: slot drained by both CTAs
     uint64_t* mma_done = tempty + 4;         // even CTA: every issued MMA finished (exit path)
+    uint64_t* merge = mma_done + 1;          // gated epilogue: hand-over buffer free / written
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
     volatile uint32_t* abort_flag = tmem_slot + 1;
     uint8_t* min_region = smem + off_min<TYPE>();
@@ -331,6 +333,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&tempty[i], CG * DRAIN_WARPS);  // the drain warps of every CTA of the tile
         }
         mbar_init(mma_done, 1);
+        mbar_init(&merge[0], DRAIN_WARPS);
+        mbar_init(&merge[1], DRAIN_WARPS);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -565,8 +569,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
         };
         int slot = 0, se = 0;
-        uint32_t tph = 0, sph = 0;
+        uint32_t tph = 0, sph = 0, mgph = 0;
         uint64_t gsb = 0, item = 0;
+        // all drain warps meet (bounded wait, like every wait of this kernel)
+        auto drain_meet = [&](int i) -> bool {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&merge[i]);
+            return mbar_wait(&merge[i], mgph, abort_flag, status, kDevTimeoutTmemFull);
+        };
         for (int64_t tile = pair; tile < tiles; tile += pairs) {
             const int64_t m0 = (tile % mt_count) * TMP;
             const int64_t n0 = (tile / mt_count) * CG * TN + rank * TN;  // view-local, this CTA's rows
@@ -656,7 +666,39 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                 }
             }
-            if (!DUMP) {
+            if (!DUMP && p.gated) {
+                // gated weight: this CTA's lanes 64..127 hold the up projection of the
+                // outputs whose gate projection lanes 0..63 hold (the repack interleaves
+                // 64-row groups); the up warps hand their sums over through the staging
+                // buffer and the gate warps finish tensor_silu + tensor_gate
+                // (src/tensor.cpp:199-208, :334-345)
+                float* xfer = reinterpret_cast<float*>(smem + off_staging<TYPE>()) + ((quad & 1) * 2 + half) * (HC * 32);
+                if (!drain_meet(0)) goto done;  // the previous tile's hand-over has been read
+                if (quad >= 2) {
+#pragma unroll
+                    for (int i = 0; i < HC; i++) xfer[i * 32 + lane] = acc[i];
+                }
+                if (!drain_meet(1)) goto done;
+                mgph ^= 1u;
+                if (quad < 2) {
+#pragma unroll
+                    for (int i = 0; i < HC; i++) {
+                        // element i's output row (lane) and activation row (column)
+                        int lo, col;
+                        if (SPLIT) {
+                            const int c = i & 1, h = (i >> 1) & 1, k = (i >> 2) & 7, lh = (i >> 5) & 1, ch = i >> 6;
+                            lo = 16 * lh + 8 * h + (int)(lane >> 2);
+                            col = 64 * ch + 8 * k + 2 * (int)(lane & 3) + c;
+                        } else {
+                            lo = (int)lane;
+                            col = i;
+                        }
+                        const int64_t on = n0 / 2 + quad * 32 + lo, m = mfirst + col;
+                        const float g = acc[i], u = xfer[i * 32 + lane];
+                        if (on < p.N / 2 && m < p.M) p.y[m * p.ldy + on] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+                    }
+                }
+            } else if (!DUMP) {
                 // this thread's lanes (weight rows, CTA-local): row layout (Q8_0) the
                 // thread's own lane; split layout lane_off(lh, h) = 16lh + 8h + lane/4
                 float bv[4];
@@ -786,7 +828,7 @@ cudaError_t launch_typed(const GemmOperands& op, int num_sms, cudaStream_t s)
     if (tiles < groups) groups = tiles;
     if (groups < 1) groups = 1;
     cfg.gridDim = dim3((unsigned)(CG * groups));
-    Params p{op.M, op.N, op.K, op.n_first, op.y, op.ldy, op.bias, op.dump, op.status, (op.tma_store && !DUMP) ? 1 : 0};
+    Params p{op.M, op.N, op.K, op.n_first, op.y, op.ldy, op.bias, op.dump, op.status, (op.tma_store && !DUMP) ? 1 : 0, op.gated};
     return cudaLaunchKernelEx(&cfg, kern, op.tm[0], op.tm[1], op.tm[2], op.tm[3], op.tm[4], op.tm[5], op.tm[6], op.tm_y, p);
 }
 

@@ -75,7 +75,7 @@ extern "C" int pxq_matvec_noalloc(pxq_weight* w, size_t row_first, size_t row_co
     const uint8_t* raw = nullptr;
     int wdev = -1;
     if (!w || !input || !output || !pxq::weight_view(w, &type, &inner, &rows, &stride, &raw, &wdev))
-        return noalloc_fail(PXQ_ERR_INVALID, "null weight, input or output");
+        return noalloc_fail(PXQ_ERR_INVALID, "null or gated weight, null input or output");
     if (!columns || !row_count || columns > 8)
         return noalloc_fail(PXQ_ERR_INVALID, "columns must be 1..8 and row_count > 0");
     if (row_first > (size_t)rows || row_count > (size_t)rows - row_first)

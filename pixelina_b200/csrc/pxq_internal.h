@@ -39,13 +39,20 @@ cudaError_t launch_pad_q6_K(const void* src, void* dst, int64_t superblocks, cud
 
 // ---- repack.cu -------------------------------------------------------------
 // One-time weight repack into the GEMM operand layout (bit-exact unpack).
+// gate_rows = F > 0: a gated weight (F gate rows, then F up rows) packed as
+// 128-row groups [64 gate rows j..j+63][the 64 matching up rows].
 cudaError_t launch_repack_q8_0(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wq, __half* ws1h,
-                               cudaStream_t s);
+                               int64_t gate_rows, cudaStream_t s);
 cudaError_t launch_repack_q5_K(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wv, float* dT,
-                               float* dminT, __half* bmin, int64_t ldn, cudaStream_t s);
+                               float* dminT, __half* bmin, int64_t ldn, int64_t gate_rows, cudaStream_t s);
 // Q6_K: raw rows are the device's padded super-blocks (stride bytes per row).
 cudaError_t launch_repack_q6_K(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wab, float* dT,
-                               int64_t ldn, cudaStream_t s);
+                               int64_t ldn, int64_t gate_rows, cudaStream_t s);
+
+// y[c*ldy + n] = silu(s[c*2F + n]) * s[c*2F + F + n] for c < columns, n < F:
+// the gated epilogue after a matvec over a gated weight's 2F rows
+// (tensor_silu then tensor_gate, src/tensor.cpp:199-208, :334-345).
+cudaError_t launch_gate_rows(const float* s, int64_t columns, int64_t F, float* y, int64_t ldy, cudaStream_t st);
 
 cudaError_t launch_decode(const uint8_t* data, uint32_t type, int64_t count, float* out, cudaStream_t s);
 
@@ -146,6 +153,7 @@ struct GemmOperands {
     int64_t ldy;
     const float* bias;    // may be null (indexed by view-local column)
     float* dump;          // debug: raw per-item block dots, or null
+    int gated;            // gated weight (2F interleaved rows, N = 2F): y[m][n < F] = silu(gate) * up
     uint32_t* status;     // device status word
 };
 // Rows of one CTA's activation box in the GEMM's tensor maps (tmX, tmXs),

@@ -44,14 +44,25 @@ __device__ __forceinline__ float load_half(const uint8_t* p)
     return __half2float(__ushort_as_half(bits));
 }
 
+// Raw row behind packed operand row r.  gate_rows = 0: r itself.  A gated
+// weight (F = gate_rows gate rows, then F up rows) packs as 128-row groups of
+// 64 gate rows and the 64 matching up rows, so that each GEMM CTA tile holds
+// both halves of its outputs.
+__device__ __forceinline__ int64_t src_row(int64_t r, int64_t gate_rows)
+{
+    if (!gate_rows) return r;
+    const int64_t j = r >> 7, q = r & 127;
+    return q < 64 ? 64 * j + q : gate_rows + 64 * j + (q - 64);
+}
+
 __global__ void k_repack_q8_0(const uint8_t* __restrict__ raw, int64_t rows, int64_t inner, int64_t stride,
-                              __half* __restrict__ wq, __half* __restrict__ ws1h)
+                              __half* __restrict__ wq, __half* __restrict__ ws1h, int64_t gate_rows)
 {
     const int64_t nb = inner / kQK8_0;
     const int64_t total = rows * nb;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = i / nb, b = i % nb;
-        const uint8_t* blk = raw + r * stride + b * kQ8_0Bytes;
+        const uint8_t* blk = raw + src_row(r, gate_rows) * stride + b * kQ8_0Bytes;
         __half h[32];
 #pragma unroll
         for (int j = 0; j < 32; j++) h[j] = __int2half_rn((int)(int8_t)blk[2 + j]);
@@ -70,7 +81,7 @@ __global__ void k_repack_q8_0(const uint8_t* __restrict__ raw, int64_t rows, int
 
 __global__ void k_repack_q5_K(const uint8_t* __restrict__ raw, int64_t rows, int64_t inner, int64_t stride,
                               __half* __restrict__ wv, float* __restrict__ dT, float* __restrict__ dminT,
-                              __half* __restrict__ bmin, int64_t ldn)
+                              __half* __restrict__ bmin, int64_t ldn, int64_t gate_rows)
 {
     const int64_t nsb = inner / kQKK;
     const int64_t total = rows * nsb * 8;
@@ -78,7 +89,7 @@ __global__ void k_repack_q5_K(const uint8_t* __restrict__ raw, int64_t rows, int
         const int g = (int)(i % 8);
         const int64_t sbi = i / 8;
         const int64_t r = sbi / nsb, sb = sbi % nsb;
-        const uint8_t* blk = raw + r * stride + sb * kQ5KBytes;
+        const uint8_t* blk = raw + src_row(r, gate_rows) * stride + sb * kQ5KBytes;
         int sc, mn;
         k_scale_min(blk + 4, g, sc, mn);
         const uint8_t* qh = blk + 16;
@@ -105,7 +116,7 @@ __global__ void k_repack_q5_K(const uint8_t* __restrict__ raw, int64_t rows, int
 // Q6_K rows as stored on the device: 224-byte padded super-blocks with the
 // GGUF field offsets (ql at 0, qh at 128, scales at 192, d at 208).
 __global__ void k_repack_q6_K(const uint8_t* __restrict__ raw, int64_t rows, int64_t inner, int64_t stride,
-                              __half* __restrict__ wab, float* __restrict__ dT, int64_t ldn)
+                              __half* __restrict__ wab, float* __restrict__ dT, int64_t ldn, int64_t gate_rows)
 {
     const int64_t nsb = inner / kQKK;
     const int64_t total = rows * nsb * 8;
@@ -113,7 +124,7 @@ __global__ void k_repack_q6_K(const uint8_t* __restrict__ raw, int64_t rows, int
         const int G = (int)(i % 8);  // values 32G .. 32G+31 of the super-block
         const int64_t sbi = i / 8;
         const int64_t r = sbi / nsb, sb = sbi % nsb;
-        const uint8_t* blk = raw + r * stride + sb * kQ6KPadBytes;
+        const uint8_t* blk = raw + src_row(r, gate_rows) * stride + sb * kQ6KPadBytes;
         const int h = G / 4, g = G % 4;
         const uint8_t* ql = blk + 64 * h + 32 * (g % 2);
         const uint8_t* qh = blk + 128 + 32 * h;
@@ -182,23 +193,24 @@ int grid_for(int64_t work, int threads)
 }  // namespace
 
 cudaError_t launch_repack_q8_0(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wq, __half* ws1h,
-                               cudaStream_t s)
+                               int64_t gate_rows, cudaStream_t s)
 {
-    k_repack_q8_0<<<grid_for(rows * (inner / kQK8_0), 256), 256, 0, s>>>(raw, rows, inner, stride, wq, ws1h);
+    k_repack_q8_0<<<grid_for(rows * (inner / kQK8_0), 256), 256, 0, s>>>(raw, rows, inner, stride, wq, ws1h, gate_rows);
     return cudaGetLastError();
 }
 
 cudaError_t launch_repack_q5_K(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wv, float* dT,
-                               float* dminT, __half* bmin, int64_t ldn, cudaStream_t s)
+                               float* dminT, __half* bmin, int64_t ldn, int64_t gate_rows, cudaStream_t s)
 {
-    k_repack_q5_K<<<grid_for(rows * (inner / kQKK) * 8, 256), 256, 0, s>>>(raw, rows, inner, stride, wv, dT, dminT, bmin, ldn);
+    k_repack_q5_K<<<grid_for(rows * (inner / kQKK) * 8, 256), 256, 0, s>>>(raw, rows, inner, stride, wv, dT, dminT, bmin, ldn,
+                                                                         gate_rows);
     return cudaGetLastError();
 }
 
 cudaError_t launch_repack_q6_K(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wab, float* dT,
-                               int64_t ldn, cudaStream_t s)
+                               int64_t ldn, int64_t gate_rows, cudaStream_t s)
 {
-    k_repack_q6_K<<<grid_for(rows * (inner / kQKK) * 8, 256), 256, 0, s>>>(raw, rows, inner, stride, wab, dT, ldn);
+    k_repack_q6_K<<<grid_for(rows * (inner / kQKK) * 8, 256), 256, 0, s>>>(raw, rows, inner, stride, wab, dT, ldn, gate_rows);
     return cudaGetLastError();
 }
 

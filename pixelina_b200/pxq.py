@@ -56,6 +56,8 @@ SIGNATURES = {
     "pxq_quantize_q8_K_matvec": (_i, [_vp, _vp, _sz, _sz, _vp]),
     "pxq_decode": (_i, [_vp, _u32, _sz, _vp, _vp]),
     "pxq_weight_upload": (_i, [_vp, _i, _u32, _sz, _sz, C.c_char_p, C.POINTER(_vp)]),
+    "pxq_weight_upload_gated": (_i, [_vp, _vp, _i, _u32, _sz, _sz, C.c_char_p, C.POINTER(_vp)]),
+    "pxq_matmul_gated": (_i, [_vp, _vp, _sz, _vp, _sz, _vp]),
     "pxq_weight_release": (_i, [_vp]),
     "pxq_weight_cache_clear": (_i, []),
     "pxq_matmul": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _sz, _vp, _vp]),
@@ -201,6 +203,50 @@ class Weight:
         if self.handle:
             _check(load().pxq_weight_release(self.handle))
             self.handle = C.c_void_p()
+
+
+class GatedWeight:
+    """The gate and up projections of a gated feed-forward, resident on the
+    current device as one weight (pxq_weight_upload_gated)."""
+
+    def __init__(self, gate, up, wtype: int, inner: int, rows: int, key: Optional[str] = None):
+        lib = load()
+        self.wtype, self.inner, self.rows = wtype, inner, rows
+        keep, ptrs, on_dev = [], [], 0
+        for data in (gate, up):
+            if hasattr(data, "data_ptr"):
+                on_dev = 1 if data.is_cuda else 0
+                ptrs.append(C.c_void_p(data.data_ptr()))
+                keep.append(data)
+            else:
+                arr = np.ascontiguousarray(data, dtype=np.uint8)
+                ptrs.append(arr.ctypes.data_as(C.c_void_p))
+                keep.append(arr)
+        handle = C.c_void_p()
+        kb = key.encode() if key else None
+        _check(lib.pxq_weight_upload_gated(ptrs[0], ptrs[1], on_dev, wtype, inner, rows, kb, C.byref(handle)))
+        self.handle = handle
+
+    def release(self) -> None:
+        if self.handle:
+            _check(load().pxq_weight_release(self.handle))
+            self.handle = C.c_void_p()
+
+
+def matmul_gated(w: GatedWeight, x, out=None, ldy: Optional[int] = None, stream=None):
+    """Y[c, r] = silu(x[c] . gate[r]) * (x[c] . up[r]) on the device."""
+    torch = _torch()
+    x = x.contiguous()
+    columns, inner = x.shape
+    if inner != w.inner:
+        raise ValueError(f"input has {inner} features, weight expects {w.inner}")
+    if out is None:
+        out = torch.empty((columns, w.rows), dtype=torch.float32, device=x.device)
+        ldy = w.rows
+    elif ldy is None:
+        ldy = out.stride(0)
+    _check(load().pxq_matmul_gated(w.handle, _ptr(x), columns, _ptr(out), ldy, _stream_ptr(stream)))
+    return out
 
 
 def matmul(w: Weight, x, row_first: int = 0, row_count: Optional[int] = None, bias=None, out=None, ldy: Optional[int] = None,

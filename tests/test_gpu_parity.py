@@ -299,3 +299,43 @@ def test_gather_shards(pxq):
     out = pxq.gather_shards(src, shards, columns, shard_rows)
     want = src.view(shards, columns, shard_rows).permute(1, 0, 2).reshape(columns, shards * shard_rows)
     assert torch.equal(out, want)
+
+
+# ------------------------------------------------------------ gated matmul --
+
+def _silu_gate(g, u):
+    # tensor_silu then tensor_gate (src/tensor.cpp:199-208, :334-345), in fp32
+    g = g.astype(np.float32)
+    return (g / (np.float32(1.0) + np.exp(-g))).astype(np.float32) * u.astype(np.float32)
+
+
+@pytest.mark.parametrize("wtype", [Q8_0, Q5_K, Q6_K])
+@pytest.mark.parametrize("rows,columns", [(192, 1), (64, 5), (320, 8), (192, 9), (320, 140), (2048, 300)])
+def test_matmul_gated_vs_oracle(pxq, oracle, wtype, rows, columns):
+    """pxq_matmul_gated = the callers' gate/up linears, tensor_silu, tensor_gate:
+    the matvec path (<= 8 rows) and the GEMM with the gate in its epilogue
+    (the repack interleaves gate and up rows in 64-row groups)."""
+    inner = 512
+    g = synth.weights_for(wtype, rows, inner, seed=21)
+    u = synth.weights_for(wtype, rows, inner, seed=22)
+    x = synth.activations(columns, inner, seed=23)
+    W = pxq.GatedWeight(g, u, wtype, inner, rows)
+    y = pxq.matmul_gated(W, cuda(x)).cpu().numpy()
+    pxq.synchronize()
+    okg, G = oracle.quant_matmul(g, wtype, x, rows)
+    oku, U = oracle.quant_matmul(u, wtype, x, rows)
+    assert okg and oku
+    assert max_abs_rel(y, _silu_gate(G, U)) <= TOL
+    # a strided output leaves the padding untouched
+    import torch
+
+    out = torch.full((columns, rows + 5), float("nan"), device="cuda")
+    pxq.matmul_gated(W, cuda(x), out=out, ldy=rows + 5)
+    pxq.synchronize()
+    got = out.cpu().numpy()
+    assert max_abs_rel(got[:, :rows], _silu_gate(G, U)) <= TOL and np.isnan(got[:, rows:]).all()
+    # the gated weight serves pxq_matmul_gated only
+    with pytest.raises(pxq.PxqError) as err:
+        pxq.matmul(W, cuda(x))
+    assert err.value.code == pxq.ERR_INVALID
+    W.release()
