@@ -8,7 +8,7 @@ tensor-core GEMM, inputs resident in HBM; L2 is flushed (256 MB write)
 between timed steps, outside the timed events.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload q5k_gemm|q8_0_gemm|q8_0_large|q6k_gemm|dit|decode|decode_shapes|sharded]
+                    [--workload q5k_gemm|q8_0_gemm|q8_0_large|q6k_gemm|dit|decode|decode_gated|decode_shapes|sharded]
 
 Multi-GPU (torchrun, one rank per GPU): each rank processes its own batch of
 activation rows against the same weights (data parallel over independent
@@ -483,9 +483,11 @@ def run_reference(args, dist: Dist):
 
 # ---------------------------------------------------- other workloads ---
 
-def run_decode(args, dist: Dist):
+def run_decode(args, dist: Dist, gated: bool = False):
     """Q5_K decode, 28 layers, M in {1,4,8}; one step =
-    one token through every layer's 7 matvecs.  Metric: weight GB/s."""
+    one token through every layer's matvecs (QKV, out, gate, up, down).
+    gated: gate and up as one pxq_matmul_gated call, silu(gate) * up included
+    (the callers' tensor_silu + tensor_gate).  Metric: weight GB/s."""
     import torch
 
     from pixelina_b200 import pxq
@@ -499,6 +501,11 @@ def run_decode(args, dist: Dist):
     for _ in range(L):
         ws = {}
         for name, n, k in shapes:
+            if gated and name == "up":
+                continue
+            if gated and name == "gate":
+                ws["gate_up"] = pxq.GatedWeight(gpu_random_q5_K(n, k, gen), gpu_random_q5_K(n, k, gen), Q5_K, k, n)
+                continue
             ws[name] = pxq.Weight(gpu_random_q5_K(n, k, gen), Q5_K, k, n)
         layers.append(ws)
     torch.cuda.synchronize()
@@ -512,6 +519,11 @@ def run_decode(args, dist: Dist):
         def token():
             for ws in layers:
                 for name, n, k in shapes:
+                    if gated and name == "up":
+                        continue
+                    if gated and name == "gate":
+                        pxq.matmul_gated(ws["gate_up"], xs[k], out=ys[n])
+                        continue
                     pxq.matmul(ws[name], xs[k], out=ys[n], path="matvec")
 
         # one token = 140 matvecs (each: activation quantize + matvec); replay it as a
@@ -545,7 +557,9 @@ def run_decode(args, dist: Dist):
         results[f"M={M}"] = {"ms_per_token": round(ms, 4), "weight_GBps": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
                              "clocks": clocks}
         del graph
-    return {"metric": METRIC, "workload": "decode: Q5_K matvec, 28 layers (BASELINE configs[3])", "unit": "GB/s",
+    name = "decode_gated: Q5_K matvec, 28 layers, gate/up as one gated call" if gated else \
+        "decode: Q5_K matvec, 28 layers (BASELINE configs[3])"
+    return {"metric": METRIC, "workload": name, "unit": "GB/s",
             "weight_bytes_per_token": wbytes_total, "peak_hbm_gbs": hbm, "peak_source": peak_src,
             "launches_per_token": 2 * 5 * L, "results": results}
 
@@ -716,7 +730,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="q5k_gemm",
-                    choices=sorted(GEMM_WORKLOADS) + ["decode", "decode_shapes", "dit", "sharded"])
+                    choices=sorted(GEMM_WORKLOADS) + ["decode", "decode_gated", "decode_shapes", "dit", "sharded"])
     ap.add_argument("--soak", type=float, default=1.5, help="seconds of untimed steps before timing (clock settling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -733,6 +747,8 @@ def main():
             out = run_gemm_workload(args, dist, GEMM_WORKLOADS[args.workload])
         elif args.workload == "decode":
             out = run_decode(args, dist)
+        elif args.workload == "decode_gated":
+            out = run_decode(args, dist, gated=True)
         elif args.workload == "decode_shapes":
             out = run_decode_shapes(args, dist)
         elif args.workload == "dit":
