@@ -37,6 +37,8 @@ extern "C" {
 #define PXQ_ERR_NO_MEMORY 4     /* device allocation failed */
 #define PXQ_ERR_NO_DEVICE 5     /* no usable sm_100 device */
 #define PXQ_ERR_DEVICE_STATUS 6 /* a kernel reported a bounded-wait timeout */
+#define PXQ_ERR_IO 7            /* a model file could not be opened or mapped */
+#define PXQ_ERR_FORMAT 8        /* a model file is not a GGUF v3 file this loader accepts */
 
 /* GGML type ids, src/model_types.h:13-21 */
 #define PXQ_TYPE_F32 0
@@ -237,6 +239,48 @@ PXQ_API int pxq_matvec_noalloc(pxq_weight* w, size_t row_first, size_t row_count
  * :163-254, :256-337), exact as floats. */
 PXQ_API int pxq_gemm_block_dots(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* dump,
                         void* stream);
+
+/* ---- GGUF model files: the format step in front of the upload ---------- */
+
+/* A GGUF v3 file mapped read-only, its tensor directory parsed with the
+ * acceptance rules of Pixelina's loader (PixModelFile::open,
+ * src/model.cpp:138-251). */
+typedef struct pxq_gguf pxq_gguf;
+
+/* One tensor of the directory (PixWeight, src/model.h:33-39). */
+typedef struct {
+    const char* name;    /* valid while the file is open */
+    uint32_t type;       /* GGML type id (PXQ_TYPE_*) */
+    uint32_t rank;       /* 1..5 */
+    uint64_t shape[5];   /* GGML order: shape[0] is contiguous (inner) */
+    uint64_t offset;     /* absolute byte offset of the tensor data in the file */
+    uint64_t bytes;      /* storage bytes */
+} pxq_gguf_tensor;
+
+/* Open and parse; PXQ_ERR_IO when the file cannot be opened or mapped,
+ * PXQ_ERR_FORMAT where the reference's loader returns MODEL_ERROR_FORMAT. */
+PXQ_API int pxq_gguf_open(const char* path, pxq_gguf** out);
+PXQ_API int pxq_gguf_close(pxq_gguf* f);
+PXQ_API size_t pxq_gguf_tensor_count(const pxq_gguf* f);
+PXQ_API size_t pxq_gguf_metadata_count(const pxq_gguf* f);
+/* The mapped file (tensor bytes at data + offset). */
+PXQ_API const void* pxq_gguf_data(const pxq_gguf* f);
+/* Tensor `index` in name order (the reference's std::map order). */
+PXQ_API int pxq_gguf_tensor_at(const pxq_gguf* f, size_t index, pxq_gguf_tensor* out);
+PXQ_API int pxq_gguf_find(const pxq_gguf* f, const char* name, pxq_gguf_tensor* out);
+
+/* Upload rows [row_first, row_first + row_count) of a Q8_0 / Q5_K / Q6_K
+ * tensor (row_count 0: to the end) through pxq_weight_upload, cached under
+ * "file:name:offset:bytes" of the row range -- the Vulkan backend's weight
+ * cache identity (src/backend_vulkan.cpp:742-758), which also gives
+ * tensor_linear_rows views (src/tensor.cpp:529-544) their own entry. */
+PXQ_API int pxq_gguf_upload(pxq_gguf* f, const char* name, size_t row_first, size_t row_count, pxq_weight** out);
+
+/* Upload a gated pair for pxq_matmul_gated: `rows` rows of tensor `gate`
+ * from gate_first and of tensor `up` from up_first (the same tensor for the
+ * DiT's fused gate/up, src/qwen_image.cpp:271). */
+PXQ_API int pxq_gguf_upload_gated(pxq_gguf* f, const char* gate, size_t gate_first, const char* up, size_t up_first,
+                                  size_t rows, pxq_weight** out);
 
 #ifdef __cplusplus
 }

@@ -171,6 +171,23 @@ class Reference(_Lib):
     def set_threads(self, n: int) -> None:
         self.lib.pixref_set_threads(n)
 
+    def gguf_list(self, path: str, cap: int = 256):
+        """PixModelFile::open on `path`: (result code, tensors in name order, metadata key count)."""
+
+        class T(C.Structure):
+            _fields_ = [("name", C.c_char * 256), ("type", C.c_uint32), ("rank", C.c_uint32), ("shape", C.c_uint64 * 5),
+                        ("offset", C.c_uint64), ("bytes", C.c_uint64)]
+
+        buf = (T * cap)()
+        count, keys = C.c_size_t(0), C.c_size_t(0)
+        fn = self.lib.pixref_gguf_list
+        fn.argtypes = [C.c_char_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]
+        fn.restype = C.c_int
+        rc = fn(path.encode(), C.cast(buf, C.c_void_p), cap, C.byref(count), C.byref(keys))
+        tensors = [{"name": buf[i].name.decode(), "type": int(buf[i].type), "shape": [int(v) for v in buf[i].shape[:buf[i].rank]],
+                    "offset": int(buf[i].offset), "bytes": int(buf[i].bytes)} for i in range(min(count.value, cap))]
+        return int(rc), tensors, int(keys.value)
+
     def thread_count(self) -> int:
         return int(self.lib.pixref_thread_count())
 

@@ -11,9 +11,22 @@
  * reference translation unit src/kernels_quant.cpp is included here whole
  * (unmodified) to reach them; everything else links against the reference's
  * other objects (tensor.cpp for cpu_parallel, backend_cpu.cpp for cpu_decode,
- * model.cpp for weight_bytes, ...).
+ * model.cpp for weight_bytes and the GGUF loader, ...).
  */
 #include "kernels_quant.cpp"
+#include "model.h"
+
+#include <cstring>
+
+// One tensor of a model file as the reference's loader parsed it.
+struct PixrefTensor {
+    char name[256];
+    uint32_t type;
+    uint32_t rank;
+    uint64_t shape[5];
+    uint64_t offset;
+    uint64_t bytes;
+};
 
 extern "C" {
 
@@ -55,6 +68,34 @@ void pixref_decode(const unsigned char* data, uint32_t type, size_t count, float
 uint64_t pixref_weight_bytes(uint64_t inner, uint64_t rows, uint32_t type)
 {
     return weight_bytes({inner, rows}, type);
+}
+
+// Open a GGUF file with PixModelFile::open (src/model.cpp:138-251): returns
+// its result (0, MODEL_ERROR_OPEN or MODEL_ERROR_FORMAT); on success the
+// tensor directory in name order (the std::map's order) goes to `out` (up to
+// `cap` entries) and the count to *count, the metadata key count to *keys.
+int pixref_gguf_list(const char* path, PixrefTensor* out, size_t cap, size_t* count, size_t* keys)
+{
+    PixModelFile file;
+    const int rc = file.open(path, false);
+    *count = 0;
+    *keys = 0;
+    if (rc) return rc;
+    *keys = file.metadata.size();
+    for (const auto& entry : file.weights) {
+        if (*count < cap) {
+            PixrefTensor& t = out[*count];
+            std::memset(&t, 0, sizeof(t));
+            std::strncpy(t.name, entry.second.name.c_str(), sizeof(t.name) - 1);
+            t.type = entry.second.type;
+            t.rank = (uint32_t)entry.second.shape.size();
+            for (size_t d = 0; d < entry.second.shape.size() && d < 5; d++) t.shape[d] = entry.second.shape[d];
+            t.offset = entry.second.offset;
+            t.bytes = entry.second.bytes;
+        }
+        (*count)++;
+    }
+    return 0;
 }
 
 void pixref_set_threads(size_t count)

@@ -73,7 +73,31 @@ SIGNATURES = {
     "pxq_activation_release": (_i, [_vp, _vp]),
     "pxq_kernel_launches": (_u64, []),
     "pxq_matvec_noalloc": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _sz, _vp, _vp]),
+    "pxq_gguf_open": (_i, [C.c_char_p, C.POINTER(_vp)]),
+    "pxq_gguf_close": (_i, [_vp]),
+    "pxq_gguf_tensor_count": (_sz, [_vp]),
+    "pxq_gguf_metadata_count": (_sz, [_vp]),
+    "pxq_gguf_data": (_vp, [_vp]),
+    "pxq_gguf_tensor_at": (_i, [_vp, _sz, _vp]),
+    "pxq_gguf_find": (_i, [_vp, C.c_char_p, _vp]),
+    "pxq_gguf_upload": (_i, [_vp, C.c_char_p, _sz, _sz, C.POINTER(_vp)]),
+    "pxq_gguf_upload_gated": (_i, [_vp, C.c_char_p, _sz, C.c_char_p, _sz, _sz, C.POINTER(_vp)]),
 }
+
+
+ERR_IO = 7
+ERR_FORMAT = 8
+
+
+class GGUFTensor(C.Structure):
+    """pxq_gguf_tensor (include/pxq.h)."""
+
+    _fields_ = [("name", C.c_char_p), ("type", C.c_uint32), ("rank", C.c_uint32), ("shape", C.c_uint64 * 5),
+                ("offset", C.c_uint64), ("bytes", C.c_uint64)]
+
+    def as_dict(self) -> dict:
+        return {"name": self.name.decode(), "type": int(self.type), "shape": [int(v) for v in self.shape[:self.rank]],
+                "offset": int(self.offset), "bytes": int(self.bytes)}
 
 
 class PxqError(RuntimeError):
@@ -231,6 +255,71 @@ class GatedWeight:
         if self.handle:
             _check(load().pxq_weight_release(self.handle))
             self.handle = C.c_void_p()
+
+
+class _Uploaded:
+    """A weight uploaded from a model file (pxq_gguf_upload*)."""
+
+    def __init__(self, handle, wtype: int, inner: int, rows: int):
+        self.handle, self.wtype, self.inner, self.rows = handle, wtype, inner, rows
+
+    def release(self) -> None:
+        if self.handle:
+            _check(load().pxq_weight_release(self.handle))
+            self.handle = C.c_void_p()
+
+
+class GGUF:
+    """A GGUF model file opened with pxq_gguf_open (a read-only mapping)."""
+
+    def __init__(self, path: str):
+        h = C.c_void_p()
+        _check(load().pxq_gguf_open(path.encode(), C.byref(h)))
+        self.handle, self.path = h, path
+
+    def close(self) -> None:
+        if self.handle:
+            load().pxq_gguf_close(self.handle)
+            self.handle = C.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @property
+    def metadata_count(self) -> int:
+        return int(load().pxq_gguf_metadata_count(self.handle))
+
+    def tensors(self) -> list:
+        lib = load()
+        out = []
+        for i in range(int(lib.pxq_gguf_tensor_count(self.handle))):
+            t = GGUFTensor()
+            _check(lib.pxq_gguf_tensor_at(self.handle, i, C.byref(t)))
+            out.append(t.as_dict())
+        return out
+
+    def find(self, name: str) -> dict:
+        t = GGUFTensor()
+        _check(load().pxq_gguf_find(self.handle, name.encode(), C.byref(t)))
+        return t.as_dict()
+
+    def upload(self, name: str, row_first: int = 0, row_count: int = 0) -> _Uploaded:
+        t = self.find(name)
+        rows = 1
+        for v in t["shape"][1:]:
+            rows *= v
+        h = C.c_void_p()
+        _check(load().pxq_gguf_upload(self.handle, name.encode(), row_first, row_count, C.byref(h)))
+        return _Uploaded(h, t["type"], t["shape"][0], row_count or rows - row_first)
+
+    def upload_gated(self, gate: str, gate_first: int, up: str, up_first: int, rows: int) -> _Uploaded:
+        t = self.find(gate)
+        h = C.c_void_p()
+        _check(load().pxq_gguf_upload_gated(self.handle, gate.encode(), gate_first, up.encode(), up_first, rows, C.byref(h)))
+        return _Uploaded(h, t["type"], t["shape"][0], rows)
 
 
 def matmul_gated(w: GatedWeight, x, out=None, ldy: Optional[int] = None, stream=None):
