@@ -908,14 +908,17 @@ MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t colum
         const int64_t slots = (int64_t)num_sms * 2;  // two CTAs per SM
         // Whole tiles per CTA (no cross-CTA sums) when some tile height gives
         // a tile count that fills the grid well, or when the matrix is small
-        // enough that the extra wave costs less than the cross-CTA sums;
-        // otherwise 64-row tiles in a stream-K split over the whole grid.
+        // enough that the extra wave costs less than the cross-CTA sums (for
+        // Q5_K, 16-row tiles at any length: measured faster than stream-K on
+        // the 3584 x 18944 down projection); otherwise 64-row tiles in a
+        // stream-K split over the whole grid.
         p.tile_rows = 64;
         bool whole = false;
         for (int tr : {64, 32, 16}) {
             const int64_t tiles = (rows + tr - 1) / tr;
             const int64_t tile_bytes = (int64_t)tr * nsb * sb_bytes;
-            if (tiles <= slots && (tiles * 20 >= slots * 19 || (tiles * 4 >= slots * 3 && tile_bytes <= 64 * 1024))) {
+            const bool short_tiles = tile_bytes <= 64 * 1024 || (type == kTypeQ5_K && tr == 16);
+            if (tiles <= slots && (tiles * 20 >= slots * 19 || (tiles * 4 >= slots * 3 && short_tiles))) {
                 p.tile_rows = tr;
                 whole = true;
                 break;

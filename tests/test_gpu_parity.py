@@ -157,18 +157,20 @@ def test_q6_K_golden_past_the_matvec(pxq, golden):
 def test_matvec_scratch_reuse_across_schedules(pxq, oracle):
     """Consecutive calls on one stream share the matvec scratch: activation
     sizes, fused vs separate quantize and whole-tile vs stream-K alternate
-    (down-shape 3584x18944 at M=8 is stream-K with a separate quantize, at M=1
-    stream-K with the quantize fused into the matvec; QKV-shape whole tiles),
-    and every result must still match the oracle."""
+    (down-shape 3584x18944: whole 16-row tiles with a separate quantize; a
+    200x18944 slice: stream-K, the quantize fused into the matvec at M=1 and
+    separate at M=8; QKV-shape whole tiles, fused), and every result must still
+    match the oracle."""
     down = synth.random_q5_K(3584, 18944, np.random.default_rng(21))
     qkv = synth.random_q5_K(4608, 3584, np.random.default_rng(22))
     xd = synth.activations(8, 18944, seed=23)
     xq = synth.activations(8, 3584, seed=24)
     Wd = pxq.Weight(down, Q5_K, 18944, 3584)
+    Ws = pxq.Weight(down[:200], Q5_K, 18944, 200)
     Wq = pxq.Weight(qkv, Q5_K, 3584, 4608)
     refs = {}
-    for W, w, x, m in ((Wd, down, xd, 8), (Wd, down, xd, 1), (Wq, qkv, xq, 1), (Wd, down, xd, 2), (Wd, down, xd, 8),
-                       (Wq, qkv, xq, 8), (Wd, down, xd, 1)):
+    for W, w, x, m in ((Wd, down, xd, 8), (Ws, down[:200], xd, 1), (Wd, down, xd, 1), (Wq, qkv, xq, 1), (Ws, down[:200], xd, 8),
+                       (Wd, down, xd, 2), (Ws, down[:200], xd, 1), (Wd, down, xd, 8), (Wq, qkv, xq, 8), (Wd, down, xd, 1)):
         rows = W.rows
         y = pxq.matmul(W, cuda(x[:m]), path="matvec").cpu().numpy()
         pxq.synchronize()
@@ -178,6 +180,7 @@ def test_matvec_scratch_reuse_across_schedules(pxq, oracle):
             assert ok
         assert max_abs_rel(y, refs[key]) <= TOL, key
     Wd.release()
+    Ws.release()
     Wq.release()
 
 
