@@ -240,6 +240,28 @@ PXQ_API int pxq_matvec_noalloc(pxq_weight* w, size_t row_first, size_t row_count
 PXQ_API int pxq_gemm_block_dots(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* dump,
                         void* stream);
 
+/* ---- attention: the callers' step after the quantized linears --------- */
+
+/* A query range of tensor_attention's second overload (PixAttentionRange,
+ * src/tensor.h:58-63): rows [query_begin, query_end) may attend to keys
+ * [0, key_end), further limited to key <= query_offset + row when causal. */
+typedef struct {
+    size_t query_begin, query_end, key_end;
+    int causal;
+} pxq_attention_range;
+
+/* Multi-head softmax attention in fp32 with the semantics of
+ * tensor_attention (src/tensor.cpp:347-427): q and output [q_rows][heads *
+ * head_dim], k and v [k_rows][kv_heads * head_dim] (device, row-major),
+ * kv head of head h = h / (heads / kv_heads), scores scaled by
+ * 1/sqrt(head_dim).  ranges: 1..8 contiguous ranges covering [0, q_rows)
+ * (NULL with nranges 0: one range with key_end = k_rows, causal = 0 -- the
+ * first overload's non-causal case; its causal case is one range with
+ * causal = 1 and query_offset 0).  head_dim 64, 80 or 128. */
+PXQ_API int pxq_attention(const float* q, size_t q_rows, const float* k, const float* v, size_t k_rows, size_t heads,
+                          size_t kv_heads, size_t head_dim, const pxq_attention_range* ranges, size_t nranges,
+                          size_t query_offset, float* output, void* stream);
+
 /* ---- GGUF model files: the format step in front of the upload ---------- */
 
 /* A GGUF v3 file mapped read-only, its tensor directory parsed with the

@@ -171,6 +171,22 @@ class Reference(_Lib):
     def set_threads(self, n: int) -> None:
         self.lib.pixref_set_threads(n)
 
+    def attention(self, q: np.ndarray, k: np.ndarray, v: np.ndarray, heads: int, kv_heads: int, ranges, query_offset: int = 0):
+        """tensor_attention's range overload; ranges [(begin, end, key_end, causal)].  None when it rejects the arguments."""
+        q, k, v = (np.ascontiguousarray(a, dtype=np.float32) for a in (q, k, v))
+        d = q.shape[1] // heads
+        out = np.zeros_like(q)
+        n = len(ranges)
+        arrs = [np.array([r[i] for r in ranges], dtype=np.uint64) for i in range(3)]
+        cz = np.array([1 if r[3] else 0 for r in ranges], dtype=np.int32)
+        fn = self.lib.pixref_attention
+        fn.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t,
+                       C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p]
+        fn.restype = C.c_int
+        ok = fn(_ptr(q), q.shape[0], _ptr(k), _ptr(v), k.shape[0], heads, kv_heads, d, _ptr(arrs[0]), _ptr(arrs[1]), _ptr(arrs[2]),
+                _ptr(cz), n, query_offset, _ptr(out))
+        return out if ok else None
+
     def gguf_list(self, path: str, cap: int = 256):
         """PixModelFile::open on `path`: (result code, tensors in name order, metadata key count)."""
 

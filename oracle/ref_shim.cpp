@@ -15,6 +15,7 @@
  */
 #include "kernels_quant.cpp"
 #include "model.h"
+#include "tensor.h"
 
 #include <cstring>
 
@@ -96,6 +97,25 @@ int pixref_gguf_list(const char* path, PixrefTensor* out, size_t cap, size_t* co
         (*count)++;
     }
     return 0;
+}
+
+// tensor_attention's range overload (src/tensor.cpp:384-427) on host arrays:
+// q [q_rows][heads*d], k, v [k_rows][kv_heads*d], out [q_rows][heads*d].
+// Returns 0 when the reference returned an empty tensor (invalid arguments).
+int pixref_attention(const float* q, size_t q_rows, const float* k, const float* v, size_t k_rows, size_t heads,
+                     size_t kv_heads, size_t head_dim, const size_t* begin, const size_t* end, const size_t* key_end,
+                     const int* causal, size_t nranges, size_t query_offset, float* out)
+{
+    PixTensor tq(q_rows, heads * head_dim), tk(k_rows, kv_heads * head_dim), tv(k_rows, kv_heads * head_dim);
+    std::copy(q, q + tq.values.size(), tq.values.begin());
+    std::copy(k, k + tk.values.size(), tk.values.begin());
+    std::copy(v, v + tv.values.size(), tv.values.begin());
+    std::vector<PixAttentionRange> ranges;
+    for (size_t i = 0; i < nranges; i++) ranges.push_back({begin[i], end[i], key_end[i], causal[i] != 0});
+    PixTensor r = tensor_attention(tq, tk, tv, heads, kv_heads, ranges, query_offset);
+    if (r.values.empty()) return 0;
+    std::copy(r.values.begin(), r.values.end(), out);
+    return 1;
 }
 
 void pixref_set_threads(size_t count)

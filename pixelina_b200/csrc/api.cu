@@ -917,6 +917,55 @@ int pxq_matmul_gated(pxq_weight* w, const float* input, size_t columns, float* o
     return PXQ_OK;
 }
 
+int pxq_attention(const float* q, size_t q_rows, const float* k, const float* v, size_t k_rows, size_t heads,
+                  size_t kv_heads, size_t head_dim, const pxq_attention_range* ranges, size_t nranges, size_t query_offset,
+                  float* output, void* stream)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    // the reference's argument checks (src/tensor.cpp:386-393)
+    if (!q || !k || !v || !output) return fail(PXQ_ERR_INVALID, "null q, k, v or output");
+    if (!heads || !kv_heads || heads % kv_heads || !q_rows || !k_rows) return fail(PXQ_ERR_INVALID, "bad head counts or sizes");
+    if (heads > 0x7fffffffu || q_rows > 0x7fffffffu || k_rows > 0x7fffffffu) return fail(PXQ_ERR_UNSUPPORTED, "sizes exceed INT32_MAX");
+    if (head_dim != 64 && head_dim != 80 && head_dim != 128)
+        return fail(PXQ_ERR_UNSUPPORTED, "head size %zu (64, 80 and 128 are handled)", head_dim);
+    int64_t ends[kAttnMaxRanges], keys[kAttnMaxRanges];
+    int causal[kAttnMaxRanges];
+    int n = 0;
+    if (!ranges || !nranges) {
+        ends[0] = (int64_t)q_rows;
+        keys[0] = (int64_t)k_rows;
+        causal[0] = 0;
+        n = 1;
+    } else {
+        if (nranges > (size_t)kAttnMaxRanges) return fail(PXQ_ERR_UNSUPPORTED, "more than %d query ranges", kAttnMaxRanges);
+        size_t covered = 0;
+        for (size_t i = 0; i < nranges; i++) {
+            const pxq_attention_range& r = ranges[i];
+            if (r.query_begin != covered || r.query_end <= r.query_begin || r.query_end > q_rows || !r.key_end ||
+                r.key_end > k_rows)
+                return fail(PXQ_ERR_INVALID, "query range %zu does not continue [0, q_rows) or names keys outside [1, k_rows]", i);
+            covered = r.query_end;
+            ends[n] = (int64_t)r.query_end;
+            keys[n] = (int64_t)r.key_end;
+            causal[n] = r.causal ? 1 : 0;
+            n++;
+        }
+        if (covered != q_rows) return fail(PXQ_ERR_INVALID, "query ranges cover %zu of %zu rows", covered, q_rows);
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t need = attention_scratch_bytes((int64_t)q_rows, (int64_t)heads, (int64_t)head_dim, d->sms);
+    float* scratch = nullptr;
+    if (need) {
+        scratch = static_cast<float*>(stream_scratch(t_device, s, need));
+        if (!scratch) return fail(PXQ_ERR_NO_MEMORY, "attention scratch of %zu bytes", need);
+    }
+    const cudaError_t e = launch_attention(q, (int64_t)q_rows, k, v, (int64_t)k_rows, (int)heads, (int)kv_heads, (int)head_dim,
+                                           ends, keys, causal, n, (int64_t)query_offset, output, scratch, need, d->sms, s);
+    if (counted(e, need ? 2 : 1) != cudaSuccess) return fail(PXQ_ERR_CUDA, "attention launch failed: %s", cudaGetErrorString(e));
+    return PXQ_OK;
+}
+
 int pxq_gemm_block_dots(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* dump,
                         void* stream)
 {

@@ -133,6 +133,20 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
+// ---- attention.cu ----------------------------------------------------------
+// fp32 multi-head attention with the semantics of tensor_attention
+// (src/tensor.cpp:347-427): q/out [q_rows][heads*head_dim], k/v
+// [k_rows][kv_heads*head_dim]; query ranges (host arrays, at most
+// kAttnMaxRanges) give each row's permitted key prefix.  head_dim 64, 80 or
+// 128.  q_rows <= 8 uses the key-split kernel and needs
+// attention_scratch_bytes() of scratch.
+constexpr int kAttnMaxRanges = 8;
+size_t attention_scratch_bytes(int64_t q_rows, int64_t heads, int64_t head_dim, int num_sms);
+cudaError_t launch_attention(const float* q, int64_t q_rows, const float* k, const float* v, int64_t k_rows, int heads,
+                             int kv_heads, int head_dim, const int64_t* range_end, const int64_t* range_keys,
+                             const int* range_causal, int nranges, int64_t query_offset, float* out, float* scratch,
+                             size_t scratch_bytes, int num_sms, cudaStream_t s);
+
 // ---- shards.cu -------------------------------------------------------------
 cudaError_t launch_gather_shards(const float* src, int64_t shards, int64_t columns, int64_t shard_rows, float* dst,
                                  int64_t ldy, cudaStream_t s);

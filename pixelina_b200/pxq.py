@@ -73,6 +73,7 @@ SIGNATURES = {
     "pxq_activation_release": (_i, [_vp, _vp]),
     "pxq_kernel_launches": (_u64, []),
     "pxq_matvec_noalloc": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _sz, _vp, _vp]),
+    "pxq_attention": (_i, [_vp, _sz, _vp, _vp, _sz, _sz, _sz, _sz, _vp, _sz, _sz, _vp, _vp]),
     "pxq_gguf_open": (_i, [C.c_char_p, C.POINTER(_vp)]),
     "pxq_gguf_close": (_i, [_vp]),
     "pxq_gguf_tensor_count": (_sz, [_vp]),
@@ -255,6 +256,31 @@ class GatedWeight:
         if self.handle:
             _check(load().pxq_weight_release(self.handle))
             self.handle = C.c_void_p()
+
+
+class AttentionRange(C.Structure):
+    """pxq_attention_range (include/pxq.h)."""
+
+    _fields_ = [("query_begin", C.c_size_t), ("query_end", C.c_size_t), ("key_end", C.c_size_t), ("causal", C.c_int)]
+
+
+def attention(q, k, v, heads: int, kv_heads: int, ranges=None, query_offset: int = 0, causal: bool = False, out=None,
+              stream=None):
+    """tensor_attention on device fp32 tensors q [rows][heads*d], k, v [keys][kv_heads*d].
+    ranges: [(query_begin, query_end, key_end, causal)] (the second overload);
+    None: one range over all rows and keys with `causal` (the first overload)."""
+    torch = _torch()
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    rows, keys = q.shape[0], k.shape[0]
+    d = q.shape[1] // heads
+    if ranges is None:
+        ranges = [(0, rows, keys, causal)]
+    arr = (AttentionRange * len(ranges))(*[AttentionRange(b, e, ke, 1 if c else 0) for b, e, ke, c in ranges])
+    if out is None:
+        out = torch.empty_like(q)
+    _check(load().pxq_attention(_ptr(q), rows, _ptr(k), _ptr(v), keys, heads, kv_heads, d, C.cast(arr, C.c_void_p), len(ranges),
+                                query_offset, _ptr(out), _stream_ptr(stream)))
+    return out
 
 
 class _Uploaded:

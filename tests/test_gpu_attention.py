@@ -1,0 +1,68 @@
+"""pxq_attention against Pixelina's own tensor_attention (src/tensor.cpp:347-427,
+built into oracle/_ref) on the same fp32 inputs: multi-head with grouped
+key/value heads, non-causal, causal, query ranges with a key-cache offset,
+head sizes 64 / 80 / 128, the tiled prefill kernel and the key-split decode
+kernel.  Both sides compute in fp32; the kernel takes the softmax online over
+key tiles, so the sums are reordered: outputs agree to ATT_TOL max-abs-rel."""
+import numpy as np
+import pytest
+
+from conftest import max_abs_rel
+from oracle.oracle import Reference, reference_available
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not reference_available(), reason="oracle/_ref is missing")]
+ATT_TOL = 2e-5
+
+CASES = [
+    # q_rows, k_rows, heads, kv_heads, d, ranges, query_offset
+    (96, 96, 4, 4, 128, [(0, 96, 96, False)], 0),                      # DiT-like, non-causal
+    (70, 70, 4, 2, 64, [(0, 70, 70, True)], 0),                        # causal, grouped kv heads
+    (130, 150, 2, 1, 80, [(0, 50, 150, False), (50, 130, 120, True)], 20),  # ranges with an offset
+    (300, 300, 8, 8, 128, [(0, 300, 300, False)], 0),                   # several 64-row query tiles
+    (1, 777, 7, 1, 128, [(0, 1, 777, True)], 776),                      # decode, one row
+    (5, 1000, 8, 2, 64, [(0, 5, 1000, True)], 995),                     # decode, five rows
+    (8, 4096, 28, 4, 128, [(0, 8, 4096, True)], 4088),                  # VL decode shape, eight rows
+    (3, 50, 2, 2, 80, [(0, 2, 50, False), (2, 3, 30, True)], 10),      # decode with two ranges
+]
+
+
+@pytest.mark.parametrize("case", range(len(CASES)))
+def test_attention_matches_reference(pxq, case):
+    import torch
+
+    rows, keys, heads, kvh, d, ranges, off = CASES[case]
+    rng = np.random.default_rng(100 + case)
+    q = rng.standard_normal((rows, heads * d)).astype(np.float32)
+    k = rng.standard_normal((keys, kvh * d)).astype(np.float32)
+    v = rng.standard_normal((keys, kvh * d)).astype(np.float32)
+    want = Reference().attention(q, k, v, heads, kvh, ranges, off)
+    assert want is not None
+    got = pxq.attention(torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(), heads, kvh,
+                        ranges=ranges, query_offset=off).cpu().numpy()
+    pxq.synchronize()
+    assert max_abs_rel(got, want) <= ATT_TOL
+
+
+def test_attention_first_overload_and_argument_checks(pxq):
+    """ranges=None is the first overload (non-causal or causal from row 0); the
+    reference's argument checks are errors here."""
+    import torch
+
+    rng = np.random.default_rng(7)
+    q = rng.standard_normal((40, 2 * 64)).astype(np.float32)
+    k = rng.standard_normal((40, 64)).astype(np.float32)
+    v = rng.standard_normal((40, 64)).astype(np.float32)
+    qd, kd, vd = (torch.from_numpy(a).cuda() for a in (q, k, v))
+    for causal in (False, True):
+        want = Reference().attention(q, k, v, 2, 1, [(0, 40, 40, causal)], 0)
+        got = pxq.attention(qd, kd, vd, 2, 1, causal=causal).cpu().numpy()
+        assert max_abs_rel(got, want) <= ATT_TOL
+    for bad in ([(0, 20, 40, False)], [(0, 20, 40, False), (21, 40, 40, False)], [(0, 40, 41, False)], [(0, 40, 0, False)]):
+        assert Reference().attention(q, k, v, 2, 1, bad, 0) is None  # the reference rejects these too
+        with pytest.raises(pxq.PxqError) as err:
+            pxq.attention(qd, kd, vd, 2, 1, ranges=bad)
+        assert err.value.code == pxq.ERR_INVALID
+    with pytest.raises(pxq.PxqError) as err:  # 3 heads over 2 kv heads
+        pxq.attention(torch.zeros((4, 3 * 64), device="cuda"), torch.zeros((4, 2 * 64), device="cuda"),
+                      torch.zeros((4, 2 * 64), device="cuda"), 3, 2)
+    assert err.value.code == pxq.ERR_INVALID

@@ -276,6 +276,27 @@ def test_row_views_ldy_bias(pxq, oracle, path, wtype):
     W.release()
 
 
+@pytest.mark.parametrize("wtype", [Q8_0, Q5_K])
+@pytest.mark.parametrize("columns", [4, 150])
+def test_qkv_split_into_separate_outputs(pxq, oracle, wtype, columns):
+    """The QKV split of src/inference.cpp:299-313 (tensor_linear, then copying
+    the three row ranges of each output row into q, k, v) as one activation
+    quantize and three row-view products writing q, k and v directly."""
+    H, inner = 192, 512
+    w = synth.weights_for(wtype, 3 * H, inner, seed=31)
+    x = synth.activations(columns, inner, seed=32)
+    W = pxq.Weight(w, wtype, inner, 3 * H)
+    a = pxq.Activation(wtype, cuda(x))
+    q, k, v = (pxq.matmul_quantized(W, a, row_first=i * H, row_count=H) for i in range(3))
+    pxq.synchronize()
+    a.release()
+    W.release()
+    ok, ref = oracle.quant_matmul(w, wtype, x, 3 * H)
+    assert ok
+    for i, t in enumerate((q, k, v)):
+        assert max_abs_rel(t.cpu().numpy(), ref[:, i * H:(i + 1) * H]) <= TOL
+
+
 def test_host_drop_in_matches_reference_contract(pxq, oracle, golden):
     for name, wtype in (("q8_0", Q8_0), ("q5_K", Q5_K)):
         w = golden[f"w_{name}"]
