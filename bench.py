@@ -8,7 +8,7 @@ tensor-core GEMM, inputs resident in HBM; L2 is flushed (256 MB write)
 between timed steps, outside the timed events.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload q5k_gemm|q8_0_gemm|q8_0_large|q6k_gemm|dit|decode|decode_gated|decode_shapes|sharded]
+                    [--workload q5k_gemm|q8_0_gemm|q8_0_large|q6k_gemm|dit|decode|decode_gated|decode_shapes|attention|sharded]
 
 Multi-GPU (torchrun, one rank per GPU): each rank processes its own batch of
 activation rows against the same weights (data parallel over independent
@@ -672,6 +672,55 @@ def run_dit(args, dist: Dist):
             "peak_source": peak_src, "clocks": clocks}
 
 
+def run_attention(args, dist: Dist):
+    """The callers' attention step (tensor_attention) at the BASELINE models'
+    shapes: DiT prefill (configs[2]: 4352 tokens, 24 heads of 128, non-causal)
+    and VL decode (configs[3]: 28 heads of 128 over 4 kv heads, 8 query rows
+    against a 4096-token key cache, causal).  fp32 on the CUDA cores; the
+    prefill roofline is the fp32 FMA rate, the decode one HBM (keys + values)."""
+    import torch
+
+    from pixelina_b200 import pxq
+
+    pxq.init(dist.local)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(13)
+    cases = {
+        "dit_prefill": dict(rows=DIT["M"], keys=DIT["M"], heads=24, kvh=24, d=128, ranges=None, off=0, causal=False),
+        "vl_decode_8": dict(rows=8, keys=4096, heads=28, kvh=4, d=128, ranges=[(0, 8, 4096, True)], off=4088, causal=True),
+    }
+    hbm, _, _, peak_src = measured_peaks()
+    props = torch.cuda.get_device_properties(dist.local)
+    fp32_peak = props.multi_processor_count * 128 * 2 * 1.965e9 / 1e12  # TFLOP/s at the max SM clock
+    results = {}
+    for name, c in cases.items():
+        q = torch.randn((c["rows"], c["heads"] * c["d"]), device="cuda", generator=gen)
+        k = torch.randn((c["keys"], c["kvh"] * c["d"]), device="cuda", generator=gen)
+        v = torch.randn((c["keys"], c["kvh"] * c["d"]), device="cuda", generator=gen)
+        out = torch.empty_like(q)
+
+        def step(ev):
+            if ev is not None:
+                ev["start"], ev["end"] = ev_pair()
+                ev["start"].record()
+            pxq.attention(q, k, v, c["heads"], c["kvh"], ranges=c["ranges"], query_offset=c["off"], causal=c["causal"], out=out)
+            if ev is not None:
+                ev["end"].record()
+
+        flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+        step_ms, _, clocks = time_steps(step, args.steps, args.warmup, flush_buf.zero_, args.soak, ClockSampler(dist.local), dist)
+        ms = dist.max(statistics.mean(step_ms))
+        flops = 4.0 * c["rows"] * c["keys"] * c["heads"] * c["d"]
+        kv_bytes = 2.0 * c["keys"] * c["kvh"] * c["d"] * 4
+        results[name] = {"ms": round(ms, 4), "TFLOPs": round(flops / (ms * 1e-3) / 1e12, 2),
+                         "fp32_frac": round(flops / (ms * 1e-3) / 1e12 / fp32_peak, 4),
+                         "kv_GBps": round(kv_bytes / (ms * 1e-3) / 1e9, 1), "hbm_frac": round(kv_bytes / (ms * 1e-3) / 1e9 / hbm, 4),
+                         "clocks": clocks}
+    return {"metric": METRIC, "workload": "attention: DiT prefill and VL decode shapes (tensor_attention, fp32)",
+            "unit": "TFLOP/s", "value": results["dit_prefill"]["TFLOPs"], "results": results, "n_gpus": dist.world,
+            "fp32_peak_tflops": round(fp32_peak, 1), "peak_hbm_gbs": hbm, "peak_source": peak_src}
+
+
 def run_sharded(args, dist: Dist):
     """BASELINE configs[4] N-sharded across ranks: rank r computes weight rows
     [r*N/G, (r+1)*N/G) for all M activation rows, then an NCCL all-gather of
@@ -730,7 +779,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="q5k_gemm",
-                    choices=sorted(GEMM_WORKLOADS) + ["decode", "decode_gated", "decode_shapes", "dit", "sharded"])
+                    choices=sorted(GEMM_WORKLOADS) + ["attention", "decode", "decode_gated", "decode_shapes", "dit", "sharded"])
     ap.add_argument("--soak", type=float, default=1.5, help="seconds of untimed steps before timing (clock settling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -749,6 +798,8 @@ def main():
             out = run_decode(args, dist)
         elif args.workload == "decode_gated":
             out = run_decode(args, dist, gated=True)
+        elif args.workload == "attention":
+            out = run_attention(args, dist)
         elif args.workload == "decode_shapes":
             out = run_decode_shapes(args, dist)
         elif args.workload == "dit":

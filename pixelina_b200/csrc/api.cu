@@ -954,7 +954,7 @@ int pxq_attention(const float* q, size_t q_rows, const float* k, const float* v,
         if (covered != q_rows) return fail(PXQ_ERR_INVALID, "query ranges cover %zu of %zu rows", covered, q_rows);
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const size_t need = attention_scratch_bytes((int64_t)q_rows, (int64_t)heads, (int64_t)head_dim, d->sms);
+    const size_t need = attention_scratch_bytes((int64_t)q_rows, (int64_t)heads, (int64_t)kv_heads, (int64_t)head_dim, (int64_t)k_rows, d->sms);
     float* scratch = nullptr;
     if (need) {
         scratch = static_cast<float*>(stream_scratch(t_device, s, need));

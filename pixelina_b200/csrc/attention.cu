@@ -12,13 +12,14 @@
 // taken online over key tiles, which reorders the reference's sums (fp32
 // rounding differences only).
 //
-//   k_attn_tiled   64 query rows x one head per CTA, 64-key tiles staged in
-//                  shared memory (keys and queries transposed so that a
-//                  thread's 4x4 score block and 4x(d/16) output block read
-//                  whole float4 words), online softmax per row.
-//   k_attn_split   few query rows (decode): one CTA per (head, key split),
-//                  partial (max, sum, out) per query row; k_attn_combine
-//                  merges the splits.
+//   k_attn         16-64 rows per CTA against 64-key tiles staged in shared
+//                  memory, online softmax per row.  Prefill: a CTA takes one
+//                  head and up to 64 query rows over all keys.  Decode (at
+//                  most 8 query rows): a CTA takes every head of one
+//                  key/value head (up to 64 head x row pairs, so each key and
+//                  value is read once for the whole group) over one key
+//                  split and writes partial (max, sum, out) per row;
+//                  k_attn_combine merges the splits.
 #include <cfloat>
 #include "pxq_device.cuh"
 #include "pxq_internal.h"
@@ -26,7 +27,8 @@
 namespace pxq {
 namespace {
 
-constexpr int BQ = 64, BKT = 64, ATT_THREADS = 256;
+constexpr int KT = 64, ATT_THREADS = 256;
+constexpr int64_t kSplitRows = 8;  // query rows up to which the keys are split across CTAs
 
 struct AttnArgs {
     const float* q;
@@ -40,6 +42,7 @@ struct AttnArgs {
     int64_t q_rows, k_rows, query_offset;
     int heads, kv_heads;
     float scale;
+    int vec;  // q, k, v and out are 16-byte aligned: whole float4 accesses
 };
 
 // Permitted key count of query row t.
@@ -53,292 +56,417 @@ __device__ __forceinline__ int64_t keys_of(const AttnArgs& a, int64_t t)
     return c < ke ? c : ke;
 }
 
-template <int D>
-__global__ void __launch_bounds__(ATT_THREADS) k_attn_tiled(const __grid_constant__ AttnArgs a)
+__device__ __forceinline__ float4 ld4(const float* p, bool vec)
 {
-    static_assert(D % 16 == 0 && D <= 128, "head size");
-    constexpr int OC = D / 16;  // output columns per thread
-    extern __shared__ float sm[];
-    float* qt = sm;                 // [D][BQ]   queries, transposed
-    float* kt = qt + D * BQ;        // [D][BKT]  keys, transposed
-    float* vs = kt + D * BKT;       // [BKT][D]  values
-    float* ps = vs + BKT * D;       // [BQ][BKT] probabilities of the tile
-    __shared__ int64_t lim[BQ];     // permitted keys per query row
+    if (vec) return *reinterpret_cast<const float4*>(p);
+    return make_float4(p[0], p[1], p[2], p[3]);
+}
 
-    const int h = blockIdx.y, kh = h / (a.heads / a.kv_heads);
-    const int64_t t0 = (int64_t)blockIdx.x * BQ;
-    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;  // 16 x 16 threads
-    const int64_t qs = (int64_t)a.heads * D, ks = (int64_t)a.kv_heads * D;
-
-    for (int i = tid; i < BQ * D; i += ATT_THREADS) {
-        const int r = i / D, c = i % D;
-        const int64_t t = t0 + r;
-        qt[c * BQ + r] = t < a.q_rows ? a.q[t * qs + (int64_t)h * D + c] * a.scale : 0.f;
-    }
-    int64_t kmax = 0;
-    for (int r = tid; r < BQ; r += ATT_THREADS) lim[r] = t0 + r < a.q_rows ? keys_of(a, t0 + r) : 0;
-    __syncthreads();
-    for (int r = 0; r < BQ; r++) kmax = lim[r] > kmax ? lim[r] : kmax;
-
-    // rows ty*4 .. ty*4+3; score columns tx*4 .. tx*4+3; output columns tx*OC .. tx*OC+OC-1
-    float m[4], l[4], o[4][OC];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        m[i] = -FLT_MAX;
-        l[i] = 0.f;
-#pragma unroll
-        for (int c = 0; c < OC; c++) o[i][c] = 0.f;
-    }
-    for (int64_t j0 = 0; j0 < kmax; j0 += BKT) {
-        __syncthreads();  // the previous tile's keys, values and probabilities are consumed
-        for (int i = tid; i < BKT * D; i += ATT_THREADS) {
-            const int j = i / D, c = i % D;
-            const int64_t key = j0 + j;
-            const bool in = key < a.k_rows;
-            kt[c * BKT + j] = in ? a.k[key * ks + (int64_t)kh * D + c] : 0.f;
-            vs[j * D + c] = in ? a.v[key * ks + (int64_t)kh * D + c] : 0.f;
-        }
-        __syncthreads();
-        float s[4][4];
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-#pragma unroll
-            for (int j = 0; j < 4; j++) s[i][j] = 0.f;
-#pragma unroll 8
-        for (int c = 0; c < D; c++) {
-            const float4 qv = *reinterpret_cast<const float4*>(qt + c * BQ + ty * 4);
-            const float4 kv = *reinterpret_cast<const float4*>(kt + c * BKT + tx * 4);
-            const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, ka[4] = {kv.x, kv.y, kv.z, kv.w};
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-#pragma unroll
-                for (int j = 0; j < 4; j++) s[i][j] = __fmaf_rn(qa[i], ka[j], s[i][j]);
-        }
-        // online softmax over this tile, per row (16 threads of a half warp share a row group)
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int64_t L = lim[ty * 4 + i];
-            float tm = -FLT_MAX;
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                if (j0 + tx * 4 + j >= L) s[i][j] = -FLT_MAX;
-                tm = fmaxf(tm, s[i][j]);
-            }
-#pragma unroll
-            for (int off = 8; off; off >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, off));
-            const float mn = fmaxf(m[i], tm);
-            float ts = 0.f;
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const float e = s[i][j] == -FLT_MAX ? 0.f : expf(s[i][j] - mn);
-                ps[(ty * 4 + i) * BKT + tx * 4 + j] = e;
-                ts += e;
-            }
-#pragma unroll
-            for (int off = 8; off; off >>= 1) ts += __shfl_xor_sync(0xffffffffu, ts, off);
-            const float corr = m[i] == -FLT_MAX ? 0.f : expf(m[i] - mn);
-            l[i] = __fmaf_rn(l[i], corr, ts);
-#pragma unroll
-            for (int c = 0; c < OC; c++) o[i][c] *= corr;
-            m[i] = mn;
-        }
-        __syncthreads();
-        const int64_t jn = kmax - j0 < BKT ? kmax - j0 : BKT;
-        for (int j = 0; j < jn; j++) {
-            float p[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) p[i] = ps[(ty * 4 + i) * BKT + j];
-            const float* vr = vs + j * D + tx * OC;
-#pragma unroll
-            for (int c = 0; c < OC; c++) {
-                const float vv = vr[c];
-#pragma unroll
-                for (int i = 0; i < 4; i++) o[i][c] = __fmaf_rn(p[i], vv, o[i][c]);
-            }
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int64_t t = t0 + ty * 4 + i;
-        if (t >= a.q_rows) continue;
-        const float inv = l[i] > 0.f ? 1.f / l[i] : 0.f;
-        float* dst = a.out + t * qs + (int64_t)h * D + tx * OC;
-#pragma unroll
-        for (int c = 0; c < OC; c++) dst[c] = o[i][c] * inv;
+__device__ __forceinline__ void st4(float* p, float4 v, bool vec)
+{
+    if (vec) {
+        *reinterpret_cast<float4*>(p) = v;
+    } else {
+        p[0] = v.x;
+        p[1] = v.y;
+        p[2] = v.z;
+        p[3] = v.w;
     }
 }
 
-// Decode: CTA (head h, split sp) over keys [sp*chunk, (sp+1)*chunk) for every
-// query row (at most 8).  Partials per (split, row, head): running max pm,
-// sum pl, unnormalised output po[D].
-template <int D>
-__global__ void __launch_bounds__(ATT_THREADS) k_attn_split(const __grid_constant__ AttnArgs a, int64_t chunk, float* pm, float* pl,
-                                                            float* po)
+// 16-byte asynchronous copy global -> shared (zero fill when !valid; src is
+// then not read), completion tracked per thread by commit/wait groups.
+__device__ __forceinline__ void cp16(float* dst, const float* src, bool valid)
 {
-    constexpr int R = 8, SUB = 256, KW = (D + 31) / 32;
-    constexpr int RSTEP = ATT_THREADS / D;  // output rows covered per pass
-    __shared__ float qv[R][D];
-    __shared__ float sc[R][SUB];
-    __shared__ float corr[R], mrow[R], lrow[R];
-    __shared__ int64_t lim[R];
-    const int h = blockIdx.x, kh = h / (a.heads / a.kv_heads), sp = blockIdx.y;
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_wait_prior() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
+
+// One CTA: QR = 16*RE rows against key tiles of KT keys.  A row is a (head,
+// query row) pair: without SPLIT the CTA takes one head and QR consecutive
+// query rows over all keys and writes the normalised output; with SPLIT it
+// takes heads [hb, he) of one key/value head (all q_rows <= 8 rows of each)
+// over one key range and writes partials (max pm, sum pl, unnormalised po)
+// for k_attn_combine.  Queries and keys sit row-major in shared memory with
+// stride D+4, so that the 4-word reads of thread tx (keys tx, tx+16, tx+32,
+// tx+48) fall in distinct banks; a thread's block is RE rows (ty + 16f) x 4
+// keys for the scores and RE rows x up to 8 output columns (float4 groups
+// tx + 16h) for the values.  After the scores, the key buffer holds the
+// tile's probabilities.  SPLIT CTAs (one per SM) double-buffer the key and
+// value tiles: the copy of tile i+1 (cp.async, or plain loads when a tensor is
+// not 16-byte aligned) runs while tile i is computed.  Prefill CTAs (two per
+// SM, the other CTA hiding the copy) stage one tile at a time and write the
+// probabilities over the keys once the scores are taken.
+template <int D, int RE, bool SPLIT>
+constexpr size_t attn_smem_bytes()
+{
+    constexpr int DP = D + 4, PS = KT + 4, QR = 16 * RE;
+    return (size_t)(SPLIT ? QR * DP + 2 * KT * DP + 2 * KT * D + QR * PS : QR * DP + KT * DP + KT * D) * sizeof(float);
+}
+
+template <int D, int RE, bool SPLIT>
+__global__ void __launch_bounds__(ATT_THREADS, SPLIT ? 1 : 2)
+    k_attn(const __grid_constant__ AttnArgs a, int hpc, int hgroups, int64_t chunk, float* pm, float* pl, float* po)
+{
+    static_assert(D % 16 == 0 && D <= 128, "head size");
+    constexpr bool PIPE = SPLIT;
+    constexpr int DP = D + 4, PS = KT + 4, QR = 16 * RE, NG = D / 4, H = (NG + 15) / 16;
+    static_assert(PIPE || QR * PS <= KT * DP, "probabilities fit over the keys");
+    extern __shared__ float4 sm4[];
+    float* qs = reinterpret_cast<float*>(sm4);          // [QR][DP] queries, pre-scaled
+    float* kbuf = qs + QR * DP;                         // (2 x) [KT][DP] keys
+    float* vbuf = kbuf + (PIPE ? 2 : 1) * KT * DP;      // (2 x) [KT][D]  values
+    float* ps = PIPE ? vbuf + 2 * KT * D : kbuf;        // [QR][PS] the tile's probabilities
+    __shared__ int64_t lim[QR];                 // permitted keys per row
+
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const bool vec = a.vec != 0;
+    const int64_t qst = (int64_t)a.heads * D, kst = (int64_t)a.kv_heads * D;
+    const int group = a.heads / a.kv_heads;
+    int hb, he, kh;
+    int64_t t0 = 0, kb = 0, ke = a.k_rows;
+    if (SPLIT) {
+        kh = blockIdx.x / hgroups;
+        hb = kh * group + (int)(blockIdx.x % hgroups) * hpc;
+        he = hb + hpc < (kh + 1) * group ? hb + hpc : (kh + 1) * group;
+        kb = (int64_t)blockIdx.y * chunk;
+        ke = kb + chunk < a.k_rows ? kb + chunk : a.k_rows;
+    } else {
+        hb = blockIdx.y;
+        he = hb + 1;
+        kh = hb / group;
+        t0 = (int64_t)blockIdx.x * QR;
+    }
     const int rows = (int)a.q_rows;
-    const int64_t qs = (int64_t)a.heads * D, ks = (int64_t)a.kv_heads * D;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    for (int i = tid; i < R * D; i += ATT_THREADS) {
-        const int r = i / D, c = i % D;
-        qv[r][c] = r < rows ? a.q[(int64_t)r * qs + (int64_t)h * D + c] * a.scale : 0.f;
+    // (head, query row) of CTA row lr; false past the CTA's rows
+    auto row_of = [&](int lr, int& h, int64_t& t) -> bool {
+        if (SPLIT) {
+            h = hb + lr / rows;
+            t = lr % rows;
+            return h < he;
+        }
+        h = hb;
+        t = t0 + lr;
+        return t < a.q_rows;
+    };
+
+    for (int i = tid; i < QR * NG; i += ATT_THREADS) {
+        const int lr = i / NG, g = i % NG;
+        int h;
+        int64_t t;
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row_of(lr, h, t)) {
+            x = ld4(a.q + t * qst + (int64_t)h * D + 4 * g, vec);
+            x.x *= a.scale;
+            x.y *= a.scale;
+            x.z *= a.scale;
+            x.w *= a.scale;
+        }
+        *reinterpret_cast<float4*>(qs + lr * DP + 4 * g) = x;
     }
-    if (tid < R) {
-        lim[tid] = tid < rows ? keys_of(a, tid) : 0;
-        mrow[tid] = -FLT_MAX;
-        lrow[tid] = 0.f;
+    for (int lr = tid; lr < QR; lr += ATT_THREADS) {
+        int h;
+        int64_t t;
+        lim[lr] = row_of(lr, h, t) ? keys_of(a, t) : 0;
     }
-    // thread tid < RSTEP*D owns column tid % D of rows tid / D + RSTEP*u
-    const bool owner = tid < RSTEP * D;
-    const int oc = tid % D, orow = tid / D;
-    float o[(R + RSTEP - 1) / RSTEP];
+    __syncthreads();
+    int64_t kmax = 0;
+    for (int lr = 0; lr < QR; lr++) kmax = lim[lr] > kmax ? lim[lr] : kmax;
+    if (ke > kmax) ke = kmax;  // keys past every row's limit contribute nothing
+
+    float m[RE], l[RE], o[RE][H][4];
 #pragma unroll
-    for (int u = 0; u < (R + RSTEP - 1) / RSTEP; u++) o[u] = 0.f;
-    const int64_t k0 = (int64_t)sp * chunk;
-    const int64_t k1 = k0 + chunk < a.k_rows ? k0 + chunk : a.k_rows;
-    for (int64_t j0 = k0; j0 < k1; j0 += SUB) {
-        const int n = (int)(k1 - j0 < SUB ? k1 - j0 : SUB);
-        __syncthreads();  // q and the row state are written; the previous sub-chunk's probabilities are consumed
-        for (int j = warp; j < n; j += ATT_THREADS / 32) {
-            const float* kr = a.k + (j0 + j) * ks + (int64_t)kh * D;
-            float kk[KW];
+    for (int f = 0; f < RE; f++) {
+        m[f] = -FLT_MAX;
+        l[f] = 0.f;
 #pragma unroll
-            for (int u = 0; u < KW; u++) kk[u] = lane + 32 * u < D ? kr[lane + 32 * u] : 0.f;
-            for (int r = 0; r < rows; r++) {
-                float acc = 0.f;
+        for (int hh = 0; hh < H; hh++)
 #pragma unroll
-                for (int u = 0; u < KW; u++)
-                    if (lane + 32 * u < D) acc = __fmaf_rn(qv[r][lane + 32 * u], kk[u], acc);
-#pragma unroll
-                for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-                if (lane == 0) sc[r][j] = j0 + j < lim[r] ? acc : -FLT_MAX;
+            for (int c = 0; c < 4; c++) o[f][hh][c] = 0.f;
+    }
+    // copy the keys and values of tile [j0, j0 + KT) into buffer b
+    auto stage = [&](int b, int64_t j0) {
+        const int n = (int)(ke - j0 < KT ? ke - j0 : KT);
+        float* kd = kbuf + b * KT * DP;
+        float* vd = vbuf + b * KT * D;
+        for (int i = tid; i < KT * NG; i += ATT_THREADS) {
+            const int j = i / NG, g = i % NG;
+            const int64_t off = (j0 + j) * kst + (int64_t)kh * D + 4 * g;
+            if (PIPE && vec) {
+                cp16(kd + j * DP + 4 * g, j < n ? a.k + off : a.k, j < n);
+                cp16(vd + j * D + 4 * g, j < n ? a.v + off : a.v, j < n);
+            } else {
+                float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+                if (j < n) {
+                    kv = ld4(a.k + off, vec);
+                    vv = ld4(a.v + off, vec);
+                }
+                *reinterpret_cast<float4*>(kd + j * DP + 4 * g) = kv;
+                *reinterpret_cast<float4*>(vd + j * D + 4 * g) = vv;
             }
         }
+        if (PIPE) cp_commit();
+    };
+    if (PIPE && kb < ke) stage(0, kb);
+    int cur = 0;
+    for (int64_t j0 = kb; j0 < ke; j0 += KT, cur ^= PIPE ? 1 : 0) {
+        const int n = (int)(ke - j0 < KT ? ke - j0 : KT);
+        if (PIPE) {
+            if (j0 + KT < ke) {
+                stage(cur ^ 1, j0 + KT);  // buffer cur^1 was released by the barrier closing the previous tile
+            } else {
+                cp_commit();  // an empty group keeps "all but the newest group" meaning this tile
+            }
+            cp_wait_prior();
+        } else {
+            stage(0, j0);  // the barrier closing the previous tile released the buffers
+        }
         __syncthreads();
-        if (warp < rows) {  // warp r: row r's new max, probabilities, sum, rescale factor
-            const int r = warp;
+        const float* ks = kbuf + cur * KT * DP;
+        const float* vs = vbuf + cur * KT * D;
+        float s[RE][4];
+#pragma unroll
+        for (int f = 0; f < RE; f++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) s[f][e] = 0.f;
+#pragma unroll 4
+        for (int c = 0; c < D; c += 4) {
+            float4 kf[4], qf[RE];
+#pragma unroll
+            for (int e = 0; e < 4; e++) kf[e] = *reinterpret_cast<const float4*>(ks + (tx + 16 * e) * DP + c);
+#pragma unroll
+            for (int f = 0; f < RE; f++) qf[f] = *reinterpret_cast<const float4*>(qs + (ty + 16 * f) * DP + c);
+#pragma unroll
+            for (int f = 0; f < RE; f++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    float acc = s[f][e];
+                    acc = __fmaf_rn(qf[f].x, kf[e].x, acc);
+                    acc = __fmaf_rn(qf[f].y, kf[e].y, acc);
+                    acc = __fmaf_rn(qf[f].z, kf[e].z, acc);
+                    s[f][e] = __fmaf_rn(qf[f].w, kf[e].w, acc);
+                }
+        }
+        if (!PIPE) __syncthreads();  // every thread is done with the keys: their buffer takes the probabilities
+        // online softmax per row; the 16 threads of a half warp hold a row's 64 scores
+#pragma unroll
+        for (int f = 0; f < RE; f++) {
+            const int lr = ty + 16 * f;
+            const int64_t L = lim[lr];
             float tm = -FLT_MAX;
-            for (int j = lane; j < n; j += 32) tm = fmaxf(tm, sc[r][j]);
 #pragma unroll
-            for (int off = 16; off; off >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, off));
-            const float mo = mrow[r], mn = fmaxf(mo, tm);
+            for (int e = 0; e < 4; e++) {
+                const int j = tx + 16 * e;
+                if (j >= n || j0 + j >= L) s[f][e] = -FLT_MAX;
+                tm = fmaxf(tm, s[f][e]);
+            }
+#pragma unroll
+            for (int off = 8; off; off >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, off));
+            const float mn = fmaxf(m[f], tm);
             float ts = 0.f;
-            for (int j = lane; j < n; j += 32) {
-                const float e = sc[r][j] == -FLT_MAX ? 0.f : expf(sc[r][j] - mn);
-                sc[r][j] = e;
-                ts += e;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float p = s[f][e] == -FLT_MAX ? 0.f : expf(s[f][e] - mn);
+                ps[lr * PS + tx + 16 * e] = p;
+                ts += p;
             }
 #pragma unroll
-            for (int off = 16; off; off >>= 1) ts += __shfl_xor_sync(0xffffffffu, ts, off);
-            if (lane == 0) {
-                const float cf = mo == -FLT_MAX ? 0.f : expf(mo - mn);
-                corr[r] = cf;
-                lrow[r] = __fmaf_rn(lrow[r], cf, ts);
-                mrow[r] = mn;
-            }
+            for (int off = 8; off; off >>= 1) ts += __shfl_xor_sync(0xffffffffu, ts, off);
+            const float corr = m[f] == -FLT_MAX ? 0.f : expf(m[f] - mn);
+            l[f] = __fmaf_rn(l[f], corr, ts);
+#pragma unroll
+            for (int hh = 0; hh < H; hh++)
+#pragma unroll
+                for (int c = 0; c < 4; c++) o[f][hh][c] *= corr;
+            m[f] = mn;
         }
         __syncthreads();
-        if (owner) {
+        const int nj = (n + 3) & ~3;  // probabilities past n are 0, value rows past n are zero
+        for (int j = 0; j < nj; j += 4) {
+            float4 pf[RE];
 #pragma unroll
-            for (int u = 0; u < (R + RSTEP - 1) / RSTEP; u++) {
-                const int r = orow + RSTEP * u;
-                if (r < rows) o[u] *= corr[r];
-            }
-            for (int j = 0; j < n; j++) {
-                const float vv = a.v[(j0 + j) * ks + (int64_t)kh * D + oc];
+            for (int f = 0; f < RE; f++) pf[f] = *reinterpret_cast<const float4*>(ps + (ty + 16 * f) * PS + j);
 #pragma unroll
-                for (int u = 0; u < (R + RSTEP - 1) / RSTEP; u++) {
-                    const int r = orow + RSTEP * u;
-                    if (r < rows) o[u] = __fmaf_rn(sc[r][j], vv, o[u]);
+            for (int jj = 0; jj < 4; jj++) {
+#pragma unroll
+                for (int hh = 0; hh < H; hh++) {
+                    const int g = tx + 16 * hh;
+                    if (NG % 16 != 0 && g >= NG) continue;
+                    const float4 vv = *reinterpret_cast<const float4*>(vs + (j + jj) * D + 4 * g);
+#pragma unroll
+                    for (int f = 0; f < RE; f++) {
+                        const float p = jj == 0 ? pf[f].x : jj == 1 ? pf[f].y : jj == 2 ? pf[f].z : pf[f].w;
+                        o[f][hh][0] = __fmaf_rn(p, vv.x, o[f][hh][0]);
+                        o[f][hh][1] = __fmaf_rn(p, vv.y, o[f][hh][1]);
+                        o[f][hh][2] = __fmaf_rn(p, vv.z, o[f][hh][2]);
+                        o[f][hh][3] = __fmaf_rn(p, vv.w, o[f][hh][3]);
+                    }
                 }
             }
         }
+        __syncthreads();  // probabilities and buffer cur are consumed
     }
-    __syncthreads();
-    const int64_t base = ((int64_t)sp * rows) * a.heads;
-    if (tid < rows) {
-        pm[base + (int64_t)tid * a.heads + h] = mrow[tid];
-        pl[base + (int64_t)tid * a.heads + h] = lrow[tid];
-    }
-    if (owner) {
 #pragma unroll
-        for (int u = 0; u < (R + RSTEP - 1) / RSTEP; u++) {
-            const int r = orow + RSTEP * u;
-            if (r < rows) po[(base + (int64_t)r * a.heads + h) * D + oc] = o[u];
+    for (int f = 0; f < RE; f++) {
+        int h;
+        int64_t t;
+        if (!row_of(ty + 16 * f, h, t)) continue;
+        if (SPLIT) {
+            const int64_t part = ((int64_t)blockIdx.y * rows + t) * a.heads + h;
+            if (tx == 0) {
+                pm[part] = m[f];
+                pl[part] = l[f];
+            }
+#pragma unroll
+            for (int hh = 0; hh < H; hh++) {
+                const int g = tx + 16 * hh;
+                if (NG % 16 != 0 && g >= NG) continue;
+                st4(po + part * D + 4 * g, make_float4(o[f][hh][0], o[f][hh][1], o[f][hh][2], o[f][hh][3]), true);
+            }
+        } else {
+            const float inv = l[f] > 0.f ? 1.f / l[f] : 0.f;
+            float* dst = a.out + t * qst + (int64_t)h * D;
+#pragma unroll
+            for (int hh = 0; hh < H; hh++) {
+                const int g = tx + 16 * hh;
+                if (NG % 16 != 0 && g >= NG) continue;
+                st4(dst + 4 * g, make_float4(o[f][hh][0] * inv, o[f][hh][1] * inv, o[f][hh][2] * inv, o[f][hh][3] * inv),
+                    vec);
+            }
         }
     }
 }
 
 // Merge the key splits: out = sum_s e^(m_s - M) o_s / sum_s e^(m_s - M) l_s.
+// One CTA of 128 threads per (query row, head): the split weights first (a
+// max and a sum over the CTA), then one output column per thread over the
+// splits, loads unrolled so that several are in flight.
 template <int D>
-__global__ void k_attn_combine(const __grid_constant__ AttnArgs a, int splits, const float* pm, const float* pl, const float* po)
+__global__ void __launch_bounds__(128) k_attn_combine(const __grid_constant__ AttnArgs a, int splits, const float* pm,
+                                                      const float* pl, const float* po)
 {
-    const int rows = (int)a.q_rows;
-    const int64_t total = (int64_t)rows * a.heads * D;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int c = (int)(i % D);
-        const int64_t rh = i / D;  // r * heads + h
-        float M = -FLT_MAX;
-        for (int s = 0; s < splits; s++) M = fmaxf(M, pm[(int64_t)s * rows * a.heads + rh]);
-        float L = 0.f, acc = 0.f;
-        for (int s = 0; s < splits; s++) {
-            const float ms = pm[(int64_t)s * rows * a.heads + rh];
-            if (ms == -FLT_MAX) continue;
-            const float w = expf(ms - M);
-            L = __fmaf_rn(pl[(int64_t)s * rows * a.heads + rh], w, L);
-            acc = __fmaf_rn(po[((int64_t)s * rows * a.heads + rh) * D + c], w, acc);
-        }
-        const int64_t r = rh / a.heads, h = rh % a.heads;
-        a.out[r * (int64_t)a.heads * D + h * D + c] = L > 0.f ? acc / L : 0.f;
+    extern __shared__ float wsplit[];  // [splits] weights e^(m_s - M)
+    __shared__ float red[4];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t rh = blockIdx.x;  // r * heads + h
+    const int64_t stride = a.q_rows * a.heads;
+    float mx = -FLT_MAX;
+    for (int sp = tid; sp < splits; sp += 128) mx = fmaxf(mx, pm[sp * stride + rh]);
+#pragma unroll
+    for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();
+    float ls = 0.f;
+    for (int sp = tid; sp < splits; sp += 128) {
+        const float ms = pm[sp * stride + rh];
+        const float w = ms == -FLT_MAX ? 0.f : expf(ms - M);
+        wsplit[sp] = w;
+        ls = __fmaf_rn(pl[sp * stride + rh], w, ls);
     }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+    if (lane == 0) red[warp] = ls;
+    __syncthreads();
+    const float L = (red[0] + red[1]) + (red[2] + red[3]);
+    if (tid >= D) return;
+    float acc = 0.f;
+    const float* col = po + rh * D + tid;
+    int sp = 0;
+    for (; sp + 8 <= splits; sp += 8) {
+        float x[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) x[u] = col[(sp + u) * stride * D];
+#pragma unroll
+        for (int u = 0; u < 8; u++) acc = __fmaf_rn(x[u], wsplit[sp + u], acc);
+    }
+    for (; sp < splits; sp++) acc = __fmaf_rn(col[sp * stride * D], wsplit[sp], acc);
+    const int64_t r = rh / a.heads, h = rh % a.heads;
+    a.out[r * (int64_t)a.heads * D + h * D + tid] = L > 0.f ? acc / L : 0.f;
+}
+
+// Key-split plan of the decode path (q_rows <= kSplitRows): heads per CTA, CTAs
+// per key/value head, keys per split (whole tiles) and the split count, sized
+// for one CTA per SM.
+struct SplitPlan {
+    int hpc, hgroups;
+    int64_t chunk, splits, parts;
+};
+
+SplitPlan plan_split(int64_t q_rows, int heads, int kv_heads, int64_t k_rows, int num_sms)
+{
+    SplitPlan p{};
+    const int group = heads / kv_heads;
+    p.hpc = (int)(64 / q_rows) < group ? (int)(64 / q_rows) : group;
+    p.hgroups = (group + p.hpc - 1) / p.hpc;
+    const int64_t base = (int64_t)kv_heads * p.hgroups;
+    int64_t splits = ((int64_t)num_sms + base - 1) / base;
+    const int64_t tiles = (k_rows + KT - 1) / KT;
+    if (splits > tiles) splits = tiles;
+    if (splits < 1) splits = 1;
+    p.chunk = (tiles + splits - 1) / splits * KT;
+    p.splits = (k_rows + p.chunk - 1) / p.chunk;
+    if (p.splits < 1) p.splits = 1;
+    p.parts = p.splits * q_rows * heads;
+    return p;
+}
+
+size_t split_scratch_bytes(const SplitPlan& p, int64_t head_dim)
+{
+    return ((size_t)(2 * p.parts + 3) / 4 * 4 + (size_t)p.parts * head_dim) * sizeof(float);
+}
+
+template <int D, int RE, bool SPLIT>
+cudaError_t launch_tiles(const AttnArgs& a, dim3 grid, int hpc, int hgroups, int64_t chunk, float* pm, float* pl, float* po,
+                         cudaStream_t s)
+{
+    constexpr size_t smem = attn_smem_bytes<D, RE, SPLIT>();
+    cudaError_t e = cudaFuncSetAttribute(k_attn<D, RE, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    k_attn<D, RE, SPLIT><<<grid, ATT_THREADS, smem, s>>>(a, hpc, hgroups, chunk, pm, pl, po);
+    return cudaGetLastError();
+}
+
+template <int D, bool SPLIT>
+cudaError_t launch_rows(const AttnArgs& a, int64_t cta_rows, dim3 grid, int hpc, int hgroups, int64_t chunk, float* pm, float* pl,
+                        float* po, cudaStream_t s)
+{
+    if (cta_rows <= 16) return launch_tiles<D, 1, SPLIT>(a, grid, hpc, hgroups, chunk, pm, pl, po, s);
+    if (cta_rows <= 32) return launch_tiles<D, 2, SPLIT>(a, grid, hpc, hgroups, chunk, pm, pl, po, s);
+    return launch_tiles<D, 4, SPLIT>(a, grid, hpc, hgroups, chunk, pm, pl, po, s);
 }
 
 template <int D>
 cudaError_t launch_attention_d(const AttnArgs& a, float* scratch, size_t scratch_bytes, int num_sms, cudaStream_t s)
 {
-    if (a.q_rows <= 8) {
-        // split the keys so that about two CTAs per SM work
-        int64_t splits = (2 * (int64_t)num_sms + a.heads - 1) / a.heads;
-        const int64_t max_splits = (a.k_rows + 63) / 64;
-        if (splits > max_splits) splits = max_splits;
-        if (splits < 1) splits = 1;
-        const int64_t chunk = (a.k_rows + splits - 1) / splits;
-        splits = (a.k_rows + chunk - 1) / chunk;
-        const int64_t parts = splits * a.q_rows * a.heads;
-        if ((size_t)parts * (2 + D) * sizeof(float) > scratch_bytes) return cudaErrorInvalidValue;
+    if (a.q_rows <= kSplitRows) {
+        const SplitPlan p = plan_split(a.q_rows, a.heads, a.kv_heads, a.k_rows, num_sms);
+        if (split_scratch_bytes(p, D) > scratch_bytes) return cudaErrorInvalidValue;
         float* pm = scratch;
-        float* pl = pm + parts;
-        float* po = pl + parts;
-        k_attn_split<D><<<dim3((unsigned)a.heads, (unsigned)splits), ATT_THREADS, 0, s>>>(a, chunk, pm, pl, po);
-        cudaError_t e = cudaGetLastError();
+        float* pl = pm + p.parts;
+        float* po = scratch + (2 * p.parts + 3) / 4 * 4;
+        const dim3 grid((unsigned)(a.kv_heads * p.hgroups), (unsigned)p.splits);
+        cudaError_t e = launch_rows<D, true>(a, (int64_t)p.hpc * a.q_rows, grid, p.hpc, p.hgroups, p.chunk, pm, pl, po, s);
         if (e != cudaSuccess) return e;
-        const int64_t total = a.q_rows * a.heads * D;
-        int64_t blocks = (total + 255) / 256;
-        if (blocks > 4 * num_sms) blocks = 4 * num_sms;
-        k_attn_combine<D><<<(unsigned)blocks, 256, 0, s>>>(a, (int)splits, pm, pl, po);
+        const size_t wbytes = (size_t)p.splits * sizeof(float);
+        if (wbytes > 48 * 1024) return cudaErrorInvalidValue;
+        k_attn_combine<D><<<(unsigned)(a.q_rows * a.heads), 128, wbytes, s>>>(a, (int)p.splits, pm, pl, po);
         return cudaGetLastError();
     }
-    constexpr size_t smem = (size_t)(D * BQ + D * BKT + BKT * D + BQ * BKT) * sizeof(float);
-    cudaError_t e = cudaFuncSetAttribute(k_attn_tiled<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    const dim3 grid((unsigned)((a.q_rows + BQ - 1) / BQ), (unsigned)a.heads);
-    k_attn_tiled<D><<<grid, ATT_THREADS, smem, s>>>(a);
-    return cudaGetLastError();
+    const int64_t cta_rows = a.q_rows <= 16 ? 16 : a.q_rows <= 32 ? 32 : 64;
+    const dim3 grid((unsigned)((a.q_rows + cta_rows - 1) / cta_rows), (unsigned)a.heads);
+    return launch_rows<D, false>(a, cta_rows, grid, 1, 1, 0, nullptr, nullptr, nullptr, s);
 }
 
 }  // namespace
 
-size_t attention_scratch_bytes(int64_t q_rows, int64_t heads, int64_t head_dim, int num_sms)
+size_t attention_scratch_bytes(int64_t q_rows, int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t k_rows, int num_sms)
 {
-    if (q_rows > 8) return 0;
-    const int64_t splits = (2 * (int64_t)num_sms + heads - 1) / heads;
-    return (size_t)splits * q_rows * heads * (2 + head_dim) * sizeof(float);
+    if (q_rows > kSplitRows) return 0;
+    return split_scratch_bytes(plan_split(q_rows, (int)heads, (int)kv_heads, k_rows, num_sms), head_dim);
 }
 
 cudaError_t launch_attention(const float* q, int64_t q_rows, const float* k, const float* v, int64_t k_rows, int heads,
@@ -364,6 +492,7 @@ cudaError_t launch_attention(const float* q, int64_t q_rows, const float* k, con
     a.heads = heads;
     a.kv_heads = kv_heads;
     a.scale = 1.0f / sqrtf((float)head_dim);
+    a.vec = (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15) == 0;
     switch (head_dim) {
     case 64: return launch_attention_d<64>(a, scratch, scratch_bytes, num_sms, s);
     case 80: return launch_attention_d<80>(a, scratch, scratch_bytes, num_sms, s);

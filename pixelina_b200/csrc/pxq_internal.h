@@ -141,7 +141,7 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 // 128.  q_rows <= 8 uses the key-split kernel and needs
 // attention_scratch_bytes() of scratch.
 constexpr int kAttnMaxRanges = 8;
-size_t attention_scratch_bytes(int64_t q_rows, int64_t heads, int64_t head_dim, int num_sms);
+size_t attention_scratch_bytes(int64_t q_rows, int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t k_rows, int num_sms);
 cudaError_t launch_attention(const float* q, int64_t q_rows, const float* k, const float* v, int64_t k_rows, int heads,
                              int kv_heads, int head_dim, const int64_t* range_end, const int64_t* range_keys,
                              const int* range_causal, int nranges, int64_t query_offset, float* out, float* scratch,

@@ -23,6 +23,9 @@ CASES = [
     (5, 1000, 8, 2, 64, [(0, 5, 1000, True)], 995),                     # decode, five rows
     (8, 4096, 28, 4, 128, [(0, 8, 4096, True)], 4088),                  # VL decode shape, eight rows
     (3, 50, 2, 2, 80, [(0, 2, 50, False), (2, 3, 30, True)], 10),      # decode with two ranges
+    (12, 40, 3, 1, 64, [(0, 12, 40, True)], 28),                        # 16-row query tiles
+    (20, 200, 4, 2, 80, [(0, 20, 200, False)], 0),                      # 32-row query tiles
+    (8, 300, 28, 2, 128, [(0, 8, 300, True)], 292),                     # 14 heads per kv head: two CTAs per group
 ]
 
 
@@ -66,3 +69,28 @@ def test_attention_first_overload_and_argument_checks(pxq):
         pxq.attention(torch.zeros((4, 3 * 64), device="cuda"), torch.zeros((4, 2 * 64), device="cuda"),
                       torch.zeros((4, 2 * 64), device="cuda"), 3, 2)
     assert err.value.code == pxq.ERR_INVALID
+
+
+def test_attention_unaligned_rows(pxq):
+    """Tensors that start one float past a 16-byte boundary take the kernel's
+    word-by-word loads and stores; results are the same."""
+    import torch
+
+    rows, keys, heads, kvh, d = 70, 90, 2, 1, 64
+    rng = np.random.default_rng(11)
+    q = rng.standard_normal((rows, heads * d)).astype(np.float32)
+    k = rng.standard_normal((keys, kvh * d)).astype(np.float32)
+    v = rng.standard_normal((keys, kvh * d)).astype(np.float32)
+
+    def shifted(x):
+        buf = torch.zeros(x.size + 1, device="cuda")
+        buf[1:] = torch.from_numpy(x.reshape(-1)).cuda()
+        return buf[1:].view(x.shape)
+
+    for r, ranges in ((rows, [(0, rows, keys, True)]), (3, [(0, 3, keys, True)])):
+        want = Reference().attention(q[:r], k, v, heads, kvh, ranges, keys - r)
+        out = shifted(np.zeros((r, heads * d), np.float32))
+        assert out.data_ptr() % 16 == 4
+        pxq.attention(shifted(q[:r]), shifted(k), shifted(v), heads, kvh, ranges=ranges, query_offset=keys - r, out=out)
+        pxq.synchronize()
+        assert max_abs_rel(out.cpu().numpy(), want) <= ATT_TOL
