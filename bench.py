@@ -716,9 +716,37 @@ def run_attention(args, dist: Dist):
                          "fp32_frac": round(flops / (ms * 1e-3) / 1e12 / fp32_peak, 4),
                          "kv_GBps": round(kv_bytes / (ms * 1e-3) / 1e9, 1), "hbm_frac": round(kv_bytes / (ms * 1e-3) / 1e9 / hbm, 4),
                          "clocks": clocks}
+        if dist.rank == 0 and not args.no_cpu_baseline:
+            results[name]["cpu_baseline"] = attention_cpu_baseline(c, q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy())
     return {"metric": METRIC, "workload": "attention: DiT prefill and VL decode shapes (tensor_attention, fp32)",
             "unit": "TFLOP/s", "value": results["dit_prefill"]["TFLOPs"], "results": results, "n_gpus": dist.world,
             "fp32_peak_tflops": round(fp32_peak, 1), "peak_hbm_gbs": hbm, "peak_source": peak_src}
+
+
+def attention_cpu_baseline(c, q, k, v, target_s: float = 6.0):
+    """The reference's tensor_attention (oracle/_ref, all host threads) on the
+    first query rows of the same inputs, sized to about target_s per call."""
+    lib, kind = cpu_library()
+    if kind != "reference":
+        return {"value": None, "unit": "TFLOP/s", "cores": 0, "kind": "unavailable", "sample": "oracle/_ref was not built"}
+    cores = os.cpu_count() or 1
+    lib.set_threads(cores)
+
+    def call(r):
+        ranges = c["ranges"] if r == c["rows"] and c["ranges"] else [(0, r, c["keys"], c["causal"])]
+        off = c["off"] + (c["rows"] - r if c["causal"] else 0)
+        t0 = time.perf_counter()
+        out = lib.attention(q[:r], k, v, c["heads"], c["kvh"], ranges, off)
+        assert out is not None
+        return time.perf_counter() - t0
+
+    probe = min(c["rows"], 8)
+    per_row = call(probe) / probe
+    rows = int(min(c["rows"], max(probe, target_s / 3 / max(per_row, 1e-9))))
+    t = statistics.median([call(rows) for _ in range(3)])
+    flops = 4.0 * rows * c["keys"] * c["heads"] * c["d"]
+    return {"value": round(flops / t / 1e12, 5), "unit": "TFLOP/s", "cores": cores, "kind": kind,
+            "sample": f"first {rows} of {c['rows']} query rows against all {c['keys']} keys; median of 3 ({t:.2f} s each)"}
 
 
 def run_sharded(args, dist: Dist):
