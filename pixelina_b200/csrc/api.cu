@@ -957,8 +957,10 @@ int pxq_attention(const float* q, size_t q_rows, const float* k, const float* v,
     const size_t need = attention_scratch_bytes((int64_t)q_rows, (int64_t)heads, (int64_t)kv_heads, (int64_t)head_dim, (int64_t)k_rows, d->sms);
     float* scratch = nullptr;
     if (need) {
-        scratch = static_cast<float*>(stream_scratch(t_device, s, need));
-        if (!scratch) return fail(PXQ_ERR_NO_MEMORY, "attention scratch of %zu bytes", need);
+        // past the matvec's counter region, which every call must leave zero
+        uint8_t* base = static_cast<uint8_t*>(stream_scratch(t_device, s, kMvCounterRegion + need));
+        if (!base) return fail(PXQ_ERR_NO_MEMORY, "attention scratch of %zu bytes", need);
+        scratch = reinterpret_cast<float*>(base + kMvCounterRegion);
     }
     const cudaError_t e = launch_attention(q, (int64_t)q_rows, k, v, (int64_t)k_rows, (int)heads, (int)kv_heads, (int)head_dim,
                                            ends, keys, causal, n, (int64_t)query_offset, output, scratch, need, d->sms, s);

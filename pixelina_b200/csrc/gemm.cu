@@ -333,8 +333,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&tempty[i], CG * DRAIN_WARPS);  // the drain warps of every CTA of the tile
         }
         mbar_init(mma_done, 1);
-        mbar_init(&merge[0], DRAIN_WARPS);
-        mbar_init(&merge[1], DRAIN_WARPS);
+        mbar_init(&merge[0], 32 * DRAIN_WARPS);  // every lane: each releases its own staging stores
+        mbar_init(&merge[1], 32 * DRAIN_WARPS);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -573,8 +573,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint64_t gsb = 0, item = 0;
         // all drain warps meet (bounded wait, like every wait of this kernel)
         auto drain_meet = [&](int i) -> bool {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&merge[i]);
+            mbar_arrive(&merge[i]);  // all lanes: a single lane's release does not cover the others' stores
             return mbar_wait(&merge[i], mgph, abort_flag, status, kDevTimeoutTmemFull);
         };
         for (int64_t tile = pair; tile < tiles; tile += pairs) {

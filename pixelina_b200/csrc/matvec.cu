@@ -617,7 +617,7 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_kq(const __grid_consta
             mbar_init(&sm.full[i], 1);
             mbar_init(&sm.empty[i], kMvConsumers);
         }
-        mbar_init(&sm.part, kRg);
+        mbar_init(&sm.part, 32 * kRg);  // every lane of the row-group warps that store partial sums
         sm.abort = 0;
         fence_mbar_init();
     }
@@ -816,8 +816,7 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_kq(const __grid_consta
                     mine[(2 * t + 1) * TR + la] = v[1];
                     mine[(2 * t + 1) * TR + lb] = v[3];
                 }
-                __syncwarp();
-                if (seg == 0 && first_async && lane == 0) mbar_arrive(&sm.part);
+                if (seg == 0 && first_async) mbar_arrive(&sm.part);  // each lane releases its own stores
             }
         }
         acc[0] = acc[1] = acc[2] = acc[3] = 0.f;

@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 from conftest import max_abs_rel
-from oracle.oracle import Reference, reference_available
+from oracle.oracle import TYPE_Q5_K, Reference, reference_available
 
 pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not reference_available(), reason="oracle/_ref is missing")]
 ATT_TOL = 2e-5
@@ -94,3 +94,26 @@ def test_attention_unaligned_rows(pxq):
         pxq.attention(shifted(q[:r]), shifted(k), shifted(v), heads, kvh, ranges=ranges, query_offset=keys - r, out=out)
         pxq.synchronize()
         assert max_abs_rel(out.cpu().numpy(), want) <= ATT_TOL
+
+
+def test_attention_leaves_matvec_counters_alone(pxq, oracle):
+    """The decode kernels' partial sums share the stream's scratch with the
+    matvec's stream-K counters, which every call must leave zero: a stream-K
+    matvec right after a decode attention on the same stream is still exact."""
+    import torch
+
+    from pixelina_b200 import synth
+
+    rng = np.random.default_rng(3)
+    q = torch.from_numpy(rng.standard_normal((8, 28 * 128)).astype(np.float32)).cuda()
+    kv = torch.from_numpy(rng.standard_normal((4096, 4 * 128)).astype(np.float32)).cuda()
+    pxq.attention(q, kv, kv, 28, 4, ranges=[(0, 8, 4096, True)], query_offset=4088)
+    rows, inner = 100, 1024  # a few stream-K CTAs sharing tiles
+    w = synth.weights_for(TYPE_Q5_K, rows, inner, seed=1)
+    x = synth.activations(1, inner, seed=51)
+    W = pxq.Weight(w, TYPE_Q5_K, inner, rows)
+    y = pxq.matmul(W, torch.from_numpy(x).cuda(), path="matvec").cpu().numpy()
+    pxq.synchronize()
+    W.release()
+    ok, ref = oracle.quant_matmul(w, TYPE_Q5_K, x, rows)
+    assert ok and max_abs_rel(y, ref) <= 1e-3
