@@ -896,7 +896,22 @@ int pxq_matmul_gated(pxq_weight* w, const float* input, size_t columns, float* o
         free_activation(a, s);
         return rc;
     }
-    // matvec over the 2F rows into scratch after the matvec's own, then the epilogue
+    if (w->type == kTypeQ5_K || w->type == kTypeQ6_K) {
+        // one matvec: each CTA streams gate tile j and up tile j and writes silu(g) * u
+        const MatvecPlan plan = plan_matvec(w->type, w->rows, w->inner, (int64_t)columns, d->sms, true, true);
+        void* scratch = stream_scratch(t_device, s, plan.total_bytes);
+        const bool own = scratch == nullptr;
+        if (own && cudaMallocAsync(&scratch, plan.total_bytes, s) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(PXQ_ERR_NO_MEMORY, "gated matvec scratch allocation of %zu bytes failed", plan.total_bytes);
+        }
+        cudaError_t e = matvec_fused(w, 0, (size_t)w->rows, input, output, ldy, nullptr, plan, static_cast<uint8_t*>(scratch),
+                                     d->status, s);
+        if (own) cudaFreeAsync(scratch, s);
+        if (e != cudaSuccess) return fail(PXQ_ERR_CUDA, "gated matvec launch failed: %s", cudaGetErrorString(e));
+        return PXQ_OK;
+    }
+    // Q8_0: matvec over the 2F rows into scratch after the matvec's own, then the epilogue
     const MatvecPlan plan = plan_matvec(w->type, w->rows, w->inner, (int64_t)columns, d->sms, true);
     const size_t off_s = (plan.total_bytes + 255) & ~(size_t)255;
     const size_t need = off_s + (size_t)columns * (size_t)w->rows * 4;

@@ -296,6 +296,7 @@ struct MvParams {
     uint32_t* counters;                // [tiles]
     uint32_t* status;
     int64_t ldy, rows, row_first, stages;
+    int64_t gated_half;                // gated pair: F / 64; logical tile 2j = gate tile j, 2j+1 = up tile j
     int32_t nsb, spt, columns;
 };
 
@@ -654,11 +655,13 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_kq(const __grid_consta
                 const uint32_t nsb_here = nsb - kSbs * q < (uint32_t)kSbs ? nsb - kSbs * q : (uint32_t)kSbs;
                 const uint32_t act_tx = fused ? 0u : columns * nsb_here * kRec;
                 mbar_expect_tx(&sm.full[slot], Sh::kWeightBytes + act_tx);
+                // weight tile of logical tile T (gated pairs: gate tile T/2, then up tile T/2)
+                const int64_t Tw = p.gated_half ? (int64_t)(T >> 1) + ((T & 1u) ? p.gated_half : 0) : (int64_t)T;
                 if (Sh::kRowMajor)
                     tma_load_2d(sm.weight[slot], &p.map, &sm.full[slot], (int32_t)(q * (Sh::kRowBytes / 8)),
-                                (int32_t)(p.row_first + (int64_t)T * TR));
+                                (int32_t)(p.row_first + Tw * TR));
                 else
-                    tma_load_3d(sm.weight[slot], &p.map, &sm.full[slot], 0, (int32_t)(p.row_first + (int64_t)T * TR),
+                    tma_load_3d(sm.weight[slot], &p.map, &sm.full[slot], 0, (int32_t)(p.row_first + Tw * TR),
                                 (int32_t)(q * kSbs));
                 if (fused) {
                     // the consumers quantize the activation themselves
@@ -744,6 +747,7 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_kq(const __grid_consta
     const uint32_t x0_off = act_row_off<TR, WT>(2 * t) + sbl * kRec;      // activation row 2t
     const uint32_t x1_off = act_row_off<TR, WT>(2 * t + 1) + sbl * kRec;  // activation row 2t+1
     float acc[4] = {0.f, 0.f, 0.f, 0.f}, summ[4] = {0.f, 0.f, 0.f, 0.f};
+    float gate_v[4] = {0.f, 0.f, 0.f, 0.f};  // gated pairs: the gate tile's sums, until the up tile ends
     bool ok = true;
     uint32_t seg = 0, slot = 0, phase = 0, T = T0, q = q0;
     bool seg_whole_start = q0 == 0;  // this segment starts at its tile's first stage
@@ -799,7 +803,25 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_kq(const __grid_consta
                 v[3] += red[k][rg][g + 8][2 * t + 1];
             }
             const int64_t ra = (int64_t)Tcur * TR + 16 * rg + g, rb = ra + 8;
-            if (seg_whole_start && tile_last) {
+            if (p.gated_half) {
+                // whole tiles in pairs: keep the gate sums, then finish tensor_silu +
+                // tensor_gate on the up sums of the same rows (the order of operations
+                // of the two-kernel path)
+                if ((Tcur & 1u) == 0) {
+#pragma unroll
+                    for (int k = 0; k < 4; k++) gate_v[k] = v[k];
+                } else {
+                    const int64_t na = (int64_t)(Tcur >> 1) * TR + 16 * rg + g, nb = na + 8;
+                    float o[4];
+#pragma unroll
+                    for (int k = 0; k < 4; k++)
+                        o[k] = __fmul_rn(__fdiv_rn(gate_v[k], __fadd_rn(1.0f, expf(-gate_v[k]))), v[k]);
+                    if (vc0) p.y[(int64_t)(2 * t) * p.ldy + na] = o[0];
+                    if (vc1) p.y[(int64_t)(2 * t + 1) * p.ldy + na] = o[1];
+                    if (vc0) p.y[(int64_t)(2 * t) * p.ldy + nb] = o[2];
+                    if (vc1) p.y[(int64_t)(2 * t + 1) * p.ldy + nb] = o[3];
+                }
+            } else if (seg_whole_start && tile_last) {
                 if (vc0 && ra < p.rows) store_out(p, ra, 2 * t, v[0]);
                 if (vc1 && ra < p.rows) store_out(p, ra, 2 * t + 1, v[1]);
                 if (vc0 && rb < p.rows) store_out(p, rb, 2 * t, v[2]);
@@ -873,6 +895,7 @@ cudaError_t launch_kq(const MatvecPlan& plan, const CUtensorMap* map, int64_t ro
     prm.nsb = (int32_t)(plan.inner / kQKK);
     prm.spt = (int32_t)plan.spt;
     prm.columns = (int32_t)plan.columns;
+    prm.gated_half = plan.gated_half;
     return launch_pdl(k_matvec_kq<TR, FUSED, WT>, dim3(plan.grid), dim3(kMvThreads), sizeof(MvSmem<TR, FUSED, WT>), s, prm);
 }
 
@@ -893,7 +916,8 @@ cudaError_t launch_kq3(const MatvecPlan& plan, const CUtensorMap* map, int64_t r
 
 int matvec_map_index(int tile_rows) { return tile_rows == 64 ? 0 : tile_rows == 32 ? 1 : 2; }
 
-MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t columns, int num_sms, bool fuse_quantize)
+MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t columns, int num_sms, bool fuse_quantize,
+                       bool gated)
 {
     MatvecPlan p;
     p.type = type;
@@ -913,7 +937,10 @@ MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t colum
         // stream-K split over the whole grid.
         p.tile_rows = 64;
         bool whole = false;
+        // gated: 64-row tiles taken in pairs (gate tile j, up tile j) by one CTA each
+        if (gated) p.gated_half = rows / 128;
         for (int tr : {64, 32, 16}) {
+            if (gated) break;
             const int64_t tiles = (rows + tr - 1) / tr;
             const int64_t tile_bytes = (int64_t)tr * nsb * sb_bytes;
             const bool short_tiles = tile_bytes <= 64 * 1024 || (type == kTypeQ5_K && tr == 16);
@@ -927,13 +954,13 @@ MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t colum
         p.tiles = (rows + p.tile_rows - 1) / p.tile_rows;
         p.spt = (nsb + sbs - 1) / sbs;
         p.stages = p.tiles * p.spt;
-        p.grid = (int)(whole ? p.tiles : (p.stages < slots ? p.stages : slots));
+        p.grid = (int)(gated ? p.tiles / 2 : whole ? p.tiles : (p.stages < slots ? p.stages : slots));
         // small activations: every CTA quantizes the records of its own stages
         // (at most kMvFusedRecords), no separate quantize kernel
         const int64_t max_stages = (p.stages + p.grid - 1) / p.grid;
         p.fused = fuse_quantize && columns * max_stages * sbs <= kMvFusedRecords;
         p.act_bytes = p.fused ? 0 : (size_t)(columns * nsb * rec_bytes);
-        p.partial_bytes = whole ? 0 : (size_t)p.grid * 2 * columns * p.tile_rows * sizeof(float);
+        p.partial_bytes = whole || gated ? 0 : (size_t)p.grid * 2 * columns * p.tile_rows * sizeof(float);
         p.counter_bytes = (size_t)p.tiles * sizeof(uint32_t);
     } else {
         const int64_t nblocks = inner / kQK8_0;

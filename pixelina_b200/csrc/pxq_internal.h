@@ -94,12 +94,17 @@ struct MatvecPlan {
     int ks = 1, chunk = 0;                   // Q8_0: K slices per row group, blocks per slice
     int64_t rowgroups = 0;                   // Q8_0: 16-row groups
     bool fused = false;                      // Q5_K: the matvec quantizes the activation itself
+    int64_t gated_half = 0;                  // K-quants, gated weight [gate; up]: F / 64 (the epilogue writes silu(g) * u)
     size_t act_bytes = 0, partial_bytes = 0, counter_bytes = 0;
     size_t off_counters = 0, off_act = 0, off_partial = 0, total_bytes = 0;
 };
 // fuse_quantize: allow the plan to let the matvec quantize a small
 // activation itself (then act_bytes is 0 and launch_matvec takes x).
-MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t columns, int num_sms, bool fuse_quantize = false);
+// gated (K-quants, rows = 2F, F % 64 == 0): the weight is a gated pair [gate;
+// up] and the matvec writes y[c][n] = silu(gate_n . x_c) * (up_n . x_c) for
+// n < F, each CTA taking gate tile j and up tile j (64 rows each).
+MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t columns, int num_sms, bool fuse_quantize = false,
+                       bool gated = false);
 int matvec_map_index(int tile_rows);
 // Quantize the plan's `columns` activation rows (row stride ldx floats) into
 // the operand at `act`; clears `counters` (plan.counter_bytes) when non-null.
