@@ -244,10 +244,15 @@ def time_steps(step, steps: int, warmup: int, flush, soak_s: float, sampler: Clo
         step(None)
     torch.cuda.synchronize()
     sampler.start()
-    t0 = time.perf_counter()
-    while time.perf_counter() - t0 < soak_s:
+    if soak_s > 0:
+        # the same number of soak steps on every rank (steps may hold collectives)
+        t0 = time.perf_counter()
         step(None)
         torch.cuda.synchronize()
+        n_soak = int(dist.max(soak_s / max(time.perf_counter() - t0, 1e-6)))
+        for _ in range(n_soak):
+            step(None)
+            torch.cuda.synchronize()
     events = []
     dist.barrier()
     torch.cuda.synchronize()
@@ -793,11 +798,33 @@ def run_sharded(args, dist: Dist):
                                             ClockSampler(dist.local), dist)
     ms = dist.max(statistics.mean(step_ms))
     gemm_ms = dist.max(statistics.mean(kernel_ms["gemm"]))
-    return {"metric": METRIC, "workload": "sharded: Q8_0 M=16384 N=12288 K=3072 N-sharded + NCCL all-gather (configs[4])",
-            "unit": "TOPS", "n_gpus": G, "value_with_gather": round(ops / (ms * 1e-3) / 1e12, 2),
-            "value_gemm_only": round(ops / (gemm_ms * 1e-3) / 1e12, 2), "ms_per_step": round(ms, 3),
-            "gemm_ms": round(gemm_ms, 3), "gather_bytes_per_rank": (G - 1) * M * Ns * 4, "clocks": clocks,
-            "scaling": "strong"}
+    del scratch
+    out = {"metric": METRIC, "workload": "sharded: Q8_0 M=16384 N=12288 K=3072 N-sharded (configs[4])",
+           "unit": "TOPS", "n_gpus": G, "value_with_gather": round(ops / (ms * 1e-3) / 1e12, 2),
+           "value_gemm_only": round(ops / (gemm_ms * 1e-3) / 1e12, 2), "ms_per_step": round(ms, 3),
+           "gemm_ms": round(gemm_ms, 3), "gather_bytes_per_rank": (G - 1) * M * Ns * 4, "clocks": clocks,
+           "scaling": "strong"}
+    if G > 1:
+        # the one-kernel path: each rank's GEMM epilogue stores its columns into
+        # every rank's Y over NVLink (CUDA IPC mappings), a device barrier before
+        # (Y free) and after (all stores landed) -- no all-gather, no re-layout
+        del y
+        po = sharded.PeerOutput(M, N)
+
+        def step_p2p(ev):
+            if ev is not None:
+                ev["start"], ev["end"] = ev_pair()
+                ev["start"].record()
+            sharded.sharded_matmul_p2p(sw, x, po)
+            if ev is not None:
+                ev["end"].record()
+
+        p2p_ms, _, clocks2 = time_steps(step_p2p, args.steps, args.warmup, flush_buf.zero_, 0.0, ClockSampler(dist.local), dist)
+        ms2 = dist.max(statistics.mean(p2p_ms))
+        po.close()
+        out.update({"value_p2p": round(ops / (ms2 * 1e-3) / 1e12, 2), "ms_per_step_p2p": round(ms2, 3),
+                    "p2p_bytes_per_rank": (G - 1) * M * Ns * 4, "clocks_p2p": clocks2})
+    return out
 
 
 def main():

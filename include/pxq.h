@@ -180,6 +180,29 @@ PXQ_API int pxq_synchronize(void* stream);
 PXQ_API int pxq_gather_shards(const float* src, size_t shards, size_t columns, size_t shard_rows, float* dst, size_t ldy,
                       void* stream);
 
+/* The N-sharded multi-GPU matmul in one kernel: this rank's weight rows
+ * [row_first, row_first + row_count) times `input` (columns > 8: the GEMM
+ * path), with element (m, n) stored into dsts[k][m * ldy + col_offset + n]
+ * for every k < ndst -- this GPU's output and the other ranks' outputs
+ * (device pointers opened with pxq_ipc_open), written by the GEMM epilogue
+ * over NVLink while the next tiles compute.  Replaces the matmul, the
+ * all-gather and pxq_gather_shards of the N-sharded path (each rank holding
+ * weight rows of cpu_quant_matmul's independent output columns,
+ * src/kernels_quant.cpp:390-398).  The caller orders the ranks around the
+ * call (every rank's buffers free before, a barrier after).  1 <= ndst <= 8. */
+PXQ_API int pxq_matmul_scatter(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns,
+                               float* const* dsts, size_t ndst, size_t ldy, size_t col_offset, void* stream);
+
+/* Device buffers other processes of the node can map (CUDA IPC): allocate
+ * `bytes` on the current device and write its PXQ_IPC_HANDLE_BYTES handle;
+ * open another process's handle as a pointer usable in this process's
+ * kernels (peer access over NVLink); close / free them. */
+#define PXQ_IPC_HANDLE_BYTES 64
+PXQ_API int pxq_ipc_alloc(size_t bytes, void** ptr, void* handle);
+PXQ_API int pxq_ipc_free(void* ptr);
+PXQ_API int pxq_ipc_open(const void* handle, void** ptr);
+PXQ_API int pxq_ipc_close(void* ptr);
+
 /* ---- quantize once, multiply many ----------------------------------------
  * The reference quantizes the activation inside every cpu_quant_matmul call
  * (src/kernels_quant.cpp:382-388).  These entry points split that step out so

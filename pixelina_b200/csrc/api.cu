@@ -464,7 +464,8 @@ void* stream_scratch(int device, cudaStream_t s, size_t need)
 }
 
 int run_gemm(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, const pxq_activation* a, float* output,
-             size_t ldy, const float* bias, float* dump, cudaStream_t s)
+             size_t ldy, const float* bias, float* dump, cudaStream_t s, float* const* dsts = nullptr, int ndst = 0,
+             int64_t col_off = 0)
 {
     if (a->blocks) return fail(PXQ_ERR_UNSUPPORTED, "activation was quantized for the matvec path");
     const Packed* pk = nullptr;
@@ -484,6 +485,9 @@ int run_gemm(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, co
     op.dump = dump;
     op.status = d->status;
     op.gated = w->gated ? 1 : 0;
+    op.ndst = ndst;
+    op.col_off = col_off;
+    for (int k = 0; k < ndst; k++) op.ydst[k] = dsts[k];
     op.tm[0] = pk->tmW;
     op.tm[1] = a->tmX;
     op.tm[2] = pk->tmWs;
@@ -496,7 +500,7 @@ int run_gemm(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, co
     // innermost dimension only at 16-byte granularity)
     op.tma_store = 0;
     op.tm_y = op.tm[0];
-    if (!dump && !w->gated && gemm_store_rows(w->type) > 0 && (reinterpret_cast<uintptr_t>(output) & 15u) == 0 &&
+    if (!dump && !w->gated && !ndst && gemm_store_rows(w->type) > 0 && (reinterpret_cast<uintptr_t>(output) & 15u) == 0 &&
         (ldy % 4) == 0 && (row_count % 4) == 0) {
         if (make_map(d, &op.tm_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, output, row_count, (uint64_t)a->M, ldy * 4, 32,
                      (uint32_t)gemm_store_rows(w->type),
@@ -875,6 +879,83 @@ int pxq_matmul(pxq_weight* w, size_t row_first, size_t row_count, const float* i
     if (int rc = check_matmul_args(w, row_first, row_count, input, columns, output, ldy)) return rc;
     return run_matmul(d, w, row_first, row_count, input, columns, output, ldy, bias, nullptr, 0,
                       static_cast<cudaStream_t>(stream));
+}
+
+int pxq_matmul_scatter(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns,
+                       float* const* dsts, size_t ndst, size_t ldy, size_t col_offset, void* stream)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (!dsts || !ndst || ndst > (size_t)kMaxScatter) return fail(PXQ_ERR_INVALID, "1 to %d destinations (got %zu)", kMaxScatter, ndst);
+    for (size_t k = 0; k < ndst; k++)
+        if (!dsts[k]) return fail(PXQ_ERR_INVALID, "null destination %zu", k);
+    if (int rc = check_matmul_args(w, row_first, row_count, input, columns, dsts[0], ldy)) return rc;
+    if (columns <= 8) return fail(PXQ_ERR_UNSUPPORTED, "scatter runs on the GEMM path (more than 8 columns, got %zu)", columns);
+    if (col_offset + row_count > ldy) return fail(PXQ_ERR_INVALID, "columns [%zu, %zu) outside ldy %zu", col_offset,
+                                                  col_offset + row_count, ldy);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    pxq_activation* a = nullptr;
+    int rc = quantize_activation(d, w->type, input, (int64_t)columns, w->inner, 2, &a, s);
+    if (rc) return rc;
+    rc = run_gemm(d, w, row_first, row_count, a, nullptr, ldy, nullptr, nullptr, s, dsts, (int)ndst, (int64_t)col_offset);
+    free_activation(a, s);
+    return rc;
+}
+
+int pxq_ipc_alloc(size_t bytes, void** ptr, void* handle)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (!ptr || !handle || !bytes) return fail(PXQ_ERR_INVALID, "null pointer or zero bytes");
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(PXQ_ERR_NO_MEMORY, "%zu bytes", bytes);
+    }
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(p);
+        return fail(PXQ_ERR_CUDA, "cudaIpcGetMemHandle failed");
+    }
+    static_assert(sizeof(h) == PXQ_IPC_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(handle, &h, sizeof(h));
+    *ptr = p;
+    return PXQ_OK;
+}
+
+int pxq_ipc_free(void* ptr)
+{
+    if (ptr && cudaFree(ptr) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(PXQ_ERR_CUDA, "cudaFree failed");
+    }
+    return PXQ_OK;
+}
+
+int pxq_ipc_open(const void* handle, void** ptr)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (!handle || !ptr) return fail(PXQ_ERR_INVALID, "null handle or pointer");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(PXQ_ERR_CUDA, "cudaIpcOpenMemHandle failed");
+    }
+    *ptr = p;
+    return PXQ_OK;
+}
+
+int pxq_ipc_close(void* ptr)
+{
+    if (ptr && cudaIpcCloseMemHandle(ptr) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(PXQ_ERR_CUDA, "cudaIpcCloseMemHandle failed");
+    }
+    return PXQ_OK;
 }
 
 int pxq_matmul_gated(pxq_weight* w, const float* input, size_t columns, float* output, size_t ldy, void* stream)

@@ -165,7 +165,22 @@ struct Params {
     uint32_t* status;
     int tma_store;  // 1: epilogue through shared memory + TMA store (tmY)
     int gated;      // 1: gated weight, y = silu(gate) * up over N/2 outputs (direct stores)
+    int ndst;       // > 0: scatter, element (m, n) to ydst[k][m * ldy + col_off + n], k < ndst (direct stores)
+    int64_t col_off;
+    float* ydst[kMaxScatter];
 };
+
+// One output element: this GPU's y, or every destination of a scatter (its own
+// buffer and the peers', written straight over NVLink).
+__device__ __forceinline__ void put_y(const Params& p, int64_t m, int64_t n, float v)
+{
+    if (p.ndst == 0) {
+        p.y[m * p.ldy + n] = v;
+        return;
+    }
+    const int64_t off = m * p.ldy + p.col_off + n;
+    for (int k = 0; k < p.ndst; k++) p.ydst[k][off] = v;
+}
 
 // tcgen05 and stage-load forms for one CTA per tile (CG = 1) or a CTA pair
 // (CG = 2); a kernel uses one form throughout, as tcgen05 requires.
@@ -755,15 +770,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                                         const int64_t nn = n0 + quad * 32 + 16 * lh + 8 * h + (lane >> 2);
                                         const int64_t m = mfirst + 64 * ch + 8 * k + 2 * (lane & 3) + c;
                                         const float v = acc[split_idx(ch, lh, k, h, c)];
-                                        if (nn < p.N && m < p.M) p.y[m * p.ldy + nn] = p.bias ? __fadd_rn(v, bv[2 * lh + h]) : v;
+                                        if (nn < p.N && m < p.M) put_y(p, m, nn, p.bias ? __fadd_rn(v, bv[2 * lh + h]) : v);
                                     }
                 } else if (n < p.N) {
                     // lane = weight row: for each activation row, 32 lanes store 128 contiguous bytes
-                    float* yc = p.y + n;
 #pragma unroll
                     for (int j = 0; j < HC; j++) {
                         const int64_t m = mfirst + j;
-                        if (m < p.M) yc[m * p.ldy] = p.bias ? __fadd_rn(acc[j], bv[0]) : acc[j];
+                        if (m < p.M) put_y(p, m, n, p.bias ? __fadd_rn(acc[j], bv[0]) : acc[j]);
                     }
                 }
             }
@@ -827,7 +841,9 @@ cudaError_t launch_typed(const GemmOperands& op, int num_sms, cudaStream_t s)
     if (tiles < groups) groups = tiles;
     if (groups < 1) groups = 1;
     cfg.gridDim = dim3((unsigned)(CG * groups));
-    Params p{op.M, op.N, op.K, op.n_first, op.y, op.ldy, op.bias, op.dump, op.status, (op.tma_store && !DUMP) ? 1 : 0, op.gated};
+    Params p{op.M, op.N, op.K, op.n_first, op.y, op.ldy, op.bias, op.dump, op.status, (op.tma_store && !DUMP) ? 1 : 0, op.gated,
+             op.ndst, op.col_off, {}};
+    for (int k = 0; k < kMaxScatter; k++) p.ydst[k] = op.ydst[k];
     return cudaLaunchKernelEx(&cfg, kern, op.tm[0], op.tm[1], op.tm[2], op.tm[3], op.tm[4], op.tm[5], op.tm[6], op.tm_y, p);
 }
 

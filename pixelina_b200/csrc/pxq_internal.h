@@ -157,6 +157,8 @@ cudaError_t launch_gather_shards(const float* src, int64_t shards, int64_t colum
                                  int64_t ldy, cudaStream_t s);
 
 // ---- gemm.cu ---------------------------------------------------------------
+constexpr int kMaxScatter = 8;  // destinations of a scattering GEMM (one per rank of a node)
+
 struct GemmOperands {
     uint32_t type;        // kTypeQ8_0, kTypeQ5_K or kTypeQ6_K
     int64_t M, N, K;      // activation rows, view rows (output columns), inner
@@ -174,6 +176,11 @@ struct GemmOperands {
     float* dump;          // debug: raw per-item block dots, or null
     int gated;            // gated weight (2F interleaved rows, N = 2F): y[m][n < F] = silu(gate) * up
     uint32_t* status;     // device status word
+    // scatter (ndst > 0, no TMA store): element (m, n) goes to ydst[k][m * ldy + col_off + n] for
+    // every k < ndst -- this GPU's buffer and peers' buffers (P2P stores over NVLink)
+    float* ydst[kMaxScatter];
+    int ndst;
+    int64_t col_off;
 };
 // Rows of one CTA's activation box in the GEMM's tensor maps (tmX, tmXs),
 // and of a whole output tile (the activation scale map tmDx's box).

@@ -67,6 +67,11 @@ SIGNATURES = {
     "pxq_matmul_host": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _sz]),
     "pxq_synchronize": (_i, [_vp]),
     "pxq_gather_shards": (_i, [_vp, _sz, _sz, _sz, _vp, _sz, _vp]),
+    "pxq_matmul_scatter": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _sz, _sz, _sz, _vp]),
+    "pxq_ipc_alloc": (_i, [_sz, _vp, _vp]),
+    "pxq_ipc_free": (_i, [_vp]),
+    "pxq_ipc_open": (_i, [_vp, _vp]),
+    "pxq_ipc_close": (_i, [_vp]),
     "pxq_gemm_block_dots": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _vp]),
     "pxq_activation_quantize": (_i, [_u32, _vp, _sz, _sz, C.POINTER(_vp), _vp]),
     "pxq_matmul_quantized": (_i, [_vp, _sz, _sz, _vp, _vp, _sz, _vp, _vp]),
@@ -436,6 +441,61 @@ def gather_shards(src, shards: int, columns: int, shard_rows: int, out=None, str
         out = torch.empty((columns, shards * shard_rows), dtype=torch.float32, device=src.device)
     _check(load().pxq_gather_shards(_ptr(src), shards, columns, shard_rows, _ptr(out), out.stride(0), _stream_ptr(stream)))
     return out
+
+
+IPC_HANDLE_BYTES = 64
+
+
+class IpcBuffer:
+    """fp32 device buffer [rows][cols] that other processes of the node can
+    map (pxq_ipc_alloc); ``handle`` is its 64-byte CUDA IPC handle and
+    ``tensor`` a torch view of it on this device."""
+
+    def __init__(self, rows: int, cols: int):
+        torch = _torch()
+        ptr, handle = C.c_void_p(), (C.c_uint8 * IPC_HANDLE_BYTES)()
+        _check(load().pxq_ipc_alloc(rows * cols * 4, C.byref(ptr), C.cast(handle, C.c_void_p)))
+        self.ptr, self.handle, self.shape = ptr.value, bytes(handle), (rows, cols)
+        self.tensor = torch.as_tensor(_CudaArray(self.ptr, self.shape), device="cuda")
+
+    def free(self) -> None:
+        if self.ptr:
+            self.tensor = None
+            _check(load().pxq_ipc_free(C.c_void_p(self.ptr)))
+            self.ptr = None
+
+
+class IpcPeer:
+    """Another process's IpcBuffer opened in this one (pxq_ipc_open)."""
+
+    def __init__(self, handle: bytes):
+        ptr = C.c_void_p()
+        buf = (C.c_uint8 * IPC_HANDLE_BYTES).from_buffer_copy(handle)
+        _check(load().pxq_ipc_open(C.cast(buf, C.c_void_p), C.byref(ptr)))
+        self.ptr = ptr.value
+
+    def close(self) -> None:
+        if self.ptr:
+            _check(load().pxq_ipc_close(C.c_void_p(self.ptr)))
+            self.ptr = None
+
+
+class _CudaArray:
+    """Minimal __cuda_array_interface__ over a raw fp32 device pointer."""
+
+    def __init__(self, ptr: int, shape):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<f4", "data": (ptr, False), "version": 2}
+
+
+def matmul_scatter(W: "Weight", x, dst_ptrs, ldy: int, col_offset: int, row_first: int = 0, row_count=None, stream=None):
+    """pxq_matmul_scatter: rows [row_first, row_first + row_count) of W times
+    x (device fp32 [M][K], M > 8), every element written to each pointer of
+    ``dst_ptrs`` at [m][col_offset + n] with row stride ``ldy``."""
+    x = x.contiguous()
+    row_count = W.rows - row_first if row_count is None else row_count
+    arr = (C.c_void_p * len(dst_ptrs))(*[C.c_void_p(p) for p in dst_ptrs])
+    _check(load().pxq_matmul_scatter(W.handle, row_first, row_count, _ptr(x), x.shape[0], C.cast(arr, C.c_void_p), len(dst_ptrs),
+                                     ldy, col_offset, _stream_ptr(stream)))
 
 
 def synchronize(stream=None) -> None:

@@ -8,8 +8,14 @@ Y[:, shard] for all M activation rows, an all-gather collects the G blocks
 caller's row-major Y[M][N] (``output[c*rows + r]``, src/kernels_quant.cpp:398).
 Each rank quantizes the replicated activation itself; the quantized bytes
 are identical on every rank, so the gathered Y is bit-identical to a 1-GPU
-run.  Collectives go through ``torch.distributed`` (NCCL on GPUs); this
-module adds no compute path of its own.
+run.
+
+Two ways to assemble Y: ``sharded_matmul`` (local matmul, NCCL all-gather,
+re-layout) and ``sharded_matmul_p2p`` (one kernel per rank: the GEMM epilogue
+stores each output tile straight into every rank's Y through CUDA IPC
+mappings over NVLink, so the transfer overlaps the next tiles' math and no
+all-gather or re-layout pass remains).  Rank synchronisation goes through
+``torch.distributed`` (NCCL on GPUs).
 """
 from __future__ import annotations
 
@@ -78,3 +84,65 @@ def sharded_matmul(sw: ShardedWeight, x, out=None, group=None, path: str = "auto
     dist.all_gather_into_tensor(gathered, local.view(-1), group=group)
     pxq.gather_shards(gathered, G, M, Ns, out=out)
     return out
+
+
+class PeerOutput:
+    """Y [columns][rows] on every rank of the group, each rank's buffer mapped
+    into every other rank (CUDA IPC): the destinations of
+    ``pxq.matmul_scatter``.  Collective: every rank constructs and closes it
+    together."""
+
+    def __init__(self, columns: int, rows: int, group=None):
+        import torch
+        import torch.distributed as dist
+
+        from . import pxq
+
+        self.group = group
+        self.buf = pxq.IpcBuffer(columns, rows)
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        handles = [None] * world
+        dist.all_gather_object(handles, self.buf.handle, group=group)
+        self.peers, self.ptrs = [], []
+        for r, h in enumerate(handles):
+            if r == rank:
+                self.ptrs.append(self.buf.ptr)
+            else:
+                peer = pxq.IpcPeer(h)
+                self.peers.append(peer)
+                self.ptrs.append(peer.ptr)
+        self.tensor = self.buf.tensor
+        self._flag = torch.zeros(1, dtype=torch.float32, device=self.tensor.device)
+
+    def sync(self) -> None:
+        """Device-ordered barrier of the group (a one-element NCCL all-reduce)."""
+        import torch.distributed as dist
+
+        dist.all_reduce(self._flag, group=self.group)
+
+    def close(self) -> None:
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.synchronize()
+        for peer in self.peers:
+            peer.close()
+        self.peers = []
+        dist.barrier(group=self.group)  # every mapping of this buffer is closed before it is freed
+        self.tensor = None
+        self.buf.free()
+
+
+def sharded_matmul_p2p(sw: ShardedWeight, x, out: PeerOutput, sync_before: bool = True):
+    """Y[M][N] = X * W^T with W's rows split over the group, each rank's GEMM
+    writing its columns into every rank's ``out`` (M > 8: the GEMM path).
+    ``sync_before``: wait until every rank is done with the previous contents
+    of its Y before anyone overwrites it.  Returns this rank's Y (a view of
+    ``out``), complete once the call returns in stream order."""
+    from . import pxq
+
+    if sync_before:
+        out.sync()
+    pxq.matmul_scatter(sw.weight, x, out.ptrs, ldy=sw.rows, col_offset=sw.first)
+    out.sync()  # every rank's stores into this Y have landed
+    return out.tensor

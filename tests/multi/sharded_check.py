@@ -1,6 +1,7 @@
-"""Run under torchrun (one rank per GPU): the N-sharded matmul with NCCL
-all-gather must give Y bit-identical to the single-GPU matmul of the whole
-weight.  Exit status 0 on success; rank 0 prints one line."""
+"""Run under torchrun (one rank per GPU): the N-sharded matmul -- NCCL
+all-gather, and for the GEMM cases also the one-kernel P2P-store path -- must
+give Y bit-identical to the single-GPU matmul of the whole weight.  Exit
+status 0 on success; rank 0 prints one line per check."""
 import os
 import sys
 
@@ -29,6 +30,12 @@ def main() -> int:
             sw = sharded.ShardedWeight(w, wtype, inner, rows, world, rank)
             y = sharded.sharded_matmul(sw, x, path=path)
             torch.cuda.synchronize()
+            y2 = None
+            if path == "gemm":  # the one-kernel path: GEMM epilogue stores into every rank's Y
+                po = sharded.PeerOutput(columns, rows)
+                y2 = sharded.sharded_matmul_p2p(sw, x, po).clone()
+                torch.cuda.synchronize()
+                po.close()
             sw.release()
             if rank == 0:
                 W = pxq.Weight(w, wtype, inner, rows)
@@ -39,6 +46,11 @@ def main() -> int:
                 failures += 0 if same else 1
                 print(f"type {wtype} [{rows}x{inner}] M={columns} {path}: {'bit-identical' if same else 'DIFFERENT'}",
                       flush=True)
+                if y2 is not None:
+                    same = torch.equal(y2.view(torch.int32), ref.view(torch.int32))
+                    failures += 0 if same else 1
+                    print(f"type {wtype} [{rows}x{inner}] M={columns} gemm, P2P stores: "
+                          f"{'bit-identical' if same else 'DIFFERENT'}", flush=True)
         flag = torch.tensor([failures], device="cuda")
         dist.broadcast(flag, 0)
         failures = int(flag.item())

@@ -315,6 +315,34 @@ def test_host_drop_in_matches_reference_contract(pxq, oracle, golden):
     assert handled and max_abs_rel(y, ref) <= TOL
 
 
+@pytest.mark.parametrize("wtype", [Q8_0, Q5_K, Q6_K])
+def test_matmul_scatter_local_destinations(pxq, wtype):
+    """pxq_matmul_scatter writes each element to every destination at the
+    column offset (the N-sharded path's P2P-store GEMM, here with two buffers
+    on one GPU): both hold exactly the plain GEMM's output there, and nothing
+    outside the rank's columns is touched."""
+    import torch
+
+    rows, inner, M, total, off = 192, 1024, 40, 512, 128
+    w = synth.weights_for(wtype, rows, inner, seed=21)
+    x = cuda(synth.activations(M, inner, seed=22))
+    W = pxq.Weight(w, wtype, inner, rows)
+    ref = pxq.matmul(W, x, path="gemm")
+    dst = [torch.full((M, total), 7.0, device="cuda") for _ in range(2)]
+    pxq.matmul_scatter(W, x, [d.data_ptr() for d in dst], ldy=total, col_offset=off)
+    pxq.synchronize()
+    W.release()
+    for d in dst:
+        assert torch.equal(d[:, off:off + rows].contiguous().view(torch.int32), ref.view(torch.int32))
+        assert bool((d[:, :off] == 7.0).all()) and bool((d[:, off + rows:] == 7.0).all())
+    with pytest.raises(pxq.PxqError):  # the scatter runs on the GEMM path only
+        W2 = pxq.Weight(w, wtype, inner, rows)
+        try:
+            pxq.matmul_scatter(W2, x[:4], [dst[0].data_ptr()], ldy=total, col_offset=off)
+        finally:
+            W2.release()
+
+
 def test_gather_shards(pxq):
     import torch
 
