@@ -11,7 +11,7 @@
 // no device allocation.  (A rejected call records its message for
 // pxq_last_error() in host memory.)
 //
-// The array: g_noalloc_scratch, PXQ_NOALLOC_SCRATCH_BYTES (1 MiB) per device
+// The array: g_noalloc_scratch, PXQ_NOALLOC_SCRATCH_BYTES (4 MiB) per device
 // that loads the library, held until the process exits.  Host code never
 // touches it by name (its host-side symbol is not a device address): on the
 // first call on each device, with that device current, the address is looked
