@@ -608,6 +608,7 @@ namespace {
 // per-thread stream for the host-buffer entry point (the reference's session
 // is thread-local too, src/backend_vulkan.cpp:86)
 thread_local cudaStream_t t_stream = nullptr;
+thread_local cudaStream_t t_up = nullptr, t_down = nullptr;  // host-buffer path: uploads, downloads
 thread_local int t_stream_device = -1;
 
 }  // namespace
@@ -1139,6 +1140,8 @@ int pxq_matmul_host(pxq_weight* w, size_t row_first, size_t row_count, const flo
     if (int rc = check_matmul_args(w, row_first, row_count, input, columns, output, ldy)) return rc;
     if (!t_stream || t_stream_device != t_device) {
         PXQ_CUDA(cudaStreamCreateWithFlags(&t_stream, cudaStreamNonBlocking));
+        PXQ_CUDA(cudaStreamCreateWithFlags(&t_up, cudaStreamNonBlocking));
+        PXQ_CUDA(cudaStreamCreateWithFlags(&t_down, cudaStreamNonBlocking));
         t_stream_device = t_device;
     }
     cudaStream_t s = t_stream;
@@ -1152,21 +1155,61 @@ int pxq_matmul_host(pxq_weight* w, size_t row_first, size_t row_count, const flo
         if (xin) cudaFreeAsync(xin, s);
         return fail(PXQ_ERR_NO_MEMORY, "cannot allocate device buffers");
     }
+    // Chunks of activation rows (GEMM path only): chunk i's upload, chunk
+    // i-1's quantize + GEMM and chunk i-2's download run at the same time (the
+    // link is full duplex).  Activation rows are quantized independently and
+    // every output element depends on its own row only, so the result is the
+    // same bit for bit as one call over all rows.
+    const size_t chunk = columns > 8 ? std::max<size_t>(512, (columns + 7) / 8) : columns;
+    const size_t nchunks = (columns + chunk - 1) / chunk;
     int rc = PXQ_OK;
-    cudaError_t e = cudaMemcpyAsync(xin, input, xbytes, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) {
-        // keep caller-owned output elements between rows (ldy > row_count) intact
-        if (ldy != row_count && columns > 1) e = cudaMemcpyAsync(yout, output, ybytes, cudaMemcpyHostToDevice, s);
+    cudaError_t e = cudaSuccess;
+    cudaEvent_t ready = nullptr;  // buffers allocated on s (and the caller's output rows uploaded)
+    e = cudaEventCreateWithFlags(&ready, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventRecord(ready, s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(t_up, ready, 0);
+    // keep caller-owned output elements between rows (ldy > row_count) intact
+    if (e == cudaSuccess && ldy != row_count && columns > 1) e = cudaMemcpyAsync(yout, output, ybytes, cudaMemcpyHostToDevice, t_up);
+    std::vector<cudaEvent_t> evs;
+    for (size_t i = 0; i < nchunks && e == cudaSuccess && !rc; i++) {
+        const size_t c0 = i * chunk, cn = std::min(chunk, columns - c0);
+        cudaEvent_t up = nullptr, done = nullptr;
+        if ((e = cudaEventCreateWithFlags(&up, cudaEventDisableTiming)) != cudaSuccess) break;
+        evs.push_back(up);
+        if ((e = cudaEventCreateWithFlags(&done, cudaEventDisableTiming)) != cudaSuccess) break;
+        evs.push_back(done);
+        e = cudaMemcpyAsync(xin + c0 * inner, input + c0 * inner, cn * inner * sizeof(float), cudaMemcpyHostToDevice, t_up);
+        if (e == cudaSuccess) e = cudaEventRecord(up, t_up);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(s, up, 0);
+        if (e != cudaSuccess) break;
+        rc = run_matmul(d, w, row_first, row_count, xin + c0 * inner, cn, yout + c0 * ldy, ldy, nullptr, nullptr, 0, s);
+        if (rc) break;
+        e = cudaEventRecord(done, s);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(t_down, done, 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(output + c0 * ldy, yout + c0 * ldy, ((cn - 1) * ldy + row_count) * sizeof(float),
+                                cudaMemcpyDeviceToHost, t_down);
     }
-    if (e == cudaSuccess) {
-        rc = run_matmul(d, w, row_first, row_count, xin, columns, yout, ldy, nullptr, nullptr, 0, s);
-        if (!rc) e = cudaMemcpyAsync(output, yout, ybytes, cudaMemcpyDeviceToHost, s);
+    // the buffers are freed on s once every copy on the two copy streams is done
+    cudaEvent_t fin_up = nullptr, fin_down = nullptr;
+    if (cudaEventCreateWithFlags(&fin_up, cudaEventDisableTiming) == cudaSuccess) {
+        cudaEventRecord(fin_up, t_up);
+        cudaStreamWaitEvent(s, fin_up, 0);
+    }
+    if (cudaEventCreateWithFlags(&fin_down, cudaEventDisableTiming) == cudaSuccess) {
+        cudaEventRecord(fin_down, t_down);
+        cudaStreamWaitEvent(s, fin_down, 0);
     }
     cudaFreeAsync(xin, s);
     cudaFreeAsync(yout, s);
+    const int sync_rc = pxq_synchronize(s);
+    for (cudaEvent_t ev : evs) cudaEventDestroy(ev);
+    if (ready) cudaEventDestroy(ready);
+    if (fin_up) cudaEventDestroy(fin_up);
+    if (fin_down) cudaEventDestroy(fin_down);
     if (e != cudaSuccess) return fail(PXQ_ERR_CUDA, "copy failed: %s", cudaGetErrorString(e));
     if (rc) return rc;
-    return pxq_synchronize(s);
+    return sync_rc;
 }
 
 int pxq_quant_matmul(const unsigned char* weights, uint32_t type, const float* input, float* output, size_t rows,

@@ -343,6 +343,31 @@ def test_matmul_scatter_local_destinations(pxq, wtype):
             W2.release()
 
 
+@pytest.mark.parametrize("wtype", [Q8_0, Q5_K])
+def test_host_matmul_chunked_pipeline(pxq, oracle, wtype):
+    """Host-buffer calls with many activation rows run as chunks whose
+    uploads, GEMMs and downloads overlap: the result is the one-shot result
+    (each output element depends on its own activation row only), and with
+    ldy > rows the caller's elements between output rows are left as they were."""
+    import ctypes as C
+
+    rows, inner, M = 96, 512, 1300  # chunks of 512, 512, 276
+    w = synth.weights_for(wtype, rows, inner, seed=41)
+    x = synth.activations(M, inner, seed=42)
+    ok, ref = oracle.quant_matmul(w, wtype, x, rows)
+    assert ok
+    handled, y = pxq.quant_matmul(w, wtype, x, rows)
+    assert handled and max_abs_rel(y, ref) <= TOL
+    W = pxq.Weight(w, wtype, inner, rows)
+    ldy = rows + 5
+    out = np.full((M, ldy), -3.0, dtype=np.float32)
+    rc = pxq.load().pxq_matmul_host(W.handle, 0, rows, x.ctypes.data_as(C.c_void_p), M, out.ctypes.data_as(C.c_void_p), ldy)
+    W.release()
+    assert rc == pxq.OK
+    assert np.array_equal(out[:, :rows].view(np.uint32), y.view(np.uint32))
+    assert bool((out[:, rows:] == -3.0).all())
+
+
 def test_gather_shards(pxq):
     import torch
 
