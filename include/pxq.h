@@ -183,9 +183,10 @@ PXQ_API int pxq_gather_shards(const float* src, size_t shards, size_t columns, s
 /* The N-sharded multi-GPU matmul in one kernel: this rank's weight rows
  * [row_first, row_first + row_count) times `input` (columns > 8: the GEMM
  * path), with element (m, n) stored into dsts[k][m * ldy + col_offset + n]
- * for every k < ndst -- this GPU's output and the other ranks' outputs
- * (device pointers opened with pxq_ipc_open), written by the GEMM epilogue
- * over NVLink while the next tiles compute.  Replaces the matmul, the
+ * for every k < ndst: dsts[0] is this GPU's own output (written like any
+ * output), dsts[1..] the other ranks' outputs (device pointers opened with
+ * pxq_ipc_open), written by the GEMM epilogue over NVLink from the same
+ * staged tiles while the next tiles compute.  Replaces the matmul, the
  * all-gather and pxq_gather_shards of the N-sharded path (each rank holding
  * weight rows of cpu_quant_matmul's independent output columns,
  * src/kernels_quant.cpp:390-398).  The caller orders the ranks around the

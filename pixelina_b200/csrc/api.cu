@@ -500,7 +500,7 @@ int run_gemm(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, co
     // innermost dimension only at 16-byte granularity)
     op.tma_store = 0;
     op.tm_y = op.tm[0];
-    if (!dump && !w->gated && !ndst && gemm_store_rows(w->type) > 0 && (reinterpret_cast<uintptr_t>(output) & 15u) == 0 &&
+    if (!dump && !w->gated && gemm_store_rows(w->type) > 0 && (reinterpret_cast<uintptr_t>(output) & 15u) == 0 &&
         (ldy % 4) == 0 && (row_count % 4) == 0) {
         if (make_map(d, &op.tm_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, output, row_count, (uint64_t)a->M, ldy * 4, 32,
                      (uint32_t)gemm_store_rows(w->type),
@@ -898,7 +898,10 @@ int pxq_matmul_scatter(pxq_weight* w, size_t row_first, size_t row_count, const 
     pxq_activation* a = nullptr;
     int rc = quantize_activation(d, w->type, input, (int64_t)columns, w->inner, 2, &a, s);
     if (rc) return rc;
-    rc = run_gemm(d, w, row_first, row_count, a, nullptr, ldy, nullptr, nullptr, s, dsts, (int)ndst, (int64_t)col_offset);
+    // dsts[0]: this GPU's output, written like any output (TMA-store epilogue where aligned);
+    // dsts[1..]: the peers', written from the same staged tiles
+    rc = run_gemm(d, w, row_first, row_count, a, dsts[0] + col_offset, ldy, nullptr, nullptr, s, dsts + 1, (int)ndst - 1,
+                  (int64_t)col_offset);
     free_activation(a, s);
     return rc;
 }

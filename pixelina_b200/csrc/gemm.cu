@@ -165,19 +165,16 @@ struct Params {
     uint32_t* status;
     int tma_store;  // 1: epilogue through shared memory + TMA store (tmY)
     int gated;      // 1: gated weight, y = silu(gate) * up over N/2 outputs (direct stores)
-    int ndst;       // > 0: scatter, element (m, n) to ydst[k][m * ldy + col_off + n], k < ndst (direct stores)
+    int ndst;       // scatter: also store element (m, n) at ydst[k][m * ldy + col_off + n], k < ndst
     int64_t col_off;
     float* ydst[kMaxScatter];
 };
 
-// One output element: this GPU's y, or every destination of a scatter (its own
-// buffer and the peers', written straight over NVLink).
+// One output element: this GPU's y and, for a scatter, the same element in
+// every peer's buffer (plain stores over NVLink).
 __device__ __forceinline__ void put_y(const Params& p, int64_t m, int64_t n, float v)
 {
-    if (p.ndst == 0) {
-        p.y[m * p.ldy + n] = v;
-        return;
-    }
+    p.y[m * p.ldy + n] = v;
     const int64_t off = m * p.ldy + p.col_off + n;
     for (int k = 0; k < p.ndst; k++) p.ydst[k][off] = v;
 }
@@ -754,6 +751,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                         if (lane == 0) {
                             tma_store_2d(&tmY, stg, (int32_t)(n0 + quad * 32), (int32_t)(mfirst + SR * r));
                             bulk_commit();
+                        }
+                        if (p.ndst) {
+                            // the peers' copies from the same staged block: row j, column
+                            // lane -- 32 lanes store 128 contiguous bytes of a peer's row
+                            const int64_t nn = n0 + quad * 32 + lane;
+                            if (nn < p.N) {
+                                for (int j = 0; j < SR; j++) {
+                                    const int64_t m = mfirst + SR * r + j;
+                                    if (m >= p.M) break;
+                                    const float v = stg[j * 32 + lane];
+                                    const int64_t off = m * p.ldy + p.col_off + nn;
+                                    for (int k = 0; k < p.ndst; k++) p.ydst[k][off] = v;
+                                }
+                            }
                         }
                     }
                 } else if (SPLIT) {

@@ -176,8 +176,8 @@ struct GemmOperands {
     float* dump;          // debug: raw per-item block dots, or null
     int gated;            // gated weight (2F interleaved rows, N = 2F): y[m][n < F] = silu(gate) * up
     uint32_t* status;     // device status word
-    // scatter (ndst > 0, no TMA store): element (m, n) goes to ydst[k][m * ldy + col_off + n] for
-    // every k < ndst -- this GPU's buffer and peers' buffers (P2P stores over NVLink)
+    // scatter (ndst > 0): element (m, n), besides y[m * ldy + n], also goes to
+    // ydst[k][m * ldy + col_off + n] for every k < ndst -- peers' buffers (P2P stores over NVLink)
     float* ydst[kMaxScatter];
     int ndst;
     int64_t col_off;

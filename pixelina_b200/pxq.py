@@ -490,7 +490,8 @@ class _CudaArray:
 def matmul_scatter(W: "Weight", x, dst_ptrs, ldy: int, col_offset: int, row_first: int = 0, row_count=None, stream=None):
     """pxq_matmul_scatter: rows [row_first, row_first + row_count) of W times
     x (device fp32 [M][K], M > 8), every element written to each pointer of
-    ``dst_ptrs`` at [m][col_offset + n] with row stride ``ldy``."""
+    ``dst_ptrs`` at [m][col_offset + n] with row stride ``ldy``; dst_ptrs[0]
+    is this GPU's own buffer, the rest the other ranks' (pxq_ipc_open)."""
     x = x.contiguous()
     row_count = W.rows - row_first if row_count is None else row_count
     arr = (C.c_void_p * len(dst_ptrs))(*[C.c_void_p(p) for p in dst_ptrs])

@@ -103,11 +103,10 @@ class PeerOutput:
         world, rank = dist.get_world_size(group), dist.get_rank(group)
         handles = [None] * world
         dist.all_gather_object(handles, self.buf.handle, group=group)
-        self.peers, self.ptrs = [], []
+        self.peers = []
+        self.ptrs = [self.buf.ptr]  # this rank's buffer first, then the others' (the scatter's order)
         for r, h in enumerate(handles):
-            if r == rank:
-                self.ptrs.append(self.buf.ptr)
-            else:
+            if r != rank:
                 peer = pxq.IpcPeer(h)
                 self.peers.append(peer)
                 self.ptrs.append(peer.ptr)
