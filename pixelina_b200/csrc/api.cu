@@ -487,7 +487,11 @@ int run_gemm(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, co
     op.gated = w->gated ? 1 : 0;
     op.ndst = ndst;
     op.col_off = col_off;
-    for (int k = 0; k < ndst; k++) op.ydst[k] = dsts[k];
+    op.dst_vec4 = ldy % 4 == 0 ? 1 : 0;
+    for (int k = 0; k < ndst; k++) {
+        op.ydst[k] = dsts[k];
+        if ((reinterpret_cast<uintptr_t>(dsts[k] + col_off) & 15u) != 0) op.dst_vec4 = 0;
+    }
     op.tm[0] = pk->tmW;
     op.tm[1] = a->tmX;
     op.tm[2] = pk->tmWs;

@@ -166,6 +166,7 @@ struct Params {
     int tma_store;  // 1: epilogue through shared memory + TMA store (tmY)
     int gated;      // 1: gated weight, y = silu(gate) * up over N/2 outputs (direct stores)
     int ndst;       // scatter: also store element (m, n) at ydst[k][m * ldy + col_off + n], k < ndst
+    int dst_vec4;   // scatter: every ydst[k] + col_off 16-byte aligned and ldy % 4 == 0 (4-float stores)
     int64_t col_off;
     float* ydst[kMaxScatter];
 };
@@ -752,9 +753,26 @@ __global__ void __launch_bounds__(THREADS, 1)
                             tma_store_2d(&tmY, stg, (int32_t)(n0 + quad * 32), (int32_t)(mfirst + SR * r));
                             bulk_commit();
                         }
-                        if (p.ndst) {
-                            // the peers' copies from the same staged block: row j, column
-                            // lane -- 32 lanes store 128 contiguous bytes of a peer's row
+                        if (p.ndst && p.dst_vec4) {
+                            // the peers' copies from the same staged block, 4 floats a lane:
+                            // 8 lanes store one row's 128 contiguous bytes, a warp 4 rows
+                            const int jr = lane >> 3, c4 = 4 * (lane & 7);
+                            const int64_t nn = n0 + quad * 32 + c4;
+                            for (int j = jr; j < SR; j += 4) {
+                                const int64_t m = mfirst + SR * r + j;
+                                if (m >= p.M) break;
+                                const float4 v = *reinterpret_cast<const float4*>(stg + j * 32 + c4);
+                                const int64_t off = m * p.ldy + p.col_off + nn;
+                                if (nn + 3 < p.N) {
+                                    for (int k = 0; k < p.ndst; k++) *reinterpret_cast<float4*>(p.ydst[k] + off) = v;
+                                } else {
+                                    const float vs[4] = {v.x, v.y, v.z, v.w};
+                                    for (int q = 0; q < 4 && nn + q < p.N; q++)
+                                        for (int k = 0; k < p.ndst; k++) p.ydst[k][off + q] = vs[q];
+                                }
+                            }
+                        } else if (p.ndst) {
+                            // the same, one float a lane: 32 lanes store 128 contiguous bytes
                             const int64_t nn = n0 + quad * 32 + lane;
                             if (nn < p.N) {
                                 for (int j = 0; j < SR; j++) {
@@ -853,7 +871,7 @@ cudaError_t launch_typed(const GemmOperands& op, int num_sms, cudaStream_t s)
     if (groups < 1) groups = 1;
     cfg.gridDim = dim3((unsigned)(CG * groups));
     Params p{op.M, op.N, op.K, op.n_first, op.y, op.ldy, op.bias, op.dump, op.status, (op.tma_store && !DUMP) ? 1 : 0, op.gated,
-             op.ndst, op.col_off, {}};
+             op.ndst, op.dst_vec4, op.col_off, {}};
     for (int k = 0; k < kMaxScatter; k++) p.ydst[k] = op.ydst[k];
     return cudaLaunchKernelEx(&cfg, kern, op.tm[0], op.tm[1], op.tm[2], op.tm[3], op.tm[4], op.tm[5], op.tm[6], op.tm_y, p);
 }

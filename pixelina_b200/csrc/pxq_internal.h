@@ -180,6 +180,7 @@ struct GemmOperands {
     // ydst[k][m * ldy + col_off + n] for every k < ndst -- peers' buffers (P2P stores over NVLink)
     float* ydst[kMaxScatter];
     int ndst;
+    int dst_vec4;         // every ydst[k] + col_off 16-byte aligned and ldy % 4 == 0
     int64_t col_off;
 };
 // Rows of one CTA's activation box in the GEMM's tensor maps (tmX, tmXs),

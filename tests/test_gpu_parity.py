@@ -315,15 +315,16 @@ def test_host_drop_in_matches_reference_contract(pxq, oracle, golden):
     assert handled and max_abs_rel(y, ref) <= TOL
 
 
+@pytest.mark.parametrize("off", [128, 129])  # 16-byte aligned (4-float peer stores, TMA-store local copy) or not
 @pytest.mark.parametrize("wtype", [Q8_0, Q5_K, Q6_K])
-def test_matmul_scatter_local_destinations(pxq, wtype):
+def test_matmul_scatter_local_destinations(pxq, wtype, off):
     """pxq_matmul_scatter writes each element to every destination at the
     column offset (the N-sharded path's P2P-store GEMM, here with two buffers
     on one GPU): both hold exactly the plain GEMM's output there, and nothing
     outside the rank's columns is touched."""
     import torch
 
-    rows, inner, M, total, off = 192, 1024, 40, 512, 128
+    rows, inner, M, total = 192, 1024, 40, 512
     w = synth.weights_for(wtype, rows, inner, seed=21)
     x = cuda(synth.activations(M, inner, seed=22))
     W = pxq.Weight(w, wtype, inner, rows)
