@@ -1167,8 +1167,11 @@ int pxq_matmul_host(pxq_weight* w, size_t row_first, size_t row_count, const flo
     // link is full duplex).  Activation rows are quantized independently and
     // every output element depends on its own row only, so the result is the
     // same bit for bit as one call over all rows.
+    // The first chunk is short (128 rows), so the downloads -- the longest
+    // stream of a large call -- start as early as possible.
     const size_t chunk = columns > 8 ? std::max<size_t>(512, (columns + 7) / 8) : columns;
-    const size_t nchunks = (columns + chunk - 1) / chunk;
+    const size_t first = columns > 1024 ? 128 : chunk;
+    const size_t nchunks = columns <= first ? 1 : 1 + (columns - first + chunk - 1) / chunk;
     int rc = PXQ_OK;
     cudaError_t e = cudaSuccess;
     cudaEvent_t ready = nullptr;  // buffers allocated on s (and the caller's output rows uploaded)
@@ -1179,7 +1182,8 @@ int pxq_matmul_host(pxq_weight* w, size_t row_first, size_t row_count, const flo
     if (e == cudaSuccess && ldy != row_count && columns > 1) e = cudaMemcpyAsync(yout, output, ybytes, cudaMemcpyHostToDevice, t_up);
     std::vector<cudaEvent_t> evs;
     for (size_t i = 0; i < nchunks && e == cudaSuccess && !rc; i++) {
-        const size_t c0 = i * chunk, cn = std::min(chunk, columns - c0);
+        const size_t c0 = i == 0 ? 0 : first + (i - 1) * chunk;
+        const size_t cn = std::min(i == 0 ? first : chunk, columns - c0);
         cudaEvent_t up = nullptr, done = nullptr;
         if ((e = cudaEventCreateWithFlags(&up, cudaEventDisableTiming)) != cudaSuccess) break;
         evs.push_back(up);
