@@ -1,20 +1,29 @@
 #!/usr/bin/env python
 """Benchmark of the quantized-matmul hot path.
 
-Default workload: Q5_K GEMM, activations M=4096 x K=3840
-fp32 N(0,1), weights N=10240 x K=3840 Q5_K encoded from N(0, 0.02) floats.
-One step = activation quantize (Q8_K, as the reference's CPU path) + the
-tensor-core GEMM, inputs resident in HBM; L2 is flushed (256 MB write)
-between timed steps, outside the timed events.
+Default workload: the large-image Q8_0 GEMM, activations
+M=16384 x K=3072 fp32 N(0,1), weights N=12288 x K=3072 Q8_0 encoded from
+N(0, 0.02) floats.  One step = the activation quantize + the tensor-core
+GEMM, inputs resident in HBM; L2 is flushed (256 MB write) between timed
+steps, outside the timed events.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload q5k_gemm|q8_0_gemm|q8_0_large|q6k_gemm|dit|decode|decode_gated|decode_shapes|attention|sharded]
+                    [--workload q8_0_large|q8_0_gemm|q5k_gemm|q6k_gemm|dit|decode|decode_gated|decode_shapes|attention]
 
-Multi-GPU (torchrun, one rank per GPU): each rank processes its own batch of
-activation rows against the same weights (data parallel over independent
-rows, no collective on the data path, "scaling": "weak"); the job time is the
-max over ranks of the device-timed steps.  The N-sharded GEMM with an NCCL
-all-gather of Y is `--workload sharded` (reported separately).
+Multi-GPU (torchrun, one rank per GPU): the same whole problem N-sharded by
+output column (weight rows) over the ranks -- rank r holds weight rows
+[r*N/G, (r+1)*N/G) -- through libpxq's communicator (NCCL inside libpxq):
+one step = every rank quantizes the replicated activation, its GEMM
+epilogue stores its columns into every rank's Y over NVLink, with a device
+barrier before and after, so every rank ends with the full Y ("scaling":
+"strong"; value = whole-problem ops / max over ranks of the step time).  The
+NCCL all-gather + re-layout variant is reported beside it.
+
+At N=1 the line also carries the other BASELINE figures ("extras"): the
+Q5_K GEMM, the Q8_0 GEMM, the Q5_K decode matvec
+(configs[3], ms per token and HBM fraction at M=1/4/8) and the activation
+quantize kernels (HBM GB/s), and a parity figure: the whole timed output
+against the reference's own cpu_quant_matmul (the cpu_baseline run).
 
 `--impl reference` times Pixelina's own CPU cpu_quant_matmul (built from the
 reference sources into oracle/_ref) on the host cores, same metric/config.
@@ -105,6 +114,10 @@ class ClockSampler:
             return
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
+        # the sampler is running before the caller's timed region starts
+        t0 = time.perf_counter()
+        while not self.lines and time.perf_counter() - t0 < 3.0:
+            time.sleep(0.02)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -361,8 +374,12 @@ def run_gemm_workload(args, dist: Dist, wl: dict):
     # end to end through the host-buffer C-ABI drop-in (cpu_quant_matmul)
     result["e2e"] = e2e_host(args, dist, wbytes, wtype, x_host, N, ops)
     if dist.world == 1 and dist.rank == 0 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(wbytes, wtype, x_host, N, ops)
+        # the reference on a bounded sample of weight rows; its outputs check the timed Y
+        result["cpu_baseline"], result["parity"] = cpu_baseline(wbytes, wtype, x_host, N, ops, y_dev=y)
     W.release()
+    del y
+    if dist.world == 1 and not args.no_extras:
+        result["extras"] = run_extras(args, dist)
     return result
 
 
@@ -405,11 +422,16 @@ def cpu_library():
     return None, None
 
 
-def cpu_baseline(wbytes, wtype, x_host, rows, ops, target_s: float = 12.0):
-    """Reference CPU cpu_quant_matmul on the host cores, bounded sample."""
+def cpu_baseline(wbytes, wtype, x_host, rows, ops, target_s: float = 12.0, y_dev=None):
+    """Reference CPU cpu_quant_matmul on the host cores, bounded sample: a set
+    of weight rows spread over every output tile, against all activation
+    rows.  With y_dev (the GPU's output of the timed steps) the reference's
+    outputs for those rows are also the parity check: returns (baseline,
+    parity) then."""
     lib, kind = cpu_library()
     if lib is None:
-        return {"value": None, "unit": "TOPS", "cores": 0, "kind": "unavailable", "sample": "no CPU library built"}
+        none = {"value": None, "unit": "TOPS", "cores": 0, "kind": "unavailable", "sample": "no CPU library built"}
+        return (none, None) if y_dev is not None else none
     cores = os.cpu_count() or 1
     if kind == "reference":
         lib.set_threads(cores)
@@ -423,17 +445,29 @@ def cpu_baseline(wbytes, wtype, x_host, rows, ops, target_s: float = 12.0):
     sample_rows = int(min(rows, max(16, target_s / 3 / max(per_row, 1e-9))))
     sample_rows -= sample_rows % 16 or 0
     sample_rows = max(16, sample_rows)
-    times = []
+    # rows spread evenly over the whole weight, so every output tile is sampled
+    idx = np.unique(np.linspace(0, rows - 1, sample_rows).round().astype(np.int64))
+    wsample = np.ascontiguousarray(wbytes[idx])
+    times, ref = [], None
     for _ in range(3):
         t0 = time.perf_counter()
-        ok, _ = lib.quant_matmul(wbytes[:sample_rows], wtype, x_host, sample_rows)
+        ok, ref = lib.quant_matmul(wsample, wtype, x_host, len(idx))
         times.append(time.perf_counter() - t0)
         assert ok
     t = statistics.median(times)
-    sample_ops = ops * sample_rows / rows
-    return {"value": round(sample_ops / t / 1e12, 5), "unit": "TOPS", "cores": cores if kind == "reference" else 1,
-            "kind": kind, "sample": f"{M}x{K} activations against the first {sample_rows} of {rows} weight rows, "
-                                    f"incl. quantize; median of 3 ({t:.2f} s each)"}
+    sample_ops = ops * len(idx) / rows
+    base = {"value": round(sample_ops / t / 1e12, 5), "unit": "TOPS", "cores": cores if kind == "reference" else 1,
+            "kind": kind, "sample": f"{M}x{K} activations against {len(idx)} of {rows} weight rows spread over all output "
+                                    f"tiles, incl. quantize; median of 3 ({t:.2f} s each)"}
+    if y_dev is None:
+        return base
+    import torch
+
+    got = y_dev[:, torch.from_numpy(idx).to(y_dev.device)].cpu().numpy().astype(np.float64)
+    err = float(np.abs(got - ref).max()) / max(float(np.abs(ref).max()), 1e-30)
+    parity = {"max_abs_rel": err, "tolerance": 1e-3, "ok": err <= 1e-3, "against": f"{kind} cpu_quant_matmul",
+              "elements_checked": int(got.size), "of_elements": int(M * rows)}
+    return base, parity
 
 
 # -------------------------------------------------------- reference arm ---
@@ -441,7 +475,7 @@ def cpu_baseline(wbytes, wtype, x_host, rows, ops, target_s: float = 12.0):
 def run_reference(args, dist: Dist):
     from pixelina_b200 import synth
 
-    wl = GEMM_WORKLOADS.get(args.workload, GEMM_WORKLOADS["q5k_gemm"])
+    wl = GEMM_WORKLOADS.get(args.workload, GEMM_WORKLOADS["q8_0_large"])
     M, N, K, wtype = wl["M"], wl["N"], wl["K"], wl["wtype"]
     lib, kind = cpu_library()
     if lib is None:
@@ -754,76 +788,207 @@ def attention_cpu_baseline(c, q, k, v, target_s: float = 6.0):
             "sample": f"first {rows} of {c['rows']} query rows against all {c['keys']} keys; median of 3 ({t:.2f} s each)"}
 
 
-def run_sharded(args, dist: Dist):
-    """BASELINE configs[4] N-sharded across ranks: rank r computes weight rows
-    [r*N/G, (r+1)*N/G) for all M activation rows, then an NCCL all-gather of
-    the shards and one re-layout to row-major [M][N]."""
+def run_gemm_sharded(args, dist: Dist, wl: dict):
+    """The whole GEMM problem N-sharded over the ranks through libpxq's
+    communicator (pxq_comm / pxq_sharded_matmul): rank r holds weight rows
+    [r*N/G, (r+1)*N/G); one step = activation quantize + the GEMM whose
+    epilogue stores every rank's columns into every rank's Y over NVLink,
+    between device barriers.  value = 2*M*N*K / max over ranks of the step
+    time (strong scaling)."""
     import torch
-    import torch.distributed as tdist
 
-    from pixelina_b200 import pxq, sharded
+    from pixelina_b200 import pxq, sharded, synth
 
-    wl = GEMM_WORKLOADS["q8_0_large"]
-    M, N, K = wl["M"], wl["N"], wl["K"]
-    G, r = dist.world, dist.rank
     pxq.init(dist.local)
-    gen = torch.Generator(device="cuda")
-    gen.manual_seed(5)
-    full = gpu_random_q8_0(N, K, gen)  # same seed on every rank -> same weights
-    sw = sharded.ShardedWeight(full, Q8_0, K, N, G, r)
-    Ns = sw.count
-    del full
-    x = torch.randn((M, K), device="cuda", generator=gen)
-    scratch = (torch.empty((M, Ns), device="cuda"), torch.empty((G * M * Ns,), device="cuda"))
-    y = torch.empty((M, N), device="cuda")
+    M, N, K, wtype = wl["M"], wl["N"], wl["K"], wl["wtype"]
+    G, r = dist.world, dist.rank
+    comm = sharded.Comm(G, r, timeout_ms=120000)
+    wbytes = synth.weights_for(wtype, N, K, seed=1)  # the same bytes on every rank
+    sw = sharded.ShardedWeight(wbytes, wtype, K, N, G, r)
+    x_host = synth.activations(M, K, seed=100)       # replicated activation
+    x = torch.from_numpy(x_host).cuda()
+    out = sharded.ShardedOutput(comm, M, N)
+    flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     ops = 2.0 * M * N * K
 
     def step(ev):
         if ev is not None:
             ev["start"], ev["end"] = ev_pair()
-            g0, g1 = ev_pair()
-            ev["kernels"] = {"gemm": (ev["start"], g1)}
             ev["start"].record()
-        pxq.matmul(sw.weight, x, out=scratch[0], path="gemm")
-        if ev is not None:
-            g1.record()
-        if G > 1:
-            tdist.all_gather_into_tensor(scratch[1], scratch[0].view(-1))
-            pxq.gather_shards(scratch[1], G, M, Ns, out=y)
+        sharded.sharded_matmul(comm, sw, x, out=out)
         if ev is not None:
             ev["end"].record()
 
-    flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
-    step_ms, kernel_ms, clocks = time_steps(step, args.steps, args.warmup, flush_buf.zero_, args.soak,
-                                            ClockSampler(dist.local), dist)
+    launches0 = pxq.kernel_launches()
+    step_ms, _, clocks = time_steps(step, args.steps, args.warmup, flush_buf.zero_, args.soak, ClockSampler(dist.local), dist)
+    comm.synchronize()
+    launches = pxq.kernel_launches() - launches0
     ms = dist.max(statistics.mean(step_ms))
-    gemm_ms = dist.max(statistics.mean(kernel_ms["gemm"]))
-    del scratch
-    out = {"metric": METRIC, "workload": "sharded: Q8_0 M=16384 N=12288 K=3072 N-sharded (configs[4])",
-           "unit": "TOPS", "n_gpus": G, "value_with_gather": round(ops / (ms * 1e-3) / 1e12, 2),
-           "value_gemm_only": round(ops / (gemm_ms * 1e-3) / 1e12, 2), "ms_per_step": round(ms, 3),
-           "gemm_ms": round(gemm_ms, 3), "gather_bytes_per_rank": (G - 1) * M * Ns * 4, "clocks": clocks,
-           "scaling": "strong"}
-    if G > 1:
-        # the one-kernel path: each rank's GEMM epilogue stores its columns into
-        # every rank's Y over NVLink (CUDA IPC mappings), a device barrier before
-        # (Y free) and after (all stores landed) -- no all-gather, no re-layout
-        del y
-        po = sharded.PeerOutput(M, N)
+    value = ops / (ms * 1e-3) / 1e12
+    # this rank's GEMM kernel alone, for the roofline (no collective)
+    a = pxq.Activation(wtype, x)
+    ylocal = torch.empty((M, sw.count), device="cuda")
+    pxq.matmul_quantized(sw.weight, a, out=ylocal)
+    torch.cuda.synchronize()
+    g0, g1 = ev_pair()
+    g0.record()
+    for _ in range(5):
+        pxq.matmul_quantized(sw.weight, a, out=ylocal)
+    g1.record()
+    torch.cuda.synchronize()
+    gemm_ms = dist.max(g0.elapsed_time(g1) / 5)
+    a.release()
+    del ylocal
+    # the NCCL all-gather + re-layout variant
+    y_ag = torch.empty((M, N), device="cuda")
 
-        def step_p2p(ev):
+    def step_ag(ev):
+        if ev is not None:
+            ev["start"], ev["end"] = ev_pair()
+            ev["start"].record()
+        sharded.sharded_matmul(comm, sw, x, out=y_ag)
+        if ev is not None:
+            ev["end"].record()
+
+    ag_ms, _, ag_clocks = time_steps(step_ag, args.steps, args.warmup, flush_buf.zero_, 1.0, ClockSampler(dist.local), dist)
+    comm.synchronize()
+    ag = dist.max(statistics.mean(ag_ms))
+    same = bool(torch.equal(y_ag.view(torch.int32), out.tensor.view(torch.int32)))
+    del y_ag
+    # end to end: host buffers in and out through pxq_sharded_matmul_host
+    xin = torch.from_numpy(x_host).pin_memory()
+    yout = torch.empty((M, N), dtype=torch.float32).pin_memory()
+    call = lambda: sharded.sharded_matmul_host_ptr(comm, sw, xin.data_ptr(), M, K, yout.data_ptr())  # noqa: E731
+    assert call() == 0, pxq.last_error()
+    n = max(3, min(args.steps, 10))
+    dist.barrier()
+    times = []
+    for _ in range(n):
+        t0 = time.perf_counter()
+        rc = call()
+        times.append(time.perf_counter() - t0)
+        assert rc == 0, pxq.last_error()
+    dist.barrier()
+    t = dist.max(statistics.mean(times))
+    hbm, bf16, _, peak_src = measured_peaks()
+    gemm_ops = 2.0 * M * sw.count * K
+    achieved = gemm_ops / (gemm_ms * 1e-3) / 1e12
+    result = {
+        "metric": METRIC, "value": round(value, 3), "unit": "TOPS", "n_gpus": G, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "i8xi8->f32",
+        "data": "synthetic (seeded N(0,1) activations; weights encoded from N(0,0.02))",
+        "config": {"workload": f"{args.workload}: {wl['name']}, N-sharded over {G} GPUs", "M": M, "N": N, "K": K,
+                   "weight_type": TYPE_NAMES[wtype], "activation_quant": "Q8_0" if wtype == Q8_0 else "Q8_K",
+                   "parallelism": f"N-sharded x{G} (rows {sw.count} per rank), Y assembled on every rank by the GEMM's "
+                                  "peer stores over NVLink",
+                   "l2": "flushed between timed steps (256 MB write, outside the events)"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": bf16, "unit": "TFLOP/s",
+                     "frac": round(achieved / bf16, 4), "peak_source": f"{peak_src} bf16 dense (burst)",
+                     "int8_peak_equiv": 2 * bf16, "int8_frac": round(achieved / (2 * bf16), 4),
+                     "kernel": "k_gemm_q8 (this rank's shard)", "kernel_ms": round(gemm_ms, 4),
+                     "traffic": None},
+        "exchange": {"bytes_per_rank": int((G - 1) * M * sw.count * 4), "link_GBps_per_rank":
+                     round((G - 1) * M * sw.count * 4 / (ms * 1e-3) / 1e9, 1),
+                     "gemm_only_TOPS_per_rank": round(achieved, 2)},
+        "allgather": {"value": round(ops / (ag * 1e-3) / 1e12, 3), "ms_per_step": round(ag, 4), "clocks": ag_clocks,
+                      "bit_identical_to_fused": same},
+        "clocks": clocks,
+        "gpu_launches": int(dist.sum(launches)),
+        "e2e": {"value": round(ops / t / 1e12, 3), "unit": "TOPS", "h2d_bytes_per_step": int(x_host.nbytes),
+                "d2h_bytes_per_step": int(M * N * 4), "ms_per_step": round(t * 1e3, 3),
+                "timing": "host wall clock around the synchronous C-ABI call on every rank (pinned host buffers; every "
+                          "rank uploads X and downloads the full Y), max over ranks",
+                "api": "pxq_sharded_matmul_host"},
+    }
+    out.close()
+    sw.release()
+    comm.close()
+    return result
+
+
+def run_extras(args, dist: Dist) -> dict:
+    """The other BASELINE figures at N=1, each timed with CUDA events on its
+    own: the Q5_K GEMM and Q8_0 GEMM with their
+    activation quantize, the Q5_K decode and the activation
+    quantize kernels (HBM-bound)."""
+    import torch
+
+    from pixelina_b200 import pxq
+
+    hbm, bf16, _, peak_src = measured_peaks()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(17)
+    flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    out = {"peak_source": peak_src}
+    for key, name in (("q5k_gemm_configs1", "q5k_gemm"), ("q8_0_gemm_configs0", "q8_0_gemm")):
+        wl = GEMM_WORKLOADS[name]
+        M, N, K, wtype = wl["M"], wl["N"], wl["K"], wl["wtype"]
+        make = gpu_random_q5_K if wtype == Q5_K else gpu_random_q8_0
+        W = pxq.Weight(make(N, K, gen), wtype, K, N)
+        x = torch.randn((M, K), device="cuda", generator=gen)
+        y = torch.empty((M, N), device="cuda")
+
+        def step(ev):
             if ev is not None:
                 ev["start"], ev["end"] = ev_pair()
+                g0, g1 = ev_pair()
+                ev["kernels"] = {"gemm": (g0, g1)}
                 ev["start"].record()
-            sharded.sharded_matmul_p2p(sw, x, po)
+            a = pxq.Activation(wtype, x)
             if ev is not None:
+                g0.record()
+            pxq.matmul_quantized(W, a, out=y)
+            if ev is not None:
+                g1.record()
                 ev["end"].record()
+            a.release()
 
-        p2p_ms, _, clocks2 = time_steps(step_p2p, args.steps, args.warmup, flush_buf.zero_, 0.0, ClockSampler(dist.local), dist)
-        ms2 = dist.max(statistics.mean(p2p_ms))
-        po.close()
-        out.update({"value_p2p": round(ops / (ms2 * 1e-3) / 1e12, 2), "ms_per_step_p2p": round(ms2, 3),
-                    "p2p_bytes_per_rank": (G - 1) * M * Ns * 4, "clocks_p2p": clocks2})
+        step_ms, kernel_ms, clocks = time_steps(step, args.steps, args.warmup, flush_buf.zero_, 0.5, ClockSampler(dist.local), dist)
+        ops = 2.0 * M * N * K
+        ms, gms = statistics.mean(step_ms), statistics.mean(kernel_ms["gemm"])
+        out[key] = {"M": M, "N": N, "K": K, "weights": TYPE_NAMES[wtype], "TOPS": round(ops / (ms * 1e-3) / 1e12, 2),
+                    "ms_per_step": round(ms, 4), "gemm_ms": round(gms, 4),
+                    "gemm_TFLOPs": round(ops / (gms * 1e-3) / 1e12, 2),
+                    "bf16_frac": round(ops / (gms * 1e-3) / 1e12 / bf16, 4),
+                    "int8_frac": round(ops / (gms * 1e-3) / 1e12 / (2 * bf16), 4), "sm_mhz": clocks["sm_mhz"],
+                    "reasons": clocks["reasons"]}
+        W.release()
+        del x, y
+    # activation quantize kernels, inputs larger than L2
+    for key, wtype, M, K, layout in (("quantize_q8_0_blocks", Q8_0, 16384, 3072, "gguf"),
+                                     ("quantize_q8_0_operand", Q8_0, 16384, 3072, "operand"),
+                                     ("quantize_q8_K_blocks", Q5_K, 16384, 3840, "gguf")):
+        x = torch.randn((M, K), device="cuda", generator=gen)
+        if layout == "gguf":
+            fn = (lambda: pxq.quantize_q8_0(x)) if wtype == Q8_0 else (lambda: pxq.quantize_q8_K(x))
+            wbytes = M * K // 32 * 34 if wtype == Q8_0 else M * K // 256 * 292
+        else:
+            def fn():
+                pxq.Activation(wtype, x).release()
+            wbytes = M * K * (1 if os.environ.get("PXQ_Q8_0_MMA", "i8") != "f16" else 2) + M * K // 32 * 4
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = ev_pair()
+        e0.record()
+        for _ in range(10):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / 10
+        nbytes = M * K * 4 + wbytes
+        out[key] = {"M": M, "K": K, "ms": round(ms, 4), "GBps": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                    "hbm_frac": round(nbytes / (ms * 1e-3) / 1e9 / hbm, 4), "bytes": int(nbytes),
+                    "timing": "10 back-to-back calls (each a quantize kernel; the GGUF-block calls include the output "
+                              "tensor's allocation from the caching allocator)"}
+        del x
+    # the decode matvec stack, gate/up as one gated call
+    dec = run_decode(args, dist, gated=True)
+    out["decode_configs3"] = {"weight_bytes_per_token": dec["weight_bytes_per_token"],
+                              **{m: {"ms_per_token": v["ms_per_token"], "weight_GBps": v["weight_GBps"],
+                                     "hbm_frac": v["hbm_frac"], "sm_mhz": v["clocks"]["sm_mhz"]}
+                                 for m, v in dec["results"].items()}}
     return out
 
 
@@ -833,10 +998,11 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="q5k_gemm",
-                    choices=sorted(GEMM_WORKLOADS) + ["attention", "decode", "decode_gated", "decode_shapes", "dit", "sharded"])
+    ap.add_argument("--workload", default="q8_0_large",
+                    choices=sorted(GEMM_WORKLOADS) + ["attention", "decode", "decode_gated", "decode_shapes", "dit"])
     ap.add_argument("--soak", type=float, default=1.5, help="seconds of untimed steps before timing (clock settling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="N=1: skip the other BASELINE figures")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     dist = Dist(args.gpus)
@@ -847,7 +1013,9 @@ def main():
         return
     dist.init()
     try:
-        if args.workload in GEMM_WORKLOADS:
+        if args.workload in GEMM_WORKLOADS and dist.world > 1:
+            out = run_gemm_sharded(args, dist, GEMM_WORKLOADS[args.workload])
+        elif args.workload in GEMM_WORKLOADS:
             out = run_gemm_workload(args, dist, GEMM_WORKLOADS[args.workload])
         elif args.workload == "decode":
             out = run_decode(args, dist)
@@ -857,10 +1025,8 @@ def main():
             out = run_attention(args, dist)
         elif args.workload == "decode_shapes":
             out = run_decode_shapes(args, dist)
-        elif args.workload == "dit":
-            out = run_dit(args, dist)
         else:
-            out = run_sharded(args, dist)
+            out = run_dit(args, dist)
         if dist.rank == 0:
             print(json.dumps(out), flush=True)
     finally:

@@ -39,6 +39,7 @@ extern "C" {
 #define PXQ_ERR_DEVICE_STATUS 6 /* a kernel reported a bounded-wait timeout */
 #define PXQ_ERR_IO 7            /* a model file could not be opened or mapped */
 #define PXQ_ERR_FORMAT 8        /* a model file is not a GGUF v3 file this loader accepts */
+#define PXQ_ERR_TIMEOUT 9       /* a multi-GPU set-up or collective did not complete in time (communicator aborted) */
 
 /* GGML type ids, src/model_types.h:13-21 */
 #define PXQ_TYPE_F32 0
@@ -203,6 +204,71 @@ PXQ_API int pxq_ipc_alloc(size_t bytes, void** ptr, void* handle);
 PXQ_API int pxq_ipc_free(void* ptr);
 PXQ_API int pxq_ipc_open(const void* handle, void** ptr);
 PXQ_API int pxq_ipc_close(void* ptr);
+
+/* ---- N-sharded multi-GPU matmul (one process per GPU, NCCL) ---------------
+ * No counterpart in the single-process reference: its CPU path computes all
+ * output columns of cpu_quant_matmul in one process
+ * (src/kernels_quant.cpp:389-400).  Output columns (weight rows) are
+ * independent, so G ranks each hold an even share of the weight rows --
+ * rank r the rows [r*N/G, (r+1)*N/G), uploaded as an ordinary pxq_weight --
+ * compute their columns for the replicated activation, and assemble the
+ * full row-major output on every rank, bit-identical to one GPU.
+ *
+ * Failure handling: the communicator is created non-blocking and every wait
+ * (set-up, collectives, synchronize) polls NCCL's asynchronous error state
+ * against the communicator's timeout; on expiry it is aborted and the call
+ * returns PXQ_ERR_TIMEOUT (a rank that never joins or never reaches a
+ * collective).  An aborted communicator fails every later call; destroy it
+ * and create a new one. */
+typedef struct pxq_comm pxq_comm;
+typedef struct pxq_sharded_out pxq_sharded_out;
+#define PXQ_COMM_ID_BYTES 128
+
+/* One rank (usually rank 0) creates the communicator id and hands its
+ * PXQ_COMM_ID_BYTES bytes to every rank by any channel (ncclGetUniqueId). */
+PXQ_API int pxq_comm_unique_id(void* id);
+
+/* Join communicator `id` as `rank` of `world` (1..8) on the calling thread's
+ * current device (select it with pxq_init first).  Returns PXQ_ERR_TIMEOUT
+ * if not every rank joined within timeout_ms. */
+PXQ_API int pxq_comm_init(const void* id, int world, int rank, int timeout_ms, pxq_comm** out);
+PXQ_API int pxq_comm_size(const pxq_comm* comm, int* world, int* rank);
+/* Host-side barrier of all ranks (bounded by the timeout). */
+PXQ_API int pxq_comm_barrier(pxq_comm* comm);
+/* Wait for `stream` (bounded by the timeout; NCCL errors abort the
+ * communicator), then report kernel status like pxq_synchronize. */
+PXQ_API int pxq_comm_synchronize(pxq_comm* comm, void* stream);
+PXQ_API int pxq_comm_destroy(pxq_comm* comm);
+
+/* Collective: an fp32 output [columns][ldy] on every rank, each rank's
+ * buffer mapped into every other rank's address space (CUDA IPC handles
+ * exchanged over the communicator).  *local (may be NULL) receives this
+ * rank's buffer (device pointer).  Destroy collectively too. */
+PXQ_API int pxq_sharded_output_create(pxq_comm* comm, size_t columns, size_t ldy, pxq_sharded_out** out, float** local);
+PXQ_API int pxq_sharded_output_destroy(pxq_sharded_out* out);
+
+/* Y = input * W^T with W's N = G*shard_rows rows split over the ranks;
+ * `shard` holds this rank's shard_rows rows.  input: device fp32
+ * [columns][inner], replicated on every rank.  Every rank calls it with the
+ * same shapes, in the same order.  Queued on `stream`; complete after
+ * pxq_comm_synchronize.
+ *   out != NULL (columns > 8): fused -- the GEMM epilogue stores its
+ *     columns into every rank's `out` buffer over NVLink while later tiles
+ *     compute, between two device-side barriers; Y is in each rank's local
+ *     buffer (`output`, `ldy` unused).
+ *   out == NULL: the rank's columns go to stream-ordered scratch, an NCCL
+ *     all-gather collects every rank's block and one re-layout kernel
+ *     writes `output` (device [columns][ldy], ldy >= N). */
+PXQ_API int pxq_sharded_matmul(pxq_comm* comm, pxq_weight* shard, size_t shard_rows, const float* input, size_t columns,
+                               pxq_sharded_out* out, float* output, size_t ldy, void* stream);
+
+/* The same with host buffers, the multi-GPU counterpart of pxq_quant_matmul:
+ * the host input [columns][inner] is copied to this rank's device, the fused
+ * sharded product computed, and the full output [columns][N] copied back to
+ * the host before the call returns.  Output buffers are created on the
+ * first call of a shape (collectively) and kept for later calls. */
+PXQ_API int pxq_sharded_matmul_host(pxq_comm* comm, pxq_weight* shard, size_t shard_rows, const float* input, size_t columns,
+                                    size_t inner, float* output);
 
 /* ---- quantize once, multiply many ----------------------------------------
  * The reference quantizes the activation inside every cpu_quant_matmul call

@@ -15,6 +15,7 @@
 // error status (the reference's `false`), never computed on the host.
 #include <atomic>
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <list>
@@ -154,9 +155,10 @@ struct Packed {
     int64_t rows = 0;   // packed rows
     int64_t ldn = 0;    // row stride of the K-quant scale planes
     void* mem = nullptr;
-    __half* wv = nullptr;     // fp16 operand [rows][K] (Q6_K: [rows][2K], even and parity planes)
-    __half* ws = nullptr;     // Q8_0 one-hot scales [rows][nb*16] / Q5_K min operand [rows][nsb*16]
-    float* d = nullptr;       // Q5_K / Q6_K d [nsb][ldn]
+    void* wv = nullptr;       // operand [rows][K]: fp16 (Q6_K: [rows][2K], even and parity planes) or Q8_0 int8
+    __half* ws = nullptr;     // Q5_K min operand [rows][nsb*16]
+    float* d = nullptr;       // block scales: Q8_0 d [K/32][ldn], Q5_K / Q6_K d [nsb][ldn]
+    int q8_int8 = 0;          // Q8_0: int8 operand (kind::i8 GEMM)
     float* dmin = nullptr;    // Q5_K dmin [nsb][ldn]
     CUtensorMap tmW, tmWs, tmD, tmDm;
     ~Packed()
@@ -193,8 +195,9 @@ struct pxq_activation {
     int64_t M = 0, K = 0;
     bool blocks = false;    // true: matvec operand; false: GEMM operand
     void* mem = nullptr;
-    __half* xq = nullptr;   // operand: exact fp16 quants [M][K]
-    void* scale = nullptr;  // operand: Q8_0 fp16 scales [M][ldd] / Q8_K fp32 d [nsb][ldd]
+    void* xq = nullptr;     // operand: the quants [M][K], exact fp16 values (Q8_0: or int8)
+    void* scale = nullptr;  // operand: fp32 block scales, block-major [K/block][ldd]
+    int q8_int8 = 0;        // Q8_0: int8 operand
     __half* amin = nullptr; // operand (Q8_K): min-term split sums [M][nsb*16]
     int64_t ldd = 0;
     CUtensorMap tmX, tmXs, tmDx;
@@ -209,6 +212,17 @@ cudaError_t matvec_fused(const pxq_weight* w, size_t row_first, size_t row_count
 namespace {
 
 std::unordered_map<std::string, pxq_weight*> g_cache;  // guarded by g_mutex
+
+// Q8_0 GEMM operand kind: 1 = int8 quants and kind::i8 MMA, 0 = exact fp16
+// copies and kind::f16.  Read once from PXQ_Q8_0_MMA ("i8" / "f16").
+int q8_int8_operands()
+{
+    static const int v = [] {
+        const char* e = getenv("PXQ_Q8_0_MMA");
+        return (e && strcmp(e, "f16") == 0) ? 0 : 1;
+    }();
+    return v;
+}
 std::atomic<uint64_t> g_launches{0};
 
 cudaError_t counted(cudaError_t e, uint64_t n = 1)
@@ -222,24 +236,28 @@ int build_packed(const DeviceCtx* d, pxq_weight* w, int64_t first, int64_t count
 {
     auto pk = std::make_unique<Packed>();
     const int64_t K = w->inner;
-    const bool q5 = w->type == kTypeQ5_K, q6 = w->type == kTypeQ6_K;
+    const bool q5 = w->type == kTypeQ5_K, q6 = w->type == kTypeQ6_K, q8 = w->type == kTypeQ8_0;
+    const int i8 = q8 ? q8_int8_operands() : 0;
     const int64_t nb = (q5 || q6) ? K / kQKK : K / kQK8_0;
     const int64_t Kop = q6 ? 2 * K : K;  // Q6_K: even and parity planes per chunk
+    const int64_t elem = i8 ? 1 : 2;
     pk->rows = count;
     pk->ldn = round_up(count, 4);
-    const size_t wv_bytes = (size_t)count * Kop * 2;
-    const size_t ws_bytes = q6 ? 0 : (size_t)count * nb * 32;
-    const size_t s_bytes = (q5 || q6) ? (size_t)nb * pk->ldn * 4 : 0;
+    pk->q8_int8 = i8;
+    const size_t wv_bytes = (size_t)count * Kop * elem;
+    const size_t ws_bytes = q5 ? (size_t)count * nb * 32 : 0;
+    const size_t s_bytes = (size_t)nb * pk->ldn * 4;
+    const size_t dm_bytes = q5 ? s_bytes : 0;
     const size_t off_ws = round_up((int64_t)wv_bytes, 1024);
     const size_t off_d = off_ws + round_up((int64_t)ws_bytes, 1024);
     const size_t off_dm = off_d + round_up((int64_t)s_bytes, 1024);
-    const size_t total = off_dm + round_up((int64_t)s_bytes, 1024) + 1024;
+    const size_t total = off_dm + round_up((int64_t)dm_bytes, 1024) + 1024;
     if (cudaMalloc(&pk->mem, total) != cudaSuccess) {
         cudaGetLastError();
         return fail(PXQ_ERR_NO_MEMORY, "cannot allocate %zu bytes for the GEMM operand copy", total);
     }
     uint8_t* base = static_cast<uint8_t*>(pk->mem);
-    pk->wv = reinterpret_cast<__half*>(base);
+    pk->wv = base;
     pk->ws = reinterpret_cast<__half*>(base + off_ws);
     pk->d = reinterpret_cast<float*>(base + off_d);
     pk->dmin = reinterpret_cast<float*>(base + off_dm);
@@ -247,22 +265,24 @@ int build_packed(const DeviceCtx* d, pxq_weight* w, int64_t first, int64_t count
     const uint8_t* src = w->raw + first * w->stride;
     const int64_t gate_rows = w->gated ? w->rows / 2 : 0;  // whole-tensor copies only (first = 0)
     if (q6) {
-        PXQ_CUDA(counted(launch_repack_q6_K(src, count, K, w->stride, pk->wv, pk->d, pk->ldn, gate_rows, s)));
-    } else if (!q5) {
-        PXQ_CUDA(counted(launch_repack_q8_0(src, count, K, w->stride, pk->wv, pk->ws, gate_rows, s)));
+        PXQ_CUDA(counted(launch_repack_q6_K(src, count, K, w->stride, static_cast<__half*>(pk->wv), pk->d, pk->ldn, gate_rows, s)));
+    } else if (q8) {
+        PXQ_CUDA(counted(launch_repack_q8_0(src, count, K, w->stride, pk->wv, pk->d, pk->ldn, i8, gate_rows, s)));
     } else {
-        PXQ_CUDA(counted(launch_repack_q5_K(src, count, K, w->stride, pk->wv, pk->d, pk->dmin, pk->ws, pk->ldn, gate_rows, s)));
+        PXQ_CUDA(counted(launch_repack_q5_K(src, count, K, w->stride, static_cast<__half*>(pk->wv), pk->d, pk->dmin, pk->ws,
+                                            pk->ldn, gate_rows, s)));
     }
-    int rc = make_map(d, &pk->tmW, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pk->wv, Kop, count, Kop * 2, 64, 128,
-                      CU_TENSOR_MAP_SWIZZLE_128B);
+    // operand box: one 128-byte swizzle row (64 fp16 or 128 int8) x 128 rows
+    int rc = make_map(d, &pk->tmW, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pk->wv, Kop, count,
+                      Kop * elem, (uint32_t)(128 / elem), 128, CU_TENSOR_MAP_SWIZZLE_128B);
     // unused maps of a type hold the weight map (any valid map will do)
     pk->tmWs = pk->tmD = pk->tmDm = pk->tmW;
-    if (!rc && !q6)
+    if (!rc && q5)
         rc = make_map(d, &pk->tmWs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pk->ws, nb * 16, count, nb * 32, 16, 128,
                       CU_TENSOR_MAP_SWIZZLE_32B);
-    if (!rc && (q5 || q6))
-        rc = make_map(d, &pk->tmD, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pk->d, count, nb, pk->ldn * 4, 128, 1,
-                      CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (!rc)
+        rc = make_map(d, &pk->tmD, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pk->d, count, nb, pk->ldn * 4, 128,
+                      q8 ? (uint32_t)gemm_q8_scale_box(i8) : 1u, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (!rc && q5)
         rc = make_map(d, &pk->tmDm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pk->dmin, count, nb, pk->ldn * 4, 128, 1,
                       CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -340,9 +360,11 @@ int quantize_activation(DeviceCtx* d, uint32_t wtype, const float* input, int64_
         }
         e = launch_matvec_quantize(plan, input, K, a->mem, nullptr, s);
     } else {
-        a->ldd = q5 ? round_up(M, 4) : round_up(nb, 8);
-        const size_t xq_bytes = (size_t)M * K * 2;
-        const size_t sc_bytes = q5 ? (size_t)nb * a->ldd * 4 : (size_t)M * a->ldd * 2;
+        const int i8 = q5 ? 0 : q8_int8_operands();
+        a->q8_int8 = i8;
+        a->ldd = round_up(M, 4);
+        const size_t xq_bytes = (size_t)M * K * (i8 ? 1 : 2);
+        const size_t sc_bytes = (size_t)nb * a->ldd * 4;
         const size_t amin_bytes = q5 ? (size_t)M * nb * 32 : 0;
         const size_t off_sc = round_up((int64_t)xq_bytes, 1024);
         const size_t off_amin = off_sc + round_up((int64_t)sc_bytes, 1024);
@@ -352,13 +374,16 @@ int quantize_activation(DeviceCtx* d, uint32_t wtype, const float* input, int64_
             return fail(PXQ_ERR_NO_MEMORY, "scratch allocation of %zu bytes failed", total);
         }
         uint8_t* base = static_cast<uint8_t*>(a->mem);
-        a->xq = reinterpret_cast<__half*>(base);
+        a->xq = base;
         a->scale = base + off_sc;
         a->amin = reinterpret_cast<__half*>(base + off_amin);
-        e = q5 ? launch_quantize_q8_K_operand(input, a->xq, static_cast<float*>(a->scale), a->amin, M, K, K, a->ldd, s)
-               : launch_quantize_q8_0_operand(input, a->xq, static_cast<__half*>(a->scale), M, K, K, a->ldd, s);
+        e = q5 ? launch_quantize_q8_K_operand(input, static_cast<__half*>(a->xq), static_cast<float*>(a->scale), a->amin, M, K, K,
+                                              a->ldd, s)
+               : launch_quantize_q8_0_operand(input, a->xq, static_cast<float*>(a->scale), i8, M, K, K, a->ldd, s);
         const uint32_t xr = (uint32_t)gemm_activation_rows(wtype);  // one CTA's rows of an output tile
-        int rc = make_map(d, &a->tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->xq, K, M, K * 2, 64, xr, CU_TENSOR_MAP_SWIZZLE_128B);
+        const int64_t elem = i8 ? 1 : 2;
+        int rc = make_map(d, &a->tmX, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->xq, K, M, K * elem,
+                          (uint32_t)(128 / elem), xr, CU_TENSOR_MAP_SWIZZLE_128B);
         if (!rc && q5) {
             rc = make_map(d, &a->tmXs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->amin, nb * 16, M, nb * 32, 16, xr,
                           CU_TENSOR_MAP_SWIZZLE_32B);
@@ -366,9 +391,9 @@ int quantize_activation(DeviceCtx* d, uint32_t wtype, const float* input, int64_
                                    (uint32_t)gemm_tile_activation_rows(wtype), 1,
                                    CU_TENSOR_MAP_SWIZZLE_NONE);
         } else if (!rc) {
-            rc = make_map(d, &a->tmXs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->scale, nb, M, a->ldd * 2, 16, xr,
-                          CU_TENSOR_MAP_SWIZZLE_32B);
-            a->tmDx = a->tmX;
+            a->tmXs = a->tmX;
+            rc = make_map(d, &a->tmDx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a->scale, M, nb, a->ldd * 4,
+                          (uint32_t)gemm_tile_activation_rows(wtype), (uint32_t)gemm_q8_scale_box(i8), CU_TENSOR_MAP_SWIZZLE_NONE);
         }
         if (rc) {
             cudaFreeAsync(a->mem, s);
@@ -472,9 +497,12 @@ int run_gemm(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, co
     int64_t n_first = 0;
     int rc = get_packed(d, w, (int64_t)row_first, (int64_t)row_count, &pk, &n_first, s);
     if (rc) return rc;
+    if (w->type == kTypeQ8_0 && pk->q8_int8 != a->q8_int8)
+        return fail(PXQ_ERR_INVALID, "Q8_0 weight and activation operands were built for different MMA kinds");
     GemmOperands op;
     std::memset(&op, 0, sizeof(op));
     op.type = w->type;
+    op.q8_int8 = pk->q8_int8;
     op.M = a->M;
     op.N = (int64_t)row_count;
     op.K = a->K;

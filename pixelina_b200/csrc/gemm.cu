@@ -1,21 +1,19 @@
-// gemm.cu -- large-M quantized GEMM on the 5th-generation tensor cores,
-// one CTA pair per output tile.
+// gemm.cu -- large-M K-quant (Q5_K, Q6_K) GEMM on the 5th-generation
+// tensor cores, one CTA pair per output tile.  (Q8_0: gemm_q8.cu.)
 //
 // Computes Y[m, n] = sum over K-blocks b of  s(m,n,b) * I(m,n,b)
 // where I is the exact integer dot of one block of quants and s the product
-// of the block scales -- the arithmetic of pix_dot_q8_0
-// (src/kernels_quant.cpp:339-365), pix_dot_q5_K (:163-254) and pix_dot_q6_K
-// (:256-337) as driven by cpu_quant_matmul (:389-400), for every
-// (activation row m, weight row n).
+// of the block scales -- the arithmetic of pix_dot_q5_K
+// (src/kernels_quant.cpp:163-254) and pix_dot_q6_K (:256-337) as driven by
+// cpu_quant_matmul (:389-400), for every (activation row m, weight row n).
 //
 // Design (sm_100a):
 //   * Operands are exact fp16 copies of the int8 quants (activations from
-//     quantize.cu, weights from the one-time repack in repack.cu).  A
-//     kind::f16 tcgen05.mma with fp32 accumulation computes each block dot
-//     exactly (|I| <= 32*127*127 for Q8_0, < 2^24 for a K-quant 64-value
-//     chunk with the sub-block scale folded in) and hands the drain a float.
-//     (kind::i8 runs the MMA twice as fast but needs an int->float
-//     conversion per element per block on the CUDA cores.)
+//     quantize.cu, weights from the one-time repack in repack.cu) with the
+//     sub-block scales folded into the weight side.  A kind::f16 tcgen05.mma
+//     with fp32 accumulation computes each 64-value chunk dot exactly
+//     (< 2^24) and hands the drain a float; the folded scales make the
+//     chunk values larger than int8, so kind::i8 does not apply.
 //   * CTA pairs (cta_group::2): the two CTAs of a cluster share every MMA.
 //     The pair's tile is 256 weight rows (the MMA's M; each CTA stages and
 //     accumulates its 128) by TMP activation rows (the MMA's N; each CTA
@@ -30,11 +28,6 @@
 //   * Orientation: TMEM lanes are WEIGHT rows, TMEM columns are ACTIVATION
 //     rows.  Per-weight-row scales are then per-thread scalars, and the 32
 //     lanes of a warp store 32 consecutive outputs.
-//   * Q8_0 (TMP = 128, four 128-column slots): the per-block scale product
-//     dW[n,b]*dX[m,b] is itself computed by the tensor core -- a K=16 MMA of
-//     a one-hot weight-scale tile (dW at position b%16) against the
-//     activations' 16-block fp16 scale tile, exact because fp16*fp16 fits
-//     fp32 -- so the drain is one FMA per element per block.
 //   * Q5_K (TMP = 256, two 256-column slots): 6-bit sub-block scales are
 //     folded into the weight operand (sc*q5 <= 1953, exact in fp16), so every
 //     64-value chunk dot is exact in the fp32 accumulator, and the four
@@ -54,7 +47,7 @@
 //   * The block-dot dump (pxq_gemm_block_dots) drains every block / chunk /
 //     min sum on its own, so the exact int32 dots stay checkable.
 //   * Warp roles (12 warps, 3 warpgroups): warpgroups 0-1 drain TMEM (warp w
-//     reads lane quadrant w%4 and column half w/4) with 224-232 registers
+//     reads lane quadrant w%4 and column half w/4) with 224 registers
 //     (setmaxnreg); warpgroup 2 runs the TMA producer (warp 8, every CTA)
 //     and the single-thread MMA issuer (warp 9 of the even CTA) with 40-56,
 //     within the 384*168 registers the block launches with.
@@ -86,23 +79,10 @@ constexpr int MAX_SB_DEPTH = 4;        // super-block scale entry ring (per type
 template <uint32_t TYPE>
 struct Cfg;
 template <>
-struct Cfg<kTypeQ8_0> {
-    // one CTA per tile: a Q8_0 block is too little MMA work to cover a
-    // hand-off between two SMs per block
-    static constexpr int CG = 1, TMP = 128, SLOTS = 4, STAGES = 3;
-    static constexpr uint32_t PRODUCER_REGS = 40, DRAIN_REGS = 232;
-    static constexpr int SROWS = 64;  // activation rows per TMA store of a drain warp (0: direct stores)
-    static constexpr int XR = TMP / CG, X_BYTES = XR * BK * 2, SW32_X = XR * 32;
-    // stage: W | X | one-hot weight scales of the stage's 2 blocks | activation scales (16 blocks)
-    static constexpr int STAGE = W_BYTES + X_BYTES + 2 * SW32_W + SW32_X;  // 44 KB
-    static constexpr int MIN_ENTRY = 0, SB_ENTRY = 0, SB_DEPTH = 1;
-    static constexpr int OFF_DW = 0, OFF_DMW = 0, OFF_DX = 0;  // no super-block entries
-};
-template <>
 struct Cfg<kTypeQ5_K> {
     static constexpr int CG = 2, TMP = 256, SLOTS = 2, STAGES = 4;
     static constexpr uint32_t PRODUCER_REGS = 56, DRAIN_REGS = 224;
-    static constexpr int SROWS = 64;
+    static constexpr int SROWS = 64;  // activation rows per TMA store of a drain warp
     static constexpr int XR = TMP / CG, X_BYTES = XR * BK * 2, SW32_X = XR * 32;
     static constexpr int STAGE = W_BYTES + X_BYTES;                          // 32 KB
     static constexpr int MIN_ENTRY = SW32_W + SW32_X;                        // weight | activation min operands
@@ -114,7 +94,7 @@ struct Cfg<kTypeQ6_K> {
     static constexpr int CG = 2, TMP = 256, SLOTS = 2, STAGES = 3;
     static constexpr uint32_t PRODUCER_REGS = 56, DRAIN_REGS = 224;
     static constexpr int SROWS = 64;
-    static constexpr int XR = TMP / CG, X_BYTES = XR * BK * 2, SW32_X = XR * 32;
+    static constexpr int XR = TMP / CG, X_BYTES = XR * BK * 2;
     static constexpr int STAGE = 2 * W_BYTES + X_BYTES;                      // even | parity | X: 48 KB
     static constexpr int MIN_ENTRY = 0;
     // an entry is freed only when the drain has finished its super-block, one
@@ -143,16 +123,14 @@ __host__ __device__ constexpr int smem_bytes() { return off_bar<TYPE>() + NUM_BA
 // 384 x 168 registers the block launches with
 template <uint32_t TYPE>
 constexpr bool regs_fit() { return 256 * Cfg<TYPE>::DRAIN_REGS + 128 * Cfg<TYPE>::PRODUCER_REGS <= 384 * 168; }
-static_assert(regs_fit<kTypeQ8_0>() && regs_fit<kTypeQ5_K>() && regs_fit<kTypeQ6_K>(), "setmaxnreg split");
-static_assert(Cfg<kTypeQ8_0>::STAGES <= MAX_STAGES && Cfg<kTypeQ5_K>::STAGES <= MAX_STAGES &&
-                  Cfg<kTypeQ6_K>::STAGES <= MAX_STAGES, "stage count");
-static_assert(smem_bytes<kTypeQ8_0>() <= 232448, "Q8_0 shared memory");
+static_assert(regs_fit<kTypeQ5_K>() && regs_fit<kTypeQ6_K>(), "setmaxnreg split");
+static_assert(Cfg<kTypeQ5_K>::STAGES <= MAX_STAGES && Cfg<kTypeQ6_K>::STAGES <= MAX_STAGES, "stage count");
 static_assert(smem_bytes<kTypeQ5_K>() <= 232448, "Q5_K shared memory");
 static_assert(smem_bytes<kTypeQ6_K>() <= 232448, "Q6_K shared memory");
-static_assert(Cfg<kTypeQ8_0>::STAGE % 1024 == 0 && Cfg<kTypeQ5_K>::STAGE % 1024 == 0 && Cfg<kTypeQ6_K>::STAGE % 1024 == 0 &&
+static_assert(Cfg<kTypeQ5_K>::STAGE % 1024 == 0 && Cfg<kTypeQ6_K>::STAGE % 1024 == 0 &&
                   Cfg<kTypeQ5_K>::MIN_ENTRY % 1024 == 0 && Cfg<kTypeQ5_K>::SB_ENTRY % 1024 == 0,
               "swizzled tiles need 1024-byte alignment");
-static_assert(Cfg<kTypeQ8_0>::SLOTS * Cfg<kTypeQ8_0>::TMP <= (int)TMEM_COLS && Cfg<kTypeQ5_K>::SLOTS * Cfg<kTypeQ5_K>::TMP <= (int)TMEM_COLS,
+static_assert(Cfg<kTypeQ5_K>::SLOTS * Cfg<kTypeQ5_K>::TMP <= (int)TMEM_COLS && Cfg<kTypeQ6_K>::SLOTS * Cfg<kTypeQ6_K>::TMP <= (int)TMEM_COLS,
               "TMEM columns");
 
 struct Params {
@@ -180,28 +158,10 @@ __device__ __forceinline__ void put_y(const Params& p, int64_t m, int64_t n, flo
     for (int k = 0; k < p.ndst; k++) p.ydst[k][off] = v;
 }
 
-// tcgen05 and stage-load forms for one CTA per tile (CG = 1) or a CTA pair
-// (CG = 2); a kernel uses one form throughout, as tcgen05 requires.
+// tcgen05 and stage-load forms for a CTA pair (CG = 2); a kernel uses one
+// form throughout, as tcgen05 requires.
 template <int CG>
 struct Grp;
-template <>
-struct Grp<1> {
-    static __device__ __forceinline__ void alloc(uint32_t* dst, uint32_t n) { tmem_alloc(dst, n); }
-    static __device__ __forceinline__ void relinquish() { tmem_relinquish(); }
-    static __device__ __forceinline__ void dealloc(uint32_t t, uint32_t n) { tmem_dealloc(t, n); }
-    static __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc)
-    {
-        mma_f16(d, a, b, idesc, acc);
-    }
-    static __device__ __forceinline__ void commit(uint64_t* bar) { mma_commit(bar); }
-    static __device__ __forceinline__ void commit_local(uint64_t* bar) { mma_commit(bar); }
-    // stage load reporting on this CTA's barrier
-    static __device__ __forceinline__ void load(void* dst, const void* map, uint64_t* bar, uint32_t, int32_t c0, int32_t c1)
-    {
-        tma_load_2d(dst, map, bar, c0, c1);
-    }
-    static __device__ __forceinline__ void sync() { __syncthreads(); }
-};
 template <>
 struct Grp<2> {
     static __device__ __forceinline__ void alloc(uint32_t* dst, uint32_t n) { tmem_alloc_pair(dst, n); }
@@ -280,7 +240,6 @@ __device__ __forceinline__ void drain_dump(uint32_t taddr, const Params& p, int6
 // tensor maps:
 //   tmW   weight operand fp16 [N][K] (Q6_K: [N][2K])  box {64, 128}  128B swizzle
 //   tmX   activation operand fp16 [M][K]               box {64, TMP/2} 128B swizzle
-//   Q8_0: tmWs  one-hot weight scales fp16 [N][nb*16]   box {16, 128} 32B swizzle
 //         tmXs  activation scales fp16 [M][nb]          box {16, TMP/2} 32B swizzle
 //   Q5_K: tmWs  weight min operand fp16 [N][nsb*16]     box {16, 128} 32B swizzle
 //         tmXs  activation min operand fp16 [M][nsb*16] box {16, TMP/2} 32B swizzle
@@ -298,13 +257,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     using C = Cfg<TYPE>;
     using G = Grp<C::CG>;
     constexpr int CG = C::CG;
-    constexpr bool Q8 = TYPE == kTypeQ8_0;
     constexpr bool Q5 = TYPE == kTypeQ5_K;
     constexpr bool Q6 = TYPE == kTypeQ6_K;
-    constexpr int TMP = C::TMP, XR = C::XR, SLOTS = C::SLOTS, STAGES = C::STAGES;
+    constexpr int TMP = C::TMP, XR = C::XR, STAGES = C::STAGES;
     constexpr int HC = TMP / 2;  // TMEM columns per drain warp
-    constexpr bool SPLIT = !Q8;  // K-quant accumulators in the 16x256b layout (drain_split)
-    static_assert(!SPLIT || HC == 128, "split layout covers 128 columns per warp");
+    static_assert(HC == 128, "the 16x256b accumulator layout covers 128 columns per warp");
     constexpr uint32_t IDESC = idesc_f16_f32(CG * TN, TMP);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -363,10 +320,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             tma_prefetch_desc(&tmXs);
         }
         if (C::SROWS > 0 && p.tma_store) tma_prefetch_desc(&tmY);
-        if (!Q8) {
-            tma_prefetch_desc(&tmD);
-            tma_prefetch_desc(&tmDx);
-        }
+        tma_prefetch_desc(&tmD);
+        tma_prefetch_desc(&tmDx);
         if (Q5) tma_prefetch_desc(&tmDm);
     }
     // barriers initialised and TMEM allocated in both CTAs before any cross-CTA traffic
@@ -380,7 +335,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int64_t tiles = mt_count * nt_count;
     const int64_t pair = CG == 2 ? (int64_t)cluster_id_x() : (int64_t)blockIdx.x;
     const int64_t pairs = CG == 2 ? (int64_t)cluster_count_x() : (int64_t)gridDim.x;
-    const int64_t nb = Q8 ? p.K / kQK8_0 : p.K / kQKK;  // blocks (Q8_0) or super-blocks
+    const int64_t nb = p.K / kQKK;  // super-blocks
     const int64_t nchunks = (p.K + BK - 1) / BK;
     uint32_t* status = p.status;
 
@@ -397,7 +352,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int32_t mc = m0 + (int32_t)(rank * XR);
                 const int32_t nc = (int32_t)(p.n_first + (tile / mt_count) * CG * TN + rank * TN);
                 for (int64_t kc = 0; kc < nchunks; kc++) {
-                    if (!Q8 && kc % 4 == 0) {
+                    if (kc % 4 == 0) {
                         const int32_t sb = (int32_t)(kc / 4);
                         // this CTA's scales for its drain
                         if (!mbar_wait(&sempty[se], sph ^ 1u, abort_flag, status, kDevTimeoutScaleEmpty)) goto done;
@@ -428,15 +383,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const uint32_t fb = full0 + 8u * stage;
                     uint64_t* fl = &full[stage];
                     const int32_t kx = (int32_t)(kc * BK);
-                    if (Q8) {
-                        const int nblk = (2 * kc + 1 < nb) ? 2 : 1;
-                        if (leader) mbar_expect_tx(fl, CG * (W_BYTES + C::X_BYTES + nblk * SW32_W + C::SW32_X));
-                        G::load(st, &tmW, fl, fb, kx, nc);
-                        G::load(st + W_BYTES, &tmX, fl, fb, kx, mc);
-                        for (int b = 0; b < nblk; b++)
-                            G::load(st + W_BYTES + C::X_BYTES + b * SW32_W, &tmWs, fl, fb, (int32_t)((2 * kc + b) * 16), nc);
-                        G::load(st + W_BYTES + C::X_BYTES + 2 * SW32_W, &tmXs, fl, fb, (int32_t)(((2 * kc) / 16) * 16), mc);
-                    } else if (Q6) {
+                    if (Q6) {
                         // chunk kc's even and parity planes sit side by side in the [N][2K] operand
                         if (leader) mbar_expect_tx(fl, CG * (2 * W_BYTES + C::X_BYTES));
                         G::load(st, &tmW, fl, fb, 2 * kx, nc);
@@ -454,9 +401,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
             }
         } else if (warp == MMA_WARP && lane == 0 && leader) {
-            int stage = 0, me = 0, slot = 0;
-            uint32_t ph = 0, mph = 0, tph = 0;
-            uint64_t gsb = 0;   // super-blocks issued (K-quants): selects the slots' roles
+            int stage = 0, me = 0;
+            uint32_t ph = 0, mph = 0;
+            uint64_t gsb = 0;   // super-blocks issued: selects the slots' roles
             uint64_t item = 0;  // items issued (K-quant block-dot dump: every item in the next slot)
             for (int64_t tile = pair; tile < tiles; tile += pairs) {
                 for (int64_t kc = 0; kc < nchunks; kc++) {
@@ -482,34 +429,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     tc_fence_after();
                     const uint32_t w_addr = smem_u32(smem + stage * C::STAGE);
                     const uint32_t x_addr = w_addr + (Q6 ? 2 * W_BYTES : W_BYTES);
-                    if (Q8) {
-                        const uint32_t ws_addr = x_addr + C::X_BYTES;
-                        const uint32_t xs_addr = ws_addr + 2 * SW32_W;
-#pragma unroll
-                        for (int blk = 0; blk < 2; blk++) {
-                            if (2 * kc + blk >= nb) break;
-                            // slots (slot, slot+1) hold (scale product, block dot); slot is even
-                            if (!mbar_wait_cluster(&tempty[slot], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
-                            if (!mbar_wait_cluster(&tempty[slot + 1], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty))
-                                goto done;
-                            tc_fence_after();
-                            const uint32_t ds = tmem_base + (uint32_t)slot * TMP;
-                            // the activation scale tile covers blocks 16*g .. 16*g+15; the one-hot
-                            // weight tile selects block (2kc+blk) % 16 of it
-                            G::mma(ds, desc_sw32(ws_addr + blk * SW32_W), desc_sw32(xs_addr), IDESC, 0u);
-#pragma unroll
-                            for (int k = 0; k < 2; k++) {
-                                const uint32_t koff = (uint32_t)(blk * 2 + k) * 32u;  // 16 fp16 = 32 bytes
-                                G::mma(ds + TMP, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC, (uint32_t)k);
-                            }
-                            G::commit(&tfull[slot]);
-                            slot += 2;
-                            if (slot == SLOTS) {
-                                slot = 0;
-                                tph ^= 1u;
-                            }
-                        }
-                    } else {
+                    {
                         // this stage's chunk: into the super-block's chunk slot (or, dumping, its own slot)
                         const bool first = DUMP || q == 0;
                         const bool last = DUMP || q == 3 || kc == nchunks - 1;
@@ -581,8 +501,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                     mbar_arrive_remote(tempty0 + 8u * (uint32_t)s);
             }
         };
-        int slot = 0, se = 0;
-        uint32_t tph = 0, sph = 0, mgph = 0;
+        int se = 0;
+        uint32_t sph = 0, mgph = 0;
         uint64_t gsb = 0, item = 0;
         // all drain warps meet (bounded wait, like every wait of this kernel)
         auto drain_meet = [&](int i) -> bool {
@@ -597,39 +517,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             float acc[HC];
 #pragma unroll
             for (int i = 0; i < HC; i++) acc[i] = 0.f;
-            if constexpr (Q8) {
-                for (int64_t b = 0; b < nb; b++) {
-                    if (!mbar_wait(&tfull[slot], tph, abort_flag, status, kDevTimeoutTmemFull)) goto done;
-                    tc_fence_after();
-                    const uint32_t ts = tmem_base + lane_base + (uint32_t)slot * TMP + half * HC;
-                    if (DUMP) {
-                        drain_dump<HC>(ts + TMP, p, b, mfirst, n);
-                    } else {
-                        uint32_t sv[32], sv2[32], iv[32], iv2[32];
-                        tmem_ld32(ts, sv);
-                        tmem_ld32(ts + 32, sv2);
-                        tmem_ld32(ts + TMP, iv);
-                        tmem_ld32(ts + TMP + 32, iv2);
-                        tmem_ld_wait();
-                        // pix_dot_q8_0: acc = fma(fp16(dw)*fp16(dx), float(block dot), acc), two per instruction
-#pragma unroll
-                        for (int j = 0; j < 32; j += 2)
-                            ffma2(acc[j], acc[j + 1], __uint_as_float(sv[j]), __uint_as_float(sv[j + 1]), __uint_as_float(iv[j]),
-                                  __uint_as_float(iv[j + 1]));
-#pragma unroll
-                        for (int j = 0; j < 32; j += 2)
-                            ffma2(acc[32 + j], acc[33 + j], __uint_as_float(sv2[j]), __uint_as_float(sv2[j + 1]),
-                                  __uint_as_float(iv2[j]), __uint_as_float(iv2[j + 1]));
-                    }
-                    release(slot);
-                    release(slot + 1);
-                    slot += 2;
-                    if (slot == SLOTS) {
-                        slot = 0;
-                        tph ^= 1u;
-                    }
-                }
-            } else {
+            {
                 for (int64_t sb = 0; sb < nb; sb++) {
                     if (!mbar_wait(&sfull[se], sph, abort_flag, status, kDevTimeoutScaleFull)) goto done;
                     const uint8_t* e = sb_region + se * C::SB_ENTRY;
@@ -696,27 +584,20 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int i = 0; i < HC; i++) {
                         // element i's output row (lane) and activation row (column)
-                        int lo, col;
-                        if (SPLIT) {
-                            const int c = i & 1, h = (i >> 1) & 1, k = (i >> 2) & 7, lh = (i >> 5) & 1, ch = i >> 6;
-                            lo = 16 * lh + 8 * h + (int)(lane >> 2);
-                            col = 64 * ch + 8 * k + 2 * (int)(lane & 3) + c;
-                        } else {
-                            lo = (int)lane;
-                            col = i;
-                        }
+                        const int c = i & 1, h = (i >> 1) & 1, k = (i >> 2) & 7, lh = (i >> 5) & 1, ch = i >> 6;
+                        const int lo = 16 * lh + 8 * h + (int)(lane >> 2);
+                        const int col = 64 * ch + 8 * k + 2 * (int)(lane & 3) + c;
                         const int64_t on = n0 / 2 + quad * 32 + lo, m = mfirst + col;
                         const float g = acc[i], u = xfer[i * 32 + lane];
                         if (on < p.N / 2 && m < p.M) p.y[m * p.ldy + on] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
                     }
                 }
             } else if (!DUMP) {
-                // this thread's lanes (weight rows, CTA-local): row layout (Q8_0) the
-                // thread's own lane; split layout lane_off(lh, h) = 16lh + 8h + lane/4
+                // this thread's lanes (weight rows, CTA-local): 16lh + 8h + lane/4
                 float bv[4];
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
-                    const int64_t nn = n0 + quad * 32 + (SPLIT ? 8 * i + (lane >> 2) : lane);
+                    const int64_t nn = n0 + quad * 32 + 8 * i + (lane >> 2);
                     bv[i] = (p.bias && nn < p.N) ? p.bias[nn] : 0.f;
                 }
                 if (C::SROWS > 0 && p.tma_store) {
@@ -724,29 +605,24 @@ __global__ void __launch_bounds__(THREADS, 1)
                     // stores each with one TMA store; lane 0 first waits until the warp's
                     // previous store has finished reading the buffer (no cross-warp sync)
                     constexpr int SR = C::SROWS > 0 ? C::SROWS : 64;
-                    static_assert(!SPLIT || SR == 64, "split layout stages 64 columns per round");
+                    static_assert(SR == 64, "the 16x256b layout stages 64 columns per round");
                     float* stg = reinterpret_cast<float*>(smem + off_staging<TYPE>()) + warp * (SR * 32);
 #pragma unroll
                     for (int r = 0; r < HC / SR; r++) {
                         if (lane == 0) bulk_wait_read_all();
                         __syncwarp();
-                        if (SPLIT) {
 #pragma unroll
-                            for (int lh = 0; lh < 2; lh++)
+                        for (int lh = 0; lh < 2; lh++)
 #pragma unroll
-                                for (int k = 0; k < 8; k++)
+                            for (int k = 0; k < 8; k++)
 #pragma unroll
-                                    for (int h = 0; h < 2; h++)
+                                for (int h = 0; h < 2; h++)
 #pragma unroll
-                                        for (int c = 0; c < 2; c++) {
-                                            const float v = acc[split_idx(r, lh, k, h, c)];
-                                            stg[(8 * k + 2 * (lane & 3) + c) * 32 + 16 * lh + 8 * h + (lane >> 2)] =
-                                                p.bias ? __fadd_rn(v, bv[2 * lh + h]) : v;
-                                        }
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < SR; j++) stg[j * 32 + lane] = p.bias ? __fadd_rn(acc[SR * r + j], bv[0]) : acc[SR * r + j];
-                        }
+                                    for (int c = 0; c < 2; c++) {
+                                        const float v = acc[split_idx(r, lh, k, h, c)];
+                                        stg[(8 * k + 2 * (lane & 3) + c) * 32 + 16 * lh + 8 * h + (lane >> 2)] =
+                                            p.bias ? __fadd_rn(v, bv[2 * lh + h]) : v;
+                                    }
                         fence_proxy_async_smem();
                         __syncwarp();
                         if (lane == 0) {
@@ -785,7 +661,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                             }
                         }
                     }
-                } else if (SPLIT) {
+                } else {
 #pragma unroll
                     for (int ch = 0; ch < 2; ch++)
 #pragma unroll
@@ -801,13 +677,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                                         const float v = acc[split_idx(ch, lh, k, h, c)];
                                         if (nn < p.N && m < p.M) put_y(p, m, nn, p.bias ? __fadd_rn(v, bv[2 * lh + h]) : v);
                                     }
-                } else if (n < p.N) {
-                    // lane = weight row: for each activation row, 32 lanes store 128 contiguous bytes
-#pragma unroll
-                    for (int j = 0; j < HC; j++) {
-                        const int64_t m = mfirst + j;
-                        if (m < p.M) put_y(p, m, n, p.bias ? __fadd_rn(acc[j], bv[0]) : acc[j]);
-                    }
                 }
             }
         }
@@ -815,6 +684,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 done:
     // outstanding output stores must finish reading shared memory before exit
     if (C::SROWS > 0 && p.tma_store && warp < DRAIN_WARPS && lane == 0) bulk_wait_all();
+    // peer stores are visible system-wide before the kernel ends (the
+    // N-sharded path's barrier after the kernel then orders them for the peers)
+    if (p.ndst && warp < DRAIN_WARPS) __threadfence_system();
     if (warp == MMA_WARP && lane == 0 && leader) {
         // no MMA of this pair may still be writing TMEM when it is freed (after a
         // normal run the drains have consumed every result; this covers aborts)
@@ -878,18 +750,17 @@ cudaError_t launch_typed(const GemmOperands& op, int num_sms, cudaStream_t s)
 
 }  // namespace
 
-int gemm_activation_rows(uint32_t type) { return type == kTypeQ8_0 ? Cfg<kTypeQ8_0>::XR : Cfg<kTypeQ5_K>::XR; }
-int gemm_tile_activation_rows(uint32_t type) { return type == kTypeQ8_0 ? Cfg<kTypeQ8_0>::TMP : Cfg<kTypeQ5_K>::TMP; }
+// Q8_0 (gemm_q8.cu): one CTA per 128 x 128 tile, 32-row stores
+int gemm_activation_rows(uint32_t type) { return type == kTypeQ8_0 ? 128 : Cfg<kTypeQ5_K>::XR; }
+int gemm_tile_activation_rows(uint32_t type) { return type == kTypeQ8_0 ? 128 : Cfg<kTypeQ5_K>::TMP; }
 int gemm_store_rows(uint32_t type)
 {
-    return type == kTypeQ8_0 ? Cfg<kTypeQ8_0>::SROWS : type == kTypeQ5_K ? Cfg<kTypeQ5_K>::SROWS : Cfg<kTypeQ6_K>::SROWS;
+    return type == kTypeQ8_0 ? 32 : type == kTypeQ5_K ? Cfg<kTypeQ5_K>::SROWS : Cfg<kTypeQ6_K>::SROWS;
 }
 
 cudaError_t launch_gemm(const GemmOperands& op, int num_sms, cudaStream_t s)
 {
-    if (op.type == kTypeQ8_0) {
-        return op.dump ? launch_typed<kTypeQ8_0, true>(op, num_sms, s) : launch_typed<kTypeQ8_0, false>(op, num_sms, s);
-    }
+    if (op.type == kTypeQ8_0) return launch_gemm_q8(op, num_sms, s);
     if (op.type == kTypeQ5_K) {
         return op.dump ? launch_typed<kTypeQ5_K, true>(op, num_sms, s) : launch_typed<kTypeQ5_K, false>(op, num_sms, s);
     }

@@ -1,0 +1,561 @@
+// gemm_q8.cu -- large-M Q8_0 GEMM on the 5th-generation tensor cores.
+//
+// Computes, for every activation row m and weight row n,
+//     Y[m, n] = sum over 32-blocks b of  (dW[n,b] * dX[m,b]) * I(m,n,b)
+// where I is the exact integer dot of the block's int8 quants -- the
+// arithmetic of pix_dot_q8_0 (src/kernels_quant.cpp:339-365: the fp32
+// product of the two fp16 block scales times the float of an exact int32
+// dot, accumulated in fp32) as driven by cpu_quant_matmul (:389-400).
+//
+// Design (sm_100a, one CTA per SM, persistent over 128 x 128 output tiles):
+//   * The tensor core computes only the block dots I, one TMEM slot of
+//     128 columns per 32-block; four slots, so the MMA runs up to four
+//     blocks ahead of the drain.  Two operand kinds share the kernel:
+//       OPK 0: exact fp16 copies of the quants, kind::f16 MMA (fp32 I);
+//       OPK 1: the int8 quants themselves, kind::i8 MMA (s32 I) -- half the
+//              operand bytes and half the MMA time, plus one int->float
+//              conversion per element and block in the drain.
+//   * The drain (16 warps, TMEM lane quadrant = warp % 4, column quarter =
+//     warp / 4) applies the scales on the CUDA cores: S = dW * dX and
+//     acc += S * I, two packed fp32 instructions per element pair and
+//     block.  Per block each warp waits for its slot, loads it, frees it and
+//     does the arithmetic; four drain warps per scheduler overlap those
+//     chains (with two, their latency bounded the kernel).  TMEM is read in
+//     the 16x256b layout: each thread holds 4 weight rows x 8 activation
+//     rows, so it reads a quarter of the per-column activation scales that
+//     one row per thread would need from shared memory.
+//   * Scales are fp32 block-major planes ([blocks][rows], the stored fp16
+//     values exactly), loaded by TMA into a ring of their own that the drain
+//     releases, so an operand stage is free as soon as its MMAs are done.
+//   * Tiles are walked in groups of 16 activation-row tiles, so the CTAs
+//     running at the same time share their operand rows in L2.
+//   * Every mbarrier wait is bounded (pxq_device.cuh); no TMA load uses a
+//     cluster multicast, and every CTA loads from this GPU's memory only.
+// The epilogue (bias, TMA-store staging, stores into peers' outputs for the
+// N-sharded path, the gated feed-forward product, the block-dot dump) is
+// the one of gemm.cu for the 32x32b accumulator layout.
+#include "pxq_device.cuh"
+#include "pxq_internal.h"
+
+namespace pxq {
+namespace {
+
+constexpr int Q8_TN = 128;           // weight rows per tile (TMEM lanes)
+constexpr int Q8_TM = 128;           // activation rows per tile (TMEM columns per slot)
+constexpr int Q8_OP_BYTES = 128 * 128;  // one operand per stage: 128 rows x one 128-byte swizzle row
+constexpr int Q8_STAGE = 2 * Q8_OP_BYTES;
+constexpr int Q8_STAGES = 4;
+constexpr int Q8_SLOTS = 4;
+constexpr int Q8_MAX_SD = 8;
+constexpr int Q8_DRAIN_WARPS = 16;   // four per scheduler: the per-block wait/load/release chains overlap
+constexpr int Q8_THREADS = 640;
+constexpr int Q8_PRODUCER_WARP = 16;
+constexpr int Q8_MMA_WARP = 17;
+constexpr int Q8_HC = 32;            // TMEM columns (activation rows) per drain warp
+constexpr int Q8_GROUP_M = 16;       // activation-row tiles per raster group
+constexpr uint32_t Q8_PRODUCER_REGS = 40, Q8_DRAIN_REGS = 104;
+// the split must fit the registers the block launches with (640 x 96)
+static_assert(32 * Q8_DRAIN_WARPS * Q8_DRAIN_REGS + 128 * Q8_PRODUCER_REGS <= Q8_THREADS * 96, "setmaxnreg split");
+
+template <int OPK>
+struct Q8Op;
+template <>
+struct Q8Op<0> {                     // fp16 operands, kind::f16
+    static constexpr int BPS = 2;    // 32-blocks per stage (64 fp16 = 128 bytes)
+    static constexpr int SD = 8;     // scale ring entries
+    static constexpr int MMAS = 2;   // K = 16 per MMA
+    static constexpr int ELEMS = 64; // operand elements per 128-byte row
+};
+template <>
+struct Q8Op<1> {                     // int8 operands, kind::i8
+    static constexpr int BPS = 4;
+    static constexpr int SD = 6;
+    static constexpr int MMAS = 1;   // K = 32 per MMA
+    static constexpr int ELEMS = 128;
+};
+
+template <int OPK>
+__host__ __device__ constexpr int q8_entry_bytes() { return Q8Op<OPK>::BPS * 2 * 128 * 4; }  // dW | dX fp32
+template <int OPK>
+__host__ __device__ constexpr int q8_off_scales() { return Q8_STAGES * Q8_STAGE; }
+template <int OPK>
+__host__ __device__ constexpr int q8_off_staging() { return q8_off_scales<OPK>() + Q8Op<OPK>::SD * q8_entry_bytes<OPK>(); }
+constexpr int Q8_STAGING = Q8_DRAIN_WARPS * Q8_HC * 32 * 4;  // per drain warp [32 activation rows][32 weight rows] fp32
+template <int OPK>
+__host__ __device__ constexpr int q8_off_bar() { return q8_off_staging<OPK>() + Q8_STAGING; }
+// full/empty, scale full/empty, slot full/empty, MMA drain-out, gated hand-over
+constexpr int Q8_NUM_BARS = 2 * Q8_STAGES + 2 * Q8_MAX_SD + 2 * Q8_SLOTS + 1 + 2;
+template <int OPK>
+__host__ __device__ constexpr int q8_smem_bytes() { return q8_off_bar<OPK>() + Q8_NUM_BARS * 8 + 16 + 1024; }
+static_assert(q8_smem_bytes<0>() <= 232448 && q8_smem_bytes<1>() <= 232448, "shared memory");
+static_assert(Q8Op<0>::SD <= Q8_MAX_SD && Q8Op<1>::SD <= Q8_MAX_SD, "scale ring");
+static_assert(Q8_SLOTS * Q8_TM <= 512, "TMEM columns");
+
+struct Q8Params {
+    int64_t M, N, K;
+    int64_t n_first;
+    float* y;
+    int64_t ldy;
+    const float* bias;
+    float* dump;
+    uint32_t* status;
+    int tma_store;
+    int gated;
+    int ndst;
+    int dst_vec4;
+    int64_t col_off;
+    float* ydst[kMaxScatter];
+};
+
+__device__ __forceinline__ void put_y(const Q8Params& p, int64_t m, int64_t n, float v)
+{
+    p.y[m * p.ldy + n] = v;
+    const int64_t off = m * p.ldy + p.col_off + n;
+    for (int k = 0; k < p.ndst; k++) p.ydst[k][off] = v;
+}
+
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) { return smem_desc(saddr, 16, 1024, 2); }
+
+// Tile t -> (activation tile, weight tile): groups of Q8_GROUP_M activation
+// tiles, weight tiles outer within a group.
+__device__ __forceinline__ void q8_tile(int64_t t, int64_t mt, int64_t nt, int64_t& mi, int64_t& ni)
+{
+    const int64_t per_group = (int64_t)Q8_GROUP_M * nt;
+    const int64_t g = t / per_group;
+    const int64_t fm = g * Q8_GROUP_M;
+    const int64_t gm = mt - fm < Q8_GROUP_M ? mt - fm : Q8_GROUP_M;
+    const int64_t r = t - g * per_group;
+    mi = fm + r % gm;
+    ni = r / gm;
+}
+
+// One block's accumulators for a drain warp (its 32 TMEM lanes x 32
+// columns) in the 16x256b layout: two loads, lanes 0-15 (a) and 16-31 (b) of
+// the warp's quadrant.  Thread t holds, per load, r[4k + 2h + c] = lane
+// 8h + t/4, column 8k + 2(t%4) + c (k < 4): 4 weight rows and 8 activation
+// rows in all, so it needs 8 per-column activation scales per block (4x
+// fewer shared-memory reads than one lane x 32 columns).
+struct Blk {
+    uint32_t a[16], b[16];
+};
+__device__ __forceinline__ void q8_ld(Blk& v, uint32_t taddr)
+{
+    tmem_ld16x256_x4(taddr, v.a);
+    tmem_ld16x256_x4(taddr + (16u << 16), v.b);
+}
+// element (lh, k, h, c) of a thread's 32: weight row 16lh + 8h + t/4,
+// activation row 8k + 2(t%4) + c (relative to the warp's quadrant / quarter)
+__host__ __device__ constexpr int q8_idx(int lh, int k, int h, int c) { return ((lh * 4 + k) * 2 + h) * 2 + c; }
+
+template <int OPK>
+__device__ __forceinline__ float q8_val(uint32_t bits)
+{
+    if constexpr (OPK == 1) {
+        return __int2float_rn((int)bits);  // exact: |I| <= 32 * 127 * 127
+    } else {
+        return __uint_as_float(bits);
+    }
+}
+
+// acc += (dx * dw) * I over one load's 16 elements, as packed column pairs:
+// acc2[(lh*4 + k)*2 + h] holds columns (8k + 2(t%4), +1) of weight row
+// 16lh + 8h + t/4.  dx2[k]: the pair's activation scales; dw2[h]: the row's
+// weight scale, duplicated.
+template <int OPK>
+__device__ __forceinline__ void q8_fma_load(float2* acc2, const uint32_t (&v)[16], const float2 (&dx2)[4], const float2 (&dw2)[2])
+{
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const float2 sc = __fmul2_rn(dx2[k], dw2[h]);
+            acc2[k * 2 + h] = __ffma2_rn(sc, make_float2(q8_val<OPK>(v[4 * k + 2 * h]), q8_val<OPK>(v[4 * k + 2 * h + 1])),
+                                         acc2[k * 2 + h]);
+        }
+    }
+}
+
+// tensor maps:
+//   tmW   weight operand [N][K] (fp16 or int8), box {128 bytes, 128 rows}, 128B swizzle
+//   tmX   activation operand [M][K],             box {128 bytes, 128 rows}, 128B swizzle
+//   tmDw  weight block scales fp32 [K/32][ldn],  box {128, BPS}
+//   tmDx  activation block scales fp32 [K/32][ldm], box {128, BPS}
+//   tmY   output fp32 [M][ldy], box {32, 64} (TMA-store epilogue)
+template <int OPK, bool DUMP>
+__global__ void __launch_bounds__(Q8_THREADS, 1)
+    k_gemm_q8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+              const __grid_constant__ CUtensorMap tmDw, const __grid_constant__ CUtensorMap tmDx,
+              const __grid_constant__ CUtensorMap tmY, const Q8Params p)
+{
+    using O = Q8Op<OPK>;
+    constexpr int BPS = O::BPS, SD = O::SD, EB = q8_entry_bytes<OPK>();
+    constexpr uint32_t IDESC = OPK == 1 ? idesc_i8_s32(Q8_TN, Q8_TM) : idesc_f16_f32(Q8_TN, Q8_TM);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + q8_off_bar<OPK>());
+    uint64_t* full = bars;                      // operand stage loaded
+    uint64_t* empty = full + Q8_STAGES;         // operand stage consumed by the MMAs
+    uint64_t* sfull = empty + Q8_STAGES;        // scale entry loaded
+    uint64_t* sempty = sfull + Q8_MAX_SD;       // scale entry read by every drain warp
+    uint64_t* tfull = sempty + Q8_MAX_SD;       // accumulator slot holds a finished block
+    uint64_t* tempty = tfull + Q8_SLOTS;        // accumulator slot read by every drain warp
+    uint64_t* mma_done = tempty + Q8_SLOTS;     // every issued MMA finished (exit path)
+    uint64_t* merge = mma_done + 1;             // gated epilogue hand-over
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Q8_NUM_BARS);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+    uint8_t* scale_ring = smem + q8_off_scales<OPK>();
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < Q8_STAGES; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < Q8_MAX_SD; i++) {
+            mbar_init(&sfull[i], 1);
+            mbar_init(&sempty[i], Q8_DRAIN_WARPS);
+        }
+        for (int i = 0; i < Q8_SLOTS; i++) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], Q8_DRAIN_WARPS);
+        }
+        mbar_init(mma_done, 1);
+        mbar_init(&merge[0], 32 * Q8_DRAIN_WARPS);
+        mbar_init(&merge[1], 32 * Q8_DRAIN_WARPS);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    if (warp == Q8_PRODUCER_WARP && lane == 0) {
+        tma_prefetch_desc(&tmW);
+        tma_prefetch_desc(&tmX);
+        tma_prefetch_desc(&tmDw);
+        tma_prefetch_desc(&tmDx);
+        if (p.tma_store) tma_prefetch_desc(&tmY);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int64_t mt = (p.M + Q8_TM - 1) / Q8_TM;
+    const int64_t nt = (p.N + Q8_TN - 1) / Q8_TN;
+    const int64_t tiles = mt * nt;
+    const int64_t nb = p.K / kQK8_0;
+    const int64_t nstages = (nb + BPS - 1) / BPS;
+    uint32_t* status = p.status;
+
+    if (warp >= Q8_DRAIN_WARPS) {
+        regs_dec<Q8_PRODUCER_REGS>();
+        if (warp == Q8_PRODUCER_WARP && lane == 0) {
+            int stage = 0, se = 0;
+            uint32_t ph = 0, sph = 0;
+            for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+                int64_t mi, ni;
+                q8_tile(tile, mt, nt, mi, ni);
+                const int32_t m0 = (int32_t)(mi * Q8_TM);
+                const int32_t n0 = (int32_t)(p.n_first + ni * Q8_TN);
+                for (int64_t kc = 0; kc < nstages; kc++) {
+                    // the stage's block scales, for the drain
+                    if (!mbar_wait(&sempty[se], sph ^ 1u, abort_flag, status, kDevTimeoutScaleEmpty)) goto done;
+                    uint8_t* e = scale_ring + se * EB;
+                    mbar_expect_tx(&sfull[se], EB);
+                    tma_load_2d(e, &tmDw, &sfull[se], n0, (int32_t)(kc * BPS));
+                    tma_load_2d(e + EB / 2, &tmDx, &sfull[se], m0, (int32_t)(kc * BPS));
+                    if (++se == SD) {
+                        se = 0;
+                        sph ^= 1u;
+                    }
+                    // the stage's operands, for the MMAs
+                    if (!mbar_wait(&empty[stage], ph ^ 1u, abort_flag, status, kDevTimeoutEmpty)) goto done;
+                    uint8_t* st = smem + stage * Q8_STAGE;
+                    mbar_expect_tx(&full[stage], Q8_STAGE);
+                    const int32_t kx = (int32_t)(kc * O::ELEMS);
+                    tma_load_2d(st, &tmW, &full[stage], kx, n0);
+                    tma_load_2d(st + Q8_OP_BYTES, &tmX, &full[stage], kx, m0);
+                    if (++stage == Q8_STAGES) {
+                        stage = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+        } else if (warp == Q8_MMA_WARP && lane == 0) {
+            int stage = 0, slot = 0;
+            uint32_t ph = 0, tph = 0;
+            for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+                for (int64_t kc = 0; kc < nstages; kc++) {
+                    if (!mbar_wait(&full[stage], ph, abort_flag, status, kDevTimeoutFull)) goto done;
+                    tc_fence_after();
+                    const uint32_t w_addr = smem_u32(smem + stage * Q8_STAGE);
+                    const uint32_t x_addr = w_addr + Q8_OP_BYTES;
+#pragma unroll
+                    for (int bi = 0; bi < BPS; bi++) {
+                        if (kc * BPS + bi >= nb) break;
+                        if (!mbar_wait(&tempty[slot], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
+                        tc_fence_after();
+                        const uint32_t d = tmem_base + (uint32_t)(slot * Q8_TM);
+#pragma unroll
+                        for (int k = 0; k < O::MMAS; k++) {
+                            const uint32_t koff = (uint32_t)(bi * O::MMAS + k) * 32u;  // 32 bytes of K per MMA
+                            if constexpr (OPK == 1)
+                                mma_i8(d, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC, (uint32_t)k);
+                            else
+                                mma_f16(d, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC, (uint32_t)k);
+                        }
+                        mma_commit(&tfull[slot]);
+                        if (++slot == Q8_SLOTS) {
+                            slot = 0;
+                            tph ^= 1u;
+                        }
+                    }
+                    mma_commit(&empty[stage]);
+                    if (++stage == Q8_STAGES) {
+                        stage = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+        }
+    } else {
+        // ------------------------------------------------------ drain warps --
+        regs_inc<Q8_DRAIN_REGS>();
+        const uint32_t quad = warp & 3u, quarter = warp >> 2;
+        const uint32_t lane_base = (quad * 32u) << 16;
+        const uint32_t col0 = quarter * Q8_HC;
+        const uint32_t tr = lane >> 2, tc = 2u * (lane & 3u);  // this thread's row in an 8-row group, column pair
+        int slot = 0, se = 0;
+        uint32_t tph = 0, sph = 0, mgph = 0;
+        auto drain_meet = [&](int i) -> bool {
+            mbar_arrive(&merge[i]);
+            return mbar_wait(&merge[i], mgph, abort_flag, status, kDevTimeoutTmemFull);
+        };
+        for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+            int64_t mi, ni;
+            q8_tile(tile, mt, nt, mi, ni);
+            const int64_t m0 = mi * Q8_TM;
+            const int64_t n0 = ni * Q8_TN;  // view-local
+            const int64_t nq = n0 + quad * 32u;  // the warp's first weight row
+            const int64_t mfirst = m0 + col0;
+            float2 acc2[Q8_HC / 2];
+#pragma unroll
+            for (int i = 0; i < Q8_HC / 2; i++) acc2[i] = make_float2(0.f, 0.f);
+            for (int64_t b = 0; b < nb; b++) {
+                const int bi = (int)(b % BPS);
+                if (bi == 0 && !mbar_wait(&sfull[se], sph, abort_flag, status, kDevTimeoutScaleFull)) goto done;
+                if (!mbar_wait(&tfull[slot], tph, abort_flag, status, kDevTimeoutTmemFull)) goto done;
+                tc_fence_after();
+                Blk v;
+                q8_ld(v, tmem_base + lane_base + (uint32_t)(slot * Q8_TM) + col0);
+                // the scales while the accumulators load
+                const float* e = reinterpret_cast<const float*>(scale_ring + se * EB);
+                const float* dw = e + bi * 128 + quad * 32u + tr;
+                const float* dx = e + BPS * 128 + bi * 128 + col0 + tc;
+                float2 dx2[4];
+#pragma unroll
+                for (int k = 0; k < 4; k++) dx2[k] = *reinterpret_cast<const float2*>(dx + 8 * k);
+                const float2 dwa[2] = {make_float2(dw[0], dw[0]), make_float2(dw[8], dw[8])};
+                const float2 dwb[2] = {make_float2(dw[16], dw[16]), make_float2(dw[24], dw[24])};
+                tmem_ld_wait();
+                // the slot is free once its values are in registers
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[slot]);
+                if (++slot == Q8_SLOTS) {
+                    slot = 0;
+                    tph ^= 1u;
+                }
+                if (bi == BPS - 1 || b + 1 == nb) {
+                    if (lane == 0) mbar_arrive(&sempty[se]);
+                    if (++se == SD) {
+                        se = 0;
+                        sph ^= 1u;
+                    }
+                }
+                if constexpr (DUMP) {
+#pragma unroll
+                    for (int lh = 0; lh < 2; lh++)
+#pragma unroll
+                        for (int k = 0; k < 4; k++)
+#pragma unroll
+                            for (int h = 0; h < 2; h++)
+#pragma unroll
+                                for (int c = 0; c < 2; c++) {
+                                    const int64_t n = nq + 16 * lh + 8 * h + tr, m = mfirst + 8 * k + tc + c;
+                                    const uint32_t bits = lh ? v.b[4 * k + 2 * h + c] : v.a[4 * k + 2 * h + c];
+                                    if (n < p.N && m < p.M) p.dump[(b * p.M + m) * p.N + n] = q8_val<OPK>(bits);
+                                }
+                } else {
+                    q8_fma_load<OPK>(acc2, v.a, dx2, dwa);
+                    q8_fma_load<OPK>(acc2 + 8, v.b, dx2, dwb);
+                }
+            }
+            if constexpr (!DUMP) {
+                float acc[Q8_HC];
+#pragma unroll
+                for (int i = 0; i < Q8_HC / 2; i++) {
+                    acc[2 * i] = acc2[i].x;
+                    acc[2 * i + 1] = acc2[i].y;
+                }
+                if (p.gated) {
+                    // gated weight: lanes 64..127 hold the up projections of the
+                    // outputs whose gate projections lanes 0..63 hold (the repack
+                    // interleaves 64-row groups); the up warps hand their sums over
+                    // through the staging buffer and the gate warps finish
+                    // tensor_silu + tensor_gate (src/tensor.cpp:199-208, :334-345)
+                    float* xfer = reinterpret_cast<float*>(smem + q8_off_staging<OPK>()) + ((quad & 1) * 4 + quarter) * (Q8_HC * 32);
+                    if (!drain_meet(0)) goto done;
+                    if (quad >= 2) {
+#pragma unroll
+                        for (int i = 0; i < Q8_HC; i++) xfer[i * 32 + lane] = acc[i];
+                    }
+                    if (!drain_meet(1)) goto done;
+                    mgph ^= 1u;
+                    if (quad < 2) {
+#pragma unroll
+                        for (int lh = 0; lh < 2; lh++)
+#pragma unroll
+                            for (int k = 0; k < 4; k++)
+#pragma unroll
+                                for (int h = 0; h < 2; h++)
+#pragma unroll
+                                    for (int c = 0; c < 2; c++) {
+                                        const int i = q8_idx(lh, k, h, c);
+                                        const int64_t on = n0 / 2 + quad * 32 + 16 * lh + 8 * h + tr, m = mfirst + 8 * k + tc + c;
+                                        const float g = acc[i], u = xfer[i * 32 + lane];
+                                        if (on < p.N / 2 && m < p.M)
+                                            p.y[m * p.ldy + on] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+                                    }
+                    }
+                    continue;
+                }
+                // bias of the thread's weight rows 8i + t/4 of the quadrant
+                float bv[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int64_t nn = nq + 8 * i + tr;
+                    bv[i] = (p.bias && nn < p.N) ? p.bias[nn] : 0.f;
+                }
+                if (p.tma_store) {
+                    // stage [32 activation rows][32 weight rows] and store it with one
+                    // TMA store; lane 0 first waits until the warp's previous store
+                    // has finished reading the buffer
+                    float* stg = reinterpret_cast<float*>(smem + q8_off_staging<OPK>()) + warp * (Q8_HC * 32);
+                    if (lane == 0) bulk_wait_read_all();
+                    __syncwarp();
+#pragma unroll
+                    for (int lh = 0; lh < 2; lh++)
+#pragma unroll
+                        for (int k = 0; k < 4; k++)
+#pragma unroll
+                            for (int h = 0; h < 2; h++)
+#pragma unroll
+                                for (int c = 0; c < 2; c++) {
+                                    const float v = acc[q8_idx(lh, k, h, c)];
+                                    stg[(8 * k + tc + c) * 32 + 16 * lh + 8 * h + tr] = p.bias ? __fadd_rn(v, bv[2 * lh + h]) : v;
+                                }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmY, stg, (int32_t)nq, (int32_t)mfirst);
+                        bulk_commit();
+                    }
+                    if (p.ndst && p.dst_vec4) {
+                        // the peers' copies from the same staged block, 4 floats a lane
+                        const int jr = lane >> 3, c4 = 4 * (lane & 7);
+                        const int64_t nn = nq + c4;
+                        for (int j = jr; j < Q8_HC; j += 4) {
+                            const int64_t m = mfirst + j;
+                            if (m >= p.M) break;
+                            const float4 v = *reinterpret_cast<const float4*>(stg + j * 32 + c4);
+                            const int64_t off = m * p.ldy + p.col_off + nn;
+                            if (nn + 3 < p.N) {
+                                for (int k = 0; k < p.ndst; k++) *reinterpret_cast<float4*>(p.ydst[k] + off) = v;
+                            } else {
+                                const float vs[4] = {v.x, v.y, v.z, v.w};
+                                for (int q = 0; q < 4 && nn + q < p.N; q++)
+                                    for (int k = 0; k < p.ndst; k++) p.ydst[k][off + q] = vs[q];
+                            }
+                        }
+                    } else if (p.ndst) {
+                        const int64_t nn = nq + lane;
+                        if (nn < p.N) {
+                            for (int j = 0; j < Q8_HC; j++) {
+                                const int64_t m = mfirst + j;
+                                if (m >= p.M) break;
+                                const float v = stg[j * 32 + lane];
+                                const int64_t off = m * p.ldy + p.col_off + nn;
+                                for (int k = 0; k < p.ndst; k++) p.ydst[k][off] = v;
+                            }
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int lh = 0; lh < 2; lh++)
+#pragma unroll
+                        for (int k = 0; k < 4; k++)
+#pragma unroll
+                            for (int h = 0; h < 2; h++)
+#pragma unroll
+                                for (int c = 0; c < 2; c++) {
+                                    const int64_t nn = nq + 16 * lh + 8 * h + tr, m = mfirst + 8 * k + tc + c;
+                                    const float v = acc[q8_idx(lh, k, h, c)];
+                                    if (nn < p.N && m < p.M) put_y(p, m, nn, p.bias ? __fadd_rn(v, bv[2 * lh + h]) : v);
+                                }
+                }
+            }
+        }
+    }
+done:
+    if (p.tma_store && warp < Q8_DRAIN_WARPS && lane == 0) bulk_wait_all();
+    // peer stores are visible system-wide before the kernel ends (the
+    // N-sharded path's barrier after the kernel then orders them for the peers)
+    if (p.ndst && warp < Q8_DRAIN_WARPS) __threadfence_system();
+    if (warp == Q8_MMA_WARP && lane == 0) {
+        // no MMA may still be writing TMEM when it is freed (after a normal run
+        // the drain has consumed every result; this covers aborts)
+        mma_commit(mma_done);
+        const uint64_t t0 = global_ns();
+        while (!mbar_try_wait(mma_done, 0) && global_ns() - t0 < PXQ_WAIT_NS) {
+        }
+    }
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(tmem_base, 512);
+}
+
+template <int OPK, bool DUMP>
+cudaError_t launch_q8_typed(const GemmOperands& op, int num_sms, cudaStream_t s)
+{
+    auto kern = k_gemm_q8<OPK, DUMP>;
+    constexpr int smem = q8_smem_bytes<OPK>();
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    const int64_t tiles = ((op.M + Q8_TM - 1) / Q8_TM) * ((op.N + Q8_TN - 1) / Q8_TN);
+    int64_t grid = num_sms;
+    if (tiles < grid) grid = tiles;
+    if (grid < 1) grid = 1;
+    Q8Params p{op.M, op.N, op.K, op.n_first, op.y, op.ldy, op.bias, op.dump, op.status, (op.tma_store && !DUMP) ? 1 : 0,
+               op.gated, op.ndst, op.dst_vec4, op.col_off, {}};
+    for (int k = 0; k < kMaxScatter; k++) p.ydst[k] = op.ydst[k];
+    kern<<<(unsigned)grid, Q8_THREADS, smem, s>>>(op.tm[0], op.tm[1], op.tm[4], op.tm[6], op.tm_y, p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_q8(const GemmOperands& op, int num_sms, cudaStream_t s)
+{
+    if (op.q8_int8)
+        return op.dump ? launch_q8_typed<1, true>(op, num_sms, s) : launch_q8_typed<1, false>(op, num_sms, s);
+    return op.dump ? launch_q8_typed<0, true>(op, num_sms, s) : launch_q8_typed<0, false>(op, num_sms, s);
+}
+
+int gemm_q8_operand_elems(int int8_operands) { return int8_operands ? Q8Op<1>::ELEMS : Q8Op<0>::ELEMS; }
+int gemm_q8_scale_box(int int8_operands) { return int8_operands ? Q8Op<1>::BPS : Q8Op<0>::BPS; }
+
+}  // namespace pxq

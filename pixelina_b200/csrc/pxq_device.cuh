@@ -261,27 +261,19 @@ __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wa
 __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // Two fp32 FMAs / products in one packed instruction (sm_100a), each rounded
-// to nearest exactly like __fmaf_rn / __fmul_rn.
+// to nearest exactly like __fmaf_rn / __fmul_rn.  The compiler builtins let
+// the register allocator keep each pair in an aligned register pair.
 __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1)
 {
-    asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
-        "mov.b64 ra, {%2, %3};\n\t"
-        "mov.b64 rb, {%4, %5};\n\t"
-        "mov.b64 rc, {%0, %1};\n\t"
-        "fma.rn.f32x2 rc, ra, rb, rc;\n\t"
-        "mov.b64 {%0, %1}, rc;\n\t}"
-        : "+f"(d0), "+f"(d1)
-        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+    const float2 r = __ffma2_rn(make_float2(a0, a1), make_float2(b0, b1), make_float2(d0, d1));
+    d0 = r.x;
+    d1 = r.y;
 }
 __device__ __forceinline__ void fmul2(float& d0, float& d1, float a0, float a1, float b0, float b1)
 {
-    asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
-        "mov.b64 ra, {%2, %3};\n\t"
-        "mov.b64 rb, {%4, %5};\n\t"
-        "mul.rn.f32x2 rc, ra, rb;\n\t"
-        "mov.b64 {%0, %1}, rc;\n\t}"
-        : "=f"(d0), "=f"(d1)
-        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+    const float2 r = __fmul2_rn(make_float2(a0, a1), make_float2(b0, b1));
+    d0 = r.x;
+    d1 = r.y;
 }
 
 // Plain (coherent) global loads for data that an earlier kernel of the stream
@@ -363,6 +355,18 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_
         : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::i8 (signed 8-bit inputs, exact
+// signed 32-bit accumulate).
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrive once on `bar` when all previously issued MMAs of this thread finish.
 __device__ __forceinline__ void mma_commit(uint64_t* bar)
 {
@@ -433,6 +437,17 @@ __device__ __forceinline__ void tmem_ld16x256_x8(uint32_t taddr, uint32_t (&r)[3
         : "r"(taddr));
 }
 
+// 16 lanes x 32 columns: the .x4 form of tmem_ld16x256_x8 (k = 0..3).
+__device__ __forceinline__ void tmem_ld16x256_x4(uint32_t taddr, uint32_t (&r)[16])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.16x256b.x4.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
 // 32 lanes x 16 consecutive 32-bit columns.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16])
 {
@@ -474,6 +489,16 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t m, uint32_t n)
     return (1u << 4)              // D format: f32
            | (0u << 7)            // A format: f16
            | (0u << 10)           // B format: f16
+           | ((n >> 3) << 17)     // N / 8
+           | ((m >> 4) << 24);    // M / 16
+}
+
+// Instruction descriptor for kind::i8 with signed 8-bit A/B, s32 D, both K-major.
+__host__ __device__ constexpr uint32_t idesc_i8_s32(uint32_t m, uint32_t n)
+{
+    return (2u << 4)              // D format: s32
+           | (1u << 7)            // A format: signed 8-bit
+           | (1u << 10)           // B format: signed 8-bit
            | ((n >> 3) << 17)     // N / 8
            | ((m >> 4) << 24);    // M / 16
 }

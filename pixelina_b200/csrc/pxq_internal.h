@@ -24,13 +24,15 @@ constexpr uint32_t kTypeQ6_K = 14;
 cudaError_t launch_quantize_q8_0_blocks(const float* x, void* y, int64_t rows, int64_t inner, int64_t ldx, cudaStream_t s);
 cudaError_t launch_quantize_q8_K_blocks(const float* x, void* y, int64_t rows, int64_t inner, int64_t ldx, cudaStream_t s);
 // Tensor-core operand formats for the GEMM (same rounding, different layout):
-//   xq  fp16 [rows][inner]: the int8 quants as exact fp16 values
-//   Q8_0: dx16 fp16 [rows][ldd]: the stored fp16 block scales, row-major
-//   Q8_K: dxT fp32 [inner/256][ldd]: per-block scale, block-major
+//   Q8_0: xq [rows][inner]: the int8 quants themselves (int8_operands) or as
+//         exact fp16 values; dxT fp32 [inner/32][ldd]: the stored fp16 block
+//         scales as fp32, block-major
+//   Q8_K: xq fp16 [rows][inner]: the int8 quants as exact fp16 values
+//         dxT fp32 [inner/256][ldd]: per-block scale, block-major
 //         amin fp16 [rows][inner/256*16]: split 32-element sums for the Q5_K
 //         min term, (hi_j, lo_j) with bsum2_j = 64*hi_j + lo_j
-cudaError_t launch_quantize_q8_0_operand(const float* x, __half* xq, __half* dx16, int64_t rows, int64_t inner, int64_t ldx,
-                                         int64_t ldd, cudaStream_t s);
+cudaError_t launch_quantize_q8_0_operand(const float* x, void* xq, float* dxT, int int8_operands, int64_t rows, int64_t inner,
+                                         int64_t ldx, int64_t ldd, cudaStream_t s);
 cudaError_t launch_quantize_q8_K_operand(const float* x, __half* xq, float* dxT, __half* amin, int64_t rows, int64_t inner,
                                          int64_t ldx, int64_t ldd, cudaStream_t s);
 
@@ -41,8 +43,10 @@ cudaError_t launch_pad_q6_K(const void* src, void* dst, int64_t superblocks, cud
 // One-time weight repack into the GEMM operand layout (bit-exact unpack).
 // gate_rows = F > 0: a gated weight (F gate rows, then F up rows) packed as
 // 128-row groups [64 gate rows j..j+63][the 64 matching up rows].
-cudaError_t launch_repack_q8_0(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wq, __half* ws1h,
-                               int64_t gate_rows, cudaStream_t s);
+// Q8_0: wq [rows][inner] int8 quants (int8_operands) or their exact fp16
+// values; dT fp32 [inner/32][ldn] the fp16 block scales, block-major.
+cudaError_t launch_repack_q8_0(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, void* wq, float* dT,
+                               int64_t ldn, int int8_operands, int64_t gate_rows, cudaStream_t s);
 cudaError_t launch_repack_q5_K(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wv, float* dT,
                                float* dminT, __half* bmin, int64_t ldn, int64_t gate_rows, cudaStream_t s);
 // Q6_K: raw rows are the device's padded super-blocks (stride bytes per row).
@@ -161,12 +165,14 @@ constexpr int kMaxScatter = 8;  // destinations of a scattering GEMM (one per ra
 
 struct GemmOperands {
     uint32_t type;        // kTypeQ8_0, kTypeQ5_K or kTypeQ6_K
+    int q8_int8;          // Q8_0: int8 operands and kind::i8 MMA (else fp16 operands, kind::f16)
     int64_t M, N, K;      // activation rows, view rows (output columns), inner
     int64_t n_first;      // first weight row of the view (multiple of 4)
-    // tensor maps (boxes as listed in gemm.cu): 0 weight operand, 1 activation operand, 2 weight scale
-    // tile (Q8_0 one-hot scales / Q5_K min operand), 3 activation scale tile
-    // (Q8_0 fp16 scales / Q8_K min operand), 4 K-quant weight d, 5 Q5_K
-    // weight dmin, 6 Q8_K activation d (unused entries may hold any valid map)
+    // tensor maps (boxes as listed in gemm.cu and gemm_q8.cu): 0 weight
+    // operand, 1 activation operand, 2 Q5_K weight min operand, 3 Q8_K
+    // activation min operand, 4 weight block scales (Q8_0 d / K-quant d),
+    // 5 Q5_K weight dmin, 6 activation block scales (unused entries may hold
+    // any valid map)
     CUtensorMap tm[7];
     CUtensorMap tm_y;     // output map (fp32 [M][ldy], box {32, gemm_store_rows}) when tma_store
     int tma_store;        // 1: write the output tile with TMA stores
@@ -191,5 +197,12 @@ int gemm_tile_activation_rows(uint32_t type);
 // 0 when the type's epilogue stores directly.
 int gemm_store_rows(uint32_t type);
 cudaError_t launch_gemm(const GemmOperands& op, int num_sms, cudaStream_t s);
+
+// ---- gemm_q8.cu -------------------------------------------------------------
+// The Q8_0 GEMM (called by launch_gemm).  Operand elements per 128-byte TMA
+// box row (64 fp16 or 128 int8) and 32-blocks per scale box (2 or 4).
+cudaError_t launch_gemm_q8(const GemmOperands& op, int num_sms, cudaStream_t s);
+int gemm_q8_operand_elems(int int8_operands);
+int gemm_q8_scale_box(int int8_operands);
 
 }  // namespace pxq

@@ -7,8 +7,8 @@
 // reference produces, checked by the parity tests; the Q8_0 matvec reads it
 // too), the Q8_K matvec operand (the same bytes permuted for the matvec's
 // fragments, plus 32-element sums), and the tensor-core operand layout used
-// by the GEMM (exact fp16 copies of the int8 quants plus block-major scale
-// planes).  All layouts come from the same arithmetic.
+// by the GEMM (the int8 quants, or exact fp16 copies of them, plus
+// block-major scale planes).  All layouts come from the same arithmetic.
 //
 // Bit-exactness rules (all arithmetic uses explicit _rn intrinsics so that
 // nvcc's default FMA contraction cannot change a rounding):
@@ -107,8 +107,11 @@ __global__ void k_quantize_q8_0_blocks(const float* x, uint8_t* __restrict__ y, 
     }
 }
 
-__global__ void k_quantize_q8_0_operand(const float* __restrict__ x, __half* __restrict__ xq, __half* __restrict__ dx16,
-                                        int64_t rows, int64_t inner, int64_t ldx, int64_t ldd)
+// GEMM operand: the quants as int8 (int8_operands) or exact fp16 values,
+// [rows][inner], and the stored fp16 block scales as fp32, block-major
+// [inner/32][ldd].
+__global__ void k_quantize_q8_0_operand(const float* __restrict__ x, void* __restrict__ xq, float* __restrict__ dxT,
+                                        int int8_operands, int64_t rows, int64_t inner, int64_t ldx, int64_t ldd)
 {
     const int64_t quads_per_row = inner / 4;
     const int64_t total = rows * quads_per_row;
@@ -122,13 +125,17 @@ __global__ void k_quantize_q8_0_operand(const float* __restrict__ x, __half* __r
         if (live) v = ld_dep_f4(x + row * ldx + quad * 4);
         const Q80Part p = q8_0_part(v);
         if (!live) continue;
-        __half2 h01 = __halves2half2(__int2half_rn(p.q[0]), __int2half_rn(p.q[1]));
-        __half2 h23 = __halves2half2(__int2half_rn(p.q[2]), __int2half_rn(p.q[3]));
-        uint2 packed;
-        packed.x = *reinterpret_cast<uint32_t*>(&h01);
-        packed.y = *reinterpret_cast<uint32_t*>(&h23);
-        *reinterpret_cast<uint2*>(xq + row * inner + quad * 4) = packed;
-        if ((quad & 7) == 0) dx16[row * ldd + quad / 8] = p.d16;
+        if (int8_operands) {
+            reinterpret_cast<uint32_t*>(static_cast<int8_t*>(xq) + row * inner)[quad] = p.packed;
+        } else {
+            __half2 h01 = __halves2half2(__int2half_rn(p.q[0]), __int2half_rn(p.q[1]));
+            __half2 h23 = __halves2half2(__int2half_rn(p.q[2]), __int2half_rn(p.q[3]));
+            uint2 packed;
+            packed.x = *reinterpret_cast<uint32_t*>(&h01);
+            packed.y = *reinterpret_cast<uint32_t*>(&h23);
+            *reinterpret_cast<uint2*>(static_cast<__half*>(xq) + row * inner + quad * 4) = packed;
+        }
+        if ((quad & 7) == 0) dxT[(quad / 8) * ldd + row] = __half2float(p.d16);
     }
 }
 
@@ -289,11 +296,12 @@ cudaError_t launch_quantize_q8_K_blocks(const float* x, void* y, int64_t rows, i
     return cudaGetLastError();
 }
 
-cudaError_t launch_quantize_q8_0_operand(const float* x, __half* xq, __half* dx16, int64_t rows, int64_t inner, int64_t ldx,
-                                         int64_t ldd, cudaStream_t s)
+cudaError_t launch_quantize_q8_0_operand(const float* x, void* xq, float* dxT, int int8_operands, int64_t rows, int64_t inner,
+                                         int64_t ldx, int64_t ldd, cudaStream_t s)
 {
     const int threads = 256;
-    k_quantize_q8_0_operand<<<grid_for(rows * inner / 4, threads), threads, 0, s>>>(x, xq, dx16, rows, inner, ldx, ldd);
+    k_quantize_q8_0_operand<<<grid_for(rows * inner / 4, threads), threads, 0, s>>>(x, xq, dxT, int8_operands, rows, inner, ldx,
+                                                                                    ldd);
     return cudaGetLastError();
 }
 

@@ -4,10 +4,9 @@
 //     done when a weight is first used by the GEMM and then cached with it
 //     (the device-side counterpart of the Vulkan backend's upload cache,
 //     src/backend_vulkan.cpp:742-758):
-//       Q8_0: wq   fp16 [rows][inner]   = the int8 quants, exactly
-//             ws1h fp16 [rows][inner/32*16]: for block b a 16-wide group holding
-//                  the block's fp16 scale at position b%16 and zeros elsewhere
-//                  (the weight side of the tensor-core scale product)
+//       Q8_0: wq   [rows][inner] = the int8 quants, as stored (int8
+//                  operands) or as exact fp16 values
+//             dT   fp32 [inner/32][ldn] = the fp16 block scales, block-major
 //       Q5_K: wv   fp16 [rows][inner]   = sc_g * q5 (<= 63*31 = 1953, exact)
 //             dT, dminT fp32 [inner/256][ldn]
 //             bmin fp16 [rows][inner/256*16] = (64*m_g, m_g) pairs, the weight
@@ -55,27 +54,34 @@ __device__ __forceinline__ int64_t src_row(int64_t r, int64_t gate_rows)
     return q < 64 ? 64 * j + q : gate_rows + 64 * j + (q - 64);
 }
 
+// One thread per (row, 32-block): the block's 32 quants into the operand row
+// (int8 as stored, or their exact fp16 values) and its fp16 scale, as fp32,
+// into the block-major scale plane.
 __global__ void k_repack_q8_0(const uint8_t* __restrict__ raw, int64_t rows, int64_t inner, int64_t stride,
-                              __half* __restrict__ wq, __half* __restrict__ ws1h, int64_t gate_rows)
+                              void* __restrict__ wq, float* __restrict__ dT, int64_t ldn, int int8_operands, int64_t gate_rows)
 {
     const int64_t nb = inner / kQK8_0;
     const int64_t total = rows * nb;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = i / nb, b = i % nb;
         const uint8_t* blk = raw + src_row(r, gate_rows) * stride + b * kQ8_0Bytes;
-        __half h[32];
+        if (int8_operands) {
+            // qs start at byte 2 of the 34-byte block: 2-byte aligned loads
+            uint16_t q[16];
 #pragma unroll
-        for (int j = 0; j < 32; j++) h[j] = __int2half_rn((int)(int8_t)blk[2 + j]);
-        uint4* dst = reinterpret_cast<uint4*>(wq + r * inner + b * kQK8_0);
+            for (int j = 0; j < 16; j++) q[j] = reinterpret_cast<const uint16_t*>(blk + 2)[j];
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<int8_t*>(wq) + r * inner + b * kQK8_0);
+            dst[0] = reinterpret_cast<uint4*>(q)[0];
+            dst[1] = reinterpret_cast<uint4*>(q)[1];
+        } else {
+            __half h[32];
 #pragma unroll
-        for (int j = 0; j < 4; j++) dst[j] = reinterpret_cast<uint4*>(h)[j];
-        __half g[16];
+            for (int j = 0; j < 32; j++) h[j] = __int2half_rn((int)(int8_t)blk[2 + j]);
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(wq) + r * inner + b * kQK8_0);
 #pragma unroll
-        for (int j = 0; j < 16; j++) g[j] = __ushort_as_half((unsigned short)0);
-        g[b % 16] = __ushort_as_half((unsigned short)((uint16_t)blk[0] | ((uint16_t)blk[1] << 8)));
-        uint4* gd = reinterpret_cast<uint4*>(ws1h + (r * nb + b) * 16);
-        gd[0] = reinterpret_cast<uint4*>(g)[0];
-        gd[1] = reinterpret_cast<uint4*>(g)[1];
+            for (int j = 0; j < 4; j++) dst[j] = reinterpret_cast<uint4*>(h)[j];
+        }
+        dT[b * ldn + r] = load_half(blk);
     }
 }
 
@@ -192,10 +198,11 @@ int grid_for(int64_t work, int threads)
 
 }  // namespace
 
-cudaError_t launch_repack_q8_0(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wq, __half* ws1h,
-                               int64_t gate_rows, cudaStream_t s)
+cudaError_t launch_repack_q8_0(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, void* wq, float* dT,
+                               int64_t ldn, int int8_operands, int64_t gate_rows, cudaStream_t s)
 {
-    k_repack_q8_0<<<grid_for(rows * (inner / kQK8_0), 256), 256, 0, s>>>(raw, rows, inner, stride, wq, ws1h, gate_rows);
+    k_repack_q8_0<<<grid_for(rows * (inner / kQK8_0), 256), 256, 0, s>>>(raw, rows, inner, stride, wq, dT, ldn, int8_operands,
+                                                                          gate_rows);
     return cudaGetLastError();
 }
 

@@ -35,6 +35,9 @@ ERR_CUDA = 3
 ERR_NO_MEMORY = 4
 ERR_NO_DEVICE = 5
 ERR_DEVICE_STATUS = 6
+ERR_IO = 7
+ERR_FORMAT = 8
+ERR_TIMEOUT = 9
 
 TYPE_Q8_0 = 8
 TYPE_Q5_K = 13
@@ -78,6 +81,16 @@ SIGNATURES = {
     "pxq_activation_release": (_i, [_vp, _vp]),
     "pxq_kernel_launches": (_u64, []),
     "pxq_matvec_noalloc": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _sz, _vp, _vp]),
+    "pxq_comm_unique_id": (_i, [_vp]),
+    "pxq_comm_init": (_i, [_vp, _i, _i, _i, C.POINTER(_vp)]),
+    "pxq_comm_size": (_i, [_vp, C.POINTER(_i), C.POINTER(_i)]),
+    "pxq_comm_barrier": (_i, [_vp]),
+    "pxq_comm_synchronize": (_i, [_vp, _vp]),
+    "pxq_comm_destroy": (_i, [_vp]),
+    "pxq_sharded_output_create": (_i, [_vp, _sz, _sz, C.POINTER(_vp), C.POINTER(_vp)]),
+    "pxq_sharded_output_destroy": (_i, [_vp]),
+    "pxq_sharded_matmul": (_i, [_vp, _vp, _sz, _vp, _sz, _vp, _vp, _sz, _vp]),
+    "pxq_sharded_matmul_host": (_i, [_vp, _vp, _sz, _vp, _sz, _sz, _vp]),
     "pxq_attention": (_i, [_vp, _sz, _vp, _vp, _sz, _sz, _sz, _sz, _vp, _sz, _sz, _vp, _vp]),
     "pxq_gguf_open": (_i, [C.c_char_p, C.POINTER(_vp)]),
     "pxq_gguf_close": (_i, [_vp]),
@@ -89,10 +102,6 @@ SIGNATURES = {
     "pxq_gguf_upload": (_i, [_vp, C.c_char_p, _sz, _sz, C.POINTER(_vp)]),
     "pxq_gguf_upload_gated": (_i, [_vp, C.c_char_p, _sz, C.c_char_p, _sz, _sz, C.POINTER(_vp)]),
 }
-
-
-ERR_IO = 7
-ERR_FORMAT = 8
 
 
 class GGUFTensor(C.Structure):

@@ -1,30 +1,33 @@
-"""N-sharded quantized matmul over the ranks of one node.
+"""N-sharded quantized matmul over the ranks of one node (Python side of the
+C ABI's pxq_comm_* / pxq_sharded_* entry points, include/pxq.h).
 
 Every output column n of ``cpu_quant_matmul`` (one weight row) is independent
 of the others (src/kernels_quant.cpp:390-397), so the weight rows split
 across G ranks: rank r holds rows [r*N/G, (r+1)*N/G) and computes
-Y[:, shard] for all M activation rows, an all-gather collects the G blocks
-[G][M][N/G], and one CUDA re-layout (``pxq.gather_shards``) produces the
-caller's row-major Y[M][N] (``output[c*rows + r]``, src/kernels_quant.cpp:398).
-Each rank quantizes the replicated activation itself; the quantized bytes
-are identical on every rank, so the gathered Y is bit-identical to a 1-GPU
-run.
+Y[:, shard] for all M activation rows.  libpxq assembles the row-major
+Y[M][N] (``output[c*rows + r]``, src/kernels_quant.cpp:398) on every rank,
+either fused -- each rank's GEMM epilogue stores its columns into every
+rank's output over NVLink (``ShardedOutput``) -- or through an NCCL
+all-gather and one re-layout kernel.  Each rank quantizes the replicated
+activation itself; the quantized bytes are identical on every rank, so Y is
+bit-identical to a 1-GPU run.
 
-Two ways to assemble Y: ``sharded_matmul`` (local matmul, NCCL all-gather,
-re-layout) and ``sharded_matmul_p2p`` (one kernel per rank: the GEMM epilogue
-stores each output tile straight into every rank's Y through CUDA IPC
-mappings over NVLink, so the transfer overlaps the next tiles' math and no
-all-gather or re-layout pass remains).  Rank synchronisation goes through
-``torch.distributed`` (NCCL on GPUs).
+The communicator (NCCL inside libpxq) needs its 128-byte id on every rank;
+``Comm`` takes it from rank 0 through a ``torch.distributed`` broadcast, or
+from the caller.  Every wait is bounded by the communicator's timeout.
 """
 from __future__ import annotations
+
+import ctypes as C
+
+COMM_ID_BYTES = 128
 
 
 def shard_rows(rows: int, world: int, rank: int) -> tuple[int, int]:
     """(first row, row count) of ``rank``'s contiguous shard of ``rows``.
 
-    The split is even: all-gather needs equal blocks, so ``rows`` must be a
-    multiple of ``world`` (BASELINE's sharded shapes are: 12288/8 = 1536).
+    The split is even (every rank's block has the same shape), so ``rows``
+    must be a multiple of ``world`` (BASELINE's sharded shapes are: 12288/8 = 1536).
     """
     if world < 1 or not 0 <= rank < world:
         raise ValueError(f"rank {rank} outside world of size {world}")
@@ -36,9 +39,55 @@ def shard_rows(rows: int, world: int, rank: int) -> tuple[int, int]:
 
 def gathered_layout(gathered, world: int, columns: int, shard: int):
     """The [G][M][N/G] all-gather result viewed as row-major [M][N], as a
-    strided view (no copy); ``pxq.gather_shards`` writes the same layout
+    strided view (no copy); ``pxq_gather_shards`` writes the same layout
     densely on the GPU."""
     return gathered.view(world, columns, shard).permute(1, 0, 2).reshape(columns, world * shard)
+
+
+class Comm:
+    """pxq_comm: this rank's member of a node-wide communicator.
+
+    ``comm_id``: the id bytes from ``unique_id()`` on one rank; ``None`` takes
+    it from rank 0 of the default ``torch.distributed`` group (collective)."""
+
+    def __init__(self, world: int, rank: int, comm_id: bytes | None = None, timeout_ms: int = 60000):
+        from . import pxq
+
+        if comm_id is None:
+            import torch.distributed as dist
+
+            box = [unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(box, src=0)
+            comm_id = box[0]
+        buf = (C.c_uint8 * COMM_ID_BYTES).from_buffer_copy(comm_id)
+        h = C.c_void_p()
+        pxq._check(pxq.load().pxq_comm_init(C.cast(buf, C.c_void_p), world, rank, timeout_ms, C.byref(h)))
+        self.handle, self.world, self.rank = h.value, world, rank
+
+    def barrier(self) -> None:
+        from . import pxq
+
+        pxq._check(pxq.load().pxq_comm_barrier(C.c_void_p(self.handle)))
+
+    def synchronize(self, stream=None) -> None:
+        from . import pxq
+
+        pxq._check(pxq.load().pxq_comm_synchronize(C.c_void_p(self.handle), pxq._stream_ptr(stream)))
+
+    def close(self) -> None:
+        from . import pxq
+
+        if self.handle:
+            pxq._check(pxq.load().pxq_comm_destroy(C.c_void_p(self.handle)))
+            self.handle = None
+
+
+def unique_id() -> bytes:
+    from . import pxq
+
+    buf = (C.c_uint8 * COMM_ID_BYTES)()
+    pxq._check(pxq.load().pxq_comm_unique_id(C.cast(buf, C.c_void_p)))
+    return bytes(buf)
 
 
 class ShardedWeight:
@@ -57,91 +106,57 @@ class ShardedWeight:
         self.weight.release()
 
 
-def sharded_matmul(sw: ShardedWeight, x, out=None, group=None, path: str = "auto", scratch=None):
-    """Y[M][N] = X * W^T with W's rows split over the process group.
+class ShardedOutput:
+    """pxq_sharded_output: Y [columns][rows] on every rank, mapped into every
+    other rank (the fused path's destinations).  Collective to create and to
+    close; ``tensor`` views this rank's buffer."""
+
+    def __init__(self, comm: Comm, columns: int, rows: int):
+        from . import pxq
+
+        torch = pxq._torch()
+        h, local = C.c_void_p(), C.c_void_p()
+        pxq._check(pxq.load().pxq_sharded_output_create(C.c_void_p(comm.handle), columns, rows, C.byref(h), C.byref(local)))
+        self.handle, self.comm = h.value, comm
+        self.tensor = torch.as_tensor(pxq._CudaArray(local.value, (columns, rows)), device="cuda")
+
+    def close(self) -> None:
+        from . import pxq
+
+        if self.handle:
+            self.tensor = None
+            pxq._check(pxq.load().pxq_sharded_output_destroy(C.c_void_p(self.handle)))
+            self.handle = None
+
+
+def sharded_matmul(comm: Comm, sw: ShardedWeight, x, out=None, stream=None):
+    """Y[M][N] = X * W^T with W's rows split over the communicator.
 
     ``x``: fp32 [M][K] on this rank's device (replicated on every rank).
-    ``scratch``: optional (local block [M][N/G], gather buffer [G*M*N/G])
-    reused across calls.  Every rank must call it with the same shapes.
-    """
-    import torch
-    import torch.distributed as dist
-
+    ``out``: a ``ShardedOutput`` (fused path; returns its tensor) or a device
+    tensor [M][N] (NCCL all-gather path) or ``None`` (a new tensor, all-gather
+    path).  Queued on ``stream``; every rank makes the same calls."""
     from . import pxq
 
+    torch = pxq._torch()
+    x = x.contiguous()
     M = x.shape[0]
-    G, Ns = sw.world, sw.count
-    if scratch is None:
-        scratch = (torch.empty((M, Ns), dtype=torch.float32, device=x.device),
-                   torch.empty((G * M * Ns,), dtype=torch.float32, device=x.device))
-    local, gathered = scratch
-    pxq.matmul(sw.weight, x, out=local, path=path)
+    lib = pxq.load()
+    if isinstance(out, ShardedOutput):
+        pxq._check(lib.pxq_sharded_matmul(C.c_void_p(comm.handle), sw.weight.handle, sw.count, pxq._ptr(x), M,
+                                          C.c_void_p(out.handle), C.c_void_p(0), 0, pxq._stream_ptr(stream)))
+        return out.tensor
     if out is None:
-        out = torch.empty((M, G * Ns), dtype=torch.float32, device=x.device)
-    if G == 1:
-        out.copy_(local)
-        return out
-    dist.all_gather_into_tensor(gathered, local.view(-1), group=group)
-    pxq.gather_shards(gathered, G, M, Ns, out=out)
+        out = torch.empty((M, sw.rows), dtype=torch.float32, device=x.device)
+    pxq._check(lib.pxq_sharded_matmul(C.c_void_p(comm.handle), sw.weight.handle, sw.count, pxq._ptr(x), M, C.c_void_p(0),
+                                      pxq._ptr(out), out.stride(0), pxq._stream_ptr(stream)))
     return out
 
 
-class PeerOutput:
-    """Y [columns][rows] on every rank of the group, each rank's buffer mapped
-    into every other rank (CUDA IPC): the destinations of
-    ``pxq.matmul_scatter``.  Collective: every rank constructs and closes it
-    together."""
-
-    def __init__(self, columns: int, rows: int, group=None):
-        import torch
-        import torch.distributed as dist
-
-        from . import pxq
-
-        self.group = group
-        self.buf = pxq.IpcBuffer(columns, rows)
-        world, rank = dist.get_world_size(group), dist.get_rank(group)
-        handles = [None] * world
-        dist.all_gather_object(handles, self.buf.handle, group=group)
-        self.peers = []
-        self.ptrs = [self.buf.ptr]  # this rank's buffer first, then the others' (the scatter's order)
-        for r, h in enumerate(handles):
-            if r != rank:
-                peer = pxq.IpcPeer(h)
-                self.peers.append(peer)
-                self.ptrs.append(peer.ptr)
-        self.tensor = self.buf.tensor
-        self._flag = torch.zeros(1, dtype=torch.float32, device=self.tensor.device)
-
-    def sync(self) -> None:
-        """Device-ordered barrier of the group (a one-element NCCL all-reduce)."""
-        import torch.distributed as dist
-
-        dist.all_reduce(self._flag, group=self.group)
-
-    def close(self) -> None:
-        import torch
-        import torch.distributed as dist
-
-        torch.cuda.synchronize()
-        for peer in self.peers:
-            peer.close()
-        self.peers = []
-        dist.barrier(group=self.group)  # every mapping of this buffer is closed before it is freed
-        self.tensor = None
-        self.buf.free()
-
-
-def sharded_matmul_p2p(sw: ShardedWeight, x, out: PeerOutput, sync_before: bool = True):
-    """Y[M][N] = X * W^T with W's rows split over the group, each rank's GEMM
-    writing its columns into every rank's ``out`` (M > 8: the GEMM path).
-    ``sync_before``: wait until every rank is done with the previous contents
-    of its Y before anyone overwrites it.  Returns this rank's Y (a view of
-    ``out``), complete once the call returns in stream order."""
+def sharded_matmul_host_ptr(comm: Comm, sw: ShardedWeight, x_ptr: int, columns: int, inner: int, y_ptr: int) -> int:
+    """pxq_sharded_matmul_host on raw host pointers (pinned or pageable):
+    returns the status code; the full Y [columns][rows] lands in y_ptr."""
     from . import pxq
 
-    if sync_before:
-        out.sync()
-    pxq.matmul_scatter(sw.weight, x, out.ptrs, ldy=sw.rows, col_offset=sw.first)
-    out.sync()  # every rank's stores into this Y have landed
-    return out.tensor
+    return pxq.load().pxq_sharded_matmul_host(C.c_void_p(comm.handle), sw.weight.handle, sw.count, C.c_void_p(x_ptr), columns,
+                                              inner, C.c_void_p(y_ptr))

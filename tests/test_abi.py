@@ -67,3 +67,37 @@ def test_init_without_device_is_an_error_not_a_crash():
     rc = pxq.load().pxq_init(0)
     assert rc == pxq.ERR_NO_DEVICE
     assert "device" in pxq.last_error()
+
+
+def test_library_loads_no_nccl_until_a_communicator_is_used():
+    """libpxq binds NCCL at the first communicator call, so loading it never
+    pulls an NCCL into a process (one loaded later, e.g. PyTorch's, would
+    otherwise clash with it)."""
+    import subprocess
+    import sys
+
+    code = ("import ctypes, sys; sys.path.insert(0, %r); from pixelina_b200 import pxq; pxq.load(); "
+            "maps = open('/proc/self/maps').read(); print('nccl' in maps)") % ROOT
+    res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
+    assert res.returncode == 0, res.stderr
+    assert res.stdout.strip() == "False"
+
+
+def test_comm_argument_contract():
+    """The multi-GPU entry points reject bad arguments before any NCCL or
+    device work."""
+    lib = pxq.load()
+    cid = (C.c_uint8 * 128)()
+    h = C.c_void_p()
+    assert lib.pxq_comm_init(None, 2, 0, 1000, C.byref(h)) == pxq.ERR_INVALID
+    assert lib.pxq_comm_init(C.cast(cid, C.c_void_p), 0, 0, 1000, C.byref(h)) == pxq.ERR_INVALID
+    assert lib.pxq_comm_init(C.cast(cid, C.c_void_p), 2, 2, 1000, C.byref(h)) == pxq.ERR_INVALID
+    assert lib.pxq_comm_init(C.cast(cid, C.c_void_p), 9, 0, 1000, C.byref(h)) == pxq.ERR_INVALID
+    assert lib.pxq_comm_init(C.cast(cid, C.c_void_p), 2, 0, 0, C.byref(h)) == pxq.ERR_INVALID
+    assert lib.pxq_comm_unique_id(None) == pxq.ERR_INVALID
+    assert lib.pxq_comm_destroy(None) == pxq.ERR_INVALID
+    assert lib.pxq_comm_barrier(None) == pxq.ERR_INVALID
+    assert lib.pxq_sharded_output_destroy(None) == pxq.ERR_INVALID
+    assert lib.pxq_sharded_matmul(None, None, 1, None, 1, None, None, 0, None) == pxq.ERR_INVALID
+    assert lib.pxq_sharded_matmul_host(None, None, 1, None, 1, 1, None) == pxq.ERR_INVALID
+    assert "communicator" in pxq.last_error()

@@ -1,6 +1,8 @@
-"""Multi-GPU (one node): the N-sharded matmul over NCCL and through the
-one-kernel P2P-store GEMM, checked bit for bit against the single-GPU result.  Needs at least two visible GPUs; with one it
-is skipped (the CPU path of the same host logic is tests/test_sharded_gloo.py)."""
+"""Multi-GPU (one node): the N-sharded matmul of the C ABI -- NCCL all-gather,
+the fused P2P-store GEMM and the host-buffer entry point -- checked bit for
+bit against the single-GPU result.  Needs at least two visible GPUs; with one
+it is skipped (tests/test_gpu_comm.py runs the same entry points on a
+one-rank communicator, tests/test_sharded_gloo.py the host logic on CPU)."""
 import os
 import socket
 import subprocess
@@ -29,4 +31,4 @@ def test_sharded_matmul_two_gpus_bit_identical():
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     res = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
     assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-2000:]
-    assert res.stdout.count("bit-identical") == 6
+    assert res.stdout.count("bit-identical") == 11

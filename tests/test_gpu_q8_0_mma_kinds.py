@@ -1,0 +1,24 @@
+"""The Q8_0 GEMM has two operand kinds (gemm_q8.cu): the int8 quants with
+kind::i8 MMAs, and exact fp16 copies with kind::f16 MMAs.  The library picks
+one per process (PXQ_Q8_0_MMA = "i8" or "f16", read once).  The rest of the
+GPU suite runs the default kind; this test reruns the GEMM parity files in a
+child process with the other kind, so both stay bit-exact in their block dots
+and within max-abs-rel 1e-3 of the oracle."""
+import os
+import subprocess
+import sys
+
+import pytest
+
+from conftest import ROOT
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("kind", ["f16", "i8"])
+def test_q8_0_gemm_parity_in_each_mma_kind(kind):
+    env = dict(os.environ, PXQ_Q8_0_MMA=kind)
+    files = [os.path.join(ROOT, "tests", f) for f in ("test_gpu_parity.py", "test_gpu_baseline_shapes.py")]
+    res = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-k", "gemm or matmul or q6_K_golden",
+                          *files], cwd=ROOT, env=env, capture_output=True, text=True, timeout=900)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-2000:]
