@@ -170,7 +170,11 @@ PXQ_API int pxq_matmul_host(pxq_weight* w, size_t row_first, size_t row_count, c
                             float* output, size_t ldy);
 
 /* Wait for `stream` and report any bounded-wait timeout a kernel recorded
- * since the last call (PXQ_ERR_DEVICE_STATUS), then clear it. */
+ * since the last call (PXQ_ERR_DEVICE_STATUS), then clear it.  On that
+ * error it also waits for the whole device and zeroes the split-K counters
+ * of every matvec scratch on it (the per-stream buffers and the
+ * no-allocation array), which an interrupted matvec may leave non-zero;
+ * later calls then compute correctly again. */
 PXQ_API int pxq_synchronize(void* stream);
 
 /* Reorder all-gathered output shards into one row-major output: src holds
@@ -303,12 +307,14 @@ PXQ_API uint64_t pxq_kernel_launches(void);
  * pxq_matvec (columns 1..8), but the quantized activation rows go to a
  * static device array of PXQ_NOALLOC_SCRATCH_BYTES owned by this library
  * (held on every device that loads it, until exit) instead of freshly
- * allocated scratch.  The array holds the quantized activation rows
- * (columns * inner/32 * 34 bytes for Q8_0, columns * inner/256 * 288 for
- * Q5_K) and the matvec's fp32 partial sums (up to 2 * columns * 256 bytes
- * per CTA, about 1.2 MB for 8 columns on a 148-SM GPU); a call whose total
- * exceeds PXQ_NOALLOC_SCRATCH_BYTES is rejected with PXQ_ERR_UNSUPPORTED
- * before any work is queued.
+ * allocated scratch.  The array holds the matvec's counters (16 KiB), the
+ * quantized activation rows (columns * inner/32 * 34 bytes for Q8_0,
+ * columns * inner/256 * 288 for Q5_K, columns * inner/256 * 304 for Q6_K;
+ * none when the matvec quantizes a small activation itself) and its fp32
+ * partial sums (up to 2 * columns * 256 bytes per CTA, about 1.2 MB for 8
+ * columns on a 148-SM GPU); a call whose total exceeds
+ * PXQ_NOALLOC_SCRATCH_BYTES is rejected with PXQ_ERR_UNSUPPORTED before any
+ * work is queued.
  * The weight must already be uploaded and the current device must be the
  * weight's.  The first call on a device looks up the array's device address
  * (one-time set-up); make that call before any stream capture.  All calls on
@@ -318,6 +324,16 @@ PXQ_API uint64_t pxq_kernel_launches(void);
 
 PXQ_API int pxq_matvec_noalloc(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns,
                                float* output, size_t ldy, const float* bias, void* stream);
+
+/* Testing the failure path: a K-quant matvec of the whole weight (columns
+ * 1..8) in which CTA 0 loads nothing, so its bounded waits run out after
+ * their limit (about 2 s) and record a status, and its split-K counters are
+ * left the way an interrupted call leaves them -- in the stream's scratch
+ * (static_scratch == 0) or in the no-allocation array (1).  The output is
+ * not meaningful.  pxq_synchronize then returns PXQ_ERR_DEVICE_STATUS and
+ * restores the scratch.  Nothing faults or hangs: every wait is bounded. */
+PXQ_API int pxq_debug_matvec_stall(pxq_weight* w, const float* input, size_t columns, float* output, int static_scratch,
+                                   void* stream);
 
 /* Debug/parity: run the tensor-core GEMM but store, instead of the scaled
  * sum, every exact block dot it computed.  dump (device) receives

@@ -158,7 +158,7 @@ struct Packed {
     void* wv = nullptr;       // operand [rows][K]: fp16 (Q6_K: [rows][2K], even and parity planes) or Q8_0 int8
     __half* ws = nullptr;     // Q5_K min operand [rows][nsb*16]
     float* d = nullptr;       // block scales: Q8_0 d [K/32][ldn], Q5_K / Q6_K d [nsb][ldn]
-    int q8_int8 = 0;          // Q8_0: int8 operand (kind::i8 GEMM)
+    int q8_kind = 0;          // Q8_0: int8 operand (kind::i8 GEMM)
     float* dmin = nullptr;    // Q5_K dmin [nsb][ldn]
     CUtensorMap tmW, tmWs, tmD, tmDm;
     ~Packed()
@@ -197,7 +197,7 @@ struct pxq_activation {
     void* mem = nullptr;
     void* xq = nullptr;     // operand: the quants [M][K], exact fp16 values (Q8_0: or int8)
     void* scale = nullptr;  // operand: fp32 block scales, block-major [K/block][ldd]
-    int q8_int8 = 0;        // Q8_0: int8 operand
+    int q8_kind = 0;        // Q8_0: int8 operand
     __half* amin = nullptr; // operand (Q8_K): min-term split sums [M][nsb*16]
     int64_t ldd = 0;
     CUtensorMap tmX, tmXs, tmDx;
@@ -213,13 +213,18 @@ namespace {
 
 std::unordered_map<std::string, pxq_weight*> g_cache;  // guarded by g_mutex
 
-// Q8_0 GEMM operand kind: 1 = int8 quants and kind::i8 MMA, 0 = exact fp16
-// copies and kind::f16.  Read once from PXQ_Q8_0_MMA ("i8" / "f16").
-int q8_int8_operands()
+// Q8_0 GEMM operand kind (gemm_q8.cu): 0 = exact fp16 copies of the quants
+// (kind::f16) with the scales applied on the CUDA cores, 1 = the int8 quants
+// (kind::i8) likewise, 2 = fp16 copies with the scale products from a
+// one-hot tensor-core MMA.  Read once from PXQ_Q8_0_MMA ("f16", "i8",
+// "f16s"); the default is kind 2, the fastest measured.
+int q8_operand_kind()
 {
     static const int v = [] {
         const char* e = getenv("PXQ_Q8_0_MMA");
-        return (e && strcmp(e, "f16") == 0) ? 0 : 1;
+        if (e && strcmp(e, "f16") == 0) return 0;
+        if (e && strcmp(e, "i8") == 0) return 1;
+        return 2;
     }();
     return v;
 }
@@ -237,16 +242,17 @@ int build_packed(const DeviceCtx* d, pxq_weight* w, int64_t first, int64_t count
     auto pk = std::make_unique<Packed>();
     const int64_t K = w->inner;
     const bool q5 = w->type == kTypeQ5_K, q6 = w->type == kTypeQ6_K, q8 = w->type == kTypeQ8_0;
-    const int i8 = q8 ? q8_int8_operands() : 0;
+    const int kind = q8 ? q8_operand_kind() : 0;
+    const bool i8 = kind == 1, onehot = q8 && kind == 2;
     const int64_t nb = (q5 || q6) ? K / kQKK : K / kQK8_0;
     const int64_t Kop = q6 ? 2 * K : K;  // Q6_K: even and parity planes per chunk
     const int64_t elem = i8 ? 1 : 2;
     pk->rows = count;
     pk->ldn = round_up(count, 4);
-    pk->q8_int8 = i8;
+    pk->q8_kind = kind;
     const size_t wv_bytes = (size_t)count * Kop * elem;
-    const size_t ws_bytes = q5 ? (size_t)count * nb * 32 : 0;
-    const size_t s_bytes = (size_t)nb * pk->ldn * 4;
+    const size_t ws_bytes = (q5 || onehot) ? (size_t)count * nb * 32 : 0;
+    const size_t s_bytes = onehot ? 0 : (size_t)nb * pk->ldn * 4;
     const size_t dm_bytes = q5 ? s_bytes : 0;
     const size_t off_ws = round_up((int64_t)wv_bytes, 1024);
     const size_t off_d = off_ws + round_up((int64_t)ws_bytes, 1024);
@@ -267,7 +273,7 @@ int build_packed(const DeviceCtx* d, pxq_weight* w, int64_t first, int64_t count
     if (q6) {
         PXQ_CUDA(counted(launch_repack_q6_K(src, count, K, w->stride, static_cast<__half*>(pk->wv), pk->d, pk->ldn, gate_rows, s)));
     } else if (q8) {
-        PXQ_CUDA(counted(launch_repack_q8_0(src, count, K, w->stride, pk->wv, pk->d, pk->ldn, i8, gate_rows, s)));
+        PXQ_CUDA(counted(launch_repack_q8_0(src, count, K, w->stride, pk->wv, pk->d, pk->ws, pk->ldn, kind, gate_rows, s)));
     } else {
         PXQ_CUDA(counted(launch_repack_q5_K(src, count, K, w->stride, static_cast<__half*>(pk->wv), pk->d, pk->dmin, pk->ws,
                                             pk->ldn, gate_rows, s)));
@@ -277,12 +283,12 @@ int build_packed(const DeviceCtx* d, pxq_weight* w, int64_t first, int64_t count
                       Kop * elem, (uint32_t)(128 / elem), 128, CU_TENSOR_MAP_SWIZZLE_128B);
     // unused maps of a type hold the weight map (any valid map will do)
     pk->tmWs = pk->tmD = pk->tmDm = pk->tmW;
-    if (!rc && q5)
+    if (!rc && (q5 || onehot))
         rc = make_map(d, &pk->tmWs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pk->ws, nb * 16, count, nb * 32, 16, 128,
                       CU_TENSOR_MAP_SWIZZLE_32B);
-    if (!rc)
+    if (!rc && !onehot)
         rc = make_map(d, &pk->tmD, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pk->d, count, nb, pk->ldn * 4, 128,
-                      q8 ? (uint32_t)gemm_q8_scale_box(i8) : 1u, CU_TENSOR_MAP_SWIZZLE_NONE);
+                      q8 ? (uint32_t)gemm_q8_scale_box(kind) : 1u, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (!rc && q5)
         rc = make_map(d, &pk->tmDm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pk->dmin, count, nb, pk->ldn * 4, 128, 1,
                       CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -360,11 +366,14 @@ int quantize_activation(DeviceCtx* d, uint32_t wtype, const float* input, int64_
         }
         e = launch_matvec_quantize(plan, input, K, a->mem, nullptr, s);
     } else {
-        const int i8 = q5 ? 0 : q8_int8_operands();
-        a->q8_int8 = i8;
-        a->ldd = round_up(M, 4);
+        const int kind = q5 ? 0 : q8_operand_kind();
+        const bool i8 = kind == 1, onehot = !q5 && kind == 2;
+        a->q8_kind = kind;
+        // scales: fp32 block-major [nb][round_up(M, 4)], or (one-hot kind) fp16
+        // row-major [M][round_up(nb, 8)]
+        a->ldd = onehot ? round_up(nb, 8) : round_up(M, 4);
         const size_t xq_bytes = (size_t)M * K * (i8 ? 1 : 2);
-        const size_t sc_bytes = (size_t)nb * a->ldd * 4;
+        const size_t sc_bytes = onehot ? (size_t)M * a->ldd * 2 : (size_t)nb * a->ldd * 4;
         const size_t amin_bytes = q5 ? (size_t)M * nb * 32 : 0;
         const size_t off_sc = round_up((int64_t)xq_bytes, 1024);
         const size_t off_amin = off_sc + round_up((int64_t)sc_bytes, 1024);
@@ -379,7 +388,7 @@ int quantize_activation(DeviceCtx* d, uint32_t wtype, const float* input, int64_
         a->amin = reinterpret_cast<__half*>(base + off_amin);
         e = q5 ? launch_quantize_q8_K_operand(input, static_cast<__half*>(a->xq), static_cast<float*>(a->scale), a->amin, M, K, K,
                                               a->ldd, s)
-               : launch_quantize_q8_0_operand(input, a->xq, static_cast<float*>(a->scale), i8, M, K, K, a->ldd, s);
+               : launch_quantize_q8_0_operand(input, a->xq, a->scale, kind, M, K, K, a->ldd, s);
         const uint32_t xr = (uint32_t)gemm_activation_rows(wtype);  // one CTA's rows of an output tile
         const int64_t elem = i8 ? 1 : 2;
         int rc = make_map(d, &a->tmX, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->xq, K, M, K * elem,
@@ -390,10 +399,14 @@ int quantize_activation(DeviceCtx* d, uint32_t wtype, const float* input, int64_
             if (!rc) rc = make_map(d, &a->tmDx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a->scale, M, nb, a->ldd * 4,
                                    (uint32_t)gemm_tile_activation_rows(wtype), 1,
                                    CU_TENSOR_MAP_SWIZZLE_NONE);
+        } else if (!rc && onehot) {
+            rc = make_map(d, &a->tmXs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->scale, nb, M, a->ldd * 2, 16, xr,
+                          CU_TENSOR_MAP_SWIZZLE_32B);
+            a->tmDx = a->tmX;
         } else if (!rc) {
             a->tmXs = a->tmX;
             rc = make_map(d, &a->tmDx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a->scale, M, nb, a->ldd * 4,
-                          (uint32_t)gemm_tile_activation_rows(wtype), (uint32_t)gemm_q8_scale_box(i8), CU_TENSOR_MAP_SWIZZLE_NONE);
+                          (uint32_t)gemm_tile_activation_rows(wtype), (uint32_t)gemm_q8_scale_box(kind), CU_TENSOR_MAP_SWIZZLE_NONE);
         }
         if (rc) {
             cudaFreeAsync(a->mem, s);
@@ -455,6 +468,18 @@ struct StreamScratch {
 std::map<std::pair<int, cudaStream_t>, StreamScratch> g_stream_scratch;  // guarded by g_mutex
 std::vector<void*> g_retired_scratch;                                     // guarded by g_mutex
 
+// Zero the counter region of every matvec scratch on `device`: the
+// per-stream buffers (current and retired) and the no-allocation array.  The
+// caller has synchronized the device.
+void reset_scratch_counters(int device)
+{
+    std::lock_guard<std::mutex> lock(g_mutex);
+    for (auto& kv : g_stream_scratch)
+        if (kv.first.first == device && kv.second.ptr) cudaMemset(kv.second.ptr, 0, kMvCounterRegion);
+    for (void* p : g_retired_scratch) cudaMemset(p, 0, kMvCounterRegion);
+    noalloc_clear_counters(device);
+}
+
 // The stream's scratch (at least `need` bytes), or null when no device memory
 // is left.  Growing it during a stream capture is allowed: like PyTorch's
 // allocator, the cudaMalloc runs with this thread's capture mode relaxed, so
@@ -497,12 +522,12 @@ int run_gemm(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, co
     int64_t n_first = 0;
     int rc = get_packed(d, w, (int64_t)row_first, (int64_t)row_count, &pk, &n_first, s);
     if (rc) return rc;
-    if (w->type == kTypeQ8_0 && pk->q8_int8 != a->q8_int8)
+    if (w->type == kTypeQ8_0 && pk->q8_kind != a->q8_kind)
         return fail(PXQ_ERR_INVALID, "Q8_0 weight and activation operands were built for different MMA kinds");
     GemmOperands op;
     std::memset(&op, 0, sizeof(op));
     op.type = w->type;
-    op.q8_int8 = pk->q8_int8;
+    op.q8_kind = pk->q8_kind;
     op.M = a->M;
     op.N = (int64_t)row_count;
     op.K = a->K;
@@ -1151,9 +1176,35 @@ int pxq_synchronize(void* stream)
     uint32_t st = 0;
     PXQ_CUDA(cudaMemcpy(&st, d->status, 4, cudaMemcpyDeviceToHost));
     if (st) {
+        // A kernel gave up a bounded wait.  A matvec interrupted that way may
+        // leave counts in the split-K counters of its scratch, which later
+        // fused calls (no quantize kernel to clear them) rely on finding zero:
+        // once the device is idle, zero every counter region on this device.
+        cudaDeviceSynchronize();
+        reset_scratch_counters(t_device);
         cudaMemset(d->status, 0, 4);
-        return fail(PXQ_ERR_DEVICE_STATUS, "a kernel gave up waiting (status %u)", st);
+        return fail(PXQ_ERR_DEVICE_STATUS, "a kernel gave up waiting (status %u); scratch counters reset", st);
     }
+    return PXQ_OK;
+}
+
+int pxq_debug_matvec_stall(pxq_weight* w, const float* input, size_t columns, float* output, int static_scratch, void* stream)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    if (!w || !input || !output || w->gated) return fail(PXQ_ERR_INVALID, "null or gated weight, null input or output");
+    if (w->type != kTypeQ5_K && w->type != kTypeQ6_K) return fail(PXQ_ERR_UNSUPPORTED, "K-quant weights only");
+    if (!columns || columns > 8) return fail(PXQ_ERR_INVALID, "columns must be 1..8");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    MatvecPlan plan = plan_matvec(w->type, w->rows, w->inner, (int64_t)columns, d->sms, true);
+    plan.debug_stall = true;
+    void* scratch = static_scratch ? noalloc_scratch(t_device) : stream_scratch(t_device, s, plan.total_bytes);
+    if (!scratch) return fail(PXQ_ERR_NO_MEMORY, "no scratch");
+    if (static_scratch && plan.total_bytes > (size_t)PXQ_NOALLOC_SCRATCH_BYTES)
+        return fail(PXQ_ERR_UNSUPPORTED, "the call does not fit the static scratch");
+    cudaError_t e = matvec_fused(w, 0, (size_t)w->rows, input, output, (size_t)w->rows, nullptr, plan,
+                                 static_cast<uint8_t*>(scratch), d->status, s);
+    if (e != cudaSuccess) return fail(PXQ_ERR_CUDA, "matvec launch failed: %s", cudaGetErrorString(e));
     return PXQ_OK;
 }
 

@@ -7,33 +7,37 @@
 // product of the two fp16 block scales times the float of an exact int32
 // dot, accumulated in fp32) as driven by cpu_quant_matmul (:389-400).
 //
-// Design (sm_100a, one CTA per SM, persistent over 128 x 128 output tiles):
-//   * The tensor core computes only the block dots I, one TMEM slot of
-//     128 columns per 32-block; four slots, so the MMA runs up to four
-//     blocks ahead of the drain.  Two operand kinds share the kernel:
-//       OPK 0: exact fp16 copies of the quants, kind::f16 MMA (fp32 I);
-//       OPK 1: the int8 quants themselves, kind::i8 MMA (s32 I) -- half the
-//              operand bytes and half the MMA time, plus one int->float
-//              conversion per element and block in the drain.
-//   * The drain (16 warps, TMEM lane quadrant = warp % 4, column quarter =
-//     warp / 4) applies the scales on the CUDA cores: S = dW * dX and
-//     acc += S * I, two packed fp32 instructions per element pair and
-//     block.  Per block each warp waits for its slot, loads it, frees it and
-//     does the arithmetic; four drain warps per scheduler overlap those
-//     chains (with two, their latency bounded the kernel).  TMEM is read in
-//     the 16x256b layout: each thread holds 4 weight rows x 8 activation
-//     rows, so it reads a quarter of the per-column activation scales that
-//     one row per thread would need from shared memory.
-//   * Scales are fp32 block-major planes ([blocks][rows], the stored fp16
-//     values exactly), loaded by TMA into a ring of their own that the drain
-//     releases, so an operand stage is free as soon as its MMAs are done.
+// Design (sm_100a, one CTA per SM, persistent over 128 x 128 output tiles,
+// 16 drain warps -- four per scheduler -- plus a producer and an MMA warp):
+//   * Per 32-block the tensor core computes the block dots I into TMEM and
+//     the drain accumulates S * I per element.  Three operand kinds
+//     (GemmOperands::q8_kind, PXQ_Q8_0_MMA):
+//       2 (default, fastest measured): exact fp16 copies of the quants,
+//         kind::f16 MMAs for I, and a K = 16 MMA of a one-hot weight-scale
+//         tile against the activations' fp16 scale tile for S, exact
+//         because fp16 x fp16 fits fp32 (k_gemm_q8s).  TMEM holds (S, I)
+//         for two blocks; the drain does one packed FMA per element pair
+//         and block and reads no scales from shared memory.
+//       0: fp16 copies, kind::f16 for I; the drain forms S = dW * dX itself
+//         from fp32 block-major scale planes (k_gemm_q8<0>): two packed fp32
+//         instructions per element pair, four blocks of I in TMEM.
+//       1: as 0 with the int8 quants and kind::i8 MMAs (half the operand
+//         bytes and MMA time) plus an int -> float conversion per element in
+//         the drain (k_gemm_q8<1>).
+//     Kinds 0 and 1 read TMEM in the 16x256b layout (each thread: 4 weight
+//     rows x 8 activation rows), so the per-column activation scales they
+//     read from shared memory are a quarter of what one row per thread would
+//     need; that traffic, then the per-block wait / load / free latency of
+//     two drain warps per scheduler, bounded their first versions.
+//   * Scales for kinds 0 and 1 come by TMA into a ring of their own that the
+//     drain releases, so an operand stage is free as soon as its MMAs are done.
 //   * Tiles are walked in groups of 16 activation-row tiles, so the CTAs
 //     running at the same time share their operand rows in L2.
 //   * Every mbarrier wait is bounded (pxq_device.cuh); no TMA load uses a
 //     cluster multicast, and every CTA loads from this GPU's memory only.
 // The epilogue (bias, TMA-store staging, stores into peers' outputs for the
 // N-sharded path, the gated feed-forward product, the block-dot dump) is
-// the one of gemm.cu for the 32x32b accumulator layout.
+// the one of gemm.cu, per accumulator layout.
 #include "pxq_device.cuh"
 #include "pxq_internal.h"
 
@@ -359,7 +363,8 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
                 const float2 dwa[2] = {make_float2(dw[0], dw[0]), make_float2(dw[8], dw[8])};
                 const float2 dwb[2] = {make_float2(dw[16], dw[16]), make_float2(dw[24], dw[24])};
                 tmem_ld_wait();
-                // the slot is free once its values are in registers
+                // the slot is free once its values are in registers; every lane's
+                // scale loads are done before lane 0 frees the scale entry
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[slot]);
@@ -528,6 +533,314 @@ done:
     if (warp == 0) tmem_dealloc(tmem_base, 512);
 }
 
+// ---------------------------------------------------------------------------
+// OPK 2: the scale products on the tensor core.  Per 32-block b, besides the
+// block dots I (two kind::f16 MMAs on the exact fp16 quants), one K = 16 MMA
+// of a one-hot weight-scale tile (dW[n,b] at position b % 16 of a 16-wide
+// row, from the repack) against the activations' fp16 scale tile (dX[m, 16g
+// .. 16g+15]) gives S[n,m] = dW[n,b] * dX[m,b] exactly (fp16 x fp16 fits
+// fp32).  The drain then does one FMA per element and block, acc += S * I,
+// and reads no scales from shared memory; TMEM holds (S, I) for two blocks.
+constexpr int Q8S_STAGES = 3;
+constexpr int Q8S_W1H = 128 * 32;                                   // one-hot tile [128][16] fp16, 32-byte swizzle
+constexpr int Q8S_XS = 128 * 32;                                    // activation scale tile [128][16] fp16
+constexpr int Q8S_STAGE = 2 * Q8_OP_BYTES + 2 * Q8S_W1H + Q8S_XS;  // W | X | one-hot x 2 | X scales: 44 KB
+constexpr int Q8S_OFF_STAGING = Q8S_STAGES * Q8S_STAGE;
+constexpr int Q8S_OFF_BAR = Q8S_OFF_STAGING + Q8_STAGING;
+constexpr int Q8S_NUM_BARS = 2 * Q8S_STAGES + 2 * 2 + 1 + 2;
+constexpr int Q8S_SMEM = Q8S_OFF_BAR + Q8S_NUM_BARS * 8 + 16 + 1024;
+static_assert(Q8S_SMEM <= 232448, "shared memory");
+static_assert(Q8S_STAGE % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+
+__device__ __forceinline__ uint64_t desc_sw32(uint32_t saddr) { return smem_desc(saddr, 16, 256, 6); }
+
+// tensor maps:
+//   tmW   weight operand fp16 [N][K]            box {64, 128}  128B swizzle
+//   tmX   activation operand fp16 [M][K]        box {64, 128}  128B swizzle
+//   tmWs  one-hot weight scales fp16 [N][nb*16] box {16, 128}  32B swizzle
+//   tmXs  activation scales fp16 [M][ldd]       box {16, 128}  32B swizzle
+//   tmY   output fp32 [M][ldy], box {32, 32} (TMA-store epilogue)
+template <bool DUMP>
+__global__ void __launch_bounds__(Q8_THREADS, 1)
+    k_gemm_q8s(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+               const __grid_constant__ CUtensorMap tmWs, const __grid_constant__ CUtensorMap tmXs,
+               const __grid_constant__ CUtensorMap tmY, const Q8Params p)
+{
+    constexpr uint32_t IDESC = idesc_f16_f32(Q8_TN, Q8_TM);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Q8S_OFF_BAR);
+    uint64_t* full = bars;                   // operand stage loaded
+    uint64_t* empty = full + Q8S_STAGES;     // operand stage consumed by the MMAs
+    uint64_t* tfull = empty + Q8S_STAGES;    // slot pair holds a block's (S, I)
+    uint64_t* tempty = tfull + 2;            // slot pair read by every drain warp
+    uint64_t* mma_done = tempty + 2;
+    uint64_t* merge = mma_done + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Q8S_NUM_BARS);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < Q8S_STAGES; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], Q8_DRAIN_WARPS);
+        }
+        mbar_init(mma_done, 1);
+        mbar_init(&merge[0], 32 * Q8_DRAIN_WARPS);
+        mbar_init(&merge[1], 32 * Q8_DRAIN_WARPS);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    if (warp == Q8_PRODUCER_WARP && lane == 0) {
+        tma_prefetch_desc(&tmW);
+        tma_prefetch_desc(&tmX);
+        tma_prefetch_desc(&tmWs);
+        tma_prefetch_desc(&tmXs);
+        if (p.tma_store) tma_prefetch_desc(&tmY);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int64_t mt = (p.M + Q8_TM - 1) / Q8_TM;
+    const int64_t nt = (p.N + Q8_TN - 1) / Q8_TN;
+    const int64_t tiles = mt * nt;
+    const int64_t nb = p.K / kQK8_0;
+    const int64_t nstages = (nb + 1) / 2;
+    uint32_t* status = p.status;
+
+    if (warp >= Q8_DRAIN_WARPS) {
+        regs_dec<Q8_PRODUCER_REGS>();
+        if (warp == Q8_PRODUCER_WARP && lane == 0) {
+            int stage = 0;
+            uint32_t ph = 0;
+            for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+                int64_t mi, ni;
+                q8_tile(tile, mt, nt, mi, ni);
+                const int32_t m0 = (int32_t)(mi * Q8_TM);
+                const int32_t n0 = (int32_t)(p.n_first + ni * Q8_TN);
+                for (int64_t kc = 0; kc < nstages; kc++) {
+                    if (!mbar_wait(&empty[stage], ph ^ 1u, abort_flag, status, kDevTimeoutEmpty)) goto done;
+                    uint8_t* st = smem + stage * Q8S_STAGE;
+                    const int nblk = (2 * kc + 1 < nb) ? 2 : 1;
+                    mbar_expect_tx(&full[stage], 2 * Q8_OP_BYTES + nblk * Q8S_W1H + Q8S_XS);
+                    const int32_t kx = (int32_t)(kc * 64);
+                    tma_load_2d(st, &tmW, &full[stage], kx, n0);
+                    tma_load_2d(st + Q8_OP_BYTES, &tmX, &full[stage], kx, m0);
+                    for (int b = 0; b < nblk; b++)
+                        tma_load_2d(st + 2 * Q8_OP_BYTES + b * Q8S_W1H, &tmWs, &full[stage], (int32_t)((2 * kc + b) * 16), n0);
+                    tma_load_2d(st + 2 * Q8_OP_BYTES + 2 * Q8S_W1H, &tmXs, &full[stage], (int32_t)(((2 * kc) / 16) * 16), m0);
+                    if (++stage == Q8S_STAGES) {
+                        stage = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+        } else if (warp == Q8_MMA_WARP && lane == 0) {
+            int stage = 0, pair = 0;
+            uint32_t ph = 0, tph = 0;
+            for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+                for (int64_t kc = 0; kc < nstages; kc++) {
+                    if (!mbar_wait(&full[stage], ph, abort_flag, status, kDevTimeoutFull)) goto done;
+                    tc_fence_after();
+                    const uint32_t w_addr = smem_u32(smem + stage * Q8S_STAGE);
+                    const uint32_t x_addr = w_addr + Q8_OP_BYTES;
+                    const uint32_t ws_addr = x_addr + Q8_OP_BYTES;
+                    const uint32_t xs_addr = ws_addr + 2 * Q8S_W1H;
+#pragma unroll
+                    for (int bi = 0; bi < 2; bi++) {
+                        if (2 * kc + bi >= nb) break;
+                        if (!mbar_wait(&tempty[pair], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
+                        tc_fence_after();
+                        const uint32_t ds = tmem_base + (uint32_t)(pair * 2 * Q8_TM);
+                        // S: the one-hot tile selects block (2kc+bi) % 16 of the activation scale tile
+                        if (!DUMP) mma_f16(ds, desc_sw32(ws_addr + bi * Q8S_W1H), desc_sw32(xs_addr), IDESC, 0u);
+#pragma unroll
+                        for (int k = 0; k < 2; k++) {
+                            const uint32_t koff = (uint32_t)(bi * 2 + k) * 32u;
+                            mma_f16(ds + Q8_TM, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC, (uint32_t)k);
+                        }
+                        mma_commit(&tfull[pair]);
+                        if (++pair == 2) {
+                            pair = 0;
+                            tph ^= 1u;
+                        }
+                    }
+                    mma_commit(&empty[stage]);
+                    if (++stage == Q8S_STAGES) {
+                        stage = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+        }
+    } else {
+        // ------------------------------------------------------ drain warps --
+        regs_inc<Q8_DRAIN_REGS>();
+        const uint32_t quad = warp & 3u, quarter = warp >> 2;
+        const uint32_t lane_base = (quad * 32u) << 16;
+        const uint32_t col0 = quarter * Q8_HC;
+        int pair = 0;
+        uint32_t tph = 0, mgph = 0;
+        auto drain_meet = [&](int i) -> bool {
+            mbar_arrive(&merge[i]);
+            return mbar_wait(&merge[i], mgph, abort_flag, status, kDevTimeoutTmemFull);
+        };
+        for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+            int64_t mi, ni;
+            q8_tile(tile, mt, nt, mi, ni);
+            const int64_t m0 = mi * Q8_TM;
+            const int64_t n0 = ni * Q8_TN;       // view-local
+            const int64_t nq = n0 + quad * 32u;  // the warp's first weight row
+            const int64_t n = nq + lane;         // this thread's weight row == TMEM lane
+            const int64_t mfirst = m0 + col0;
+            float acc[Q8_HC];
+#pragma unroll
+            for (int i = 0; i < Q8_HC; i++) acc[i] = 0.f;
+            for (int64_t b = 0; b < nb; b++) {
+                if (!mbar_wait(&tfull[pair], tph, abort_flag, status, kDevTimeoutTmemFull)) goto done;
+                tc_fence_after();
+                const uint32_t ts = tmem_base + lane_base + (uint32_t)(pair * 2 * Q8_TM) + col0;
+                uint32_t sv[32], iv[32];
+                if (!DUMP) tmem_ld32(ts, sv);
+                tmem_ld32(ts + Q8_TM, iv);
+                tmem_ld_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[pair]);
+                if (++pair == 2) {
+                    pair = 0;
+                    tph ^= 1u;
+                }
+                if constexpr (DUMP) {
+#pragma unroll
+                    for (int j = 0; j < Q8_HC; j++) {
+                        const int64_t m = mfirst + j;
+                        if (n < p.N && m < p.M) p.dump[(b * p.M + m) * p.N + n] = __uint_as_float(iv[j]);
+                    }
+                } else {
+                    // pix_dot_q8_0: acc = fma(fp16(dw)*fp16(dx), float(block dot), acc), two per instruction
+#pragma unroll
+                    for (int j = 0; j < Q8_HC; j += 2)
+                        ffma2(acc[j], acc[j + 1], __uint_as_float(sv[j]), __uint_as_float(sv[j + 1]), __uint_as_float(iv[j]),
+                              __uint_as_float(iv[j + 1]));
+                }
+            }
+            if constexpr (!DUMP) {
+                if (p.gated) {
+                    // gated weight: lanes 64..127 hold the up projections of the
+                    // outputs whose gate projections lanes 0..63 hold (the repack
+                    // interleaves 64-row groups); the up warps hand their sums over
+                    // through the staging buffer and the gate warps finish
+                    // tensor_silu + tensor_gate (src/tensor.cpp:199-208, :334-345)
+                    float* xfer = reinterpret_cast<float*>(smem + Q8S_OFF_STAGING) + ((quad & 1) * 4 + quarter) * (Q8_HC * 32);
+                    if (!drain_meet(0)) goto done;
+                    if (quad >= 2) {
+#pragma unroll
+                        for (int i = 0; i < Q8_HC; i++) xfer[i * 32 + lane] = acc[i];
+                    }
+                    if (!drain_meet(1)) goto done;
+                    mgph ^= 1u;
+                    if (quad < 2) {
+#pragma unroll
+                        for (int i = 0; i < Q8_HC; i++) {
+                            const int64_t on = n0 / 2 + quad * 32 + lane, m = mfirst + i;
+                            const float g = acc[i], u = xfer[i * 32 + lane];
+                            if (on < p.N / 2 && m < p.M) p.y[m * p.ldy + on] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+                        }
+                    }
+                    continue;
+                }
+                const float bv = (p.bias && n < p.N) ? p.bias[n] : 0.f;
+                if (p.tma_store) {
+                    float* stg = reinterpret_cast<float*>(smem + Q8S_OFF_STAGING) + warp * (Q8_HC * 32);
+                    if (lane == 0) bulk_wait_read_all();
+                    __syncwarp();
+#pragma unroll
+                    for (int j = 0; j < Q8_HC; j++) stg[j * 32 + lane] = p.bias ? __fadd_rn(acc[j], bv) : acc[j];
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmY, stg, (int32_t)nq, (int32_t)mfirst);
+                        bulk_commit();
+                    }
+                    if (p.ndst && p.dst_vec4) {
+                        const int jr = lane >> 3, c4 = 4 * (lane & 7);
+                        const int64_t nn = nq + c4;
+                        for (int j = jr; j < Q8_HC; j += 4) {
+                            const int64_t m = mfirst + j;
+                            if (m >= p.M) break;
+                            const float4 v = *reinterpret_cast<const float4*>(stg + j * 32 + c4);
+                            const int64_t off = m * p.ldy + p.col_off + nn;
+                            if (nn + 3 < p.N) {
+                                for (int k = 0; k < p.ndst; k++) *reinterpret_cast<float4*>(p.ydst[k] + off) = v;
+                            } else {
+                                const float vs[4] = {v.x, v.y, v.z, v.w};
+                                for (int q = 0; q < 4 && nn + q < p.N; q++)
+                                    for (int k = 0; k < p.ndst; k++) p.ydst[k][off + q] = vs[q];
+                            }
+                        }
+                    } else if (p.ndst && n < p.N) {
+                        for (int j = 0; j < Q8_HC; j++) {
+                            const int64_t m = mfirst + j;
+                            if (m >= p.M) break;
+                            const float v = stg[j * 32 + lane];
+                            const int64_t off = m * p.ldy + p.col_off + n;
+                            for (int k = 0; k < p.ndst; k++) p.ydst[k][off] = v;
+                        }
+                    }
+                } else if (n < p.N) {
+#pragma unroll
+                    for (int j = 0; j < Q8_HC; j++) {
+                        const int64_t m = mfirst + j;
+                        if (m < p.M) put_y(p, m, n, p.bias ? __fadd_rn(acc[j], bv) : acc[j]);
+                    }
+                }
+            }
+        }
+    }
+done:
+    if (p.tma_store && warp < Q8_DRAIN_WARPS && lane == 0) bulk_wait_all();
+    if (p.ndst && warp < Q8_DRAIN_WARPS) __threadfence_system();
+    if (warp == Q8_MMA_WARP && lane == 0) {
+        mma_commit(mma_done);
+        const uint64_t t0 = global_ns();
+        while (!mbar_try_wait(mma_done, 0) && global_ns() - t0 < PXQ_WAIT_NS) {
+        }
+    }
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(tmem_base, 512);
+}
+
+template <bool DUMP>
+cudaError_t launch_q8s(const GemmOperands& op, int num_sms, cudaStream_t s)
+{
+    auto kern = k_gemm_q8s<DUMP>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Q8S_SMEM);
+    if (e != cudaSuccess) return e;
+    const int64_t tiles = ((op.M + Q8_TM - 1) / Q8_TM) * ((op.N + Q8_TN - 1) / Q8_TN);
+    int64_t grid = num_sms;
+    if (tiles < grid) grid = tiles;
+    if (grid < 1) grid = 1;
+    Q8Params p{op.M, op.N, op.K, op.n_first, op.y, op.ldy, op.bias, op.dump, op.status, (op.tma_store && !DUMP) ? 1 : 0,
+               op.gated, op.ndst, op.dst_vec4, op.col_off, {}};
+    for (int k = 0; k < kMaxScatter; k++) p.ydst[k] = op.ydst[k];
+    kern<<<(unsigned)grid, Q8_THREADS, Q8S_SMEM, s>>>(op.tm[0], op.tm[1], op.tm[2], op.tm[3], op.tm_y, p);
+    return cudaGetLastError();
+}
+
 template <int OPK, bool DUMP>
 cudaError_t launch_q8_typed(const GemmOperands& op, int num_sms, cudaStream_t s)
 {
@@ -550,12 +863,12 @@ cudaError_t launch_q8_typed(const GemmOperands& op, int num_sms, cudaStream_t s)
 
 cudaError_t launch_gemm_q8(const GemmOperands& op, int num_sms, cudaStream_t s)
 {
-    if (op.q8_int8)
+    if (op.q8_kind == 2) return op.dump ? launch_q8s<true>(op, num_sms, s) : launch_q8s<false>(op, num_sms, s);
+    if (op.q8_kind == 1)
         return op.dump ? launch_q8_typed<1, true>(op, num_sms, s) : launch_q8_typed<1, false>(op, num_sms, s);
     return op.dump ? launch_q8_typed<0, true>(op, num_sms, s) : launch_q8_typed<0, false>(op, num_sms, s);
 }
 
-int gemm_q8_operand_elems(int int8_operands) { return int8_operands ? Q8Op<1>::ELEMS : Q8Op<0>::ELEMS; }
-int gemm_q8_scale_box(int int8_operands) { return int8_operands ? Q8Op<1>::BPS : Q8Op<0>::BPS; }
+int gemm_q8_scale_box(int kind) { return kind == 1 ? Q8Op<1>::BPS : Q8Op<0>::BPS; }
 
 }  // namespace pxq

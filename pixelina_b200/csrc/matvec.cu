@@ -34,6 +34,8 @@
 // whole row, or a 1/ks slice when there are too few row groups to fill the
 // GPU); warps walk the blocks round-robin with the next block's weight bytes
 // in flight (register double buffering).
+#include <atomic>
+
 #include "pxq_device.cuh"
 #include "pxq_internal.h"
 #include "q8k.cuh"
@@ -298,6 +300,7 @@ struct MvParams {
     int64_t ldy, rows, row_first, stages;
     int64_t gated_half;                // gated pair: F / 64; logical tile 2j = gate tile j, 2j+1 = up tile j
     int32_t nsb, spt, columns;
+    int32_t stall;                     // testing: CTA 0 loads nothing (MatvecPlan::debug_stall)
 };
 
 // First CTA whose stage range [c*S/G, (c+1)*S/G) holds stage s.
@@ -642,7 +645,7 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_kq(const __grid_consta
     }
 
     if (warp == kMvProducerWarp) {
-        if (lane == 0) {
+        if (lane == 0 && !(p.stall && blockIdx.x == 0)) {
             // producer.  The weights do not depend on earlier kernels: the
             // first stages' weights are requested before griddep_wait, their
             // activation records after it.
@@ -866,17 +869,17 @@ cudaError_t launch_kq(const MatvecPlan& plan, const CUtensorMap* map, int64_t ro
                       int64_t ldx, float* y, int64_t ldy, const float* bias, float* partial, uint32_t* counters,
                       uint32_t* status, cudaStream_t s)
 {
-    static bool attr_set[16] = {};
+    static std::atomic<bool> attr_set[16] = {};  // set once per device (racing threads set the same values)
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 16 && !attr_set[dev]) {
+    if (dev >= 0 && dev < 16 && !attr_set[dev].load(std::memory_order_acquire)) {
         cudaError_t e = cudaFuncSetAttribute(k_matvec_kq<TR, FUSED, WT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)sizeof(MvSmem<TR, FUSED, WT>));
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(k_matvec_kq<TR, FUSED, WT>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                      (int)cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return e;
-        attr_set[dev] = true;
+        attr_set[dev].store(true, std::memory_order_release);
     }
     MvParams prm;
     prm.map = *map;
@@ -896,6 +899,7 @@ cudaError_t launch_kq(const MatvecPlan& plan, const CUtensorMap* map, int64_t ro
     prm.spt = (int32_t)plan.spt;
     prm.columns = (int32_t)plan.columns;
     prm.gated_half = plan.gated_half;
+    prm.stall = plan.debug_stall ? 1 : 0;
     return launch_pdl(k_matvec_kq<TR, FUSED, WT>, dim3(plan.grid), dim3(kMvThreads), sizeof(MvSmem<TR, FUSED, WT>), s, prm);
 }
 

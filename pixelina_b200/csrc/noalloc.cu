@@ -19,12 +19,14 @@
 // does the set-up (and may make the runtime load this module); make it before
 // any stream capture.
 //
-// Layout of the array per call: the quantized activation rows (none when the
-// matvec quantizes a small activation itself), then the matvec's fp32 partial
-// sums and counters.  The counters must start at zero: the array starts
-// zeroed, the quantize kernel of a call (when there is one) clears them, and
-// every completed matvec leaves them zero; every other byte the kernels read
-// is written earlier in the same call.
+// Layout of the array per call: the matvec's counters (a region of their
+// own), the quantized activation rows (none when the matvec quantizes a small
+// activation itself), then its fp32 partial sums.  The counters must start
+// at zero: the array starts zeroed, the quantize kernel of a call (when there
+// is one) clears them, every completed matvec leaves them zero, and after a
+// call whose bounded wait ran out (pxq_synchronize reports
+// PXQ_ERR_DEVICE_STATUS) pxq_synchronize clears them again; every other byte
+// the kernels read is written earlier in the same call.
 //
 // Sharing: every call on a device uses the same array and it keeps the last
 // call's contents.  Two calls whose work overlaps on the GPU (different
@@ -67,6 +69,39 @@ int noalloc_fail(int code, const char* msg)
 }
 }  // namespace
 
+namespace pxq {
+// The array's device address on `device` (with that device current): looked
+// up once per device with cudaGetSymbolAddress -- the host-side symbol is not
+// a device address -- and cached.  Null if the look-up fails.
+void* noalloc_scratch(int device)
+{
+    if (device < 0 || device >= kMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> lock(g_setup_mutex);
+    if (!g_scratch_ptr[device]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        g_scratch_ptr[device] = p;
+    }
+    return g_scratch_ptr[device];
+}
+
+// Zero the counter region (after a call that a bounded wait interrupted may
+// have left counts in it; the caller has synchronized the device).  No-op
+// when the array was never set up on `device`.
+cudaError_t noalloc_clear_counters(int device)
+{
+    void* p = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_setup_mutex);
+        if (device >= 0 && device < kMaxDevices) p = g_scratch_ptr[device];
+    }
+    return p ? cudaMemset(p, 0, kMvCounterRegion) : cudaSuccess;
+}
+}  // namespace pxq
+
 extern "C" int pxq_matvec_noalloc(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns,
                                   float* output, size_t ldy, const float* bias, void* stream)
 {
@@ -83,11 +118,13 @@ extern "C" int pxq_matvec_noalloc(pxq_weight* w, size_t row_first, size_t row_co
     if (ldy < row_count && columns > 1) return noalloc_fail(PXQ_ERR_INVALID, "ldy < row_count");
     if (type != pxq::kTypeQ8_0 && type != pxq::kTypeQ5_K && type != pxq::kTypeQ6_K)
         return noalloc_fail(PXQ_ERR_UNSUPPORTED, "weight type not supported");
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+        return noalloc_fail(PXQ_ERR_NO_DEVICE, "no current CUDA device");
+    if (dev != wdev) return noalloc_fail(PXQ_ERR_INVALID, "the weight lives on another device than the current one");
     // the static array holds the quantized activation rows and the matvec's
     // partial sums and counters
-    int cur_dev = -1;
-    cudaGetDevice(&cur_dev);
-    const pxq::MatvecPlan plan = pxq::plan_matvec(type, (int64_t)row_count, inner, (int64_t)columns, pxq::device_sm_count(cur_dev),
+    const pxq::MatvecPlan plan = pxq::plan_matvec(type, (int64_t)row_count, inner, (int64_t)columns, pxq::device_sm_count(dev),
                                                   true);
     const uint64_t need = plan.total_bytes;
     if (need > PXQ_NOALLOC_SCRATCH_BYTES) {
@@ -96,25 +133,8 @@ extern "C" int pxq_matvec_noalloc(pxq_weight* w, size_t row_first, size_t row_co
                  "(PXQ_NOALLOC_SCRATCH_BYTES)", (unsigned long long)need, PXQ_NOALLOC_SCRATCH_BYTES);
         return noalloc_fail(PXQ_ERR_UNSUPPORTED, msg);
     }
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
-        return noalloc_fail(PXQ_ERR_NO_DEVICE, "no current CUDA device");
-    if (dev != wdev) return noalloc_fail(PXQ_ERR_INVALID, "the weight lives on another device than the current one");
-    void* scratch = nullptr;
-    {
-        std::lock_guard<std::mutex> lock(g_setup_mutex);
-        if (!g_scratch_ptr[dev]) {
-            void* p = nullptr;
-            cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-            if (e != cudaSuccess || !p) {
-                char msg[200];
-                snprintf(msg, sizeof(msg), "cudaGetSymbolAddress of the static scratch failed: %s", cudaGetErrorString(e));
-                return noalloc_fail(PXQ_ERR_CUDA, msg);
-            }
-            g_scratch_ptr[dev] = p;
-        }
-        scratch = g_scratch_ptr[dev];
-    }
+    void* scratch = pxq::noalloc_scratch(dev);
+    if (!scratch) return noalloc_fail(PXQ_ERR_CUDA, "cudaGetSymbolAddress of the static scratch failed");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const cudaError_t e = pxq::matvec_fused(w, row_first, row_count, input, output, ldy, bias, plan,
                                             static_cast<uint8_t*>(scratch), pxq::device_status(dev), s);

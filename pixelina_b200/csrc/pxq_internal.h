@@ -24,14 +24,15 @@ constexpr uint32_t kTypeQ6_K = 14;
 cudaError_t launch_quantize_q8_0_blocks(const float* x, void* y, int64_t rows, int64_t inner, int64_t ldx, cudaStream_t s);
 cudaError_t launch_quantize_q8_K_blocks(const float* x, void* y, int64_t rows, int64_t inner, int64_t ldx, cudaStream_t s);
 // Tensor-core operand formats for the GEMM (same rounding, different layout):
-//   Q8_0: xq [rows][inner]: the int8 quants themselves (int8_operands) or as
-//         exact fp16 values; dxT fp32 [inner/32][ldd]: the stored fp16 block
-//         scales as fp32, block-major
+//   Q8_0: xq [rows][inner]: the int8 quants themselves (kind 1) or as exact
+//         fp16 values (kinds 0, 2); kinds 0, 1: dxT fp32 [inner/32][ldd], the
+//         stored fp16 block scales as fp32, block-major; kind 2: the fp16
+//         scales row-major [rows][ldd]
 //   Q8_K: xq fp16 [rows][inner]: the int8 quants as exact fp16 values
 //         dxT fp32 [inner/256][ldd]: per-block scale, block-major
 //         amin fp16 [rows][inner/256*16]: split 32-element sums for the Q5_K
 //         min term, (hi_j, lo_j) with bsum2_j = 64*hi_j + lo_j
-cudaError_t launch_quantize_q8_0_operand(const float* x, void* xq, float* dxT, int int8_operands, int64_t rows, int64_t inner,
+cudaError_t launch_quantize_q8_0_operand(const float* x, void* xq, void* dx, int kind, int64_t rows, int64_t inner,
                                          int64_t ldx, int64_t ldd, cudaStream_t s);
 cudaError_t launch_quantize_q8_K_operand(const float* x, __half* xq, float* dxT, __half* amin, int64_t rows, int64_t inner,
                                          int64_t ldx, int64_t ldd, cudaStream_t s);
@@ -43,10 +44,14 @@ cudaError_t launch_pad_q6_K(const void* src, void* dst, int64_t superblocks, cud
 // One-time weight repack into the GEMM operand layout (bit-exact unpack).
 // gate_rows = F > 0: a gated weight (F gate rows, then F up rows) packed as
 // 128-row groups [64 gate rows j..j+63][the 64 matching up rows].
-// Q8_0: wq [rows][inner] int8 quants (int8_operands) or their exact fp16
-// values; dT fp32 [inner/32][ldn] the fp16 block scales, block-major.
+// Q8_0 (operand kind as in GemmOperands::q8_kind): wq [rows][inner] int8
+// quants (kind 1) or their exact fp16 values (kinds 0, 2); kinds 0, 1: dT
+// fp32 [inner/32][ldn] the fp16 block scales, block-major; kind 2: ws1h fp16
+// [rows][inner/32*16], for block b a 16-wide group with the block's scale at
+// position b % 16 and zeros elsewhere (the weight side of the tensor-core
+// scale product).
 cudaError_t launch_repack_q8_0(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, void* wq, float* dT,
-                               int64_t ldn, int int8_operands, int64_t gate_rows, cudaStream_t s);
+                               __half* ws1h, int64_t ldn, int kind, int64_t gate_rows, cudaStream_t s);
 cudaError_t launch_repack_q5_K(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, __half* wv, float* dT,
                                float* dminT, __half* bmin, int64_t ldn, int64_t gate_rows, cudaStream_t s);
 // Q6_K: raw rows are the device's padded super-blocks (stride bytes per row).
@@ -59,6 +64,12 @@ cudaError_t launch_repack_q6_K(const uint8_t* raw, int64_t rows, int64_t inner, 
 cudaError_t launch_gate_rows(const float* s, int64_t columns, int64_t F, float* y, int64_t ldy, cudaStream_t st);
 
 cudaError_t launch_decode(const uint8_t* data, uint32_t type, int64_t count, float* out, cudaStream_t s);
+
+// ---- noalloc.cu ------------------------------------------------------------
+// The static scratch array's device address on `device` (set up on first
+// use, with that device current), or null; and clearing its counter region.
+void* noalloc_scratch(int device);
+cudaError_t noalloc_clear_counters(int device);
 
 // ---- matvec.cu -------------------------------------------------------------
 // y[c*ldy + r] = dot(W row r, X row c) for c < columns <= 8, raw GGUF weights.
@@ -101,6 +112,10 @@ struct MatvecPlan {
     int64_t gated_half = 0;                  // K-quants, gated weight [gate; up]: F / 64 (the epilogue writes silu(g) * u)
     size_t act_bytes = 0, partial_bytes = 0, counter_bytes = 0;
     size_t off_counters = 0, off_act = 0, off_partial = 0, total_bytes = 0;
+    // testing only (K-quants): CTA 0 loads nothing, so its bounded waits run
+    // out and report a status, and the call's split-K counters are left the
+    // way an interrupted call leaves them
+    bool debug_stall = false;
 };
 // fuse_quantize: allow the plan to let the matvec quantize a small
 // activation itself (then act_bytes is 0 and launch_matvec takes x).
@@ -165,7 +180,9 @@ constexpr int kMaxScatter = 8;  // destinations of a scattering GEMM (one per ra
 
 struct GemmOperands {
     uint32_t type;        // kTypeQ8_0, kTypeQ5_K or kTypeQ6_K
-    int q8_int8;          // Q8_0: int8 operands and kind::i8 MMA (else fp16 operands, kind::f16)
+    int q8_kind;          // Q8_0 operand kind (gemm_q8.cu): 0 fp16 quants, scales applied on the CUDA cores;
+                          // 1 int8 quants (kind::i8), scales on the CUDA cores; 2 fp16 quants, scale
+                          // products from a one-hot tensor-core MMA
     int64_t M, N, K;      // activation rows, view rows (output columns), inner
     int64_t n_first;      // first weight row of the view (multiple of 4)
     // tensor maps (boxes as listed in gemm.cu and gemm_q8.cu): 0 weight
@@ -199,10 +216,9 @@ int gemm_store_rows(uint32_t type);
 cudaError_t launch_gemm(const GemmOperands& op, int num_sms, cudaStream_t s);
 
 // ---- gemm_q8.cu -------------------------------------------------------------
-// The Q8_0 GEMM (called by launch_gemm).  Operand elements per 128-byte TMA
-// box row (64 fp16 or 128 int8) and 32-blocks per scale box (2 or 4).
+// The Q8_0 GEMM (called by launch_gemm).  32-blocks per fp32 scale box
+// (operand kinds 0 and 1: 2 or 4).
 cudaError_t launch_gemm_q8(const GemmOperands& op, int num_sms, cudaStream_t s);
-int gemm_q8_operand_elems(int int8_operands);
-int gemm_q8_scale_box(int int8_operands);
+int gemm_q8_scale_box(int kind);
 
 }  // namespace pxq

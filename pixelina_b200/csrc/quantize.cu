@@ -7,8 +7,8 @@
 // reference produces, checked by the parity tests; the Q8_0 matvec reads it
 // too), the Q8_K matvec operand (the same bytes permuted for the matvec's
 // fragments, plus 32-element sums), and the tensor-core operand layout used
-// by the GEMM (the int8 quants, or exact fp16 copies of them, plus
-// block-major scale planes).  All layouts come from the same arithmetic.
+// by the GEMM (the int8 quants, or exact fp16 copies of them, plus their
+// block scales).  All layouts come from the same arithmetic.
 //
 // Bit-exactness rules (all arithmetic uses explicit _rn intrinsics so that
 // nvcc's default FMA contraction cannot change a rounding):
@@ -20,6 +20,8 @@
 //     kernel uses __fmaf_rn for that step;
 //   * the stored fp16 scale is round-to-nearest-even (F16C with
 //     _MM_FROUND_TO_NEAREST_INT).
+#include <atomic>
+
 #include "pxq_device.cuh"
 #include "pxq_internal.h"
 #include "q8k.cuh"
@@ -107,11 +109,11 @@ __global__ void k_quantize_q8_0_blocks(const float* x, uint8_t* __restrict__ y, 
     }
 }
 
-// GEMM operand: the quants as int8 (int8_operands) or exact fp16 values,
-// [rows][inner], and the stored fp16 block scales as fp32, block-major
-// [inner/32][ldd].
-__global__ void k_quantize_q8_0_operand(const float* __restrict__ x, void* __restrict__ xq, float* __restrict__ dxT,
-                                        int int8_operands, int64_t rows, int64_t inner, int64_t ldx, int64_t ldd)
+// GEMM operand: the quants as int8 (kind 1) or exact fp16 values (kinds 0,
+// 2), [rows][inner], and the stored fp16 block scales: as fp32, block-major
+// [inner/32][ldd] (kinds 0, 1), or as fp16, row-major [rows][ldd] (kind 2).
+__global__ void k_quantize_q8_0_operand(const float* __restrict__ x, void* __restrict__ xq, void* __restrict__ dx, int kind,
+                                        int64_t rows, int64_t inner, int64_t ldx, int64_t ldd)
 {
     const int64_t quads_per_row = inner / 4;
     const int64_t total = rows * quads_per_row;
@@ -125,7 +127,7 @@ __global__ void k_quantize_q8_0_operand(const float* __restrict__ x, void* __res
         if (live) v = ld_dep_f4(x + row * ldx + quad * 4);
         const Q80Part p = q8_0_part(v);
         if (!live) continue;
-        if (int8_operands) {
+        if (kind == 1) {
             reinterpret_cast<uint32_t*>(static_cast<int8_t*>(xq) + row * inner)[quad] = p.packed;
         } else {
             __half2 h01 = __halves2half2(__int2half_rn(p.q[0]), __int2half_rn(p.q[1]));
@@ -135,7 +137,12 @@ __global__ void k_quantize_q8_0_operand(const float* __restrict__ x, void* __res
             packed.y = *reinterpret_cast<uint32_t*>(&h23);
             *reinterpret_cast<uint2*>(static_cast<__half*>(xq) + row * inner + quad * 4) = packed;
         }
-        if ((quad & 7) == 0) dxT[(quad / 8) * ldd + row] = __half2float(p.d16);
+        if ((quad & 7) == 0) {
+            if (kind == 2)
+                static_cast<__half*>(dx)[row * ldd + quad / 8] = p.d16;
+            else
+                static_cast<float*>(dx)[(quad / 8) * ldd + row] = __half2float(p.d16);
+        }
     }
 }
 
@@ -273,14 +280,15 @@ cudaError_t launch_matvec_quantize(const MatvecPlan& plan, const float* x, int64
         auto kern = q6 ? k_quantize_q8_K_mv<true> : k_quantize_q8_K_mv<false>;
         // same shared-memory carveout as the matvec, so that the SMs need no
         // reconfiguration between the two kernels
-        static bool carveout_set[2][16] = {};
+        // (set once per device; setting it twice from racing threads is harmless)
+        static std::atomic<bool> carveout_set[2][16] = {};
         int dev = 0;
         cudaGetDevice(&dev);
-        if (dev >= 0 && dev < 16 && !carveout_set[q6][dev]) {
+        if (dev >= 0 && dev < 16 && !carveout_set[q6][dev].load(std::memory_order_acquire)) {
             cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                                                  (int)cudaSharedmemCarveoutMaxShared);
             if (e != cudaSuccess) return e;
-            carveout_set[q6][dev] = true;
+            carveout_set[q6][dev].store(true, std::memory_order_release);
         }
         return launch_pdl(kern, dim3(grid_for(plan.columns * (plan.inner / kQKK) * 32, threads)), dim3(threads), 0, s, x, out,
                           plan.columns, plan.inner, ldx, counters, nzero);
@@ -296,12 +304,11 @@ cudaError_t launch_quantize_q8_K_blocks(const float* x, void* y, int64_t rows, i
     return cudaGetLastError();
 }
 
-cudaError_t launch_quantize_q8_0_operand(const float* x, void* xq, float* dxT, int int8_operands, int64_t rows, int64_t inner,
+cudaError_t launch_quantize_q8_0_operand(const float* x, void* xq, void* dx, int kind, int64_t rows, int64_t inner,
                                          int64_t ldx, int64_t ldd, cudaStream_t s)
 {
     const int threads = 256;
-    k_quantize_q8_0_operand<<<grid_for(rows * inner / 4, threads), threads, 0, s>>>(x, xq, dxT, int8_operands, rows, inner, ldx,
-                                                                                    ldd);
+    k_quantize_q8_0_operand<<<grid_for(rows * inner / 4, threads), threads, 0, s>>>(x, xq, dx, kind, rows, inner, ldx, ldd);
     return cudaGetLastError();
 }
 

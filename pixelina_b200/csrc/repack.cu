@@ -4,9 +4,11 @@
 //     done when a weight is first used by the GEMM and then cached with it
 //     (the device-side counterpart of the Vulkan backend's upload cache,
 //     src/backend_vulkan.cpp:742-758):
-//       Q8_0: wq   [rows][inner] = the int8 quants, as stored (int8
-//                  operands) or as exact fp16 values
+//       Q8_0: wq   [rows][inner] = the int8 quants, as stored (operand kind
+//                  1) or as exact fp16 values (kinds 0, 2)
 //             dT   fp32 [inner/32][ldn] = the fp16 block scales, block-major
+//                  (kinds 0, 1); kind 2: ws1h fp16 [rows][inner/32*16], the
+//                  one-hot weight side of the tensor-core scale product
 //       Q5_K: wv   fp16 [rows][inner]   = sc_g * q5 (<= 63*31 = 1953, exact)
 //             dT, dminT fp32 [inner/256][ldn]
 //             bmin fp16 [rows][inner/256*16] = (64*m_g, m_g) pairs, the weight
@@ -55,17 +57,19 @@ __device__ __forceinline__ int64_t src_row(int64_t r, int64_t gate_rows)
 }
 
 // One thread per (row, 32-block): the block's 32 quants into the operand row
-// (int8 as stored, or their exact fp16 values) and its fp16 scale, as fp32,
-// into the block-major scale plane.
+// (int8 as stored for kind 1, their exact fp16 values otherwise) and its
+// fp16 scale into the block-major fp32 plane (kinds 0, 1) or the one-hot
+// tile (kind 2).
 __global__ void k_repack_q8_0(const uint8_t* __restrict__ raw, int64_t rows, int64_t inner, int64_t stride,
-                              void* __restrict__ wq, float* __restrict__ dT, int64_t ldn, int int8_operands, int64_t gate_rows)
+                              void* __restrict__ wq, float* __restrict__ dT, __half* __restrict__ ws1h, int64_t ldn, int kind,
+                              int64_t gate_rows)
 {
     const int64_t nb = inner / kQK8_0;
     const int64_t total = rows * nb;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = i / nb, b = i % nb;
         const uint8_t* blk = raw + src_row(r, gate_rows) * stride + b * kQ8_0Bytes;
-        if (int8_operands) {
+        if (kind == 1) {
             // qs start at byte 2 of the 34-byte block: 2-byte aligned loads
             uint16_t q[16];
 #pragma unroll
@@ -81,7 +85,17 @@ __global__ void k_repack_q8_0(const uint8_t* __restrict__ raw, int64_t rows, int
 #pragma unroll
             for (int j = 0; j < 4; j++) dst[j] = reinterpret_cast<uint4*>(h)[j];
         }
-        dT[b * ldn + r] = load_half(blk);
+        if (kind == 2) {
+            __half g[16];
+#pragma unroll
+            for (int j = 0; j < 16; j++) g[j] = __ushort_as_half((unsigned short)0);
+            g[b % 16] = __ushort_as_half((unsigned short)((uint16_t)blk[0] | ((uint16_t)blk[1] << 8)));
+            uint4* gd = reinterpret_cast<uint4*>(ws1h + (r * nb + b) * 16);
+            gd[0] = reinterpret_cast<uint4*>(g)[0];
+            gd[1] = reinterpret_cast<uint4*>(g)[1];
+        } else {
+            dT[b * ldn + r] = load_half(blk);
+        }
     }
 }
 
@@ -199,9 +213,9 @@ int grid_for(int64_t work, int threads)
 }  // namespace
 
 cudaError_t launch_repack_q8_0(const uint8_t* raw, int64_t rows, int64_t inner, int64_t stride, void* wq, float* dT,
-                               int64_t ldn, int int8_operands, int64_t gate_rows, cudaStream_t s)
+                               __half* ws1h, int64_t ldn, int kind, int64_t gate_rows, cudaStream_t s)
 {
-    k_repack_q8_0<<<grid_for(rows * (inner / kQK8_0), 256), 256, 0, s>>>(raw, rows, inner, stride, wq, dT, ldn, int8_operands,
+    k_repack_q8_0<<<grid_for(rows * (inner / kQK8_0), 256), 256, 0, s>>>(raw, rows, inner, stride, wq, dT, ws1h, ldn, kind,
                                                                           gate_rows);
     return cudaGetLastError();
 }

@@ -81,6 +81,7 @@ SIGNATURES = {
     "pxq_activation_release": (_i, [_vp, _vp]),
     "pxq_kernel_launches": (_u64, []),
     "pxq_matvec_noalloc": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _sz, _vp, _vp]),
+    "pxq_debug_matvec_stall": (_i, [_vp, _vp, _sz, _vp, _i, _vp]),
     "pxq_comm_unique_id": (_i, [_vp]),
     "pxq_comm_init": (_i, [_vp, _i, _i, _i, C.POINTER(_vp)]),
     "pxq_comm_size": (_i, [_vp, C.POINTER(_i), C.POINTER(_i)]),

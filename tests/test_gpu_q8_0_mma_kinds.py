@@ -1,9 +1,11 @@
-"""The Q8_0 GEMM has two operand kinds (gemm_q8.cu): the int8 quants with
-kind::i8 MMAs, and exact fp16 copies with kind::f16 MMAs.  The library picks
-one per process (PXQ_Q8_0_MMA = "i8" or "f16", read once).  The rest of the
-GPU suite runs the default kind; this test reruns the GEMM parity files in a
-child process with the other kind, so both stay bit-exact in their block dots
-and within max-abs-rel 1e-3 of the oracle."""
+"""The Q8_0 GEMM has three operand kinds (gemm_q8.cu): exact fp16 copies of
+the quants with the block scales applied on the CUDA cores ("f16"), the int8
+quants with kind::i8 MMAs likewise ("i8"), and fp16 copies with the scale
+products from a one-hot tensor-core MMA ("f16s", the default).  The library
+picks one per process (PXQ_Q8_0_MMA, read once).  The rest of the GPU suite
+runs the default kind; this test reruns the GEMM parity files in a child
+process with each kind, so all stay bit-exact in their block dots and within
+max-abs-rel 1e-3 of the oracle."""
 import os
 import subprocess
 import sys
@@ -15,7 +17,7 @@ from conftest import ROOT
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("kind", ["f16", "i8"])
+@pytest.mark.parametrize("kind", ["f16", "i8", "f16s"])
 def test_q8_0_gemm_parity_in_each_mma_kind(kind):
     env = dict(os.environ, PXQ_Q8_0_MMA=kind)
     files = [os.path.join(ROOT, "tests", f) for f in ("test_gpu_parity.py", "test_gpu_baseline_shapes.py")]

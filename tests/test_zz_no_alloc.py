@@ -23,7 +23,7 @@ def _p(t):
     return C.c_void_p(t.data_ptr()) if t is not None else C.c_void_p(0)
 
 
-@pytest.mark.parametrize("wtype", [8, 13])
+@pytest.mark.parametrize("wtype", [8, 13, 14])
 def test_noalloc_matches_allocating_matvec_twice(pxq, wtype):
     import torch
 
@@ -33,9 +33,10 @@ def test_noalloc_matches_allocating_matvec_twice(pxq, wtype):
     W = pxq.Weight(w, wtype, inner, rows)
     stream = torch.cuda.current_stream()
     sp = C.c_void_p(stream.cuda_stream)
-    # two calls in a row with different inputs and shapes: the second reuses
-    # the static scratch the first one filled
-    for call, (columns, first, count) in enumerate(((8, 0, 300), (3, 7, 250))):
+    # calls in a row with different inputs and shapes, each reusing the static
+    # scratch the one before filled: 8 activation rows (a separate quantize
+    # kernel for the K-quants), then 3 and 1 (the matvec quantizes them itself)
+    for call, (columns, first, count) in enumerate(((8, 0, 300), (3, 7, 250), (1, 0, 300))):
         x = torch.from_numpy(synth.activations(columns, inner, seed=30 + call)).cuda()
         bias = torch.linspace(-0.5, 0.5, count, device="cuda")
         want = torch.empty((columns, count), device="cuda")
@@ -80,4 +81,38 @@ def test_noalloc_rejects_oversized_activation(pxq):
     rc = lib.pxq_matvec_noalloc(W.handle, 0, rows, _p(x), 8, _p(y), rows, None, None)
     assert rc == pxq.ERR_UNSUPPORTED
     assert "PXQ_NOALLOC_SCRATCH_BYTES" in pxq.last_error()
+    W.release()
+
+
+def test_bounded_wait_timeout_then_both_scratches_recover(pxq, oracle):
+    """Failure detection without a fault: a matvec whose CTA 0 loads nothing
+    (pxq_debug_matvec_stall) gives up its bounded waits after their limit and
+    records a status; pxq_synchronize reports PXQ_ERR_DEVICE_STATUS.  The
+    interrupted call leaves split-K counts behind in the scratch it used --
+    the static no-allocation array or the stream's buffer -- and the next
+    fused calls (which have no quantize kernel to clear them) must still
+    compute correctly, because pxq_synchronize zeroes them on that error."""
+    import torch
+
+    lib = pxq.load()
+    rows, inner = 200, 18944  # split-K over the whole grid, one activation row: the fused path
+    w = synth.random_q5_K(rows, inner, np.random.default_rng(5))
+    W = pxq.Weight(w, 13, inner, rows)
+    xh = synth.activations(1, inner, seed=6)
+    ok, ref = oracle.quant_matmul(w, 13, xh, rows)
+    assert ok
+    x = torch.from_numpy(xh).cuda()
+    sp = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for static in (1, 0):
+        junk = torch.empty((1, rows), device="cuda")
+        assert lib.pxq_debug_matvec_stall(W.handle, _p(x), 1, _p(junk), static, sp) == 0, pxq.last_error()
+        assert lib.pxq_synchronize(sp) == pxq.ERR_DEVICE_STATUS
+        assert "gave up" in pxq.last_error()
+        for name in ("pxq_matvec_noalloc", "pxq_matvec"):
+            for _ in range(2):
+                y = torch.full((1, rows), float("nan"), device="cuda")
+                rc = getattr(lib, name)(W.handle, 0, rows, _p(x), 1, _p(y), rows, None, sp)
+                assert rc == 0, pxq.last_error()
+                assert lib.pxq_synchronize(sp) == 0, pxq.last_error()
+                assert max_abs_rel(y.cpu().numpy(), ref) <= TOL, (static, name)
     W.release()
