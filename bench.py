@@ -336,7 +336,7 @@ def run_gemm_workload(args, dist: Dist, wl: dict):
     ops = 2.0 * M * N * K
     mean_step = statistics.mean(step_ms)
     job_ms = dist.max(mean_step)
-    value = dist.world * ops / (job_ms * 1e-3) / 1e12
+    value = ops / (job_ms * 1e-3) / 1e12
     gemm_ms = dist.max(statistics.mean(kernel_ms["gemm"]))
     quant_ms = dist.max(statistics.mean(kernel_ms["quantize"]))
     hbm, bf16, bf16_sus, peak_src = measured_peaks()
@@ -351,7 +351,7 @@ def run_gemm_workload(args, dist: Dist, wl: dict):
         "warmup": args.warmup,
         "ms_per_step": round(job_ms, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "i8xi8->f32",
         "data": "synthetic (seeded N(0,1) activations; " + ("weights with uniformly random Q6_K fields)" if wtype == Q6_K
@@ -359,16 +359,17 @@ def run_gemm_workload(args, dist: Dist, wl: dict):
         "config": {"workload": f"{args.workload}: {wl['name']}", "M": M, "N": N, "K": K,
                    "weight_type": TYPE_NAMES[wtype],
                    "activation_quant": "Q8_0" if wtype == Q8_0 else "Q8_K",
-                   "per_rank_M": M, "global_M": M * dist.world, "parallelism": f"dp{dist.world}",
+                   "parallelism": "one GPU (N>1: the same problem N-sharded)",
                    "l2": "flushed between timed steps (256 MB write, outside the events)"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": bf16, "unit": "TFLOP/s",
                      "frac": round(achieved / bf16, 4),
                      "peak_source": f"{peak_src} bf16 dense (burst); the GEMM issues kind::f16 MMA on exact int8 values",
                      "int8_peak_equiv": 2 * bf16, "int8_frac": round(achieved / (2 * bf16), 4),
-                     "kernel": "k_gemm", "kernel_ms": round(gemm_ms, 4), "quantize_ms": round(quant_ms, 4),
+                     "kernel": "k_gemm_q8s" if wtype == Q8_0 else "k_gemm", "kernel_ms": round(gemm_ms, 4),
+                     "quantize_ms": round(quant_ms, 4),
                      "traffic": traffic},
         "clocks": clocks,
-        "gpu_launches": int(dist.sum(launches_per_step * args.steps)),
+        "gpu_launches": launches_per_step * args.steps,
         "library_launch_counter": pxq.kernel_launches() - launches0,
     }
     # end to end through the host-buffer C-ABI drop-in (cpu_quant_matmul)
@@ -406,7 +407,7 @@ def e2e_host(args, dist: Dist, wbytes, wtype, x_host, rows, ops):
         assert rc == 0, pxq.last_error()
     dist.barrier()
     t = dist.max(statistics.mean(times))
-    return {"value": round(dist.world * ops / t / 1e12, 3), "unit": "TOPS", "h2d_bytes_per_step": int(x_host.nbytes),
+    return {"value": round(ops / t / 1e12, 3), "unit": "TOPS", "h2d_bytes_per_step": int(x_host.nbytes),
             "d2h_bytes_per_step": int(M * rows * 4), "ms_per_step": round(t * 1e3, 3),
             "timing": "host wall clock around the synchronous C-ABI call (pinned host buffers)",
             "api": "pxq_quant_matmul (cpu_quant_matmul drop-in)"}
@@ -886,7 +887,8 @@ def run_gemm_sharded(args, dist: Dist, wl: dict):
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": bf16, "unit": "TFLOP/s",
                      "frac": round(achieved / bf16, 4), "peak_source": f"{peak_src} bf16 dense (burst)",
                      "int8_peak_equiv": 2 * bf16, "int8_frac": round(achieved / (2 * bf16), 4),
-                     "kernel": "k_gemm_q8 (this rank's shard)", "kernel_ms": round(gemm_ms, 4),
+                     "kernel": "k_gemm_q8s (this rank's shard)" if wtype == Q8_0 else "k_gemm (this rank's shard)",
+                     "kernel_ms": round(gemm_ms, 4),
                      "traffic": None},
         "exchange": {"bytes_per_rank": int((G - 1) * M * sw.count * 4), "link_GBps_per_rank":
                      round((G - 1) * M * sw.count * 4 / (ms * 1e-3) / 1e9, 1),
@@ -966,7 +968,9 @@ def run_extras(args, dist: Dist) -> dict:
         else:
             def fn():
                 pxq.Activation(wtype, x).release()
-            wbytes = M * K * (1 if os.environ.get("PXQ_Q8_0_MMA", "i8") != "f16" else 2) + M * K // 32 * 4
+            kind = os.environ.get("PXQ_Q8_0_MMA", "f16s")
+            # quants (int8 for kind "i8", else fp16) and block scales (fp16 for "f16s", else fp32)
+            wbytes = M * K * (1 if kind == "i8" else 2) + M * K // 32 * (2 if kind == "f16s" else 4)
         for _ in range(3):
             fn()
         torch.cuda.synchronize()

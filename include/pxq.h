@@ -129,6 +129,24 @@ PXQ_API int pxq_weight_release(pxq_weight* w);
 /* Drop every cached weight. */
 PXQ_API int pxq_weight_cache_clear(void);
 
+/* Residency budget of the weight cache on the current device, in bytes (the
+ * Vulkan backend's cache_limit, src/backend_vulkan.cpp:421 and :1055).
+ * Cached weights -- uploads with a key and the host-buffer drop-in's own
+ * uploads -- count their device bytes against it: the raw rows plus the GEMM
+ * operand copies.  When an upload or an operand copy would exceed it, the
+ * least recently used entries give way (src/backend_vulkan.cpp:671-681,
+ * :751): the drop-in's uploads whole (made again from the caller's bytes on
+ * its next call), other cached weights their operand copies (rebuilt on the
+ * next GEMM); weights in use by a call are skipped, and an upload goes ahead
+ * when nothing is left to evict.  A cached upload larger than the whole
+ * budget fails with PXQ_ERR_UNSUPPORTED (the reference returns nullptr, its
+ * caller falls back).  Uploads without a key are the caller's and not
+ * counted.  0 restores the default: 85 % of device memory less min(512 MiB,
+ * a quarter of that). */
+PXQ_API int pxq_weight_cache_limit(uint64_t bytes);
+/* Cached bytes, budget and entries on the current device. */
+PXQ_API int pxq_weight_cache_usage(uint64_t* bytes, uint64_t* limit, uint64_t* entries);
+
 /* Device matmul through a weight: the operator behind cpu_matmul
  * (src/backend_cpu.cpp:103-133) and vulkan_matmul
  * (src/backend_vulkan.cpp:1083-1094).
@@ -154,9 +172,12 @@ PXQ_API int pxq_gemm(pxq_weight* w, size_t row_first, size_t row_count, const fl
 
 /* Host-buffer drop-in for cpu_quant_matmul (src/kernels_quant.cpp:369-412,
  * declared src/tensor.h:74): same arguments, same output layout
- * output[c*rows + r].  Weights are cached on the device by (pointer, size,
- * type); the input is copied to the device and the output back before the
- * call returns.  Returns PXQ_OK when handled, PXQ_ERR_UNSUPPORTED exactly
+ * output[c*rows + r].  Weights are cached on the device by host address,
+ * shape, type and a fingerprint of the bytes (the first and last 256 bytes
+ * and 256 samples of 16 bytes), so a buffer freed and refilled at the same
+ * address is uploaded again; the entries live in the weight cache
+ * (pxq_weight_cache_limit).  The input is copied to the device and the
+ * output back before the call returns.  Returns PXQ_OK when handled, PXQ_ERR_UNSUPPORTED exactly
  * where the reference returns false (unsupported type, zero sizes,
  * inner % block != 0, inner > INT32_MAX). */
 PXQ_API int pxq_quant_matmul(const unsigned char* weights, uint32_t type, const float* input, float* output, size_t rows,

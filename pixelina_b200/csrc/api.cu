@@ -61,6 +61,11 @@ struct DeviceCtx {
     int sms = 0;
     uint32_t* status = nullptr;  // device word written by kernels on a bounded-wait timeout
     EncodeTiledFn encode = nullptr;
+    // weight cache residency (guarded by g_mutex): the device bytes of cached
+    // weights (raw rows + GEMM operand copies) and their budget
+    uint64_t cache_bytes = 0;
+    uint64_t cache_limit = 0;
+    uint64_t cache_default = 0;
 };
 
 constexpr int kMaxDevices = 16;
@@ -85,6 +90,12 @@ int init_device(int device)
         if (prop.major != 10)
             return fail(PXQ_ERR_NO_DEVICE, "device %d is sm_%d%d; this build targets sm_100a", device, prop.major, prop.minor);
         d.sms = prop.multiProcessorCount;
+        // the weight cache's default budget, as the Vulkan backend sizes its
+        // cache_limit: 85 % of device memory less a reserve of min(512 MiB, a
+        // quarter) for activations and scratch (src/backend_vulkan.cpp:417-421)
+        const uint64_t heap = (uint64_t)((double)prop.totalGlobalMem * 0.85);
+        const uint64_t reserve = std::min<uint64_t>((uint64_t)512 << 20, heap / 4);
+        d.cache_default = d.cache_limit = heap - reserve;
         PXQ_CUDA(cudaMalloc(&d.status, 256));
         PXQ_CUDA(cudaMemset(d.status, 0, 256));
         void* fn = nullptr;
@@ -155,6 +166,7 @@ struct Packed {
     int64_t rows = 0;   // packed rows
     int64_t ldn = 0;    // row stride of the K-quant scale planes
     void* mem = nullptr;
+    uint64_t bytes = 0;       // device bytes of `mem`
     void* wv = nullptr;       // operand [rows][K]: fp16 (Q6_K: [rows][2K], even and parity planes) or Q8_0 int8
     __half* ws = nullptr;     // Q5_K min operand [rows][nsb*16]
     float* d = nullptr;       // block scales: Q8_0 d [K/32][ldn], Q5_K / Q6_K d [nsb][ldn]
@@ -181,6 +193,21 @@ struct pxq_weight {
     std::string key;
     std::unique_ptr<Packed> packed;                       // whole tensor
     std::map<std::pair<int64_t, int64_t>, std::unique_ptr<Packed>> views;  // unaligned row views
+    // weight cache (guarded by g_mutex): a keyed weight counts its device
+    // bytes against the device's budget; `internal` ones (the host-buffer
+    // drop-in's own uploads) may be evicted whole, any cached weight may lose
+    // its operand copies (rebuilt on the next GEMM); `pins` counts the calls
+    // using the weight right now, which nothing evicts under
+    uint64_t raw_bytes = 0;
+    bool cached = false, internal = false;
+    uint64_t last_use = 0;
+    int pins = 0;
+    uint64_t packed_bytes() const
+    {
+        uint64_t b = packed ? packed->bytes : 0;
+        for (const auto& kv : views) b += kv.second->bytes;
+        return b;
+    }
     ~pxq_weight()
     {
         if (raw) cudaFree(raw);
@@ -236,6 +263,93 @@ cudaError_t counted(cudaError_t e, uint64_t n = 1)
     return e;
 }
 
+// 64-bit FNV-1a over the first and last 256 bytes and 256 samples of 16
+// bytes spread over the buffer: the host-buffer drop-in's cache identity.
+uint64_t fingerprint(const void* data, uint64_t n)
+{
+    const uint8_t* p = static_cast<const uint8_t*>(data);
+    uint64_t h = 1469598103934665603ull ^ n;
+    auto mix = [&](uint64_t off, uint64_t len) {
+        for (uint64_t i = 0; i < len && off + i < n; i++) {
+            h ^= p[off + i];
+            h *= 1099511628211ull;
+        }
+    };
+    mix(0, 256);
+    if (n > 256) mix(n - 256, 256);
+    for (uint64_t k = 0; k < 256; k++) mix(n / 256 * k, 16);
+    return h;
+}
+
+// ---- weight cache residency (the Vulkan backend's weight cache,
+// src/backend_vulkan.cpp:671-681 evict, :742-758 weight) ---------------------
+std::atomic<uint64_t> g_use_clock{0};
+
+// Drop a cached weight's bytes from its device's count and forget it.
+// g_mutex held; the caller frees the weight.
+void uncache(pxq_weight* w)
+{
+    if (!w->cached) return;
+    DeviceCtx& d = g_dev[w->device];
+    d.cache_bytes -= w->raw_bytes + w->packed_bytes();
+    auto it = g_cache.find(w->key);
+    if (it != g_cache.end() && it->second == w) g_cache.erase(it);
+    w->cached = false;
+}
+
+// Evict, least recently used first, until `need` more bytes fit the budget
+// of `device`: internal weights (the host-buffer drop-in's uploads, re-made
+// from the caller's bytes on the next call) whole, other cached weights
+// their GEMM operand copies (rebuilt on the next GEMM).  Weights in use
+// (pins) and `keep` are skipped.  g_mutex held.  Like the Vulkan backend,
+// an upload still goes ahead when nothing is left to evict.
+void make_room(int device, uint64_t need, const pxq_weight* keep)
+{
+    DeviceCtx& d = g_dev[device];
+    bool synced = false;
+    while (d.cache_bytes + need > d.cache_limit) {
+        pxq_weight* victim = nullptr;
+        for (auto& kv : g_cache) {
+            pxq_weight* w = kv.second;
+            if (w->device != device || w == keep || w->pins) continue;
+            if (!w->internal && !w->packed_bytes()) continue;
+            if (!victim || w->last_use < victim->last_use) victim = w;
+        }
+        if (!victim) return;
+        if (!synced) {
+            cudaDeviceSynchronize();  // no kernel still reads what is freed
+            synced = true;
+        }
+        if (victim->internal) {
+            uncache(victim);
+            delete victim;
+        } else {
+            d.cache_bytes -= victim->packed_bytes();
+            victim->packed.reset();
+            victim->views.clear();
+        }
+    }
+}
+
+// A weight used by a call: most recently used, and not evicted until the call
+// has queued its work.
+struct Pin {
+    pxq_weight* w;
+    explicit Pin(pxq_weight* w_) : w(w_)
+    {
+        if (!w) return;
+        std::lock_guard<std::mutex> lock(g_mutex);
+        w->pins++;
+        w->last_use = ++g_use_clock;
+    }
+    ~Pin()
+    {
+        if (!w) return;
+        std::lock_guard<std::mutex> lock(g_mutex);
+        w->pins--;
+    }
+};
+
 int build_packed(const DeviceCtx* d, pxq_weight* w, int64_t first, int64_t count, std::unique_ptr<Packed>& out,
                  cudaStream_t s)
 {
@@ -258,10 +372,13 @@ int build_packed(const DeviceCtx* d, pxq_weight* w, int64_t first, int64_t count
     const size_t off_d = off_ws + round_up((int64_t)ws_bytes, 1024);
     const size_t off_dm = off_d + round_up((int64_t)s_bytes, 1024);
     const size_t total = off_dm + round_up((int64_t)dm_bytes, 1024) + 1024;
+    if (w->cached) make_room(w->device, total, w);
     if (cudaMalloc(&pk->mem, total) != cudaSuccess) {
         cudaGetLastError();
         return fail(PXQ_ERR_NO_MEMORY, "cannot allocate %zu bytes for the GEMM operand copy", total);
     }
+    pk->bytes = total;
+    if (w->cached) g_dev[w->device].cache_bytes += total;
     uint8_t* base = static_cast<uint8_t*>(pk->mem);
     pk->wv = base;
     pk->ws = reinterpret_cast<__half*>(base + off_ws);
@@ -795,15 +912,25 @@ int create_weight(DeviceCtx* d, const void* const* parts, int nparts, int bytes_
     if (inner > 0x7fffffffu || rows * nparts > 0x7fffffffu)
         return fail(PXQ_ERR_UNSUPPORTED, "weight shape [%zu, %zu] exceeds INT32_MAX", inner, rows);
     std::string k = key ? std::string(key) : std::string();
+    const bool q6t = type == PXQ_TYPE_Q6_K;
+    const uint64_t stride_dev = q6t ? (uint64_t)(inner / 256) * kQ6KPadBytes : pxq_weight_bytes(inner, 1, type);
+    const uint64_t raw_need = stride_dev * (uint64_t)(rows * nparts) + 64;
     if (!k.empty()) {
         std::lock_guard<std::mutex> lock(g_mutex);
         auto it = g_cache.find(k);
         if (it != g_cache.end() && it->second->device == t_device) {
             if (it->second->gated != (nparts == 2))
                 return fail(PXQ_ERR_INVALID, "cached weight \"%s\" was uploaded %s gated", k.c_str(), nparts == 2 ? "not" : "as");
+            it->second->last_use = ++g_use_clock;
             *out = it->second;
             return PXQ_OK;
         }
+        // a tensor larger than the whole budget is not cached: the reference's
+        // "return nullptr" (src/backend_vulkan.cpp:750), the caller falls back
+        if (raw_need > d->cache_limit)
+            return fail(PXQ_ERR_UNSUPPORTED, "weight of %llu bytes exceeds the weight cache budget of %llu bytes",
+                        (unsigned long long)raw_need, (unsigned long long)d->cache_limit);
+        make_room(t_device, raw_need, nullptr);
     }
     auto w = std::make_unique<pxq_weight>();
     w->type = type;
@@ -848,12 +975,22 @@ int create_weight(DeviceCtx* d, const void* const* parts, int nparts, int bytes_
                 return rc;
         }
     }
-    pxq_weight* raw = w.release();
+    w->raw_bytes = raw_need;
     if (!k.empty()) {
         std::lock_guard<std::mutex> lock(g_mutex);
-        g_cache[k] = raw;
+        auto it = g_cache.find(k);
+        if (it != g_cache.end()) {
+            // another thread cached the same key meanwhile: keep that one
+            // (the new copy is freed when `w` goes out of scope)
+            *out = it->second;
+            return PXQ_OK;
+        }
+        w->cached = true;
+        w->last_use = ++g_use_clock;
+        g_dev[t_device].cache_bytes += raw_need;
+        g_cache[k] = w.get();
     }
-    *out = raw;
+    *out = w.release();
     return PXQ_OK;
 }
 
@@ -887,10 +1024,7 @@ int pxq_weight_release(pxq_weight* w)
     if (!w) return fail(PXQ_ERR_INVALID, "null weight");
     {
         std::lock_guard<std::mutex> lock(g_mutex);
-        if (!w->key.empty()) {
-            auto it = g_cache.find(w->key);
-            if (it != g_cache.end() && it->second == w) g_cache.erase(it);
-        }
+        uncache(w);
     }
     cudaDeviceSynchronize();
     delete w;
@@ -899,19 +1033,45 @@ int pxq_weight_release(pxq_weight* w)
 
 int pxq_weight_cache_clear(void)
 {
-    std::unordered_map<std::string, pxq_weight*> victims;
+    std::vector<pxq_weight*> victims;
     {
         std::lock_guard<std::mutex> lock(g_mutex);
-        victims.swap(g_cache);
+        for (auto& kv : g_cache) victims.push_back(kv.second);
+        for (pxq_weight* w : victims) uncache(w);
     }
     cudaDeviceSynchronize();
-    for (auto& kv : victims) delete kv.second;
+    for (pxq_weight* w : victims) delete w;
+    return PXQ_OK;
+}
+
+int pxq_weight_cache_limit(uint64_t bytes)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    std::lock_guard<std::mutex> lock(g_mutex);
+    d->cache_limit = bytes ? bytes : d->cache_default;
+    make_room(t_device, 0, nullptr);
+    return PXQ_OK;
+}
+
+int pxq_weight_cache_usage(uint64_t* bytes, uint64_t* limit, uint64_t* entries)
+{
+    DeviceCtx* d;
+    if (int rc = ensure_device(&d)) return rc;
+    std::lock_guard<std::mutex> lock(g_mutex);
+    uint64_t n = 0;
+    for (auto& kv : g_cache)
+        if (kv.second->device == t_device) n++;
+    if (bytes) *bytes = d->cache_bytes;
+    if (limit) *limit = d->cache_limit;
+    if (entries) *entries = n;
     return PXQ_OK;
 }
 
 int pxq_matvec(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* output,
                size_t ldy, const float* bias, void* stream)
 {
+    Pin pin_(w);
     DeviceCtx* d;
     if (int rc = ensure_device(&d)) return rc;
     if (int rc = check_matmul_args(w, row_first, row_count, input, columns, output, ldy)) return rc;
@@ -922,6 +1082,7 @@ int pxq_matvec(pxq_weight* w, size_t row_first, size_t row_count, const float* i
 int pxq_gemm(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* output,
              size_t ldy, const float* bias, void* stream)
 {
+    Pin pin_(w);
     DeviceCtx* d;
     if (int rc = ensure_device(&d)) return rc;
     if (int rc = check_matmul_args(w, row_first, row_count, input, columns, output, ldy)) return rc;
@@ -932,6 +1093,7 @@ int pxq_gemm(pxq_weight* w, size_t row_first, size_t row_count, const float* inp
 int pxq_matmul(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* output,
                size_t ldy, const float* bias, void* stream)
 {
+    Pin pin_(w);
     DeviceCtx* d;
     if (int rc = ensure_device(&d)) return rc;
     if (int rc = check_matmul_args(w, row_first, row_count, input, columns, output, ldy)) return rc;
@@ -942,6 +1104,7 @@ int pxq_matmul(pxq_weight* w, size_t row_first, size_t row_count, const float* i
 int pxq_matmul_scatter(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns,
                        float* const* dsts, size_t ndst, size_t ldy, size_t col_offset, void* stream)
 {
+    Pin pin_(w);
     DeviceCtx* d;
     if (int rc = ensure_device(&d)) return rc;
     if (!dsts || !ndst || ndst > (size_t)kMaxScatter) return fail(PXQ_ERR_INVALID, "1 to %d destinations (got %zu)", kMaxScatter, ndst);
@@ -1021,6 +1184,7 @@ int pxq_ipc_close(void* ptr)
 
 int pxq_matmul_gated(pxq_weight* w, const float* input, size_t columns, float* output, size_t ldy, void* stream)
 {
+    Pin pin_(w);
     DeviceCtx* d;
     if (int rc = ensure_device(&d)) return rc;
     if (!w || !input || !output) return fail(PXQ_ERR_INVALID, "null weight, input or output");
@@ -1128,6 +1292,7 @@ int pxq_attention(const float* q, size_t q_rows, const float* k, const float* v,
 int pxq_gemm_block_dots(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* dump,
                         void* stream)
 {
+    Pin pin_(w);
     DeviceCtx* d;
     if (int rc = ensure_device(&d)) return rc;
     if (int rc = check_matmul_args(w, row_first, row_count, input, columns, dump, row_count)) return rc;
@@ -1148,6 +1313,7 @@ int pxq_activation_quantize(uint32_t weight_type, const float* input, size_t col
 int pxq_matmul_quantized(pxq_weight* w, size_t row_first, size_t row_count, const pxq_activation* a, float* output,
                          size_t ldy, const float* bias, void* stream)
 {
+    Pin pin_(w);
     DeviceCtx* d;
     if (int rc = ensure_device(&d)) return rc;
     if (int rc = check_matmul_args(w, row_first, row_count, a, a ? (size_t)a->M : 0, output, ldy)) return rc;
@@ -1190,6 +1356,7 @@ int pxq_synchronize(void* stream)
 
 int pxq_debug_matvec_stall(pxq_weight* w, const float* input, size_t columns, float* output, int static_scratch, void* stream)
 {
+    Pin pin_(w);
     DeviceCtx* d;
     if (int rc = ensure_device(&d)) return rc;
     if (!w || !input || !output || w->gated) return fail(PXQ_ERR_INVALID, "null or gated weight, null input or output");
@@ -1221,6 +1388,7 @@ int pxq_gather_shards(const float* src, size_t shards, size_t columns, size_t sh
 int pxq_matmul_host(pxq_weight* w, size_t row_first, size_t row_count, const float* input, size_t columns, float* output,
                     size_t ldy)
 {
+    Pin pin_(w);
     DeviceCtx* d;
     if (int rc = ensure_device(&d)) return rc;
     if (int rc = check_matmul_args(w, row_first, row_count, input, columns, output, ldy)) return rc;
@@ -1314,10 +1482,35 @@ int pxq_quant_matmul(const unsigned char* weights, uint32_t type, const float* i
     if (!weights || !input || !output) return fail(PXQ_ERR_INVALID, "null pointer");
     DeviceCtx* d;
     if (int rc = ensure_device(&d)) return rc;
-    char key[96];
-    snprintf(key, sizeof(key), "host:%p:%zu:%zu:%u", (const void*)weights, rows, inner, type);
+    // The device copy is cached under the host address, the shape and a
+    // fingerprint of the bytes: a weight freed and replaced at the same
+    // address gets its own entry (and the stale one is dropped) instead of
+    // the old device copy.
+    const uint64_t nbytes = pxq_weight_bytes(inner, rows, type);
+    const uint64_t fp = fingerprint(weights, nbytes);
+    char prefix[96], key[128];
+    snprintf(prefix, sizeof(prefix), "host:%p:%zu:%zu:%u:", (const void*)weights, rows, inner, type);
+    snprintf(key, sizeof(key), "%s%016llx", prefix, (unsigned long long)fp);
+    {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        std::vector<pxq_weight*> stale;
+        for (auto& kv : g_cache)
+            if (kv.second->internal && !kv.second->pins && kv.first.compare(0, strlen(prefix), prefix) == 0 && kv.first != key)
+                stale.push_back(kv.second);
+        if (!stale.empty()) {
+            cudaDeviceSynchronize();
+            for (pxq_weight* w : stale) {
+                uncache(w);
+                delete w;
+            }
+        }
+    }
     pxq_weight* w = nullptr;
     if (int rc = pxq_weight_upload(weights, 0, type, inner, rows, key, &w)) return rc;
+    {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        w->internal = true;
+    }
     return pxq_matmul_host(w, 0, rows, input, columns, output, rows);
 }
 

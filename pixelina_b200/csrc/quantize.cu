@@ -89,15 +89,8 @@ __global__ void k_quantize_q8_0_blocks(const float* x, uint8_t* __restrict__ y, 
     const int64_t total = rows * quads_per_row;
     const int64_t nb = inner / kQK8_0;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < total; base += stride) {
-        const int64_t i = base + threadIdx.x;
-        const bool live = i < total;
-        const int64_t row = live ? i / quads_per_row : 0;
-        const int64_t quad = live ? i % quads_per_row : 0;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (live) v = ld_dep_f4(x + row * ldx + quad * 4);
-        const Q80Part p = q8_0_part(v);
-        if (!live) continue;
+    auto emit = [&](int64_t i, const Q80Part& p) {
+        const int64_t row = i / quads_per_row, quad = i % quads_per_row;
         const int64_t blk = quad / 8;
         const int t = (int)(quad % 8);
         uint8_t* out = y + (row * nb + blk) * kQ8_0Bytes;
@@ -106,6 +99,19 @@ __global__ void k_quantize_q8_0_blocks(const float* x, uint8_t* __restrict__ y, 
         q16[0] = (uint16_t)(p.packed & 0xffffu);
         q16[1] = (uint16_t)(p.packed >> 16);
         if (t == 0) *reinterpret_cast<__half*>(out) = p.d16;
+    };
+    // two quads per thread and trip, both loads issued before either block
+    // reduction, so twice the bytes are in flight
+    for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < total; base += 2 * stride) {
+        const int64_t i0 = base + threadIdx.x, i1 = i0 + stride;
+        const bool l0 = i0 < total, l1 = i1 < total;
+        float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+        if (l0) v0 = ld_dep_f4(x + (i0 / quads_per_row) * ldx + (i0 % quads_per_row) * 4);
+        if (l1) v1 = ld_dep_f4(x + (i1 / quads_per_row) * ldx + (i1 % quads_per_row) * 4);
+        const Q80Part p0 = q8_0_part(v0);
+        const Q80Part p1 = q8_0_part(v1);
+        if (l0) emit(i0, p0);
+        if (l1) emit(i1, p1);
     }
 }
 
@@ -118,15 +124,8 @@ __global__ void k_quantize_q8_0_operand(const float* __restrict__ x, void* __res
     const int64_t quads_per_row = inner / 4;
     const int64_t total = rows * quads_per_row;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < total; base += stride) {
-        const int64_t i = base + threadIdx.x;
-        const bool live = i < total;
-        const int64_t row = live ? i / quads_per_row : 0;
-        const int64_t quad = live ? i % quads_per_row : 0;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (live) v = ld_dep_f4(x + row * ldx + quad * 4);
-        const Q80Part p = q8_0_part(v);
-        if (!live) continue;
+    auto emit = [&](int64_t i, const Q80Part& p) {
+        const int64_t row = i / quads_per_row, quad = i % quads_per_row;
         if (kind == 1) {
             reinterpret_cast<uint32_t*>(static_cast<int8_t*>(xq) + row * inner)[quad] = p.packed;
         } else {
@@ -143,6 +142,18 @@ __global__ void k_quantize_q8_0_operand(const float* __restrict__ x, void* __res
             else
                 static_cast<float*>(dx)[(quad / 8) * ldd + row] = __half2float(p.d16);
         }
+    };
+    // two quads per thread and trip, both loads in flight together
+    for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < total; base += 2 * stride) {
+        const int64_t i0 = base + threadIdx.x, i1 = i0 + stride;
+        const bool l0 = i0 < total, l1 = i1 < total;
+        float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+        if (l0) v0 = ld_dep_f4(x + (i0 / quads_per_row) * ldx + (i0 % quads_per_row) * 4);
+        if (l1) v1 = ld_dep_f4(x + (i1 / quads_per_row) * ldx + (i1 % quads_per_row) * 4);
+        const Q80Part p0 = q8_0_part(v0);
+        const Q80Part p1 = q8_0_part(v1);
+        if (l0) emit(i0, p0);
+        if (l1) emit(i1, p1);
     }
 }
 
@@ -155,9 +166,7 @@ __global__ void k_quantize_q8_K_blocks(const float* __restrict__ x, uint8_t* __r
     const int64_t nsb = inner / kQKK;
     const int64_t total = rows * nsb;
     const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    for (int64_t w = (((int64_t)blockIdx.x * blockDim.x) >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
-        const int64_t row = w / nsb, sb = w % nsb;
-        const Q8KWarp r = q8_K_warp(x + row * ldx + sb * kQKK, lane);
+    auto emit = [&](int64_t w, const Q8KWarp& r) {
         uint8_t* out = y + w * kQ8KBytes;
         uint32_t lo = 0, hi = 0;
         int sum8 = 0;
@@ -172,6 +181,16 @@ __global__ void k_quantize_q8_K_blocks(const float* __restrict__ x, uint8_t* __r
         const int sum16 = sum8 + __shfl_xor_sync(0xffffffffu, sum8, 1);  // 16-element group = lane pair
         if ((lane & 1u) == 0) *reinterpret_cast<int16_t*>(out + 4 + kQKK + lane) = (int16_t)sum16;
         if (lane == 0) *reinterpret_cast<float*>(out) = r.d;
+    };
+    // two blocks per warp and trip, both loads in flight together
+    for (int64_t w = (((int64_t)blockIdx.x * blockDim.x) >> 5) + (threadIdx.x >> 5); w < total; w += 2 * warps) {
+        const int64_t w2 = w + warps;
+        const bool has2 = w2 < total;  // warp-uniform
+        float va[8], vb[8];
+        q8_K_load(x + (w / nsb) * ldx + (w % nsb) * kQKK, lane, va);
+        if (has2) q8_K_load(x + (w2 / nsb) * ldx + (w2 % nsb) * kQKK, lane, vb);
+        emit(w, q8_K_warp_vals(va, lane));
+        if (has2) emit(w2, q8_K_warp_vals(vb, lane));
     }
 }
 
@@ -204,9 +223,8 @@ __global__ void k_quantize_q8_K_operand(const float* __restrict__ x, __half* __r
     const int64_t nsb = inner / kQKK;
     const int64_t total = rows * nsb;
     const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    for (int64_t w = (((int64_t)blockIdx.x * blockDim.x) >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
+    auto emit = [&](int64_t w, const Q8KWarp& r) {
         const int64_t row = w / nsb, sb = w % nsb;
-        const Q8KWarp r = q8_K_warp(x + row * ldx + sb * kQKK, lane);
         __half h[8];
         int sum8 = 0;
 #pragma unroll
@@ -226,6 +244,16 @@ __global__ void k_quantize_q8_K_operand(const float* __restrict__ x, __half* __r
             *reinterpret_cast<__half2*>(amin + row * (nsb * 16) + sb * 16 + 2 * j) = pair;
         }
         if (lane == 0) dxT[sb * ldd + row] = r.d;
+    };
+    // two blocks per warp and trip, both loads in flight together
+    for (int64_t w = (((int64_t)blockIdx.x * blockDim.x) >> 5) + (threadIdx.x >> 5); w < total; w += 2 * warps) {
+        const int64_t w2 = w + warps;
+        const bool has2 = w2 < total;  // warp-uniform
+        float va[8], vb[8];
+        q8_K_load(x + (w / nsb) * ldx + (w % nsb) * kQKK, lane, va);
+        if (has2) q8_K_load(x + (w2 / nsb) * ldx + (w2 % nsb) * kQKK, lane, vb);
+        emit(w, q8_K_warp_vals(va, lane));
+        if (has2) emit(w2, q8_K_warp_vals(vb, lane));
     }
 }
 

@@ -63,6 +63,8 @@ SIGNATURES = {
     "pxq_matmul_gated": (_i, [_vp, _vp, _sz, _vp, _sz, _vp]),
     "pxq_weight_release": (_i, [_vp]),
     "pxq_weight_cache_clear": (_i, []),
+    "pxq_weight_cache_limit": (_i, [_u64]),
+    "pxq_weight_cache_usage": (_i, [C.POINTER(_u64), C.POINTER(_u64), C.POINTER(_u64)]),
     "pxq_matmul": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _sz, _vp, _vp]),
     "pxq_matvec": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _sz, _vp, _vp]),
     "pxq_gemm": (_i, [_vp, _sz, _sz, _vp, _sz, _vp, _sz, _vp, _vp]),
@@ -439,6 +441,18 @@ def matmul_quantized(w: Weight, a: Activation, row_first: int = 0, row_count: Op
         ldy = out.stride(0)
     _check(load().pxq_matmul_quantized(w.handle, row_first, rc, a.handle, _ptr(out), ldy, _ptr(bias), _stream_ptr(stream)))
     return out
+
+
+def cache_limit(nbytes: int) -> None:
+    """pxq_weight_cache_limit: the weight cache's budget on this device (0: default)."""
+    _check(load().pxq_weight_cache_limit(nbytes))
+
+
+def cache_usage() -> tuple[int, int, int]:
+    """pxq_weight_cache_usage: (cached bytes, budget, entries) on this device."""
+    b, l, n = C.c_uint64(), C.c_uint64(), C.c_uint64()
+    _check(load().pxq_weight_cache_usage(C.byref(b), C.byref(l), C.byref(n)))
+    return b.value, l.value, n.value
 
 
 def kernel_launches() -> int:
