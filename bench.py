@@ -510,7 +510,7 @@ def run_reference(args, dist: Dist):
     return {
         "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "TOPS", "n_gpus": dist.world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "i8xi8->f32",
+        "scaling": "strong", "vs_baseline": None, "dtype": "i8xi8->f32",
         "data": "synthetic (seeded N(0,1) activations; " + ("weights with uniformly random Q6_K fields)" if wtype == Q6_K
                                                             else "weights encoded from N(0,0.02))"),
         "config": {"workload": f"{args.workload}: {wl['name']}", "M": M, "N": N, "K": K,
@@ -607,7 +607,8 @@ def run_decode(args, dist: Dist, gated: bool = False):
 def run_decode_shapes(args, dist: Dist):
     """Per-shape view of BASELINE configs[3]: each decode matrix (QKV, out,
     gate/up, down) at M = 1 and 8, one call = activation quantize + matvec;
-    also gate/up and down as Q6_K (GGUF mixes Q6_K tensors into Q5_K models).
+    also gate/up and down as Q6_K (GGUF mixes Q6_K tensors into Q5_K models)
+    and QKV, gate/up and down as Q8_0 (Q8_0 models: the streamed Q8_0 matvec).
     Each shape cycles through enough distinct copies of its weight to exceed
     the 126 MB L2, replayed as a CUDA graph, so the rate is HBM, not L2."""
     import torch
@@ -621,11 +622,12 @@ def run_decode_shapes(args, dist: Dist):
     hbm, _, _, peak_src = measured_peaks()
     results = {}
     shapes = [("qkv", QKV, H, Q5_K), ("out", H, H, Q5_K), ("gate_up", F, H, Q5_K), ("down", H, F, Q5_K),
-              ("gate_up q6_K", F, H, Q6_K), ("down q6_K", H, F, Q6_K)]
+              ("gate_up q6_K", F, H, Q6_K), ("down q6_K", H, F, Q6_K),
+              ("qkv q8_0", QKV, H, Q8_0), ("gate_up q8_0", F, H, Q8_0), ("down q8_0", H, F, Q8_0)]
     for name, n, k, wtype in shapes:
         wbytes = pxq.weight_bytes(k, n, wtype)
         copies = max(2, -(-(320 << 20) // wbytes))
-        make = gpu_random_q5_K if wtype == Q5_K else gpu_random_q6_K
+        make = {Q5_K: gpu_random_q5_K, Q6_K: gpu_random_q6_K, Q8_0: gpu_random_q8_0}[wtype]
         ws = [pxq.Weight(make(n, k, gen), wtype, k, n) for _ in range(copies)]
         for M in (1, 8):
             x = torch.randn((M, k), device="cuda", generator=gen)
@@ -971,21 +973,36 @@ def run_extras(args, dist: Dist) -> dict:
             kind = os.environ.get("PXQ_Q8_0_MMA", "f16s")
             # quants (int8 for kind "i8", else fp16) and block scales (fp16 for "f16s", else fp32)
             wbytes = M * K * (1 if kind == "i8" else 2) + M * K // 32 * (2 if kind == "f16s" else 4)
+        # 10 calls captured in a CUDA graph (no host launch gaps), replayed
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph):
+            for _ in range(10):
+                fn()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
         e0, e1 = ev_pair()
         e0.record()
-        for _ in range(10):
-            fn()
+        for _ in range(5):
+            graph.replay()
         e1.record()
         torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / 10
+        ms = e0.elapsed_time(e1) / 50
+        del graph
         nbytes = M * K * 4 + wbytes
         out[key] = {"M": M, "K": K, "ms": round(ms, 4), "GBps": round(nbytes / (ms * 1e-3) / 1e9, 1),
                     "hbm_frac": round(nbytes / (ms * 1e-3) / 1e9 / hbm, 4), "bytes": int(nbytes),
-                    "timing": "10 back-to-back calls (each a quantize kernel; the GGUF-block calls include the output "
-                              "tensor's allocation from the caching allocator)"}
+                    "timing": "10 calls per CUDA graph, 5 replays (each call one quantize kernel; inputs and outputs "
+                              "larger than L2)"}
         del x
     # the decode matvec stack, gate/up as one gated call
     dec = run_decode(args, dist, gated=True)

@@ -329,8 +329,9 @@ PXQ_API uint64_t pxq_kernel_launches(void);
  * static device array of PXQ_NOALLOC_SCRATCH_BYTES owned by this library
  * (held on every device that loads it, until exit) instead of freshly
  * allocated scratch.  The array holds the matvec's counters (16 KiB), the
- * quantized activation rows (columns * inner/32 * 34 bytes for Q8_0,
- * columns * inner/256 * 288 for Q5_K, columns * inner/256 * 304 for Q6_K;
+ * quantized activation rows (columns * inner/256 * 288 bytes for Q5_K and
+ * for Q8_0 when inner % 256 == 0, columns * inner/32 * 34 + 64 for other
+ * Q8_0, columns * inner/256 * 304 for Q6_K;
  * none when the matvec quantizes a small activation itself) and its fp32
  * partial sums (up to 2 * columns * 256 bytes per CTA, about 1.2 MB for 8
  * columns on a 148-SM GPU); a call whose total exceeds

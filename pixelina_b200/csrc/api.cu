@@ -243,14 +243,16 @@ std::unordered_map<std::string, pxq_weight*> g_cache;  // guarded by g_mutex
 // Q8_0 GEMM operand kind (gemm_q8.cu): 0 = exact fp16 copies of the quants
 // (kind::f16) with the scales applied on the CUDA cores, 1 = the int8 quants
 // (kind::i8) likewise, 2 = fp16 copies with the scale products from a
-// one-hot tensor-core MMA.  Read once from PXQ_Q8_0_MMA ("f16", "i8",
-// "f16s"); the default is kind 2, the fastest measured.
+// one-hot tensor-core MMA, 3 = kind 0's operands on CTA pairs (256 x 256
+// tiles).  Read once from PXQ_Q8_0_MMA ("f16", "i8", "f16s", "pair"); the
+// default is kind 2.
 int q8_operand_kind()
 {
     static const int v = [] {
         const char* e = getenv("PXQ_Q8_0_MMA");
         if (e && strcmp(e, "f16") == 0) return 0;
         if (e && strcmp(e, "i8") == 0) return 1;
+        if (e && strcmp(e, "pair") == 0) return 3;
         return 2;
     }();
     return v;
@@ -522,8 +524,10 @@ int quantize_activation(DeviceCtx* d, uint32_t wtype, const float* input, int64_
             a->tmDx = a->tmX;
         } else if (!rc) {
             a->tmXs = a->tmX;
-            rc = make_map(d, &a->tmDx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a->scale, M, nb, a->ldd * 4,
-                          (uint32_t)gemm_tile_activation_rows(wtype), (uint32_t)gemm_q8_scale_box(kind), CU_TENSOR_MAP_SWIZZLE_NONE);
+            // the drain's activation scales: a whole output tile's rows (kind 3: a CTA pair's 256)
+            const uint32_t tile_rows = kind == 3 ? 256u : (uint32_t)gemm_tile_activation_rows(wtype);
+            rc = make_map(d, &a->tmDx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a->scale, M, nb, a->ldd * 4, tile_rows,
+                          (uint32_t)gemm_q8_scale_box(kind), CU_TENSOR_MAP_SWIZZLE_NONE);
         }
         if (rc) {
             cudaFreeAsync(a->mem, s);
@@ -955,20 +959,22 @@ int create_weight(DeviceCtx* d, const void* const* parts, int nparts, int bytes_
         if (int rc = copy_rows(w.get(), parts[i], bytes_on_device, (int64_t)(i * rows), (int64_t)rows)) return rc;
     const uint64_t all_rows = (uint64_t)w->rows;
     std::memset(w->mv_map, 0, sizeof(w->mv_map));
-    if (type == PXQ_TYPE_Q5_K || q6) {
+    const bool q8_streamed = type == PXQ_TYPE_Q8_0 && inner % 256 == 0;
+    if (type == PXQ_TYPE_Q5_K || q6 || q8_streamed) {
         // the matvec's TMA views, one box = one stage of a tr-row tile
         // (kMvStageSuperBlocks*16/tr super-blocks): Q5_K 64-row stages as a
         // 2-D view (rows of stride/8 64-bit words), the others as a 3-D view
-        // (super-block, row, super-block words) that lands super-block-major
-        const uint32_t sbb = q6 ? kQ6KPadBytes : kQ5KBytes;
-        if (!q6) {
+        // (super-block, row, super-block words) that lands super-block-major;
+        // a Q8_0 "super-block" is eight raw blocks (272 bytes)
+        const uint32_t sbb = q6 ? kQ6KPadBytes : q8_streamed ? kQ80SbBytes : kQ5KBytes;
+        if (type == PXQ_TYPE_Q5_K) {
             if (int rc = make_map(d, &w->mv_map[matvec_map_index(64)], CU_TENSOR_MAP_DATA_TYPE_UINT64, w->raw,
                                   (uint64_t)w->stride / 8, all_rows, (uint64_t)w->stride,
                                   (uint32_t)(kMvStageSuperBlocks / 4 * kQ5KBytes / 8), 64, CU_TENSOR_MAP_SWIZZLE_NONE))
                 return rc;
         }
         for (int tr : {64, 32, 16}) {
-            if (tr == 64 && !q6) continue;
+            if (tr == 64 && type == PXQ_TYPE_Q5_K) continue;
             if (int rc = make_map3(d, &w->mv_map[matvec_map_index(tr)], CU_TENSOR_MAP_DATA_TYPE_UINT64, w->raw, sbb / 8,
                                    all_rows, nsb, (uint64_t)w->stride, sbb, sbb / 8, (uint32_t)tr,
                                    (uint32_t)(kMvStageSuperBlocks * 16 / tr)))
@@ -1202,7 +1208,7 @@ int pxq_matmul_gated(pxq_weight* w, const float* input, size_t columns, float* o
         free_activation(a, s);
         return rc;
     }
-    if (w->type == kTypeQ5_K || w->type == kTypeQ6_K) {
+    if (w->type == kTypeQ5_K || w->type == kTypeQ6_K || w->inner % 256 == 0) {
         // one matvec: each CTA streams gate tile j and up tile j and writes silu(g) * u
         const MatvecPlan plan = plan_matvec(w->type, w->rows, w->inner, (int64_t)columns, d->sms, true, true);
         void* scratch = stream_scratch(t_device, s, plan.total_bytes);
@@ -1217,7 +1223,8 @@ int pxq_matmul_gated(pxq_weight* w, const float* input, size_t columns, float* o
         if (e != cudaSuccess) return fail(PXQ_ERR_CUDA, "gated matvec launch failed: %s", cudaGetErrorString(e));
         return PXQ_OK;
     }
-    // Q8_0: matvec over the 2F rows into scratch after the matvec's own, then the epilogue
+    // Q8_0 with K not a multiple of 256: matvec over the 2F rows into scratch
+    // after the matvec's own, then the epilogue
     const MatvecPlan plan = plan_matvec(w->type, w->rows, w->inner, (int64_t)columns, d->sms, true);
     const size_t off_s = (plan.total_bytes + 255) & ~(size_t)255;
     const size_t need = off_s + (size_t)columns * (size_t)w->rows * 4;

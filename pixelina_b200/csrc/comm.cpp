@@ -190,8 +190,40 @@ int comm_wait(pxq_comm* c, cudaStream_t s, const char* what)
     }
 }
 
-// A non-blocking NCCL call: ncclInProgress is the normal return.
+// A non-blocking NCCL call: ncclInProgress is a normal return.
 bool nccl_ok(ncclResult_t r) { return r == ncclSuccess || r == ncclInProgress; }
+
+// After a call on a non-blocking communicator returned ncclInProgress (a
+// collective whose connections NCCL is still setting up in the background,
+// typically the first of its kind), NCCL takes no further call on the
+// communicator until its state is ncclSuccess again: poll it, against the
+// deadline.  This waits for the call to be queued, not for its completion on
+// the device.  On an error or a timeout the communicator is aborted.
+int nccl_queued(pxq_comm* c, ncclResult_t r, const char* what)
+{
+    if (r == ncclSuccess) return PXQ_OK;
+    if (r != ncclInProgress) {
+        comm_break(c);
+        return comm_fail(PXQ_ERR_CUDA, "%s could not be queued: NCCL error %d (%s); communicator aborted", what, (int)r,
+                         nccl_error(r));
+    }
+    const auto deadline = clk::now() + std::chrono::milliseconds(c->timeout_ms);
+    while (true) {
+        ncclResult_t ar = ncclSuccess;
+        if (nccl().CommGetAsyncError(c->nccl, &ar) != ncclSuccess) ar = ncclInternalError;
+        if (ar == ncclSuccess) return PXQ_OK;
+        if (ar != ncclInProgress) {
+            comm_break(c);
+            return comm_fail(PXQ_ERR_CUDA, "%s: NCCL error %d (%s); communicator aborted", what, (int)ar, nccl_error(ar));
+        }
+        if (clk::now() > deadline) {
+            comm_break(c);
+            return comm_fail(PXQ_ERR_TIMEOUT, "%s: not queued after %d ms (a rank missing?); communicator aborted", what,
+                             c->timeout_ms);
+        }
+        std::this_thread::yield();
+    }
+}
 
 int check_comm(pxq_comm* c)
 {
@@ -207,11 +239,7 @@ int check_comm(pxq_comm* c)
 // Device-ordered barrier of all ranks on `s`.
 int comm_barrier(pxq_comm* c, cudaStream_t s)
 {
-    if (!nccl_ok(nccl().AllReduce(c->flag, c->flag, 1, ncclInt32, ncclMax, c->nccl, s))) {
-        comm_break(c);
-        return comm_fail(PXQ_ERR_CUDA, "barrier all-reduce could not be queued");
-    }
-    return PXQ_OK;
+    return nccl_queued(c, nccl().AllReduce(c->flag, c->flag, 1, ncclInt32, ncclMax, c->nccl, s), "barrier all-reduce");
 }
 
 }  // namespace
@@ -343,11 +371,11 @@ int pxq_sharded_output_create(pxq_comm* comm, size_t columns, size_t ldy, pxq_sh
     if (!rc && cudaMemcpyAsync(dh + (size_t)comm->rank * PXQ_IPC_HANDLE_BYTES, handle, PXQ_IPC_HANDLE_BYTES,
                                cudaMemcpyHostToDevice, comm->stream) != cudaSuccess)
         rc = comm_fail(PXQ_ERR_CUDA, "handle upload failed");
-    if (!rc && !nccl_ok(nccl().AllGather(dh + (size_t)comm->rank * PXQ_IPC_HANDLE_BYTES, dh, PXQ_IPC_HANDLE_BYTES, ncclUint8,
-                                      comm->nccl, comm->stream))) {
-        comm_break(comm);
-        rc = comm_fail(PXQ_ERR_CUDA, "handle all-gather could not be queued");
-    }
+    if (!rc)
+        rc = nccl_queued(comm,
+                         nccl().AllGather(dh + (size_t)comm->rank * PXQ_IPC_HANDLE_BYTES, dh, PXQ_IPC_HANDLE_BYTES, ncclUint8,
+                                          comm->nccl, comm->stream),
+                         "handle all-gather");
     if (!rc) rc = comm_wait(comm, comm->stream, "output handle exchange");
     if (!rc && cudaMemcpy(all, dh, (size_t)G * PXQ_IPC_HANDLE_BYTES, cudaMemcpyDeviceToHost) != cudaSuccess)
         rc = comm_fail(PXQ_ERR_CUDA, "handle download failed");
@@ -423,10 +451,7 @@ int pxq_sharded_matmul(pxq_comm* comm, pxq_weight* shard, size_t shard_rows, con
         return comm_fail(PXQ_ERR_NO_MEMORY, "all-gather scratch of %zu bytes", block * (size_t)(G + 1) * sizeof(float));
     }
     int rc = pxq_matmul(shard, 0, shard_rows, input, columns, local, shard_rows, nullptr, s);
-    if (!rc && !nccl_ok(nccl().AllGather(local, gathered, block, ncclFloat32, comm->nccl, s))) {
-        comm_break(comm);
-        rc = comm_fail(PXQ_ERR_CUDA, "all-gather could not be queued");
-    }
+    if (!rc) rc = nccl_queued(comm, nccl().AllGather(local, gathered, block, ncclFloat32, comm->nccl, s), "all-gather");
     if (!rc) rc = pxq_gather_shards(gathered, (size_t)G, columns, shard_rows, output, ldy, s);
     cudaFreeAsync(local, s);
     cudaFreeAsync(gathered, s);

@@ -38,6 +38,7 @@
 // The epilogue (bias, TMA-store staging, stores into peers' outputs for the
 // N-sharded path, the gated feed-forward product, the block-dot dump) is
 // the one of gemm.cu, per accumulator layout.
+#include <mutex>
 #include "pxq_device.cuh"
 #include "pxq_internal.h"
 
@@ -824,6 +825,446 @@ done:
     if (warp == 0) tmem_dealloc(tmem_base, 512);
 }
 
+// ---------------------------------------------------------------------------
+// OPK 3: CTA pairs.  The pair's tile is 256 weight rows (the MMA's M; each
+// CTA stages and accumulates its 128) by 256 activation rows (the MMA's N;
+// each CTA stages 128 of them and receives all 256 columns in its TMEM), so
+// per block an SM drains 128 x 256 block dots and streams 16 KB of fp16
+// operands for them -- half the operand bytes per output of the one-CTA
+// kinds.  Two 256-column accumulator slots alternate per 32-block.  The
+// drain reads each block dot once from TMEM (32x32b layout: a thread holds
+// one weight row, whose scale is a register, and 128 activation rows, whose
+// scales are shared-memory broadcasts) and does two packed fp32 operations
+// per element pair: S = dX * dW, acc = fma(S, I, acc).  That FP32 work --
+// 2 * 128 * 256 lane operations per block and SM, 512 clocks at 128 lanes
+// per clock -- is the kernel's floor; the MMAs (292 clocks per block on the
+// f16 pipe) and the TMEM reads (about 280) fit beside it.
+//   Roles (12 warps): warps 0-7 drain (warp w: TMEM lane quadrant w % 4,
+//   columns 128 * (w / 4) ..+128); warp 8 loads (both CTAs); warp 9 of the
+//   even CTA issues the pair MMAs.  Barriers as in gemm.cu's pair kernel:
+//   both CTAs' stage loads complete on the even CTA's stage barrier, its
+//   commits arrive on both CTAs' barriers, the odd CTA's drain releases slots
+//   on the even CTA's barriers.
+constexpr int Q8P_TN = 128;                         // weight rows per CTA (TMEM lanes)
+constexpr int Q8P_TMP = 256;                        // activation rows per pair tile (TMEM columns per slot)
+constexpr int Q8P_XR = 128;                         // activation rows staged per CTA
+constexpr int Q8P_STAGE = 2 * Q8_OP_BYTES;          // W [128][64 fp16] | X [128][64 fp16], 128B swizzle: 32 KB
+constexpr int Q8P_STAGES = 4;
+constexpr int Q8P_BPS = 2;                          // 32-blocks per stage and per scale entry
+constexpr int Q8P_SE = 8;                           // scale entries
+constexpr int Q8P_ENTRY = Q8P_BPS * (Q8P_TN + Q8P_TMP) * 4;  // dW [2][128] | dX [2][256] fp32: 3 KB
+constexpr int Q8P_DX_OFF = Q8P_BPS * Q8P_TN * 4;
+constexpr int Q8P_DRAIN = 8;
+constexpr int Q8P_THREADS = 384;
+constexpr int Q8P_HC = 128;                         // TMEM columns per drain warp
+constexpr int Q8P_CW = 16;                          // columns per TMEM load
+constexpr uint32_t Q8P_DRAIN_REGS = 224, Q8P_PRODUCER_REGS = 56;
+static_assert(256 * Q8P_DRAIN_REGS + 128 * Q8P_PRODUCER_REGS <= Q8P_THREADS * 168, "setmaxnreg split");
+constexpr int Q8P_OFF_SCALES = Q8P_STAGES * Q8P_STAGE;
+constexpr int Q8P_OFF_STAGING = Q8P_OFF_SCALES + Q8P_SE * Q8P_ENTRY;
+constexpr int Q8P_STAGING = Q8P_DRAIN * 2 * 32 * 32 * 4;  // two [32 activation rows][32 weight rows] fp32 per drain warp
+constexpr int Q8P_OFF_BAR = Q8P_OFF_STAGING + Q8P_STAGING;
+// full/empty, scale full/empty, slot full/empty, MMA drain-out, gated hand-over
+constexpr int Q8P_NUM_BARS = 2 * Q8P_STAGES + 2 * Q8P_SE + 2 * 2 + 1 + 2;
+constexpr int Q8P_SMEM = Q8P_OFF_BAR + Q8P_NUM_BARS * 8 + 16 + 1024;
+static_assert(Q8P_SMEM <= 232448, "shared memory");
+static_assert(Q8P_STAGE % 1024 == 0 && Q8P_OFF_SCALES % 1024 == 0 && Q8P_ENTRY % 128 == 0, "alignment");
+static_assert(2 * Q8P_TMP <= 512, "TMEM columns");
+static_assert(Q8P_STAGING >= 4 * Q8P_HC * 32 * 4, "gated hand-over buffer");
+
+// acc[j] += (dx[j] * dw) * I[j] over one TMEM load's columns, two per instruction
+// (pix_dot_q8_0: the fp32 product of the two fp16 scales, exact, times the
+// exact block dot, accumulated with one rounding).
+__device__ __forceinline__ void q8p_fma(float* acc, const uint32_t (&v)[Q8P_CW], const float* dx, float dw)
+{
+#pragma unroll
+    for (int j = 0; j < Q8P_CW; j += 4) {
+        const float4 d4 = *reinterpret_cast<const float4*>(dx + j);
+        float s0, s1, s2, s3;
+        fmul2(s0, s1, d4.x, d4.y, dw, dw);
+        fmul2(s2, s3, d4.z, d4.w, dw, dw);
+        ffma2(acc[j], acc[j + 1], s0, s1, __uint_as_float(v[j]), __uint_as_float(v[j + 1]));
+        ffma2(acc[j + 2], acc[j + 3], s2, s3, __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+    }
+}
+
+// tensor maps:
+//   tmW   weight operand fp16 [N][K]             box {64, 128}  128B swizzle
+//   tmX   activation operand fp16 [M][K]         box {64, 128}  128B swizzle
+//   tmDw  weight block scales fp32 [K/32][ldn]   box {128, 2}
+//   tmDx  activation block scales fp32 [K/32][ldm] box {256, 2}
+//   tmY   output fp32 [M][ldy], box {32, 32} (TMA-store epilogue)
+template <bool DUMP>
+__global__ void __launch_bounds__(Q8P_THREADS, 1)
+    k_gemm_q8p(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+               const __grid_constant__ CUtensorMap tmDw, const __grid_constant__ CUtensorMap tmDx,
+               const __grid_constant__ CUtensorMap tmY, const Q8Params p)
+{
+    constexpr uint32_t IDESC = idesc_f16_f32(2 * Q8P_TN, Q8P_TMP);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Q8P_OFF_BAR);
+    uint64_t* full = bars;                   // even CTA: stage loaded (both CTAs' bytes)
+    uint64_t* empty = full + Q8P_STAGES;     // stage consumed by the MMAs (both CTAs)
+    uint64_t* sfull = empty + Q8P_STAGES;    // this CTA's scale entry loaded
+    uint64_t* sempty = sfull + Q8P_SE;       // ... and read by this CTA's drain warps
+    uint64_t* tfull = sempty + Q8P_SE;       // slot holds a finished block (both CTAs)
+    uint64_t* tempty = tfull + 2;            // even CTA: slot read by both CTAs' drain warps
+    uint64_t* mma_done = tempty + 2;         // even CTA: every issued MMA finished (exit path)
+    uint64_t* merge = mma_done + 1;          // gated epilogue hand-over
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Q8P_NUM_BARS);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+    uint8_t* scale_ring = smem + Q8P_OFF_SCALES;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < Q8P_STAGES; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < Q8P_SE; i++) {
+            mbar_init(&sfull[i], 1);
+            mbar_init(&sempty[i], Q8P_DRAIN);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], 2 * Q8P_DRAIN);  // the drain warps of both CTAs
+        }
+        mbar_init(mma_done, 1);
+        mbar_init(&merge[0], 32 * Q8P_DRAIN);
+        mbar_init(&merge[1], 32 * Q8P_DRAIN);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc_pair(tmem_slot, 512);
+        tmem_relinquish_pair();
+    }
+    if (warp == 8 && lane == 0) {
+        tma_prefetch_desc(&tmW);
+        tma_prefetch_desc(&tmX);
+        tma_prefetch_desc(&tmDw);
+        tma_prefetch_desc(&tmDx);
+        if (p.tma_store) tma_prefetch_desc(&tmY);
+    }
+    // barriers initialised and TMEM allocated in both CTAs before any cross-CTA traffic
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int64_t mt = (p.M + Q8P_TMP - 1) / Q8P_TMP;
+    const int64_t nt = (p.N + 2 * Q8P_TN - 1) / (2 * Q8P_TN);
+    const int64_t tiles = mt * nt;
+    const int64_t pair = (int64_t)cluster_id_x(), pairs = (int64_t)cluster_count_x();
+    const int64_t nb = p.K / kQK8_0;
+    const int64_t nstages = (nb + Q8P_BPS - 1) / Q8P_BPS;
+    uint32_t* status = p.status;
+
+    if (warp >= Q8P_DRAIN) {
+        regs_dec<Q8P_PRODUCER_REGS>();
+        if (warp == 8 && lane == 0) {
+            const uint32_t full0 = cluster_map(smem_u32(full), 0);  // the even CTA's stage barriers
+            int stage = 0, se = 0;
+            uint32_t ph = 0, sph = 0;
+            for (int64_t tile = pair; tile < tiles; tile += pairs) {
+                int64_t mi, ni;
+                q8_tile(tile, mt, nt, mi, ni);
+                const int32_t m0 = (int32_t)(mi * Q8P_TMP);
+                const int32_t mc = m0 + (int32_t)(rank * Q8P_XR);
+                const int32_t nc = (int32_t)(p.n_first + ni * 2 * Q8P_TN + rank * Q8P_TN);
+                for (int64_t kc = 0; kc < nstages; kc++) {
+                    // this CTA's block scales for its drain: its 128 weight rows, all 256 activation rows
+                    if (!mbar_wait(&sempty[se], sph ^ 1u, abort_flag, status, kDevTimeoutScaleEmpty)) goto done;
+                    uint8_t* e = scale_ring + se * Q8P_ENTRY;
+                    mbar_expect_tx(&sfull[se], Q8P_ENTRY);
+                    tma_load_2d(e, &tmDw, &sfull[se], nc, (int32_t)(kc * Q8P_BPS));
+                    tma_load_2d(e + Q8P_DX_OFF, &tmDx, &sfull[se], m0, (int32_t)(kc * Q8P_BPS));
+                    if (++se == Q8P_SE) {
+                        se = 0;
+                        sph ^= 1u;
+                    }
+                    // this CTA's halves of the stage's operands, reported to the even CTA
+                    if (!mbar_wait(&empty[stage], ph ^ 1u, abort_flag, status, kDevTimeoutEmpty)) goto done;
+                    uint8_t* st = smem + stage * Q8P_STAGE;
+                    if (leader) mbar_expect_tx(&full[stage], 2 * Q8P_STAGE);
+                    const int32_t kx = (int32_t)(kc * 64);
+                    tma_load_2d_pair(st, &tmW, full0 + 8u * stage, kx, nc);
+                    tma_load_2d_pair(st + Q8_OP_BYTES, &tmX, full0 + 8u * stage, kx, mc);
+                    if (++stage == Q8P_STAGES) {
+                        stage = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+        } else if (warp == 9 && lane == 0 && leader) {
+            int stage = 0, slot = 0;
+            uint32_t ph = 0, tph = 0;
+            for (int64_t tile = pair; tile < tiles; tile += pairs) {
+                for (int64_t kc = 0; kc < nstages; kc++) {
+                    if (!mbar_wait(&full[stage], ph, abort_flag, status, kDevTimeoutFull)) goto done;
+                    tc_fence_after();
+                    const uint32_t w_addr = smem_u32(smem + stage * Q8P_STAGE);
+                    const uint32_t x_addr = w_addr + Q8_OP_BYTES;
+#pragma unroll
+                    for (int bi = 0; bi < Q8P_BPS; bi++) {
+                        if (kc * Q8P_BPS + bi >= nb) break;
+                        if (!mbar_wait_cluster(&tempty[slot], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
+                        tc_fence_after();
+                        const uint32_t d = tmem_base + (uint32_t)(slot * Q8P_TMP);
+#pragma unroll
+                        for (int k = 0; k < 2; k++) {
+                            const uint32_t koff = (uint32_t)(bi * 2 + k) * 32u;  // 16 fp16 of K per MMA
+                            mma_f16_pair(d, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC, (uint32_t)k);
+                        }
+                        mma_commit_pair(&tfull[slot]);
+                        if (++slot == 2) {
+                            slot = 0;
+                            tph ^= 1u;
+                        }
+                    }
+                    mma_commit_pair(&empty[stage]);
+                    if (++stage == Q8P_STAGES) {
+                        stage = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+        }
+    } else {
+        // ------------------------------------------------------ drain warps --
+        regs_inc<Q8P_DRAIN_REGS>();
+        const uint32_t quad = warp & 3u, half = warp >> 2;
+        const uint32_t lane_base = (quad * 32u) << 16;
+        const uint32_t tempty0 = cluster_map(smem_u32(tempty), 0);  // the even CTA's slot barriers
+        auto release = [&](int s) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if (leader)
+                    mbar_arrive(&tempty[s]);
+                else
+                    mbar_arrive_remote(tempty0 + 8u * (uint32_t)s);
+            }
+        };
+        int slot = 0, se = 0;
+        uint32_t tph = 0, sph = 0, mgph = 0;
+        auto drain_meet = [&](int i) -> bool {
+            mbar_arrive(&merge[i]);
+            return mbar_wait(&merge[i], mgph, abort_flag, status, kDevTimeoutTmemFull);
+        };
+        constexpr int NCH = Q8P_HC / Q8P_CW;
+        for (int64_t tile = pair; tile < tiles; tile += pairs) {
+            int64_t mi, ni;
+            q8_tile(tile, mt, nt, mi, ni);
+            const int64_t m0 = mi * Q8P_TMP;
+            const int64_t n0 = ni * 2 * Q8P_TN + rank * Q8P_TN;  // view-local, this CTA's first weight row
+            const int64_t nq = n0 + quad * 32u;                   // the warp's first weight row
+            const int64_t n = nq + lane;                          // this thread's weight row == TMEM lane
+            const int64_t mfirst = m0 + half * Q8P_HC;
+            float acc[Q8P_HC];
+#pragma unroll
+            for (int i = 0; i < Q8P_HC; i++) acc[i] = 0.f;
+            for (int64_t b = 0; b < nb; b++) {
+                const int bi = (int)(b % Q8P_BPS);
+                if (bi == 0 && !mbar_wait(&sfull[se], sph, abort_flag, status, kDevTimeoutScaleFull)) goto done;
+                const float* ef = reinterpret_cast<const float*>(scale_ring + se * Q8P_ENTRY);
+                const float dw = ef[bi * Q8P_TN + quad * 32u + lane];
+                const float* dx = ef + Q8P_BPS * Q8P_TN + bi * Q8P_TMP + half * Q8P_HC;
+                if (!mbar_wait(&tfull[slot], tph, abort_flag, status, kDevTimeoutTmemFull)) goto done;
+                tc_fence_after();
+                const uint32_t taddr = tmem_base + lane_base + (uint32_t)(slot * Q8P_TMP) + half * Q8P_HC;
+                if constexpr (DUMP) {
+#pragma unroll 1
+                    for (int c = 0; c < NCH; c++) {
+                        uint32_t v[Q8P_CW];
+                        tmem_ld16(taddr + (uint32_t)(c * Q8P_CW), v);
+                        tmem_ld_wait_dep(v);
+#pragma unroll
+                        for (int j = 0; j < Q8P_CW; j++) {
+                            const int64_t m = mfirst + c * Q8P_CW + j;
+                            if (n < p.N && m < p.M) p.dump[(b * p.M + m) * p.N + n] = __uint_as_float(v[j]);
+                        }
+                    }
+                    release(slot);
+                } else {
+                    // chunk c+1 loads while chunk c is accumulated; the slot is
+                    // released once its last chunk is in registers
+                    uint32_t va[Q8P_CW], vb[Q8P_CW];
+                    tmem_ld16(taddr, va);
+                    tmem_ld_wait_dep(va);
+#pragma unroll
+                    for (int c = 0; c < NCH; c += 2) {
+                        tmem_ld16(taddr + (uint32_t)((c + 1) * Q8P_CW), vb);
+                        q8p_fma(acc + c * Q8P_CW, va, dx + c * Q8P_CW, dw);
+                        tmem_ld_wait_dep(vb);
+                        if (c + 2 < NCH)
+                            tmem_ld16(taddr + (uint32_t)((c + 2) * Q8P_CW), va);
+                        else
+                            release(slot);
+                        q8p_fma(acc + (c + 1) * Q8P_CW, vb, dx + (c + 1) * Q8P_CW, dw);
+                        if (c + 2 < NCH) tmem_ld_wait_dep(va);
+                    }
+                }
+                if (++slot == 2) {
+                    slot = 0;
+                    tph ^= 1u;
+                }
+                if (bi == Q8P_BPS - 1 || b + 1 == nb) {
+                    // every lane's scale reads are done before lane 0 frees the entry
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sempty[se]);
+                    if (++se == Q8P_SE) {
+                        se = 0;
+                        sph ^= 1u;
+                    }
+                }
+            }
+            if constexpr (!DUMP) {
+                if (p.gated) {
+                    // gated weight: this CTA's lanes 64..127 hold the up projections of
+                    // the outputs whose gate projections lanes 0..63 hold (the repack
+                    // interleaves 64-row groups); the up warps hand their sums over
+                    // through the staging buffer and the gate warps finish
+                    // tensor_silu + tensor_gate (src/tensor.cpp:199-208, :334-345)
+                    float* xfer = reinterpret_cast<float*>(smem + Q8P_OFF_STAGING) + ((quad & 1) * 2 + half) * (Q8P_HC * 32);
+                    if (!drain_meet(0)) goto done;
+                    if (quad >= 2) {
+#pragma unroll
+                        for (int i = 0; i < Q8P_HC; i++) xfer[i * 32 + lane] = acc[i];
+                    }
+                    if (!drain_meet(1)) goto done;
+                    mgph ^= 1u;
+                    if (quad < 2) {
+                        const int64_t on = n0 / 2 + quad * 32 + lane;
+#pragma unroll
+                        for (int i = 0; i < Q8P_HC; i++) {
+                            const int64_t m = mfirst + i;
+                            const float g = acc[i], u = xfer[i * 32 + lane];
+                            if (on < p.N / 2 && m < p.M) p.y[m * p.ldy + on] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+                        }
+                    }
+                    continue;
+                }
+                const float bv = (p.bias && n < p.N) ? p.bias[n] : 0.f;
+                if (p.tma_store) {
+                    // four rounds of [32 activation rows][32 weight rows], double-buffered
+                    // per warp: lane 0 waits only for the store two rounds back
+                    float* stg0 = reinterpret_cast<float*>(smem + Q8P_OFF_STAGING) + warp * (2 * 32 * 32);
+#pragma unroll
+                    for (int r = 0; r < Q8P_HC / 32; r++) {
+                        float* stg = stg0 + (r & 1) * (32 * 32);
+                        const int64_t mr = mfirst + 32 * r;
+                        if (lane == 0) bulk_wait_read_1();
+                        __syncwarp();
+#pragma unroll
+                        for (int j = 0; j < 32; j++) stg[j * 32 + lane] = p.bias ? __fadd_rn(acc[32 * r + j], bv) : acc[32 * r + j];
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&tmY, stg, (int32_t)nq, (int32_t)mr);
+                            bulk_commit();
+                        }
+                        if (p.ndst && p.dst_vec4) {
+                            // the peers' copies from the same staged block, 4 floats a lane
+                            const int jr = lane >> 3, c4 = 4 * (lane & 7);
+                            const int64_t nn = nq + c4;
+                            for (int j = jr; j < 32; j += 4) {
+                                const int64_t m = mr + j;
+                                if (m >= p.M) break;
+                                const float4 v = *reinterpret_cast<const float4*>(stg + j * 32 + c4);
+                                const int64_t off = m * p.ldy + p.col_off + nn;
+                                if (nn + 3 < p.N) {
+                                    for (int k = 0; k < p.ndst; k++) *reinterpret_cast<float4*>(p.ydst[k] + off) = v;
+                                } else {
+                                    const float vs[4] = {v.x, v.y, v.z, v.w};
+                                    for (int q = 0; q < 4 && nn + q < p.N; q++)
+                                        for (int k = 0; k < p.ndst; k++) p.ydst[k][off + q] = vs[q];
+                                }
+                            }
+                        } else if (p.ndst && n < p.N) {
+                            for (int j = 0; j < 32; j++) {
+                                const int64_t m = mr + j;
+                                if (m >= p.M) break;
+                                const float v = stg[j * 32 + lane];
+                                const int64_t off = m * p.ldy + p.col_off + n;
+                                for (int k = 0; k < p.ndst; k++) p.ydst[k][off] = v;
+                            }
+                        }
+                    }
+                } else if (n < p.N) {
+#pragma unroll
+                    for (int j = 0; j < Q8P_HC; j++) {
+                        const int64_t m = mfirst + j;
+                        if (m < p.M) put_y(p, m, n, p.bias ? __fadd_rn(acc[j], bv) : acc[j]);
+                    }
+                }
+            }
+        }
+    }
+done:
+    // outstanding output stores must finish reading shared memory before exit
+    if (p.tma_store && warp < Q8P_DRAIN && lane == 0) bulk_wait_all();
+    // peer stores are visible system-wide before the kernel ends
+    if (p.ndst && warp < Q8P_DRAIN) __threadfence_system();
+    if (warp == 9 && lane == 0 && leader) {
+        // no MMA of this pair may still be writing TMEM when it is freed (after a
+        // normal run the drains have consumed every result; this covers aborts)
+        mma_commit_pair_local(mma_done);
+        const uint64_t t0 = global_ns();
+        while (!mbar_try_wait(mma_done, 0) && global_ns() - t0 < PXQ_WAIT_NS) {
+        }
+    }
+    __syncwarp();
+    // the peer CTA no longer touches this CTA's barriers or TMEM after this
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc_pair(tmem_base, 512);
+}
+
+template <bool DUMP>
+cudaError_t launch_q8p(const GemmOperands& op, int num_sms, cudaStream_t s)
+{
+    auto kern = k_gemm_q8p<DUMP>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Q8P_SMEM);
+    if (e != cudaSuccess) return e;
+    const int64_t tiles = ((op.M + Q8P_TMP - 1) / Q8P_TMP) * ((op.N + 2 * Q8P_TN - 1) / (2 * Q8P_TN));
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(Q8P_THREADS);
+    cfg.dynamicSmemBytes = Q8P_SMEM;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // pairs that can be resident at once
+    static int max_pairs = 0;
+    static std::once_flag once;
+    std::call_once(once, [&] {
+        cfg.gridDim = dim3(2 * (num_sms / 2));
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
+            cudaGetLastError();
+            n = num_sms / 2;
+        }
+        max_pairs = n;
+    });
+    int64_t groups = max_pairs;
+    if (tiles < groups) groups = tiles;
+    if (groups < 1) groups = 1;
+    cfg.gridDim = dim3((unsigned)(2 * groups));
+    Q8Params p{op.M, op.N, op.K, op.n_first, op.y, op.ldy, op.bias, op.dump, op.status, (op.tma_store && !DUMP) ? 1 : 0,
+               op.gated, op.ndst, op.dst_vec4, op.col_off, {}};
+    for (int k = 0; k < kMaxScatter; k++) p.ydst[k] = op.ydst[k];
+    return cudaLaunchKernelEx(&cfg, kern, op.tm[0], op.tm[1], op.tm[4], op.tm[6], op.tm_y, p);
+}
+
 template <bool DUMP>
 cudaError_t launch_q8s(const GemmOperands& op, int num_sms, cudaStream_t s)
 {
@@ -863,6 +1304,7 @@ cudaError_t launch_q8_typed(const GemmOperands& op, int num_sms, cudaStream_t s)
 
 cudaError_t launch_gemm_q8(const GemmOperands& op, int num_sms, cudaStream_t s)
 {
+    if (op.q8_kind == 3) return op.dump ? launch_q8p<true>(op, num_sms, s) : launch_q8p<false>(op, num_sms, s);
     if (op.q8_kind == 2) return op.dump ? launch_q8s<true>(op, num_sms, s) : launch_q8s<false>(op, num_sms, s);
     if (op.q8_kind == 1)
         return op.dump ? launch_q8_typed<1, true>(op, num_sms, s) : launch_q8_typed<1, false>(op, num_sms, s);

@@ -30,10 +30,16 @@
 // before it still run, and waits for them (griddep_wait) before it fetches
 // activations; the consumers wait before touching any output.
 //
-// Q8_0: a CTA of 4 warps owns 16 weight rows and a range of K blocks (the
-// whole row, or a 1/ks slice when there are too few row groups to fill the
-// GPU); warps walk the blocks round-robin with the next block's weight bytes
-// in flight (register double buffering).
+// Q8_0 runs in the same kernel when K is a multiple of 256: a "super-block"
+// is then eight raw 34-byte blocks (272 bytes, so rows are 16-byte multiples
+// as TMA needs), streamed by the same 3-D tensor maps; each block is one MMA
+// whose quants the consumers read from shared memory with aligned loads and
+// funnel shifts, and the activation records hold the blocks' quants in the
+// fragment layout plus their scales as fp32.  Other K: a CTA of 4 warps owns
+// 16 weight rows and a range of K blocks (the whole row, or a 1/ks slice when
+// there are too few row groups to fill the GPU); warps walk the blocks
+// round-robin with the next block's weight bytes in flight (register double
+// buffering).
 #include <atomic>
 
 #include "pxq_device.cuh"
@@ -234,6 +240,12 @@ struct MvFmt<kTypeQ6_K> {
     static constexpr int kRecBytes = kQ8KQ6Bytes; // 304
     static constexpr bool kRowMajor64 = false;
 };
+template <>
+struct MvFmt<kTypeQ8_0> {
+    static constexpr int kSbBytes = kQ80SbBytes;  // 272: eight raw 34-byte blocks
+    static constexpr int kRecBytes = kQ80MvBytes; // 288
+    static constexpr bool kRowMajor64 = false;
+};
 
 // Tile shapes: TR weight rows x 128/TR super-blocks per stage.  Every stage is
 // 128 row-super-blocks of weights (22.5 KB of Q5_K, 28 KB of Q6_K); consumer
@@ -256,8 +268,9 @@ struct MvShape {
     static constexpr int kActPitch = kSbs * Fmt::kRecBytes;         // one activation row's records per stage
     static constexpr int kActBytes = 8 * kActPitch + 512;           // up to 8 activation rows, skewed
     // two CTAs per SM within 228 KB; with a fused quantize there is no
-    // per-stage activation buffer, so the Q5_K weight ring gets a fourth stage
-    static constexpr int kStages = FUSED ? (WT == kTypeQ5_K ? 4 : 3) : (TR == 16 ? 2 : 3);
+    // per-stage activation buffer, so the Q5_K weight ring gets a fourth
+    // stage; Q8_0 stages are 34 KB, two of them
+    static constexpr int kStages = WT == kTypeQ8_0 ? 2 : FUSED ? (WT == kTypeQ5_K ? 4 : 3) : (TR == 16 ? 2 : 3);
     static_assert(kRowBytes % 16 == 0 && kActPitch % 16 == 0, "bulk copies move 16-byte multiples");
     static_assert(kWeightBytes == 16 * kMvStageSuperBlocks * Fmt::kSbBytes, "every shape streams the same stage size");
 };
@@ -501,6 +514,74 @@ __device__ __forceinline__ void q6_unit(const uint8_t* wa, const uint8_t* wb, co
     acc[3] = __fmaf_rn(__fmul_rn(dx1, db), (float)sumi[3], acc[3]);
 }
 
+// 8 bytes of shared memory at p, where p % 8 == M (M even; the quants of a
+// 34-byte Q8_0 block start 2-byte aligned): aligned loads, then funnel shifts.
+template <int M>
+__device__ __forceinline__ uint2 lds8(const uint8_t* p)
+{
+    if constexpr (M == 0) {
+        return *reinterpret_cast<const uint2*>(p);
+    } else if constexpr (M == 4) {
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(p);
+        return make_uint2(w[0], w[1]);
+    } else if constexpr (M == 2) {
+        const uint2 w01 = *reinterpret_cast<const uint2*>(p - 2);
+        const uint32_t w2 = *reinterpret_cast<const uint32_t*>(p + 6);
+        return make_uint2(__funnelshift_r(w01.x, w01.y, 16), __funnelshift_r(w01.y, w2, 16));
+    } else {
+        static_assert(M == 6, "Q8_0 quants are 2-byte aligned");
+        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(p - 2);
+        const uint2 w12 = *reinterpret_cast<const uint2*>(p + 2);
+        return make_uint2(__funnelshift_r(w0, w12.x, 16), __funnelshift_r(w12.x, w12.y, 16));
+    }
+}
+
+// Block J of a 272-byte group (eight raw Q8_0 blocks) of weight rows a = g,
+// b = g+8 (16-byte aligned rows): one MMA for the int32 block dots against
+// activation rows g (B fragment b0, b1), then pix_dot_q8_0's
+// acc += (fp16 dw * fp16 dx) * dot for activation rows 2t, 2t+1.
+template <int J>
+__device__ __forceinline__ void q8_block(const uint8_t* wa, const uint8_t* wb, uint32_t t, uint32_t b0, uint32_t b1,
+                                         float dx0, float dx1, float (&acc)[4])
+{
+    constexpr int M = (2 * J + 2) & 7;  // alignment of the quants at 34J + 2 (8t keeps it)
+    const uint2 qa = lds8<M>(wa + 34 * J + 2 + 8 * t), qb = lds8<M>(wb + 34 * J + 2 + 8 * t);
+    const uint32_t a[4] = {qa.x, qb.x, qa.y, qb.y};
+    int d[4];
+    mma_s8(d, a, b0, b1);
+    const float dwa = __half2float(*reinterpret_cast<const __half*>(wa + 34 * J));
+    const float dwb = __half2float(*reinterpret_cast<const __half*>(wb + 34 * J));
+    acc[0] = __fmaf_rn(__fmul_rn(dwa, dx0), (float)d[0], acc[0]);
+    acc[1] = __fmaf_rn(__fmul_rn(dwa, dx1), (float)d[1], acc[1]);
+    acc[2] = __fmaf_rn(__fmul_rn(dwb, dx0), (float)d[2], acc[2]);
+    acc[3] = __fmaf_rn(__fmul_rn(dwb, dx1), (float)d[3], acc[3]);
+}
+
+// One group of eight Q8_0 blocks (256 values, 272 bytes per row as stored)
+// of weight rows a, b against the records of activation rows g (quants, B
+// fragments: lane t's eight bytes of blocks 2P, 2P+1 are one 16-byte word)
+// and 2t, 2t+1 (block scales, fp32 at byte 256).  The per-element order of
+// a block is permuted identically for A and B (lane t: bytes 8t..8t+7).
+__device__ __forceinline__ void q8_unit(const uint8_t* wa, const uint8_t* wb, const uint8_t* xg, const uint8_t* x0,
+                                        const uint8_t* x1, uint32_t t, float (&acc)[4])
+{
+    const float4 s0a = *reinterpret_cast<const float4*>(x0 + kQKK), s0b = *reinterpret_cast<const float4*>(x0 + kQKK + 16);
+    const float4 s1a = *reinterpret_cast<const float4*>(x1 + kQKK), s1b = *reinterpret_cast<const float4*>(x1 + kQKK + 16);
+    const uint8_t* xr = xg + 16 * t;
+    uint4 bx = *reinterpret_cast<const uint4*>(xr);
+    q8_block<0>(wa, wb, t, bx.x, bx.y, s0a.x, s1a.x, acc);
+    q8_block<1>(wa, wb, t, bx.z, bx.w, s0a.y, s1a.y, acc);
+    bx = *reinterpret_cast<const uint4*>(xr + 64);
+    q8_block<2>(wa, wb, t, bx.x, bx.y, s0a.z, s1a.z, acc);
+    q8_block<3>(wa, wb, t, bx.z, bx.w, s0a.w, s1a.w, acc);
+    bx = *reinterpret_cast<const uint4*>(xr + 128);
+    q8_block<4>(wa, wb, t, bx.x, bx.y, s0b.x, s1b.x, acc);
+    q8_block<5>(wa, wb, t, bx.z, bx.w, s0b.y, s1b.y, acc);
+    bx = *reinterpret_cast<const uint4*>(xr + 192);
+    q8_block<6>(wa, wb, t, bx.x, bx.y, s0b.z, s1b.z, acc);
+    q8_block<7>(wa, wb, t, bx.z, bx.w, s0b.w, s1b.w, acc);
+}
+
 __device__ __forceinline__ void store_out(const MvParams& p, int64_t r, int64_t col, float v)
 {
     p.y[col * p.ldy + r] = p.bias ? __fadd_rn(v, p.bias[r]) : v;
@@ -515,7 +596,7 @@ __device__ __forceinline__ void store_out(const MvParams& p, int64_t r, int64_t 
 template <int TR, uint32_t WT>
 __device__ __host__ constexpr uint32_t act_row_off(uint32_t c)
 {
-    constexpr uint32_t P = MvShape<TR, false, WT>::kActPitch;
+    constexpr uint32_t P = kMvStageSuperBlocks / (TR / 16) * MvFmt<WT>::kRecBytes;  // MvShape::kActPitch
     return c * P + (P % 128 == 0 ? 144 * (c >> 1) + 64 * (c & 1) : 16 * (c >> 1));
 }
 static_assert(act_row_off<16, kTypeQ5_K>(7) + MvShape<16, false, kTypeQ5_K>::kActPitch <= MvShape<16, false, kTypeQ5_K>::kActBytes,
@@ -528,6 +609,10 @@ static_assert(act_row_off<16, kTypeQ6_K>(7) + MvShape<16, false, kTypeQ6_K>::kAc
               "activation rows fit the stage");
 static_assert(act_row_off<32, kTypeQ6_K>(7) + MvShape<32, false, kTypeQ6_K>::kActPitch <= MvShape<32, false, kTypeQ6_K>::kActBytes,
               "activation rows fit the stage");
+static_assert(act_row_off<64, kTypeQ8_0>(7) + MvShape<64, false, kTypeQ8_0>::kActPitch <= MvShape<64, false, kTypeQ8_0>::kActBytes,
+              "activation rows fit the stage buffer");
+static_assert(act_row_off<32, kTypeQ8_0>(7) + MvShape<32, false, kTypeQ8_0>::kActPitch <= MvShape<32, false, kTypeQ8_0>::kActBytes,
+              "activation rows fit the stage buffer");
 static_assert(act_row_off<64, kTypeQ6_K>(7) + MvShape<64, false, kTypeQ6_K>::kActPitch <= MvShape<64, false, kTypeQ6_K>::kActBytes,
               "activation rows fit the stage");
 
@@ -738,11 +823,15 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_kq(const __grid_consta
 #pragma unroll
         for (int k = 0; k < kPerWarp; k++) {
             if (sbk[k] >= nsb) continue;  // warp-uniform; past the end of K the record is never read
-            const Q8KWarp r = q8_K_warp_vals(v[k], lane);
-            if constexpr (WT == kTypeQ5_K)
-                q8_K_store_mv(act_flat + (warp + kMvConsumers * k) * kRec, r, lane);
-            else
-                q8_K_store_q6(act_flat + (warp + kMvConsumers * k) * kRec, r, lane);
+            if constexpr (WT == kTypeQ8_0) {
+                q8_0_store_mv(act_flat + (warp + kMvConsumers * k) * kRec, v[k], lane);
+            } else {
+                const Q8KWarp r = q8_K_warp_vals(v[k], lane);
+                if constexpr (WT == kTypeQ5_K)
+                    q8_K_store_mv(act_flat + (warp + kMvConsumers * k) * kRec, r, lane);
+                else
+                    q8_K_store_q6(act_flat + (warp + kMvConsumers * k) * kRec, r, lane);
+            }
         }
     }
     named_bar_sync(7, 32 * kMvConsumers);
@@ -773,8 +862,10 @@ __global__ void __launch_bounds__(kMvThreads, 2) k_matvec_kq(const __grid_consta
             }
             if constexpr (WT == kTypeQ5_K)
                 q5_unit(wa, wb, xg, x0, x1, t, acc, summ);
-            else
+            else if constexpr (WT == kTypeQ6_K)
                 q6_unit(wa, wb, xg, x0, x1, t, acc);
+            else
+                q8_unit(wa, wb, xg, x0, x1, t, acc);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.empty[slot]);
@@ -909,6 +1000,17 @@ cudaError_t launch_kq3(const MatvecPlan& plan, const CUtensorMap* map, int64_t r
                        int64_t ldx, float* y, int64_t ldy, const float* bias, float* partial, uint32_t* counters,
                        uint32_t* status, cudaStream_t s)
 {
+    if (plan.type == kTypeQ8_0) {
+        // 16-row tiles only with the fused quantize: two CTAs of the unfused
+        // variant (per-stage activation buffers) do not fit one SM
+        if constexpr (TR == 16) {
+            if (!plan.fused) return cudaErrorInvalidValue;
+            return launch_kq<16, true, kTypeQ8_0>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
+        } else {
+            return plan.fused ? launch_kq<TR, true, kTypeQ8_0>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s)
+                              : launch_kq<TR, false, kTypeQ8_0>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
+        }
+    }
     if (plan.type == kTypeQ5_K)
         return plan.fused ? launch_kq<TR, true, kTypeQ5_K>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s)
                           : launch_kq<TR, false, kTypeQ5_K>(plan, map, row_first, act, x, ldx, y, ldy, bias, partial, counters, status, s);
@@ -928,10 +1030,14 @@ MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t colum
     p.rows = rows;
     p.inner = inner;
     p.columns = columns;
-    if (type == kTypeQ5_K || type == kTypeQ6_K) {
+    const bool q8 = type == kTypeQ8_0;
+    if (type == kTypeQ5_K || type == kTypeQ6_K || (q8 && inner % kQKK == 0)) {
+        // the TMA-fed kernel; Q8_0 rows stream as groups of eight blocks
+        // (272 bytes), which needs whole groups (and so 16-byte row strides)
+        p.streamed = true;
         const int64_t nsb = inner / kQKK;
-        const int64_t sb_bytes = type == kTypeQ5_K ? kQ5KBytes : kQ6KPadBytes;
-        const int64_t rec_bytes = type == kTypeQ5_K ? kQ8KMvBytes : kQ8KQ6Bytes;
+        const int64_t sb_bytes = type == kTypeQ5_K ? kQ5KBytes : q8 ? kQ80SbBytes : kQ6KPadBytes;
+        const int64_t rec_bytes = type == kTypeQ5_K ? kQ8KMvBytes : q8 ? kQ80MvBytes : kQ8KQ6Bytes;
         const int64_t slots = (int64_t)num_sms * 2;  // two CTAs per SM
         // Whole tiles per CTA (no cross-CTA sums) when some tile height gives
         // a tile count that fills the grid well, or when the matrix is small
@@ -945,6 +1051,8 @@ MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t colum
         if (gated) p.gated_half = rows / 128;
         for (int tr : {64, 32, 16}) {
             if (gated) break;
+            // Q8_0: 16-row tiles only when every CTA quantizes its own records
+            if (q8 && tr == 16 && !(fuse_quantize && columns * ((nsb + 7) / 8) * 8 <= kMvFusedRecords)) continue;
             const int64_t tiles = (rows + tr - 1) / tr;
             const int64_t tile_bytes = (int64_t)tr * nsb * sb_bytes;
             const bool short_tiles = tile_bytes <= 64 * 1024 || (type == kTypeQ5_K && tr == 16);
@@ -991,7 +1099,8 @@ MatvecPlan plan_matvec(uint32_t type, int64_t rows, int64_t inner, int64_t colum
     // kernel to clear them) finds zeros there whatever the previous call was.
     if (p.fused && p.counter_bytes > kMvCounterRegion) {
         p.fused = false;
-        p.act_bytes = (size_t)(columns * (inner / kQKK) * (type == kTypeQ5_K ? kQ8KMvBytes : kQ8KQ6Bytes));
+        p.act_bytes = (size_t)(columns * (inner / kQKK) *
+                               (type == kTypeQ5_K ? kQ8KMvBytes : type == kTypeQ8_0 ? kQ80MvBytes : kQ8KQ6Bytes));
     }
     p.off_counters = 0;
     p.off_act = (p.counter_bytes > kMvCounterRegion ? p.counter_bytes + 255 : kMvCounterRegion) / 256 * 256;
@@ -1005,7 +1114,7 @@ cudaError_t launch_matvec(const MatvecPlan& plan, const CUtensorMap* maps, int64
                           const float* bias, float* partial, uint32_t* counters, uint32_t* status, cudaStream_t s)
 {
     if (plan.columns < 1 || plan.columns > 8 || plan.grid < 1) return cudaErrorInvalidValue;
-    if (plan.type == kTypeQ5_K || plan.type == kTypeQ6_K) {
+    if (plan.streamed) {
         if (!maps || !counters || (plan.partial_bytes && !partial)) return cudaErrorInvalidValue;
         if (plan.fused ? !x : !act) return cudaErrorInvalidValue;
         const CUtensorMap* map = maps + matvec_map_index(plan.tile_rows);

@@ -97,6 +97,8 @@ constexpr int kMvStageSuperBlocks = 8;                    // tile rows / 16 x su
 constexpr int kMvStageWeightBytes = 16 * kMvStageSuperBlocks * kQ5KBytes;  // 22528, any tile shape
 constexpr int kMvTileShapes = 3;                         // 64 x 2, 32 x 4 and 16 x 8 super-blocks
 constexpr int kQ8KMvBytes = 288;
+constexpr int kQ80SbBytes = 8 * 34;                       // eight Q8_0 blocks (256 values) as stored
+constexpr int kQ80MvBytes = 288;                          // Q8_0 matvec record: {i8 quants as kQ8KMvBytes; f32 d[8] at 256}
 constexpr int kQ8KQ6Bytes = 304;                          // Q8_K record for Q6_K weights: {f32 d; pad; i8 qs[256] at 16; i16 bsums[16] at 272}
 constexpr size_t kMvCounterRegion = 16 << 10;            // scratch bytes reserved for counters  // {i8 quants [4 pairs][4 lanes][2][8]; i16 32-element sums[8]; f32 d; pad}
 
@@ -108,7 +110,8 @@ struct MatvecPlan {
     int grid = 0;                            // CTAs
     int ks = 1, chunk = 0;                   // Q8_0: K slices per row group, blocks per slice
     int64_t rowgroups = 0;                   // Q8_0: 16-row groups
-    bool fused = false;                      // Q5_K: the matvec quantizes the activation itself
+    bool streamed = false;                   // the TMA-fed kernel (K-quants; Q8_0 when inner % 256 == 0)
+    bool fused = false;                      // streamed: the matvec quantizes the activation itself
     int64_t gated_half = 0;                  // K-quants, gated weight [gate; up]: F / 64 (the epilogue writes silu(g) * u)
     size_t act_bytes = 0, partial_bytes = 0, counter_bytes = 0;
     size_t off_counters = 0, off_act = 0, off_partial = 0, total_bytes = 0;
@@ -182,7 +185,7 @@ struct GemmOperands {
     uint32_t type;        // kTypeQ8_0, kTypeQ5_K or kTypeQ6_K
     int q8_kind;          // Q8_0 operand kind (gemm_q8.cu): 0 fp16 quants, scales applied on the CUDA cores;
                           // 1 int8 quants (kind::i8), scales on the CUDA cores; 2 fp16 quants, scale
-                          // products from a one-hot tensor-core MMA
+                          // products from a one-hot tensor-core MMA; 3 kind 0's operands on CTA pairs
     int64_t M, N, K;      // activation rows, view rows (output columns), inner
     int64_t n_first;      // first weight row of the view (multiple of 4)
     // tensor maps (boxes as listed in gemm.cu and gemm_q8.cu): 0 weight

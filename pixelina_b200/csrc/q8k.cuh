@@ -100,6 +100,46 @@ __device__ __forceinline__ void q8_K_store_mv(uint8_t* out, const Q8KWarp& r, ui
     if (lane == 0) *reinterpret_cast<float*>(out + kQKK + 16) = r.d;
 }
 
+// ---- Q8_0 (quantize_row_q8_0_ref, src/kernels_quant.cpp:120-144) ----
+
+// roundf: half away from zero, after the rounded product x * id.
+__device__ __forceinline__ float round_half_away(float v)
+{
+    const float t = truncf(v);
+    const float r = __fsub_rn(v, t);  // exact: fractional part of v
+    return fabsf(r) >= 0.5f ? __fadd_rn(t, copysignf(1.0f, v)) : t;
+}
+
+__device__ __forceinline__ int8_t q8_0_quant(float x, float id)
+{
+    return static_cast<int8_t>(static_cast<int>(round_half_away(__fmul_rn(x, id))));
+}
+
+// Eight Q8_0 blocks (256 values) as one matvec record (kQ80MvBytes at
+// `out`), one warp, the values 8*lane .. 8*lane+7 in v: block j = lane / 4
+// is quantized by lanes 4j..4j+3 (d = amax/127 and 1/d as IEEE divisions,
+// the stored fp16 scale round-to-nearest-even), its quants land where
+// q8_K_store_mv puts sub-block j (byte 64*(j/2) + 16*t + 8*(j%2), t = lane %
+// 4), and the stored scale, widened exactly to fp32, at byte 256 + 4*j.
+__device__ __forceinline__ void q8_0_store_mv(uint8_t* out, const float (&v)[8], uint32_t lane)
+{
+    float amax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; k++) amax = fmaxf(amax, fabsf(v[k]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int k = 0; k < 4; k++) lo |= (uint32_t)(uint8_t)q8_0_quant(v[k], id) << (8 * k);
+#pragma unroll
+    for (int k = 0; k < 4; k++) hi |= (uint32_t)(uint8_t)q8_0_quant(v[4 + k], id) << (8 * k);
+    const uint32_t j = lane >> 2, t = lane & 3u;
+    *reinterpret_cast<uint2*>(out + 64 * (j >> 1) + 16 * t + 8 * (j & 1u)) = make_uint2(lo, hi);
+    if (t == 0) *reinterpret_cast<float*>(out + kQKK + 4 * j) = __half2float(__float2half_rn(d));
+}
+
 // This warp's block as a Q6_K matvec record (kQ8KQ6Bytes at `out`): d (fp32)
 // at byte 0, the quants in their natural order at byte 16 (lane l's eight at
 // 16 + 8l), the sixteen 16-element sums (int16) at byte 272.

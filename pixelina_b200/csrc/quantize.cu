@@ -29,18 +29,6 @@
 namespace pxq {
 namespace {
 
-__device__ __forceinline__ float round_half_away(float v)
-{
-    const float t = truncf(v);
-    const float r = __fsub_rn(v, t);  // exact: fractional part of v
-    return fabsf(r) >= 0.5f ? __fadd_rn(t, copysignf(1.0f, v)) : t;
-}
-
-__device__ __forceinline__ int8_t q8_0_quant(float x, float id)
-{
-    return static_cast<int8_t>(static_cast<int>(round_half_away(__fmul_rn(x, id))));
-}
-
 // One Q8_0 block per 8 consecutive threads, 4 elements per thread.
 // Returns (d as stored fp16, 4 quants packed little-endian).
 struct Q80Part {
@@ -67,8 +55,6 @@ __device__ __forceinline__ Q80Part q8_0_part(const float4 v)
     return p;
 }
 
-// grid-stride over groups of 4 elements; all 32 lanes of a warp stay active
-// (padding lanes compute on zeros and store nothing) so the shuffles are full.
 // Start of every kernel that may run under programmatic stream serialization:
 // let the next kernel launch, wait for the previous one, then clear the
 // caller's counters (the matvec's split-K counters) if any.
@@ -76,43 +62,67 @@ __device__ __forceinline__ void pdl_prologue(uint32_t* __restrict__ zero, int64_
 {
     griddep_launch_dependents();
     griddep_wait();
-    if (zero)
-        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nzero; i += (int64_t)gridDim.x * blockDim.x)
-            zero[i] = 0u;
+    if (zero) {
+        const int64_t cta = (int64_t)blockIdx.y * gridDim.x + blockIdx.x, nthr = (int64_t)gridDim.x * gridDim.y * blockDim.x;
+        for (int64_t i = cta * blockDim.x + threadIdx.x; i < nzero; i += nthr) zero[i] = 0u;
+    }
+}
+
+// The Q8_0 kernels walk a 2-D grid: x = groups of kQ80Threads consecutive
+// 4-value quads of a row (8 threads per 32-block), y = a slab of rows taken
+// kQ80Rows at a time (their loads all in flight before any block is
+// reduced); no index divisions.  Threads past the row end compute on zeros
+// and store nothing, so every shuffle has its full warp.
+constexpr int kQ80Threads = 256;
+constexpr int kQ80Rows = 4;
+
+dim3 q8_0_grid(int64_t rows, int64_t inner)
+{
+    const int64_t gx = (inner / 4 + kQ80Threads - 1) / kQ80Threads;
+    int64_t gy = (148 * 16 + gx - 1) / gx;  // about 16 CTAs per SM in all
+    const int64_t max_gy = (rows + kQ80Rows - 1) / kQ80Rows;
+    if (gy > max_gy) gy = max_gy;
+    if (gy < 1) gy = 1;
+    if (gy > 65535) gy = 65535;
+    return dim3((unsigned)gx, (unsigned)gy);
+}
+
+// For every (row, quad) of this thread: emit(row, quad, part).
+template <typename Emit>
+__device__ __forceinline__ void q8_0_rows(const float* x, int64_t rows, int64_t inner, int64_t ldx, Emit emit)
+{
+    const int64_t quad = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const bool on = quad < inner / 4;
+    for (int64_t r0 = blockIdx.y; r0 < rows; r0 += (int64_t)kQ80Rows * gridDim.y) {
+        float4 v[kQ80Rows];
+#pragma unroll
+        for (int u = 0; u < kQ80Rows; u++) {
+            const int64_t r = r0 + (int64_t)u * gridDim.y;
+            v[u] = on && r < rows ? ld_dep_f4(x + r * ldx + quad * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < kQ80Rows; u++) {
+            const int64_t r = r0 + (int64_t)u * gridDim.y;
+            const Q80Part p = q8_0_part(v[u]);
+            if (on && r < rows) emit(r, quad, p);
+        }
+    }
 }
 
 __global__ void k_quantize_q8_0_blocks(const float* x, uint8_t* __restrict__ y, int64_t rows, int64_t inner,
                                        int64_t ldx, uint32_t* __restrict__ zero, int64_t nzero)
 {
     pdl_prologue(zero, nzero);
-    const int64_t quads_per_row = inner / 4;
-    const int64_t total = rows * quads_per_row;
     const int64_t nb = inner / kQK8_0;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    auto emit = [&](int64_t i, const Q80Part& p) {
-        const int64_t row = i / quads_per_row, quad = i % quads_per_row;
-        const int64_t blk = quad / 8;
+    q8_0_rows(x, rows, inner, ldx, [&](int64_t row, int64_t quad, const Q80Part& p) {
+        uint8_t* out = y + (row * nb + quad / 8) * kQ8_0Bytes;
         const int t = (int)(quad % 8);
-        uint8_t* out = y + (row * nb + blk) * kQ8_0Bytes;
         // qs start at byte 2 of the 34-byte block: 2-byte aligned stores only
         uint16_t* q16 = reinterpret_cast<uint16_t*>(out + 2 + 4 * t);
         q16[0] = (uint16_t)(p.packed & 0xffffu);
         q16[1] = (uint16_t)(p.packed >> 16);
         if (t == 0) *reinterpret_cast<__half*>(out) = p.d16;
-    };
-    // two quads per thread and trip, both loads issued before either block
-    // reduction, so twice the bytes are in flight
-    for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < total; base += 2 * stride) {
-        const int64_t i0 = base + threadIdx.x, i1 = i0 + stride;
-        const bool l0 = i0 < total, l1 = i1 < total;
-        float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
-        if (l0) v0 = ld_dep_f4(x + (i0 / quads_per_row) * ldx + (i0 % quads_per_row) * 4);
-        if (l1) v1 = ld_dep_f4(x + (i1 / quads_per_row) * ldx + (i1 % quads_per_row) * 4);
-        const Q80Part p0 = q8_0_part(v0);
-        const Q80Part p1 = q8_0_part(v1);
-        if (l0) emit(i0, p0);
-        if (l1) emit(i1, p1);
-    }
+    });
 }
 
 // GEMM operand: the quants as int8 (kind 1) or exact fp16 values (kinds 0,
@@ -121,11 +131,7 @@ __global__ void k_quantize_q8_0_blocks(const float* x, uint8_t* __restrict__ y, 
 __global__ void k_quantize_q8_0_operand(const float* __restrict__ x, void* __restrict__ xq, void* __restrict__ dx, int kind,
                                         int64_t rows, int64_t inner, int64_t ldx, int64_t ldd)
 {
-    const int64_t quads_per_row = inner / 4;
-    const int64_t total = rows * quads_per_row;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    auto emit = [&](int64_t i, const Q80Part& p) {
-        const int64_t row = i / quads_per_row, quad = i % quads_per_row;
+    q8_0_rows(x, rows, inner, ldx, [&](int64_t row, int64_t quad, const Q80Part& p) {
         if (kind == 1) {
             reinterpret_cast<uint32_t*>(static_cast<int8_t*>(xq) + row * inner)[quad] = p.packed;
         } else {
@@ -142,19 +148,7 @@ __global__ void k_quantize_q8_0_operand(const float* __restrict__ x, void* __res
             else
                 static_cast<float*>(dx)[(quad / 8) * ldd + row] = __half2float(p.d16);
         }
-    };
-    // two quads per thread and trip, both loads in flight together
-    for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < total; base += 2 * stride) {
-        const int64_t i0 = base + threadIdx.x, i1 = i0 + stride;
-        const bool l0 = i0 < total, l1 = i1 < total;
-        float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
-        if (l0) v0 = ld_dep_f4(x + (i0 / quads_per_row) * ldx + (i0 % quads_per_row) * 4);
-        if (l1) v1 = ld_dep_f4(x + (i1 / quads_per_row) * ldx + (i1 % quads_per_row) * 4);
-        const Q80Part p0 = q8_0_part(v0);
-        const Q80Part p1 = q8_0_part(v1);
-        if (l0) emit(i0, p0);
-        if (l1) emit(i1, p1);
-    }
+    });
 }
 
 // ---- Q8_K: one warp per 256-block (q8k.cuh) -------------------------------
@@ -213,6 +207,23 @@ __global__ void k_quantize_q8_K_mv(const float* x, uint8_t* __restrict__ y, int6
             q8_K_store_q6(y + w * kQ8KQ6Bytes, r, lane);
         else
             q8_K_store_mv(y + w * kQ8KMvBytes, r, lane);
+    }
+}
+
+// Q8_0 activation rows as the streamed matvec's records: one warp per 256
+// values (eight blocks), kQ80MvBytes each (q8_0_store_mv).
+__global__ void k_quantize_q8_0_mv(const float* x, uint8_t* __restrict__ y, int64_t rows, int64_t inner, int64_t ldx,
+                                   uint32_t* __restrict__ zero, int64_t nzero)
+{
+    pdl_prologue(zero, nzero);
+    const uint32_t lane = threadIdx.x & 31u;
+    const int64_t ngr = inner / kQKK;
+    const int64_t total = rows * ngr;
+    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t w = (((int64_t)blockIdx.x * blockDim.x) >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
+        float v[8];
+        q8_K_load(x + (w / ngr) * ldx + (w % ngr) * kQKK, lane, v);
+        q8_0_store_mv(y + w * kQ80MvBytes, v, lane);
     }
 }
 
@@ -288,9 +299,8 @@ cudaError_t launch_pad_q6_K(const void* src, void* dst, int64_t superblocks, cud
 
 cudaError_t launch_quantize_q8_0_blocks(const float* x, void* y, int64_t rows, int64_t inner, int64_t ldx, cudaStream_t s)
 {
-    const int threads = 256;
-    k_quantize_q8_0_blocks<<<grid_for(rows * inner / 4, threads), threads, 0, s>>>(x, static_cast<uint8_t*>(y), rows, inner, ldx,
-                                                                                   nullptr, 0);
+    k_quantize_q8_0_blocks<<<q8_0_grid(rows, inner), kQ80Threads, 0, s>>>(x, static_cast<uint8_t*>(y), rows, inner, ldx,
+                                                                          nullptr, 0);
     return cudaGetLastError();
 }
 
@@ -300,8 +310,11 @@ cudaError_t launch_matvec_quantize(const MatvecPlan& plan, const float* x, int64
     const int threads = 256;
     const int64_t nzero = counters ? (int64_t)(plan.counter_bytes / 4) : 0;
     uint8_t* out = static_cast<uint8_t*>(act);
+    if (plan.type == kTypeQ8_0 && plan.streamed)
+        return launch_pdl(k_quantize_q8_0_mv, dim3(grid_for(plan.columns * (plan.inner / kQKK) * 32, threads)), dim3(threads), 0, s,
+                          x, out, plan.columns, plan.inner, ldx, counters, nzero);
     if (plan.type == kTypeQ8_0)
-        return launch_pdl(k_quantize_q8_0_blocks, dim3(grid_for(plan.columns * plan.inner / 4, threads)), dim3(threads), 0, s,
+        return launch_pdl(k_quantize_q8_0_blocks, q8_0_grid(plan.columns, plan.inner), dim3(kQ80Threads), 0, s,
                           x, out, plan.columns, plan.inner, ldx, counters, nzero);
     if (plan.type == kTypeQ5_K || plan.type == kTypeQ6_K) {
         const bool q6 = plan.type == kTypeQ6_K;
@@ -335,8 +348,7 @@ cudaError_t launch_quantize_q8_K_blocks(const float* x, void* y, int64_t rows, i
 cudaError_t launch_quantize_q8_0_operand(const float* x, void* xq, void* dx, int kind, int64_t rows, int64_t inner,
                                          int64_t ldx, int64_t ldd, cudaStream_t s)
 {
-    const int threads = 256;
-    k_quantize_q8_0_operand<<<grid_for(rows * inner / 4, threads), threads, 0, s>>>(x, xq, dx, kind, rows, inner, ldx, ldd);
+    k_quantize_q8_0_operand<<<q8_0_grid(rows, inner), kQ80Threads, 0, s>>>(x, xq, dx, kind, rows, inner, ldx, ldd);
     return cudaGetLastError();
 }
 

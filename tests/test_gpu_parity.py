@@ -137,6 +137,37 @@ def test_matvec_kquant_tile_shapes(pxq, oracle, wtype, rows, inner, columns):
     assert ok and max_abs_rel(y, ref) <= TOL
 
 
+@pytest.mark.parametrize("rows", [18944, 9472, 4608, 3584, 200])
+@pytest.mark.parametrize("inner,columns", [(256, 1), (768, 3), (3584, 8), (3584, 2)])
+def test_matvec_q8_0_streamed_tile_shapes(pxq, oracle, rows, inner, columns):
+    """Q8_0 with K a multiple of 256 streams groups of eight raw blocks
+    through the TMA-fed kernel: every schedule (whole 64/32-row tiles,
+    16-row tiles with the fused quantize, stream-K) against the oracle."""
+    w = synth.q8_0_weights(rows, inner, seed=rows + columns)
+    x = synth.activations(columns, inner, seed=columns)
+    W = pxq.Weight(w, Q8_0, inner, rows)
+    y = pxq.matmul(W, cuda(x), path="matvec").cpu().numpy()
+    pxq.synchronize()
+    W.release()
+    ok, ref = oracle.quant_matmul(w, Q8_0, x, rows)
+    assert ok and max_abs_rel(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("rows,inner", [(300, 96), (4608, 800), (200, 18976)])
+@pytest.mark.parametrize("columns", [1, 3, 8])
+def test_matvec_q8_0_unaligned_k(pxq, oracle, rows, inner, columns):
+    """Q8_0 with K not a multiple of 256 (rows that are no 16-byte multiple):
+    the block-walking kernel, with and without the K split."""
+    w = synth.q8_0_weights(rows, inner, seed=inner + columns)
+    x = synth.activations(columns, inner, seed=columns + 7)
+    W = pxq.Weight(w, Q8_0, inner, rows)
+    y = pxq.matmul(W, cuda(x), path="matvec").cpu().numpy()
+    pxq.synchronize()
+    W.release()
+    ok, ref = oracle.quant_matmul(w, Q8_0, x, rows)
+    assert ok and max_abs_rel(y, ref) <= TOL
+
+
 def test_q6_K_golden_past_the_matvec(pxq, golden):
     """Q6_K weights with more activation rows than the matvec takes go to the
     tensor-core GEMM; each output row depends on its own activation row only,
@@ -417,3 +448,20 @@ def test_matmul_gated_vs_oracle(pxq, oracle, wtype, rows, columns):
         pxq.matmul(W, cuda(x))
     assert err.value.code == pxq.ERR_INVALID
     W.release()
+
+
+@pytest.mark.parametrize("columns", [1, 8])
+def test_matmul_gated_q8_0_unaligned_k(pxq, oracle, columns):
+    """Q8_0 gated pair with K not a multiple of 256: the block-walking matvec
+    over both halves, then the silu(gate) * up epilogue kernel."""
+    rows, inner = 192, 800
+    g = synth.weights_for(Q8_0, rows, inner, seed=24)
+    u = synth.weights_for(Q8_0, rows, inner, seed=25)
+    x = synth.activations(columns, inner, seed=26)
+    W = pxq.GatedWeight(g, u, Q8_0, inner, rows)
+    y = pxq.matmul_gated(W, cuda(x)).cpu().numpy()
+    pxq.synchronize()
+    W.release()
+    okg, G = oracle.quant_matmul(g, Q8_0, x, rows)
+    oku, U = oracle.quant_matmul(u, Q8_0, x, rows)
+    assert okg and oku and max_abs_rel(y, _silu_gate(G, U)) <= TOL

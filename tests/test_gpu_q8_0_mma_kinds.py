@@ -17,7 +17,7 @@ from conftest import ROOT
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("kind", ["f16", "i8", "f16s"])
+@pytest.mark.parametrize("kind", ["f16", "i8", "f16s", "pair"])
 def test_q8_0_gemm_parity_in_each_mma_kind(kind):
     env = dict(os.environ, PXQ_Q8_0_MMA=kind)
     files = [os.path.join(ROOT, "tests", f) for f in ("test_gpu_parity.py", "test_gpu_baseline_shapes.py")]
