@@ -855,14 +855,17 @@ constexpr int Q8P_SE = 8;                           // scale entries
 constexpr int Q8P_ENTRY = Q8P_BPS * (Q8P_TN + Q8P_TMP) * 4;  // dW [2][128] | dX [2][256] fp32: 3 KB
 constexpr int Q8P_DX_OFF = Q8P_BPS * Q8P_TN * 4;
 constexpr int Q8P_DRAIN = 8;
-constexpr int Q8P_THREADS = 384;
-constexpr int Q8P_HC = 128;                         // TMEM columns per drain warp
+constexpr int Q8P_THREADS = 32 * (Q8P_DRAIN + 4);
+constexpr int Q8P_PRODUCER_WARP = Q8P_DRAIN, Q8P_MMA_WARP = Q8P_DRAIN + 1;
+constexpr int Q8P_HC = Q8P_TMP / (Q8P_DRAIN / 4);    // TMEM columns per drain warp: 128
 constexpr int Q8P_CW = 16;                          // columns per TMEM load
-constexpr uint32_t Q8P_DRAIN_REGS = 224, Q8P_PRODUCER_REGS = 56;
+constexpr int Q8P_STG_BUFS = 2;                     // output staging buffers per drain warp
+// the drain's 128 accumulators, two loads and their scales need 232 registers
+constexpr uint32_t Q8P_DRAIN_REGS = 232, Q8P_PRODUCER_REGS = 40;
 static_assert(256 * Q8P_DRAIN_REGS + 128 * Q8P_PRODUCER_REGS <= Q8P_THREADS * 168, "setmaxnreg split");
 constexpr int Q8P_OFF_SCALES = Q8P_STAGES * Q8P_STAGE;
 constexpr int Q8P_OFF_STAGING = Q8P_OFF_SCALES + Q8P_SE * Q8P_ENTRY;
-constexpr int Q8P_STAGING = Q8P_DRAIN * 2 * 32 * 32 * 4;  // two [32 activation rows][32 weight rows] fp32 per drain warp
+constexpr int Q8P_STAGING = Q8P_DRAIN * Q8P_STG_BUFS * 32 * 32 * 4;  // [32 activation rows][32 weight rows] fp32 buffers
 constexpr int Q8P_OFF_BAR = Q8P_OFF_STAGING + Q8P_STAGING;
 // full/empty, scale full/empty, slot full/empty, MMA drain-out, gated hand-over
 constexpr int Q8P_NUM_BARS = 2 * Q8P_STAGES + 2 * Q8P_SE + 2 * 2 + 1 + 2;
@@ -870,16 +873,22 @@ constexpr int Q8P_SMEM = Q8P_OFF_BAR + Q8P_NUM_BARS * 8 + 16 + 1024;
 static_assert(Q8P_SMEM <= 232448, "shared memory");
 static_assert(Q8P_STAGE % 1024 == 0 && Q8P_OFF_SCALES % 1024 == 0 && Q8P_ENTRY % 128 == 0, "alignment");
 static_assert(2 * Q8P_TMP <= 512, "TMEM columns");
-static_assert(Q8P_STAGING >= 4 * Q8P_HC * 32 * 4, "gated hand-over buffer");
+static_assert(Q8P_STAGING >= 2 * (Q8P_DRAIN / 4) * Q8P_HC * 32 * 4, "gated hand-over buffer");
 
 // acc[j] += (dx[j] * dw) * I[j] over one TMEM load's columns, two per instruction
 // (pix_dot_q8_0: the fp32 product of the two fp16 scales, exact, times the
-// exact block dot, accumulated with one rounding).
-__device__ __forceinline__ void q8p_fma(float* acc, const uint32_t (&v)[Q8P_CW], const float* dx, float dw)
+// exact block dot, accumulated with one rounding).  dx: the columns' scales,
+// loaded from shared memory one load ahead (q8p_dx).
+__device__ __forceinline__ void q8p_dx(float4 (&d)[Q8P_CW / 4], const float* dx)
+{
+#pragma unroll
+    for (int j = 0; j < Q8P_CW / 4; j++) d[j] = reinterpret_cast<const float4*>(dx)[j];
+}
+__device__ __forceinline__ void q8p_fma(float* acc, const uint32_t (&v)[Q8P_CW], const float4 (&d)[Q8P_CW / 4], float dw)
 {
 #pragma unroll
     for (int j = 0; j < Q8P_CW; j += 4) {
-        const float4 d4 = *reinterpret_cast<const float4*>(dx + j);
+        const float4 d4 = d[j / 4];
         float s0, s1, s2, s3;
         fmul2(s0, s1, d4.x, d4.y, dw, dw);
         fmul2(s2, s3, d4.z, d4.w, dw, dw);
@@ -942,7 +951,7 @@ __global__ void __launch_bounds__(Q8P_THREADS, 1)
         tmem_alloc_pair(tmem_slot, 512);
         tmem_relinquish_pair();
     }
-    if (warp == 8 && lane == 0) {
+    if (warp == Q8P_PRODUCER_WARP && lane == 0) {
         tma_prefetch_desc(&tmW);
         tma_prefetch_desc(&tmX);
         tma_prefetch_desc(&tmDw);
@@ -965,7 +974,7 @@ __global__ void __launch_bounds__(Q8P_THREADS, 1)
 
     if (warp >= Q8P_DRAIN) {
         regs_dec<Q8P_PRODUCER_REGS>();
-        if (warp == 8 && lane == 0) {
+        if (warp == Q8P_PRODUCER_WARP && lane == 0) {
             const uint32_t full0 = cluster_map(smem_u32(full), 0);  // the even CTA's stage barriers
             int stage = 0, se = 0;
             uint32_t ph = 0, sph = 0;
@@ -999,7 +1008,7 @@ __global__ void __launch_bounds__(Q8P_THREADS, 1)
                     }
                 }
             }
-        } else if (warp == 9 && lane == 0 && leader) {
+        } else if (warp == Q8P_MMA_WARP && lane == 0 && leader) {
             int stage = 0, slot = 0;
             uint32_t ph = 0, tph = 0;
             for (int64_t tile = pair; tile < tiles; tile += pairs) {
@@ -1036,7 +1045,7 @@ __global__ void __launch_bounds__(Q8P_THREADS, 1)
     } else {
         // ------------------------------------------------------ drain warps --
         regs_inc<Q8P_DRAIN_REGS>();
-        const uint32_t quad = warp & 3u, half = warp >> 2;
+        const uint32_t quad = warp & 3u, half = warp >> 2;  // half: the warp's column group
         const uint32_t lane_base = (quad * 32u) << 16;
         const uint32_t tempty0 = cluster_map(smem_u32(tempty), 0);  // the even CTA's slot barriers
         auto release = [&](int s) {
@@ -1092,19 +1101,26 @@ __global__ void __launch_bounds__(Q8P_THREADS, 1)
                 } else {
                     // chunk c+1 loads while chunk c is accumulated; the slot is
                     // released once its last chunk is in registers
+                    // chunk c+1 (its block dots from TMEM, its scales from shared
+                    // memory) loads while chunk c is accumulated
                     uint32_t va[Q8P_CW], vb[Q8P_CW];
+                    float4 xa[Q8P_CW / 4], xb[Q8P_CW / 4];
                     tmem_ld16(taddr, va);
+                    q8p_dx(xa, dx);
                     tmem_ld_wait_dep(va);
 #pragma unroll
                     for (int c = 0; c < NCH; c += 2) {
                         tmem_ld16(taddr + (uint32_t)((c + 1) * Q8P_CW), vb);
-                        q8p_fma(acc + c * Q8P_CW, va, dx + c * Q8P_CW, dw);
+                        q8p_dx(xb, dx + (c + 1) * Q8P_CW);
+                        q8p_fma(acc + c * Q8P_CW, va, xa, dw);
                         tmem_ld_wait_dep(vb);
-                        if (c + 2 < NCH)
+                        if (c + 2 < NCH) {
                             tmem_ld16(taddr + (uint32_t)((c + 2) * Q8P_CW), va);
-                        else
+                            q8p_dx(xa, dx + (c + 2) * Q8P_CW);
+                        } else {
                             release(slot);
-                        q8p_fma(acc + (c + 1) * Q8P_CW, vb, dx + (c + 1) * Q8P_CW, dw);
+                        }
+                        q8p_fma(acc + (c + 1) * Q8P_CW, vb, xb, dw);
                         if (c + 2 < NCH) tmem_ld_wait_dep(va);
                     }
                 }
@@ -1129,7 +1145,7 @@ __global__ void __launch_bounds__(Q8P_THREADS, 1)
                     // interleaves 64-row groups); the up warps hand their sums over
                     // through the staging buffer and the gate warps finish
                     // tensor_silu + tensor_gate (src/tensor.cpp:199-208, :334-345)
-                    float* xfer = reinterpret_cast<float*>(smem + Q8P_OFF_STAGING) + ((quad & 1) * 2 + half) * (Q8P_HC * 32);
+                    float* xfer = reinterpret_cast<float*>(smem + Q8P_OFF_STAGING) + ((quad & 1) * (Q8P_DRAIN / 4) + half) * (Q8P_HC * 32);
                     if (!drain_meet(0)) goto done;
                     if (quad >= 2) {
 #pragma unroll
@@ -1152,10 +1168,10 @@ __global__ void __launch_bounds__(Q8P_THREADS, 1)
                 if (p.tma_store) {
                     // four rounds of [32 activation rows][32 weight rows], double-buffered
                     // per warp: lane 0 waits only for the store two rounds back
-                    float* stg0 = reinterpret_cast<float*>(smem + Q8P_OFF_STAGING) + warp * (2 * 32 * 32);
+                    float* stg0 = reinterpret_cast<float*>(smem + Q8P_OFF_STAGING) + warp * (Q8P_STG_BUFS * 32 * 32);
 #pragma unroll
                     for (int r = 0; r < Q8P_HC / 32; r++) {
-                        float* stg = stg0 + (r & 1) * (32 * 32);
+                        float* stg = stg0 + (r % Q8P_STG_BUFS) * (32 * 32);
                         const int64_t mr = mfirst + 32 * r;
                         if (lane == 0) bulk_wait_read_1();
                         __syncwarp();
@@ -1209,7 +1225,7 @@ done:
     if (p.tma_store && warp < Q8P_DRAIN && lane == 0) bulk_wait_all();
     // peer stores are visible system-wide before the kernel ends
     if (p.ndst && warp < Q8P_DRAIN) __threadfence_system();
-    if (warp == 9 && lane == 0 && leader) {
+    if (warp == Q8P_MMA_WARP && lane == 0 && leader) {
         // no MMA of this pair may still be writing TMEM when it is freed (after a
         // normal run the drains have consumed every result; this covers aborts)
         mma_commit_pair_local(mma_done);

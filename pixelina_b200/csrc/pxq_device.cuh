@@ -17,6 +17,11 @@
 #ifndef PXQ_WAIT_NS
 #define PXQ_WAIT_NS 2000000000ull  // 2 s: far above any legitimate wait
 #endif
+// Longest time (ns) a thread waiting in mbarrier.try_wait may stay suspended
+// before it polls again.
+#ifndef PXQ_SUSPEND_NS
+#define PXQ_SUSPEND_NS 1000000u
+#endif
 
 namespace pxq {
 
@@ -87,12 +92,22 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes)
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
 {
     uint32_t ok;
+#ifdef PXQ_TEST_WAIT
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+#endif
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(PXQ_SUSPEND_NS)
         : "memory");
     return ok != 0;
 }
@@ -121,12 +136,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity)
 {
     uint32_t ok;
+#ifdef PXQ_TEST_WAIT
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+#endif
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(PXQ_SUSPEND_NS)
         : "memory");
     return ok != 0;
 }
@@ -464,14 +489,17 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16])
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // tcgen05.wait::ld that the compiler sees as redefining the registers of the
-// load it waits for, so that no use of them can be scheduled before it.
+// load it waits for, so that no use of them can be scheduled before it.  No
+// memory clobber: shared-memory loads that do not depend on the TMEM data
+// may be scheduled across it (ordering against other tcgen05 and mbarrier
+// asm statements is kept, as between all volatile asm).
 __device__ __forceinline__ void tmem_ld_wait_dep(uint32_t (&r)[16])
 {
     asm volatile("tcgen05.wait::ld.sync.aligned;"
                  : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
                    "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
                  :
-                 : "memory");
+                 :);
 }
 __device__ __forceinline__ void tmem_ld_wait_dep(uint32_t (&r)[32])
 {
@@ -481,7 +509,7 @@ __device__ __forceinline__ void tmem_ld_wait_dep(uint32_t (&r)[32])
                    "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
                    "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
                  :
-                 : "memory");
+                 :);
 }
 
 // Warpgroup register reallocation (all warps of a warpgroup execute it).

@@ -100,20 +100,41 @@ __device__ __forceinline__ void q8_K_store_mv(uint8_t* out, const Q8KWarp& r, ui
     if (lane == 0) *reinterpret_cast<float*>(out + kQKK + 16) = r.d;
 }
 
+// Exact fp16 of a small integer (|q| < 512) without a conversion
+// instruction: 1536 + q is an fp16 with unit spacing (bits 0x6600 + q), and
+// subtracting 1536 from it is exact.
+__device__ __forceinline__ __half small_int_half(int q)
+{
+    return __hsub(__ushort_as_half((unsigned short)(0x6600 + q)), __ushort_as_half((unsigned short)0x6600));
+}
+// The same for two values, (lo, hi) in one half2.
+__device__ __forceinline__ __half2 small_int_half2(int lo, int hi)
+{
+    const uint32_t b = ((uint32_t)(0x6600 + lo) & 0xffffu) | ((uint32_t)(0x6600 + hi) << 16);
+    const __half m = __ushort_as_half((unsigned short)0x6600);
+    return __hsub2(*reinterpret_cast<const __half2*>(&b), __halves2half2(m, m));
+}
+
 // ---- Q8_0 (quantize_row_q8_0_ref, src/kernels_quant.cpp:120-144) ----
 
-// roundf: half away from zero, after the rounded product x * id.
-__device__ __forceinline__ float round_half_away(float v)
+// roundf(x * id) -- half away from zero, after the rounded product -- as an
+// integer, for |x * id| < 2^22 (the quantizer's products are at most 127 and
+// a little), without conversion instructions: adding 1.5 * 2^23 rounds the
+// product to the nearest integer, ties to even, into the low mantissa bits;
+// a tie rounded that way toward zero then moves one away from zero.  A NaN
+// product gives 0, as the float -> int conversion does.
+__device__ __forceinline__ int q8_0_round(float x, float id)
 {
-    const float t = truncf(v);
-    const float r = __fsub_rn(v, t);  // exact: fractional part of v
-    return fabsf(r) >= 0.5f ? __fadd_rn(t, copysignf(1.0f, v)) : t;
+    const float v = __fmul_rn(x, id);
+    const float t = __fadd_rn(v, 12582912.0f);
+    const float r = __fsub_rn(t, 12582912.0f);  // rint(v), exact
+    const float d = __fsub_rn(v, r);            // exact, |d| <= 0.5
+    int q = __float_as_int(t) - 0x4B400000;
+    if (d == copysignf(0.5f, v)) q += v > 0.0f ? 1 : -1;
+    return v == v ? q : 0;
 }
 
-__device__ __forceinline__ int8_t q8_0_quant(float x, float id)
-{
-    return static_cast<int8_t>(static_cast<int>(round_half_away(__fmul_rn(x, id))));
-}
+__device__ __forceinline__ int8_t q8_0_quant(float x, float id) { return static_cast<int8_t>(q8_0_round(x, id)); }
 
 // Eight Q8_0 blocks (256 values) as one matvec record (kQ80MvBytes at
 // `out`), one warp, the values 8*lane .. 8*lane+7 in v: block j = lane / 4

@@ -34,7 +34,7 @@ namespace {
 struct Q80Part {
     __half d16;
     uint32_t packed;
-    int8_t q[4];
+    int q[4];
 };
 
 __device__ __forceinline__ Q80Part q8_0_part(const float4 v)
@@ -46,12 +46,12 @@ __device__ __forceinline__ Q80Part q8_0_part(const float4 v)
     const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
     Q80Part p;
     p.d16 = __float2half_rn(d);
-    p.q[0] = q8_0_quant(v.x, id);
-    p.q[1] = q8_0_quant(v.y, id);
-    p.q[2] = q8_0_quant(v.z, id);
-    p.q[3] = q8_0_quant(v.w, id);
-    p.packed = (uint32_t)(uint8_t)p.q[0] | ((uint32_t)(uint8_t)p.q[1] << 8) | ((uint32_t)(uint8_t)p.q[2] << 16) |
-               ((uint32_t)(uint8_t)p.q[3] << 24);
+    p.q[0] = q8_0_round(v.x, id);
+    p.q[1] = q8_0_round(v.y, id);
+    p.q[2] = q8_0_round(v.z, id);
+    p.q[3] = q8_0_round(v.w, id);
+    p.packed = ((uint32_t)p.q[0] & 0xffu) | (((uint32_t)p.q[1] & 0xffu) << 8) | (((uint32_t)p.q[2] & 0xffu) << 16) |
+               ((uint32_t)p.q[3] << 24);
     return p;
 }
 
@@ -135,8 +135,8 @@ __global__ void k_quantize_q8_0_operand(const float* __restrict__ x, void* __res
         if (kind == 1) {
             reinterpret_cast<uint32_t*>(static_cast<int8_t*>(xq) + row * inner)[quad] = p.packed;
         } else {
-            __half2 h01 = __halves2half2(__int2half_rn(p.q[0]), __int2half_rn(p.q[1]));
-            __half2 h23 = __halves2half2(__int2half_rn(p.q[2]), __int2half_rn(p.q[3]));
+            __half2 h01 = small_int_half2(p.q[0], p.q[1]);
+            __half2 h23 = small_int_half2(p.q[2], p.q[3]);
             uint2 packed;
             packed.x = *reinterpret_cast<uint32_t*>(&h01);
             packed.y = *reinterpret_cast<uint32_t*>(&h23);
@@ -236,13 +236,12 @@ __global__ void k_quantize_q8_K_operand(const float* __restrict__ x, __half* __r
     const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     auto emit = [&](int64_t w, const Q8KWarp& r) {
         const int64_t row = w / nsb, sb = w % nsb;
-        __half h[8];
+        __half2 h[4];
         int sum8 = 0;
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            h[j] = __int2half_rn(r.q[j]);
-            sum8 += r.q[j];
-        }
+        for (int j = 0; j < 4; j++) h[j] = small_int_half2(r.q[2 * j], r.q[2 * j + 1]);
+#pragma unroll
+        for (int j = 0; j < 8; j++) sum8 += r.q[j];
         *reinterpret_cast<uint4*>(xq + row * inner + sb * kQKK + lane * 8) = *reinterpret_cast<uint4*>(h);
         // 32-element sub-block sums (lanes 4j..4j+3), split exactly for fp16
         int s32 = sum8 + __shfl_xor_sync(0xffffffffu, sum8, 1);
@@ -251,7 +250,7 @@ __global__ void k_quantize_q8_K_operand(const float* __restrict__ x, __half* __r
             const int j = (int)(lane >> 2);
             const int hi = s32 >> 6;            // floor(s32 / 64)
             const int lo = s32 - (hi << 6);     // 0..63
-            __half2 pair = __halves2half2(__int2half_rn(hi), __int2half_rn(lo));
+            __half2 pair = small_int_half2(hi, lo);
             *reinterpret_cast<__half2*>(amin + row * (nsb * 16) + sb * 16 + 2 * j) = pair;
         }
         if (lane == 0) dxT[sb * ldd + row] = r.d;
