@@ -705,6 +705,9 @@ def run_dit(args, dist: Dist):
 
     flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     step_ms, _, clocks = time_steps(step, args.steps, args.warmup, flush_buf.zero_, args.soak, ClockSampler(dist.local), dist)
+    for blk in blocks:
+        for w in blk.values():
+            w.release()
     ms = dist.max(statistics.mean(step_ms))
     _, bf16, _, peak_src = measured_peaks()
     tops = dist.world * ops / (ms * 1e-3) / 1e12
@@ -914,8 +917,8 @@ def run_gemm_sharded(args, dist: Dist, wl: dict):
 def run_extras(args, dist: Dist) -> dict:
     """The other BASELINE figures at N=1, each timed with CUDA events on its
     own: the Q5_K GEMM and Q8_0 GEMM with their
-    activation quantize, the Q5_K decode and the activation
-    quantize kernels (HBM-bound)."""
+    activation quantize, the activation quantize kernels (HBM-bound), the
+    Q8_0 DiT linear stack and the Q5_K decode."""
     import torch
 
     from pixelina_b200 import pxq
@@ -1004,6 +1007,12 @@ def run_extras(args, dist: Dist) -> dict:
                     "timing": "10 calls per CUDA graph, 5 replays (each call one quantize kernel; inputs and outputs "
                               "larger than L2)"}
         del x
+    # the DiT linear stack: 240 quantize + GEMM calls per step
+    dit_args = argparse.Namespace(**{**vars(args), "steps": 3, "warmup": 1, "soak": 0.0})
+    dit = run_dit(dit_args, dist)
+    out["dit_configs2"] = {k: dit[k] for k in ("value", "unit", "ms_per_step", "ops_per_step", "bf16_frac", "int8_frac")}
+    out["dit_configs2"]["sm_mhz"] = dit["clocks"]["sm_mhz"]
+    torch.cuda.empty_cache()
     # the decode matvec stack, gate/up as one gated call
     dec = run_decode(args, dist, gated=True)
     out["decode_configs3"] = {"weight_bytes_per_token": dec["weight_bytes_per_token"],
