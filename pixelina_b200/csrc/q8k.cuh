@@ -27,29 +27,26 @@ __device__ __forceinline__ void q8_K_load(const float* src, uint32_t lane, float
 
 __device__ __forceinline__ Q8KWarp q8_K_warp_vals(const float (&v)[8], uint32_t lane)
 {
-    // first element (in index order) with the largest |x|: strict '>' scan
-    float amax = 0.0f, vmax = 0.0f;
-    int idx = 0x7fffffff;
+    // the reference's strict '>' scan keeps the first element (in index
+    // order) with the largest |x|: the largest |x| over the warp (NaNs never
+    // win, as there), then the lowest lane holding it gives that element
+    float amax = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const float ax = fabsf(v[j]);
-        if (ax > amax) {
-            amax = ax;
-            vmax = v[j];
-            idx = (int)lane * 8 + j;
+    for (int j = 0; j < 8; j++) amax = fmaxf(amax, fabsf(v[j]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    float vsel = 0.0f;
+    bool hit = false;
+#pragma unroll
+    for (int j = 7; j >= 0; j--) {
+        if (fabsf(v[j]) == amax) {
+            vsel = v[j];
+            hit = true;
         }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float oa = __shfl_xor_sync(0xffffffffu, amax, o);
-        const float ov = __shfl_xor_sync(0xffffffffu, vmax, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-        if (oa > amax || (oa == amax && oi < idx)) {
-            amax = oa;
-            vmax = ov;
-            idx = oi;
-        }
-    }
+    const uint32_t hits = __ballot_sync(0xffffffffu, hit);
+    const float vmax = __shfl_sync(0xffffffffu, vsel, hits ? __ffs(hits) - 1 : 0);
+    (void)lane;
     Q8KWarp r;
     if (amax == 0.0f) {
         r.d = 0.0f;
@@ -119,19 +116,17 @@ __device__ __forceinline__ __half2 small_int_half2(int lo, int hi)
 
 // roundf(x * id) -- half away from zero, after the rounded product -- as an
 // integer, for |x * id| < 2^22 (the quantizer's products are at most 127 and
-// a little), without conversion instructions: adding 1.5 * 2^23 rounds the
-// product to the nearest integer, ties to even, into the low mantissa bits;
-// a tie rounded that way toward zero then moves one away from zero.  A NaN
+// a little), without conversion instructions: floor(|v| + 0.5) is roundf(|v|);
+// adding 0.5 rounded toward zero keeps the floor of the exact sum, and adding
+// 2^23 rounded toward zero leaves that floor in the low mantissa bits.  A NaN
 // product gives 0, as the float -> int conversion does.
 __device__ __forceinline__ int q8_0_round(float x, float id)
 {
     const float v = __fmul_rn(x, id);
-    const float t = __fadd_rn(v, 12582912.0f);
-    const float r = __fsub_rn(t, 12582912.0f);  // rint(v), exact
-    const float d = __fsub_rn(v, r);            // exact, |d| <= 0.5
-    int q = __float_as_int(t) - 0x4B400000;
-    if (d == copysignf(0.5f, v)) q += v > 0.0f ? 1 : -1;
-    return v == v ? q : 0;
+    const float t = __fadd_rz(__fadd_rz(fabsf(v), 0.5f), 8388608.0f);
+    const int a = __float_as_int(t) - 0x4B000000;  // roundf(|v|); out of range for a NaN
+    const int q = (unsigned)a < 256u ? a : 0;
+    return v < 0.0f ? -q : q;
 }
 
 __device__ __forceinline__ int8_t q8_0_quant(float x, float id) { return static_cast<int8_t>(q8_0_round(x, id)); }
