@@ -566,9 +566,12 @@ def run_decode(args, dist: Dist, gated: bool = False):
                         continue
                     pxq.matmul(ws[name], xs[k], out=ys[n], path="matvec")
 
-        # one token = 140 matvecs (each: activation quantize + matvec); replay it as a
-        # CUDA graph so that host launch overhead does not hide the device time
+        # one token = 140 matvecs (112 with gate/up as one call), each a matvec that
+        # quantizes its activation itself or a quantize kernel + matvec; replay it as
+        # a CUDA graph so that host launch overhead does not hide the device time
+        n0 = pxq.kernel_launches()
         token()
+        launches = pxq.kernel_launches() - n0  # this library's kernels in one token
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         side = torch.cuda.Stream()
@@ -595,13 +598,13 @@ def run_decode(args, dist: Dist, gated: bool = False):
         ms = dist.max(statistics.mean(step_ms))
         gbs = wbytes_total / (ms * 1e-3) / 1e9
         results[f"M={M}"] = {"ms_per_token": round(ms, 4), "weight_GBps": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
-                             "clocks": clocks}
+                             "launches_per_token": int(launches), "clocks": clocks}
         del graph
     name = "decode_gated: Q5_K matvec, 28 layers, gate/up as one gated call" if gated else \
         "decode: Q5_K matvec, 28 layers (BASELINE configs[3])"
     return {"metric": METRIC, "workload": name, "unit": "GB/s",
             "weight_bytes_per_token": wbytes_total, "peak_hbm_gbs": hbm, "peak_source": peak_src,
-            "launches_per_token": 2 * 5 * L, "results": results}
+            "results": results}
 
 
 def run_decode_shapes(args, dist: Dist):
@@ -1017,7 +1020,8 @@ def run_extras(args, dist: Dist) -> dict:
     dec = run_decode(args, dist, gated=True)
     out["decode_configs3"] = {"weight_bytes_per_token": dec["weight_bytes_per_token"],
                               **{m: {"ms_per_token": v["ms_per_token"], "weight_GBps": v["weight_GBps"],
-                                     "hbm_frac": v["hbm_frac"], "sm_mhz": v["clocks"]["sm_mhz"]}
+                                     "hbm_frac": v["hbm_frac"], "launches_per_token": v["launches_per_token"],
+                                     "sm_mhz": v["clocks"]["sm_mhz"]}
                                  for m, v in dec["results"].items()}}
     return out
 

@@ -1421,11 +1421,12 @@ int pxq_matmul_host(pxq_weight* w, size_t row_first, size_t row_count, const flo
     // link is full duplex).  Activation rows are quantized independently and
     // every output element depends on its own row only, so the result is the
     // same bit for bit as one call over all rows.
-    // The first chunk is short (128 rows), so the downloads -- the longest
-    // stream of a large call -- start as early as possible.
+    // The first chunk is short (128 rows) and the next ones double up to the
+    // full chunk size, so the downloads -- the longest stream of a large call
+    // when the weight has more rows than its inner size -- start early and
+    // do not wait for the next chunk's upload and GEMM.
     const size_t chunk = columns > 8 ? std::max<size_t>(512, (columns + 7) / 8) : columns;
     const size_t first = columns > 1024 ? 128 : chunk;
-    const size_t nchunks = columns <= first ? 1 : 1 + (columns - first + chunk - 1) / chunk;
     int rc = PXQ_OK;
     cudaError_t e = cudaSuccess;
     cudaEvent_t ready = nullptr;  // buffers allocated on s (and the caller's output rows uploaded)
@@ -1435,9 +1436,9 @@ int pxq_matmul_host(pxq_weight* w, size_t row_first, size_t row_count, const flo
     // keep caller-owned output elements between rows (ldy > row_count) intact
     if (e == cudaSuccess && ldy != row_count && columns > 1) e = cudaMemcpyAsync(yout, output, ybytes, cudaMemcpyHostToDevice, t_up);
     std::vector<cudaEvent_t> evs;
-    for (size_t i = 0; i < nchunks && e == cudaSuccess && !rc; i++) {
-        const size_t c0 = i == 0 ? 0 : first + (i - 1) * chunk;
-        const size_t cn = std::min(i == 0 ? first : chunk, columns - c0);
+    size_t c0 = 0, step = first;
+    for (; c0 < columns && e == cudaSuccess && !rc; c0 += step, step = std::min(2 * step, chunk)) {
+        const size_t cn = std::min(step, columns - c0);
         cudaEvent_t up = nullptr, done = nullptr;
         if ((e = cudaEventCreateWithFlags(&up, cudaEventDisableTiming)) != cudaSuccess) break;
         evs.push_back(up);

@@ -13,7 +13,9 @@
 // Bit-exactness rules (all arithmetic uses explicit _rn intrinsics so that
 // nvcc's default FMA contraction cannot change a rounding):
 //   * d = amax/127 and 1/d are IEEE divisions;
-//   * Q8_0 rounds x*id half away from zero (roundf) after a rounded product;
+//   * Q8_0 rounds x*id half away from zero (roundf) after a rounded product
+//     (q8_0_round in q8k.cuh: two round-toward-zero adds, no conversion
+//     instruction);
 //   * Q8_K rounds iscale*x half to even through the 1.5*2^23 bias, and the
 //     reference build evaluates `iscale*x + bias` as ONE fused multiply-add
 //     (g++ -O3 -std=c++17 contracts it; pinned by the golden vectors), so the

@@ -383,7 +383,7 @@ def test_host_matmul_chunked_pipeline(pxq, oracle, wtype):
     ldy > rows the caller's elements between output rows are left as they were."""
     import ctypes as C
 
-    rows, inner, M = 96, 512, 1300  # chunks of 512, 512, 276
+    rows, inner, M = 96, 512, 1300  # chunks of 128, 256, 512 and 404 rows
     w = synth.weights_for(wtype, rows, inner, seed=41)
     x = synth.activations(M, inner, seed=42)
     ok, ref = oracle.quant_matmul(w, wtype, x, rows)
