@@ -720,6 +720,63 @@ def run_dit(args, dist: Dist):
             "peak_source": peak_src, "clocks": clocks}
 
 
+def run_dit_sharded(args, dist: Dist):
+    """BASELINE configs[2] N-sharded over the ranks: every linear's weight rows
+    split evenly (rank r holds rows [r*n/G, (r+1)*n/G) of each of the 240
+    weights), each call the sharded GEMM whose epilogue stores the rank's
+    columns into every rank's output over NVLink (pxq_sharded_matmul), so each
+    linear's whole output is on every rank.  value = the whole stack's
+    2*M*N*K over the max over ranks of the step time (strong scaling)."""
+    import torch
+
+    from pixelina_b200 import pxq, sharded
+
+    pxq.init(dist.local)
+    G, r = dist.world, dist.rank
+    comm = sharded.Comm(G, r, timeout_ms=120000)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(11)  # the same weights on every rank
+    H, F, B, M, QKV = DIT["hidden"], DIT["ffn"], DIT["blocks"], DIT["M"], DIT["qkv"]
+    shapes = [("qkv", QKV, H), ("out", H, H), ("up", F, H), ("down", H, F)]
+    blocks = []
+    for _ in range(B):
+        blk = {}
+        for name, n, k in shapes:
+            full = gpu_random_q8_0(n, k, gen)
+            blk[name] = sharded.ShardedWeight(full, Q8_0, k, n, G, r)
+            del full
+        blocks.append(blk)
+    xs = {H: torch.randn((M, H), device="cuda", generator=gen), F: torch.randn((M, F), device="cuda", generator=gen)}
+    outs = {n: sharded.ShardedOutput(comm, M, n) for n in sorted({n for _, n, _ in shapes})}
+    ops = sum(2.0 * M * n * k for _, n, k in shapes) * B
+
+    def step(ev):
+        if ev is not None:
+            ev["start"], ev["end"] = ev_pair()
+            ev["start"].record()
+        for blk in blocks:
+            for name, n, k in shapes:
+                sharded.sharded_matmul(comm, blk[name], xs[k], out=outs[n])
+        if ev is not None:
+            ev["end"].record()
+
+    flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    step_ms, _, clocks = time_steps(step, args.steps, args.warmup, flush_buf.zero_, args.soak, ClockSampler(dist.local), dist)
+    comm.synchronize()
+    ms = dist.max(statistics.mean(step_ms))
+    _, bf16, _, peak_src = measured_peaks()
+    tops = ops / (ms * 1e-3) / 1e12
+    for o in outs.values():
+        o.close()
+    for blk in blocks:
+        for w in blk.values():
+            w.release()
+    comm.close()
+    return {"metric": METRIC, "workload": f"dit: 60 Q8_0 DiT blocks, M=4352 (BASELINE configs[2]), N-sharded over {G} GPUs",
+            "unit": "TOPS", "value": round(tops, 2), "ms_per_step": round(ms, 3), "ops_per_step": ops, "n_gpus": G,
+            "scaling": "strong", "per_gpu_bf16_frac": round(tops / G / bf16, 4), "peak_source": peak_src, "clocks": clocks}
+
+
 def run_attention(args, dist: Dist):
     """The callers' attention step (tensor_attention) at the BASELINE models'
     shapes: DiT prefill (configs[2]: 4352 tokens, 24 heads of 128, non-causal)
@@ -1060,7 +1117,7 @@ def main():
         elif args.workload == "decode_shapes":
             out = run_decode_shapes(args, dist)
         else:
-            out = run_dit(args, dist)
+            out = run_dit_sharded(args, dist) if dist.world > 1 else run_dit(args, dist)
         if dist.rank == 0:
             print(json.dumps(out), flush=True)
     finally:
