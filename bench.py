@@ -79,6 +79,18 @@ def measured_peaks():
         return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, 1400.0, "fallback"
 
 
+def gemm_peak(wtype, bf16, peak_src):
+    """The roofline peak of a GEMM line: the Q8_0 kernel's block dots are
+    kind::i8 MMAs (the int8 rate, 2x the measured bf16 dense peak on this
+    part: the kind::i8 and kind::f16 MMA rates were measured in the ratio
+    2.00), the K-quant kernels issue kind::f16 MMAs (the bf16 peak)."""
+    if wtype == Q8_0:
+        return {"peak": 2 * bf16, "unit": "TFLOP/s",
+                "peak_source": f"{peak_src} bf16 dense (burst) x 2: the block dots are kind::i8 MMAs"}
+    return {"peak": bf16, "unit": "TFLOP/s",
+            "peak_source": f"{peak_src} bf16 dense (burst); the GEMM issues kind::f16 MMAs on exact integer values"}
+
+
 def committed_traffic(kernel_key):
     """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
@@ -361,10 +373,10 @@ def run_gemm_workload(args, dist: Dist, wl: dict):
                    "activation_quant": "Q8_0" if wtype == Q8_0 else "Q8_K",
                    "parallelism": "one GPU (N>1: the same problem N-sharded)",
                    "l2": "flushed between timed steps (256 MB write, outside the events)"},
-        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": bf16, "unit": "TFLOP/s",
-                     "frac": round(achieved / bf16, 4),
-                     "peak_source": f"{peak_src} bf16 dense (burst); the GEMM issues kind::f16 MMA on exact int8 values",
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), **gemm_peak(wtype, bf16, peak_src),
+                     "frac": round(achieved / gemm_peak(wtype, bf16, peak_src)["peak"], 4),
                      "int8_peak_equiv": 2 * bf16, "int8_frac": round(achieved / (2 * bf16), 4),
+                     "bf16_frac": round(achieved / bf16, 4),
                      "kernel": "k_gemm_q8s" if wtype == Q8_0 else "k_gemm", "kernel_ms": round(gemm_ms, 4),
                      "quantize_ms": round(quant_ms, 4),
                      "traffic": traffic},
@@ -949,9 +961,10 @@ def run_gemm_sharded(args, dist: Dist, wl: dict):
                    "parallelism": f"N-sharded x{G} (rows {sw.count} per rank), Y assembled on every rank by the GEMM's "
                                   "peer stores over NVLink",
                    "l2": "flushed between timed steps (256 MB write, outside the events)"},
-        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": bf16, "unit": "TFLOP/s",
-                     "frac": round(achieved / bf16, 4), "peak_source": f"{peak_src} bf16 dense (burst)",
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), **gemm_peak(wtype, bf16, peak_src),
+                     "frac": round(achieved / gemm_peak(wtype, bf16, peak_src)["peak"], 4),
                      "int8_peak_equiv": 2 * bf16, "int8_frac": round(achieved / (2 * bf16), 4),
+                     "bf16_frac": round(achieved / bf16, 4),
                      "kernel": "k_gemm_q8s (this rank's shard)" if wtype == Q8_0 else "k_gemm (this rank's shard)",
                      "kernel_ms": round(gemm_ms, 4),
                      "traffic": None},
@@ -1033,9 +1046,9 @@ def run_extras(args, dist: Dist) -> dict:
         else:
             def fn():
                 pxq.Activation(wtype, x).release()
-            kind = os.environ.get("PXQ_Q8_0_MMA", "f16s")
-            # quants (int8 for kind "i8", else fp16) and block scales (fp16 for "f16s", else fp32)
-            wbytes = M * K * (1 if kind == "i8" else 2) + M * K // 32 * (2 if kind == "f16s" else 4)
+            kind = os.environ.get("PXQ_Q8_0_MMA", "i8s")  # the library's default operand kind
+            # quants (int8 for kinds "i8" and "i8s", else fp16) and block scales (fp16 for "f16s" and "i8s", else fp32)
+            wbytes = M * K * (1 if kind in ("i8", "i8s") else 2) + M * K // 32 * (2 if kind in ("f16s", "i8s") else 4)
         # 10 calls captured in a CUDA graph (no host launch gaps), replayed
         for _ in range(3):
             fn()

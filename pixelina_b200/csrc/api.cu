@@ -244,8 +244,9 @@ std::unordered_map<std::string, pxq_weight*> g_cache;  // guarded by g_mutex
 // (kind::f16) with the scales applied on the CUDA cores, 1 = the int8 quants
 // (kind::i8) likewise, 2 = fp16 copies with the scale products from a
 // one-hot tensor-core MMA, 3 = kind 0's operands on CTA pairs (256 x 256
-// tiles).  Read once from PXQ_Q8_0_MMA ("f16", "i8", "f16s", "pair"); the
-// default is kind 2.
+// tiles), 4 = kind 2 with the int8 quants (kind::i8 block dots).  Read once
+// from PXQ_Q8_0_MMA ("f16", "i8", "f16s", "pair", "i8s"); the default is
+// kind 4, the fastest measured.
 int q8_operand_kind()
 {
     static const int v = [] {
@@ -253,7 +254,8 @@ int q8_operand_kind()
         if (e && strcmp(e, "f16") == 0) return 0;
         if (e && strcmp(e, "i8") == 0) return 1;
         if (e && strcmp(e, "pair") == 0) return 3;
-        return 2;
+        if (e && strcmp(e, "f16s") == 0) return 2;
+        return 4;
     }();
     return v;
 }
@@ -359,7 +361,7 @@ int build_packed(const DeviceCtx* d, pxq_weight* w, int64_t first, int64_t count
     const int64_t K = w->inner;
     const bool q5 = w->type == kTypeQ5_K, q6 = w->type == kTypeQ6_K, q8 = w->type == kTypeQ8_0;
     const int kind = q8 ? q8_operand_kind() : 0;
-    const bool i8 = kind == 1, onehot = q8 && kind == 2;
+    const bool i8 = kind == 1 || kind == 4, onehot = q8 && (kind == 2 || kind == 4);
     const int64_t nb = (q5 || q6) ? K / kQKK : K / kQK8_0;
     const int64_t Kop = q6 ? 2 * K : K;  // Q6_K: even and parity planes per chunk
     const int64_t elem = i8 ? 1 : 2;
@@ -486,7 +488,7 @@ int quantize_activation(DeviceCtx* d, uint32_t wtype, const float* input, int64_
         e = launch_matvec_quantize(plan, input, K, a->mem, nullptr, s);
     } else {
         const int kind = q5 ? 0 : q8_operand_kind();
-        const bool i8 = kind == 1, onehot = !q5 && kind == 2;
+        const bool i8 = kind == 1 || kind == 4, onehot = !q5 && (kind == 2 || kind == 4);
         a->q8_kind = kind;
         // scales: fp32 block-major [nb][round_up(M, 4)], or (one-hot kind) fp16
         // row-major [M][round_up(nb, 8)]

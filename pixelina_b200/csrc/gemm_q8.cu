@@ -10,14 +10,19 @@
 // Design (sm_100a, one CTA per SM, persistent over 128 x 128 output tiles,
 // 16 drain warps -- four per scheduler -- plus a producer and an MMA warp):
 //   * Per 32-block the tensor core computes the block dots I into TMEM and
-//     the drain accumulates S * I per element.  Three operand kinds
+//     the drain accumulates S * I per element.  Operand kinds
 //     (GemmOperands::q8_kind, PXQ_Q8_0_MMA):
-//       2 (default, fastest measured): exact fp16 copies of the quants,
-//         kind::f16 MMAs for I, and a K = 16 MMA of a one-hot weight-scale
-//         tile against the activations' fp16 scale tile for S, exact
-//         because fp16 x fp16 fits fp32 (k_gemm_q8s).  TMEM holds (S, I)
-//         for two blocks; the drain does one packed FMA per element pair
-//         and block and reads no scales from shared memory.
+//       4 (default, fastest measured): the int8 quants, one kind::i8 MMA
+//         (K = 32) per block for the exact int32 dots I, and a K = 16
+//         kind::f16 MMA of a one-hot weight-scale tile against the
+//         activations' fp16 scale tile for S = dW * dX, exact because
+//         fp16 x fp16 fits fp32 (k_gemm_q8s<., true>).  TMEM holds (S, I)
+//         for two blocks; the drain converts I to fp32 (exact: |I| <=
+//         32 * 127 * 127) and does one packed FMA per element pair and
+//         block, reading no scales from shared memory.
+//       2: the same with exact fp16 copies of the quants and two kind::f16
+//         MMAs (K = 16 each) for I (k_gemm_q8s<., false>).
+//       3: kind 0's operands on CTA pairs (k_gemm_q8p, below).
 //       0: fp16 copies, kind::f16 for I; the drain forms S = dW * dX itself
 //         from fp32 block-major scale planes (k_gemm_q8<0>): two packed fp32
 //         instructions per element pair, four blocks of I in TMEM.
@@ -545,13 +550,22 @@ done:
 constexpr int Q8S_STAGES = 3;
 constexpr int Q8S_W1H = 128 * 32;                                   // one-hot tile [128][16] fp16, 32-byte swizzle
 constexpr int Q8S_XS = 128 * 32;                                    // activation scale tile [128][16] fp16
-constexpr int Q8S_STAGE = 2 * Q8_OP_BYTES + 2 * Q8S_W1H + Q8S_XS;  // W | X | one-hot x 2 | X scales: 44 KB
-constexpr int Q8S_OFF_STAGING = Q8S_STAGES * Q8S_STAGE;
-constexpr int Q8S_OFF_BAR = Q8S_OFF_STAGING + Q8_STAGING;
+// blocks per operand stage: one 128-byte swizzle row holds 2 blocks of fp16
+// quants, 4 of int8 quants (operand kind 4)
+template <bool I8>
+__host__ __device__ constexpr int q8s_bps() { return I8 ? 4 : 2; }
+// W | X | one-hot x BPS | X scales: 44 KB (fp16 quants), 52 KB (int8 quants)
+template <bool I8>
+__host__ __device__ constexpr int q8s_stage() { return 2 * Q8_OP_BYTES + q8s_bps<I8>() * Q8S_W1H + Q8S_XS; }
+template <bool I8>
+__host__ __device__ constexpr int q8s_off_staging() { return Q8S_STAGES * q8s_stage<I8>(); }
+template <bool I8>
+__host__ __device__ constexpr int q8s_off_bar() { return q8s_off_staging<I8>() + Q8_STAGING; }
 constexpr int Q8S_NUM_BARS = 2 * Q8S_STAGES + 2 * 2 + 1 + 2;
-constexpr int Q8S_SMEM = Q8S_OFF_BAR + Q8S_NUM_BARS * 8 + 16 + 1024;
-static_assert(Q8S_SMEM <= 232448, "shared memory");
-static_assert(Q8S_STAGE % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+template <bool I8>
+__host__ __device__ constexpr int q8s_smem() { return q8s_off_bar<I8>() + Q8S_NUM_BARS * 8 + 16 + 1024; }
+static_assert(q8s_smem<false>() <= 232448 && q8s_smem<true>() <= 232448, "shared memory");
+static_assert(q8s_stage<false>() % 1024 == 0 && q8s_stage<true>() % 1024 == 0, "swizzled tiles need 1024-byte alignment");
 
 __device__ __forceinline__ uint64_t desc_sw32(uint32_t saddr) { return smem_desc(saddr, 16, 256, 6); }
 
@@ -561,16 +575,18 @@ __device__ __forceinline__ uint64_t desc_sw32(uint32_t saddr) { return smem_desc
 //   tmWs  one-hot weight scales fp16 [N][nb*16] box {16, 128}  32B swizzle
 //   tmXs  activation scales fp16 [M][ldd]       box {16, 128}  32B swizzle
 //   tmY   output fp32 [M][ldy], box {32, 32} (TMA-store epilogue)
-template <bool DUMP>
+template <bool DUMP, bool I8>
 __global__ void __launch_bounds__(Q8_THREADS, 1)
     k_gemm_q8s(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                const __grid_constant__ CUtensorMap tmWs, const __grid_constant__ CUtensorMap tmXs,
                const __grid_constant__ CUtensorMap tmY, const Q8Params p)
 {
     constexpr uint32_t IDESC = idesc_f16_f32(Q8_TN, Q8_TM);
+    constexpr uint32_t IDESC_I8 = idesc_i8_s32(Q8_TN, Q8_TM);
+    constexpr int BPS = q8s_bps<I8>(), STAGE = q8s_stage<I8>();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Q8S_OFF_BAR);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + q8s_off_bar<I8>());
     uint64_t* full = bars;                   // operand stage loaded
     uint64_t* empty = full + Q8S_STAGES;     // operand stage consumed by the MMAs
     uint64_t* tfull = empty + Q8S_STAGES;    // slot pair holds a block's (S, I)
@@ -616,7 +632,7 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
     const int64_t nt = (p.N + Q8_TN - 1) / Q8_TN;
     const int64_t tiles = mt * nt;
     const int64_t nb = p.K / kQK8_0;
-    const int64_t nstages = (nb + 1) / 2;
+    const int64_t nstages = (nb + BPS - 1) / BPS;
     uint32_t* status = p.status;
 
     if (warp >= Q8_DRAIN_WARPS) {
@@ -631,15 +647,15 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
                 const int32_t n0 = (int32_t)(p.n_first + ni * Q8_TN);
                 for (int64_t kc = 0; kc < nstages; kc++) {
                     if (!mbar_wait(&empty[stage], ph ^ 1u, abort_flag, status, kDevTimeoutEmpty)) goto done;
-                    uint8_t* st = smem + stage * Q8S_STAGE;
-                    const int nblk = (2 * kc + 1 < nb) ? 2 : 1;
+                    uint8_t* st = smem + stage * STAGE;
+                    const int nblk = nb - BPS * kc < BPS ? (int)(nb - BPS * kc) : BPS;
                     mbar_expect_tx(&full[stage], 2 * Q8_OP_BYTES + nblk * Q8S_W1H + Q8S_XS);
-                    const int32_t kx = (int32_t)(kc * 64);
+                    const int32_t kx = (int32_t)(kc * 32 * BPS);  // quants of BPS blocks: one 128-byte row
                     tma_load_2d(st, &tmW, &full[stage], kx, n0);
                     tma_load_2d(st + Q8_OP_BYTES, &tmX, &full[stage], kx, m0);
                     for (int b = 0; b < nblk; b++)
-                        tma_load_2d(st + 2 * Q8_OP_BYTES + b * Q8S_W1H, &tmWs, &full[stage], (int32_t)((2 * kc + b) * 16), n0);
-                    tma_load_2d(st + 2 * Q8_OP_BYTES + 2 * Q8S_W1H, &tmXs, &full[stage], (int32_t)(((2 * kc) / 16) * 16), m0);
+                        tma_load_2d(st + 2 * Q8_OP_BYTES + b * Q8S_W1H, &tmWs, &full[stage], (int32_t)((BPS * kc + b) * 16), n0);
+                    tma_load_2d(st + 2 * Q8_OP_BYTES + BPS * Q8S_W1H, &tmXs, &full[stage], (int32_t)(((BPS * kc) / 16) * 16), m0);
                     if (++stage == Q8S_STAGES) {
                         stage = 0;
                         ph ^= 1u;
@@ -653,22 +669,28 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
                 for (int64_t kc = 0; kc < nstages; kc++) {
                     if (!mbar_wait(&full[stage], ph, abort_flag, status, kDevTimeoutFull)) goto done;
                     tc_fence_after();
-                    const uint32_t w_addr = smem_u32(smem + stage * Q8S_STAGE);
+                    const uint32_t w_addr = smem_u32(smem + stage * STAGE);
                     const uint32_t x_addr = w_addr + Q8_OP_BYTES;
                     const uint32_t ws_addr = x_addr + Q8_OP_BYTES;
-                    const uint32_t xs_addr = ws_addr + 2 * Q8S_W1H;
+                    const uint32_t xs_addr = ws_addr + BPS * Q8S_W1H;
 #pragma unroll
-                    for (int bi = 0; bi < 2; bi++) {
-                        if (2 * kc + bi >= nb) break;
+                    for (int bi = 0; bi < BPS; bi++) {
+                        if (BPS * kc + bi >= nb) break;
                         if (!mbar_wait(&tempty[pair], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
                         tc_fence_after();
                         const uint32_t ds = tmem_base + (uint32_t)(pair * 2 * Q8_TM);
-                        // S: the one-hot tile selects block (2kc+bi) % 16 of the activation scale tile
+                        // S: the one-hot tile selects block (BPS*kc+bi) % 16 of the activation scale tile
                         if (!DUMP) mma_f16(ds, desc_sw32(ws_addr + bi * Q8S_W1H), desc_sw32(xs_addr), IDESC, 0u);
+                        if constexpr (I8) {
+                            // I: one kind::i8 MMA, K = 32 (the block's 32 bytes)
+                            const uint32_t koff = (uint32_t)bi * 32u;
+                            mma_i8(ds + Q8_TM, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC_I8, 0u);
+                        } else {
 #pragma unroll
-                        for (int k = 0; k < 2; k++) {
-                            const uint32_t koff = (uint32_t)(bi * 2 + k) * 32u;
-                            mma_f16(ds + Q8_TM, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC, (uint32_t)k);
+                            for (int k = 0; k < 2; k++) {
+                                const uint32_t koff = (uint32_t)(bi * 2 + k) * 32u;
+                                mma_f16(ds + Q8_TM, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC, (uint32_t)k);
+                            }
                         }
                         mma_commit(&tfull[pair]);
                         if (++pair == 2) {
@@ -726,14 +748,18 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < Q8_HC; j++) {
                         const int64_t m = mfirst + j;
-                        if (n < p.N && m < p.M) p.dump[(b * p.M + m) * p.N + n] = __uint_as_float(iv[j]);
+                        if (n < p.N && m < p.M)
+                            p.dump[(b * p.M + m) * p.N + n] = I8 ? __int2float_rn((int)iv[j]) : __uint_as_float(iv[j]);
                     }
                 } else {
                     // pix_dot_q8_0: acc = fma(fp16(dw)*fp16(dx), float(block dot), acc), two per instruction
 #pragma unroll
-                    for (int j = 0; j < Q8_HC; j += 2)
-                        ffma2(acc[j], acc[j + 1], __uint_as_float(sv[j]), __uint_as_float(sv[j + 1]), __uint_as_float(iv[j]),
-                              __uint_as_float(iv[j + 1]));
+                    for (int j = 0; j < Q8_HC; j += 2) {
+                        // kind::i8 leaves exact int32 dots: |I| <= 32 * 127 * 127, exact in fp32
+                        const float i0 = I8 ? __int2float_rn((int)iv[j]) : __uint_as_float(iv[j]);
+                        const float i1 = I8 ? __int2float_rn((int)iv[j + 1]) : __uint_as_float(iv[j + 1]);
+                        ffma2(acc[j], acc[j + 1], __uint_as_float(sv[j]), __uint_as_float(sv[j + 1]), i0, i1);
+                    }
                 }
             }
             if constexpr (!DUMP) {
@@ -743,7 +769,7 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
                     // interleaves 64-row groups); the up warps hand their sums over
                     // through the staging buffer and the gate warps finish
                     // tensor_silu + tensor_gate (src/tensor.cpp:199-208, :334-345)
-                    float* xfer = reinterpret_cast<float*>(smem + Q8S_OFF_STAGING) + ((quad & 1) * 4 + quarter) * (Q8_HC * 32);
+                    float* xfer = reinterpret_cast<float*>(smem + q8s_off_staging<I8>()) + ((quad & 1) * 4 + quarter) * (Q8_HC * 32);
                     if (!drain_meet(0)) goto done;
                     if (quad >= 2) {
 #pragma unroll
@@ -763,7 +789,7 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
                 }
                 const float bv = (p.bias && n < p.N) ? p.bias[n] : 0.f;
                 if (p.tma_store) {
-                    float* stg = reinterpret_cast<float*>(smem + Q8S_OFF_STAGING) + warp * (Q8_HC * 32);
+                    float* stg = reinterpret_cast<float*>(smem + q8s_off_staging<I8>()) + warp * (Q8_HC * 32);
                     if (lane == 0) bulk_wait_read_all();
                     __syncwarp();
 #pragma unroll
@@ -1281,11 +1307,12 @@ cudaError_t launch_q8p(const GemmOperands& op, int num_sms, cudaStream_t s)
     return cudaLaunchKernelEx(&cfg, kern, op.tm[0], op.tm[1], op.tm[4], op.tm[6], op.tm_y, p);
 }
 
-template <bool DUMP>
+template <bool DUMP, bool I8>
 cudaError_t launch_q8s(const GemmOperands& op, int num_sms, cudaStream_t s)
 {
-    auto kern = k_gemm_q8s<DUMP>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Q8S_SMEM);
+    auto kern = k_gemm_q8s<DUMP, I8>;
+    constexpr int smem = q8s_smem<I8>();
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     const int64_t tiles = ((op.M + Q8_TM - 1) / Q8_TM) * ((op.N + Q8_TN - 1) / Q8_TN);
     int64_t grid = num_sms;
@@ -1294,7 +1321,7 @@ cudaError_t launch_q8s(const GemmOperands& op, int num_sms, cudaStream_t s)
     Q8Params p{op.M, op.N, op.K, op.n_first, op.y, op.ldy, op.bias, op.dump, op.status, (op.tma_store && !DUMP) ? 1 : 0,
                op.gated, op.ndst, op.dst_vec4, op.col_off, {}};
     for (int k = 0; k < kMaxScatter; k++) p.ydst[k] = op.ydst[k];
-    kern<<<(unsigned)grid, Q8_THREADS, Q8S_SMEM, s>>>(op.tm[0], op.tm[1], op.tm[2], op.tm[3], op.tm_y, p);
+    kern<<<(unsigned)grid, Q8_THREADS, smem, s>>>(op.tm[0], op.tm[1], op.tm[2], op.tm[3], op.tm_y, p);
     return cudaGetLastError();
 }
 
@@ -1321,7 +1348,8 @@ cudaError_t launch_q8_typed(const GemmOperands& op, int num_sms, cudaStream_t s)
 cudaError_t launch_gemm_q8(const GemmOperands& op, int num_sms, cudaStream_t s)
 {
     if (op.q8_kind == 3) return op.dump ? launch_q8p<true>(op, num_sms, s) : launch_q8p<false>(op, num_sms, s);
-    if (op.q8_kind == 2) return op.dump ? launch_q8s<true>(op, num_sms, s) : launch_q8s<false>(op, num_sms, s);
+    if (op.q8_kind == 2) return op.dump ? launch_q8s<true, false>(op, num_sms, s) : launch_q8s<false, false>(op, num_sms, s);
+    if (op.q8_kind == 4) return op.dump ? launch_q8s<true, true>(op, num_sms, s) : launch_q8s<false, true>(op, num_sms, s);
     if (op.q8_kind == 1)
         return op.dump ? launch_q8_typed<1, true>(op, num_sms, s) : launch_q8_typed<1, false>(op, num_sms, s);
     return op.dump ? launch_q8_typed<0, true>(op, num_sms, s) : launch_q8_typed<0, false>(op, num_sms, s);

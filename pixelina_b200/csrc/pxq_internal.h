@@ -185,7 +185,8 @@ struct GemmOperands {
     uint32_t type;        // kTypeQ8_0, kTypeQ5_K or kTypeQ6_K
     int q8_kind;          // Q8_0 operand kind (gemm_q8.cu): 0 fp16 quants, scales applied on the CUDA cores;
                           // 1 int8 quants (kind::i8), scales on the CUDA cores; 2 fp16 quants, scale
-                          // products from a one-hot tensor-core MMA; 3 kind 0's operands on CTA pairs
+                          // products from a one-hot tensor-core MMA; 3 kind 0's operands on CTA pairs;
+                          // 4 int8 quants (kind::i8) with kind 2's scale products
     int64_t M, N, K;      // activation rows, view rows (output columns), inner
     int64_t n_first;      // first weight row of the view (multiple of 4)
     // tensor maps (boxes as listed in gemm.cu and gemm_q8.cu): 0 weight

@@ -127,14 +127,15 @@ __global__ void k_quantize_q8_0_blocks(const float* x, uint8_t* __restrict__ y, 
     });
 }
 
-// GEMM operand: the quants as int8 (kind 1) or exact fp16 values (kinds 0,
-// 2), [rows][inner], and the stored fp16 block scales: as fp32, block-major
-// [inner/32][ldd] (kinds 0, 1), or as fp16, row-major [rows][ldd] (kind 2).
+// GEMM operand: the quants as int8 (kinds 1, 4) or exact fp16 values (kinds
+// 0, 2), [rows][inner], and the stored fp16 block scales: as fp32,
+// block-major [inner/32][ldd] (kinds 0, 1), or as fp16, row-major
+// [rows][ldd] (kinds 2, 4).
 __global__ void k_quantize_q8_0_operand(const float* __restrict__ x, void* __restrict__ xq, void* __restrict__ dx, int kind,
                                         int64_t rows, int64_t inner, int64_t ldx, int64_t ldd)
 {
     q8_0_rows(x, rows, inner, ldx, [&](int64_t row, int64_t quad, const Q80Part& p) {
-        if (kind == 1) {
+        if (kind == 1 || kind == 4) {
             reinterpret_cast<uint32_t*>(static_cast<int8_t*>(xq) + row * inner)[quad] = p.packed;
         } else {
             __half2 h01 = small_int_half2(p.q[0], p.q[1]);
@@ -145,7 +146,7 @@ __global__ void k_quantize_q8_0_operand(const float* __restrict__ x, void* __res
             *reinterpret_cast<uint2*>(static_cast<__half*>(xq) + row * inner + quad * 4) = packed;
         }
         if ((quad & 7) == 0) {
-            if (kind == 2)
+            if (kind == 2 || kind == 4)
                 static_cast<__half*>(dx)[row * ldd + quad / 8] = p.d16;
             else
                 static_cast<float*>(dx)[(quad / 8) * ldd + row] = __half2float(p.d16);

@@ -57,9 +57,9 @@ __device__ __forceinline__ int64_t src_row(int64_t r, int64_t gate_rows)
 }
 
 // One thread per (row, 32-block): the block's 32 quants into the operand row
-// (int8 as stored for kind 1, their exact fp16 values otherwise) and its
-// fp16 scale into the block-major fp32 plane (kinds 0, 1) or the one-hot
-// tile (kind 2).
+// (int8 as stored for kinds 1 and 4, their exact fp16 values otherwise) and
+// its fp16 scale into the block-major fp32 plane (kinds 0, 1) or the one-hot
+// tile (kinds 2, 4).
 __global__ void k_repack_q8_0(const uint8_t* __restrict__ raw, int64_t rows, int64_t inner, int64_t stride,
                               void* __restrict__ wq, float* __restrict__ dT, __half* __restrict__ ws1h, int64_t ldn, int kind,
                               int64_t gate_rows)
@@ -69,7 +69,7 @@ __global__ void k_repack_q8_0(const uint8_t* __restrict__ raw, int64_t rows, int
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = i / nb, b = i % nb;
         const uint8_t* blk = raw + src_row(r, gate_rows) * stride + b * kQ8_0Bytes;
-        if (kind == 1) {
+        if (kind == 1 || kind == 4) {
             // qs start at byte 2 of the 34-byte block: 2-byte aligned loads
             uint16_t q[16];
 #pragma unroll
@@ -85,7 +85,7 @@ __global__ void k_repack_q8_0(const uint8_t* __restrict__ raw, int64_t rows, int
 #pragma unroll
             for (int j = 0; j < 4; j++) dst[j] = reinterpret_cast<uint4*>(h)[j];
         }
-        if (kind == 2) {
+        if (kind == 2 || kind == 4) {
             __half g[16];
 #pragma unroll
             for (int j = 0; j < 16; j++) g[j] = __ushort_as_half((unsigned short)0);

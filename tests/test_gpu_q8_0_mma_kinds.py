@@ -1,10 +1,11 @@
-"""The Q8_0 GEMM has three operand kinds (gemm_q8.cu): exact fp16 copies of
-the quants with the block scales applied on the CUDA cores ("f16"), the int8
-quants with kind::i8 MMAs likewise ("i8"), and fp16 copies with the scale
-products from a one-hot tensor-core MMA ("f16s", the default).  The library
-picks one per process (PXQ_Q8_0_MMA, read once).  The rest of the GPU suite
-runs the default kind; this test reruns the GEMM parity files in a child
-process with each kind, so all stay bit-exact in their block dots and within
+"""The Q8_0 GEMM has five operand kinds (gemm_q8.cu): the int8 quants with
+kind::i8 block-dot MMAs and the scale products from a one-hot tensor-core MMA
+("i8s", the default), the same on exact fp16 copies of the quants ("f16s"),
+fp16 copies with the block scales applied on the CUDA cores ("f16"), the int8
+quants likewise ("i8"), and "f16" on CTA pairs ("pair").  The library picks
+one per process (PXQ_Q8_0_MMA, read once).  The rest of the GPU suite runs
+the default kind; this test reruns the GEMM parity files in a child process
+with each kind, so all stay bit-exact in their block dots and within
 max-abs-rel 1e-3 of the oracle."""
 import os
 import subprocess
@@ -17,7 +18,7 @@ from conftest import ROOT
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("kind", ["f16", "i8", "f16s", "pair"])
+@pytest.mark.parametrize("kind", ["f16", "i8", "f16s", "pair", "i8s"])
 def test_q8_0_gemm_parity_in_each_mma_kind(kind):
     env = dict(os.environ, PXQ_Q8_0_MMA=kind)
     files = [os.path.join(ROOT, "tests", f) for f in ("test_gpu_parity.py", "test_gpu_baseline_shapes.py")]
