@@ -80,13 +80,16 @@ def measured_peaks():
 
 
 def gemm_peak(wtype, bf16, peak_src):
-    """The roofline peak of a GEMM line: the Q8_0 kernel's block dots are
-    kind::i8 MMAs (the int8 rate, 2x the measured bf16 dense peak on this
-    part: the kind::i8 and kind::f16 MMA rates were measured in the ratio
-    2.00), the K-quant kernels issue kind::f16 MMAs (the bf16 peak)."""
+    """The roofline peak of a GEMM line.  Q8_0 is held to the int8 tensor
+    rate (2x the measured bf16 dense peak on this part: the kind::i8 and
+    kind::f16 MMA rates were measured in the ratio 2.00), whichever MMA kind
+    its operand kind issues; the K-quant kernels issue kind::f16 MMAs (the
+    bf16 peak)."""
     if wtype == Q8_0:
+        kind = os.environ.get("PXQ_Q8_0_MMA", "f16s")
+        mma = "kind::i8" if kind in ("i8", "i8s") else "kind::f16 on exact fp16 copies of the int8 quants"
         return {"peak": 2 * bf16, "unit": "TFLOP/s",
-                "peak_source": f"{peak_src} bf16 dense (burst) x 2: the block dots are kind::i8 MMAs"}
+                "peak_source": f"{peak_src} bf16 dense (burst) x 2, the int8 rate; the block dots are {mma} MMAs"}
     return {"peak": bf16, "unit": "TFLOP/s",
             "peak_source": f"{peak_src} bf16 dense (burst); the GEMM issues kind::f16 MMAs on exact integer values"}
 
@@ -1046,7 +1049,7 @@ def run_extras(args, dist: Dist) -> dict:
         else:
             def fn():
                 pxq.Activation(wtype, x).release()
-            kind = os.environ.get("PXQ_Q8_0_MMA", "i8s")  # the library's default operand kind
+            kind = os.environ.get("PXQ_Q8_0_MMA", "f16s")  # the library's default operand kind
             # quants (int8 for kinds "i8" and "i8s", else fp16) and block scales (fp16 for "f16s" and "i8s", else fp32)
             wbytes = M * K * (1 if kind in ("i8", "i8s") else 2) + M * K // 32 * (2 if kind in ("f16s", "i8s") else 4)
         # 10 calls captured in a CUDA graph (no host launch gaps), replayed

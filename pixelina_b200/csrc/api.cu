@@ -246,7 +246,9 @@ std::unordered_map<std::string, pxq_weight*> g_cache;  // guarded by g_mutex
 // one-hot tensor-core MMA, 3 = kind 0's operands on CTA pairs (256 x 256
 // tiles), 4 = kind 2 with the int8 quants (kind::i8 block dots).  Read once
 // from PXQ_Q8_0_MMA ("f16", "i8", "f16s", "pair", "i8s"); the default is
-// kind 4, the fastest measured.
+// kind 2, the fastest measured (its drain converts nothing: the kind::f16
+// block dots arrive in TMEM as fp32, where kind 4's int32 dots cost one
+// int-to-float conversion per element and block).
 int q8_operand_kind()
 {
     static const int v = [] {
@@ -254,8 +256,8 @@ int q8_operand_kind()
         if (e && strcmp(e, "f16") == 0) return 0;
         if (e && strcmp(e, "i8") == 0) return 1;
         if (e && strcmp(e, "pair") == 0) return 3;
-        if (e && strcmp(e, "f16s") == 0) return 2;
-        return 4;
+        if (e && strcmp(e, "i8s") == 0) return 4;
+        return 2;
     }();
     return v;
 }

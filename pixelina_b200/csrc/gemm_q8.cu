@@ -7,21 +7,23 @@
 // product of the two fp16 block scales times the float of an exact int32
 // dot, accumulated in fp32) as driven by cpu_quant_matmul (:389-400).
 //
-// Design (sm_100a, one CTA per SM, persistent over 128 x 128 output tiles,
-// 16 drain warps -- four per scheduler -- plus a producer and an MMA warp):
+// Design (sm_100a, one CTA per SM, persistent over 128 x 128 output tiles;
+// drain warps plus one warpgroup for the producer and the MMA issuers):
 //   * Per 32-block the tensor core computes the block dots I into TMEM and
 //     the drain accumulates S * I per element.  Operand kinds
 //     (GemmOperands::q8_kind, PXQ_Q8_0_MMA):
-//       4 (default, fastest measured): the int8 quants, one kind::i8 MMA
-//         (K = 32) per block for the exact int32 dots I, and a K = 16
-//         kind::f16 MMA of a one-hot weight-scale tile against the
-//         activations' fp16 scale tile for S = dW * dX, exact because
-//         fp16 x fp16 fits fp32 (k_gemm_q8s<., true>).  TMEM holds (S, I)
-//         for two blocks; the drain converts I to fp32 (exact: |I| <=
-//         32 * 127 * 127) and does one packed FMA per element pair and
-//         block, reading no scales from shared memory.
-//       2: the same with exact fp16 copies of the quants and two kind::f16
-//         MMAs (K = 16 each) for I (k_gemm_q8s<., false>).
+//       2 (default, fastest measured): exact fp16 copies of the quants, two
+//         kind::f16 MMAs (K = 16 each) per block for the block dots I (exact
+//         in fp32: |I| <= 32 * 127 * 127), and a K = 16 kind::f16 MMA of a
+//         one-hot weight-scale tile against the activations' fp16 scale tile
+//         for S = dW * dX, exact because fp16 x fp16 fits fp32
+//         (k_gemm_q8s<., false, .>).  TMEM holds (S, I) for two blocks; the
+//         drain does one packed FMA per element pair and block and reads no
+//         scales from shared memory.  Eight drain warps of 64 columns each
+//         (PXQ_Q8_0_DRAIN=16: sixteen of 32).
+//       4: the same with the int8 quants and one kind::i8 MMA (K = 32) per
+//         block for I (k_gemm_q8s<., true, .>): half the operand bytes and
+//         one MMA fewer, but the drain converts every int32 dot to fp32.
 //       3: kind 0's operands on CTA pairs (k_gemm_q8p, below).
 //       0: fp16 copies, kind::f16 for I; the drain forms S = dW * dX itself
 //         from fp32 block-major scale planes (k_gemm_q8<0>): two packed fp32
@@ -43,6 +45,8 @@
 // The epilogue (bias, TMA-store staging, stores into peers' outputs for the
 // N-sharded path, the gated feed-forward product, the block-dot dump) is
 // the one of gemm.cu, per accumulator layout.
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include "pxq_device.cuh"
 #include "pxq_internal.h"
@@ -547,6 +551,10 @@ done:
 // .. 16g+15]) gives S[n,m] = dW[n,b] * dX[m,b] exactly (fp16 x fp16 fits
 // fp32).  The drain then does one FMA per element and block, acc += S * I,
 // and reads no scales from shared memory; TMEM holds (S, I) for two blocks.
+// Two issuer threads (the two warps after the producer) take alternate
+// blocks, one per TMEM slot pair, so one pair's wait for its release
+// overlaps the other's issue; both commit to each operand stage's empty
+// barrier (count 2).
 constexpr int Q8S_STAGES = 3;
 constexpr int Q8S_W1H = 128 * 32;                                   // one-hot tile [128][16] fp16, 32-byte swizzle
 constexpr int Q8S_XS = 128 * 32;                                    // activation scale tile [128][16] fp16
@@ -575,8 +583,28 @@ __device__ __forceinline__ uint64_t desc_sw32(uint32_t saddr) { return smem_desc
 //   tmWs  one-hot weight scales fp16 [N][nb*16] box {16, 128}  32B swizzle
 //   tmXs  activation scales fp16 [M][ldd]       box {16, 128}  32B swizzle
 //   tmY   output fp32 [M][ldy], box {32, 32} (TMA-store epilogue)
-template <bool DUMP, bool I8>
-__global__ void __launch_bounds__(Q8_THREADS, 1)
+// Drain shapes: DW = 16 warps of 32 accumulator columns (104 registers each)
+// or DW = 8 warps of 64 (232 registers), plus one warpgroup for the producer
+// and the two MMA issuers.  The wider drain loads a block's S and I for its
+// 64 columns at once, so per block it pays its wait / load / release once for
+// twice the elements, and two warps per scheduler share the issue slots.
+template <int DW>
+struct Q8sDrain {
+    static constexpr int WARPS = DW;
+    static constexpr int GROUPS = DW / 4;                      // column groups per TMEM lane quadrant
+    static constexpr int HC = Q8_TN / GROUPS;                  // accumulator columns per drain warp
+    static constexpr int THREADS = (DW + 4) * 32;
+    static constexpr int PRODUCER_WARP = DW, MMA_WARP = DW + 1;
+    static constexpr uint32_t DRAIN_REGS = DW == 16 ? 104 : 232, PRODUCER_REGS = 40;
+    // the registers a CTA launches with: 64 K per SM over THREADS, in steps of 8
+    static constexpr int LAUNCH_REGS = (65536 / THREADS) / 8 * 8;
+    static_assert(DW == 16 || DW == 8, "drain shape");
+    static_assert(32 * DW * DRAIN_REGS + 128 * PRODUCER_REGS <= THREADS * LAUNCH_REGS, "setmaxnreg split");
+    static_assert(DW * HC * 32 * 4 <= Q8_STAGING, "staging holds every drain warp's output tile");
+};
+
+template <bool DUMP, bool I8, int DW>
+__global__ void __launch_bounds__(Q8sDrain<DW>::THREADS, 1)
     k_gemm_q8s(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                const __grid_constant__ CUtensorMap tmWs, const __grid_constant__ CUtensorMap tmXs,
                const __grid_constant__ CUtensorMap tmY, const Q8Params p)
@@ -584,6 +612,8 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
     constexpr uint32_t IDESC = idesc_f16_f32(Q8_TN, Q8_TM);
     constexpr uint32_t IDESC_I8 = idesc_i8_s32(Q8_TN, Q8_TM);
     constexpr int BPS = q8s_bps<I8>(), STAGE = q8s_stage<I8>();
+    using D = Q8sDrain<DW>;
+    constexpr int HC = D::HC;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + q8s_off_bar<I8>());
@@ -600,15 +630,15 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < Q8S_STAGES; i++) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 1);
+            mbar_init(&empty[i], 2);  // both MMA issuers commit
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], Q8_DRAIN_WARPS);
+            mbar_init(&tempty[i], D::WARPS);
         }
-        mbar_init(mma_done, 1);
-        mbar_init(&merge[0], 32 * Q8_DRAIN_WARPS);
-        mbar_init(&merge[1], 32 * Q8_DRAIN_WARPS);
+        mbar_init(mma_done, 2);
+        mbar_init(&merge[0], 32 * D::WARPS);
+        mbar_init(&merge[1], 32 * D::WARPS);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -616,7 +646,7 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
         tmem_alloc(tmem_slot, 512);
         tmem_relinquish();
     }
-    if (warp == Q8_PRODUCER_WARP && lane == 0) {
+    if (warp == D::PRODUCER_WARP && lane == 0) {
         tma_prefetch_desc(&tmW);
         tma_prefetch_desc(&tmX);
         tma_prefetch_desc(&tmWs);
@@ -635,9 +665,9 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
     const int64_t nstages = (nb + BPS - 1) / BPS;
     uint32_t* status = p.status;
 
-    if (warp >= Q8_DRAIN_WARPS) {
-        regs_dec<Q8_PRODUCER_REGS>();
-        if (warp == Q8_PRODUCER_WARP && lane == 0) {
+    if (warp >= D::WARPS) {
+        regs_dec<D::PRODUCER_REGS>();
+        if (warp == D::PRODUCER_WARP && lane == 0) {
             int stage = 0;
             uint32_t ph = 0;
             for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
@@ -662,9 +692,12 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
                     }
                 }
             }
-        } else if (warp == Q8_MMA_WARP && lane == 0) {
-            int stage = 0, pair = 0;
+        } else if ((warp == D::MMA_WARP || warp == D::MMA_WARP + 1) && lane == 0) {
+            // two issuers: the first takes the blocks of slot pair 0, the second those of pair 1
+            const int mine = warp - D::MMA_WARP;
+            int stage = 0;
             uint32_t ph = 0, tph = 0;
+            int64_t gb = 0;  // global block index (both issuers walk every block)
             for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
                 for (int64_t kc = 0; kc < nstages; kc++) {
                     if (!mbar_wait(&full[stage], ph, abort_flag, status, kDevTimeoutFull)) goto done;
@@ -676,27 +709,26 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
 #pragma unroll
                     for (int bi = 0; bi < BPS; bi++) {
                         if (BPS * kc + bi >= nb) break;
-                        if (!mbar_wait(&tempty[pair], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
-                        tc_fence_after();
-                        const uint32_t ds = tmem_base + (uint32_t)(pair * 2 * Q8_TM);
-                        // S: the one-hot tile selects block (BPS*kc+bi) % 16 of the activation scale tile
-                        if (!DUMP) mma_f16(ds, desc_sw32(ws_addr + bi * Q8S_W1H), desc_sw32(xs_addr), IDESC, 0u);
-                        if constexpr (I8) {
-                            // I: one kind::i8 MMA, K = 32 (the block's 32 bytes)
-                            const uint32_t koff = (uint32_t)bi * 32u;
-                            mma_i8(ds + Q8_TM, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC_I8, 0u);
-                        } else {
+                        const int pair = (int)(gb & 1);
+                        if (pair == mine) {
+                            if (!mbar_wait(&tempty[pair], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
+                            tc_fence_after();
+                            const uint32_t ds = tmem_base + (uint32_t)(pair * 2 * Q8_TM);
+                            if (!DUMP) mma_f16(ds, desc_sw32(ws_addr + bi * Q8S_W1H), desc_sw32(xs_addr), IDESC, 0u);
+                            if constexpr (I8) {
+                                const uint32_t koff = (uint32_t)bi * 32u;
+                                mma_i8(ds + Q8_TM, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC_I8, 0u);
+                            } else {
 #pragma unroll
-                            for (int k = 0; k < 2; k++) {
-                                const uint32_t koff = (uint32_t)(bi * 2 + k) * 32u;
-                                mma_f16(ds + Q8_TM, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC, (uint32_t)k);
+                                for (int k = 0; k < 2; k++) {
+                                    const uint32_t koff = (uint32_t)(bi * 2 + k) * 32u;
+                                    mma_f16(ds + Q8_TM, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC, (uint32_t)k);
+                                }
                             }
-                        }
-                        mma_commit(&tfull[pair]);
-                        if (++pair == 2) {
-                            pair = 0;
+                            mma_commit(&tfull[pair]);
                             tph ^= 1u;
                         }
+                        gb++;
                     }
                     mma_commit(&empty[stage]);
                     if (++stage == Q8S_STAGES) {
@@ -708,10 +740,12 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
         }
     } else {
         // ------------------------------------------------------ drain warps --
-        regs_inc<Q8_DRAIN_REGS>();
-        const uint32_t quad = warp & 3u, quarter = warp >> 2;
+        regs_inc<D::DRAIN_REGS>();
+        const uint32_t quad = warp & 3u, quarter = warp >> 2;  // lane quadrant, column group
         const uint32_t lane_base = (quad * 32u) << 16;
-        const uint32_t col0 = quarter * Q8_HC;
+        const uint32_t col0 = quarter * HC;
+        const uint32_t t_row = tmem_base + lane_base + col0;  // this warp's lanes and columns in slot pair 0
+        const int nb32 = (int)nb;                             // the host caps K at INT32_MAX
         int pair = 0;
         uint32_t tph = 0, mgph = 0;
         auto drain_meet = [&](int i) -> bool {
@@ -726,16 +760,19 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
             const int64_t nq = n0 + quad * 32u;  // the warp's first weight row
             const int64_t n = nq + lane;         // this thread's weight row == TMEM lane
             const int64_t mfirst = m0 + col0;
-            float acc[Q8_HC];
+            float acc[HC];
 #pragma unroll
-            for (int i = 0; i < Q8_HC; i++) acc[i] = 0.f;
-            for (int64_t b = 0; b < nb; b++) {
+            for (int i = 0; i < HC; i++) acc[i] = 0.f;
+            for (int b = 0; b < nb32; b++) {
                 if (!mbar_wait(&tfull[pair], tph, abort_flag, status, kDevTimeoutTmemFull)) goto done;
                 tc_fence_after();
-                const uint32_t ts = tmem_base + lane_base + (uint32_t)(pair * 2 * Q8_TM) + col0;
-                uint32_t sv[32], iv[32];
-                if (!DUMP) tmem_ld32(ts, sv);
-                tmem_ld32(ts + Q8_TM, iv);
+                const uint32_t ts = t_row + (uint32_t)(pair * 2 * Q8_TM);
+                uint32_t sv[HC], iv[HC];
+#pragma unroll
+                for (int c = 0; c < HC; c += 32) {
+                    if (!DUMP) tmem_ld32(ts + c, *reinterpret_cast<uint32_t(*)[32]>(sv + c));
+                    tmem_ld32(ts + Q8_TM + c, *reinterpret_cast<uint32_t(*)[32]>(iv + c));
+                }
                 tmem_ld_wait();
                 tc_fence_before();
                 __syncwarp();
@@ -746,15 +783,15 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
                 }
                 if constexpr (DUMP) {
 #pragma unroll
-                    for (int j = 0; j < Q8_HC; j++) {
+                    for (int j = 0; j < HC; j++) {
                         const int64_t m = mfirst + j;
                         if (n < p.N && m < p.M)
-                            p.dump[(b * p.M + m) * p.N + n] = I8 ? __int2float_rn((int)iv[j]) : __uint_as_float(iv[j]);
+                            p.dump[((int64_t)b * p.M + m) * p.N + n] = I8 ? __int2float_rn((int)iv[j]) : __uint_as_float(iv[j]);
                     }
                 } else {
                     // pix_dot_q8_0: acc = fma(fp16(dw)*fp16(dx), float(block dot), acc), two per instruction
 #pragma unroll
-                    for (int j = 0; j < Q8_HC; j += 2) {
+                    for (int j = 0; j < HC; j += 2) {
                         // kind::i8 leaves exact int32 dots: |I| <= 32 * 127 * 127, exact in fp32
                         const float i0 = I8 ? __int2float_rn((int)iv[j]) : __uint_as_float(iv[j]);
                         const float i1 = I8 ? __int2float_rn((int)iv[j + 1]) : __uint_as_float(iv[j + 1]);
@@ -769,17 +806,17 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
                     // interleaves 64-row groups); the up warps hand their sums over
                     // through the staging buffer and the gate warps finish
                     // tensor_silu + tensor_gate (src/tensor.cpp:199-208, :334-345)
-                    float* xfer = reinterpret_cast<float*>(smem + q8s_off_staging<I8>()) + ((quad & 1) * 4 + quarter) * (Q8_HC * 32);
+                    float* xfer = reinterpret_cast<float*>(smem + q8s_off_staging<I8>()) + ((quad & 1) * D::GROUPS + quarter) * (HC * 32);
                     if (!drain_meet(0)) goto done;
                     if (quad >= 2) {
 #pragma unroll
-                        for (int i = 0; i < Q8_HC; i++) xfer[i * 32 + lane] = acc[i];
+                        for (int i = 0; i < HC; i++) xfer[i * 32 + lane] = acc[i];
                     }
                     if (!drain_meet(1)) goto done;
                     mgph ^= 1u;
                     if (quad < 2) {
 #pragma unroll
-                        for (int i = 0; i < Q8_HC; i++) {
+                        for (int i = 0; i < HC; i++) {
                             const int64_t on = n0 / 2 + quad * 32 + lane, m = mfirst + i;
                             const float g = acc[i], u = xfer[i * 32 + lane];
                             if (on < p.N / 2 && m < p.M) p.y[m * p.ldy + on] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
@@ -789,21 +826,22 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
                 }
                 const float bv = (p.bias && n < p.N) ? p.bias[n] : 0.f;
                 if (p.tma_store) {
-                    float* stg = reinterpret_cast<float*>(smem + q8s_off_staging<I8>()) + warp * (Q8_HC * 32);
+                    float* stg = reinterpret_cast<float*>(smem + q8s_off_staging<I8>()) + warp * (HC * 32);
                     if (lane == 0) bulk_wait_read_all();
                     __syncwarp();
 #pragma unroll
-                    for (int j = 0; j < Q8_HC; j++) stg[j * 32 + lane] = p.bias ? __fadd_rn(acc[j], bv) : acc[j];
+                    for (int j = 0; j < HC; j++) stg[j * 32 + lane] = p.bias ? __fadd_rn(acc[j], bv) : acc[j];
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        tma_store_2d(&tmY, stg, (int32_t)nq, (int32_t)mfirst);
+#pragma unroll
+                        for (int c = 0; c < HC; c += 32) tma_store_2d(&tmY, stg + c * 32, (int32_t)nq, (int32_t)(mfirst + c));
                         bulk_commit();
                     }
                     if (p.ndst && p.dst_vec4) {
                         const int jr = lane >> 3, c4 = 4 * (lane & 7);
                         const int64_t nn = nq + c4;
-                        for (int j = jr; j < Q8_HC; j += 4) {
+                        for (int j = jr; j < HC; j += 4) {
                             const int64_t m = mfirst + j;
                             if (m >= p.M) break;
                             const float4 v = *reinterpret_cast<const float4*>(stg + j * 32 + c4);
@@ -817,7 +855,7 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
                             }
                         }
                     } else if (p.ndst && n < p.N) {
-                        for (int j = 0; j < Q8_HC; j++) {
+                        for (int j = 0; j < HC; j++) {
                             const int64_t m = mfirst + j;
                             if (m >= p.M) break;
                             const float v = stg[j * 32 + lane];
@@ -827,7 +865,7 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
                     }
                 } else if (n < p.N) {
 #pragma unroll
-                    for (int j = 0; j < Q8_HC; j++) {
+                    for (int j = 0; j < HC; j++) {
                         const int64_t m = mfirst + j;
                         if (m < p.M) put_y(p, m, n, p.bias ? __fadd_rn(acc[j], bv) : acc[j]);
                     }
@@ -836,9 +874,9 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
         }
     }
 done:
-    if (p.tma_store && warp < Q8_DRAIN_WARPS && lane == 0) bulk_wait_all();
-    if (p.ndst && warp < Q8_DRAIN_WARPS) __threadfence_system();
-    if (warp == Q8_MMA_WARP && lane == 0) {
+    if (p.tma_store && warp < D::WARPS && lane == 0) bulk_wait_all();
+    if (p.ndst && warp < D::WARPS) __threadfence_system();
+    if ((warp == D::MMA_WARP || warp == D::MMA_WARP + 1) && lane == 0) {
         mma_commit(mma_done);
         const uint64_t t0 = global_ns();
         while (!mbar_try_wait(mma_done, 0) && global_ns() - t0 < PXQ_WAIT_NS) {
@@ -1307,10 +1345,10 @@ cudaError_t launch_q8p(const GemmOperands& op, int num_sms, cudaStream_t s)
     return cudaLaunchKernelEx(&cfg, kern, op.tm[0], op.tm[1], op.tm[4], op.tm[6], op.tm_y, p);
 }
 
-template <bool DUMP, bool I8>
+template <bool DUMP, bool I8, int DW>
 cudaError_t launch_q8s(const GemmOperands& op, int num_sms, cudaStream_t s)
 {
-    auto kern = k_gemm_q8s<DUMP, I8>;
+    auto kern = k_gemm_q8s<DUMP, I8, DW>;
     constexpr int smem = q8s_smem<I8>();
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
@@ -1321,8 +1359,27 @@ cudaError_t launch_q8s(const GemmOperands& op, int num_sms, cudaStream_t s)
     Q8Params p{op.M, op.N, op.K, op.n_first, op.y, op.ldy, op.bias, op.dump, op.status, (op.tma_store && !DUMP) ? 1 : 0,
                op.gated, op.ndst, op.dst_vec4, op.col_off, {}};
     for (int k = 0; k < kMaxScatter; k++) p.ydst[k] = op.ydst[k];
-    kern<<<(unsigned)grid, Q8_THREADS, smem, s>>>(op.tm[0], op.tm[1], op.tm[2], op.tm[3], op.tm_y, p);
+    kern<<<(unsigned)grid, Q8sDrain<DW>::THREADS, smem, s>>>(op.tm[0], op.tm[1], op.tm[2], op.tm[3], op.tm_y, p);
     return cudaGetLastError();
+}
+
+// Drain width of the scale-product kernels: eight 64-column drain warps (the
+// faster measured), or sixteen 32-column ones with PXQ_Q8_0_DRAIN=16.
+int q8s_drain_warps()
+{
+    static const int dw = [] {
+        const char* e = getenv("PXQ_Q8_0_DRAIN");
+        return (e && strcmp(e, "16") == 0) ? 16 : 8;
+    }();
+    return dw;
+}
+
+template <bool I8>
+cudaError_t launch_q8s_any(const GemmOperands& op, int num_sms, cudaStream_t s)
+{
+    if (q8s_drain_warps() == 8)
+        return op.dump ? launch_q8s<true, I8, 8>(op, num_sms, s) : launch_q8s<false, I8, 8>(op, num_sms, s);
+    return op.dump ? launch_q8s<true, I8, 16>(op, num_sms, s) : launch_q8s<false, I8, 16>(op, num_sms, s);
 }
 
 template <int OPK, bool DUMP>
@@ -1348,8 +1405,8 @@ cudaError_t launch_q8_typed(const GemmOperands& op, int num_sms, cudaStream_t s)
 cudaError_t launch_gemm_q8(const GemmOperands& op, int num_sms, cudaStream_t s)
 {
     if (op.q8_kind == 3) return op.dump ? launch_q8p<true>(op, num_sms, s) : launch_q8p<false>(op, num_sms, s);
-    if (op.q8_kind == 2) return op.dump ? launch_q8s<true, false>(op, num_sms, s) : launch_q8s<false, false>(op, num_sms, s);
-    if (op.q8_kind == 4) return op.dump ? launch_q8s<true, true>(op, num_sms, s) : launch_q8s<false, true>(op, num_sms, s);
+    if (op.q8_kind == 2) return launch_q8s_any<false>(op, num_sms, s);
+    if (op.q8_kind == 4) return launch_q8s_any<true>(op, num_sms, s);
     if (op.q8_kind == 1)
         return op.dump ? launch_q8_typed<1, true>(op, num_sms, s) : launch_q8_typed<1, false>(op, num_sms, s);
     return op.dump ? launch_q8_typed<0, true>(op, num_sms, s) : launch_q8_typed<0, false>(op, num_sms, s);
