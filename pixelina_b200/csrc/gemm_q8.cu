@@ -24,18 +24,14 @@
 //       4: the same with the int8 quants and one kind::i8 MMA (K = 32) per
 //         block for I (k_gemm_q8s<., true, .>): half the operand bytes and
 //         one MMA fewer, but the drain converts every int32 dot to fp32.
-//       3: kind 0's operands on CTA pairs (k_gemm_q8p, below).
 //       0: fp16 copies, kind::f16 for I; the drain forms S = dW * dX itself
-//         from fp32 block-major scale planes (k_gemm_q8<0>): two packed fp32
-//         instructions per element pair, four blocks of I in TMEM.
-//       1: as 0 with the int8 quants and kind::i8 MMAs (half the operand
-//         bytes and MMA time) plus an int -> float conversion per element in
-//         the drain (k_gemm_q8<1>).
-//     Kinds 0 and 1 read TMEM in the 16x256b layout (each thread: 4 weight
-//     rows x 8 activation rows), so the per-column activation scales they
-//     read from shared memory are a quarter of what one row per thread would
-//     need; that traffic, then the per-block wait / load / free latency of
-//     two drain warps per scheduler, bounded their first versions.
+//         from fp32 block-major scale planes (k_gemm_q8s<., false, 8, true>):
+//         a packed multiply and a packed FMA per element pair and block,
+//         four blocks of I in TMEM.  Each drain warp reads its 64 activation
+//         scales per block as shared-memory broadcasts, which set its speed.
+//       1: as 0 with the int8 quants and kind::i8 MMAs plus an int -> float
+//         conversion per element in the drain (k_gemm_q8s<., true, 8, true>).
+//       3: kind 0's operands on CTA pairs (k_gemm_q8p, below).
 //   * Scales for kinds 0 and 1 come by TMA into a ring of their own that the
 //     drain releases, so an operand stage is free as soon as its MMAs are done.
 //   * Tiles are walked in groups of 16 activation-row tiles, so the CTAs
@@ -58,18 +54,8 @@ constexpr int Q8_TN = 128;           // weight rows per tile (TMEM lanes)
 constexpr int Q8_TM = 128;           // activation rows per tile (TMEM columns per slot)
 constexpr int Q8_OP_BYTES = 128 * 128;  // one operand per stage: 128 rows x one 128-byte swizzle row
 constexpr int Q8_STAGE = 2 * Q8_OP_BYTES;
-constexpr int Q8_STAGES = 4;
-constexpr int Q8_SLOTS = 4;
-constexpr int Q8_MAX_SD = 8;
-constexpr int Q8_DRAIN_WARPS = 16;   // four per scheduler: the per-block wait/load/release chains overlap
-constexpr int Q8_THREADS = 640;
-constexpr int Q8_PRODUCER_WARP = 16;
-constexpr int Q8_MMA_WARP = 17;
-constexpr int Q8_HC = 32;            // TMEM columns (activation rows) per drain warp
 constexpr int Q8_GROUP_M = 16;       // activation-row tiles per raster group
-constexpr uint32_t Q8_PRODUCER_REGS = 40, Q8_DRAIN_REGS = 104;
-// the split must fit the registers the block launches with (640 x 96)
-static_assert(32 * Q8_DRAIN_WARPS * Q8_DRAIN_REGS + 128 * Q8_PRODUCER_REGS <= Q8_THREADS * 96, "setmaxnreg split");
+constexpr int Q8_STAGING = 64 * 1024;  // output staging: every drain warp's [activation rows][32 weight rows] fp32
 
 template <int OPK>
 struct Q8Op;
@@ -77,34 +63,15 @@ template <>
 struct Q8Op<0> {                     // fp16 operands, kind::f16
     static constexpr int BPS = 2;    // 32-blocks per stage (64 fp16 = 128 bytes)
     static constexpr int SD = 8;     // scale ring entries
-    static constexpr int MMAS = 2;   // K = 16 per MMA
-    static constexpr int ELEMS = 64; // operand elements per 128-byte row
 };
 template <>
 struct Q8Op<1> {                     // int8 operands, kind::i8
-    static constexpr int BPS = 4;
+    static constexpr int BPS = 4;    // 32-blocks per stage (128 int8 = 128 bytes)
     static constexpr int SD = 6;
-    static constexpr int MMAS = 1;   // K = 32 per MMA
-    static constexpr int ELEMS = 128;
 };
 
 template <int OPK>
 __host__ __device__ constexpr int q8_entry_bytes() { return Q8Op<OPK>::BPS * 2 * 128 * 4; }  // dW | dX fp32
-template <int OPK>
-__host__ __device__ constexpr int q8_off_scales() { return Q8_STAGES * Q8_STAGE; }
-template <int OPK>
-__host__ __device__ constexpr int q8_off_staging() { return q8_off_scales<OPK>() + Q8Op<OPK>::SD * q8_entry_bytes<OPK>(); }
-constexpr int Q8_STAGING = Q8_DRAIN_WARPS * Q8_HC * 32 * 4;  // per drain warp [32 activation rows][32 weight rows] fp32
-template <int OPK>
-__host__ __device__ constexpr int q8_off_bar() { return q8_off_staging<OPK>() + Q8_STAGING; }
-// full/empty, scale full/empty, slot full/empty, MMA drain-out, gated hand-over
-constexpr int Q8_NUM_BARS = 2 * Q8_STAGES + 2 * Q8_MAX_SD + 2 * Q8_SLOTS + 1 + 2;
-template <int OPK>
-__host__ __device__ constexpr int q8_smem_bytes() { return q8_off_bar<OPK>() + Q8_NUM_BARS * 8 + 16 + 1024; }
-static_assert(q8_smem_bytes<0>() <= 232448 && q8_smem_bytes<1>() <= 232448, "shared memory");
-static_assert(Q8Op<0>::SD <= Q8_MAX_SD && Q8Op<1>::SD <= Q8_MAX_SD, "scale ring");
-static_assert(Q8_SLOTS * Q8_TM <= 512, "TMEM columns");
-
 struct Q8Params {
     int64_t M, N, K;
     int64_t n_first;
@@ -143,406 +110,6 @@ __device__ __forceinline__ void q8_tile(int64_t t, int64_t mt, int64_t nt, int64
     ni = r / gm;
 }
 
-// One block's accumulators for a drain warp (its 32 TMEM lanes x 32
-// columns) in the 16x256b layout: two loads, lanes 0-15 (a) and 16-31 (b) of
-// the warp's quadrant.  Thread t holds, per load, r[4k + 2h + c] = lane
-// 8h + t/4, column 8k + 2(t%4) + c (k < 4): 4 weight rows and 8 activation
-// rows in all, so it needs 8 per-column activation scales per block (4x
-// fewer shared-memory reads than one lane x 32 columns).
-struct Blk {
-    uint32_t a[16], b[16];
-};
-__device__ __forceinline__ void q8_ld(Blk& v, uint32_t taddr)
-{
-    tmem_ld16x256_x4(taddr, v.a);
-    tmem_ld16x256_x4(taddr + (16u << 16), v.b);
-}
-// element (lh, k, h, c) of a thread's 32: weight row 16lh + 8h + t/4,
-// activation row 8k + 2(t%4) + c (relative to the warp's quadrant / quarter)
-__host__ __device__ constexpr int q8_idx(int lh, int k, int h, int c) { return ((lh * 4 + k) * 2 + h) * 2 + c; }
-
-template <int OPK>
-__device__ __forceinline__ float q8_val(uint32_t bits)
-{
-    if constexpr (OPK == 1) {
-        return __int2float_rn((int)bits);  // exact: |I| <= 32 * 127 * 127
-    } else {
-        return __uint_as_float(bits);
-    }
-}
-
-// acc += (dx * dw) * I over one load's 16 elements, as packed column pairs:
-// acc2[(lh*4 + k)*2 + h] holds columns (8k + 2(t%4), +1) of weight row
-// 16lh + 8h + t/4.  dx2[k]: the pair's activation scales; dw2[h]: the row's
-// weight scale, duplicated.
-template <int OPK>
-__device__ __forceinline__ void q8_fma_load(float2* acc2, const uint32_t (&v)[16], const float2 (&dx2)[4], const float2 (&dw2)[2])
-{
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const float2 sc = __fmul2_rn(dx2[k], dw2[h]);
-            acc2[k * 2 + h] = __ffma2_rn(sc, make_float2(q8_val<OPK>(v[4 * k + 2 * h]), q8_val<OPK>(v[4 * k + 2 * h + 1])),
-                                         acc2[k * 2 + h]);
-        }
-    }
-}
-
-// tensor maps:
-//   tmW   weight operand [N][K] (fp16 or int8), box {128 bytes, 128 rows}, 128B swizzle
-//   tmX   activation operand [M][K],             box {128 bytes, 128 rows}, 128B swizzle
-//   tmDw  weight block scales fp32 [K/32][ldn],  box {128, BPS}
-//   tmDx  activation block scales fp32 [K/32][ldm], box {128, BPS}
-//   tmY   output fp32 [M][ldy], box {32, 64} (TMA-store epilogue)
-template <int OPK, bool DUMP>
-__global__ void __launch_bounds__(Q8_THREADS, 1)
-    k_gemm_q8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
-              const __grid_constant__ CUtensorMap tmDw, const __grid_constant__ CUtensorMap tmDx,
-              const __grid_constant__ CUtensorMap tmY, const Q8Params p)
-{
-    using O = Q8Op<OPK>;
-    constexpr int BPS = O::BPS, SD = O::SD, EB = q8_entry_bytes<OPK>();
-    constexpr uint32_t IDESC = OPK == 1 ? idesc_i8_s32(Q8_TN, Q8_TM) : idesc_f16_f32(Q8_TN, Q8_TM);
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + q8_off_bar<OPK>());
-    uint64_t* full = bars;                      // operand stage loaded
-    uint64_t* empty = full + Q8_STAGES;         // operand stage consumed by the MMAs
-    uint64_t* sfull = empty + Q8_STAGES;        // scale entry loaded
-    uint64_t* sempty = sfull + Q8_MAX_SD;       // scale entry read by every drain warp
-    uint64_t* tfull = sempty + Q8_MAX_SD;       // accumulator slot holds a finished block
-    uint64_t* tempty = tfull + Q8_SLOTS;        // accumulator slot read by every drain warp
-    uint64_t* mma_done = tempty + Q8_SLOTS;     // every issued MMA finished (exit path)
-    uint64_t* merge = mma_done + 1;             // gated epilogue hand-over
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Q8_NUM_BARS);
-    volatile uint32_t* abort_flag = tmem_slot + 1;
-    uint8_t* scale_ring = smem + q8_off_scales<OPK>();
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < Q8_STAGES; i++) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 1);
-        }
-        for (int i = 0; i < Q8_MAX_SD; i++) {
-            mbar_init(&sfull[i], 1);
-            mbar_init(&sempty[i], Q8_DRAIN_WARPS);
-        }
-        for (int i = 0; i < Q8_SLOTS; i++) {
-            mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], Q8_DRAIN_WARPS);
-        }
-        mbar_init(mma_done, 1);
-        mbar_init(&merge[0], 32 * Q8_DRAIN_WARPS);
-        mbar_init(&merge[1], 32 * Q8_DRAIN_WARPS);
-        *abort_flag = 0;
-        fence_mbar_init();
-    }
-    if (warp == 0) {
-        tmem_alloc(tmem_slot, 512);
-        tmem_relinquish();
-    }
-    if (warp == Q8_PRODUCER_WARP && lane == 0) {
-        tma_prefetch_desc(&tmW);
-        tma_prefetch_desc(&tmX);
-        tma_prefetch_desc(&tmDw);
-        tma_prefetch_desc(&tmDx);
-        if (p.tma_store) tma_prefetch_desc(&tmY);
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem_base = *tmem_slot;
-
-    const int64_t mt = (p.M + Q8_TM - 1) / Q8_TM;
-    const int64_t nt = (p.N + Q8_TN - 1) / Q8_TN;
-    const int64_t tiles = mt * nt;
-    const int64_t nb = p.K / kQK8_0;
-    const int64_t nstages = (nb + BPS - 1) / BPS;
-    uint32_t* status = p.status;
-
-    if (warp >= Q8_DRAIN_WARPS) {
-        regs_dec<Q8_PRODUCER_REGS>();
-        if (warp == Q8_PRODUCER_WARP && lane == 0) {
-            int stage = 0, se = 0;
-            uint32_t ph = 0, sph = 0;
-            for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-                int64_t mi, ni;
-                q8_tile(tile, mt, nt, mi, ni);
-                const int32_t m0 = (int32_t)(mi * Q8_TM);
-                const int32_t n0 = (int32_t)(p.n_first + ni * Q8_TN);
-                for (int64_t kc = 0; kc < nstages; kc++) {
-                    // the stage's block scales, for the drain
-                    if (!mbar_wait(&sempty[se], sph ^ 1u, abort_flag, status, kDevTimeoutScaleEmpty)) goto done;
-                    uint8_t* e = scale_ring + se * EB;
-                    mbar_expect_tx(&sfull[se], EB);
-                    tma_load_2d(e, &tmDw, &sfull[se], n0, (int32_t)(kc * BPS));
-                    tma_load_2d(e + EB / 2, &tmDx, &sfull[se], m0, (int32_t)(kc * BPS));
-                    if (++se == SD) {
-                        se = 0;
-                        sph ^= 1u;
-                    }
-                    // the stage's operands, for the MMAs
-                    if (!mbar_wait(&empty[stage], ph ^ 1u, abort_flag, status, kDevTimeoutEmpty)) goto done;
-                    uint8_t* st = smem + stage * Q8_STAGE;
-                    mbar_expect_tx(&full[stage], Q8_STAGE);
-                    const int32_t kx = (int32_t)(kc * O::ELEMS);
-                    tma_load_2d(st, &tmW, &full[stage], kx, n0);
-                    tma_load_2d(st + Q8_OP_BYTES, &tmX, &full[stage], kx, m0);
-                    if (++stage == Q8_STAGES) {
-                        stage = 0;
-                        ph ^= 1u;
-                    }
-                }
-            }
-        } else if (warp == Q8_MMA_WARP && lane == 0) {
-            int stage = 0, slot = 0;
-            uint32_t ph = 0, tph = 0;
-            for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-                for (int64_t kc = 0; kc < nstages; kc++) {
-                    if (!mbar_wait(&full[stage], ph, abort_flag, status, kDevTimeoutFull)) goto done;
-                    tc_fence_after();
-                    const uint32_t w_addr = smem_u32(smem + stage * Q8_STAGE);
-                    const uint32_t x_addr = w_addr + Q8_OP_BYTES;
-#pragma unroll
-                    for (int bi = 0; bi < BPS; bi++) {
-                        if (kc * BPS + bi >= nb) break;
-                        if (!mbar_wait(&tempty[slot], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
-                        tc_fence_after();
-                        const uint32_t d = tmem_base + (uint32_t)(slot * Q8_TM);
-#pragma unroll
-                        for (int k = 0; k < O::MMAS; k++) {
-                            const uint32_t koff = (uint32_t)(bi * O::MMAS + k) * 32u;  // 32 bytes of K per MMA
-                            if constexpr (OPK == 1)
-                                mma_i8(d, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC, (uint32_t)k);
-                            else
-                                mma_f16(d, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC, (uint32_t)k);
-                        }
-                        mma_commit(&tfull[slot]);
-                        if (++slot == Q8_SLOTS) {
-                            slot = 0;
-                            tph ^= 1u;
-                        }
-                    }
-                    mma_commit(&empty[stage]);
-                    if (++stage == Q8_STAGES) {
-                        stage = 0;
-                        ph ^= 1u;
-                    }
-                }
-            }
-        }
-    } else {
-        // ------------------------------------------------------ drain warps --
-        regs_inc<Q8_DRAIN_REGS>();
-        const uint32_t quad = warp & 3u, quarter = warp >> 2;
-        const uint32_t lane_base = (quad * 32u) << 16;
-        const uint32_t col0 = quarter * Q8_HC;
-        const uint32_t tr = lane >> 2, tc = 2u * (lane & 3u);  // this thread's row in an 8-row group, column pair
-        int slot = 0, se = 0;
-        uint32_t tph = 0, sph = 0, mgph = 0;
-        auto drain_meet = [&](int i) -> bool {
-            mbar_arrive(&merge[i]);
-            return mbar_wait(&merge[i], mgph, abort_flag, status, kDevTimeoutTmemFull);
-        };
-        for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-            int64_t mi, ni;
-            q8_tile(tile, mt, nt, mi, ni);
-            const int64_t m0 = mi * Q8_TM;
-            const int64_t n0 = ni * Q8_TN;  // view-local
-            const int64_t nq = n0 + quad * 32u;  // the warp's first weight row
-            const int64_t mfirst = m0 + col0;
-            float2 acc2[Q8_HC / 2];
-#pragma unroll
-            for (int i = 0; i < Q8_HC / 2; i++) acc2[i] = make_float2(0.f, 0.f);
-            for (int64_t b = 0; b < nb; b++) {
-                const int bi = (int)(b % BPS);
-                if (bi == 0 && !mbar_wait(&sfull[se], sph, abort_flag, status, kDevTimeoutScaleFull)) goto done;
-                if (!mbar_wait(&tfull[slot], tph, abort_flag, status, kDevTimeoutTmemFull)) goto done;
-                tc_fence_after();
-                Blk v;
-                q8_ld(v, tmem_base + lane_base + (uint32_t)(slot * Q8_TM) + col0);
-                // the scales while the accumulators load
-                const float* e = reinterpret_cast<const float*>(scale_ring + se * EB);
-                const float* dw = e + bi * 128 + quad * 32u + tr;
-                const float* dx = e + BPS * 128 + bi * 128 + col0 + tc;
-                float2 dx2[4];
-#pragma unroll
-                for (int k = 0; k < 4; k++) dx2[k] = *reinterpret_cast<const float2*>(dx + 8 * k);
-                const float2 dwa[2] = {make_float2(dw[0], dw[0]), make_float2(dw[8], dw[8])};
-                const float2 dwb[2] = {make_float2(dw[16], dw[16]), make_float2(dw[24], dw[24])};
-                tmem_ld_wait();
-                // the slot is free once its values are in registers; every lane's
-                // scale loads are done before lane 0 frees the scale entry
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[slot]);
-                if (++slot == Q8_SLOTS) {
-                    slot = 0;
-                    tph ^= 1u;
-                }
-                if (bi == BPS - 1 || b + 1 == nb) {
-                    if (lane == 0) mbar_arrive(&sempty[se]);
-                    if (++se == SD) {
-                        se = 0;
-                        sph ^= 1u;
-                    }
-                }
-                if constexpr (DUMP) {
-#pragma unroll
-                    for (int lh = 0; lh < 2; lh++)
-#pragma unroll
-                        for (int k = 0; k < 4; k++)
-#pragma unroll
-                            for (int h = 0; h < 2; h++)
-#pragma unroll
-                                for (int c = 0; c < 2; c++) {
-                                    const int64_t n = nq + 16 * lh + 8 * h + tr, m = mfirst + 8 * k + tc + c;
-                                    const uint32_t bits = lh ? v.b[4 * k + 2 * h + c] : v.a[4 * k + 2 * h + c];
-                                    if (n < p.N && m < p.M) p.dump[(b * p.M + m) * p.N + n] = q8_val<OPK>(bits);
-                                }
-                } else {
-                    q8_fma_load<OPK>(acc2, v.a, dx2, dwa);
-                    q8_fma_load<OPK>(acc2 + 8, v.b, dx2, dwb);
-                }
-            }
-            if constexpr (!DUMP) {
-                float acc[Q8_HC];
-#pragma unroll
-                for (int i = 0; i < Q8_HC / 2; i++) {
-                    acc[2 * i] = acc2[i].x;
-                    acc[2 * i + 1] = acc2[i].y;
-                }
-                if (p.gated) {
-                    // gated weight: lanes 64..127 hold the up projections of the
-                    // outputs whose gate projections lanes 0..63 hold (the repack
-                    // interleaves 64-row groups); the up warps hand their sums over
-                    // through the staging buffer and the gate warps finish
-                    // tensor_silu + tensor_gate (src/tensor.cpp:199-208, :334-345)
-                    float* xfer = reinterpret_cast<float*>(smem + q8_off_staging<OPK>()) + ((quad & 1) * 4 + quarter) * (Q8_HC * 32);
-                    if (!drain_meet(0)) goto done;
-                    if (quad >= 2) {
-#pragma unroll
-                        for (int i = 0; i < Q8_HC; i++) xfer[i * 32 + lane] = acc[i];
-                    }
-                    if (!drain_meet(1)) goto done;
-                    mgph ^= 1u;
-                    if (quad < 2) {
-#pragma unroll
-                        for (int lh = 0; lh < 2; lh++)
-#pragma unroll
-                            for (int k = 0; k < 4; k++)
-#pragma unroll
-                                for (int h = 0; h < 2; h++)
-#pragma unroll
-                                    for (int c = 0; c < 2; c++) {
-                                        const int i = q8_idx(lh, k, h, c);
-                                        const int64_t on = n0 / 2 + quad * 32 + 16 * lh + 8 * h + tr, m = mfirst + 8 * k + tc + c;
-                                        const float g = acc[i], u = xfer[i * 32 + lane];
-                                        if (on < p.N / 2 && m < p.M)
-                                            p.y[m * p.ldy + on] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
-                                    }
-                    }
-                    continue;
-                }
-                // bias of the thread's weight rows 8i + t/4 of the quadrant
-                float bv[4];
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const int64_t nn = nq + 8 * i + tr;
-                    bv[i] = (p.bias && nn < p.N) ? p.bias[nn] : 0.f;
-                }
-                if (p.tma_store) {
-                    // stage [32 activation rows][32 weight rows] and store it with one
-                    // TMA store; lane 0 first waits until the warp's previous store
-                    // has finished reading the buffer
-                    float* stg = reinterpret_cast<float*>(smem + q8_off_staging<OPK>()) + warp * (Q8_HC * 32);
-                    if (lane == 0) bulk_wait_read_all();
-                    __syncwarp();
-#pragma unroll
-                    for (int lh = 0; lh < 2; lh++)
-#pragma unroll
-                        for (int k = 0; k < 4; k++)
-#pragma unroll
-                            for (int h = 0; h < 2; h++)
-#pragma unroll
-                                for (int c = 0; c < 2; c++) {
-                                    const float v = acc[q8_idx(lh, k, h, c)];
-                                    stg[(8 * k + tc + c) * 32 + 16 * lh + 8 * h + tr] = p.bias ? __fadd_rn(v, bv[2 * lh + h]) : v;
-                                }
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) {
-                        tma_store_2d(&tmY, stg, (int32_t)nq, (int32_t)mfirst);
-                        bulk_commit();
-                    }
-                    if (p.ndst && p.dst_vec4) {
-                        // the peers' copies from the same staged block, 4 floats a lane
-                        const int jr = lane >> 3, c4 = 4 * (lane & 7);
-                        const int64_t nn = nq + c4;
-                        for (int j = jr; j < Q8_HC; j += 4) {
-                            const int64_t m = mfirst + j;
-                            if (m >= p.M) break;
-                            const float4 v = *reinterpret_cast<const float4*>(stg + j * 32 + c4);
-                            const int64_t off = m * p.ldy + p.col_off + nn;
-                            if (nn + 3 < p.N) {
-                                for (int k = 0; k < p.ndst; k++) *reinterpret_cast<float4*>(p.ydst[k] + off) = v;
-                            } else {
-                                const float vs[4] = {v.x, v.y, v.z, v.w};
-                                for (int q = 0; q < 4 && nn + q < p.N; q++)
-                                    for (int k = 0; k < p.ndst; k++) p.ydst[k][off + q] = vs[q];
-                            }
-                        }
-                    } else if (p.ndst) {
-                        const int64_t nn = nq + lane;
-                        if (nn < p.N) {
-                            for (int j = 0; j < Q8_HC; j++) {
-                                const int64_t m = mfirst + j;
-                                if (m >= p.M) break;
-                                const float v = stg[j * 32 + lane];
-                                const int64_t off = m * p.ldy + p.col_off + nn;
-                                for (int k = 0; k < p.ndst; k++) p.ydst[k][off] = v;
-                            }
-                        }
-                    }
-                } else {
-#pragma unroll
-                    for (int lh = 0; lh < 2; lh++)
-#pragma unroll
-                        for (int k = 0; k < 4; k++)
-#pragma unroll
-                            for (int h = 0; h < 2; h++)
-#pragma unroll
-                                for (int c = 0; c < 2; c++) {
-                                    const int64_t nn = nq + 16 * lh + 8 * h + tr, m = mfirst + 8 * k + tc + c;
-                                    const float v = acc[q8_idx(lh, k, h, c)];
-                                    if (nn < p.N && m < p.M) put_y(p, m, nn, p.bias ? __fadd_rn(v, bv[2 * lh + h]) : v);
-                                }
-                }
-            }
-        }
-    }
-done:
-    if (p.tma_store && warp < Q8_DRAIN_WARPS && lane == 0) bulk_wait_all();
-    // peer stores are visible system-wide before the kernel ends (the
-    // N-sharded path's barrier after the kernel then orders them for the peers)
-    if (p.ndst && warp < Q8_DRAIN_WARPS) __threadfence_system();
-    if (warp == Q8_MMA_WARP && lane == 0) {
-        // no MMA may still be writing TMEM when it is freed (after a normal run
-        // the drain has consumed every result; this covers aborts)
-        mma_commit(mma_done);
-        const uint64_t t0 = global_ns();
-        while (!mbar_try_wait(mma_done, 0) && global_ns() - t0 < PXQ_WAIT_NS) {
-        }
-    }
-    __syncwarp();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (warp == 0) tmem_dealloc(tmem_base, 512);
-}
-
 // ---------------------------------------------------------------------------
 // OPK 2: the scale products on the tensor core.  Per 32-block b, besides the
 // block dots I (two kind::f16 MMAs on the exact fp16 quants), one K = 16 MMA
@@ -565,15 +132,29 @@ __host__ __device__ constexpr int q8s_bps() { return I8 ? 4 : 2; }
 // W | X | one-hot x BPS | X scales: 44 KB (fp16 quants), 52 KB (int8 quants)
 template <bool I8>
 __host__ __device__ constexpr int q8s_stage() { return 2 * Q8_OP_BYTES + q8s_bps<I8>() * Q8S_W1H + Q8S_XS; }
-template <bool I8>
-__host__ __device__ constexpr int q8s_off_staging() { return Q8S_STAGES * q8s_stage<I8>(); }
-template <bool I8>
-__host__ __device__ constexpr int q8s_off_bar() { return q8s_off_staging<I8>() + Q8_STAGING; }
-constexpr int Q8S_NUM_BARS = 2 * Q8S_STAGES + 2 * 2 + 1 + 2;
-template <bool I8>
-__host__ __device__ constexpr int q8s_smem() { return q8s_off_bar<I8>() + Q8S_NUM_BARS * 8 + 16 + 1024; }
-static_assert(q8s_smem<false>() <= 232448 && q8s_smem<true>() <= 232448, "shared memory");
-static_assert(q8s_stage<false>() % 1024 == 0 && q8s_stage<true>() % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+// Shared memory and TMEM of the scale-product kernels.  One-hot form (CC =
+// false): 3 stages of W | X | one-hot x BPS | X scales, two TMEM slots of
+// 256 columns (S, I).  CUDA-core form (CC = true): 4 stages of W | X, a ring
+// of fp32 scale entries (dW | dX, [BPS][128] each) that the drain releases,
+// four TMEM slots of 128 columns (I).
+template <bool I8, bool CC>
+struct Q8sLayout {
+    static constexpr int BPS = q8s_bps<I8>();
+    static constexpr int STAGE = CC ? Q8_STAGE : q8s_stage<I8>();
+    static constexpr int STAGES = CC ? 4 : Q8S_STAGES;
+    static constexpr int SLOTS = CC ? 4 : 2;
+    static constexpr int SLOT_COLS = CC ? Q8_TM : 2 * Q8_TM;
+    static constexpr int SD = CC ? Q8Op<I8 ? 1 : 0>::SD : 0;
+    static constexpr int EB = CC ? q8_entry_bytes<I8 ? 1 : 0>() : 0;
+    static constexpr int OFF_RING = STAGES * STAGE;
+    static constexpr int OFF_STAGING = OFF_RING + SD * EB;
+    static constexpr int OFF_BAR = OFF_STAGING + Q8_STAGING;
+    static constexpr int NUM_BARS = 2 * STAGES + 2 * SLOTS + 2 * SD + 1 + 2;
+    static constexpr int SMEM = OFF_BAR + NUM_BARS * 8 + 16 + 1024;
+    static_assert(SMEM <= 232448, "shared memory");
+    static_assert(STAGE % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+    static_assert(SLOTS * SLOT_COLS <= 512, "TMEM columns");
+};
 
 __device__ __forceinline__ uint64_t desc_sw32(uint32_t saddr) { return smem_desc(saddr, 16, 256, 6); }
 
@@ -603,7 +184,7 @@ struct Q8sDrain {
     static_assert(DW * HC * 32 * 4 <= Q8_STAGING, "staging holds every drain warp's output tile");
 };
 
-template <bool DUMP, bool I8, int DW>
+template <bool DUMP, bool I8, int DW, bool CC>
 __global__ void __launch_bounds__(Q8sDrain<DW>::THREADS, 1)
     k_gemm_q8s(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                const __grid_constant__ CUtensorMap tmWs, const __grid_constant__ CUtensorMap tmXs,
@@ -611,30 +192,38 @@ __global__ void __launch_bounds__(Q8sDrain<DW>::THREADS, 1)
 {
     constexpr uint32_t IDESC = idesc_f16_f32(Q8_TN, Q8_TM);
     constexpr uint32_t IDESC_I8 = idesc_i8_s32(Q8_TN, Q8_TM);
-    constexpr int BPS = q8s_bps<I8>(), STAGE = q8s_stage<I8>();
+    using L = Q8sLayout<I8, CC>;
+    constexpr int BPS = L::BPS, STAGE = L::STAGE, STAGES = L::STAGES, SLOTS = L::SLOTS, SD = L::SD, EB = L::EB;
     using D = Q8sDrain<DW>;
     constexpr int HC = D::HC;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + q8s_off_bar<I8>());
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
     uint64_t* full = bars;                   // operand stage loaded
-    uint64_t* empty = full + Q8S_STAGES;     // operand stage consumed by the MMAs
-    uint64_t* tfull = empty + Q8S_STAGES;    // slot pair holds a block's (S, I)
-    uint64_t* tempty = tfull + 2;            // slot pair read by every drain warp
-    uint64_t* mma_done = tempty + 2;
+    uint64_t* empty = full + STAGES;         // operand stage consumed by the MMAs
+    uint64_t* tfull = empty + STAGES;        // slot holds a block's (S, I), or I alone (CC)
+    uint64_t* tempty = tfull + SLOTS;        // slot read by every drain warp
+    uint64_t* sfull = tempty + SLOTS;        // CC: scale entry loaded
+    uint64_t* sempty = sfull + SD;           // CC: scale entry read by every drain warp
+    uint64_t* mma_done = sempty + SD;
     uint64_t* merge = mma_done + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Q8S_NUM_BARS);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::NUM_BARS);
     volatile uint32_t* abort_flag = tmem_slot + 1;
+    uint8_t* scale_ring = smem + L::OFF_RING;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < Q8S_STAGES; i++) {
+        for (int i = 0; i < STAGES; i++) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 2);  // both MMA issuers commit
         }
-        for (int i = 0; i < 2; i++) {
+        for (int i = 0; i < SLOTS; i++) {
             mbar_init(&tfull[i], 1);
             mbar_init(&tempty[i], D::WARPS);
+        }
+        for (int i = 0; i < SD; i++) {
+            mbar_init(&sfull[i], 1);
+            mbar_init(&sempty[i], D::WARPS);
         }
         mbar_init(mma_done, 2);
         mbar_init(&merge[0], 32 * D::WARPS);
@@ -668,35 +257,50 @@ __global__ void __launch_bounds__(Q8sDrain<DW>::THREADS, 1)
     if (warp >= D::WARPS) {
         regs_dec<D::PRODUCER_REGS>();
         if (warp == D::PRODUCER_WARP && lane == 0) {
-            int stage = 0;
-            uint32_t ph = 0;
+            int stage = 0, se = 0;
+            uint32_t ph = 0, sph = 0;
             for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
                 int64_t mi, ni;
                 q8_tile(tile, mt, nt, mi, ni);
                 const int32_t m0 = (int32_t)(mi * Q8_TM);
                 const int32_t n0 = (int32_t)(p.n_first + ni * Q8_TN);
                 for (int64_t kc = 0; kc < nstages; kc++) {
+                    if constexpr (CC) {
+                        // the stage's block scales, for the drain: dW | dX fp32, [BPS][128] each
+                        if (!mbar_wait(&sempty[se], sph ^ 1u, abort_flag, status, kDevTimeoutScaleEmpty)) goto done;
+                        uint8_t* e = scale_ring + se * EB;
+                        mbar_expect_tx(&sfull[se], EB);
+                        tma_load_2d(e, &tmWs, &sfull[se], n0, (int32_t)(kc * BPS));
+                        tma_load_2d(e + EB / 2, &tmXs, &sfull[se], m0, (int32_t)(kc * BPS));
+                        if (++se == SD) {
+                            se = 0;
+                            sph ^= 1u;
+                        }
+                    }
                     if (!mbar_wait(&empty[stage], ph ^ 1u, abort_flag, status, kDevTimeoutEmpty)) goto done;
                     uint8_t* st = smem + stage * STAGE;
                     const int nblk = nb - BPS * kc < BPS ? (int)(nb - BPS * kc) : BPS;
-                    mbar_expect_tx(&full[stage], 2 * Q8_OP_BYTES + nblk * Q8S_W1H + Q8S_XS);
+                    mbar_expect_tx(&full[stage], CC ? 2 * Q8_OP_BYTES : 2 * Q8_OP_BYTES + nblk * Q8S_W1H + Q8S_XS);
                     const int32_t kx = (int32_t)(kc * 32 * BPS);  // quants of BPS blocks: one 128-byte row
                     tma_load_2d(st, &tmW, &full[stage], kx, n0);
                     tma_load_2d(st + Q8_OP_BYTES, &tmX, &full[stage], kx, m0);
-                    for (int b = 0; b < nblk; b++)
-                        tma_load_2d(st + 2 * Q8_OP_BYTES + b * Q8S_W1H, &tmWs, &full[stage], (int32_t)((BPS * kc + b) * 16), n0);
-                    tma_load_2d(st + 2 * Q8_OP_BYTES + BPS * Q8S_W1H, &tmXs, &full[stage], (int32_t)(((BPS * kc) / 16) * 16), m0);
-                    if (++stage == Q8S_STAGES) {
+                    if constexpr (!CC) {
+                        for (int b = 0; b < nblk; b++)
+                            tma_load_2d(st + 2 * Q8_OP_BYTES + b * Q8S_W1H, &tmWs, &full[stage], (int32_t)((BPS * kc + b) * 16), n0);
+                        tma_load_2d(st + 2 * Q8_OP_BYTES + BPS * Q8S_W1H, &tmXs, &full[stage], (int32_t)(((BPS * kc) / 16) * 16), m0);
+                    }
+                    if (++stage == STAGES) {
                         stage = 0;
                         ph ^= 1u;
                     }
                 }
             }
         } else if ((warp == D::MMA_WARP || warp == D::MMA_WARP + 1) && lane == 0) {
-            // two issuers: the first takes the blocks of slot pair 0, the second those of pair 1
+            // two issuers take alternate blocks: block g goes to slot g % SLOTS
+            // and to the issuer g % 2
             const int mine = warp - D::MMA_WARP;
             int stage = 0;
-            uint32_t ph = 0, tph = 0;
+            uint32_t ph = 0;
             int64_t gb = 0;  // global block index (both issuers walk every block)
             for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
                 for (int64_t kc = 0; kc < nstages; kc++) {
@@ -709,29 +313,33 @@ __global__ void __launch_bounds__(Q8sDrain<DW>::THREADS, 1)
 #pragma unroll
                     for (int bi = 0; bi < BPS; bi++) {
                         if (BPS * kc + bi >= nb) break;
-                        const int pair = (int)(gb & 1);
-                        if (pair == mine) {
-                            if (!mbar_wait(&tempty[pair], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
+                        if ((int)(gb & 1) == mine) {
+                            const int slot = (int)(gb % SLOTS);
+                            const uint32_t tph = (uint32_t)(gb / SLOTS) & 1u;
+                            if (!mbar_wait(&tempty[slot], tph ^ 1u, abort_flag, status, kDevTimeoutTmemEmpty)) goto done;
                             tc_fence_after();
-                            const uint32_t ds = tmem_base + (uint32_t)(pair * 2 * Q8_TM);
-                            if (!DUMP) mma_f16(ds, desc_sw32(ws_addr + bi * Q8S_W1H), desc_sw32(xs_addr), IDESC, 0u);
+                            const uint32_t ds = tmem_base + (uint32_t)(slot * L::SLOT_COLS);
+                            // I: the block's dots, in the slot's last 128 columns
+                            const uint32_t di = ds + (CC ? 0u : (uint32_t)Q8_TM);
+                            if constexpr (!CC) {
+                                if (!DUMP) mma_f16(ds, desc_sw32(ws_addr + bi * Q8S_W1H), desc_sw32(xs_addr), IDESC, 0u);
+                            }
                             if constexpr (I8) {
                                 const uint32_t koff = (uint32_t)bi * 32u;
-                                mma_i8(ds + Q8_TM, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC_I8, 0u);
+                                mma_i8(di, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC_I8, 0u);
                             } else {
 #pragma unroll
                                 for (int k = 0; k < 2; k++) {
                                     const uint32_t koff = (uint32_t)(bi * 2 + k) * 32u;
-                                    mma_f16(ds + Q8_TM, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC, (uint32_t)k);
+                                    mma_f16(di, desc_sw128(w_addr + koff), desc_sw128(x_addr + koff), IDESC, (uint32_t)k);
                                 }
                             }
-                            mma_commit(&tfull[pair]);
-                            tph ^= 1u;
+                            mma_commit(&tfull[slot]);
                         }
                         gb++;
                     }
                     mma_commit(&empty[stage]);
-                    if (++stage == Q8S_STAGES) {
+                    if (++stage == STAGES) {
                         stage = 0;
                         ph ^= 1u;
                     }
@@ -744,10 +352,10 @@ __global__ void __launch_bounds__(Q8sDrain<DW>::THREADS, 1)
         const uint32_t quad = warp & 3u, quarter = warp >> 2;  // lane quadrant, column group
         const uint32_t lane_base = (quad * 32u) << 16;
         const uint32_t col0 = quarter * HC;
-        const uint32_t t_row = tmem_base + lane_base + col0;  // this warp's lanes and columns in slot pair 0
+        const uint32_t t_row = tmem_base + lane_base + col0;  // this warp's lanes and columns in slot 0
         const int nb32 = (int)nb;                             // the host caps K at INT32_MAX
-        int pair = 0;
-        uint32_t tph = 0, mgph = 0;
+        int slot = 0, se = 0;
+        uint32_t tph = 0, sph = 0, mgph = 0;
         auto drain_meet = [&](int i) -> bool {
             mbar_arrive(&merge[i]);
             return mbar_wait(&merge[i], mgph, abort_flag, status, kDevTimeoutTmemFull);
@@ -764,21 +372,30 @@ __global__ void __launch_bounds__(Q8sDrain<DW>::THREADS, 1)
 #pragma unroll
             for (int i = 0; i < HC; i++) acc[i] = 0.f;
             for (int b = 0; b < nb32; b++) {
-                if (!mbar_wait(&tfull[pair], tph, abort_flag, status, kDevTimeoutTmemFull)) goto done;
+                const int bi = b % BPS;
+                if (CC && bi == 0 && !mbar_wait(&sfull[se], sph, abort_flag, status, kDevTimeoutScaleFull)) goto done;
+                if (!mbar_wait(&tfull[slot], tph, abort_flag, status, kDevTimeoutTmemFull)) goto done;
                 tc_fence_after();
-                const uint32_t ts = t_row + (uint32_t)(pair * 2 * Q8_TM);
-                uint32_t sv[HC], iv[HC];
+                const uint32_t ts = t_row + (uint32_t)(slot * L::SLOT_COLS);
+                uint32_t sv[CC ? 1 : HC], iv[HC];
 #pragma unroll
                 for (int c = 0; c < HC; c += 32) {
-                    if (!DUMP) tmem_ld32(ts + c, *reinterpret_cast<uint32_t(*)[32]>(sv + c));
-                    tmem_ld32(ts + Q8_TM + c, *reinterpret_cast<uint32_t(*)[32]>(iv + c));
+                    if constexpr (!CC) {
+                        if (!DUMP) tmem_ld32(ts + c, *reinterpret_cast<uint32_t(*)[32]>(sv + c));
+                    }
+                    tmem_ld32(ts + (CC ? 0u : (uint32_t)Q8_TM) + c, *reinterpret_cast<uint32_t(*)[32]>(iv + c));
                 }
+                // CC: this block's weight scale (the thread's row) and the warp's
+                // activation scales, from the scale entry
+                const float* se_w = reinterpret_cast<const float*>(scale_ring + se * EB) + bi * 128;
+                const float* se_x = reinterpret_cast<const float*>(scale_ring + se * EB + EB / 2) + bi * 128 + col0;
+                const float dwv = CC ? se_w[quad * 32u + lane] : 0.f;
                 tmem_ld_wait();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[pair]);
-                if (++pair == 2) {
-                    pair = 0;
+                if (lane == 0) mbar_arrive(&tempty[slot]);
+                if (++slot == SLOTS) {
+                    slot = 0;
                     tph ^= 1u;
                 }
                 if constexpr (DUMP) {
@@ -787,6 +404,22 @@ __global__ void __launch_bounds__(Q8sDrain<DW>::THREADS, 1)
                         const int64_t m = mfirst + j;
                         if (n < p.N && m < p.M)
                             p.dump[((int64_t)b * p.M + m) * p.N + n] = I8 ? __int2float_rn((int)iv[j]) : __uint_as_float(iv[j]);
+                    }
+                } else if constexpr (CC) {
+                    // pix_dot_q8_0: S = fp16(dw)*fp16(dx) (exact in fp32), acc = fma(S, float(block dot), acc),
+                    // two per instruction; the activation scales are shared-memory broadcasts
+#pragma unroll
+                    for (int j = 0; j < HC; j += 4) {
+                        const float4 dx4 = *reinterpret_cast<const float4*>(se_x + j);
+                        float s0, s1, s2, s3;
+                        fmul2(s0, s1, dx4.x, dx4.y, dwv, dwv);
+                        fmul2(s2, s3, dx4.z, dx4.w, dwv, dwv);
+                        const float i0 = I8 ? __int2float_rn((int)iv[j]) : __uint_as_float(iv[j]);
+                        const float i1 = I8 ? __int2float_rn((int)iv[j + 1]) : __uint_as_float(iv[j + 1]);
+                        const float i2 = I8 ? __int2float_rn((int)iv[j + 2]) : __uint_as_float(iv[j + 2]);
+                        const float i3 = I8 ? __int2float_rn((int)iv[j + 3]) : __uint_as_float(iv[j + 3]);
+                        ffma2(acc[j], acc[j + 1], s0, s1, i0, i1);
+                        ffma2(acc[j + 2], acc[j + 3], s2, s3, i2, i3);
                     }
                 } else {
                     // pix_dot_q8_0: acc = fma(fp16(dw)*fp16(dx), float(block dot), acc), two per instruction
@@ -798,6 +431,15 @@ __global__ void __launch_bounds__(Q8sDrain<DW>::THREADS, 1)
                         ffma2(acc[j], acc[j + 1], __uint_as_float(sv[j]), __uint_as_float(sv[j + 1]), i0, i1);
                     }
                 }
+                if (CC && (bi == BPS - 1 || b + 1 == nb32)) {
+                    // every lane's scale reads are done before lane 0 frees the entry
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sempty[se]);
+                    if (++se == SD) {
+                        se = 0;
+                        sph ^= 1u;
+                    }
+                }
             }
             if constexpr (!DUMP) {
                 if (p.gated) {
@@ -806,7 +448,7 @@ __global__ void __launch_bounds__(Q8sDrain<DW>::THREADS, 1)
                     // interleaves 64-row groups); the up warps hand their sums over
                     // through the staging buffer and the gate warps finish
                     // tensor_silu + tensor_gate (src/tensor.cpp:199-208, :334-345)
-                    float* xfer = reinterpret_cast<float*>(smem + q8s_off_staging<I8>()) + ((quad & 1) * D::GROUPS + quarter) * (HC * 32);
+                    float* xfer = reinterpret_cast<float*>(smem + L::OFF_STAGING) + ((quad & 1) * D::GROUPS + quarter) * (HC * 32);
                     if (!drain_meet(0)) goto done;
                     if (quad >= 2) {
 #pragma unroll
@@ -826,7 +468,7 @@ __global__ void __launch_bounds__(Q8sDrain<DW>::THREADS, 1)
                 }
                 const float bv = (p.bias && n < p.N) ? p.bias[n] : 0.f;
                 if (p.tma_store) {
-                    float* stg = reinterpret_cast<float*>(smem + q8s_off_staging<I8>()) + warp * (HC * 32);
+                    float* stg = reinterpret_cast<float*>(smem + L::OFF_STAGING) + warp * (HC * 32);
                     if (lane == 0) bulk_wait_read_all();
                     __syncwarp();
 #pragma unroll
@@ -1345,11 +987,11 @@ cudaError_t launch_q8p(const GemmOperands& op, int num_sms, cudaStream_t s)
     return cudaLaunchKernelEx(&cfg, kern, op.tm[0], op.tm[1], op.tm[4], op.tm[6], op.tm_y, p);
 }
 
-template <bool DUMP, bool I8, int DW>
+template <bool DUMP, bool I8, int DW, bool CC>
 cudaError_t launch_q8s(const GemmOperands& op, int num_sms, cudaStream_t s)
 {
-    auto kern = k_gemm_q8s<DUMP, I8, DW>;
-    constexpr int smem = q8s_smem<I8>();
+    auto kern = k_gemm_q8s<DUMP, I8, DW, CC>;
+    constexpr int smem = Q8sLayout<I8, CC>::SMEM;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     const int64_t tiles = ((op.M + Q8_TM - 1) / Q8_TM) * ((op.N + Q8_TN - 1) / Q8_TN);
@@ -1359,7 +1001,12 @@ cudaError_t launch_q8s(const GemmOperands& op, int num_sms, cudaStream_t s)
     Q8Params p{op.M, op.N, op.K, op.n_first, op.y, op.ldy, op.bias, op.dump, op.status, (op.tma_store && !DUMP) ? 1 : 0,
                op.gated, op.ndst, op.dst_vec4, op.col_off, {}};
     for (int k = 0; k < kMaxScatter; k++) p.ydst[k] = op.ydst[k];
-    kern<<<(unsigned)grid, Q8sDrain<DW>::THREADS, smem, s>>>(op.tm[0], op.tm[1], op.tm[2], op.tm[3], op.tm_y, p);
+    // tensor maps: W, X, then the one-hot and activation-scale tiles (CC =
+    // false) or the fp32 block-scale planes (CC = true)
+    if constexpr (CC)
+        kern<<<(unsigned)grid, Q8sDrain<DW>::THREADS, smem, s>>>(op.tm[0], op.tm[1], op.tm[4], op.tm[6], op.tm_y, p);
+    else
+        kern<<<(unsigned)grid, Q8sDrain<DW>::THREADS, smem, s>>>(op.tm[0], op.tm[1], op.tm[2], op.tm[3], op.tm_y, p);
     return cudaGetLastError();
 }
 
@@ -1378,27 +1025,10 @@ template <bool I8>
 cudaError_t launch_q8s_any(const GemmOperands& op, int num_sms, cudaStream_t s)
 {
     if (q8s_drain_warps() == 8)
-        return op.dump ? launch_q8s<true, I8, 8>(op, num_sms, s) : launch_q8s<false, I8, 8>(op, num_sms, s);
-    return op.dump ? launch_q8s<true, I8, 16>(op, num_sms, s) : launch_q8s<false, I8, 16>(op, num_sms, s);
+        return op.dump ? launch_q8s<true, I8, 8, false>(op, num_sms, s) : launch_q8s<false, I8, 8, false>(op, num_sms, s);
+    return op.dump ? launch_q8s<true, I8, 16, false>(op, num_sms, s) : launch_q8s<false, I8, 16, false>(op, num_sms, s);
 }
 
-template <int OPK, bool DUMP>
-cudaError_t launch_q8_typed(const GemmOperands& op, int num_sms, cudaStream_t s)
-{
-    auto kern = k_gemm_q8<OPK, DUMP>;
-    constexpr int smem = q8_smem_bytes<OPK>();
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    const int64_t tiles = ((op.M + Q8_TM - 1) / Q8_TM) * ((op.N + Q8_TN - 1) / Q8_TN);
-    int64_t grid = num_sms;
-    if (tiles < grid) grid = tiles;
-    if (grid < 1) grid = 1;
-    Q8Params p{op.M, op.N, op.K, op.n_first, op.y, op.ldy, op.bias, op.dump, op.status, (op.tma_store && !DUMP) ? 1 : 0,
-               op.gated, op.ndst, op.dst_vec4, op.col_off, {}};
-    for (int k = 0; k < kMaxScatter; k++) p.ydst[k] = op.ydst[k];
-    kern<<<(unsigned)grid, Q8_THREADS, smem, s>>>(op.tm[0], op.tm[1], op.tm[4], op.tm[6], op.tm_y, p);
-    return cudaGetLastError();
-}
 
 }  // namespace
 
@@ -1408,8 +1038,8 @@ cudaError_t launch_gemm_q8(const GemmOperands& op, int num_sms, cudaStream_t s)
     if (op.q8_kind == 2) return launch_q8s_any<false>(op, num_sms, s);
     if (op.q8_kind == 4) return launch_q8s_any<true>(op, num_sms, s);
     if (op.q8_kind == 1)
-        return op.dump ? launch_q8_typed<1, true>(op, num_sms, s) : launch_q8_typed<1, false>(op, num_sms, s);
-    return op.dump ? launch_q8_typed<0, true>(op, num_sms, s) : launch_q8_typed<0, false>(op, num_sms, s);
+        return op.dump ? launch_q8s<true, true, 8, true>(op, num_sms, s) : launch_q8s<false, true, 8, true>(op, num_sms, s);
+    return op.dump ? launch_q8s<true, false, 8, true>(op, num_sms, s) : launch_q8s<false, false, 8, true>(op, num_sms, s);
 }
 
 int gemm_q8_scale_box(int kind) { return kind == 1 ? Q8Op<1>::BPS : Q8Op<0>::BPS; }
