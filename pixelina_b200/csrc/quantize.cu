@@ -31,29 +31,36 @@
 namespace pxq {
 namespace {
 
-// One Q8_0 block per 8 consecutive threads, 4 elements per thread.
-// Returns (d as stored fp16, 4 quants packed little-endian).
+// One Q8_0 block per 2 consecutive threads, 16 elements per thread (the
+// block's amax meets in one shuffle; a thread's fixed costs -- indexing, the
+// two divisions, the stores -- are shared by 16 elements).
+// Returns (d as stored fp16, the 16 quants, packed little-endian in 4 words).
 struct Q80Part {
     __half d16;
-    uint32_t packed;
-    int q[4];
+    uint32_t packed[4];
+    int q[16];
 };
 
-__device__ __forceinline__ Q80Part q8_0_part(const float4 v)
+__device__ __forceinline__ Q80Part q8_0_part(const float4 (&v)[4])
 {
-    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    float amax = 0.0f;
 #pragma unroll
-    for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    for (int i = 0; i < 4; i++)
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
     Q80Part p;
     p.d16 = __float2half_rn(d);
-    p.q[0] = q8_0_round(v.x, id);
-    p.q[1] = q8_0_round(v.y, id);
-    p.q[2] = q8_0_round(v.z, id);
-    p.q[3] = q8_0_round(v.w, id);
-    p.packed = ((uint32_t)p.q[0] & 0xffu) | (((uint32_t)p.q[1] & 0xffu) << 8) | (((uint32_t)p.q[2] & 0xffu) << 16) |
-               ((uint32_t)p.q[3] << 24);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        p.q[4 * i + 0] = q8_0_round(v[i].x, id);
+        p.q[4 * i + 1] = q8_0_round(v[i].y, id);
+        p.q[4 * i + 2] = q8_0_round(v[i].z, id);
+        p.q[4 * i + 3] = q8_0_round(v[i].w, id);
+        p.packed[i] = ((uint32_t)p.q[4 * i] & 0xffu) | (((uint32_t)p.q[4 * i + 1] & 0xffu) << 8) |
+                      (((uint32_t)p.q[4 * i + 2] & 0xffu) << 16) | ((uint32_t)p.q[4 * i + 3] << 24);
+    }
     return p;
 }
 
@@ -71,17 +78,17 @@ __device__ __forceinline__ void pdl_prologue(uint32_t* __restrict__ zero, int64_
 }
 
 // The Q8_0 kernels walk a 2-D grid: x = groups of kQ80Threads consecutive
-// 4-value quads of a row (8 threads per 32-block), y = a slab of rows taken
-// kQ80Rows at a time (their loads all in flight before any block is
-// reduced); no index divisions.  Threads past the row end compute on zeros
-// and store nothing, so every shuffle has its full warp.
-constexpr int kQ80Threads = 256;
-constexpr int kQ80Rows = 4;
+// 16-value halves of a row's blocks (2 threads per 32-block), y = a slab of
+// rows taken kQ80Rows at a time (their loads all in flight before any block
+// is reduced); no index divisions.  Threads past the row end compute on
+// zeros and store nothing, so every shuffle has its full warp.
+constexpr int kQ80Threads = 64;
+constexpr int kQ80Rows = 2;
 
 dim3 q8_0_grid(int64_t rows, int64_t inner)
 {
-    const int64_t gx = (inner / 4 + kQ80Threads - 1) / kQ80Threads;
-    int64_t gy = (148 * 16 + gx - 1) / gx;  // about 16 CTAs per SM in all
+    const int64_t gx = (inner / 16 + kQ80Threads - 1) / kQ80Threads;
+    int64_t gy = (148 * 32 + gx - 1) / gx;  // about 32 CTAs per SM in all
     const int64_t max_gy = (rows + kQ80Rows - 1) / kQ80Rows;
     if (gy > max_gy) gy = max_gy;
     if (gy < 1) gy = 1;
@@ -89,24 +96,29 @@ dim3 q8_0_grid(int64_t rows, int64_t inner)
     return dim3((unsigned)gx, (unsigned)gy);
 }
 
-// For every (row, quad) of this thread: emit(row, quad, part).
+// For every (row, half) of this thread: emit(row, half, part, valid); half h
+// covers elements 16h .. 16h+15 of the row (block h / 2).  Every thread of
+// the warp calls emit with the same row (valid is false past the row end or
+// past the last row), so emitters may synchronise the warp.
 template <typename Emit>
 __device__ __forceinline__ void q8_0_rows(const float* x, int64_t rows, int64_t inner, int64_t ldx, Emit emit)
 {
-    const int64_t quad = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const bool on = quad < inner / 4;
+    const int64_t half = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const bool on = half < inner / 16;
     for (int64_t r0 = blockIdx.y; r0 < rows; r0 += (int64_t)kQ80Rows * gridDim.y) {
-        float4 v[kQ80Rows];
+        float4 v[kQ80Rows][4];
 #pragma unroll
         for (int u = 0; u < kQ80Rows; u++) {
             const int64_t r = r0 + (int64_t)u * gridDim.y;
-            v[u] = on && r < rows ? ld_dep_f4(x + r * ldx + quad * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                v[u][i] = on && r < rows ? ld_dep_f4(x + r * ldx + half * 16 + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int u = 0; u < kQ80Rows; u++) {
             const int64_t r = r0 + (int64_t)u * gridDim.y;
             const Q80Part p = q8_0_part(v[u]);
-            if (on && r < rows) emit(r, quad, p);
+            emit(r, half, p, on && r < rows);
         }
     }
 }
@@ -116,14 +128,32 @@ __global__ void k_quantize_q8_0_blocks(const float* x, uint8_t* __restrict__ y, 
 {
     pdl_prologue(zero, nzero);
     const int64_t nb = inner / kQK8_0;
-    q8_0_rows(x, rows, inner, ldx, [&](int64_t row, int64_t quad, const Q80Part& p) {
-        uint8_t* out = y + (row * nb + quad / 8) * kQ8_0Bytes;
-        const int t = (int)(quad % 8);
-        // qs start at byte 2 of the 34-byte block: 2-byte aligned stores only
-        uint16_t* q16 = reinterpret_cast<uint16_t*>(out + 2 + 4 * t);
-        q16[0] = (uint16_t)(p.packed & 0xffffu);
-        q16[1] = (uint16_t)(p.packed >> 16);
-        if (t == 0) *reinterpret_cast<__half*>(out) = p.d16;
+    // a warp's 16 consecutive 34-byte blocks are assembled in shared memory and
+    // written out as consecutive 2-byte words (the blocks are only 2-byte
+    // aligned), so every store instruction covers 64 contiguous bytes
+    constexpr int kWords = 16 * kQ8_0Bytes / 2;
+    __shared__ uint16_t stage[kQ80Threads / 32][kWords];
+    const uint32_t lane = threadIdx.x & 31u;
+    uint16_t* st = stage[threadIdx.x >> 5];
+    const int64_t h0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31u);  // lane 0's half
+    q8_0_rows(x, rows, inner, ldx, [&](int64_t row, int64_t half, const Q80Part& p, bool valid) {
+        if (row >= rows) return;  // warp-uniform
+        uint16_t* w16 = st + (lane >> 1) * (kQ8_0Bytes / 2);
+        if (valid) {
+            if ((lane & 1u) == 0) w16[0] = __half_as_ushort(p.d16);
+#pragma unroll
+            for (int w = 0; w < 4; w++) {
+                w16[1 + 8 * (lane & 1u) + 2 * w] = (uint16_t)(p.packed[w] & 0xffffu);
+                w16[2 + 8 * (lane & 1u) + 2 * w] = (uint16_t)(p.packed[w] >> 16);
+            }
+        }
+        __syncwarp();
+        int64_t nh = inner / 16 - h0;  // halves of this row from lane 0 on
+        nh = nh < 0 ? 0 : (nh > 32 ? 32 : nh);
+        const int words = (int)(nh / 2) * (kQ8_0Bytes / 2);
+        uint16_t* dst = reinterpret_cast<uint16_t*>(y + (row * nb + h0 / 2) * kQ8_0Bytes);
+        for (int i = (int)lane; i < words; i += 32) dst[i] = st[i];
+        __syncwarp();
     });
 }
 
@@ -134,22 +164,27 @@ __global__ void k_quantize_q8_0_blocks(const float* x, uint8_t* __restrict__ y, 
 __global__ void k_quantize_q8_0_operand(const float* __restrict__ x, void* __restrict__ xq, void* __restrict__ dx, int kind,
                                         int64_t rows, int64_t inner, int64_t ldx, int64_t ldd)
 {
-    q8_0_rows(x, rows, inner, ldx, [&](int64_t row, int64_t quad, const Q80Part& p) {
+    q8_0_rows(x, rows, inner, ldx, [&](int64_t row, int64_t half, const Q80Part& p, bool valid) {
+        if (!valid) return;
         if (kind == 1 || kind == 4) {
-            reinterpret_cast<uint32_t*>(static_cast<int8_t*>(xq) + row * inner)[quad] = p.packed;
+            *reinterpret_cast<uint4*>(static_cast<int8_t*>(xq) + row * inner + half * 16) =
+                make_uint4(p.packed[0], p.packed[1], p.packed[2], p.packed[3]);
         } else {
-            __half2 h01 = small_int_half2(p.q[0], p.q[1]);
-            __half2 h23 = small_int_half2(p.q[2], p.q[3]);
-            uint2 packed;
-            packed.x = *reinterpret_cast<uint32_t*>(&h01);
-            packed.y = *reinterpret_cast<uint32_t*>(&h23);
-            *reinterpret_cast<uint2*>(static_cast<__half*>(xq) + row * inner + quad * 4) = packed;
+            uint32_t h[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                __half2 v = small_int_half2(p.q[2 * i], p.q[2 * i + 1]);
+                h[i] = *reinterpret_cast<uint32_t*>(&v);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(xq) + row * inner + half * 16);
+            dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
+            dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
         }
-        if ((quad & 7) == 0) {
+        if ((half & 1) == 0) {
             if (kind == 2 || kind == 4)
-                static_cast<__half*>(dx)[row * ldd + quad / 8] = p.d16;
+                static_cast<__half*>(dx)[row * ldd + half / 2] = p.d16;
             else
-                static_cast<float*>(dx)[(quad / 8) * ldd + row] = __half2float(p.d16);
+                static_cast<float*>(dx)[(half / 2) * ldd + row] = __half2float(p.d16);
         }
     });
 }
