@@ -87,9 +87,9 @@ def gemm_peak(wtype, bf16, peak_src):
     bf16 peak)."""
     if wtype == Q8_0:
         kind = os.environ.get("PXQ_Q8_0_MMA", "f16s")
-        mma = "kind::i8" if kind in ("i8", "i8s") else "kind::f16 on exact fp16 copies of the int8 quants"
+        mma = "kind::i8 MMAs" if kind in ("i8", "i8s") else "kind::f16 MMAs on exact fp16 copies of the int8 quants"
         return {"peak": 2 * bf16, "unit": "TFLOP/s",
-                "peak_source": f"{peak_src} bf16 dense (burst) x 2, the int8 rate; the block dots are {mma} MMAs"}
+                "peak_source": f"{peak_src} bf16 dense (burst) x 2, the int8 rate; the block dots are {mma}"}
     return {"peak": bf16, "unit": "TFLOP/s",
             "peak_source": f"{peak_src} bf16 dense (burst); the GEMM issues kind::f16 MMAs on exact integer values"}
 
