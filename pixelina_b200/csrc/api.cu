@@ -691,6 +691,15 @@ int run_gemm(DeviceCtx* d, pxq_weight* w, size_t row_first, size_t row_count, co
         else
             op.tm_y = op.tm[0];
     }
+    // scatter through TMA stores too where the destinations allow the same
+    // boxes as the local output (Q8_0 one-CTA kernels)
+    if (op.tma_store && ndst > 0 && op.dst_vec4 && w->type == kTypeQ8_0 && op.q8_kind != 3) {
+        op.tma_dst = 1;
+        for (int k = 0; k < ndst && op.tma_dst; k++)
+            if (make_map(d, &op.tm_ydst[k], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dsts[k] + col_off, row_count, (uint64_t)a->M,
+                         ldy * 4, 32, (uint32_t)gemm_store_rows(w->type), CU_TENSOR_MAP_SWIZZLE_NONE) != PXQ_OK)
+                op.tma_dst = 0;
+    }
     cudaError_t e = launch_gemm(op, d->sms, s);
     if (counted(e) != cudaSuccess) return fail(PXQ_ERR_CUDA, "gemm launch failed: %s", cudaGetErrorString(e));
     return PXQ_OK;

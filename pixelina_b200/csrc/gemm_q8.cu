@@ -86,6 +86,12 @@ struct Q8Params {
     int dst_vec4;
     int64_t col_off;
     float* ydst[kMaxScatter];
+    int tma_dst;  // the scatter as TMA stores through Q8PeerMaps (one-CTA kernels)
+};
+
+// Maps of the scatter destinations (ydst[k] + col_off), shaped like tmY.
+struct Q8PeerMaps {
+    CUtensorMap m[kMaxScatter];
 };
 
 __device__ __forceinline__ void put_y(const Q8Params& p, int64_t m, int64_t n, float v)
@@ -188,7 +194,7 @@ template <bool DUMP, bool I8, int DW, bool CC>
 __global__ void __launch_bounds__(Q8sDrain<DW>::THREADS, 1)
     k_gemm_q8s(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                const __grid_constant__ CUtensorMap tmWs, const __grid_constant__ CUtensorMap tmXs,
-               const __grid_constant__ CUtensorMap tmY, const Q8Params p)
+               const __grid_constant__ CUtensorMap tmY, const Q8Params p, const __grid_constant__ Q8PeerMaps peers)
 {
     constexpr uint32_t IDESC = idesc_f16_f32(Q8_TN, Q8_TM);
     constexpr uint32_t IDESC_I8 = idesc_i8_s32(Q8_TN, Q8_TM);
@@ -478,9 +484,18 @@ __global__ void __launch_bounds__(Q8sDrain<DW>::THREADS, 1)
                     if (lane == 0) {
 #pragma unroll
                         for (int c = 0; c < HC; c += 32) tma_store_2d(&tmY, stg + c * 32, (int32_t)nq, (int32_t)(mfirst + c));
+                        // the scatter: the same boxes into every destination, asynchronous
+                        // like the local store (peers' memory over NVLink)
+                        if (p.tma_dst)
+                            for (int k = 0; k < p.ndst; k++)
+#pragma unroll
+                                for (int c = 0; c < HC; c += 32)
+                                    tma_store_2d(&peers.m[k], stg + c * 32, (int32_t)nq, (int32_t)(mfirst + c));
                         bulk_commit();
                     }
-                    if (p.ndst && p.dst_vec4) {
+                    if (p.tma_dst) {
+                        // stored above
+                    } else if (p.ndst && p.dst_vec4) {
                         const int jr = lane >> 3, c4 = 4 * (lane & 7);
                         const int64_t nn = nq + c4;
                         for (int j = jr; j < HC; j += 4) {
@@ -999,14 +1014,16 @@ cudaError_t launch_q8s(const GemmOperands& op, int num_sms, cudaStream_t s)
     if (tiles < grid) grid = tiles;
     if (grid < 1) grid = 1;
     Q8Params p{op.M, op.N, op.K, op.n_first, op.y, op.ldy, op.bias, op.dump, op.status, (op.tma_store && !DUMP) ? 1 : 0,
-               op.gated, op.ndst, op.dst_vec4, op.col_off, {}};
+               op.gated, op.ndst, op.dst_vec4, op.col_off, {}, (op.tma_dst && op.tma_store && !DUMP) ? 1 : 0};
     for (int k = 0; k < kMaxScatter; k++) p.ydst[k] = op.ydst[k];
+    Q8PeerMaps peers;
+    for (int k = 0; k < kMaxScatter; k++) peers.m[k] = op.tm_ydst[k];
     // tensor maps: W, X, then the one-hot and activation-scale tiles (CC =
     // false) or the fp32 block-scale planes (CC = true)
     if constexpr (CC)
-        kern<<<(unsigned)grid, Q8sDrain<DW>::THREADS, smem, s>>>(op.tm[0], op.tm[1], op.tm[4], op.tm[6], op.tm_y, p);
+        kern<<<(unsigned)grid, Q8sDrain<DW>::THREADS, smem, s>>>(op.tm[0], op.tm[1], op.tm[4], op.tm[6], op.tm_y, p, peers);
     else
-        kern<<<(unsigned)grid, Q8sDrain<DW>::THREADS, smem, s>>>(op.tm[0], op.tm[1], op.tm[2], op.tm[3], op.tm_y, p);
+        kern<<<(unsigned)grid, Q8sDrain<DW>::THREADS, smem, s>>>(op.tm[0], op.tm[1], op.tm[2], op.tm[3], op.tm_y, p, peers);
     return cudaGetLastError();
 }
 

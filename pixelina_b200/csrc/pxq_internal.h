@@ -209,6 +209,11 @@ struct GemmOperands {
     int ndst;
     int dst_vec4;         // every ydst[k] + col_off 16-byte aligned and ldy % 4 == 0
     int64_t col_off;
+    // Q8_0 one-CTA kernels: the scatter as TMA stores (the output tile's staged
+    // boxes also stored through tm_ydst[k], maps of ydst[k] + col_off shaped
+    // like tm_y) instead of plain stores from the drain warps
+    int tma_dst;
+    CUtensorMap tm_ydst[kMaxScatter];
 };
 // Rows of one CTA's activation box in the GEMM's tensor maps (tmX, tmXs),
 // and of a whole output tile (the activation scale map tmDx's box).
