@@ -191,6 +191,19 @@ __global__ void k_quantize_q8_0_operand(const float* __restrict__ x, void* __res
 
 // ---- Q8_K: one warp per 256-block (q8k.cuh) -------------------------------
 
+// (row, super-block) of the warp's block index w, by 32-bit division (a 64-bit
+// division costs several times more instructions than the block's own
+// arithmetic; the launchers check that rows x super-blocks fits 32 bits)
+__device__ __forceinline__ const float* q8_K_src(const float* x, int64_t w, uint32_t nsb, int64_t ldx, int64_t& row,
+                                                 int64_t& sb)
+{
+    const uint32_t r = (uint32_t)w / nsb;
+    row = r;
+    sb = (uint32_t)w - r * nsb;
+    return x + row * ldx + sb * kQKK;
+}
+
+
 __global__ void k_quantize_q8_K_blocks(const float* __restrict__ x, uint8_t* __restrict__ y, int64_t rows, int64_t inner,
                                        int64_t ldx)
 {
@@ -219,8 +232,9 @@ __global__ void k_quantize_q8_K_blocks(const float* __restrict__ x, uint8_t* __r
         const int64_t w2 = w + warps;
         const bool has2 = w2 < total;  // warp-uniform
         float va[8], vb[8];
-        q8_K_load(x + (w / nsb) * ldx + (w % nsb) * kQKK, lane, va);
-        if (has2) q8_K_load(x + (w2 / nsb) * ldx + (w2 % nsb) * kQKK, lane, vb);
+        int64_t row, sb, row2, sb2;
+        q8_K_load(q8_K_src(x, w, (uint32_t)nsb, ldx, row, sb), lane, va);
+        if (has2) q8_K_load(q8_K_src(x, w2, (uint32_t)nsb, ldx, row2, sb2), lane, vb);
         emit(w, q8_K_warp_vals(va, lane));
         if (has2) emit(w2, q8_K_warp_vals(vb, lane));
     }
@@ -239,8 +253,8 @@ __global__ void k_quantize_q8_K_mv(const float* x, uint8_t* __restrict__ y, int6
     const int64_t total = rows * nsb;
     const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t w = (((int64_t)blockIdx.x * blockDim.x) >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
-        const int64_t row = w / nsb, sb = w % nsb;
-        const Q8KWarp r = q8_K_warp(x + row * ldx + sb * kQKK, lane);
+        int64_t row, sb;
+        const Q8KWarp r = q8_K_warp(q8_K_src(x, w, (uint32_t)nsb, ldx, row, sb), lane);
         if (Q6)
             q8_K_store_q6(y + w * kQ8KQ6Bytes, r, lane);
         else
@@ -272,8 +286,7 @@ __global__ void k_quantize_q8_K_operand(const float* __restrict__ x, __half* __r
     const int64_t nsb = inner / kQKK;
     const int64_t total = rows * nsb;
     const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    auto emit = [&](int64_t w, const Q8KWarp& r) {
-        const int64_t row = w / nsb, sb = w % nsb;
+    auto emit = [&](int64_t row, int64_t sb, const Q8KWarp& r) {
         __half2 h[4];
         int sum8 = 0;
 #pragma unroll
@@ -298,10 +311,11 @@ __global__ void k_quantize_q8_K_operand(const float* __restrict__ x, __half* __r
         const int64_t w2 = w + warps;
         const bool has2 = w2 < total;  // warp-uniform
         float va[8], vb[8];
-        q8_K_load(x + (w / nsb) * ldx + (w % nsb) * kQKK, lane, va);
-        if (has2) q8_K_load(x + (w2 / nsb) * ldx + (w2 % nsb) * kQKK, lane, vb);
-        emit(w, q8_K_warp_vals(va, lane));
-        if (has2) emit(w2, q8_K_warp_vals(vb, lane));
+        int64_t row, sb, row2, sb2;
+        q8_K_load(q8_K_src(x, w, (uint32_t)nsb, ldx, row, sb), lane, va);
+        if (has2) q8_K_load(q8_K_src(x, w2, (uint32_t)nsb, ldx, row2, sb2), lane, vb);
+        emit(row, sb, q8_K_warp_vals(va, lane));
+        if (has2) emit(row2, sb2, q8_K_warp_vals(vb, lane));
     }
 }
 
@@ -377,6 +391,7 @@ cudaError_t launch_matvec_quantize(const MatvecPlan& plan, const float* x, int64
 cudaError_t launch_quantize_q8_K_blocks(const float* x, void* y, int64_t rows, int64_t inner, int64_t ldx, cudaStream_t s)
 {
     const int threads = 256;
+    if (rows * (inner / kQKK) >= (int64_t)1 << 31) return cudaErrorInvalidValue;
     k_quantize_q8_K_blocks<<<grid_for(rows * (inner / kQKK) * 32, threads), threads, 0, s>>>(x, static_cast<uint8_t*>(y), rows,
                                                                                             inner, ldx);
     return cudaGetLastError();
@@ -393,6 +408,7 @@ cudaError_t launch_quantize_q8_K_operand(const float* x, __half* xq, float* dxT,
                                          int64_t ldx, int64_t ldd, cudaStream_t s)
 {
     const int threads = 256;
+    if (rows * (inner / kQKK) >= (int64_t)1 << 31) return cudaErrorInvalidValue;
     k_quantize_q8_K_operand<<<grid_for(rows * (inner / kQKK) * 32, threads), threads, 0, s>>>(x, xq, dxT, amin, rows, inner,
                                                                                              ldx, ldd);
     return cudaGetLastError();
