@@ -279,43 +279,109 @@ __global__ void k_quantize_q8_0_mv(const float* x, uint8_t* __restrict__ y, int6
     }
 }
 
+// One super-block per half warp, 16 values per lane (lanes 16h .. 16h+15
+// hold the block's values 16*(lane%16) .. +15): the arithmetic of
+// q8_K_warp_vals, with each warp's shuffles, ballot and divisions shared by two
+// blocks.  Lanes of a half whose block is past the end compute on zeros.
+struct Q8KHalf {
+    float d;     // stored fp32 scale (1/iscale, or 0 for an all-zero block)
+    int q[16];   // this lane's 16 quants
+};
+
+__device__ __forceinline__ Q8KHalf q8_K_half_vals(const float (&v)[16], uint32_t lane)
+{
+    // first element (in index order) with the largest |x|: the half's largest
+    // |x| (NaNs never win), then the lowest lane of the half holding it
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; j++) amax = fmaxf(amax, fabsf(v[j]));
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    float vsel = 0.0f;
+    bool hit = false;
+#pragma unroll
+    for (int j = 15; j >= 0; j--) {
+        if (fabsf(v[j]) == amax) {
+            vsel = v[j];
+            hit = true;
+        }
+    }
+    const uint32_t half_mask = (lane & 16u) ? 0xffff0000u : 0x0000ffffu;
+    const uint32_t hits = __ballot_sync(0xffffffffu, hit) & half_mask;
+    const float vmax = __shfl_sync(0xffffffffu, vsel, hits ? __ffs(hits) - 1 : (int)(lane & 16u));
+    Q8KHalf r;
+    if (amax == 0.0f) {
+        r.d = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; j++) r.q[j] = 0;
+        return r;
+    }
+    const float iscale = __fdiv_rn(-127.0f, vmax);
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        const float biased = __fmaf_rn(iscale, v[j], 12582912.0f);
+        const int bits = __float_as_int(biased);
+        const int q = (bits & 0x007fffff) - 0x00400000;
+        r.q[j] = (int8_t)(q < 127 ? q : 127);
+    }
+    r.d = __fdiv_rn(1.0f, iscale);
+    return r;
+}
+
+// GEMM operand of the K-quant kernels: exact fp16 quants [rows][inner], the
+// fp32 scales block-major [inner/256][ldd], and each 32-element sum split as
+// (floor(s/64), s mod 64) in fp16 [rows][inner/256 * 16].  Two super-blocks
+// per warp (one per half).
 __global__ void k_quantize_q8_K_operand(const float* __restrict__ x, __half* __restrict__ xq, float* __restrict__ dxT,
                                         __half* __restrict__ amin, int64_t rows, int64_t inner, int64_t ldx, int64_t ldd)
 {
-    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t lane = threadIdx.x & 31u, hl = lane & 15u;
     const int64_t nsb = inner / kQKK;
     const int64_t total = rows * nsb;
     const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    auto emit = [&](int64_t row, int64_t sb, const Q8KWarp& r) {
-        __half2 h[4];
-        int sum8 = 0;
+    for (int64_t wb = 2 * ((((int64_t)blockIdx.x * blockDim.x) >> 5) + (threadIdx.x >> 5)); wb < total; wb += 2 * warps) {
+        const int64_t w = wb + (lane >> 4);
+        const bool valid = w < total;  // uniform within the half
+        float v[16];
+        int64_t row = 0, sb = 0;
+        if (valid) {
+            const float* src = q8_K_src(x, w, (uint32_t)nsb, ldx, row, sb) + hl * 16;
 #pragma unroll
-        for (int j = 0; j < 4; j++) h[j] = small_int_half2(r.q[2 * j], r.q[2 * j + 1]);
+            for (int i = 0; i < 4; i++) {
+                const float4 f = ld_dep_f4(src + 4 * i);
+                v[4 * i] = f.x;
+                v[4 * i + 1] = f.y;
+                v[4 * i + 2] = f.z;
+                v[4 * i + 3] = f.w;
+            }
+        } else {
 #pragma unroll
-        for (int j = 0; j < 8; j++) sum8 += r.q[j];
-        *reinterpret_cast<uint4*>(xq + row * inner + sb * kQKK + lane * 8) = *reinterpret_cast<uint4*>(h);
-        // 32-element sub-block sums (lanes 4j..4j+3), split exactly for fp16
-        int s32 = sum8 + __shfl_xor_sync(0xffffffffu, sum8, 1);
-        s32 += __shfl_xor_sync(0xffffffffu, s32, 2);
-        if ((lane & 3u) == 0) {
-            const int j = (int)(lane >> 2);
-            const int hi = s32 >> 6;            // floor(s32 / 64)
-            const int lo = s32 - (hi << 6);     // 0..63
-            __half2 pair = small_int_half2(hi, lo);
-            *reinterpret_cast<__half2*>(amin + row * (nsb * 16) + sb * 16 + 2 * j) = pair;
+            for (int j = 0; j < 16; j++) v[j] = 0.0f;
         }
-        if (lane == 0) dxT[sb * ldd + row] = r.d;
-    };
-    // two blocks per warp and trip, both loads in flight together
-    for (int64_t w = (((int64_t)blockIdx.x * blockDim.x) >> 5) + (threadIdx.x >> 5); w < total; w += 2 * warps) {
-        const int64_t w2 = w + warps;
-        const bool has2 = w2 < total;  // warp-uniform
-        float va[8], vb[8];
-        int64_t row, sb, row2, sb2;
-        q8_K_load(q8_K_src(x, w, (uint32_t)nsb, ldx, row, sb), lane, va);
-        if (has2) q8_K_load(q8_K_src(x, w2, (uint32_t)nsb, ldx, row2, sb2), lane, vb);
-        emit(row, sb, q8_K_warp_vals(va, lane));
-        if (has2) emit(row2, sb2, q8_K_warp_vals(vb, lane));
+        const Q8KHalf r = q8_K_half_vals(v, lane);
+        int sum16 = 0;
+#pragma unroll
+        for (int j = 0; j < 16; j++) sum16 += r.q[j];
+        const int s32 = sum16 + __shfl_xor_sync(0xffffffffu, sum16, 1);  // 32-element sub-block = lane pair
+        if (valid) {
+            uint32_t h[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                __half2 p2 = small_int_half2(r.q[2 * i], r.q[2 * i + 1]);
+                h[i] = *reinterpret_cast<uint32_t*>(&p2);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(xq + row * inner + sb * kQKK + hl * 16);
+            dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
+            dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
+            if ((hl & 1u) == 0) {
+                const int j = (int)(hl >> 1);
+                const int hi = s32 >> 6;         // floor(s32 / 64)
+                const int lo = s32 - (hi << 6);  // 0..63
+                __half2 pair = small_int_half2(hi, lo);
+                *reinterpret_cast<__half2*>(amin + row * (nsb * 16) + sb * 16 + 2 * j) = pair;
+            }
+            if (hl == 0) dxT[sb * ldd + row] = r.d;
+        }
     }
 }
 
@@ -409,7 +475,7 @@ cudaError_t launch_quantize_q8_K_operand(const float* x, __half* xq, float* dxT,
 {
     const int threads = 256;
     if (rows * (inner / kQKK) >= (int64_t)1 << 31) return cudaErrorInvalidValue;
-    k_quantize_q8_K_operand<<<grid_for(rows * (inner / kQKK) * 32, threads), threads, 0, s>>>(x, xq, dxT, amin, rows, inner,
+    k_quantize_q8_K_operand<<<grid_for(rows * (inner / kQKK) * 16, threads), threads, 0, s>>>(x, xq, dxT, amin, rows, inner,
                                                                                              ldx, ldd);
     return cudaGetLastError();
 }
