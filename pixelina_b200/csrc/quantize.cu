@@ -203,43 +203,6 @@ __device__ __forceinline__ const float* q8_K_src(const float* x, int64_t w, uint
     return x + row * ldx + sb * kQKK;
 }
 
-
-__global__ void k_quantize_q8_K_blocks(const float* __restrict__ x, uint8_t* __restrict__ y, int64_t rows, int64_t inner,
-                                       int64_t ldx)
-{
-    const uint32_t lane = threadIdx.x & 31u;
-    const int64_t nsb = inner / kQKK;
-    const int64_t total = rows * nsb;
-    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    auto emit = [&](int64_t w, const Q8KWarp& r) {
-        uint8_t* out = y + w * kQ8KBytes;
-        uint32_t lo = 0, hi = 0;
-        int sum8 = 0;
-#pragma unroll
-        for (int j = 0; j < 4; j++) lo |= (uint32_t)(uint8_t)r.q[j] << (8 * j);
-#pragma unroll
-        for (int j = 0; j < 4; j++) hi |= (uint32_t)(uint8_t)r.q[4 + j] << (8 * j);
-#pragma unroll
-        for (int j = 0; j < 8; j++) sum8 += r.q[j];
-        *reinterpret_cast<uint32_t*>(out + 4 + lane * 8) = lo;
-        *reinterpret_cast<uint32_t*>(out + 4 + lane * 8 + 4) = hi;
-        const int sum16 = sum8 + __shfl_xor_sync(0xffffffffu, sum8, 1);  // 16-element group = lane pair
-        if ((lane & 1u) == 0) *reinterpret_cast<int16_t*>(out + 4 + kQKK + lane) = (int16_t)sum16;
-        if (lane == 0) *reinterpret_cast<float*>(out) = r.d;
-    };
-    // two blocks per warp and trip, both loads in flight together
-    for (int64_t w = (((int64_t)blockIdx.x * blockDim.x) >> 5) + (threadIdx.x >> 5); w < total; w += 2 * warps) {
-        const int64_t w2 = w + warps;
-        const bool has2 = w2 < total;  // warp-uniform
-        float va[8], vb[8];
-        int64_t row, sb, row2, sb2;
-        q8_K_load(q8_K_src(x, w, (uint32_t)nsb, ldx, row, sb), lane, va);
-        if (has2) q8_K_load(q8_K_src(x, w2, (uint32_t)nsb, ldx, row2, sb2), lane, vb);
-        emit(w, q8_K_warp_vals(va, lane));
-        if (has2) emit(w2, q8_K_warp_vals(vb, lane));
-    }
-}
-
 // Matvec operand: one record per (row, super-block), kQ8KMvBytes for Q5_K
 // weights (layout: q8_K_store_mv, q8k.cuh), kQ8KQ6Bytes for Q6_K weights
 // (q8_K_store_q6).
@@ -326,6 +289,52 @@ __device__ __forceinline__ Q8KHalf q8_K_half_vals(const float (&v)[16], uint32_t
     }
     r.d = __fdiv_rn(1.0f, iscale);
     return r;
+}
+
+// GGUF Q8_K blocks {f32 d; int8 qs[256]; int16 bsums[16]}: one block per half
+// warp; lane l of a half writes quants 16l .. 16l+15 (4-byte stores: the
+// 292-byte blocks are 4-byte aligned) and their sum, which is bsums[l].
+__global__ void k_quantize_q8_K_blocks(const float* __restrict__ x, uint8_t* __restrict__ y, int64_t rows, int64_t inner,
+                                       int64_t ldx)
+{
+    const uint32_t lane = threadIdx.x & 31u, hl = lane & 15u;
+    const int64_t nsb = inner / kQKK;
+    const int64_t total = rows * nsb;
+    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t wb = 2 * ((((int64_t)blockIdx.x * blockDim.x) >> 5) + (threadIdx.x >> 5)); wb < total; wb += 2 * warps) {
+        const int64_t w = wb + (lane >> 4);
+        const bool valid = w < total;  // uniform within the half
+        float v[16];
+        if (valid) {
+            int64_t row, sb;
+            const float* src = q8_K_src(x, w, (uint32_t)nsb, ldx, row, sb) + hl * 16;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float4 f = ld_dep_f4(src + 4 * i);
+                v[4 * i] = f.x;
+                v[4 * i + 1] = f.y;
+                v[4 * i + 2] = f.z;
+                v[4 * i + 3] = f.w;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; j++) v[j] = 0.0f;
+        }
+        const Q8KHalf r = q8_K_half_vals(v, lane);
+        if (valid) {
+            uint8_t* out = y + w * kQ8KBytes;
+            uint32_t* qs = reinterpret_cast<uint32_t*>(out + 4 + hl * 16);
+            int sum16 = 0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                qs[i] = ((uint32_t)r.q[4 * i] & 0xffu) | (((uint32_t)r.q[4 * i + 1] & 0xffu) << 8) |
+                        (((uint32_t)r.q[4 * i + 2] & 0xffu) << 16) | ((uint32_t)r.q[4 * i + 3] << 24);
+                sum16 += r.q[4 * i] + r.q[4 * i + 1] + r.q[4 * i + 2] + r.q[4 * i + 3];
+            }
+            *reinterpret_cast<int16_t*>(out + 4 + kQKK + 2 * hl) = (int16_t)sum16;
+            if (hl == 0) *reinterpret_cast<float*>(out) = r.d;
+        }
+    }
 }
 
 // GEMM operand of the K-quant kernels: exact fp16 quants [rows][inner], the
@@ -458,7 +467,7 @@ cudaError_t launch_quantize_q8_K_blocks(const float* x, void* y, int64_t rows, i
 {
     const int threads = 256;
     if (rows * (inner / kQKK) >= (int64_t)1 << 31) return cudaErrorInvalidValue;
-    k_quantize_q8_K_blocks<<<grid_for(rows * (inner / kQKK) * 32, threads), threads, 0, s>>>(x, static_cast<uint8_t*>(y), rows,
+    k_quantize_q8_K_blocks<<<grid_for(rows * (inner / kQKK) * 16, threads), threads, 0, s>>>(x, static_cast<uint8_t*>(y), rows,
                                                                                             inner, ldx);
     return cudaGetLastError();
 }
